@@ -1,0 +1,66 @@
+// Python bindings of the sm_100a kernels (module mtorus._cuda).
+#include <torch/extension.h>
+
+#include "kernels/launch_counter.h"
+
+namespace mtorus {
+// layernorm.cu
+std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gamma,
+                                      const at::Tensor& beta, double eps);
+at::Tensor layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& gamma,
+                         const at::Tensor& mean, const at::Tensor& rstd, at::Tensor dgamma,
+                         at::Tensor dbeta, bool accumulate);
+// xent.cu
+at::Tensor xent_fused(at::Tensor logits, const at::Tensor& targets,
+                      const c10::optional<at::Tensor>& grad_scale, double scale_mul,
+                      bool write_grad);
+// optim.cu
+void optim_grad_sumsq(const at::Tensor& g, at::Tensor st);
+void optim_finalize(at::Tensor st, bool dynamic, int64_t growth_interval, double max_norm,
+                    bool unscale);
+void adam_step(at::Tensor p, at::Tensor m, at::Tensor v, const at::Tensor& g,
+               c10::optional<at::Tensor> w16, const at::Tensor& st, double lr, double beta1,
+               double beta2, double eps, double weight_decay, double step_override);
+void sgd_step(at::Tensor p, const at::Tensor& g, c10::optional<at::Tensor> w16,
+              const at::Tensor& st, double lr);
+// elementwise.cu
+at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& wte, const at::Tensor& wpe,
+                     int64_t S);
+void embed_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor dwte, at::Tensor dwpe,
+               int64_t S, bool accumulate);
+at::Tensor bias_gelu_fwd(at::Tensor pre, const c10::optional<at::Tensor>& bias);
+void gelu_bwd_(at::Tensor dact, const at::Tensor& pre);
+void colsum_(const at::Tensor& x, at::Tensor out, bool accumulate);
+// gemm_bf16.cu
+void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor D,
+               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+               const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
+               const c10::optional<at::Tensor>& alpha, bool beta);
+int64_t gemm_status(bool reset);
+}  // namespace mtorus
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  using namespace mtorus;
+  namespace py = pybind11;
+  m.doc() = "mtorus sm_100a kernels";
+  m.def("layernorm_fwd", &layernorm_fwd);
+  m.def("layernorm_bwd", &layernorm_bwd);
+  m.def("xent_fused", &xent_fused, py::arg("logits"), py::arg("targets"),
+        py::arg("grad_scale") = py::none(), py::arg("scale_mul") = 1.0,
+        py::arg("write_grad") = true);
+  m.def("optim_grad_sumsq", &optim_grad_sumsq);
+  m.def("optim_finalize", &optim_finalize);
+  m.def("adam_step", &adam_step);
+  m.def("sgd_step", &sgd_step);
+  m.def("embed_fwd", &embed_fwd);
+  m.def("embed_bwd", &embed_bwd);
+  m.def("bias_gelu_fwd", &bias_gelu_fwd);
+  m.def("gelu_bwd_", &gelu_bwd_);
+  m.def("colsum_", &colsum_);
+  m.def("gemm_bf16", &gemm_bf16, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"),
+        py::arg("D"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
+        py::arg("act") = py::none(), py::arg("aux") = py::none(), py::arg("alpha") = py::none(),
+        py::arg("beta") = false);
+  m.def("gemm_status", &gemm_status, py::arg("reset") = true);
+  m.def("launch_count", []() { return mtorus::launch_counter(); });
+}

@@ -1,0 +1,211 @@
+// Embedding gather/scatter and bias+GELU kernels for the GPT blocks.
+//
+// Reference semantics:
+//   * token + learned position embedding: x = wte[ids] + wpe[pos]
+//     (examples/gpt-1b/src/model.rs:113-118)
+//   * FFN activation: GELU, erf form (examples/gpt-1b/src/transformer.rs:107)
+//
+// Design (B200): 16-byte vectors; the embedding backward scatters token rows
+// straight into the fp32 master-gradient buffer with vectorised fp32 atomics
+// (red.global.add.v4.f32) and sums position rows over the batch without atomics.
+#include "common.cuh"
+
+namespace mtorus {
+
+// x[t, :] = wte[ids[t], :] + wpe[t % S, :]   (bf16 tables, bf16 output)
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ wte,
+                                 const bf16* __restrict__ wpe, bf16* __restrict__ out, int T,
+                                 int S, int d, int V) {
+  const int nv = d / 8;
+  const size_t total = (size_t)T * nv;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int t = i / nv, c = i % nv;
+    int64_t id = ids[t];
+    id = id < 0 ? 0 : (id >= V ? V - 1 : id);
+    float a[8], b[8];
+    unpack8(reinterpret_cast<const bf16x8*>(wte + (size_t)id * d)[c], a);
+    unpack8(reinterpret_cast<const bf16x8*>(wpe + (size_t)(t % S) * d)[c], b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] += b[k];
+    reinterpret_cast<bf16x8*>(out + (size_t)t * d)[c] = pack8(a);
+  }
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+// dwte[ids[t], :] += dy[t, :]
+__global__ void embed_bwd_tok_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ dy,
+                                     float* __restrict__ dwte, int T, int d, int V) {
+  const int nv = d / 8;
+  const size_t total = (size_t)T * nv;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int t = i / nv, c = i % nv;
+    int64_t id = ids[t];
+    id = id < 0 ? 0 : (id >= V ? V - 1 : id);
+    float g[8];
+    unpack8(reinterpret_cast<const bf16x8*>(dy + (size_t)t * d)[c], g);
+    float* dst = dwte + (size_t)id * d + c * 8;
+    red_add_v4(dst, g[0], g[1], g[2], g[3]);
+    red_add_v4(dst + 4, g[4], g[5], g[6], g[7]);
+  }
+}
+
+// dwpe[s, :] (+)= sum_b dy[b*S + s, :]
+__global__ void embed_bwd_pos_kernel(const bf16* __restrict__ dy, float* __restrict__ dwpe, int B,
+                                     int S, int d, int accumulate) {
+  const size_t total = (size_t)S * d;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int s = i / d, c = i % d;
+    float acc = 0.f;
+    for (int b = 0; b < B; ++b) acc += __bfloat162float(dy[((size_t)b * S + s) * d + c]);
+    dwpe[i] = accumulate ? dwpe[i] + acc : acc;
+  }
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+}
+__device__ __forceinline__ float gelu_erf_grad(float x) {
+  const float cdf = 0.5f * (1.f + erff(x * 0.70710678118654752f));
+  const float pdf = 0.39894228040143268f * __expf(-0.5f * x * x);
+  return cdf + x * pdf;
+}
+
+// pre[t, j] += bias[j] (in place, optional); act = gelu(pre)
+__global__ void bias_gelu_fwd_kernel(bf16* __restrict__ pre, const float* __restrict__ bias,
+                                     bf16* __restrict__ act, size_t rows, int F) {
+  const int nv = F / 8;
+  const size_t total = rows * nv;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = i % nv;
+    float x[8], y[8];
+    unpack8(reinterpret_cast<const bf16x8*>(pre)[i], x);
+    if (bias) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] += bias[c * 8 + k];
+      reinterpret_cast<bf16x8*>(pre)[i] = pack8(x);
+      // use the rounded pre-activation so backward sees the same value
+      unpack8(reinterpret_cast<const bf16x8*>(pre)[i], x);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) y[k] = gelu_erf(x[k]);
+    reinterpret_cast<bf16x8*>(act)[i] = pack8(y);
+  }
+}
+
+// dpre = dact * gelu'(pre)   (written in place over dact)
+__global__ void gelu_bwd_kernel(bf16* __restrict__ dact, const bf16* __restrict__ pre, size_t n8) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float g[8], x[8];
+    unpack8(reinterpret_cast<const bf16x8*>(dact)[i], g);
+    unpack8(reinterpret_cast<const bf16x8*>(pre)[i], x);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] *= gelu_erf_grad(x[k]);
+    reinterpret_cast<bf16x8*>(dact)[i] = pack8(g);
+  }
+}
+
+// column sums of a [rows, F] bf16 matrix into fp32 (bias gradients); (+)= into out
+__global__ void colsum_kernel(const bf16* __restrict__ x, float* __restrict__ out, int rows, int F,
+                              int rows_per_block) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= F) return;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  float acc = 0.f;
+  for (int r = r0; r < r1; ++r) acc += __bfloat162float(x[(size_t)r * F + c]);
+  atomicAdd(out + c, acc);
+}
+
+static int ew_grid(size_t n) {
+  return (int)std::max<size_t>(1, std::min<size_t>((n + 255) / 256, (size_t)num_sms() * 16));
+}
+
+at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& wte, const at::Tensor& wpe,
+                     int64_t S) {
+  MT_CHECK(ids.scalar_type() == at::kLong, "embed: ids must be int64");
+  MT_CHECK(wte.scalar_type() == at::kBFloat16 && wpe.scalar_type() == at::kBFloat16,
+           "embed: bf16 tables");
+  const int d = wte.size(1), V = wte.size(0);
+  MT_CHECK(d % 8 == 0, "embed: d must be a multiple of 8");
+  const int T = ids.numel();
+  auto out = at::empty({T, d}, wte.options());
+  if (T == 0) return out;
+  embed_fwd_kernel<<<ew_grid((size_t)T * d / 8), 256, 0, cur_stream()>>>(
+      ids.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(wte.data_ptr()),
+      reinterpret_cast<const bf16*>(wpe.data_ptr()), reinterpret_cast<bf16*>(out.data_ptr()), T,
+      (int)S, d, V);
+  MT_LAUNCH_CHECK();
+  return out;
+}
+
+void embed_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor dwte, at::Tensor dwpe,
+               int64_t S, bool accumulate) {
+  MT_CHECK_CONTIG(dy);
+  MT_CHECK(dwte.scalar_type() == at::kFloat && dwpe.scalar_type() == at::kFloat,
+           "embed_bwd: fp32 grads");
+  const int d = dy.size(-1);
+  const int T = ids.numel();
+  const int V = dwte.size(0);
+  auto st = cur_stream();
+  if (!accumulate) dwte.zero_();
+  if (T == 0) return;
+  embed_bwd_tok_kernel<<<ew_grid((size_t)T * d / 8), 256, 0, st>>>(
+      ids.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(dy.data_ptr()),
+      dwte.data_ptr<float>(), T, d, V);
+  MT_LAUNCH_CHECK();
+  const int B = T / S;
+  embed_bwd_pos_kernel<<<ew_grid((size_t)S * d), 256, 0, st>>>(
+      reinterpret_cast<const bf16*>(dy.data_ptr()), dwpe.data_ptr<float>(), B, (int)S, d,
+      accumulate ? 1 : 0);
+  MT_LAUNCH_CHECK();
+}
+
+at::Tensor bias_gelu_fwd(at::Tensor pre, const c10::optional<at::Tensor>& bias) {
+  MT_CHECK_CONTIG(pre);
+  MT_CHECK(pre.scalar_type() == at::kBFloat16, "gelu: bf16");
+  const int F = pre.size(-1);
+  MT_CHECK(F % 8 == 0, "gelu: F % 8");
+  const size_t rows = pre.numel() / F;
+  auto act = at::empty_like(pre);
+  if (rows == 0) return act;
+  bias_gelu_fwd_kernel<<<ew_grid(rows * F / 8), 256, 0, cur_stream()>>>(
+      reinterpret_cast<bf16*>(pre.data_ptr()),
+      bias.has_value() ? bias->data_ptr<float>() : nullptr,
+      reinterpret_cast<bf16*>(act.data_ptr()), rows, F);
+  MT_LAUNCH_CHECK();
+  return act;
+}
+
+void gelu_bwd_(at::Tensor dact, const at::Tensor& pre) {
+  MT_CHECK(dact.numel() % 8 == 0, "gelu_bwd: numel % 8");
+  const size_t n8 = dact.numel() / 8;
+  if (n8 == 0) return;
+  gelu_bwd_kernel<<<ew_grid(n8), 256, 0, cur_stream()>>>(
+      reinterpret_cast<bf16*>(dact.data_ptr()), reinterpret_cast<const bf16*>(pre.data_ptr()), n8);
+  MT_LAUNCH_CHECK();
+}
+
+void colsum_(const at::Tensor& x, at::Tensor out, bool accumulate) {
+  MT_CHECK_CONTIG(x);
+  const int F = x.size(-1);
+  const int rows = x.numel() / F;
+  if (!accumulate) out.zero_();
+  if (rows == 0) return;
+  const int rpb = 256;
+  dim3 grid((F + 255) / 256, (rows + rpb - 1) / rpb);
+  colsum_kernel<<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()),
+                                                out.data_ptr<float>(), rows, F, rpb);
+  MT_LAUNCH_CHECK();
+}
+
+}  // namespace mtorus

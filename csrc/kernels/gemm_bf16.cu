@@ -1,0 +1,446 @@
+// Persistent, warp-specialised bf16 GEMM on the 5th-generation tensor cores.
+//
+//   D[M,N] = epilogue( alpha * A[M,K] . B[N,K]^T )
+//
+// Replaces the Burn NdArray matmuls of every Linear layer of the GPT example
+// (examples/gpt-1b/src/transformer.rs:34-37,54-56,84,99-100,106,109; model.rs:89,128)
+// for the forward (both operands K-major), dgrad (B N-major) and wgrad (A and B
+// MN-major) products.
+//
+// Design (sm_100a):
+//   * one CTA per SM, static persistent tile loop with grouped rasterisation so
+//     concurrently running tiles share A/B panels in L2;
+//   * warp 0: TMA producer (128B-swizzled boxes, STAGES-deep smem ring);
+//   * warp 1: allocates TMEM and issues tcgen05.mma (M=128, N=256, K=16) from
+//     one thread, committing smem slots back to the producer;
+//   * warps 2-5: epilogue; each warp reads its 32 TMEM lanes with tcgen05.ld and
+//     applies alpha / bias / residual / GELU / dGELU / fp32 accumulate in registers;
+//   * two TMEM accumulators (2 x 256 columns) so the epilogue of tile i overlaps
+//     the main loop of tile i+1.
+// All mbarrier waits are bounded (see sm100.cuh); a timeout raises the status word.
+#include "sm100.cuh"
+
+namespace mtorus {
+
+using namespace sm100;
+
+struct GemmEpilogue {
+  void* D;
+  int64_t ldd;
+  int out_f32;          // 0 = bf16 output, 1 = fp32 output
+  int beta;             // fp32 output: D += result
+  const float* bias;    // [N] fp32 or null
+  const bf16* residual; // [M, ldr] bf16 added before the store (bf16 output) or null
+  int64_t ldr;
+  bf16* act;            // GELU(result) written here (D receives the pre-activation) or null
+  int64_t ldact;
+  const bf16* aux;      // dGELU: result *= gelu'(aux[m, n]) or null
+  int64_t ldaux;
+  const float* alpha;   // device scalar multiplier or null
+};
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, GROUP_M = 16;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
+constexpr int kThreads = 192;
+
+__device__ __forceinline__ float gelu_f(float x) {
+  return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+}
+__device__ __forceinline__ float gelu_grad_f(float x) {
+  const float cdf = 0.5f * (1.f + erff(x * 0.70710678118654752f));
+  return cdf + x * 0.39894228040143268f * __expf(-0.5f * x * x);
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = GROUP_M * num_n;
+  const int group = tile / per_group;
+  const int first_m = group * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int r = tile % per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+struct Smem {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tma_a,
+                        const __grid_constant__ CUtensorMap tma_b, int M, int N, int K, int a_mn,
+                        int b_mn, GemmEpilogue ep, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  Smem* ctl = reinterpret_cast<Smem*>(smem + STAGES * STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->tfull[b], 1);
+      mbar_init(&ctl->tempty[b], 128);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+  volatile int* abort = &ctl->abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, parity_mask = 0;  // per stage: load in flight, its phase parity
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort, status, 1)) break;
+          issued_mask |= 1u << stage;
+          parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+          mbar_arrive_expect_tx(&ctl->full[stage], STAGE_BYTES);
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          if (!a_mn) {
+            tma_load_2d(sa, &tma_a, &ctl->full[stage], kb * BK, mb * BM);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(sa + j * (BK * 128), &tma_a, &ctl->full[stage], mb * BM + j * 64, kb * BK);
+          }
+          if (!b_mn) {
+            tma_load_2d(sb, &tma_b, &ctl->full[stage], kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * (BK * 128), &tma_b, &ctl->full[stage], nb * BN + j * 64, kb * BK);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort) {
+        // drain: let every load this thread issued land before the CTA exits
+        for (int s = 0; s < STAGES; ++s) {
+          if (!(issued_mask >> s & 1u)) continue;
+          const uint32_t par = (parity_mask >> s) & 1u;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(smem_u32(&ctl->full[s]), par) &&
+                 globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      const uint32_t idesc = make_idesc_bf16(BM, BN, a_mn, b_mn);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool issued_any = false;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t tphase = (local >> 1) & 1;
+        if (!mbar_wait(&ctl->tempty[buf], tphase ^ 1, abort, status, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&ctl->full[stage], phase, abort, status, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = a_mn ? make_sdesc(sa + k * 2048, BK * 128, 1024, kSwizzle128B)
+                                     : make_sdesc(sa + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = b_mn ? make_sdesc(sb + k * 2048, BK * 128, 1024, kSwizzle128B)
+                                     : make_sdesc(sb + k * 32, 16, 1024, kSwizzle128B);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&ctl->empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&ctl->tfull[buf]);
+      }
+      if (*abort && issued_any) {
+        umma_commit(&ctl->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(smem_u32(&ctl->drain), 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int buf = local & 1;
+      const uint32_t tphase = (local >> 1) & 1;
+      if (!mbar_wait(&ctl->tfull[buf], tphase, abort, status, 4)) break;
+      tc_fence_after();
+      const int m = mb * BM + row;
+      const float alpha = ep.alpha ? *ep.alpha : 1.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c * 32, r);
+        tmem_wait_ld();
+        const int n0 = nb * BN + c * 32;
+        if (m >= M || n0 >= N) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
+        if (ep.bias) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (n0 + i < N) v[i] += ep.bias[n0 + i];
+        }
+        if (ep.aux) {
+          const bf16* ax = ep.aux + (size_t)m * ep.ldaux + n0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (n0 + j * 8 + 8 <= N) {
+              float a8[8];
+              unpack8(reinterpret_cast<const bf16x8*>(ax)[j], a8);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) v[j * 8 + i] *= gelu_grad_f(a8[i]);
+            }
+          }
+        }
+        if (ep.out_f32) {
+          float* dp = reinterpret_cast<float*>(ep.D) + (size_t)m * ep.ldd + n0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (n0 + j * 4 + 4 <= N) {
+              float4 o = make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]);
+              if (ep.beta) {
+                const float4 old = reinterpret_cast<float4*>(dp)[j];
+                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+              }
+              reinterpret_cast<float4*>(dp)[j] = o;
+            }
+          }
+        } else {
+          bf16* dp = reinterpret_cast<bf16*>(ep.D) + (size_t)m * ep.ldd + n0;
+          if (ep.residual) {
+            const bf16* rp = ep.residual + (size_t)m * ep.ldr + n0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (n0 + j * 8 + 8 <= N) {
+                float r8[8];
+                unpack8(reinterpret_cast<const bf16x8*>(rp)[j], r8);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[j * 8 + i] += r8[i];
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (n0 + j * 8 + 8 <= N) {
+              bf16x8 pk = pack8(v + j * 8);
+              reinterpret_cast<bf16x8*>(dp)[j] = pk;
+              if (ep.act) {
+                float p8[8], g8[8];
+                unpack8(pk, p8);  // GELU of the rounded pre-activation
+#pragma unroll
+                for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
+                reinterpret_cast<bf16x8*>(ep.act + (size_t)m * ep.ldact + n0)[j] = pack8(g8);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&ctl->tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p,
+                "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D row-major tensor [outer, inner] with row stride `ld` elements; 128B swizzle.
+CUtensorMap make_tma_2d(const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                        uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swz) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_tiled()(&m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r,
+              " (inner=", inner, ", outer=", outer, ", ld=", ld, ")");
+  return m;
+}
+
+static int* gemm_status_ptr() {
+  static int* p = nullptr;
+  if (!p) {
+    C10_CUDA_CHECK(cudaMalloc(&p, sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
+  }
+  return p;
+}
+
+int64_t gemm_status(bool reset) {
+  int h = 0;
+  int* p = gemm_status_ptr();
+  C10_CUDA_CHECK(cudaMemcpy(&h, p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
+  return h;
+}
+
+static void check_operand(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, ": bf16 CUDA tensor expected");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, ": 2-D with unit inner stride expected");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, ": 16-byte aligned base required");
+  TORCH_CHECK((t.stride(0) * 2) % 16 == 0, name, ": row stride must be a multiple of 16 bytes");
+}
+
+// A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] (b_mn=false) or [K,N] (b_mn=true).
+void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor D,
+               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+               const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
+               const c10::optional<at::Tensor>& alpha, bool beta) {
+  check_operand(A, "A");
+  check_operand(B, "B");
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  const int64_t Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "gemm_bf16: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(D.dim() == 2 && D.size(0) == M && D.size(1) == N && D.stride(1) == 1,
+              "gemm_bf16: D must be [M, N] with unit inner stride");
+  TORCH_CHECK(N % 8 == 0, "gemm_bf16: N must be a multiple of 8");
+  const bool out_f32 = D.scalar_type() == at::kFloat;
+  TORCH_CHECK(out_f32 || D.scalar_type() == at::kBFloat16, "gemm_bf16: D must be bf16 or fp32");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(D.data_ptr()) % 16 == 0 && (D.stride(0) % 8) == 0,
+              "gemm_bf16: D alignment");
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    if (!beta) D.zero_();
+    return;
+  }
+  GemmEpilogue ep{};
+  ep.D = D.data_ptr();
+  ep.ldd = D.stride(0);
+  ep.out_f32 = out_f32;
+  ep.beta = beta ? 1 : 0;
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == N, "bias must be fp32 [N]");
+    ep.bias = bias->data_ptr<float>();
+  }
+  if (residual.has_value()) {
+    TORCH_CHECK(!out_f32 && residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1,
+                "residual must be bf16 with bf16 output");
+    ep.residual = reinterpret_cast<const bf16*>(residual->data_ptr());
+    ep.ldr = residual->stride(0);
+  }
+  if (act.has_value()) {
+    TORCH_CHECK(!out_f32 && act->scalar_type() == at::kBFloat16 && act->stride(1) == 1, "act");
+    ep.act = reinterpret_cast<bf16*>(act->data_ptr());
+    ep.ldact = act->stride(0);
+  }
+  if (aux.has_value()) {
+    TORCH_CHECK(aux->scalar_type() == at::kBFloat16 && aux->stride(1) == 1, "aux");
+    ep.aux = reinterpret_cast<const bf16*>(aux->data_ptr());
+    ep.ldaux = aux->stride(0);
+  }
+  if (alpha.has_value()) {
+    TORCH_CHECK(alpha->scalar_type() == at::kFloat, "alpha must be an fp32 device scalar");
+    ep.alpha = alpha->data_ptr<float>();
+  }
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto swz = CU_TENSOR_MAP_SWIZZLE_128B;
+  CUtensorMap ta = a_mn ? make_tma_2d(A.data_ptr(), dt, 2, M, K, A.stride(0), 64, BK, swz)
+                        : make_tma_2d(A.data_ptr(), dt, 2, K, M, A.stride(0), BK, BM, swz);
+  CUtensorMap tb = b_mn ? make_tma_2d(B.data_ptr(), dt, 2, N, K, B.stride(0), 64, BK, swz)
+                        : make_tma_2d(B.data_ptr(), dt, 2, K, N, B.stride(0), BK, BN, swz);
+  const int num_tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
+  const int grid = std::min(num_tiles, num_sms());
+  const size_t smem = STAGES * STAGE_BYTES + sizeof(Smem) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_tn_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set = true;
+  }
+  gemm_bf16_tn_kernel<<<grid, kThreads, smem, cur_stream()>>>(ta, tb, (int)M, (int)N, (int)K,
+                                                               a_mn ? 1 : 0, b_mn ? 1 : 0, ep,
+                                                               gemm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+}  // namespace mtorus

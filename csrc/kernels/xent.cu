@@ -1,0 +1,137 @@
+// Fused softmax cross-entropy: loss and dlogits in one kernel.
+//
+// Reference: cross_entropy_loss = -mean(gather(log_softmax(logits), targets))
+// (examples/gpt-1b/src/main.rs:32-41).
+//
+// Design (B200): one CTA per row of the [T, V] bf16 logits.  Pass 1 streams the
+// row once with 16-byte loads and an online max / sum-exp; pass 2 re-reads the
+// row (an L2 hit: the row was touched microseconds earlier) and overwrites it
+// in place with dlogits = grad_scale * (softmax - onehot).  grad_scale is a
+// device scalar (1/T times the loss scale), so the backward needs no host sync
+// and fp32 logits are never materialised.
+#include "common.cuh"
+
+namespace mtorus {
+
+__device__ __forceinline__ void online_update(float& m, float& s, float x) {
+  if (x > m) {
+    s = s * __expf(m - x) + 1.f;
+    m = x;
+  } else {
+    s += __expf(x - m);
+  }
+}
+
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  const float mm = fmaxf(m, m2);
+  if (mm == -INFINITY) return;
+  s = s * __expf(m - mm) + s2 * __expf(m2 - mm);
+  m = mm;
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(512) xent_fwd_bwd(bf16* __restrict__ logits,
+                                                    const int64_t* __restrict__ targets,
+                                                    float* __restrict__ loss_rows,
+                                                    const float* __restrict__ grad_scale,
+                                                    float scale_mul, int V, int write_grad) {
+  __shared__ float red_m[32], red_s[32];
+  const int row = blockIdx.x;
+  bf16* lr = logits + (size_t)row * V;
+  float m = -INFINITY, s = 0.f;
+  if (VEC) {
+    const int nv = V / 8;
+    for (int j = threadIdx.x; j < nv; j += blockDim.x) {
+      float f[8];
+      unpack8(reinterpret_cast<const bf16x8*>(lr)[j], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) online_update(m, s, f[i]);
+    }
+  } else {
+    for (int j = threadIdx.x; j < V; j += blockDim.x) online_update(m, s, __bfloat162float(lr[j]));
+  }
+  // block reduce of (m, s)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    red_m[wid] = m;
+    red_s[wid] = s;
+  }
+  __syncthreads();
+  m = lane < nw ? red_m[lane] : -INFINITY;
+  s = lane < nw ? red_s[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  const int64_t tgt = targets[row];
+  const float lse = m + logf(s);
+  if (threadIdx.x == 0) {
+    const float xt = (tgt >= 0 && tgt < V) ? __bfloat162float(lr[tgt]) : lse;
+    loss_rows[row] = lse - xt;
+  }
+  if (!write_grad) return;
+  __syncthreads();  // thread 0 read lr[tgt] before it is overwritten
+  const float gs = (grad_scale ? *grad_scale : 1.f) * scale_mul;
+  const float inv_s = 1.f / s;
+  if (VEC) {
+    const int nv = V / 8;
+    for (int j = threadIdx.x; j < nv; j += blockDim.x) {
+      float f[8];
+      unpack8(reinterpret_cast<const bf16x8*>(lr)[j], f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float p = __expf(f[i] - m) * inv_s;
+        if (j * 8 + i == tgt) p -= 1.f;
+        f[i] = p * gs;
+      }
+      reinterpret_cast<bf16x8*>(lr)[j] = pack8(f);
+    }
+  } else {
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+      float p = __expf(__bfloat162float(lr[j]) - m) * inv_s;
+      if (j == tgt) p -= 1.f;
+      lr[j] = __float2bfloat16_rn(p * gs);
+    }
+  }
+}
+
+// logits [T, V] bf16 (overwritten with dlogits when write_grad); returns per-row loss fp32.
+at::Tensor xent_fused(at::Tensor logits, const at::Tensor& targets,
+                      const c10::optional<at::Tensor>& grad_scale, double scale_mul,
+                      bool write_grad) {
+  MT_CHECK_CUDA(logits);
+  MT_CHECK_CONTIG(logits);
+  MT_CHECK(logits.scalar_type() == at::kBFloat16, "xent: logits must be bf16");
+  MT_CHECK(targets.scalar_type() == at::kLong, "xent: targets must be int64");
+  const int V = logits.size(-1);
+  const int T = logits.numel() / V;
+  auto loss = at::empty({T}, logits.options().dtype(at::kFloat));
+  if (T == 0) return loss;
+  const float* gsp = nullptr;
+  if (grad_scale.has_value()) {
+    MT_CHECK(grad_scale->scalar_type() == at::kFloat, "grad_scale must be fp32");
+    gsp = grad_scale->data_ptr<float>();
+  }
+  auto* lp = reinterpret_cast<bf16*>(logits.data_ptr());
+  const bool vec = (V % 8 == 0) && (reinterpret_cast<uintptr_t>(lp) % 16 == 0);
+  auto st = cur_stream();
+  if (vec)
+    xent_fwd_bwd<true><<<T, 512, 0, st>>>(lp, targets.data_ptr<int64_t>(), loss.data_ptr<float>(),
+                                          gsp, (float)scale_mul, V, write_grad);
+  else
+    xent_fwd_bwd<false><<<T, 512, 0, st>>>(lp, targets.data_ptr<int64_t>(),
+                                           loss.data_ptr<float>(), gsp, (float)scale_mul, V,
+                                           write_grad);
+  MT_LAUNCH_CHECK();
+  return loss;
+}
+
+}  // namespace mtorus

@@ -1,0 +1,301 @@
+"""GPT decoder (the reference's example model) with a fused sm_100a fast path.
+
+Module tree and parameter names follow the reference GPT example
+(examples/gpt-1b/src/model.rs:56-129, transformer.rs:12-171):
+
+    token_embedding, position_embedding, blocks.{i}.{attention.{q,k,v,out}_proj,
+    ff.linear{1,2}, norm{1,2}}, ln_f, lm_head
+
+Linear weights use torch's [out, in] convention; LayerNorm parameters are named
+``gamma`` / ``beta`` as in Burn.
+
+Two execution paths share the same parameters:
+
+* ``forward(input_ids)`` -- the reference semantics in plain PyTorch ops (any
+  device / dtype): learned positions, additive 0/-inf causal mask, softmax
+  attention, erf-GELU, dropout.  This is the CPU oracle.
+* ``fused_loss(input_ids, targets)`` -- the B200 path: bf16 activations, every
+  Linear on the tcgen05 GEMM with bias / GELU / residual / dGELU fused in the
+  epilogue, fused LayerNorm, embedding and cross-entropy kernels, gradients
+  written straight into the flat fp32 ``main_grad`` buffer.  Requires the model
+  to be flattened with ``flatten()``.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+@dataclass
+class GptConfig:
+    """Reference: GptConfig (examples/gpt-1b/src/model.rs:12-49)."""
+
+    vocab_size: int
+    d_model: int
+    num_layers: int
+    num_heads: int
+    d_ff: int
+    max_seq_len: int
+    dropout: float = 0.1
+
+    @staticmethod
+    def gpt_1b() -> "GptConfig":
+        """The reference's ~1B configuration (model.rs:25-37)."""
+        return GptConfig(50257, 2048, 24, 32, 8192, 2048, 0.1)
+
+    @staticmethod
+    def test_config() -> "GptConfig":
+        """The reference's small CPU configuration (model.rs:39-49)."""
+        return GptConfig(1000, 128, 2, 4, 512, 64, 0.1)
+
+    @staticmethod
+    def gpt_1b_bench() -> "GptConfig":
+        """GPT-1B training benchmark shape: 24 layers, d 2048, 16 heads, d_ff 8192,
+        vocab 50304, seq 2048 (dropout off)."""
+        return GptConfig(50304, 2048, 24, 16, 8192, 2048, 0.0)
+
+    @staticmethod
+    def gpt_6_7b() -> "GptConfig":
+        """GPT-3 style 6.7B: 32 layers, d 4096, 32 heads, d_ff 16384, vocab 50304."""
+        return GptConfig(50304, 4096, 32, 32, 16384, 2048, 0.0)
+
+    @staticmethod
+    def example_tiny() -> "GptConfig":
+        """Tiny CPU example: 2 layers, d 128, 4 heads, d_ff 512, vocab 1024, seq 64."""
+        return GptConfig(1024, 128, 2, 4, 512, 64, 0.1)
+
+    def num_params(self) -> int:
+        d, f, V, S, L = self.d_model, self.d_ff, self.vocab_size, self.max_seq_len, self.num_layers
+        block = 4 * (d * d + d) + (d * f + f) + (f * d + d) + 4 * d
+        return V * d + S * d + L * block + 2 * d + (d * V + V)
+
+    def train_flops_per_token(self, seq_len: Optional[int] = None) -> float:
+        """6 x GEMM parameters + causal attention (fwd+bwd), per token."""
+        S = seq_len or self.max_seq_len
+        d, f, V, L = self.d_model, self.d_ff, self.vocab_size, self.num_layers
+        gemm = L * (4 * d * d + 2 * d * f) + d * V
+        attn = L * 2 * 2 * S * d * 0.5  # QK^T and PV, causal half
+        return 6.0 * gemm + 3.0 * attn
+
+
+class LayerNorm(nn.Module):
+    def __init__(self, d: int, eps: float = 1e-5):
+        super().__init__()
+        self.gamma = nn.Parameter(torch.ones(d))
+        self.beta = nn.Parameter(torch.zeros(d))
+        self.eps = eps
+
+    def forward(self, x):
+        return F.layer_norm(x, (x.shape[-1],), self.gamma.to(x.dtype), self.beta.to(x.dtype), self.eps)
+
+
+class Linear(nn.Module):
+    def __init__(self, d_in: int, d_out: int, bias: bool = True):
+        super().__init__()
+        self.weight = nn.Parameter(torch.empty(d_out, d_in))
+        self.bias = nn.Parameter(torch.empty(d_out)) if bias else None
+        bound = 1.0 / math.sqrt(d_in)
+        nn.init.uniform_(self.weight, -bound, bound)
+        if self.bias is not None:
+            nn.init.uniform_(self.bias, -bound, bound)
+
+    def forward(self, x):
+        return F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
+
+
+class Embedding(nn.Module):
+    def __init__(self, n: int, d: int):
+        super().__init__()
+        self.weight = nn.Parameter(torch.randn(n, d))
+
+    def forward(self, ids):
+        return F.embedding(ids, self.weight)
+
+
+def create_causal_mask(seq_len: int, device=None, dtype=torch.float32) -> torch.Tensor:
+    """[S, S] additive mask: 0 on and below the diagonal, -inf above
+    (reference create_causal_mask, transformer.rs:163-171)."""
+    m = torch.zeros(seq_len, seq_len, device=device, dtype=dtype)
+    return m.masked_fill(torch.ones(seq_len, seq_len, dtype=torch.bool, device=device).triu(1), float("-inf"))
+
+
+def create_position_ids(batch_size: int, seq_len: int, device=None) -> torch.Tensor:
+    return torch.arange(seq_len, device=device).unsqueeze(0).expand(batch_size, seq_len)
+
+
+class _ParamView:
+    """A contiguous run of flat-buffer parameters seen as one matrix/vector."""
+
+    def __init__(self, members, flat, shape):
+        self.members = members
+        self.data = flat.contiguous_view(members, "master").view(shape)
+        self.w16 = flat.contiguous_view(members, "w16").view(shape)
+        self.main_grad = flat.contiguous_view(members, "grad").view(shape)
+        self.shape = shape
+
+
+class MultiHeadAttention(nn.Module):
+    def __init__(self, d_model: int, num_heads: int, dropout: float = 0.1):
+        super().__init__()
+        assert d_model % num_heads == 0, f"d_model ({d_model}) must be divisible by num_heads ({num_heads})"
+        self.q_proj = Linear(d_model, d_model)
+        self.k_proj = Linear(d_model, d_model)
+        self.v_proj = Linear(d_model, d_model)
+        self.out_proj = Linear(d_model, d_model)
+        self.dropout = nn.Dropout(dropout)
+        self.num_heads = num_heads
+        self.d_head = d_model // num_heads
+        self.d_model = d_model
+
+    def forward(self, x, mask: Optional[torch.Tensor] = None):
+        B, S, _ = x.shape
+        q = self.q_proj(x).reshape(B, S, self.num_heads, self.d_head).transpose(1, 2)
+        k = self.k_proj(x).reshape(B, S, self.num_heads, self.d_head).transpose(1, 2)
+        v = self.v_proj(x).reshape(B, S, self.num_heads, self.d_head).transpose(1, 2)
+        scores = q.matmul(k.transpose(2, 3)) * (1.0 / math.sqrt(self.d_head))
+        if mask is not None:
+            scores = scores + mask.to(scores.dtype)
+        attn = self.dropout(torch.softmax(scores, dim=3))
+        out = attn.matmul(v).transpose(1, 2).reshape(B, S, self.d_model)
+        return self.out_proj(out)
+
+
+class FeedForward(nn.Module):
+    def __init__(self, d_model: int, d_ff: int, dropout: float = 0.1):
+        super().__init__()
+        self.linear1 = Linear(d_model, d_ff)
+        self.linear2 = Linear(d_ff, d_model)
+        self.dropout = nn.Dropout(dropout)
+
+    def forward(self, x):
+        return self.linear2(self.dropout(F.gelu(self.linear1(x))))
+
+
+class TransformerBlock(nn.Module):
+    def __init__(self, d_model: int, num_heads: int, d_ff: int, dropout: float = 0.1):
+        super().__init__()
+        self.attention = MultiHeadAttention(d_model, num_heads, dropout)
+        self.ff = FeedForward(d_model, d_ff, dropout)
+        self.norm1 = LayerNorm(d_model)
+        self.norm2 = LayerNorm(d_model)
+        self.dropout = nn.Dropout(dropout)
+
+    def forward(self, x, mask: Optional[torch.Tensor] = None):
+        x = self.dropout(self.attention(self.norm1(x), mask)) + x
+        return self.dropout(self.ff(self.norm2(x))) + x
+
+    # ---------------------------------------------------------------- fused path
+    def fused_forward(self, x2d, B: int, S: int):
+        from ..ops.attention import causal_attention
+        from ..ops.fused import LayerNormFn, LinearFn, MLPFn
+
+        a = self.attention
+        h = LayerNormFn.apply(x2d, (self.norm1.gamma, self.norm1.beta), self.norm1.eps)
+        qkv = LinearFn.apply(h, None, (self._qkv_w, self._qkv_b))
+        o = causal_attention(qkv, B, S, a.num_heads, a.d_head)
+        x2d = LinearFn.apply(o, x2d, (a.out_proj.weight, a.out_proj.bias))
+        h = LayerNormFn.apply(x2d, (self.norm2.gamma, self.norm2.beta), self.norm2.eps)
+        return MLPFn.apply(h, x2d, (self.ff.linear1.weight, self.ff.linear1.bias,
+                                    self.ff.linear2.weight, self.ff.linear2.bias))
+
+
+class GptModel(nn.Module):
+    """Reference: GptModel (examples/gpt-1b/src/model.rs:56-129)."""
+
+    def __init__(self, config: GptConfig, init: str = "reference"):
+        super().__init__()
+        c = config
+        self.config = c
+        self.token_embedding = Embedding(c.vocab_size, c.d_model)
+        self.position_embedding = Embedding(c.max_seq_len, c.d_model)
+        self.blocks = nn.ModuleList(
+            [TransformerBlock(c.d_model, c.num_heads, c.d_ff, c.dropout) for _ in range(c.num_layers)])
+        self.ln_f = LayerNorm(c.d_model)
+        self.lm_head = Linear(c.d_model, c.vocab_size)
+        self.dropout = nn.Dropout(c.dropout)
+        self.d_model = c.d_model
+        self.max_seq_len = c.max_seq_len
+        self.vocab_size = c.vocab_size
+        self.flat = None
+        if init == "normal":
+            self.init_normal_(0.02)
+
+    @torch.no_grad()
+    def init_normal_(self, std: float = 0.02, generator: Optional[torch.Generator] = None):
+        """N(0, std) weights, zero biases, unit LayerNorm gains."""
+        for name, p in self.named_parameters():
+            if name.endswith("gamma"):
+                p.fill_(1.0)
+            elif name.endswith("beta") or name.endswith("bias"):
+                p.zero_()
+            else:
+                p.normal_(0.0, std, generator=generator)
+
+    def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        B, S = input_ids.shape
+        dev = input_ids.device
+        hidden = self.token_embedding(input_ids) + self.position_embedding(create_position_ids(B, S, dev))
+        hidden = self.dropout(hidden)
+        mask = create_causal_mask(S, dev).reshape(1, 1, S, S)
+        for blk in self.blocks:
+            hidden = blk(hidden, mask)
+        return self.lm_head(self.ln_f(hidden))
+
+    # ---------------------------------------------------------------- fused path
+    def flat_groups(self) -> List[List[nn.Parameter]]:
+        """Parameter layout for the flat buffers: q/k/v weights (and biases) back to back."""
+        groups = [[self.token_embedding.weight], [self.position_embedding.weight]]
+        for blk in self.blocks:
+            a = blk.attention
+            groups += [[blk.norm1.gamma, blk.norm1.beta],
+                       [a.q_proj.weight, a.k_proj.weight, a.v_proj.weight],
+                       [a.q_proj.bias, a.k_proj.bias, a.v_proj.bias],
+                       [a.out_proj.weight], [a.out_proj.bias],
+                       [blk.norm2.gamma, blk.norm2.beta],
+                       [blk.ff.linear1.weight], [blk.ff.linear1.bias],
+                       [blk.ff.linear2.weight], [blk.ff.linear2.bias]]
+        groups += [[self.ln_f.gamma, self.ln_f.beta], [self.lm_head.weight], [self.lm_head.bias]]
+        return groups
+
+    def flatten(self, device, grad_dtype=torch.float32):
+        """Move parameters into flat fp32/bf16/grad buffers on `device` (fused path)."""
+        from ..parallel.flat import FlatParams
+
+        self.flat = FlatParams(self.flat_groups(), device, grad_dtype=grad_dtype)
+        d = self.d_model
+        for blk in self.blocks:
+            a = blk.attention
+            blk._qkv_w = _ParamView([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], self.flat, (3 * d, d))
+            blk._qkv_b = _ParamView([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], self.flat, (3 * d,))
+        return self.flat
+
+    def fused_hidden(self, input_ids: torch.Tensor) -> torch.Tensor:
+        from ..ops.fused import EmbeddingFn, LayerNormFn
+
+        assert self.flat is not None, "call flatten(device) before using the fused path"
+        B, S = input_ids.shape
+        x = EmbeddingFn.apply(input_ids, (self.token_embedding.weight, self.position_embedding.weight), S)
+        for blk in self.blocks:
+            x = blk.fused_forward(x, B, S)
+        return LayerNormFn.apply(x, (self.ln_f.gamma, self.ln_f.beta), self.ln_f.eps)
+
+    def fused_loss(self, input_ids: torch.Tensor, targets: torch.Tensor,
+                   grad_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Mean next-token CE through the fused kernels; backward writes main_grad."""
+        from ..ops.fused import LMHeadLossFn
+
+        h = self.fused_hidden(input_ids)
+        return LMHeadLossFn.apply(h, targets, (self.lm_head.weight, self.lm_head.bias), grad_scale)
+
+
+def cross_entropy_loss(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    """-mean(gather(log_softmax(logits, 1), targets)) over flattened rows
+    (reference cross_entropy_loss, examples/gpt-1b/src/main.rs:32-41)."""
+    V = logits.shape[-1]
+    lp = torch.log_softmax(logits.reshape(-1, V).float(), dim=1)
+    return -lp.gather(1, targets.reshape(-1, 1)).mean()

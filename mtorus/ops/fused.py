@@ -1,0 +1,174 @@
+"""Autograd functions that route the GPT hot path through the sm_100a kernels.
+
+The functions take the *parameters* as non-differentiable arguments (wrapped in
+a tuple) and write parameter gradients straight into each parameter's fp32
+``main_grad`` view of the flat gradient buffer (see ``mtorus.parallel.flat``):
+the wgrad GEMM epilogue stores / accumulates fp32, so there is no bf16 grad
+tensor, no AccumulateGrad kernel and no extra pass before the optimizer.
+
+``FusedGradState.accumulate`` is False on the first micro-batch of a step (the
+kernels overwrite ``main_grad``) and True afterwards (they add into it).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch.autograd import Function
+
+from . import kernels as K
+
+
+class FusedGradState:
+    accumulate: bool = False
+    # called as hook(param_list) after the gradients of those params are final for
+    # this backward pass (used by the data-parallel bucket scheduler)
+    grad_ready_hook = None
+
+
+def _grads_done(*params):
+    hook = FusedGradState.grad_ready_hook
+    if hook is not None:
+        hook([p for p in params if p is not None])
+
+
+class LayerNormFn(Function):
+    """y = LayerNorm(x) with fp32 gamma/beta; reference: Burn LayerNorm (eps 1e-5)."""
+
+    @staticmethod
+    def forward(ctx, x, params, eps):
+        gamma, beta = params
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1])
+        y, mean, rstd = K.layernorm_fwd(x2, gamma.data, beta.data, eps)
+        ctx.save_for_backward(x2, mean, rstd)
+        ctx.params = params
+        return y.view(shp)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, mean, rstd = ctx.saved_tensors
+        gamma, beta = ctx.params
+        dx = K.layernorm_bwd(dy.reshape(x2.shape), x2, gamma.data, mean, rstd, gamma.main_grad,
+                             beta.main_grad, FusedGradState.accumulate)
+        _grads_done(gamma, beta)
+        return dx.view(dy.shape), None, None
+
+
+class LinearFn(Function):
+    """y = x W^T + b (+ residual); reference: Burn Linear (transformer.rs:34-37,84)."""
+
+    @staticmethod
+    def forward(ctx, x, residual, params):
+        w, b = params
+        y = K.gemm(x, w.w16, bias=None if b is None else b.data, residual=residual)
+        ctx.save_for_backward(x)
+        ctx.params = params
+        ctx.has_res = residual is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        w, b = ctx.params
+        dy = dy.contiguous()
+        acc = FusedGradState.accumulate
+        dx = K.gemm(dy, w.w16, b_mn=True)
+        K.gemm(dy, x, out=w.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        if b is not None:
+            K.colsum_(dy, b.main_grad, acc)
+        _grads_done(w, b)
+        return dx, (dy if ctx.has_res else None), None
+
+
+class MLPFn(Function):
+    """out = residual + W2 GELU(W1 h + b1) + b2 with GELU and dGELU fused into the
+    GEMM epilogues (reference FeedForward, transformer.rs:89-110)."""
+
+    @staticmethod
+    def forward(ctx, h, residual, params):
+        w1, b1, w2, b2 = params
+        T = h.shape[0]
+        F = w1.shape[0]
+        pre = torch.empty((T, F), dtype=torch.bfloat16, device=h.device)
+        act = torch.empty_like(pre)
+        K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
+        out = K.gemm(act, w2.w16, bias=b2.data, residual=residual)
+        ctx.save_for_backward(h, pre, act)
+        ctx.params = params
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        h, pre, act = ctx.saved_tensors
+        w1, b1, w2, b2 = ctx.params
+        dout = dout.contiguous()
+        acc = FusedGradState.accumulate
+        # dpre = (dout W2) * gelu'(pre)
+        dpre = K.gemm(dout, w2.w16, b_mn=True, aux=pre)
+        K.gemm(dout, act, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        K.colsum_(dout, b2.main_grad, acc)
+        _grads_done(w2, b2)
+        dh = K.gemm(dpre, w1.w16, b_mn=True)
+        K.gemm(dpre, h, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        K.colsum_(dpre, b1.main_grad, acc)
+        _grads_done(w1, b1)
+        return dh, dout, None
+
+
+class EmbeddingFn(Function):
+    """x = wte[ids] + wpe[pos] (reference model.rs:113-118)."""
+
+    @staticmethod
+    def forward(ctx, ids, params, seq_len):
+        wte, wpe = params
+        x = K.embed_fwd(ids.reshape(-1), wte.w16, wpe.w16, seq_len)
+        ctx.save_for_backward(ids)
+        ctx.params = params
+        ctx.seq_len = seq_len
+        return x
+
+    @staticmethod
+    def backward(ctx, dx):
+        (ids,) = ctx.saved_tensors
+        wte, wpe = ctx.params
+        K.embed_bwd(ids.reshape(-1), dx, wte.main_grad, wpe.main_grad, ctx.seq_len,
+                    FusedGradState.accumulate)
+        _grads_done(wte, wpe)
+        return None, None, None
+
+
+class LMHeadLossFn(Function):
+    """mean CE(lm_head(h), targets) with dlogits computed in the forward kernel
+    (reference cross_entropy_loss, examples/gpt-1b/src/main.rs:32-41).
+
+    grad_scale (device fp32 scalar, optional) multiplies the gradients, e.g. the
+    dynamic loss scale; the returned loss is unscaled."""
+
+    @staticmethod
+    def forward(ctx, h, targets, params, grad_scale):
+        w, b = params
+        T = h.shape[0]
+        logits = K.gemm(h, w.w16, bias=b.data)
+        rows = K.xent_fused(logits, targets.reshape(-1), grad_scale, 1.0 / T, True)
+        ctx.save_for_backward(h, logits)
+        ctx.params = params
+        return rows.mean()
+
+    @staticmethod
+    def backward(ctx, gloss):
+        h, dlogits = ctx.saved_tensors
+        w, b = ctx.params
+        acc = FusedGradState.accumulate
+        g = gloss.reshape(1).float().contiguous()
+        dh = K.gemm(dlogits, w.w16, b_mn=True, alpha=g)
+        K.gemm(dlogits, h, out=w.main_grad, a_mn=True, b_mn=True, accumulate=acc, alpha=g)
+        if acc:
+            tmp = torch.zeros_like(b.main_grad)
+            K.colsum_(dlogits, tmp, False)
+            b.main_grad.add_(tmp * g)
+        else:
+            K.colsum_(dlogits, b.main_grad, False)
+            b.main_grad.mul_(g)
+        _grads_done(w, b)
+        return dh, None, None, None

@@ -1,0 +1,91 @@
+"""Thin Python wrappers over the sm_100a kernels of ``mtorus._cuda``.
+
+Each wrapper allocates outputs with torch's caching allocator and launches on
+the current stream.  None of them falls back to eager PyTorch: on a CUDA tensor
+the extension must be present (``mtorus._ext.cuda`` raises otherwise).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .._ext import cuda as _cuda
+
+
+def layernorm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5):
+    """bf16 LayerNorm over the last dim with fp32 gamma/beta -> (y, mean, rstd)."""
+    return _cuda().layernorm_fwd(x.contiguous(), gamma, beta, float(eps))
+
+
+def layernorm_bwd(dy, x, gamma, mean, rstd, dgamma, dbeta, accumulate: bool):
+    """Returns dx; writes (accumulate=False) or adds dgamma/dbeta (fp32)."""
+    return _cuda().layernorm_bwd(dy.contiguous(), x, gamma, mean, rstd, dgamma, dbeta, bool(accumulate))
+
+
+def xent_fused(logits: torch.Tensor, targets: torch.Tensor, grad_scale: Optional[torch.Tensor] = None,
+               scale_mul: float = 1.0, write_grad: bool = True) -> torch.Tensor:
+    """Per-row CE loss; when write_grad, logits are overwritten in place with
+    grad_scale * scale_mul * (softmax - onehot)."""
+    return _cuda().xent_fused(logits, targets, grad_scale, float(scale_mul), bool(write_grad))
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *, a_mn: bool = False,
+         b_mn: bool = False, bias=None, residual=None, act=None, aux=None, alpha=None,
+         accumulate: bool = False, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """tcgen05 GEMM: out[M,N] = epilogue(alpha * A . B^T).
+
+    A is [M,K] (or [K,M] with a_mn=True), B is [N,K] (or [K,N] with b_mn=True).
+    Epilogue: + bias[N] (fp32), + residual[M,N], act <- GELU(out) (out keeps the
+    pre-activation), out *= GELU'(aux) (dGELU), fp32 out with accumulate adds into out.
+    """
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    _cuda().gemm_bf16(a, bool(a_mn), b, bool(b_mn), out, bias, residual, act, aux, alpha, bool(accumulate))
+    return out
+
+
+def gemm_status(reset: bool = True) -> int:
+    """Non-zero when a GEMM launch timed out on an internal wait (status code of the role)."""
+    return int(_cuda().gemm_status(reset))
+
+
+def embed_fwd(ids, wte16, wpe16, seq_len: int):
+    return _cuda().embed_fwd(ids, wte16, wpe16, int(seq_len))
+
+
+def embed_bwd(ids, dy, dwte, dwpe, seq_len: int, accumulate: bool):
+    _cuda().embed_bwd(ids, dy.contiguous(), dwte, dwpe, int(seq_len), bool(accumulate))
+
+
+def bias_gelu_fwd(pre, bias=None):
+    return _cuda().bias_gelu_fwd(pre, bias)
+
+
+def gelu_bwd_(dact, pre):
+    _cuda().gelu_bwd_(dact, pre)
+    return dact
+
+
+def colsum_(x, out, accumulate: bool):
+    _cuda().colsum_(x.contiguous(), out, bool(accumulate))
+    return out
+
+
+def grad_sumsq(g, state):
+    _cuda().optim_grad_sumsq(g, state)
+
+
+def optim_finalize(state, dynamic: bool, growth_interval: int, max_norm: float, unscale: bool = True):
+    _cuda().optim_finalize(state, bool(dynamic), int(growth_interval), float(max_norm), bool(unscale))
+
+
+def adam_step(p, m, v, g, w16, state, lr, beta1=0.9, beta2=0.999, eps=1e-5, weight_decay=0.0, step_override=0.0):
+    _cuda().adam_step(p, m, v, g, w16, state, float(lr), float(beta1), float(beta2), float(eps),
+                      float(weight_decay), float(step_override))
+
+
+def sgd_step(p, g, w16, state, lr):
+    _cuda().sgd_step(p, g, w16, state, float(lr))

@@ -1,0 +1,91 @@
+"""GptTrainer: the end-to-end public training API of the fused B200 path.
+
+    trainer = GptTrainer(GptConfig.gpt_1b_bench(), device="cuda:0")
+    loss = trainer.train_step(input_ids_cpu, targets_cpu)   # host tensors in, float out
+
+One step = H2D copy of the batch (pinned, non-blocking) -> fused forward/backward
+(gradients land in the flat fp32 buffer) -> data-parallel bucket reduction
+overlapped with backward (when a process group is given) -> device-resident
+optimizer (norm, overflow, loss scale, clip, Adam) -> D2H read of the loss.
+
+This is the executable form of the reference's training path
+(examples/gpt-1b/src/main.rs:96-115 and crates/mt-training/src/step.rs:114-180),
+with the gradient all-reduce the reference leaves out.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ..models.gpt import GptConfig, GptModel
+from ..ops.fused import FusedGradState
+from .fused_optim import DeviceLossScaleConfig, FusedAdam
+
+
+class GptTrainer:
+    def __init__(self, config: GptConfig, device="cuda", lr: float = 3e-4, init: str = "normal",
+                 seed: int = 0, dp_group=None, dp: str = "nccl", bucket_mb: float = 25.0,
+                 loss_scale: Optional[DeviceLossScaleConfig] = None, max_grad_norm: float = 0.0,
+                 weight_decay: float = 0.0, warmup_steps: int = 0):
+        self.config = config
+        self.device = torch.device(device)
+        torch.manual_seed(seed)
+        with torch.device(self.device):
+            self.model = GptModel(config, init="reference")
+        if init == "normal":
+            g = torch.Generator(device=self.device)
+            g.manual_seed(seed)
+            self.model.init_normal_(0.02, generator=g)
+        self.flat = self.model.flatten(self.device)
+        self.opt = FusedAdam(self.flat, lr=lr, max_grad_norm=max_grad_norm, weight_decay=weight_decay,
+                             loss_scale=loss_scale or DeviceLossScaleConfig())
+        self.lr = lr
+        self.warmup_steps = warmup_steps
+        self.global_step = 0
+        self.reducer = None
+        if dp_group is not None or (torch.distributed.is_initialized() and torch.distributed.get_world_size() > 1):
+            if dp == "nccl":
+                from ..parallel.data_parallel import NcclBucketReducer
+
+                self.reducer = NcclBucketReducer(self.flat, dp_group, int(bucket_mb * 1024 * 1024))
+            elif dp == "symm":
+                from ..parallel.symm import SymmBucketReducer
+
+                self.reducer = SymmBucketReducer(self.flat, dp_group, int(bucket_mb * 1024 * 1024))
+            else:
+                raise ValueError(f"unknown dp reducer {dp!r}")
+        self._ids = None
+        self._tgt = None
+        self._loss_host = torch.empty((), dtype=torch.float32).pin_memory() if torch.cuda.is_available() else None
+
+    def current_lr(self) -> float:
+        """Linear warmup (reference step.rs:146-150), then constant."""
+        if self.warmup_steps > 0 and self.global_step < self.warmup_steps:
+            return self.lr * (self.global_step + 1) / self.warmup_steps
+        return self.lr
+
+    def step_device(self, ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One full training step on device tensors; returns the device loss (no sync)."""
+        FusedGradState.accumulate = False
+        FusedGradState.grad_ready_hook = self.reducer.on_ready if self.reducer is not None else None
+        loss = self.model.fused_loss(ids, targets, grad_scale=self.opt.loss_scale_tensor)
+        loss.backward()
+        if self.reducer is not None:
+            self.reducer.finish()
+        FusedGradState.grad_ready_hook = None
+        self.opt.step(self.current_lr())
+        self.global_step += 1
+        return loss.detach()
+
+    def train_step(self, input_ids: torch.Tensor, targets: torch.Tensor) -> float:
+        """Host batch in (ideally pinned), host loss out."""
+        if self._ids is None or self._ids.shape != input_ids.shape:
+            self._ids = torch.empty(input_ids.shape, dtype=torch.long, device=self.device)
+            self._tgt = torch.empty(targets.shape, dtype=torch.long, device=self.device)
+        self._ids.copy_(input_ids, non_blocking=True)
+        self._tgt.copy_(targets, non_blocking=True)
+        loss = self.step_device(self._ids, self._tgt)
+        self._loss_host.copy_(loss, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return float(self._loss_host)

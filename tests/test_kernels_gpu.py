@@ -1,0 +1,183 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def K():
+    from mtorus.ops import kernels
+
+    return kernels
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("M,N,Kd", [(128, 256, 64), (256, 512, 128), (200, 136, 72), (1000, 1032, 520),
+                                    (4096, 2048, 2048), (77, 8, 16)])
+@pytest.mark.parametrize("layout", ["tn", "dgrad", "wgrad"])
+def test_gemm_layouts(K, M, N, Kd, layout):
+    torch.manual_seed(0)
+    dev = "cuda"
+    A = torch.randn(M, Kd, device=dev).bfloat16()
+    B = torch.randn(N, Kd, device=dev).bfloat16()
+    ref = A.float() @ B.float().t()
+    if layout == "tn":
+        out = K.gemm(A, B)
+    elif layout == "dgrad":
+        out = K.gemm(A, B.t().contiguous(), b_mn=True)
+    else:
+        out = K.gemm(A.t().contiguous(), B.t().contiguous(), a_mn=True, b_mn=True)
+    torch.cuda.synchronize()
+    assert K.gemm_status() == 0
+    assert _rel(out, ref) < 1e-2, (layout, _rel(out, ref))
+
+
+def test_gemm_epilogues(K):
+    torch.manual_seed(1)
+    M, N, Kd = 384, 520, 256
+    A = torch.randn(M, Kd, device="cuda").bfloat16()
+    B = torch.randn(N, Kd, device="cuda").bfloat16() * 0.1
+    bias = torch.randn(N, device="cuda")
+    res = torch.randn(M, N, device="cuda").bfloat16()
+    base = A.float() @ B.float().t()
+    # bias + residual
+    out = K.gemm(A, B, bias=bias, residual=res)
+    assert _rel(out, base + bias + res.float()) < 1e-2
+    # gelu: out = pre, act = gelu(pre)
+    act = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    pre = K.gemm(A, B, bias=bias, act=act)
+    assert _rel(pre, base + bias) < 1e-2
+    assert _rel(act, F.gelu(pre.float())) < 1e-2
+    # dgelu via aux
+    aux = torch.randn(M, N, device="cuda").bfloat16()
+    x = aux.float().requires_grad_()
+    F.gelu(x).backward(torch.ones_like(x))
+    out = K.gemm(A, B, aux=aux)
+    assert _rel(out, base * x.grad) < 1e-2
+    # fp32 out, accumulate, alpha
+    D = torch.randn(M, N, device="cuda")
+    D0 = D.clone()
+    alpha = torch.tensor([0.5], device="cuda")
+    K.gemm(A, B, out=D, accumulate=True, alpha=alpha)
+    assert _rel(D, D0 + 0.5 * base) < 1e-3
+    torch.cuda.synchronize()
+    assert K.gemm_status() == 0
+
+
+@pytest.mark.parametrize("rows,d", [(1, 128), (37, 2048), (300, 1000), (64, 4096), (513, 768)])
+def test_layernorm(K, rows, d):
+    torch.manual_seed(2)
+    x = torch.randn(rows, d, device="cuda").bfloat16()
+    g = torch.randn(d, device="cuda")
+    b = torch.randn(d, device="cuda")
+    y, mean, rstd = K.layernorm_fwd(x, g, b, 1e-5)
+    xr = x.float().requires_grad_()
+    gr = g.clone().requires_grad_()
+    br = b.clone().requires_grad_()
+    yr = F.layer_norm(xr, (d,), gr, br, 1e-5)
+    assert _rel(y, yr) < 1e-2
+    dy = torch.randn(rows, d, device="cuda").bfloat16()
+    yr.backward(dy.float())
+    dg = torch.zeros(d, device="cuda")
+    db = torch.zeros(d, device="cuda")
+    dx = K.layernorm_bwd(dy, x, g, mean, rstd, dg, db, False)
+    assert _rel(dx, xr.grad) < 2e-2
+    assert _rel(dg, gr.grad) < 1e-2
+    assert _rel(db, br.grad) < 1e-3
+    # accumulate
+    K.layernorm_bwd(dy, x, g, mean, rstd, dg, db, True)
+    assert _rel(db, 2 * br.grad) < 1e-3
+
+
+@pytest.mark.parametrize("T,V", [(4, 1000), (64, 50304), (7, 1003)])
+def test_xent(K, T, V):
+    torch.manual_seed(3)
+    logits = (torch.randn(T, V, device="cuda") * 3).bfloat16()
+    tgt = torch.randint(0, V, (T,), device="cuda")
+    lf = logits.float().requires_grad_()
+    ref = F.cross_entropy(lf, tgt)
+    ref.backward()
+    lg = logits.clone()
+    rows = K.xent_fused(lg, tgt, None, 1.0 / T, True)
+    assert abs(rows.mean().item() - ref.item()) < 1e-3 * max(1, abs(ref.item()))
+    assert _rel(lg, lf.grad) < 2e-2
+
+
+def test_embedding(K):
+    torch.manual_seed(4)
+    V, S, d, B = 500, 64, 256, 3
+    wte = torch.randn(V, d, device="cuda").bfloat16()
+    wpe = torch.randn(S, d, device="cuda").bfloat16()
+    ids = torch.randint(0, V, (B, S), device="cuda")
+    x = K.embed_fwd(ids.reshape(-1), wte, wpe, S)
+    ref = (wte.float()[ids] + wpe.float()[None]).reshape(-1, d)
+    assert _rel(x, ref) < 1e-2
+    dy = torch.randn(B * S, d, device="cuda").bfloat16()
+    dwte = torch.zeros(V, d, device="cuda")
+    dwpe = torch.zeros(S, d, device="cuda")
+    K.embed_bwd(ids.reshape(-1), dy, dwte, dwpe, S, False)
+    rt = torch.zeros(V, d, device="cuda").index_add_(0, ids.reshape(-1), dy.float())
+    assert _rel(dwte, rt) < 1e-4
+    assert _rel(dwpe, dy.float().view(B, S, d).sum(0)) < 1e-4
+
+
+def test_gelu_and_colsum(K):
+    pre = torch.randn(33, 1024, device="cuda").bfloat16()
+    bias = torch.randn(1024, device="cuda")
+    p2 = pre.clone()
+    act = K.bias_gelu_fwd(p2, bias)
+    assert _rel(p2, pre.float() + bias) < 1e-2
+    assert _rel(act, F.gelu(p2.float())) < 1e-2
+    out = torch.zeros(1024, device="cuda")
+    K.colsum_(pre, out, False)
+    assert _rel(out, pre.float().sum(0)) < 1e-4
+
+
+def test_adam_matches_reference(K):
+    torch.manual_seed(5)
+    n = 10007
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda") * 8.0  # gradients scaled by a loss scale of 8
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    w16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    st = torch.zeros(16, device="cuda")
+    st[2] = 8.0
+    pr, mr, vr = p.clone(), m.clone(), v.clone()
+    for step in range(1, 4):
+        K.grad_sumsq(g, st)
+        K.optim_finalize(st, True, 2, 0.0, True)
+        K.adam_step(p, m, v, g, w16, st, 1e-2, 0.9, 0.999, 1e-5, 0.0)
+        # reference (scale is 8 for steps 1-2 then doubles after growth_interval=2)
+        scale = 8.0 if step <= 2 else 16.0
+        gu = g / scale
+        mr = 0.9 * mr + 0.1 * gu
+        vr = 0.999 * vr + 0.001 * gu * gu
+        pr = pr - 1e-2 / (1 - 0.9 ** step) * mr / (vr.sqrt() / math.sqrt(1 - 0.999 ** step) + 1e-5)
+    torch.cuda.synchronize()
+    assert (p - pr).abs().max().item() < 1e-5
+    assert _rel(w16, p) < 1e-2
+    assert st[2].item() == 16.0  # scale doubled once after 2 clean steps
+
+
+def test_overflow_skips_and_halves(K):
+    p = torch.ones(64, device="cuda")
+    g = torch.ones(64, device="cuda")
+    g[3] = float("inf")
+    m = torch.zeros(64, device="cuda")
+    v = torch.zeros(64, device="cuda")
+    st = torch.zeros(16, device="cuda")
+    st[2] = 4.0
+    K.grad_sumsq(g, st)
+    K.optim_finalize(st, True, 100, 0.0, True)
+    K.adam_step(p, m, v, g, None, st, 1e-2)
+    torch.cuda.synchronize()
+    assert torch.all(p == 1.0)
+    assert st[2].item() == 2.0 and st[5].item() == 1.0
