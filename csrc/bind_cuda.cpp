@@ -37,6 +37,7 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
                const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
                const c10::optional<at::Tensor>& alpha, bool beta);
 int64_t gemm_status(bool reset);
+void install_segv_handler();
 }  // namespace mtorus
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -62,5 +63,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("act") = py::none(), py::arg("aux") = py::none(), py::arg("alpha") = py::none(),
         py::arg("beta") = false);
   m.def("gemm_status", &gemm_status, py::arg("reset") = true);
+  m.def("install_segv_handler", &install_segv_handler);
   m.def("launch_count", []() { return mtorus::launch_counter(); });
 }

@@ -327,6 +327,16 @@ EncodeTiledFn get_encode_tiled() {
   return fn;
 }
 
+// Driver-API calls (the tensor-map encoder) need a current context on the
+// calling thread.  Runtime calls create it lazily, and a thread such as the
+// autograd worker may not have made one yet (its allocations can all come from
+// torch's cache), so bind the device's primary context explicitly.
+void ensure_context() {
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  C10_CUDA_CHECK(cudaSetDevice(dev));
+}
+
 // 2-D row-major tensor [outer, inner] with row stride `ld` elements; 128B swizzle.
 CUtensorMap make_tma_2d(const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                         uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer,
@@ -389,6 +399,7 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
   TORCH_CHECK(reinterpret_cast<uintptr_t>(D.data_ptr()) % 16 == 0 && (D.stride(0) % 8) == 0,
               "gemm_bf16: D alignment");
   if (M == 0 || N == 0) return;
+  ensure_context();
   if (K == 0) {
     if (!beta) D.zero_();
     return;

@@ -275,11 +275,12 @@ class GptModel(nn.Module):
         return self.flat
 
     def fused_hidden(self, input_ids: torch.Tensor) -> torch.Tensor:
-        from ..ops.fused import EmbeddingFn, LayerNormFn
+        from ..ops.fused import EmbeddingFn, LayerNormFn, grad_anchor
 
         assert self.flat is not None, "call flatten(device) before using the fused path"
         B, S = input_ids.shape
-        x = EmbeddingFn.apply(input_ids, (self.token_embedding.weight, self.position_embedding.weight), S)
+        x = EmbeddingFn.apply(input_ids, grad_anchor(input_ids.device),
+                              (self.token_embedding.weight, self.position_embedding.weight), S)
         for blk in self.blocks:
             x = blk.fused_forward(x, B, S)
         return LayerNormFn.apply(x, (self.ln_f.gamma, self.ln_f.beta), self.ln_f.eps)

@@ -116,11 +116,23 @@ class MLPFn(Function):
         return dh, dout, None
 
 
+_ANCHOR = {}
+
+
+def grad_anchor(device) -> torch.Tensor:
+    """An empty leaf that requires grad: makes the embedding output part of the
+    autograd graph although its only tensor input (token ids) is integer."""
+    key = str(device)
+    if key not in _ANCHOR:
+        _ANCHOR[key] = torch.empty(0, device=device, requires_grad=True)
+    return _ANCHOR[key]
+
+
 class EmbeddingFn(Function):
     """x = wte[ids] + wpe[pos] (reference model.rs:113-118)."""
 
     @staticmethod
-    def forward(ctx, ids, params, seq_len):
+    def forward(ctx, ids, anchor, params, seq_len):
         wte, wpe = params
         x = K.embed_fwd(ids.reshape(-1), wte.w16, wpe.w16, seq_len)
         ctx.save_for_backward(ids)
@@ -135,7 +147,7 @@ class EmbeddingFn(Function):
         K.embed_bwd(ids.reshape(-1), dx, wte.main_grad, wpe.main_grad, ctx.seq_len,
                     FusedGradState.accumulate)
         _grads_done(wte, wpe)
-        return None, None, None
+        return None, None, None, None
 
 
 class LMHeadLossFn(Function):

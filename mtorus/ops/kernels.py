@@ -6,11 +6,15 @@ the extension must be present (``mtorus._ext.cuda`` raises otherwise).
 """
 from __future__ import annotations
 
+import os
+import sys
 from typing import Optional
 
 import torch
 
 from .._ext import cuda as _cuda
+
+_TRACE = bool(os.environ.get("MTORUS_TRACE"))
 
 
 def layernorm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5):
@@ -43,6 +47,11 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
     N = b.shape[1] if b_mn else b.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    if _TRACE:
+        print(f"[gemm] A{tuple(a.shape)}{tuple(a.stride())} a_mn={a_mn} B{tuple(b.shape)}{tuple(b.stride())} "
+              f"b_mn={b_mn} out{tuple(out.shape)} {out.dtype} bias={bias is not None} res={residual is not None} "
+              f"act={act is not None} aux={aux is not None} alpha={alpha is not None} acc={accumulate}",
+              file=sys.stderr, flush=True)
     _cuda().gemm_bf16(a, bool(a_mn), b, bool(b_mn), out, bias, residual, act, aux, alpha, bool(accumulate))
     return out
 

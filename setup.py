@@ -18,6 +18,12 @@ from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtensio
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
+# Link the shared system libstdc++ explicitly: the toolchain's search path can
+# otherwise resolve -lstdc++ to a static archive, and a second, private copy of
+# libstdc++ inside the extension breaks iostream/locale state shared with torch.
+_LIBSTDCXX = "/usr/lib/x86_64-linux-gnu/libstdc++.so.6"
+_LINK = [_LIBSTDCXX] if os.path.exists(_LIBSTDCXX) else []
+
 
 def _rel(paths):
     return sorted(os.path.relpath(p, ROOT) for p in paths)
@@ -54,13 +60,14 @@ ext_modules = [
         sources=host_sources,
         include_dirs=[os.path.join(ROOT, "csrc")],
         extra_compile_args={"cxx": common_cxx + ["-pthread"]},
-        extra_link_args=["-pthread"],
+        extra_link_args=["-pthread"] + _LINK,
     ),
     CUDAExtension(
         name="mtorus._cuda",
         sources=cuda_sources,
         include_dirs=[os.path.join(ROOT, "csrc")],
         extra_compile_args={"cxx": common_cxx, "nvcc": nvcc_flags},
+        extra_link_args=_LINK,
     ),
 ]
 

@@ -28,6 +28,8 @@ def test_gemm_layouts(K, M, N, Kd, layout):
     A = torch.randn(M, Kd, device=dev).bfloat16()
     B = torch.randn(N, Kd, device=dev).bfloat16()
     ref = A.float() @ B.float().t()
+    if layout == "wgrad" and M % 8:
+        pytest.skip("MN-major A needs M % 8 == 0 (16-byte TMA row stride)")
     if layout == "tn":
         out = K.gemm(A, B)
     elif layout == "dgrad":

@@ -27,7 +27,9 @@ def test_fused_loss_and_grads_match_reference():
     assert abs(loss.item() - loss_ref.item()) < 2e-2
     worst = 0.0
     for (n, pr), (_, pf) in zip(ref.named_parameters(), fused.named_parameters()):
-        rel = ((pf.main_grad - pr.grad).norm() / (pr.grad.norm() + 1e-8)).item()
+        # the key bias has an exactly-zero true gradient (softmax shift invariance), so
+        # normalise by the larger of the grad norm and a small absolute floor
+        rel = ((pf.main_grad - pr.grad).norm() / max(pr.grad.norm().item(), 1e-2)).item()
         worst = max(worst, rel)
         assert rel < 0.08, (n, rel)
 
