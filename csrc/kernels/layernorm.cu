@@ -320,3 +320,85 @@ at::Tensor layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Te
 }
 
 }  // namespace mtorus
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of layernorm_bwd for callers that cannot allocate
+// device memory (declared in layernorm_noalloc.h, which describes the limits).
+// It launches the same ln_bwd_vec / ln_bwd_finish kernels with their partial-sum
+// scratch in a file-scope device array instead of a torch allocation.
+#include <mutex>
+
+#include "layernorm_noalloc.h"
+
+namespace mtorus {
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+constexpr size_t kNoAllocFloats =
+    (size_t)MTORUS_LN_NOALLOC_MAX_BLOCKS * 2 * MTORUS_LN_NOALLOC_MAX_D;
+
+static __device__ __align__(256) float g_ln_noalloc_scratch[kNoAllocFloats];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Once per device, with that device current: the device address of the array
+// (the host-side name g_ln_noalloc_scratch is only a stand-in, not a device
+// address) and the shared-memory opt-in of the kernels it launches.
+float* noalloc_setup(int dev) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev]) return g_noalloc_ptr[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_ln_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
+  const int smem = 4 * 2 * MTORUS_LN_NOALLOC_MAX_D * (int)sizeof(float);
+  if (cudaFuncSetAttribute(ln_bwd_vec<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(ln_bwd_vec<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(ln_bwd_vec<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(ln_bwd_vec<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+      cudaFuncSetAttribute(ln_bwd_vec<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return nullptr;
+  g_noalloc_ptr[dev] = static_cast<float*>(p);
+  return g_noalloc_ptr[dev];
+}
+
+}  // namespace
+}  // namespace mtorus
+
+extern "C" int mtorus_layernorm_bwd_noalloc(const uint16_t* dy, const uint16_t* x,
+                                            const float* gamma, const float* mean,
+                                            const float* rstd, uint16_t* dx, float* dgamma,
+                                            float* dbeta, int rows, int d, int accumulate,
+                                            cudaStream_t stream) {
+  using namespace mtorus;
+  if (!dy || !x || !gamma || !mean || !rstd || !dx || !dgamma || !dbeta || rows <= 0 || d <= 0 ||
+      d % 8 != 0)
+    return MTORUS_NOALLOC_EARG;
+  for (const void* p : {(const void*)dy, (const void*)x, (const void*)gamma, (const void*)dx})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return MTORUS_NOALLOC_EARG;
+  if (d > MTORUS_LN_NOALLOC_MAX_D) return MTORUS_NOALLOC_ESIZE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
+    return MTORUS_NOALLOC_ESETUP;
+  float* part = noalloc_setup(dev);
+  if (!part) return MTORUS_NOALLOC_ESETUP;
+  const int nch = pick_nch(d);
+  const int wpb = 4;
+  const size_t smem = (size_t)wpb * 2 * d * sizeof(float);
+  const int grid = std::min((rows + wpb - 1) / wpb, MTORUS_LN_NOALLOC_MAX_BLOCKS);
+  const auto* dyp = reinterpret_cast<const bf16*>(dy);
+  const auto* xp = reinterpret_cast<const bf16*>(x);
+  auto* dxp = reinterpret_cast<bf16*>(dx);
+  switch (nch) {
+    case 1: ln_bwd_vec<1><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
+    case 2: ln_bwd_vec<2><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
+    case 4: ln_bwd_vec<4><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
+    case 8: ln_bwd_vec<8><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
+    case 16: ln_bwd_vec<16><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
+    default: return MTORUS_NOALLOC_ESIZE;
+  }
+  if (cudaGetLastError() != cudaSuccess) return MTORUS_NOALLOC_ELAUNCH;
+  ln_bwd_finish<<<(2 * d + 255) / 256, 256, 0, stream>>>(part, dgamma, dbeta, grid, d,
+                                                         accumulate ? 1 : 0);
+  if (cudaGetLastError() != cudaSuccess) return MTORUS_NOALLOC_ELAUNCH;
+  return MTORUS_NOALLOC_OK;
+}
