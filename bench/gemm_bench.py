@@ -1,0 +1,84 @@
+#!/usr/bin/env python
+"""GEMM microbenchmark: the tcgen05 GEMM against cuBLAS (torch.matmul) on the
+GPT-1B training shapes (T = 16384 tokens, d 2048, d_ff 8192, vocab 50304).
+
+    python bench/gemm_bench.py [--shapes small]
+
+Times each case with CUDA events after warm-up (median of --iters), prints
+TFLOP/s and the fraction of the measured bf16 peak (MEASURED_PEAKS.json).
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from mtorus.ops import kernels as K  # noqa: E402
+
+
+def timeit(fn, iters=20, warmup=5):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--json", default=None)
+    args = ap.parse_args()
+    peak = 1607.9
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        peak = json.load(open(p)).get("bf16_tflops", peak)
+    T, d, F, V = 16384, 2048, 8192, 50304
+    cases = [  # name, M, N, K, layout
+        ("qkv_fwd", T, 3 * d, d, "tn"), ("out_fwd", T, d, d, "tn"), ("ffn1_fwd", T, F, d, "tn"),
+        ("ffn2_fwd", T, d, F, "tn"), ("lm_fwd", T, V, d, "tn"),
+        ("ffn1_dgrad", T, d, F, "dgrad"), ("ffn2_dgrad", T, F, d, "dgrad"), ("lm_dgrad", T, d, V, "dgrad"),
+        ("ffn1_wgrad", F, d, T, "wgrad"), ("ffn2_wgrad", d, F, T, "wgrad"), ("qkv_wgrad", 3 * d, d, T, "wgrad"),
+        ("lm_wgrad", V, d, T, "wgrad"), ("square8k", 8192, 8192, 8192, "tn"),
+    ]
+    rows = []
+    for name, M, N, Kd, lay in cases:
+        A = torch.randn(M, Kd, device="cuda").bfloat16() if lay != "wgrad" else torch.randn(Kd, M, device="cuda").bfloat16()
+        if lay == "tn":
+            B = torch.randn(N, Kd, device="cuda").bfloat16()
+            mine = lambda: K.gemm(A, B)
+            ref = lambda: torch.matmul(A, B.t())
+        elif lay == "dgrad":
+            B = torch.randn(Kd, N, device="cuda").bfloat16()
+            mine = lambda: K.gemm(A, B, b_mn=True)
+            ref = lambda: torch.matmul(A, B)
+        else:
+            B = torch.randn(Kd, N, device="cuda").bfloat16()
+            out = torch.empty(M, N, device="cuda")
+            mine = lambda: K.gemm(A, B, out=out, a_mn=True, b_mn=True)
+            ref = lambda: torch.mm(A.t(), B, out_dtype=torch.float32)
+        flops = 2.0 * M * N * Kd
+        tm = timeit(mine, args.iters)
+        tr = timeit(ref, args.iters)
+        r = {"case": name, "M": M, "N": N, "K": Kd, "layout": lay, "mine_ms": round(tm, 4),
+             "cublas_ms": round(tr, 4), "mine_tflops": round(flops / tm / 1e9, 1),
+             "cublas_tflops": round(flops / tr / 1e9, 1), "mine_frac_of_measured_peak": round(flops / tm / 1e9 / peak, 3)}
+        rows.append(r)
+        print(json.dumps(r), flush=True)
+        del A, B
+    if args.json:
+        json.dump(rows, open(args.json, "w"), indent=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -18,6 +18,8 @@
 //   * two TMEM accumulators (2 x 256 columns) so the epilogue of tile i overlaps
 //     the main loop of tile i+1.
 // All mbarrier waits are bounded (see sm100.cuh); a timeout raises the status word.
+#include <cstdlib>
+
 #include "sm100.cuh"
 
 namespace mtorus {
@@ -63,6 +65,74 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   const int r = tile % per_group;
   mb = first_m + r % gsize;
   nb = r / gsize;
+}
+
+// Applies the epilogue to 32 consecutive accumulator columns of row m
+// (columns n0..n0+31) and stores them.
+__device__ __forceinline__ void epilogue_store32(const uint32_t (&r)[32], int m, int n0, int N,
+                                                 float alpha, const GemmEpilogue& ep) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
+  if (ep.bias) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (n0 + i < N) v[i] += ep.bias[n0 + i];
+  }
+  if (ep.aux) {
+    const bf16* ax = ep.aux + (size_t)m * ep.ldaux + n0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (n0 + j * 8 + 8 <= N) {
+        float a8[8];
+        unpack8(reinterpret_cast<const bf16x8*>(ax)[j], a8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j * 8 + i] *= gelu_grad_f(a8[i]);
+      }
+    }
+  }
+  if (ep.out_f32) {
+    float* dp = reinterpret_cast<float*>(ep.D) + (size_t)m * ep.ldd + n0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (n0 + j * 4 + 4 <= N) {
+        float4 o = make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]);
+        if (ep.beta) {
+          const float4 old = reinterpret_cast<float4*>(dp)[j];
+          o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+        }
+        reinterpret_cast<float4*>(dp)[j] = o;
+      }
+    }
+  } else {
+    bf16* dp = reinterpret_cast<bf16*>(ep.D) + (size_t)m * ep.ldd + n0;
+    if (ep.residual) {
+      const bf16* rp = ep.residual + (size_t)m * ep.ldr + n0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (n0 + j * 8 + 8 <= N) {
+          float r8[8];
+          unpack8(reinterpret_cast<const bf16x8*>(rp)[j], r8);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[j * 8 + i] += r8[i];
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (n0 + j * 8 + 8 <= N) {
+        bf16x8 pk = pack8(v + j * 8);
+        reinterpret_cast<bf16x8*>(dp)[j] = pk;
+        if (ep.act) {
+          float p8[8], g8[8];
+          unpack8(pk, p8);  // GELU of the rounded pre-activation
+#pragma unroll
+          for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
+          reinterpret_cast<bf16x8*>(ep.act + (size_t)m * ep.ldact + n0)[j] = pack8(g8);
+        }
+      }
+    }
+  }
 }
 
 struct Smem {
@@ -233,6 +303,221 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         const int n0 = nb * BN + c * 32;
         if (m >= M || n0 >= N) continue;
+        epilogue_store32(r, m, n0, N, alpha, ep);
+      }
+      tc_fence_before();
+      mbar_arrive(&ctl->tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ 2-SM kernel
+//
+// The same GEMM on CTA pairs (cluster of 2, tcgen05 cta_group::2): a pair owns a
+// 256 x 256 output tile, each CTA loads its own 128 rows of A and half of the B
+// tile (128 rows), and the pair leader issues M=256 / N=256 MMAs that read both
+// CTAs' shared memory and write each CTA's 128 accumulator rows into its own
+// TMEM.  Per SM this moves 32 KB of operands per 64-deep k-block instead of
+// 48 KB, which frees shared memory for a 6-stage ring.  Loads of both CTAs
+// complete on the leader's "full" barrier; the leader's commits arrive on both
+// CTAs' "empty" / "accumulator full" barriers; both epilogues arrive on the
+// leader's "accumulator empty" barrier.
+namespace {
+
+constexpr int P_BM = 128;  // rows per CTA (pair tile M = 256)
+constexpr int P_BN = 256;  // pair tile N; each CTA stages 128 rows of B
+constexpr int P_BK = 64;
+constexpr int P_STAGES = 5;
+constexpr int P_GROUP_M = 8;  // pair tiles per raster group along M
+constexpr int P_A_BYTES = P_BM * P_BK * 2;
+constexpr int P_B_BYTES = (P_BN / 2) * P_BK * 2;
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+// Epilogue staging (per epilogue warp): two 32x32 output chunks (fp32 worst case,
+// 4 KB each) and two 32x32 bf16 GELU chunks, written to global memory by TMA.
+constexpr int P_EPI_D_BYTES = 4096, P_EPI_ACT_BYTES = 2048;
+constexpr int P_EPI_BYTES = 4 * 2 * (P_EPI_D_BYTES + P_EPI_ACT_BYTES);
+
+struct PairSmem {
+  uint64_t full[P_STAGES];   // leader: both CTAs' loads of a stage have landed
+  uint64_t empty[P_STAGES];  // each CTA: the MMAs reading a stage are done
+  uint64_t tfull[2];         // each CTA: accumulator buffer ready for the epilogue
+  uint64_t tempty[2];        // leader: both epilogues finished with a buffer
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = P_GROUP_M * num_n;
+  const int group = tile / per_group;
+  const int first_m = group * P_GROUP_M;
+  const int gsize = min(num_m - first_m, P_GROUP_M);
+  const int r = tile % per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+}  // namespace
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_bf16_2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                         const __grid_constant__ CUtensorMap tma_b,
+                         const __grid_constant__ CUtensorMap tma_d,
+                         const __grid_constant__ CUtensorMap tma_act, int M, int N, int K, int a_mn,
+                         int b_mn, GemmEpilogue ep, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* epi_smem = smem + P_STAGES * P_STAGE_BYTES;
+  PairSmem* ctl = reinterpret_cast<PairSmem*>(epi_smem + P_EPI_BYTES);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+  const int num_m = (M + 2 * P_BM - 1) / (2 * P_BM), num_n = (N + P_BN - 1) / P_BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + P_BK - 1) / P_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->tfull[b], 1);
+      mbar_init(&ctl->tempty[b], 2 * 128);
+    }
+    ctl->abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_2sm(&ctl->tmem_base, TMEM_COLS);
+    tmem_relinquish_2sm();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+  volatile int* abort = &ctl->abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+        int mb, nb;
+        pair_tile_coords(tile, num_m, num_n, mb, nb);
+        const int m0 = mb * 2 * P_BM + (int)rank * P_BM;
+        const int n0 = nb * P_BN + (int)rank * (P_BN / 2);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort, status, 11)) break;
+          if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * P_STAGE_BYTES);
+          uint8_t* sa = smem + stage * P_STAGE_BYTES;
+          uint8_t* sb = sa + P_A_BYTES;
+          if (!a_mn) {
+            tma_load_2d_pair(sa, &tma_a, &ctl->full[stage], kb * P_BK, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < P_BM / 64; ++j)
+              tma_load_2d_pair(sa + j * (P_BK * 128), &tma_a, &ctl->full[stage], m0 + j * 64, kb * P_BK);
+          }
+          if (!b_mn) {
+            tma_load_2d_pair(sb, &tma_b, &ctl->full[stage], kb * P_BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < (P_BN / 2) / 64; ++j)
+              tma_load_2d_pair(sb + j * (P_BK * 128), &tma_b, &ctl->full[stage], n0 + j * 64, kb * P_BK);
+          }
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      // ---------------------------------------------------------- MMA issuer (leader)
+      const uint32_t idesc = make_idesc_bf16(2 * P_BM, P_BN, a_mn, b_mn);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t tphase = (local >> 1) & 1;
+        if (!mbar_wait(&ctl->tempty[buf], tphase ^ 1, abort, status, 12)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * P_BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&ctl->full[stage], phase, abort, status, 13)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
+          const uint32_t sb = sa + P_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < P_BK / 16; ++k) {
+            const uint64_t ad = a_mn ? make_sdesc(sa + k * 2048, P_BK * 128, 1024, kSwizzle128B)
+                                     : make_sdesc(sa + k * 32, 16, 1024, kSwizzle128B);
+            const uint64_t bd = b_mn ? make_sdesc(sb + k * 2048, P_BK * 128, 1024, kSwizzle128B)
+                                     : make_sdesc(sb + k * 32, 16, 1024, kSwizzle128B);
+            umma_f16_2sm(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_2sm_mc(&ctl->empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_2sm_mc(&ctl->tfull[buf], 0x3);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    // TMEM -> registers (alpha, bias, dGELU, residual) -> swizzled smem chunk ->
+    // TMA store (or TMA reduce-add for fp32 accumulation).  Two staging buffers
+    // per warp let the math of chunk c overlap the store of chunk c-1.
+    const int q = warp & 3;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&ctl->tempty[0]), 0);
+    const uint32_t tempty_leader1 = mapa_shared(smem_u32(&ctl->tempty[1]), 0);
+    uint8_t* dstage = epi_smem + q * 2 * P_EPI_D_BYTES;
+    uint8_t* astage = epi_smem + 4 * 2 * P_EPI_D_BYTES + q * 2 * P_EPI_ACT_BYTES;
+    const bool f32out = ep.out_f32 != 0;
+    int chunk_count = 0;
+    int local = 0;
+    for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs, ++local) {
+      int mb, nb;
+      pair_tile_coords(tile, num_m, num_n, mb, nb);
+      const int buf = local & 1;
+      const uint32_t tphase = (local >> 1) & 1;
+      if (!mbar_wait(&ctl->tfull[buf], tphase, abort, status, 14)) break;
+      tc_fence_after();
+      const int row0 = mb * 2 * P_BM + (int)rank * P_BM + q * 32;
+      const int m = row0 + lane;
+      const float alpha = ep.alpha ? *ep.alpha : 1.f;
+#pragma unroll 1
+      for (int c = 0; c < P_BN / 32; ++c, ++chunk_count) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * P_BN + c * 32, r);
+        tmem_wait_ld();
+        if (c == P_BN / 32 - 1) {
+          // the whole accumulator buffer is in registers / smem now: release it
+          tc_fence_before();
+          mbar_arrive_cluster(buf ? tempty_leader1 : tempty_leader0);
+        }
+        const int n0 = nb * P_BN + c * 32;
+        if (n0 >= N) continue;  // warp-uniform
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
@@ -241,33 +526,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (n0 + i < N) v[i] += ep.bias[n0 + i];
         }
-        if (ep.aux) {
-          const bf16* ax = ep.aux + (size_t)m * ep.ldaux + n0;
+        if (m < M) {
+          if (ep.aux) {
+            const bf16* ax = ep.aux + (size_t)m * ep.ldaux + n0;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (n0 + j * 8 + 8 <= N) {
-              float a8[8];
-              unpack8(reinterpret_cast<const bf16x8*>(ax)[j], a8);
+            for (int j = 0; j < 4; ++j) {
+              if (n0 + j * 8 + 8 <= N) {
+                float a8[8];
+                unpack8(reinterpret_cast<const bf16x8*>(ax)[j], a8);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) v[j * 8 + i] *= gelu_grad_f(a8[i]);
-            }
-          }
-        }
-        if (ep.out_f32) {
-          float* dp = reinterpret_cast<float*>(ep.D) + (size_t)m * ep.ldd + n0;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (n0 + j * 4 + 4 <= N) {
-              float4 o = make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]);
-              if (ep.beta) {
-                const float4 old = reinterpret_cast<float4*>(dp)[j];
-                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+                for (int i = 0; i < 8; ++i) v[j * 8 + i] *= gelu_grad_f(a8[i]);
               }
-              reinterpret_cast<float4*>(dp)[j] = o;
             }
           }
-        } else {
-          bf16* dp = reinterpret_cast<bf16*>(ep.D) + (size_t)m * ep.ldd + n0;
           if (ep.residual) {
             const bf16* rp = ep.residual + (size_t)m * ep.ldr + n0;
 #pragma unroll
@@ -280,31 +551,55 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
+        }
+        const int sb = chunk_count & 1;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        if (f32out) {
+          // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row r sits at j ^ (r & 7)
+          uint8_t* base = dstage + sb * P_EPI_D_BYTES + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(base + ((j ^ (lane & 7)) << 4)) =
+                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          // 32 rows x 64 B, 64B swizzle: 16-byte chunk j of row r sits at j ^ ((r >> 1) & 3)
+          uint8_t* base = dstage + sb * P_EPI_D_BYTES + lane * 64;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            if (n0 + j * 8 + 8 <= N) {
-              bf16x8 pk = pack8(v + j * 8);
-              reinterpret_cast<bf16x8*>(dp)[j] = pk;
-              if (ep.act) {
-                float p8[8], g8[8];
-                unpack8(pk, p8);  // GELU of the rounded pre-activation
+            const bf16x8 pk = pack8(v + 8 * j);
+            *reinterpret_cast<bf16x8*>(base + ((j ^ ((lane >> 1) & 3)) << 4)) = pk;
+            if (ep.act) {
+              float p8[8], g8[8];
+              unpack8(pk, p8);  // GELU of the rounded pre-activation
 #pragma unroll
-                for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
-                reinterpret_cast<bf16x8*>(ep.act + (size_t)m * ep.ldact + n0)[j] = pack8(g8);
-              }
+              for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
+              *reinterpret_cast<bf16x8*>(astage + sb * P_EPI_ACT_BYTES + lane * 64 +
+                                         ((j ^ ((lane >> 1) & 3)) << 4)) = pack8(g8);
             }
           }
         }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          if (f32out && ep.beta)
+            tma_reduce_add_2d(&tma_d, dstage + sb * P_EPI_D_BYTES, n0, row0);
+          else
+            tma_store_2d(&tma_d, dstage + sb * P_EPI_D_BYTES, n0, row0);
+          if (ep.act) tma_store_2d(&tma_act, astage + sb * P_EPI_ACT_BYTES, n0, row0);
+          bulk_commit_group();
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&ctl->tempty[buf]);
     }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  if (warp == 1) tmem_dealloc_2sm(tmem_base, TMEM_COLS);
 }
 
 // ------------------------------------------------------------------ host side
@@ -435,6 +730,34 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
   }
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto swz = CU_TENSOR_MAP_SWIZZLE_128B;
+  static const bool force_1sm = std::getenv("MTORUS_GEMM_1SM") != nullptr;
+  if (M >= 2 * P_BM && !force_1sm) {
+    // CTA-pair kernel: per-CTA boxes of 128 rows of A and 128 rows of B.
+    CUtensorMap ta = a_mn ? make_tma_2d(A.data_ptr(), dt, 2, M, K, A.stride(0), 64, P_BK, swz)
+                          : make_tma_2d(A.data_ptr(), dt, 2, K, M, A.stride(0), P_BK, P_BM, swz);
+    CUtensorMap tb = b_mn ? make_tma_2d(B.data_ptr(), dt, 2, N, K, B.stride(0), 64, P_BK, swz)
+                          : make_tma_2d(B.data_ptr(), dt, 2, K, N, B.stride(0), P_BK, P_BN / 2, swz);
+    CUtensorMap td = out_f32
+        ? make_tma_2d(D.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, D.stride(0), 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B)
+        : make_tma_2d(D.data_ptr(), dt, 2, N, M, D.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    CUtensorMap tact = act.has_value()
+        ? make_tma_2d(act->data_ptr(), dt, 2, N, M, act->stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+        : td;
+    const int num_tiles = (int)(((M + 2 * P_BM - 1) / (2 * P_BM)) * ((N + P_BN - 1) / P_BN));
+    const int pairs = std::min(num_tiles, num_sms() / 2);
+    const size_t smem = P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + sizeof(PairSmem) + 1024;
+    static bool attr2_set = false;
+    if (!attr2_set) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_2sm_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      attr2_set = true;
+    }
+    gemm_bf16_2sm_kernel<<<2 * pairs, kThreads, smem, cur_stream()>>>(
+        ta, tb, td, tact, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, ep, gemm_status_ptr());
+    MT_LAUNCH_CHECK();
+    return;
+  }
   CUtensorMap ta = a_mn ? make_tma_2d(A.data_ptr(), dt, 2, M, K, A.stride(0), 64, BK, swz)
                         : make_tma_2d(A.data_ptr(), dt, 2, K, M, A.stride(0), BK, BM, swz);
   CUtensorMap tb = b_mn ? make_tma_2d(B.data_ptr(), dt, 2, N, K, B.stride(0), 64, BK, swz)
