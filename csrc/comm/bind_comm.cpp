@@ -81,7 +81,7 @@ void bind_comm(py::module_& m) {
       .value("Min", ReduceOp::Min)
       .value("Max", ReduceOp::Max)
       .value("Mean", ReduceOp::Mean)
-      .def("__str__", [](ReduceOp o) { return std::string(reduce_op_name(o)); });
+      .def("to_string", [](ReduceOp o) { return std::string(reduce_op_name(o)); });
   py::enum_<DType>(m, "DType")
       .value("U64", DType::U64)
       .value("I64", DType::I64)
@@ -94,7 +94,7 @@ void bind_comm(py::module_& m) {
       .value("Broadcast", CollectiveOp::Broadcast)
       .value("AllGather", CollectiveOp::AllGather)
       .value("ReduceScatter", CollectiveOp::ReduceScatter)
-      .def("__str__", [](CollectiveOp o) { return std::string(collective_op_name(o)); });
+      .def("to_string", [](CollectiveOp o) { return std::string(collective_op_name(o)); });
   m.def("reduce_buffers", [](ReduceOp op, const std::vector<std::string>& chunks, DType dt) {
     return B(reduce_buffers(op, chunks, dt));
   });

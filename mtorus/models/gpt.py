@@ -236,6 +236,9 @@ class GptModel(nn.Module):
             else:
                 p.normal_(0.0, std, generator=generator)
 
+    def num_layers(self) -> int:
+        return len(self.blocks)
+
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
         B, S = input_ids.shape
         dev = input_ids.device
