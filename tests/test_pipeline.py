@@ -1,0 +1,255 @@
+"""Parity: crates/mt-pipeline/src/{stage,communicator,schedule/*,executor,checkpoint,placement}.rs tests,
+plus schedule properties (1F1B op lists, bubble fractions, deadlock-free rank programs)."""
+import threading
+
+import pytest
+
+from mtorus.comm import MockCommunicator, local_world, run_threads
+from mtorus.core.precision import Fp8Format
+from mtorus.core.topology import MeshTorusHybrid, TorusCoordinates
+from mtorus.pipeline import (ActivationCheckpoint, CheckpointStrategy, GpipeSchedule, OneF1BSchedule, PipeOp,
+                             PipelineComm, PipelineConfig, PipelineExecutor, PipelineStage, ScheduleType, StageData,
+                             StageForward, StageForwardClosure, apply_checkpoint_forward, build_schedule,
+                             compute_hop_distance, ideal_bubble_fraction, rank_program, simulate_schedule,
+                             topology_aware_placement)
+from mtorus.pipeline.placement import torus_distance
+
+
+class Identity(StageForward):
+    def forward(self, x):
+        return x
+
+    def backward(self, x, g):
+        return g
+
+
+class Scale(StageForward):
+    def __init__(self, f):
+        self.f = f
+
+    def forward(self, x):
+        return StageData([v * self.f for v in x.values], x.rows, x.cols)
+
+    def backward(self, x, g):
+        return StageData([v * self.f for v in g.values], g.rows, g.cols)
+
+
+class Counting(StageForward):
+    def __init__(self):
+        self.fw = 0
+        self.bw = 0
+
+    def forward(self, x):
+        self.fw += 1
+        return x
+
+    def backward(self, x, g):
+        self.bw += 1
+        return g
+
+
+# ---------------------------------------------------------------- stage.rs
+def test_stages():
+    x = StageData([1.0, 2.0, 3.0, 4.0], 2, 2)
+    assert PipelineStage(0, [Identity()]).forward(x).values == x.values
+    assert PipelineStage(0, [Scale(2.0)]).forward(StageData([1.0, 2.0], 1, 2)).values == [2.0, 4.0]
+    assert PipelineStage(0, [Scale(2.0), Scale(3.0)]).forward(StageData([1.0], 1, 1)).values == [6.0]
+    assert PipelineStage(0, [Scale(2.0)]).backward(StageData([1.0], 1, 1), StageData([1.0], 1, 1)).values == [2.0]
+    s = PipelineStage(0, [Identity()])
+    s.checkpoint_forward(StageData([1.0, 2.0], 1, 2))
+    assert s.input_cache is not None and s.input_cache.values == [1.0, 2.0]
+    assert PipelineStage(0, [Identity(), Identity(), Identity()]).num_layers() == 3
+
+
+def test_recompute_and_backward():
+    s = PipelineStage(0, [Scale(3.0)])
+    s.checkpoint_forward(StageData([1.0], 1, 1))
+    assert s.recompute_and_backward(StageData([1.0], 1, 1)).values == [3.0]
+    assert s.input_cache is None
+
+
+def test_stage_data_bytes_and_zeros():
+    d = StageData([1.0, 2.0, 3.0, 4.0], 2, 2)
+    b = d.to_bytes()
+    assert len(b) == 16 + 16 and b[:8] == (2).to_bytes(8, "little")
+    r = StageData.from_bytes(b)
+    assert (r.rows, r.cols, r.values) == (2, 2, d.values)
+    z = StageData.zeros(3, 4)
+    assert (z.rows, z.cols, len(z.values)) == (3, 4, 12) and all(v == 0.0 for v in z.values)
+    with pytest.raises(ValueError):
+        StageData([1.0], 2, 2)
+
+
+# ---------------------------------------------------------------- communicator.rs
+def _pipe(n):
+    return [PipelineComm(c) for c in MockCommunicator.create_world(n)]
+
+
+@pytest.mark.parametrize("vals,rows,cols", [([1.0, 2.0, 3.0, 4.0], 2, 2), ([0.5, -0.5], 1, 2)])
+def test_send_recv(vals, rows, cols):
+    p = _pipe(2)
+    p[0].send_activations(StageData(vals, rows, cols), 1)
+    r = p[1].recv_activations(0)
+    assert (r.rows, r.cols) == (rows, cols) and all(abs(a - b) < 0.2 for a, b in zip(vals, r.values))
+    p[0].send_gradients(StageData(vals, rows, cols), 1)
+    r = p[1].recv_gradients(0)
+    assert all(abs(a - b) < 0.2 for a, b in zip(vals, r.values))
+
+
+def test_fp8_format_config_and_ranks():
+    assert PipelineComm(MockCommunicator.create_world(1)[0]).with_fp8_format(Fp8Format.E5M2).fp8_format == Fp8Format.E5M2
+    pc = PipelineComm(MockCommunicator.create_world(4)[2])
+    assert pc.rank() == 2 and pc.world_size() == 4
+
+
+def test_compression_roundtrip_and_header():
+    pc = PipelineComm(MockCommunicator.create_world(1)[0])
+    d = StageData([1.0, 2.0, 3.0, 4.0, 5.0, 6.0], 2, 3)
+    b = pc.compress_stage_data(d)
+    assert len(b) == 29 + 6 and b[16] == 0
+    r = pc.decompress_stage_data(b)
+    assert (r.rows, r.cols, len(r.values)) == (2, 3, 6)
+
+
+# ---------------------------------------------------------------- schedules
+def _counting(n):
+    layers = [Counting() for _ in range(n)]
+    return [PipelineStage(i, [layers[i]]) for i in range(n)], layers
+
+
+@pytest.mark.parametrize("S,M", [(1, 1), (3, 2)])
+def test_gpipe_counts(S, M):
+    st, ly = _counting(S)
+    GpipeSchedule().execute(st, _pipe(S), M)
+    assert all(l.fw == M and l.bw == M for l in ly)
+
+
+def test_gpipe_no_stages_and_order():
+    GpipeSchedule().execute([], _pipe(1), 4)
+    order = []
+    st = [PipelineStage(i, [StageForwardClosure(lambda x, i=i: (order.append(f"fw_{i}"), x)[1],
+                                                lambda x, g, i=i: (order.append(f"bw_{i}"), g)[1])]) for i in range(2)]
+    GpipeSchedule().execute(st, _pipe(2), 2)
+    assert sum(o.startswith("fw") for o in order) == 4 and sum(o.startswith("bw") for o in order) == 4
+    last_fw = max(i for i, o in enumerate(order) if o.startswith("fw"))
+    first_bw = min(i for i, o in enumerate(order) if o.startswith("bw"))
+    assert last_fw < first_bw
+
+
+@pytest.mark.parametrize("S,M", [(1, 2), (3, 4)])
+def test_onef1b_counts(S, M):
+    st, ly = _counting(S)
+    OneF1BSchedule().execute(st, _pipe(S), M)
+    assert all(l.fw == M and l.bw == M for l in ly)
+
+
+def test_onef1b_no_stages_and_interleaving():
+    OneF1BSchedule().execute([], _pipe(1), 4)
+    order = []
+    st = [PipelineStage(i, [StageForwardClosure(lambda x, i=i: (order.append(f"fw_{i}"), x)[1],
+                                                lambda x, g, i=i: (order.append(f"bw_{i}"), g)[1])]) for i in range(2)]
+    OneF1BSchedule().execute(st, _pipe(2), 4)
+    assert sum(o.startswith("fw") for o in order) == 8 and sum(o.startswith("bw") for o in order) == 8
+
+
+def test_onef1b_op_lists():
+    s = build_schedule(ScheduleType.OneF1B, 4, 8)
+    names = lambda ops: ["F" if o.kind == PipeOp.Kind.Forward else "B" for o in ops]
+    assert names(s[0]) == ["F"] * 3 + ["F", "B"] * 5 + ["B"] * 3
+    assert names(s[3]) == ["F", "B"] * 8
+    for ops in s:
+        assert [o.microbatch for o in ops if o.kind == PipeOp.Kind.Forward] == list(range(8))
+        assert [o.microbatch for o in ops if o.kind == PipeOp.Kind.Backward] == list(range(8))
+    g = build_schedule(ScheduleType.Gpipe, 2, 3)
+    assert names(g[0]) == ["F"] * 3 + ["B"] * 3
+
+
+@pytest.mark.parametrize("S,M", [(2, 4), (4, 16), (8, 32), (4, 4)])
+def test_bubble_fraction_matches_formula(S, M):
+    for t in (ScheduleType.OneF1B, ScheduleType.Gpipe):
+        r = simulate_schedule(t, S, M, 1.0, 2.0, 0.0)
+        assert abs(r.bubble_fraction - ideal_bubble_fraction(S, M)) < 1e-9
+    assert abs(ideal_bubble_fraction(4, 16) - 3 / 19) < 1e-12 and abs(ideal_bubble_fraction(8, 32) - 7 / 39) < 1e-12
+
+
+def test_onef1b_bounds_inflight_activations():
+    one = simulate_schedule(ScheduleType.OneF1B, 4, 16, 1.0, 2.0, 0.0)
+    gp = simulate_schedule(ScheduleType.Gpipe, 4, 16, 1.0, 2.0, 0.0)
+    assert list(one.stage_peak_inflight) == [4, 3, 2, 1] and gp.peak_inflight == 16
+
+
+@pytest.mark.parametrize("sched", [ScheduleType.OneF1B, ScheduleType.Gpipe])
+@pytest.mark.parametrize("S,M", [(2, 3), (4, 8), (3, 1)])
+def test_rank_programs_run_without_deadlock_on_blocking_transport(sched, S, M):
+    w = local_world(S, 5.0)
+    K = PipeOp.Kind
+
+    def body(c):
+        s = c.rank()
+        done = []
+        for op in rank_program(sched, s, S, M):
+            if op.kind in (K.SendAct, K.SendGrad):
+                c.send(bytes([op.microbatch]), op.peer)
+            elif op.kind in (K.RecvAct, K.RecvGrad):
+                assert c.recv(op.peer) == bytes([op.microbatch])
+            else:
+                done.append((op.kind, op.microbatch))
+        return done
+
+    res = run_threads(w, body)
+    assert all(isinstance(r, list) and len(r) == 2 * M for r in res), res
+
+
+# ---------------------------------------------------------------- executor.rs
+@pytest.mark.parametrize("t,M", [(ScheduleType.Gpipe, 2), (ScheduleType.OneF1B, 4)])
+def test_executor_runs(t, M):
+    ex = PipelineExecutor([PipelineStage(0, [Identity()]), PipelineStage(1, [Identity()])], _pipe(2),
+                          PipelineConfig(2, M, CheckpointStrategy.None_, t))
+    ex.run()
+
+
+def test_executor_num_stages_and_defaults():
+    ex = PipelineExecutor([PipelineStage(i, [Identity()]) for i in range(3)], _pipe(3), PipelineConfig())
+    assert ex.num_stages() == 3
+    c = PipelineConfig()
+    assert (c.num_stages, c.num_microbatches, c.checkpoint_strategy, c.schedule_type) == (
+        1, 1, CheckpointStrategy.None_, ScheduleType.Gpipe)
+    assert ScheduleType.Gpipe == ScheduleType.Gpipe and ScheduleType.Gpipe != ScheduleType.OneF1B
+
+
+# ---------------------------------------------------------------- checkpoint.rs
+def test_checkpoint_strategies():
+    h = ActivationCheckpoint.save_input(StageData([1.0, 2.0], 1, 2))
+    assert h.input.values == [1.0, 2.0]
+    inp, out = ActivationCheckpoint.recompute_forward(ActivationCheckpoint.save_input(StageData([3.0], 1, 1)),
+                                                      [Scale(2.0)])
+    assert inp.values == [3.0] and out.values == [6.0]
+    s = PipelineStage(0, [Scale(2.0)])
+    assert apply_checkpoint_forward(s, StageData([1.0], 1, 1), CheckpointStrategy.None_).values == [2.0]
+    assert s.input_cache is None
+    s = PipelineStage(0, [Scale(2.0)])
+    assert apply_checkpoint_forward(s, StageData([1.0], 1, 1), CheckpointStrategy.Full).values == [2.0]
+    assert s.input_cache.values == [1.0]
+    s = PipelineStage(0, [Scale(2.0), Scale(2.0)])
+    assert apply_checkpoint_forward(s, StageData([1.0], 1, 1), CheckpointStrategy.Selective).values == [4.0]
+    assert s.input_cache is not None
+    assert CheckpointStrategy.Full != CheckpointStrategy.None_ and CheckpointStrategy.Selective != CheckpointStrategy.Full
+
+
+# ---------------------------------------------------------------- placement.rs
+def test_placement():
+    topo = MeshTorusHybrid.new_2d(4, 1, 2)
+    p = topology_aware_placement(4, topo)
+    assert len(p) == 4 and [s for s, _ in p] == [0, 1, 2, 3]
+    for i in range(3):
+        assert compute_hop_distance(p[i][1], p[i + 1][1], topo) == 1
+    assert len(topology_aware_placement(8, MeshTorusHybrid.new_3d(2, 2, 2, 4))) == 8
+    assert len(topology_aware_placement(3, MeshTorusHybrid.new_2d(4, 4, 2))) == 3
+
+
+def test_distances():
+    assert (torus_distance(2, 2, 5), torus_distance(0, 2, 5), torus_distance(0, 4, 5)) == (0, 2, 1)
+    assert compute_hop_distance(TorusCoordinates.new_2d(0, 0), TorusCoordinates.new_2d(1, 1),
+                                MeshTorusHybrid.new_2d(4, 4, 2)) == 2
+    assert compute_hop_distance(TorusCoordinates.new_3d(0, 0, 0), TorusCoordinates.new_3d(1, 1, 1),
+                                MeshTorusHybrid.new_3d(4, 4, 4, 2)) == 3
