@@ -31,6 +31,7 @@ class DistCommunicator(Communicator):
             device = (torch.device("cuda", torch.cuda.current_device()) if self._backend == "nccl"
                       else torch.device("cpu"))
         self.device = device
+        self._pending = []
 
     # ------------------------------------------------------------ helpers
     def _g(self, r: int) -> int:
@@ -42,10 +43,19 @@ class DistCommunicator(Communicator):
 
     # ------------------------------------------------------------ Communicator
     def send(self, data: bytes, dst: int) -> None:
+        # Posted asynchronously (the Communicator contract lets every rank send
+        # before it receives); buffers stay referenced until the transfer ends.
         n = torch.tensor([len(data)], dtype=torch.int64, device=self.device)
-        dist.send(n, self._g(dst), group=self.group)
+        self._pending.append((dist.isend(n, self._g(dst), group=self.group), n))
         if data:
-            dist.send(self._to_tensor(data), self._g(dst), group=self.group)
+            t = self._to_tensor(data)
+            self._pending.append((dist.isend(t, self._g(dst), group=self.group), t))
+        self._pending = [(w, t) for w, t in self._pending if not w.is_completed()]
+
+    def flush(self) -> None:
+        for w, _ in self._pending:
+            w.wait()
+        self._pending = []
 
     def recv(self, src: int) -> bytes:
         n = torch.empty(1, dtype=torch.int64, device=self.device)
@@ -92,6 +102,7 @@ class DistCommunicator(Communicator):
         return [bytes(o[:s].cpu().numpy().tobytes()) for o, s in zip(outs, sizes)]
 
     def barrier(self) -> None:
+        self.flush()
         dist.barrier(group=self.group)
 
     def rank(self) -> int:

@@ -62,7 +62,8 @@ class NcclBucketReducer:
         self.group = group
         self.world = dist.get_world_size(group)
         self.plan = BucketPlan(flat, bucket_bytes)
-        self.stream = torch.cuda.Stream(priority=-1)
+        self.on_cuda = flat.grad.is_cuda
+        self.stream = torch.cuda.Stream(priority=-1) if self.on_cuda else None
         self._reset()
 
     def _reset(self):
@@ -83,6 +84,10 @@ class NcclBucketReducer:
 
     def _launch(self, b: int) -> None:
         s, e = self.plan.ranges[b]
+        if not self.on_cuda:
+            self.reduce_range(s, e)
+            self.launched[b] = True
+            return
         ev = torch.cuda.Event()
         ev.record()
         self.stream.wait_event(ev)
@@ -97,5 +102,6 @@ class NcclBucketReducer:
         while self.next_to_launch < len(self.plan):
             self._launch(self.next_to_launch)
             self.next_to_launch += 1
-        torch.cuda.current_stream().wait_stream(self.stream)
+        if self.on_cuda:
+            torch.cuda.current_stream().wait_stream(self.stream)
         self._reset()
