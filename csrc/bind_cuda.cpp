@@ -9,7 +9,7 @@ std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gam
                                       const at::Tensor& beta, double eps);
 at::Tensor layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& gamma,
                          const at::Tensor& mean, const at::Tensor& rstd, at::Tensor dgamma,
-                         at::Tensor dbeta, bool accumulate);
+                         at::Tensor dbeta, bool accumulate, const c10::optional<at::Tensor>& dres);
 // xent.cu
 at::Tensor xent_fused(at::Tensor logits, const at::Tensor& targets,
                       const c10::optional<at::Tensor>& grad_scale, double scale_mul,
@@ -30,7 +30,8 @@ void embed_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor dwte, at:
                int64_t S, bool accumulate);
 at::Tensor bias_gelu_fwd(at::Tensor pre, const c10::optional<at::Tensor>& bias);
 void gelu_bwd_(at::Tensor dact, const at::Tensor& pre);
-void colsum_(const at::Tensor& x, at::Tensor out, bool accumulate);
+void colsum_(const at::Tensor& x, at::Tensor out, bool accumulate,
+             const c10::optional<at::Tensor>& scale);
 // gemm_bf16.cu
 void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor D,
                const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
@@ -45,7 +46,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   namespace py = pybind11;
   m.doc() = "mtorus sm_100a kernels";
   m.def("layernorm_fwd", &layernorm_fwd);
-  m.def("layernorm_bwd", &layernorm_bwd);
+  m.def("layernorm_bwd", &layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("gamma"), py::arg("mean"),
+        py::arg("rstd"), py::arg("dgamma"), py::arg("dbeta"), py::arg("accumulate"),
+        py::arg("dres") = py::none());
   m.def("xent_fused", &xent_fused, py::arg("logits"), py::arg("targets"),
         py::arg("grad_scale") = py::none(), py::arg("scale_mul") = 1.0,
         py::arg("write_grad") = true);
@@ -57,7 +60,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd);
   m.def("bias_gelu_fwd", &bias_gelu_fwd);
   m.def("gelu_bwd_", &gelu_bwd_);
-  m.def("colsum_", &colsum_);
+  m.def("colsum_", &colsum_, py::arg("x"), py::arg("out"), py::arg("accumulate"),
+        py::arg("scale") = py::none());
   m.def("gemm_bf16", &gemm_bf16, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"),
         py::arg("D"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("act") = py::none(), py::arg("aux") = py::none(), py::arg("alpha") = py::none(),

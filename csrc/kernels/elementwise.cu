@@ -114,15 +114,50 @@ __global__ void gelu_bwd_kernel(bf16* __restrict__ dact, const bf16* __restrict_
   }
 }
 
-// column sums of a [rows, F] bf16 matrix into fp32 (bias gradients); (+)= into out
-__global__ void colsum_kernel(const bf16* __restrict__ x, float* __restrict__ out, int rows, int F,
-                              int rows_per_block) {
+// Column sums of a [rows, F] bf16 matrix into fp32 (bias gradients), (+)= into out.
+// Block = 32 column groups of 8 (16-byte loads, 512 contiguous bytes per warp per
+// row) x 8 row lanes; each block reduces its row slice in registers, then across
+// row lanes in shared memory, and adds into out with one atomic per column.
+__global__ void __launch_bounds__(256) colsum_vec_kernel(const bf16* __restrict__ x,
+                                                         float* __restrict__ out, const float* scale,
+                                                         int rows, int F, int rows_per_block) {
+  __shared__ float red[8][257];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 256 + tx * 8;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c0 < F) {
+    for (int r = r0 + ty; r < r1; r += 8) {
+      float f[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(x + (size_t)r * F + c0), f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += f[k];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) red[ty][tx * 8 + k] = acc[k];
+  __syncthreads();
+  const int col = threadIdx.x;  // 256 columns of this block
+  if (blockIdx.x * 256 + col < F) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][col];
+    if (scale) t *= *scale;
+    atomicAdd(out + blockIdx.x * 256 + col, t);
+  }
+}
+
+// Generic fallback (F % 8 != 0).
+__global__ void colsum_kernel(const bf16* __restrict__ x, float* __restrict__ out, const float* scale,
+                              int rows, int F, int rows_per_block) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= F) return;
   const int r0 = blockIdx.y * rows_per_block;
   const int r1 = min(rows, r0 + rows_per_block);
   float acc = 0.f;
   for (int r = r0; r < r1; ++r) acc += __bfloat162float(x[(size_t)r * F + c]);
+  if (scale) acc *= *scale;
   atomicAdd(out + c, acc);
 }
 
@@ -195,16 +230,30 @@ void gelu_bwd_(at::Tensor dact, const at::Tensor& pre) {
   MT_LAUNCH_CHECK();
 }
 
-void colsum_(const at::Tensor& x, at::Tensor out, bool accumulate) {
+void colsum_(const at::Tensor& x, at::Tensor out, bool accumulate,
+             const c10::optional<at::Tensor>& scale) {
   MT_CHECK_CONTIG(x);
+  MT_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous(), "colsum: fp32 contiguous out");
   const int F = x.size(-1);
   const int rows = x.numel() / F;
   if (!accumulate) out.zero_();
   if (rows == 0) return;
-  const int rpb = 256;
-  dim3 grid((F + 255) / 256, (rows + rpb - 1) / rpb);
-  colsum_kernel<<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()),
-                                                out.data_ptr<float>(), rows, F, rpb);
+  const float* sp = scale.has_value() ? scale->data_ptr<float>() : nullptr;
+  const bool vec = F % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0;
+  if (vec) {
+    const int col_blocks = (F + 255) / 256;
+    // enough blocks to fill the GPU several times over, >= 64 rows each
+    int row_blocks = std::max(1, std::min((rows + 63) / 64, (num_sms() * 8 + col_blocks - 1) / col_blocks));
+    const int rpb = (rows + row_blocks - 1) / row_blocks;
+    row_blocks = (rows + rpb - 1) / rpb;
+    colsum_vec_kernel<<<dim3(col_blocks, row_blocks), 256, 0, cur_stream()>>>(
+        reinterpret_cast<const bf16*>(x.data_ptr()), out.data_ptr<float>(), sp, rows, F, rpb);
+  } else {
+    const int rpb = 256;
+    dim3 grid((F + 255) / 256, (rows + rpb - 1) / rpb);
+    colsum_kernel<<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()),
+                                                  out.data_ptr<float>(), sp, rows, F, rpb);
+  }
   MT_LAUNCH_CHECK();
 }
 

@@ -209,6 +209,189 @@ __global__ void ln_bwd_finish(const float* __restrict__ part, float* __restrict_
   *dst = accumulate ? *dst + t : t;
 }
 
+// ---------------------------------------------------------------------------
+// Block-per-row kernels: one CTA of d/8 threads (8 columns per thread) walks a
+// strided set of rows, so each thread holds only 8 values of a row, and the
+// dgamma/dbeta partial sums of its 8 columns stay in registers across rows.
+// Row reductions use a parity-double-buffered shared array: one __syncthreads
+// per reduction.
+
+__device__ __forceinline__ float2 block_sum2(float a, float b, float (*red)[32], int par) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  if (lane == 0) {
+    red[par * 2][wid] = a;
+    red[par * 2 + 1][wid] = b;
+  }
+  __syncthreads();
+  float ta = 0.f, tb = 0.f;
+  for (int w = 0; w < nw; ++w) {
+    ta += red[par * 2][w];
+    tb += red[par * 2 + 1][w];
+  }
+  return make_float2(ta, tb);
+}
+
+__global__ void __launch_bounds__(1024) ln_fwd_row(const bf16* __restrict__ x,
+                                                   const float* __restrict__ gamma,
+                                                   const float* __restrict__ beta,
+                                                   bf16* __restrict__ y, float* __restrict__ mean_out,
+                                                   float* __restrict__ rstd_out, int rows, int d,
+                                                   float eps) {
+  __shared__ float red[4][32];
+  const int col = threadIdx.x * 8;
+  float g[8], b[8];
+  {
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + col);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + col + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(beta + col);
+    const float4 b1 = *reinterpret_cast<const float4*>(beta + col + 4);
+    g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+    b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+  }
+  int par = 0;
+  bf16x8 nxt;
+  if (blockIdx.x < rows) nxt = *reinterpret_cast<const bf16x8*>(x + (size_t)blockIdx.x * d + col);
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    float v[8];
+    unpack8(nxt, v);
+    if (row + gridDim.x < rows)  // prefetch the next row while this one is reduced
+      nxt = *reinterpret_cast<const bf16x8*>(x + (size_t)(row + gridDim.x) * d + col);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[i];
+    const float mean = block_sum2(s, 0.f, red, par).x / d;
+    par ^= 1;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float t = v[i] - mean;
+      q += t * t;
+    }
+    const float rstd = rsqrtf(block_sum2(q, 0.f, red, par).x / d + eps);
+    par ^= 1;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = (v[i] - mean) * rstd * g[i] + b[i];
+    *reinterpret_cast<bf16x8*>(y + (size_t)row * d + col) = pack8(o);
+    if (threadIdx.x == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
+// dx = LN backward (+ dres, the gradient of a residual branch that reads x);
+// part[block][0][:] / part[block][1][:] = this block's dgamma / dbeta sums.
+__global__ void __launch_bounds__(1024) ln_bwd_row(const bf16* __restrict__ dy,
+                                                   const bf16* __restrict__ x,
+                                                   const float* __restrict__ gamma,
+                                                   const float* __restrict__ mean_in,
+                                                   const float* __restrict__ rstd_in,
+                                                   const bf16* __restrict__ dres,
+                                                   bf16* __restrict__ dx, float* __restrict__ part,
+                                                   int rows, int d) {
+  __shared__ float red[4][32];
+  const int col = threadIdx.x * 8;
+  float gm[8], dg[8], db[8];
+  {
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + col);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + col + 4);
+    gm[0] = g0.x; gm[1] = g0.y; gm[2] = g0.z; gm[3] = g0.w; gm[4] = g1.x; gm[5] = g1.y; gm[6] = g1.z; gm[7] = g1.w;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) dg[i] = db[i] = 0.f;
+  int par = 0;
+  bf16x8 nx, ndy;
+  if (blockIdx.x < rows) {
+    nx = *reinterpret_cast<const bf16x8*>(x + (size_t)blockIdx.x * d + col);
+    ndy = *reinterpret_cast<const bf16x8*>(dy + (size_t)blockIdx.x * d + col);
+  }
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    float xv[8], dv[8];
+    unpack8(nx, xv);
+    unpack8(ndy, dv);
+    const int nrow = row + gridDim.x;
+    if (nrow < rows) {
+      nx = *reinterpret_cast<const bf16x8*>(x + (size_t)nrow * d + col);
+      ndy = *reinterpret_cast<const bf16x8*>(dy + (size_t)nrow * d + col);
+    }
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float xh[8], g[8], s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xh[i] = (xv[i] - mean) * rstd;
+      g[i] = dv[i] * gm[i];
+      s1 += g[i];
+      s2 += g[i] * xh[i];
+      dg[i] += dv[i] * xh[i];
+      db[i] += dv[i];
+    }
+    const float2 s = block_sum2(s1, s2, red, par);
+    par ^= 1;
+    const float c2 = s.x / d, c1 = s.y / d;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = (g[i] - xh[i] * c1 - c2) * rstd;
+    if (dres) {
+      float r8[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(dres + (size_t)row * d + col), r8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] += r8[i];
+    }
+    *reinterpret_cast<bf16x8*>(dx + (size_t)row * d + col) = pack8(o);
+  }
+  float* out = part + (size_t)blockIdx.x * 2 * d + col;
+  *reinterpret_cast<float4*>(out) = make_float4(dg[0], dg[1], dg[2], dg[3]);
+  *reinterpret_cast<float4*>(out + 4) = make_float4(dg[4], dg[5], dg[6], dg[7]);
+  *reinterpret_cast<float4*>(out + d) = make_float4(db[0], db[1], db[2], db[3]);
+  *reinterpret_cast<float4*>(out + d + 4) = make_float4(db[4], db[5], db[6], db[7]);
+}
+
+// out[c] (+)= sum_r part[r * ld + c], c < ncols (fp32 column sums of the partials).
+__global__ void __launch_bounds__(256) colsum_f32_kernel(const float* __restrict__ part, int nrows,
+                                                         int ncols, int ld, float* __restrict__ out,
+                                                         int rows_per_block) {
+  __shared__ float red[8][257];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 256 + tx * 8;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(nrows, r0 + rows_per_block);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c0 < ncols) {
+    for (int r = r0 + ty; r < r1; r += 8) {
+      const float4 a = *reinterpret_cast<const float4*>(part + (size_t)r * ld + c0);
+      const float4 b = *reinterpret_cast<const float4*>(part + (size_t)r * ld + c0 + 4);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) red[ty][tx * 8 + k] = acc[k];
+  __syncthreads();
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c < ncols) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][threadIdx.x];
+    atomicAdd(out + c, t);
+  }
+}
+
+static void colsum_f32(const float* part, int nrows, int ncols, int ld, float* out, cudaStream_t st) {
+  const int rpb = 32;
+  dim3 grid((ncols + 255) / 256, (nrows + rpb - 1) / rpb);
+  colsum_f32_kernel<<<grid, 256, 0, st>>>(part, nrows, ncols, ld, out, rpb);
+  MT_LAUNCH_CHECK();
+}
+
+static bool row_kernel_ok(int d, const void* a, const void* b, const void* c) {
+  return d % 8 == 0 && d / 8 <= 1024 && d / 8 >= 32 && (d / 8) % 32 == 0 &&
+         reinterpret_cast<uintptr_t>(a) % 16 == 0 && reinterpret_cast<uintptr_t>(b) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(c) % 16 == 0;
+}
+
 static int pick_nch(int d) {
   if (d % 8 != 0) return 0;
   if (d <= 256) return 1;
@@ -238,9 +421,18 @@ std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gam
   const bool aligned = (reinterpret_cast<uintptr_t>(xp) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(gamma.data_ptr()) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(beta.data_ptr()) % 16 == 0);
+  auto st = cur_stream();
+  if (row_kernel_ok(d, xp, gamma.data_ptr(), beta.data_ptr())) {
+    const int threads = d / 8;
+    const int grid = std::min(rows, num_sms() * std::max(1, 2048 / threads));
+    ln_fwd_row<<<grid, threads, 0, st>>>(xp, gamma.data_ptr<float>(), beta.data_ptr<float>(), yp,
+                                         mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, d,
+                                         (float)eps);
+    MT_LAUNCH_CHECK();
+    return {y, mean, rstd};
+  }
   const int wpb = 8;
   int grid = std::min((rows + wpb - 1) / wpb, num_sms() * 8);
-  auto st = cur_stream();
 #define LNF(N)                                                                              \
   ln_fwd_vec<N><<<grid, wpb * 32, 0, st>>>(xp, gamma.data_ptr<float>(), beta.data_ptr<float>(), \
                                            yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), \
@@ -267,7 +459,7 @@ std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gam
 // Returns dx; writes (or accumulates into) dgamma/dbeta (fp32, length d).
 at::Tensor layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& gamma,
                          const at::Tensor& mean, const at::Tensor& rstd, at::Tensor dgamma,
-                         at::Tensor dbeta, bool accumulate) {
+                         at::Tensor dbeta, bool accumulate, const c10::optional<at::Tensor>& dres) {
   MT_CHECK_CONTIG(dy);
   MT_CHECK_CONTIG(x);
   MT_CHECK(dy.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16,
@@ -276,8 +468,38 @@ at::Tensor layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Te
   const int rows = x.numel() / d;
   auto dx = at::empty_like(x);
   if (rows == 0) return dx;
-  const int nch = pick_nch(d);
   auto st = cur_stream();
+  if (dres.has_value()) {
+    MT_CHECK(dres->is_contiguous() && dres->scalar_type() == at::kBFloat16 && dres->numel() == x.numel(),
+             "layernorm_bwd: dres must be a contiguous bf16 tensor shaped like x");
+  }
+  if (row_kernel_ok(d, x.data_ptr(), dy.data_ptr(), gamma.data_ptr()) &&
+      (!dres.has_value() || reinterpret_cast<uintptr_t>(dres->data_ptr()) % 16 == 0)) {
+    const int threads = d / 8;
+    const int grid = std::min(rows, num_sms() * std::max(1, 2048 / threads));
+    auto part = at::empty({grid, 2, d}, x.options().dtype(at::kFloat));
+    ln_bwd_row<<<grid, threads, 0, st>>>(
+        reinterpret_cast<const bf16*>(dy.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
+        gamma.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+        dres.has_value() ? reinterpret_cast<const bf16*>(dres->data_ptr()) : nullptr,
+        reinterpret_cast<bf16*>(dx.data_ptr()), part.data_ptr<float>(), rows, d);
+    MT_LAUNCH_CHECK();
+    float* dg = dgamma.data_ptr<float>();
+    float* dbp = dbeta.data_ptr<float>();
+    if (!accumulate) {
+      C10_CUDA_CHECK(cudaMemsetAsync(dg, 0, d * sizeof(float), st));
+      C10_CUDA_CHECK(cudaMemsetAsync(dbp, 0, d * sizeof(float), st));
+    }
+    if (dbp == dg + d) {
+      colsum_f32(part.data_ptr<float>(), grid, 2 * d, 2 * d, dg, st);
+    } else {
+      colsum_f32(part.data_ptr<float>(), grid, d, 2 * d, dg, st);
+      colsum_f32(part.data_ptr<float>() + d, grid, d, 2 * d, dbp, st);
+    }
+    return dx;
+  }
+  MT_CHECK(!dres.has_value(), "layernorm_bwd: dres needs d % 256 == 0 and 16-byte aligned tensors");
+  const int nch = pick_nch(d);
   const int wpb = 4;
   const bool aligned = (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(dy.data_ptr()) % 16 == 0) &&

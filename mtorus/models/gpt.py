@@ -191,17 +191,15 @@ class TransformerBlock(nn.Module):
 
     # ---------------------------------------------------------------- fused path
     def fused_forward(self, x2d, B: int, S: int):
-        from ..ops.attention import causal_attention
-        from ..ops.fused import LayerNormFn, LinearFn, MLPFn
+        from ..ops.fused import AttnBlockFn, MLPBlockFn
 
         a = self.attention
-        h = LayerNormFn.apply(x2d, (self.norm1.gamma, self.norm1.beta), self.norm1.eps)
-        qkv = LinearFn.apply(h, None, (self._qkv_w, self._qkv_b))
-        o = causal_attention(qkv, B, S, a.num_heads, a.d_head)
-        x2d = LinearFn.apply(o, x2d, (a.out_proj.weight, a.out_proj.bias))
-        h = LayerNormFn.apply(x2d, (self.norm2.gamma, self.norm2.beta), self.norm2.eps)
-        return MLPFn.apply(h, x2d, (self.ff.linear1.weight, self.ff.linear1.bias,
-                                    self.ff.linear2.weight, self.ff.linear2.bias))
+        x2d = AttnBlockFn.apply(x2d, (self.norm1.gamma, self.norm1.beta, self.norm1.eps),
+                                (self._qkv_w, self._qkv_b), (a.out_proj.weight, a.out_proj.bias),
+                                (B, S, a.num_heads, a.d_head))
+        return MLPBlockFn.apply(x2d, (self.norm2.gamma, self.norm2.beta, self.norm2.eps),
+                                (self.ff.linear1.weight, self.ff.linear1.bias,
+                                 self.ff.linear2.weight, self.ff.linear2.bias))
 
 
 class GptModel(nn.Module):

@@ -128,6 +128,101 @@ def grad_anchor(device) -> torch.Tensor:
     return _ANCHOR[key]
 
 
+def _ln_fwd(x2d, ln):
+    gamma, beta, eps = ln
+    return K.layernorm_fwd(x2d, gamma.data, beta.data, eps)
+
+
+def _ln_bwd(dh, x2d, mean, rstd, ln, dres):
+    gamma, beta, _ = ln
+    dx = K.layernorm_bwd(dh, x2d, gamma.data, mean, rstd, gamma.main_grad, beta.main_grad,
+                         FusedGradState.accumulate, dres=dres)
+    _grads_done(gamma, beta)
+    return dx
+
+
+class AttnBlockFn(Function):
+    """x + out_proj(attention(qkv(LN1(x)))) as one autograd node (reference
+    TransformerBlock first half, transformer.rs:144-149).  LayerNorm, the QKV and
+    output GEMMs (bias + residual in the epilogue) are sm_100a kernels; the LN
+    backward adds the residual gradient in the same kernel."""
+
+    @staticmethod
+    def forward(ctx, x2d, ln, qkv_params, out_params, shape):
+        from .attention import causal_attention
+
+        B, S, H, dh = shape
+        h, mean, rstd = _ln_fwd(x2d, ln)
+        wq, bq = qkv_params
+        qkv = K.gemm(h, wq.w16, bias=bq.data)
+        with torch.enable_grad():
+            qkv_leaf = qkv.detach().requires_grad_(True)
+            o_graph = causal_attention(qkv_leaf, B, S, H, dh)
+        o = o_graph.detach()
+        wo, bo = out_params
+        out = K.gemm(o, wo.w16, bias=bo.data, residual=x2d)
+        ctx.save_for_backward(x2d, mean, rstd, h, o)
+        ctx.attn = (qkv_leaf, o_graph)
+        ctx.params = (ln, qkv_params, out_params)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2d, mean, rstd, h, o = ctx.saved_tensors
+        ln, (wq, bq), (wo, bo) = ctx.params
+        qkv_leaf, o_graph = ctx.attn
+        dout = dout.contiguous()
+        acc = FusedGradState.accumulate
+        do = K.gemm(dout, wo.w16, b_mn=True)
+        K.gemm(dout, o, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        K.colsum_(dout, bo.main_grad, acc)
+        _grads_done(wo, bo)
+        torch.autograd.backward(o_graph, do)
+        dqkv = qkv_leaf.grad
+        ctx.attn = None
+        K.gemm(dqkv, h, out=wq.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        K.colsum_(dqkv, bq.main_grad, acc)
+        _grads_done(wq, bq)
+        dh = K.gemm(dqkv, wq.w16, b_mn=True)
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None
+
+
+class MLPBlockFn(Function):
+    """x + W2 GELU(W1 LN2(x) + b1) + b2 as one autograd node (reference
+    TransformerBlock second half and FeedForward, transformer.rs:89-110,151-155);
+    GELU / dGELU / bias / residual live in the GEMM epilogues and the LN backward
+    adds the residual gradient."""
+
+    @staticmethod
+    def forward(ctx, x2d, ln, params):
+        w1, b1, w2, b2 = params
+        h, mean, rstd = _ln_fwd(x2d, ln)
+        T, F = h.shape[0], w1.shape[0]
+        pre = torch.empty((T, F), dtype=torch.bfloat16, device=h.device)
+        act = torch.empty_like(pre)
+        K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
+        out = K.gemm(act, w2.w16, bias=b2.data, residual=x2d)
+        ctx.save_for_backward(x2d, mean, rstd, h, pre, act)
+        ctx.params = (ln, params)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        x2d, mean, rstd, h, pre, act = ctx.saved_tensors
+        ln, (w1, b1, w2, b2) = ctx.params
+        dout = dout.contiguous()
+        acc = FusedGradState.accumulate
+        dpre = K.gemm(dout, w2.w16, b_mn=True, aux=pre)
+        K.gemm(dout, act, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        K.colsum_(dout, b2.main_grad, acc)
+        _grads_done(w2, b2)
+        K.gemm(dpre, h, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        K.colsum_(dpre, b1.main_grad, acc)
+        _grads_done(w1, b1)
+        dh = K.gemm(dpre, w1.w16, b_mn=True)
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None
+
+
 class EmbeddingFn(Function):
     """x = wte[ids] + wpe[pos] (reference model.rs:113-118)."""
 
@@ -175,12 +270,6 @@ class LMHeadLossFn(Function):
         g = gloss.reshape(1).float().contiguous()
         dh = K.gemm(dlogits, w.w16, b_mn=True, alpha=g)
         K.gemm(dlogits, h, out=w.main_grad, a_mn=True, b_mn=True, accumulate=acc, alpha=g)
-        if acc:
-            tmp = torch.zeros_like(b.main_grad)
-            K.colsum_(dlogits, tmp, False)
-            b.main_grad.add_(tmp * g)
-        else:
-            K.colsum_(dlogits, b.main_grad, False)
-            b.main_grad.mul_(g)
+        K.colsum_(dlogits, b.main_grad, acc, scale=g)
         _grads_done(w, b)
         return dh, None, None, None

@@ -22,9 +22,11 @@ def layernorm_fwd(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps:
     return _cuda().layernorm_fwd(x.contiguous(), gamma, beta, float(eps))
 
 
-def layernorm_bwd(dy, x, gamma, mean, rstd, dgamma, dbeta, accumulate: bool):
-    """Returns dx; writes (accumulate=False) or adds dgamma/dbeta (fp32)."""
-    return _cuda().layernorm_bwd(dy.contiguous(), x, gamma, mean, rstd, dgamma, dbeta, bool(accumulate))
+def layernorm_bwd(dy, x, gamma, mean, rstd, dgamma, dbeta, accumulate: bool, dres=None):
+    """Returns dx (+ dres, the gradient arriving through a residual branch that
+    reads x); writes (accumulate=False) or adds dgamma/dbeta (fp32)."""
+    return _cuda().layernorm_bwd(dy.contiguous(), x, gamma, mean, rstd, dgamma, dbeta, bool(accumulate),
+                                 None if dres is None else dres.contiguous())
 
 
 def xent_fused(logits: torch.Tensor, targets: torch.Tensor, grad_scale: Optional[torch.Tensor] = None,
@@ -78,8 +80,9 @@ def gelu_bwd_(dact, pre):
     return dact
 
 
-def colsum_(x, out, accumulate: bool):
-    _cuda().colsum_(x.contiguous(), out, bool(accumulate))
+def colsum_(x, out, accumulate: bool, scale=None):
+    """out (+)= scale * column sums of x (bf16 [rows, F] -> fp32 [F])."""
+    _cuda().colsum_(x.contiguous(), out, bool(accumulate), scale)
     return out
 
 

@@ -73,7 +73,7 @@ def test_gemm_epilogues(K):
     assert K.gemm_status() == 0
 
 
-@pytest.mark.parametrize("rows,d", [(1, 128), (37, 2048), (300, 1000), (64, 4096), (513, 768)])
+@pytest.mark.parametrize("rows,d", [(1, 128), (37, 2048), (300, 1000), (64, 4096), (513, 768), (4099, 2048)])
 def test_layernorm(K, rows, d):
     torch.manual_seed(2)
     x = torch.randn(rows, d, device="cuda").bfloat16()
@@ -96,6 +96,12 @@ def test_layernorm(K, rows, d):
     # accumulate
     K.layernorm_bwd(dy, x, g, mean, rstd, dg, db, True)
     assert _rel(db, 2 * br.grad) < 1e-3
+    if d % 256 == 0:
+        # residual-branch gradient added inside the kernel
+        dres = torch.randn(rows, d, device="cuda").bfloat16()
+        dx2 = K.layernorm_bwd(dy, x, g, mean, rstd, dg, db, False, dres=dres)
+        assert _rel(dx2, xr.grad + dres.float()) < 2e-2
+        assert _rel(dg, gr.grad) < 1e-2
 
 
 @pytest.mark.parametrize("T,V", [(4, 1000), (64, 50304), (7, 1003)])
@@ -140,6 +146,10 @@ def test_gelu_and_colsum(K):
     out = torch.zeros(1024, device="cuda")
     K.colsum_(pre, out, False)
     assert _rel(out, pre.float().sum(0)) < 1e-4
+    big = torch.randn(5000, 2048, device="cuda").bfloat16()
+    out = torch.ones(2048, device="cuda")
+    K.colsum_(big, out, True, scale=torch.tensor([0.5], device="cuda"))
+    assert _rel(out, 1 + 0.5 * big.float().sum(0)) < 1e-4
 
 
 def test_adam_matches_reference(K):
