@@ -38,6 +38,25 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
                const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
                const c10::optional<at::Tensor>& alpha, bool beta);
 int64_t gemm_status(bool reset);
+// symm.cu
+int64_t symm_status(bool reset);
+void symm_rs_bucket(const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
+                    int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot,
+                    int64_t epoch, at::Tensor st, int64_t ctas, double inv_n);
+void symm_scalars_ar(const std::vector<int64_t>& scal, const std::vector<int64_t>& flags,
+                     int64_t me, int64_t slot, int64_t epoch, at::Tensor st);
+void symm_adam_shard_ag(const at::Tensor& ranges, at::Tensor master, at::Tensor m, at::Tensor v,
+                        const at::Tensor& grad, const std::vector<int64_t>& w16, const at::Tensor& st,
+                        double lr, double beta1, double beta2, double eps, double wd);
+void symm_barrier(const std::vector<int64_t>& flags, int64_t me, int64_t slot, int64_t epoch,
+                  int64_t code);
+void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t me,
+                    int64_t numel, int64_t dtype, int64_t slot, int64_t epoch, int64_t ctas);
+void symm_allgather(int64_t src, const std::vector<int64_t>& dst, int64_t me, int64_t bytes,
+                    int64_t ctas);
+void symm_broadcast(const std::vector<int64_t>& bufs, int64_t root, int64_t bytes, int64_t ctas);
+void symm_halo(int64_t src, const std::vector<int64_t>& recv, const at::Tensor& nbr_rank,
+               const at::Tensor& nbr_slot, int64_t bytes, int64_t ctas);
 void install_segv_handler();
 }  // namespace mtorus
 
@@ -67,6 +86,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("act") = py::none(), py::arg("aux") = py::none(), py::arg("alpha") = py::none(),
         py::arg("beta") = false);
   m.def("gemm_status", &gemm_status, py::arg("reset") = true);
+  m.def("symm_status", &symm_status, py::arg("reset") = true);
+  m.def("symm_rs_bucket", &symm_rs_bucket);
+  m.def("symm_scalars_ar", &symm_scalars_ar);
+  m.def("symm_adam_shard_ag", &symm_adam_shard_ag);
+  m.def("symm_barrier", &symm_barrier);
+  m.def("symm_allreduce", &symm_allreduce);
+  m.def("symm_allgather", &symm_allgather);
+  m.def("symm_broadcast", &symm_broadcast);
+  m.def("symm_halo", &symm_halo);
   m.def("install_segv_handler", &install_segv_handler);
   m.def("launch_count", []() { return mtorus::launch_counter(); });
 }

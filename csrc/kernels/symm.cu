@@ -1,0 +1,403 @@
+// Fused data-parallel collectives over NVLink peer memory (NVSwitch full mesh).
+//
+// Every rank's flat gradient buffer, bf16 weight buffer and a small flag / scalar
+// area are allocated as symmetric memory, so kernels receive one pointer per
+// peer and move data with plain loads and stores across NVLink.
+//
+//   rs_bucket      reduce-scatter of one gradient bucket: rank r sums chunk r of
+//                  the bucket over all peers' buffers (fp32 accumulate), writes
+//                  it into its own buffer and accumulates the squared norm and
+//                  a non-finite flag (overflow detection) -- fused path (a),
+//                  the reduction half;
+//   scalars_ar     all-reduce of the per-rank norm partials (tiny);
+//   adam_shard_ag  Adam on this rank's shard (skipped on overflow, unscaled and
+//                  clipped by the device multiplier) whose new bf16 weights are
+//                  stored straight into every peer's weight buffer: the update
+//                  and the parameter all-gather in one pass -- fused path (a),
+//                  the optimizer half, and the weight broadcast of (c);
+//   wait_flags     makes a stream wait until all peers reached an epoch;
+//   allreduce / allgather / broadcast / halo: standalone collectives for the
+//                  microbenchmark and the torus neighbour exchange (path d).
+//
+// Synchronisation: flags[slot * world + src] in each rank's flag area hold an
+// epoch; a producer publishes with a system-scope fence + release store into
+// every peer's slot, consumers spin with acquire loads.  Every spin is bounded
+// by a wall-clock limit (globaltimer); on expiry the kernel records a status
+// code, skips the dependent work and returns, so a missing peer never hangs the
+// GPU.  No TMA, no cluster launches.
+#include "common.cuh"
+
+namespace mtorus {
+
+constexpr int kMaxPeers = 8;
+constexpr uint64_t kSymmSpinLimitNs = 5000000000ull;  // 5 s
+
+struct PeerPtrs {
+  uint64_t p[kMaxPeers];
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Publish `epoch` into flags[slot * n + me] of every peer.
+__device__ __forceinline__ void signal_peers(const PeerPtrs& flags, int me, int n, int slot,
+                                             uint32_t epoch) {
+  __threadfence_system();
+  for (int p = 0; p < n; ++p) {
+    uint32_t* f = reinterpret_cast<uint32_t*>(flags.p[p]) + slot * n + me;
+    st_release_sys(f, epoch);
+  }
+}
+
+// Wait until flags[slot * n + p] >= epoch for all p (own flag area).  Bounded.
+__device__ __forceinline__ bool wait_peers(const uint32_t* my_flags, int n, int slot,
+                                           uint32_t epoch, int* status, int code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int p = 0; p < n; ++p) {
+    const uint32_t* f = my_flags + slot * n + p;
+    while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
+      if (globaltimer_ns() - t0 > kSymmSpinLimitNs) {
+        if (status) atomicExch(status, code);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+// Block-wide: thread 0 (optionally) signals, then waits; the result is shared.
+__device__ __forceinline__ bool block_barrier(const PeerPtrs& flags, const uint32_t* my_flags,
+                                              int me, int n, int slot, uint32_t epoch,
+                                              bool do_signal, int* status, int code) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    if (do_signal) signal_peers(flags, me, n, slot, epoch);
+    ok = wait_peers(my_flags, n, slot, epoch, status, code) ? 1 : 0;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// ------------------------------------------------------------------ reduce-scatter
+// Bucket [start, start+len) (elements, fp32).  Chunk c = [start + c*clen, ...).
+__global__ void __launch_bounds__(512) rs_bucket_kernel(PeerPtrs grads, PeerPtrs flags,
+                                                        uint32_t* my_flags, int me, int n,
+                                                        int64_t start, int64_t len, int64_t clen,
+                                                        int slot, uint32_t epoch, float inv_n,
+                                                        float* st, int* status) {
+  __shared__ float red[32];
+  if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 21)) return;
+  const int64_t c0 = start + (int64_t)me * clen;
+  const int64_t c1 = min(start + len, c0 + clen);
+  float* mine = reinterpret_cast<float*>(grads.p[me]);
+  float acc2 = 0.f;
+  int bad = 0;
+  const int64_t nvec = (c1 > c0) ? (c1 - c0) / 4 : 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t off = c0 + i * 4;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p) {
+      if (p < n) {
+        const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(grads.p[p]) + off);
+        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+      }
+    }
+    s.x *= inv_n; s.y *= inv_n; s.z *= inv_n; s.w *= inv_n;
+    *reinterpret_cast<float4*>(mine + off) = s;
+    acc2 += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+    bad |= !(isfinite(s.x) && isfinite(s.y) && isfinite(s.z) && isfinite(s.w));
+  }
+  // scalar tail (len not a multiple of 4)
+  for (int64_t off = c0 + nvec * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; off < c1;
+       off += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int p = 0; p < n; ++p) s += reinterpret_cast<const float*>(grads.p[p])[off];
+    s *= inv_n;
+    mine[off] = s;
+    acc2 += s * s;
+    bad |= !isfinite(s);
+  }
+  acc2 = block_sum(acc2, red);
+  const int anybad = __syncthreads_or(bad);
+  if (threadIdx.x == 0) {
+    atomicAdd(st + 0, acc2);  // kStSumSq
+    if (anybad) atomicAdd(st + 1, 1.f);
+  }
+}
+
+// ------------------------------------------------------------------ scalars all-reduce
+// scal[me * 2 + k] of every peer <- st[k] (k = 0: Σg², 1: non-finite count); then sum.
+__global__ void scalars_ar_kernel(PeerPtrs scal, PeerPtrs flags, uint32_t* my_flags, int me, int n,
+                                  int slot, uint32_t epoch, float* st, int* status) {
+  if (threadIdx.x != 0) return;
+  for (int p = 0; p < n; ++p) {
+    float* d = reinterpret_cast<float*>(scal.p[p]) + me * 2;
+    d[0] = st[0];
+    d[1] = st[1];
+  }
+  signal_peers(flags, me, n, slot, epoch);
+  if (!wait_peers(my_flags, n, slot, epoch, status, 22)) {
+    st[1] += 1.f;  // treat a missing peer as an overflow: the step is skipped
+    return;
+  }
+  const float* mine = reinterpret_cast<const float*>(scal.p[me]);
+  float s0 = 0.f, s1 = 0.f;
+  for (int p = 0; p < n; ++p) {
+    s0 += mine[p * 2];
+    s1 += mine[p * 2 + 1];
+  }
+  st[0] = s0;
+  st[1] = s1;
+}
+
+// ------------------------------------------------------------------ sharded Adam + all-gather
+// ranges[r] = {flat offset, length, compact (m/v) offset}; blockIdx.y = range.
+__global__ void __launch_bounds__(256) adam_shard_ag_kernel(
+    const int64_t* __restrict__ ranges, float* __restrict__ master, float* __restrict__ m,
+    float* __restrict__ v, const float* __restrict__ grad, PeerPtrs w16, int n,
+    const float* __restrict__ st, float lr, float beta1, float beta2, float eps, float wd) {
+  const int64_t off = ranges[blockIdx.y * 3], len = ranges[blockIdx.y * 3 + 1],
+                moff = ranges[blockIdx.y * 3 + 2];
+  const bool skip = st[5] > 0.f;  // kStSkip
+  const float gm = st[4];         // kStGradMul
+  const float step = st[7];       // kStStep
+  const float bc1 = 1.f - powf(beta1, step), bc2 = 1.f - powf(beta2, step);
+  const float step_size = lr / bc1, inv_sqrt_bc2 = rsqrtf(bc2);
+  const int64_t nv = len / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = off + i * 8, mo = moff + i * 8;
+    float pf[8];
+    *reinterpret_cast<float4*>(pf) = *reinterpret_cast<const float4*>(master + o);
+    *reinterpret_cast<float4*>(pf + 4) = *reinterpret_cast<const float4*>(master + o + 4);
+    if (!skip) {
+      float gf[8], mf[8], vf[8];
+      *reinterpret_cast<float4*>(gf) = *reinterpret_cast<const float4*>(grad + o);
+      *reinterpret_cast<float4*>(gf + 4) = *reinterpret_cast<const float4*>(grad + o + 4);
+      *reinterpret_cast<float4*>(mf) = *reinterpret_cast<const float4*>(m + mo);
+      *reinterpret_cast<float4*>(mf + 4) = *reinterpret_cast<const float4*>(m + mo + 4);
+      *reinterpret_cast<float4*>(vf) = *reinterpret_cast<const float4*>(v + mo);
+      *reinterpret_cast<float4*>(vf + 4) = *reinterpret_cast<const float4*>(v + mo + 4);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float g = gf[k] * gm;
+        if (wd != 0.f) g += wd * pf[k];
+        mf[k] = beta1 * mf[k] + (1.f - beta1) * g;
+        vf[k] = beta2 * vf[k] + (1.f - beta2) * g * g;
+        pf[k] -= step_size * mf[k] / (sqrtf(vf[k]) * inv_sqrt_bc2 + eps);
+      }
+      *reinterpret_cast<float4*>(master + o) = *reinterpret_cast<float4*>(pf);
+      *reinterpret_cast<float4*>(master + o + 4) = *reinterpret_cast<float4*>(pf + 4);
+      *reinterpret_cast<float4*>(m + mo) = *reinterpret_cast<float4*>(mf);
+      *reinterpret_cast<float4*>(m + mo + 4) = *reinterpret_cast<float4*>(mf + 4);
+      *reinterpret_cast<float4*>(v + mo) = *reinterpret_cast<float4*>(vf);
+      *reinterpret_cast<float4*>(v + mo + 4) = *reinterpret_cast<float4*>(vf + 4);
+    }
+    const bf16x8 w = pack8(pf);
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p)
+      if (p < n) reinterpret_cast<bf16x8*>(reinterpret_cast<bf16*>(w16.p[p]) + o)[0] = w;
+  }
+}
+
+// Signal (this rank finished writing into peers) then wait for everyone.
+__global__ void barrier_kernel(PeerPtrs flags, uint32_t* my_flags, int me, int n, int slot,
+                               uint32_t epoch, int* status, int code) {
+  if (threadIdx.x != 0) return;
+  signal_peers(flags, me, n, slot, epoch);
+  wait_peers(my_flags, n, slot, epoch, status, code);
+}
+
+// ------------------------------------------------------------------ standalone collectives
+// out (own buffer) = sum over peers of buf[p] (fp32 or bf16), every rank computes all
+// elements it owns (chunk me), then all-gathers them with peer stores.
+template <typename T>
+__global__ void __launch_bounds__(512) allreduce_kernel(PeerPtrs bufs, PeerPtrs flags,
+                                                        uint32_t* my_flags, int me, int n,
+                                                        int64_t numel, int slot, uint32_t epoch,
+                                                        int* status) {
+  constexpr int V = 16 / sizeof(T);
+  if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 31)) return;
+  const int64_t nvec = numel / V;
+  const int64_t per = (nvec + n - 1) / n;
+  const int64_t v0 = (int64_t)me * per, v1 = min(nvec, v0 + per);
+  for (int64_t i = v0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < v1;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) acc[k] = 0.f;
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p) {
+      if (p < n) {
+        const uint4 raw = reinterpret_cast<const uint4*>(bufs.p[p])[i];
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc[k] += to_f(e[k]);
+      }
+    }
+    uint4 outv;
+    T* o = reinterpret_cast<T*>(&outv);
+#pragma unroll
+    for (int k = 0; k < V; ++k) o[k] = from_f<T>(acc[k]);
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p)
+      if (p < n) reinterpret_cast<uint4*>(bufs.p[p])[i] = outv;
+  }
+}
+
+// Each rank copies its `bytes` from src (local) into slot me of every peer's dst.
+__global__ void __launch_bounds__(512) allgather_kernel(const uint4* __restrict__ src,
+                                                        PeerPtrs dst, int me, int n,
+                                                        int64_t nvec) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 v = src[i];
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p)
+      if (p < n) reinterpret_cast<uint4*>(dst.p[p])[(int64_t)me * nvec + i] = v;
+  }
+}
+
+// Root pushes its buffer into every peer's buffer.
+__global__ void __launch_bounds__(512) broadcast_kernel(PeerPtrs bufs, int root, int n,
+                                                        int64_t nvec) {
+  const uint4* src = reinterpret_cast<const uint4*>(bufs.p[root]);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 v = src[i];
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p)
+      if (p < n && p != root) reinterpret_cast<uint4*>(bufs.p[p])[i] = v;
+  }
+}
+
+// Torus neighbour exchange: this rank stores its send buffer into slot k of
+// neighbour k's receive area (slots = 2 * axes, one per direction), so a 2-wide
+// axis whose + and - neighbour coincide still gets two distinct slots.
+__global__ void __launch_bounds__(512) halo_kernel(const uint4* __restrict__ src, PeerPtrs recv,
+                                                   const int* __restrict__ nbr_rank,
+                                                   const int* __restrict__ nbr_slot, int nslots,
+                                                   int64_t nvec) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 v = src[i];
+    for (int k = 0; k < nslots; ++k) {
+      uint4* d = reinterpret_cast<uint4*>(recv.p[nbr_rank[k]]);
+      d[(int64_t)nbr_slot[k] * nvec + i] = v;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static PeerPtrs to_peers(const std::vector<int64_t>& v) {
+  MT_CHECK(v.size() <= (size_t)kMaxPeers, "at most 8 peers");
+  PeerPtrs p{};
+  for (size_t i = 0; i < v.size(); ++i) p.p[i] = (uint64_t)v[i];
+  return p;
+}
+
+static int* symm_status_ptr() {
+  static int* s = nullptr;
+  if (!s) {
+    C10_CUDA_CHECK(cudaMalloc(&s, sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(s, 0, sizeof(int)));
+  }
+  return s;
+}
+
+int64_t symm_status(bool reset) {
+  int h = 0;
+  C10_CUDA_CHECK(cudaMemcpy(&h, symm_status_ptr(), sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) C10_CUDA_CHECK(cudaMemset(symm_status_ptr(), 0, sizeof(int)));
+  return h;
+}
+
+void symm_rs_bucket(const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
+                    int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot,
+                    int64_t epoch, at::Tensor st, int64_t ctas, double inv_n) {
+  const int n = grads.size();
+  rs_bucket_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(
+      to_peers(grads), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, start,
+      len, clen, (int)slot, (uint32_t)epoch, (float)inv_n, st.data_ptr<float>(), symm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+void symm_scalars_ar(const std::vector<int64_t>& scal, const std::vector<int64_t>& flags,
+                     int64_t me, int64_t slot, int64_t epoch, at::Tensor st) {
+  scalars_ar_kernel<<<1, 32, 0, cur_stream()>>>(to_peers(scal), to_peers(flags),
+                                                reinterpret_cast<uint32_t*>(flags[me]), (int)me,
+                                                (int)scal.size(), (int)slot, (uint32_t)epoch,
+                                                st.data_ptr<float>(), symm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+void symm_adam_shard_ag(const at::Tensor& ranges, at::Tensor master, at::Tensor m, at::Tensor v,
+                        const at::Tensor& grad, const std::vector<int64_t>& w16, const at::Tensor& st,
+                        double lr, double beta1, double beta2, double eps, double wd) {
+  const int nr = ranges.size(0);
+  if (nr == 0) return;
+  dim3 grid(std::max(1, num_sms() * 4 / std::max(nr, 1)), nr);
+  adam_shard_ag_kernel<<<grid, 256, 0, cur_stream()>>>(
+      ranges.data_ptr<int64_t>(), master.data_ptr<float>(), m.data_ptr<float>(),
+      v.data_ptr<float>(), grad.data_ptr<float>(), to_peers(w16), (int)w16.size(),
+      st.data_ptr<float>(), (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd);
+  MT_LAUNCH_CHECK();
+}
+
+void symm_barrier(const std::vector<int64_t>& flags, int64_t me, int64_t slot, int64_t epoch,
+                  int64_t code) {
+  barrier_kernel<<<1, 32, 0, cur_stream()>>>(to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]),
+                                             (int)me, (int)flags.size(), (int)slot, (uint32_t)epoch,
+                                             symm_status_ptr(), (int)code);
+  MT_LAUNCH_CHECK();
+}
+
+void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t me,
+                    int64_t numel, int64_t dtype, int64_t slot, int64_t epoch, int64_t ctas) {
+  const int n = bufs.size();
+  if (dtype == 0)
+    allreduce_kernel<float><<<(int)ctas, 512, 0, cur_stream()>>>(
+        to_peers(bufs), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, numel,
+        (int)slot, (uint32_t)epoch, symm_status_ptr());
+  else
+    allreduce_kernel<bf16><<<(int)ctas, 512, 0, cur_stream()>>>(
+        to_peers(bufs), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, numel,
+        (int)slot, (uint32_t)epoch, symm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+void symm_allgather(int64_t src, const std::vector<int64_t>& dst, int64_t me, int64_t bytes,
+                    int64_t ctas) {
+  MT_CHECK(bytes % 16 == 0, "allgather: bytes must be a multiple of 16");
+  allgather_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(reinterpret_cast<const uint4*>(src),
+                                                        to_peers(dst), (int)me, (int)dst.size(),
+                                                        bytes / 16);
+  MT_LAUNCH_CHECK();
+}
+
+void symm_broadcast(const std::vector<int64_t>& bufs, int64_t root, int64_t bytes, int64_t ctas) {
+  MT_CHECK(bytes % 16 == 0, "broadcast: bytes must be a multiple of 16");
+  broadcast_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(to_peers(bufs), (int)root,
+                                                        (int)bufs.size(), bytes / 16);
+  MT_LAUNCH_CHECK();
+}
+
+void symm_halo(int64_t src, const std::vector<int64_t>& recv, const at::Tensor& nbr_rank,
+               const at::Tensor& nbr_slot, int64_t bytes, int64_t ctas) {
+  MT_CHECK(bytes % 16 == 0, "halo: bytes must be a multiple of 16");
+  halo_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(
+      reinterpret_cast<const uint4*>(src), to_peers(recv), nbr_rank.data_ptr<int>(),
+      nbr_slot.data_ptr<int>(), (int)nbr_rank.numel(), bytes / 16);
+  MT_LAUNCH_CHECK();
+}
+
+}  // namespace mtorus

@@ -263,11 +263,13 @@ class GptModel(nn.Module):
         groups += [[self.ln_f.gamma, self.ln_f.beta], [self.lm_head.weight], [self.lm_head.bias]]
         return groups
 
-    def flatten(self, device, grad_dtype=torch.float32):
-        """Move parameters into flat fp32/bf16/grad buffers on `device` (fused path)."""
+    def flatten(self, device, grad_dtype=torch.float32, symmetric: bool = False, group=None):
+        """Move parameters into flat fp32/bf16/grad buffers on `device` (fused path);
+        ``symmetric`` places gradients and bf16 weights in peer-mapped memory for
+        the fused NVLink data-parallel path."""
         from ..parallel.flat import FlatParams
 
-        self.flat = FlatParams(self.flat_groups(), device, grad_dtype=grad_dtype)
+        self.flat = FlatParams(self.flat_groups(), device, grad_dtype=grad_dtype, symmetric=symmetric, group=group)
         d = self.d_model
         for blk in self.blocks:
             a = blk.attention

@@ -24,7 +24,8 @@ def _round_up(n: int, a: int) -> int:
 
 class FlatParams:
     def __init__(self, groups: Sequence[Sequence[torch.nn.Parameter]], device,
-                 grad_dtype: torch.dtype = torch.float32, with_w16: bool = True):
+                 grad_dtype: torch.dtype = torch.float32, with_w16: bool = True,
+                 symmetric: bool = False, group=None):
         seen = set()
         self.params: List[torch.nn.Parameter] = []
         self.groups: List[List[torch.nn.Parameter]] = []
@@ -45,8 +46,18 @@ class FlatParams:
         self.offsets = offsets
         self.device = torch.device(device)
         self.master = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
-        self.grad = torch.zeros(self.numel, dtype=grad_dtype, device=self.device)
-        self.w16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=self.device) if with_w16 else None
+        self.symmetric = symmetric
+        if symmetric:
+            # gradients and bf16 weights are read / written by peers over NVLink
+            from .symm import SymmBuffer
+
+            self.symm_grad = SymmBuffer(self.numel, grad_dtype, self.device, group)
+            self.symm_w16 = SymmBuffer(self.numel, torch.bfloat16, self.device, group)
+            self.grad = self.symm_grad.tensor
+            self.w16 = self.symm_w16.tensor
+        else:
+            self.grad = torch.zeros(self.numel, dtype=grad_dtype, device=self.device)
+            self.w16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=self.device) if with_w16 else None
         with torch.no_grad():
             for p, o in zip(self.params, offsets):
                 n = p.numel()

@@ -1,0 +1,260 @@
+"""Fused NVLink collectives over symmetric (peer-mapped) memory.
+
+Buffers are allocated with torch's symmetric-memory allocator, which maps every
+rank's allocation into every peer's address space (CUDA VMM + IPC handles on the
+NVSwitch fabric); all data movement happens in the kernels of
+``csrc/kernels/symm.cu`` with plain loads / stores to peer pointers and
+epoch-stamped flags (bounded waits, no NCCL).
+
+* ``SymmBucketReducer``  -- data-parallel gradient reduction: per 25 MB bucket, a
+  reduce-scatter kernel (fp32 sum, 1/N averaging, Σg² and overflow flag fused)
+  launched on a side stream as soon as backward finishes the bucket.
+* ``ZeroAdam``           -- the sharded optimizer that consumes it: loss-scale /
+  overflow / clip finalisation, Adam on this rank's shard, and the bf16 weight
+  all-gather done by the same kernel storing each updated weight into every
+  peer's weight buffer; a flag barrier then orders the next forward.
+* ``SymmCollectives``    -- standalone all-reduce / all-gather / broadcast and the
+  torus halo exchange for the collective microbenchmark.
+
+Reference counterpart: the DP all-reduce primitive of crates/mt-comm/src/
+collective.rs (never called by the reference's train_step) and the torus
+neighbour exchange of crates/mt-comm/src/topology_aware.rs:38-49.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+from .._ext import cuda as _cuda
+from .data_parallel import BucketPlan
+
+_ALIGN = 64
+
+
+def _group_name(group) -> str:
+    g = group if group is not None else dist.group.WORLD
+    return g.group_name
+
+
+class SymmBuffer:
+    """A symmetric allocation: the local tensor plus each peer's address of it."""
+
+    def __init__(self, numel: int, dtype: torch.dtype, device, group=None, zero: bool = True):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.tensor = symm_mem.empty(numel, dtype=dtype, device=device)
+        if zero:
+            self.tensor.zero_()
+        self.handle = symm_mem.rendezvous(self.tensor, _group_name(group))
+        self.rank = self.handle.rank
+        self.world = self.handle.world_size
+        base = self.handle.buffer_ptrs[self.rank]
+        off = self.tensor.data_ptr() - base
+        self.ptrs: List[int] = [int(p) + off for p in self.handle.buffer_ptrs]
+
+    def barrier(self) -> None:
+        self.handle.barrier()
+
+
+class SymmContext:
+    """Flag / scalar areas shared by the fused kernels of one process group."""
+
+    def __init__(self, device, group=None, num_slots: int = 1024):
+        self.device = torch.device(device)
+        self.group = group
+        self.flags = SymmBuffer(num_slots * 8, torch.int32, device, group)
+        self.scalars = SymmBuffer(64, torch.float32, device, group)
+        self.rank = self.flags.rank
+        self.world = self.flags.world
+        self.num_slots = num_slots
+        self.flags.barrier()
+
+    def status(self, reset: bool = True) -> int:
+        """Non-zero when a fused kernel gave up waiting for a peer (its wait code)."""
+        return int(_cuda().symm_status(reset))
+
+
+def _chunk_len(n_elems: int, world: int) -> int:
+    c = (n_elems + world - 1) // world
+    return (c + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+class SymmBucketReducer:
+    """Reduce-scatter of the flat gradient buffer, bucket by bucket, over NVLink."""
+
+    def __init__(self, flat, group=None, bucket_bytes: int = 25 * 1024 * 1024, ctas: int = 24,
+                 ctx: Optional[SymmContext] = None):
+        if not getattr(flat, "symmetric", False):
+            raise ValueError("SymmBucketReducer needs a FlatParams built with symmetric grad/w16 buffers")
+        self.flat = flat
+        self.ctx = ctx or SymmContext(flat.device, group, num_slots=max(1024, 4 * (flat.numel // 1000000 + 8)))
+        self.plan = BucketPlan(flat, bucket_bytes)
+        nb = len(self.plan)
+        if nb + 4 > self.ctx.num_slots:
+            raise ValueError("too many buckets for the flag area")
+        self.me, self.world = self.ctx.rank, self.ctx.world
+        self.ctas = ctas
+        self.epoch = 0
+        self.stream = torch.cuda.Stream(priority=-1)
+        self.slot_norm = nb
+        self.slot_ag = nb + 1
+        # this rank's shard: its chunk of every bucket -> (flat offset, len, compact offset)
+        ranges, moff = [], 0
+        self.clen = []
+        for s, e in self.plan.ranges:
+            c = _chunk_len(e - s, self.world)
+            self.clen.append(c)
+            c0 = s + self.me * c
+            ln = max(0, min(e, c0 + c) - c0)
+            if ln > 0:
+                ranges.append((c0, ln, moff))
+                moff += (ln + 7) // 8 * 8
+        self.shard_numel = moff
+        self.ranges = torch.tensor(ranges, dtype=torch.int64, device=flat.device).reshape(-1, 3)
+        self._reset()
+
+    def _reset(self):
+        self.pending = [len(m) for m in self.plan.members]
+        self.next_to_launch = 0
+
+    def begin_step(self) -> None:
+        self.epoch += 1
+
+    def on_ready(self, params) -> None:
+        for p in params:
+            for q in getattr(p, "members", [p]):
+                b = self.plan.bucket_of.get(id(q))
+                if b is not None:
+                    self.pending[b] -= 1
+        while self.next_to_launch < len(self.plan) and self.pending[self.next_to_launch] <= 0:
+            self._launch(self.next_to_launch)
+            self.next_to_launch += 1
+
+    def _launch(self, b: int) -> None:
+        s, e = self.plan.ranges[b]
+        ev = torch.cuda.Event()
+        ev.record()
+        self.stream.wait_event(ev)
+        with torch.cuda.stream(self.stream):
+            _cuda().symm_rs_bucket(self.flat.symm_grad.ptrs, self.ctx.flags.ptrs, self.me, s, e - s, self.clen[b],
+                                   b, self.epoch, self.state, self.ctas, 1.0 / self.world)
+
+    def finish(self) -> None:
+        while self.next_to_launch < len(self.plan):
+            self._launch(self.next_to_launch)
+            self.next_to_launch += 1
+        with torch.cuda.stream(self.stream):
+            _cuda().symm_scalars_ar(self.ctx.scalars.ptrs, self.ctx.flags.ptrs, self.me, self.slot_norm,
+                                    self.epoch, self.state)
+        torch.cuda.current_stream().wait_stream(self.stream)
+        self._reset()
+
+    # the optimizer's state block is shared (norm partials land in it)
+    state: torch.Tensor = None
+
+
+class ZeroAdam:
+    """Adam over this rank's shard, fed by SymmBucketReducer; the new bf16 weights
+    are written into every rank's weight buffer by the same kernel."""
+
+    def __init__(self, flat, reducer: SymmBucketReducer, lr: float = 3e-4, betas=(0.9, 0.999), eps: float = 1e-5,
+                 weight_decay: float = 0.0, max_grad_norm: float = 0.0, loss_scale=None):
+        from ..training.fused_optim import ST_SCALE, DeviceLossScaleConfig
+
+        self.flat = flat
+        self.reducer = reducer
+        self.lr = lr
+        self.betas = betas
+        self.eps = eps
+        self.weight_decay = weight_decay
+        self.max_grad_norm = max_grad_norm
+        self.ls = loss_scale or DeviceLossScaleConfig()
+        dev = flat.device
+        self.m = torch.zeros(reducer.shard_numel, dtype=torch.float32, device=dev)
+        self.v = torch.zeros_like(self.m)
+        self.state = torch.zeros(16, dtype=torch.float32, device=dev)
+        self.state[ST_SCALE] = self.ls.init_scale
+        reducer.state = self.state
+
+    @property
+    def loss_scale_tensor(self) -> torch.Tensor:
+        from ..training.fused_optim import ST_SCALE
+
+        return self.state[ST_SCALE:ST_SCALE + 1]
+
+    def step(self, lr: Optional[float] = None) -> None:
+        from ..ops import kernels as K
+
+        K.optim_finalize(self.state, self.ls.dynamic, self.ls.growth_interval, self.max_grad_norm, True)
+        r = self.reducer
+        _cuda().symm_adam_shard_ag(r.ranges, self.flat.master, self.m, self.v, self.flat.grad,
+                                   self.flat.symm_w16.ptrs, self.state, self.lr if lr is None else lr,
+                                   self.betas[0], self.betas[1], self.eps, self.weight_decay)
+        # every rank has written its shard into every peer: order the next forward after it
+        _cuda().symm_barrier(r.ctx.flags.ptrs, r.me, r.slot_ag, r.epoch, 23)
+
+    def stats(self) -> dict:
+        s = self.state.tolist()
+        return {"loss_scale": s[2], "grad_norm": s[6], "skipped": s[5] > 0, "steps": int(s[7])}
+
+
+class SymmCollectives:
+    """Standalone NVLink collectives on symmetric buffers (microbenchmark / halo)."""
+
+    def __init__(self, device, group=None, max_bytes: int = 1 << 30, ctas: int = 32):
+        self.ctx = SymmContext(device, group)
+        self.me, self.world = self.ctx.rank, self.ctx.world
+        self.buf = SymmBuffer(max_bytes // 4, torch.float32, device, group)
+        self.recv = SymmBuffer(max_bytes // 4, torch.float32, device, group)
+        self.ctas = ctas
+        self.epoch = 0
+
+    def _slot(self):
+        self.epoch += 1
+        return self.epoch
+
+    def all_reduce(self, numel: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """In-place sum over ranks of the first numel elements of ``buf`` (as dtype)."""
+        ep = self._slot()
+        _cuda().symm_allreduce(self.buf.ptrs, self.ctx.flags.ptrs, self.me, numel, 0 if dtype == torch.float32 else 1,
+                               0, ep, self.ctas)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 1, ep, 32)
+        return self.buf.tensor.view(dtype)[:numel]
+
+    def all_gather(self, nbytes: int) -> None:
+        """Each rank's first nbytes of ``buf`` land in slot rank of every peer's ``recv``."""
+        ep = self._slot()
+        _cuda().symm_allgather(self.buf.tensor.data_ptr(), self.recv.ptrs, self.me, nbytes, self.ctas)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 2, ep, 33)
+
+    def broadcast(self, nbytes: int, root: int = 0) -> None:
+        ep = self._slot()
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 3, ep, 34)  # root's data is ready everywhere
+        if self.me == root:
+            _cuda().symm_broadcast(self.buf.ptrs, root, nbytes, self.ctas)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 4, ep, 35)
+
+    def halo(self, nbytes: int, nbr_rank: torch.Tensor, nbr_slot: torch.Tensor) -> None:
+        """Store ``buf[:nbytes]`` into slot nbr_slot[k] of neighbour nbr_rank[k]'s ``recv``."""
+        ep = self._slot()
+        _cuda().symm_halo(self.buf.tensor.data_ptr(), self.recv.ptrs, nbr_rank, nbr_slot, nbytes, self.ctas)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 5, ep, 36)
+
+
+def halo_plan(topology, rank: int, device) -> tuple:
+    """Neighbour ranks and receive slots for the torus exchange of ``rank``: the
+    sender's k-th neighbour (+x, -x, +y, -y, ...) receives into its slot for the
+    opposite direction, so a 2-wide axis (where +x == -x) keeps both messages."""
+    coords = topology.rank_to_coords(rank)
+    nbrs = coords.neighbors(topology.dims)
+    ranks, slots = [], []
+    for k, (c, axis) in enumerate(nbrs):
+        ranks.append(topology.node_rank(c))
+        slots.append(k ^ 1)  # +axis send arrives in the receiver's -axis slot
+    return (torch.tensor(ranks, dtype=torch.int32, device=device),
+            torch.tensor(slots, dtype=torch.int32, device=device))
+
+
+__all__ = ["SymmBuffer", "SymmContext", "SymmBucketReducer", "ZeroAdam", "SymmCollectives", "halo_plan"]

@@ -37,23 +37,28 @@ class GptTrainer:
             g = torch.Generator(device=self.device)
             g.manual_seed(seed)
             self.model.init_normal_(0.02, generator=g)
-        self.flat = self.model.flatten(self.device)
-        self.opt = FusedAdam(self.flat, lr=lr, max_grad_norm=max_grad_norm, weight_decay=weight_decay,
-                             loss_scale=loss_scale or DeviceLossScaleConfig())
+        multi = dp_group is not None or (torch.distributed.is_initialized() and torch.distributed.get_world_size() > 1)
+        self.dp = dp if multi else "none"
+        self.flat = self.model.flatten(self.device, symmetric=self.dp == "symm", group=dp_group)
         self.lr = lr
         self.warmup_steps = warmup_steps
         self.global_step = 0
         self.reducer = None
-        if dp_group is not None or (torch.distributed.is_initialized() and torch.distributed.get_world_size() > 1):
-            if dp == "nccl":
+        ls = loss_scale or DeviceLossScaleConfig()
+        if self.dp == "symm":
+            from ..parallel.symm import SymmBucketReducer, ZeroAdam
+
+            self.reducer = SymmBucketReducer(self.flat, dp_group, int(bucket_mb * 1024 * 1024))
+            self.opt = ZeroAdam(self.flat, self.reducer, lr=lr, max_grad_norm=max_grad_norm,
+                                weight_decay=weight_decay, loss_scale=ls)
+        else:
+            self.opt = FusedAdam(self.flat, lr=lr, max_grad_norm=max_grad_norm, weight_decay=weight_decay,
+                                 loss_scale=ls)
+            if self.dp == "nccl":
                 from ..parallel.data_parallel import NcclBucketReducer
 
                 self.reducer = NcclBucketReducer(self.flat, dp_group, int(bucket_mb * 1024 * 1024))
-            elif dp == "symm":
-                from ..parallel.symm import SymmBucketReducer
-
-                self.reducer = SymmBucketReducer(self.flat, dp_group, int(bucket_mb * 1024 * 1024))
-            else:
+            elif self.dp != "none":
                 raise ValueError(f"unknown dp reducer {dp!r}")
         self._ids = None
         self._tgt = None
@@ -69,6 +74,8 @@ class GptTrainer:
         """One full training step on device tensors; returns the device loss (no sync)."""
         FusedGradState.accumulate = False
         FusedGradState.grad_ready_hook = self.reducer.on_ready if self.reducer is not None else None
+        if hasattr(self.reducer, "begin_step"):
+            self.reducer.begin_step()
         loss = self.model.fused_loss(ids, targets, grad_scale=self.opt.loss_scale_tensor)
         loss.backward()
         if self.reducer is not None:
