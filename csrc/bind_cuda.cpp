@@ -38,6 +38,21 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
                const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
                const c10::optional<at::Tensor>& alpha, bool beta);
 int64_t gemm_status(bool reset);
+void gemm_set_reserved_sms(int64_t n);
+void gemm_fp8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
+              int64_t b_fmt, at::Tensor D, const c10::optional<at::Tensor>& bias,
+              const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
+              const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha,
+              const c10::optional<at::Tensor>& alpha2, bool beta);
+// fp8.cu
+void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::Tensor>& scale,
+                  const c10::optional<at::Tensor>& amax, int64_t fmt);
+void fp8_amax(const at::Tensor& x, at::Tensor amax);
+void fp8_scaling_update(at::Tensor hist, at::Tensor amax, at::Tensor scale, at::Tensor inv,
+                        const at::Tensor& fmax, int64_t cursor, bool current);
+void fp8_dequantize(const at::Tensor& q, at::Tensor out, const at::Tensor& inv_scale, int64_t fmt);
+void fp8_quantize_blocks(const at::Tensor& x, at::Tensor out, at::Tensor scales, int64_t block_size,
+                         double fmax, int64_t fmt);
 // symm.cu
 int64_t symm_status(bool reset);
 void symm_rs_bucket(const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
@@ -86,6 +101,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("act") = py::none(), py::arg("aux") = py::none(), py::arg("alpha") = py::none(),
         py::arg("beta") = false);
   m.def("gemm_status", &gemm_status, py::arg("reset") = true);
+  m.def("gemm_set_reserved_sms", &gemm_set_reserved_sms);
+  m.def("gemm_fp8", &gemm_fp8, py::arg("A"), py::arg("a_mn"), py::arg("a_fmt"), py::arg("B"), py::arg("b_mn"),
+        py::arg("b_fmt"), py::arg("D"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
+        py::arg("act") = py::none(), py::arg("aux") = py::none(), py::arg("alpha") = py::none(),
+        py::arg("alpha2") = py::none(), py::arg("beta") = false);
+  m.def("fp8_quantize", &fp8_quantize, py::arg("x"), py::arg("out"), py::arg("scale") = py::none(),
+        py::arg("amax") = py::none(), py::arg("fmt") = 0);
+  m.def("fp8_amax", &fp8_amax);
+  m.def("fp8_scaling_update", &fp8_scaling_update);
+  m.def("fp8_dequantize", &fp8_dequantize);
+  m.def("fp8_quantize_blocks", &fp8_quantize_blocks);
   m.def("symm_status", &symm_status, py::arg("reset") = true);
   m.def("symm_rs_bucket", &symm_rs_bucket);
   m.def("symm_scalars_ar", &symm_scalars_ar);

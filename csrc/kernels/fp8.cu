@@ -1,0 +1,231 @@
+// FP8 quantisation with delayed (amax-history) scaling, on device.
+//
+// Reference semantics (crates/mt-core/src/precision/{quantize,scaling}.rs):
+//   scale  = format_max / amax (1 when amax == 0), stored = fp8(x * scale),
+//   DelayedScaling: amax ring buffer of `history` entries, current amax = max of
+//   the ring, the scale used in step t comes from the history up to step t-1.
+//
+// Design (B200): one fused pass per tensor reads bf16, multiplies by the current
+// scale (a device scalar: no host sync), converts two values at a time with the
+// saturating round-to-nearest-even cvt (cvt.rn.satfinite.{e4m3,e5m2}x2), writes
+// 1-byte codes with 16-byte stores and folds max|x| into the slot's running
+// amax with one atomic per block.  After the step one tiny kernel rolls every
+// slot's ring buffer and recomputes scale / inverse scale for all slots at once.
+#include "common.cuh"
+
+namespace mtorus {
+
+__device__ __forceinline__ uint16_t cvt2_e4m3(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ uint16_t cvt2_e5m2(float a, float b) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %2, %1;" : "=h"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ void atomic_max_pos(float* addr, float v) {
+  // non-negative floats order like their bit patterns
+  atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
+}
+
+template <int FMT>  // 0 = E4M3, 1 = E5M2
+__global__ void __launch_bounds__(256) fp8_quantize_kernel(const bf16* __restrict__ x,
+                                                           uint8_t* __restrict__ out,
+                                                           const float* __restrict__ scale,
+                                                           float* __restrict__ amax, size_t n) {
+  __shared__ float red[32];
+  const float s = scale ? *scale : 1.f;
+  float m = 0.f;
+  const size_t nv = n / 16;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < nv;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float f[16];
+    unpack8(reinterpret_cast<const bf16x8*>(x)[2 * i], f);
+    unpack8(reinterpret_cast<const bf16x8*>(x)[2 * i + 1], f + 8);
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(f[4 * k]), fabsf(f[4 * k + 1])),
+                         fmaxf(fabsf(f[4 * k + 2]), fabsf(f[4 * k + 3]))));
+      const uint16_t lo = FMT == 0 ? cvt2_e4m3(f[4 * k] * s, f[4 * k + 1] * s)
+                                   : cvt2_e5m2(f[4 * k] * s, f[4 * k + 1] * s);
+      const uint16_t hi = FMT == 0 ? cvt2_e4m3(f[4 * k + 2] * s, f[4 * k + 3] * s)
+                                   : cvt2_e5m2(f[4 * k + 2] * s, f[4 * k + 3] * s);
+      w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  for (size_t i = nv * 16 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float f = __bfloat162float(x[i]);
+    m = fmaxf(m, fabsf(f));
+    const uint16_t c = FMT == 0 ? cvt2_e4m3(f * s, 0.f) : cvt2_e5m2(f * s, 0.f);
+    out[i] = (uint8_t)(c & 0xFF);
+  }
+  if (amax) {
+    m = block_max(m, red);
+    if (threadIdx.x == 0) atomic_max_pos(amax, m);
+  }
+}
+
+__global__ void __launch_bounds__(256) amax_kernel(const bf16* __restrict__ x, float* __restrict__ amax,
+                                                   size_t n) {
+  __shared__ float red[32];
+  float m = 0.f;
+  const size_t nv = n / 8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < nv;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float f[8];
+    unpack8(reinterpret_cast<const bf16x8*>(x)[i], f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(f[k]));
+  }
+  for (size_t i = nv * 8 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(__bfloat162float(x[i])));
+  m = block_max(m, red);
+  if (threadIdx.x == 0) atomic_max_pos(amax, m);
+}
+
+// Roll the ring buffers of all slots:  hist[s][cursor] = amax[s]; amax[s] = 0;
+// scale[s] = fmax[s] / max(hist[s]) (1 if 0); inv[s] = 1 / scale[s].
+// When `current` is set the scale comes from the amax just measured (used for
+// the very first step, whose history is still empty).
+__global__ void fp8_scaling_update_kernel(float* __restrict__ hist, float* __restrict__ amax,
+                                          float* __restrict__ scale, float* __restrict__ inv,
+                                          const float* __restrict__ fmax_per_slot, int slots,
+                                          int H, int cursor, int current) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= slots) return;
+  const float a = amax[s];
+  float* h = hist + (size_t)s * H;
+  h[cursor] = a;
+  float m = 0.f;
+  for (int i = 0; i < H; ++i) m = fmaxf(m, h[i]);
+  if (current) m = a;
+  const float sc = m > 0.f ? fmax_per_slot[s] / m : 1.f;
+  scale[s] = sc;
+  inv[s] = 1.f / sc;
+  amax[s] = 0.f;
+}
+
+template <int FMT>
+__global__ void fp8_dequantize_kernel(const uint8_t* __restrict__ q, float* __restrict__ out,
+                                      const float* __restrict__ inv_scale, size_t n) {
+  const float s = *inv_scale;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    if (FMT == 0) {
+      __nv_fp8_e4m3 v;
+      v.__x = q[i];
+      out[i] = float(v) * s;
+    } else {
+      __nv_fp8_e5m2 v;
+      v.__x = q[i];
+      out[i] = float(v) * s;
+    }
+  }
+}
+
+// Per-block quantisation (reference to_fp8_per_block): each block of `bs`
+// consecutive values gets scale = fmax / amax(block) (1 if 0).  One warp per block.
+template <int FMT>
+__global__ void fp8_quantize_blocks_kernel(const float* __restrict__ x, uint8_t* __restrict__ out,
+                                           float* __restrict__ scales, size_t n, int bs, float fmax,
+                                           size_t nblocks) {
+  const size_t b = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (b >= nblocks) return;
+  const size_t s0 = b * bs, s1 = min(n, s0 + (size_t)bs);
+  float m = 0.f;
+  for (size_t i = s0 + lane; i < s1; i += 32) m = fmaxf(m, fabsf(x[i]));
+  m = warp_max(m);
+  const float sc = m > 0.f ? fmax / m : 1.f;
+  if (lane == 0) scales[b] = sc;
+  for (size_t i = s0 + lane; i < s1; i += 32) {
+    const uint16_t c = FMT == 0 ? cvt2_e4m3(x[i] * sc, 0.f) : cvt2_e5m2(x[i] * sc, 0.f);
+    out[i] = (uint8_t)(c & 0xFF);
+  }
+}
+
+static int q_grid(size_t n, int per) {
+  return (int)std::max<size_t>(1, std::min<size_t>((n / per + 255) / 256, (size_t)num_sms() * 8));
+}
+
+void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::Tensor>& scale,
+                  const c10::optional<at::Tensor>& amax, int64_t fmt) {
+  MT_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "fp8_quantize: contiguous bf16 input");
+  MT_CHECK(out.element_size() == 1 && out.is_contiguous() && out.numel() == x.numel(), "fp8_quantize: out");
+  MT_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+               reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+           "fp8_quantize: 16-byte aligned buffers");
+  const size_t n = x.numel();
+  if (n == 0) return;
+  const float* sp = scale.has_value() ? scale->data_ptr<float>() : nullptr;
+  float* ap = amax.has_value() ? amax->data_ptr<float>() : nullptr;
+  const auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto* op = reinterpret_cast<uint8_t*>(out.data_ptr());
+  if (fmt == 0)
+    fp8_quantize_kernel<0><<<q_grid(n, 16), 256, 0, cur_stream()>>>(xp, op, sp, ap, n);
+  else
+    fp8_quantize_kernel<1><<<q_grid(n, 16), 256, 0, cur_stream()>>>(xp, op, sp, ap, n);
+  MT_LAUNCH_CHECK();
+}
+
+void fp8_amax(const at::Tensor& x, at::Tensor amax) {
+  MT_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "fp8_amax: contiguous bf16");
+  const size_t n = x.numel();
+  if (n == 0) return;
+  amax_kernel<<<q_grid(n, 8), 256, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()),
+                                                      amax.data_ptr<float>(), n);
+  MT_LAUNCH_CHECK();
+}
+
+void fp8_scaling_update(at::Tensor hist, at::Tensor amax, at::Tensor scale, at::Tensor inv,
+                        const at::Tensor& fmax, int64_t cursor, bool current) {
+  const int slots = amax.numel();
+  const int H = hist.numel() / std::max(slots, 1);
+  if (slots == 0) return;
+  fp8_scaling_update_kernel<<<(slots + 127) / 128, 128, 0, cur_stream()>>>(
+      hist.data_ptr<float>(), amax.data_ptr<float>(), scale.data_ptr<float>(), inv.data_ptr<float>(),
+      fmax.data_ptr<float>(), slots, H, (int)cursor, current ? 1 : 0);
+  MT_LAUNCH_CHECK();
+}
+
+void fp8_dequantize(const at::Tensor& q, at::Tensor out, const at::Tensor& inv_scale, int64_t fmt) {
+  const size_t n = q.numel();
+  if (n == 0) return;
+  if (fmt == 0)
+    fp8_dequantize_kernel<0><<<q_grid(n, 1), 256, 0, cur_stream()>>>(
+        reinterpret_cast<const uint8_t*>(q.data_ptr()), out.data_ptr<float>(),
+        inv_scale.data_ptr<float>(), n);
+  else
+    fp8_dequantize_kernel<1><<<q_grid(n, 1), 256, 0, cur_stream()>>>(
+        reinterpret_cast<const uint8_t*>(q.data_ptr()), out.data_ptr<float>(),
+        inv_scale.data_ptr<float>(), n);
+  MT_LAUNCH_CHECK();
+}
+
+void fp8_quantize_blocks(const at::Tensor& x, at::Tensor out, at::Tensor scales, int64_t block_size,
+                         double fmax, int64_t fmt) {
+  MT_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous(), "fp8_quantize_blocks: contiguous fp32");
+  const size_t n = x.numel();
+  const size_t nb = (n + block_size - 1) / block_size;
+  if (n == 0) return;
+  const int threads = 256;
+  const int grid = (int)((nb * 32 + threads - 1) / threads);
+  if (fmt == 0)
+    fp8_quantize_blocks_kernel<0><<<grid, threads, 0, cur_stream()>>>(
+        x.data_ptr<float>(), reinterpret_cast<uint8_t*>(out.data_ptr()), scales.data_ptr<float>(), n,
+        (int)block_size, (float)fmax, nb);
+  else
+    fp8_quantize_blocks_kernel<1><<<grid, threads, 0, cur_stream()>>>(
+        x.data_ptr<float>(), reinterpret_cast<uint8_t*>(out.data_ptr()), scales.data_ptr<float>(), n,
+        (int)block_size, (float)fmax, nb);
+  MT_LAUNCH_CHECK();
+}
+
+}  // namespace mtorus

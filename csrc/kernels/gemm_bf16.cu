@@ -39,6 +39,7 @@ struct GemmEpilogue {
   const bf16* aux;      // dGELU: result *= gelu'(aux[m, n]) or null
   int64_t ldaux;
   const float* alpha;   // device scalar multiplier or null
+  const float* alpha2;  // second device scalar multiplier (e.g. the other operand's 1/scale) or null
 };
 
 namespace {
@@ -331,11 +332,10 @@ namespace {
 
 constexpr int P_BM = 128;  // rows per CTA (pair tile M = 256)
 constexpr int P_BN = 256;  // pair tile N; each CTA stages 128 rows of B
-constexpr int P_BK = 64;
 constexpr int P_STAGES = 5;
 constexpr int P_GROUP_M = 8;  // pair tiles per raster group along M
-constexpr int P_A_BYTES = P_BM * P_BK * 2;
-constexpr int P_B_BYTES = (P_BN / 2) * P_BK * 2;
+constexpr int P_A_BYTES = P_BM * 128;        // 128 rows x 128 bytes of K
+constexpr int P_B_BYTES = (P_BN / 2) * 128;  // 128 rows of B x 128 bytes of K
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 // Epilogue staging (per epilogue warp): two 32x32 output chunks (fp32 worst case,
 // 4 KB each) and two 32x32 bf16 GELU chunks, written to global memory by TMA.
@@ -363,12 +363,20 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n,
 
 }  // namespace
 
+// EB = operand element bytes: 2 (bf16, kind::f16) or 1 (fp8 E4M3/E5M2, kind::f8f6f4).
+// A k-block is always 128 bytes of K per row (64 bf16 / 128 fp8), so the stage
+// layout is identical and an fp8 stage carries twice the MMA work.
+template <int EB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_bf16_2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
-                         const __grid_constant__ CUtensorMap tma_b,
-                         const __grid_constant__ CUtensorMap tma_d,
-                         const __grid_constant__ CUtensorMap tma_act, int M, int N, int K, int a_mn,
-                         int b_mn, GemmEpilogue ep, int* status) {
+    gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                    const __grid_constant__ CUtensorMap tma_b,
+                    const __grid_constant__ CUtensorMap tma_d,
+                    const __grid_constant__ CUtensorMap tma_act, int M, int N, int K, int a_mn,
+                    int b_mn, uint32_t idesc, GemmEpilogue ep, int* status) {
+  constexpr int BK = 128 / EB;       // K elements per stage
+  constexpr int MMA_K = 32 / EB;     // K elements per tcgen05.mma
+  constexpr int MN_BOX = 128 / EB;   // MN elements per 128-byte swizzle row
+  constexpr int A_BOXES = P_BM * EB / 128, B_BOXES = (P_BN / 2) * EB / 128;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -381,7 +389,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
   const int num_m = (M + 2 * P_BM - 1) / (2 * P_BM), num_n = (N + P_BN - 1) / P_BN;
   const int num_tiles = num_m * num_n;
-  const int num_kb = (K + P_BK - 1) / P_BK;
+  const int num_kb = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) {
@@ -423,18 +431,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * P_STAGE_BYTES;
           uint8_t* sb = sa + P_A_BYTES;
           if (!a_mn) {
-            tma_load_2d_pair(sa, &tma_a, &ctl->full[stage], kb * P_BK, m0);
+            tma_load_2d_pair(sa, &tma_a, &ctl->full[stage], kb * BK, m0);
           } else {
 #pragma unroll
-            for (int j = 0; j < P_BM / 64; ++j)
-              tma_load_2d_pair(sa + j * (P_BK * 128), &tma_a, &ctl->full[stage], m0 + j * 64, kb * P_BK);
+            for (int j = 0; j < A_BOXES; ++j)
+              tma_load_2d_pair(sa + j * (BK * 128), &tma_a, &ctl->full[stage], m0 + j * MN_BOX, kb * BK);
           }
           if (!b_mn) {
-            tma_load_2d_pair(sb, &tma_b, &ctl->full[stage], kb * P_BK, n0);
+            tma_load_2d_pair(sb, &tma_b, &ctl->full[stage], kb * BK, n0);
           } else {
 #pragma unroll
-            for (int j = 0; j < (P_BN / 2) / 64; ++j)
-              tma_load_2d_pair(sb + j * (P_BK * 128), &tma_b, &ctl->full[stage], n0 + j * 64, kb * P_BK);
+            for (int j = 0; j < B_BOXES; ++j)
+              tma_load_2d_pair(sb + j * (BK * 128), &tma_b, &ctl->full[stage], n0 + j * MN_BOX, kb * BK);
           }
           if (++stage == P_STAGES) {
             stage = 0;
@@ -446,7 +454,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (leader && lane == 0) {
       // ---------------------------------------------------------- MMA issuer (leader)
-      const uint32_t idesc = make_idesc_bf16(2 * P_BM, P_BN, a_mn, b_mn);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -466,12 +473,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
           const uint32_t sb = sa + P_A_BYTES;
 #pragma unroll
-          for (int k = 0; k < P_BK / 16; ++k) {
-            const uint64_t ad = a_mn ? make_sdesc(sa + k * 2048, P_BK * 128, 1024, kSwizzle128B)
+          for (int k = 0; k < BK / MMA_K; ++k) {
+            const uint64_t ad = a_mn ? make_sdesc(sa + k * MMA_K * 128, BK * 128, 1024, kSwizzle128B)
                                      : make_sdesc(sa + k * 32, 16, 1024, kSwizzle128B);
-            const uint64_t bd = b_mn ? make_sdesc(sb + k * 2048, P_BK * 128, 1024, kSwizzle128B)
+            const uint64_t bd = b_mn ? make_sdesc(sb + k * MMA_K * 128, BK * 128, 1024, kSwizzle128B)
                                      : make_sdesc(sb + k * 32, 16, 1024, kSwizzle128B);
-            umma_f16_2sm(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (EB == 2)
+              umma_f16_2sm(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f8_2sm(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_2sm_mc(&ctl->empty[stage], 0x3);
           if (++stage == P_STAGES) {
@@ -505,7 +515,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row0 = mb * 2 * P_BM + (int)rank * P_BM + q * 32;
       const int m = row0 + lane;
-      const float alpha = ep.alpha ? *ep.alpha : 1.f;
+      const float alpha = (ep.alpha ? *ep.alpha : 1.f) * (ep.alpha2 ? *ep.alpha2 : 1.f);
 #pragma unroll 1
       for (int c = 0; c < P_BN / 32; ++c, ++chunk_count) {
         uint32_t r[32];
@@ -667,38 +677,34 @@ int64_t gemm_status(bool reset) {
   return h;
 }
 
-static void check_operand(const at::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, ": bf16 CUDA tensor expected");
+static void check_operand(const at::Tensor& t, const char* name, int elem_bytes) {
+  TORCH_CHECK(t.is_cuda() && t.element_size() == elem_bytes, name, ": CUDA tensor with ", elem_bytes,
+              "-byte elements expected");
   TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, ": 2-D with unit inner stride expected");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, ": 16-byte aligned base required");
-  TORCH_CHECK((t.stride(0) * 2) % 16 == 0, name, ": row stride must be a multiple of 16 bytes");
+  TORCH_CHECK((t.stride(0) * elem_bytes) % 16 == 0, name, ": row stride must be a multiple of 16 bytes");
 }
 
-// A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] (b_mn=false) or [K,N] (b_mn=true).
-void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor D,
-               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
-               const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
-               const c10::optional<at::Tensor>& alpha, bool beta) {
-  check_operand(A, "A");
-  check_operand(B, "B");
-  const int64_t M = a_mn ? A.size(1) : A.size(0);
-  const int64_t K = a_mn ? A.size(0) : A.size(1);
-  const int64_t N = b_mn ? B.size(1) : B.size(0);
-  const int64_t Kb = b_mn ? B.size(0) : B.size(1);
-  TORCH_CHECK(K == Kb, "gemm_bf16: K mismatch ", K, " vs ", Kb);
+// SMs left free for concurrently running communication kernels (set while the
+// data-parallel reducer overlaps backward): persistent GEMMs size their grid to
+// the rest so a comm kernel never leaves a GEMM CTA waiting for an SM.
+static int g_reserved_sms = 0;
+void gemm_set_reserved_sms(int64_t n) { g_reserved_sms = (int)std::max<int64_t>(0, n); }
+
+static GemmEpilogue build_epilogue(at::Tensor& D, int64_t M, int64_t N,
+                                   const c10::optional<at::Tensor>& bias,
+                                   const c10::optional<at::Tensor>& residual,
+                                   const c10::optional<at::Tensor>& act,
+                                   const c10::optional<at::Tensor>& aux,
+                                   const c10::optional<at::Tensor>& alpha,
+                                   const c10::optional<at::Tensor>& alpha2, bool beta) {
   TORCH_CHECK(D.dim() == 2 && D.size(0) == M && D.size(1) == N && D.stride(1) == 1,
-              "gemm_bf16: D must be [M, N] with unit inner stride");
-  TORCH_CHECK(N % 8 == 0, "gemm_bf16: N must be a multiple of 8");
+              "gemm: D must be [M, N] with unit inner stride");
+  TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
   const bool out_f32 = D.scalar_type() == at::kFloat;
-  TORCH_CHECK(out_f32 || D.scalar_type() == at::kBFloat16, "gemm_bf16: D must be bf16 or fp32");
+  TORCH_CHECK(out_f32 || D.scalar_type() == at::kBFloat16, "gemm: D must be bf16 or fp32");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(D.data_ptr()) % 16 == 0 && (D.stride(0) % 8) == 0,
-              "gemm_bf16: D alignment");
-  if (M == 0 || N == 0) return;
-  ensure_context();
-  if (K == 0) {
-    if (!beta) D.zero_();
-    return;
-  }
+              "gemm: D alignment");
   GemmEpilogue ep{};
   ep.D = D.data_ptr();
   ep.ldd = D.stride(0);
@@ -728,42 +734,85 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
     TORCH_CHECK(alpha->scalar_type() == at::kFloat, "alpha must be an fp32 device scalar");
     ep.alpha = alpha->data_ptr<float>();
   }
-  const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (alpha2.has_value()) {
+    TORCH_CHECK(alpha2->scalar_type() == at::kFloat, "alpha2 must be an fp32 device scalar");
+    ep.alpha2 = alpha2->data_ptr<float>();
+  }
+  return ep;
+}
+
+template <int EB>
+static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor& D,
+                        const c10::optional<at::Tensor>& act, const GemmEpilogue& ep, int64_t M,
+                        int64_t N, int64_t K, uint32_t idesc) {
+  const auto dt = EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const auto swz = CU_TENSOR_MAP_SWIZZLE_128B;
-  static const bool force_1sm = std::getenv("MTORUS_GEMM_1SM") != nullptr;
-  if (M >= 2 * P_BM && !force_1sm) {
-    // CTA-pair kernel: per-CTA boxes of 128 rows of A and 128 rows of B.
-    CUtensorMap ta = a_mn ? make_tma_2d(A.data_ptr(), dt, 2, M, K, A.stride(0), 64, P_BK, swz)
-                          : make_tma_2d(A.data_ptr(), dt, 2, K, M, A.stride(0), P_BK, P_BM, swz);
-    CUtensorMap tb = b_mn ? make_tma_2d(B.data_ptr(), dt, 2, N, K, B.stride(0), 64, P_BK, swz)
-                          : make_tma_2d(B.data_ptr(), dt, 2, K, N, B.stride(0), P_BK, P_BN / 2, swz);
-    CUtensorMap td = out_f32
-        ? make_tma_2d(D.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, D.stride(0), 32, 32,
-                      CU_TENSOR_MAP_SWIZZLE_128B)
-        : make_tma_2d(D.data_ptr(), dt, 2, N, M, D.stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
-    CUtensorMap tact = act.has_value()
-        ? make_tma_2d(act->data_ptr(), dt, 2, N, M, act->stride(0), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
-        : td;
-    const int num_tiles = (int)(((M + 2 * P_BM - 1) / (2 * P_BM)) * ((N + P_BN - 1) / P_BN));
-    const int pairs = std::min(num_tiles, num_sms() / 2);
-    const size_t smem = P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + sizeof(PairSmem) + 1024;
-    static bool attr2_set = false;
-    if (!attr2_set) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_bf16_2sm_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      attr2_set = true;
-    }
-    gemm_bf16_2sm_kernel<<<2 * pairs, kThreads, smem, cur_stream()>>>(
-        ta, tb, td, tact, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, ep, gemm_status_ptr());
-    MT_LAUNCH_CHECK();
+  constexpr uint32_t BK = 128 / EB, MN_BOX = 128 / EB;
+  // per-CTA boxes: 128 rows of A and 128 rows of B (the pair covers 256 x 256)
+  CUtensorMap ta = a_mn ? make_tma_2d(A.data_ptr(), dt, EB, M, K, A.stride(0), MN_BOX, BK, swz)
+                        : make_tma_2d(A.data_ptr(), dt, EB, K, M, A.stride(0), BK, P_BM, swz);
+  CUtensorMap tb = b_mn ? make_tma_2d(B.data_ptr(), dt, EB, N, K, B.stride(0), MN_BOX, BK, swz)
+                        : make_tma_2d(B.data_ptr(), dt, EB, K, N, B.stride(0), BK, P_BN / 2, swz);
+  const bool out_f32 = ep.out_f32 != 0;
+  CUtensorMap td = out_f32
+      ? make_tma_2d(D.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, D.stride(0), 32, 32,
+                    CU_TENSOR_MAP_SWIZZLE_128B)
+      : make_tma_2d(D.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, D.stride(0), 32, 32,
+                    CU_TENSOR_MAP_SWIZZLE_64B);
+  CUtensorMap tact = act.has_value()
+      ? make_tma_2d(act->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, act->stride(0), 32, 32,
+                    CU_TENSOR_MAP_SWIZZLE_64B)
+      : td;
+  const int num_tiles = (int)(((M + 2 * P_BM - 1) / (2 * P_BM)) * ((N + P_BN - 1) / P_BN));
+  const int avail_pairs = std::max(1, (num_sms() - g_reserved_sms) / 2);
+  const int pairs = std::min(num_tiles, avail_pairs);
+  const size_t smem = P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + sizeof(PairSmem) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set = true;
+  }
+  gemm_2sm_kernel<EB><<<2 * pairs, kThreads, smem, cur_stream()>>>(
+      ta, tb, td, tact, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, idesc, ep,
+      gemm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+// A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] (b_mn=false) or [K,N] (b_mn=true).
+void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor D,
+               const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+               const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
+               const c10::optional<at::Tensor>& alpha, bool beta) {
+  check_operand(A, "A", 2);
+  check_operand(B, "B", 2);
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 operands");
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  const int64_t Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "gemm_bf16: K mismatch ", K, " vs ", Kb);
+  GemmEpilogue ep = build_epilogue(D, M, N, bias, residual, act, aux, alpha, c10::nullopt, beta);
+  if (M == 0 || N == 0) return;
+  ensure_context();
+  if (K == 0) {
+    if (!beta) D.zero_();
     return;
   }
+  static const bool force_1sm = std::getenv("MTORUS_GEMM_1SM") != nullptr;
+  if (M >= 2 * P_BM && !force_1sm) {
+    launch_pair<2>(A, a_mn, B, b_mn, D, act, ep, M, N, K,
+                   make_idesc_bf16(2 * P_BM, P_BN, a_mn ? 1 : 0, b_mn ? 1 : 0));
+    return;
+  }
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto swz = CU_TENSOR_MAP_SWIZZLE_128B;
   CUtensorMap ta = a_mn ? make_tma_2d(A.data_ptr(), dt, 2, M, K, A.stride(0), 64, BK, swz)
                         : make_tma_2d(A.data_ptr(), dt, 2, K, M, A.stride(0), BK, BM, swz);
   CUtensorMap tb = b_mn ? make_tma_2d(B.data_ptr(), dt, 2, N, K, B.stride(0), 64, BK, swz)
                         : make_tma_2d(B.data_ptr(), dt, 2, K, N, B.stride(0), BK, BN, swz);
   const int num_tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
-  const int grid = std::min(num_tiles, num_sms());
+  const int grid = std::min(num_tiles, std::max(1, num_sms() - g_reserved_sms));
   const size_t smem = STAGES * STAGE_BYTES + sizeof(Smem) + 1024;
   static bool attr_set = false;
   if (!attr_set) {
@@ -775,6 +824,32 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
                                                                a_mn ? 1 : 0, b_mn ? 1 : 0, ep,
                                                                gemm_status_ptr());
   MT_LAUNCH_CHECK();
+}
+
+// FP8 GEMM (tcgen05 kind::f8f6f4, fp32 accumulate): A / B are 1-byte E4M3 (fmt 0)
+// or E5M2 (fmt 1) codes; the epilogue multiplies by alpha * alpha2 (the operands'
+// inverse scales) before bias / residual / GELU / dGELU / fp32 accumulate.
+void gemm_fp8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
+              int64_t b_fmt, at::Tensor D, const c10::optional<at::Tensor>& bias,
+              const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
+              const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha,
+              const c10::optional<at::Tensor>& alpha2, bool beta) {
+  check_operand(A, "A", 1);
+  check_operand(B, "B", 1);
+  TORCH_CHECK((a_fmt == 0 || a_fmt == 1) && (b_fmt == 0 || b_fmt == 1), "gemm_fp8: formats are 0 (E4M3) / 1 (E5M2)");
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  const int64_t Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "gemm_fp8: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(K % 16 == 0, "gemm_fp8: K must be a multiple of 16");
+  TORCH_CHECK(!a_mn || M % 16 == 0, "gemm_fp8: M must be a multiple of 16 for an MN-major A");
+  TORCH_CHECK(!b_mn || N % 16 == 0, "gemm_fp8: N must be a multiple of 16 for an MN-major B");
+  GemmEpilogue ep = build_epilogue(D, M, N, bias, residual, act, aux, alpha, alpha2, beta);
+  if (M == 0 || N == 0) return;
+  ensure_context();
+  launch_pair<1>(A, a_mn, B, b_mn, D, act, ep, M, N, K,
+                 make_idesc_f8(2 * P_BM, P_BN, (int)a_fmt, (int)b_fmt, a_mn ? 1 : 0, b_mn ? 1 : 0));
 }
 
 }  // namespace mtorus

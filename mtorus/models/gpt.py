@@ -190,16 +190,16 @@ class TransformerBlock(nn.Module):
         return self.dropout(self.ff(self.norm2(x))) + x
 
     # ---------------------------------------------------------------- fused path
-    def fused_forward(self, x2d, B: int, S: int):
+    def fused_forward(self, x2d, B: int, S: int, fp8=None):
         from ..ops.fused import AttnBlockFn, MLPBlockFn
 
         a = self.attention
         x2d = AttnBlockFn.apply(x2d, (self.norm1.gamma, self.norm1.beta, self.norm1.eps),
                                 (self._qkv_w, self._qkv_b), (a.out_proj.weight, a.out_proj.bias),
-                                (B, S, a.num_heads, a.d_head))
+                                (B, S, a.num_heads, a.d_head), fp8)
         return MLPBlockFn.apply(x2d, (self.norm2.gamma, self.norm2.beta, self.norm2.eps),
                                 (self.ff.linear1.weight, self.ff.linear1.bias,
-                                 self.ff.linear2.weight, self.ff.linear2.bias))
+                                 self.ff.linear2.weight, self.ff.linear2.bias), fp8)
 
 
 class GptModel(nn.Module):
@@ -284,9 +284,39 @@ class GptModel(nn.Module):
         B, S = input_ids.shape
         x = EmbeddingFn.apply(input_ids, grad_anchor(input_ids.device),
                               (self.token_embedding.weight, self.position_embedding.weight), S)
-        for blk in self.blocks:
-            x = blk.fused_forward(x, B, S)
+        st = getattr(self, "fp8_state", None)
+        for i, blk in enumerate(self.blocks):
+            x = blk.fused_forward(x, B, S, None if st is None else (st, f"L{i}"))
         return LayerNormFn.apply(x, (self.ln_f.gamma, self.ln_f.beta), self.ln_f.eps)
+
+    # ---------------------------------------------------------------- FP8
+    def fp8_weights(self):
+        """(name, weight-like) pairs whose GEMMs run in FP8 (the LM head stays bf16)."""
+        out = []
+        for i, blk in enumerate(self.blocks):
+            out += [(f"L{i}.qkv_w", blk._qkv_w), (f"L{i}.out_w", blk.attention.out_proj.weight),
+                    (f"L{i}.ffn1_w", blk.ff.linear1.weight), (f"L{i}.ffn2_w", blk.ff.linear2.weight)]
+        return out
+
+    def enable_fp8(self, history: int = 16):
+        """E4M3 weights / activations and E5M2 gradients with delayed scaling for the
+        block GEMMs; call ``refresh_fp8_weights()`` after every optimizer step and
+        ``fp8_state.end_step()`` at the end of every step."""
+        from ..ops.fp8 import Fp8State
+
+        assert self.flat is not None, "flatten() first"
+        self.fp8_state = Fp8State(self.flat.device, history)
+        for name, w in self.fp8_weights():
+            w.w8 = torch.empty(w.shape, dtype=torch.uint8, device=self.flat.device)
+            w.fp8_name = name
+        return self.fp8_state
+
+    def refresh_fp8_weights(self):
+        from ..ops import fp8 as F8
+
+        st = self.fp8_state
+        for name, w in self.fp8_weights():
+            _, w.w8_inv = st.quantize_into(w.w16, name, F8.E4M3, w.w8)
 
     def fused_loss(self, input_ids: torch.Tensor, targets: torch.Tensor,
                    grad_scale: Optional[torch.Tensor] = None) -> torch.Tensor:

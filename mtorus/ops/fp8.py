@@ -1,0 +1,143 @@
+"""Device FP8 with delayed scaling: quantisation kernels, the amax-history state,
+and the FP8 GEMM entry point.
+
+Recipe (the reference's MixedPrecisionConfig defaults, crates/mt-core/src/
+precision/config.rs): E4M3 for weights and activations in the forward pass,
+E5M2 for gradients in the backward pass, per-tensor scales from a DelayedScaling
+amax history (crates/mt-core/src/precision/scaling.rs) with the reference's
+format maxima (416 / 49152).  All scales live on the device: quantisation reads
+the slot's current scale, folds max|x| into the slot's running amax, and one
+kernel per step rolls every history ring and recomputes the scales.  The first
+step, whose history is empty, measures each tensor's amax right before
+quantising it ("current" scaling).
+
+FP8 GEMMs run on tcgen05 kind::f8f6f4 with fp32 accumulation; the epilogue
+multiplies by the two operands' inverse scales.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from .._ext import cuda as _cuda
+
+E4M3, E5M2 = 0, 1
+FMT_MAX = {E4M3: 416.0, E5M2: 49152.0}  # reference format maxima (float8 crate MAX)
+
+
+def quantize(x: torch.Tensor, fmt: int, scale: Optional[torch.Tensor] = None,
+             amax: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16 -> fp8 codes (uint8), scaled by ``scale`` (device scalar); max|x| folds into ``amax``."""
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    _cuda().fp8_quantize(x, out, scale, amax, int(fmt))
+    return out
+
+
+def dequantize(q: torch.Tensor, inv_scale: torch.Tensor, fmt: int) -> torch.Tensor:
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    _cuda().fp8_dequantize(q.contiguous(), out, inv_scale, int(fmt))
+    return out
+
+
+def quantize_blocks(x: torch.Tensor, fmt: int, block_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-block quantisation (reference to_fp8_per_block) on device: codes + one fp32 scale per block."""
+    x = x.contiguous().float()
+    nb = (x.numel() + block_size - 1) // block_size
+    out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(nb, dtype=torch.float32, device=x.device)
+    _cuda().fp8_quantize_blocks(x, out, scales, int(block_size), FMT_MAX[fmt], int(fmt))
+    return out, scales
+
+
+def gemm_fp8(a, a_fmt: int, b, b_fmt: int, out=None, *, a_mn=False, b_mn=False, bias=None, residual=None,
+             act=None, aux=None, alpha=None, alpha2=None, accumulate=False, out_dtype=torch.bfloat16):
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    _cuda().gemm_fp8(a, bool(a_mn), int(a_fmt), b, bool(b_mn), int(b_fmt), out, bias, residual, act, aux,
+                     alpha, alpha2, bool(accumulate))
+    return out
+
+
+class Fp8State:
+    """Amax histories, scales and inverse scales of every FP8 tensor role of a model."""
+
+    def __init__(self, device, history: int = 16, capacity: int = 4096):
+        self.device = torch.device(device)
+        self.history = history
+        self.names: Dict[str, int] = {}
+        self.fmts = []
+        self.cap = capacity
+        d = self.device
+        # fixed capacity: views of these buffers are captured by kernels and saved for backward
+        self.hist = torch.zeros(capacity, history, device=d)
+        self.amax = torch.zeros(capacity, device=d)
+        self.scale = torch.ones(capacity, device=d)
+        self.inv = torch.ones(capacity, device=d)
+        self.fmax = torch.zeros(capacity, device=d)
+        self.cursor = 0
+        self.first_step = True
+
+    def slot(self, name: str, fmt: int) -> int:
+        s = self.names.get(name)
+        if s is None:
+            s = len(self.fmts)
+            if s >= self.cap:
+                raise RuntimeError(f"Fp8State capacity {self.cap} exceeded")
+            self.names[name] = s
+            self.fmts.append(fmt)
+            self.fmax[s] = FMT_MAX[fmt]
+        return s
+
+    def quantize(self, x: torch.Tensor, name: str, fmt: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """-> (codes, inverse-scale view).  The inverse scale is the one this step used."""
+        s = self.slot(name, fmt)
+        sl = slice(s, s + 1)
+        if self.first_step:
+            _cuda().fp8_amax(x.contiguous(), self.amax[sl])
+            _cuda().fp8_scaling_update(self.hist[sl], self.amax[sl], self.scale[sl], self.inv[sl],
+                                       self.fmax[sl], self.cursor, True)
+        q = quantize(x, fmt, self.scale[sl], self.amax[sl])
+        # the inverse scale stays valid until end_step(), i.e. through this step's backward
+        return q, self.inv[sl]
+
+    def quantize_into(self, x: torch.Tensor, name: str, fmt: int, out: torch.Tensor):
+        s = self.slot(name, fmt)
+        sl = slice(s, s + 1)
+        if self.first_step:
+            _cuda().fp8_amax(x.contiguous(), self.amax[sl])
+            _cuda().fp8_scaling_update(self.hist[sl], self.amax[sl], self.scale[sl], self.inv[sl],
+                                       self.fmax[sl], self.cursor, True)
+        quantize(x, fmt, self.scale[sl], self.amax[sl], out=out)
+        return out, self.inv[sl]
+
+    def end_step(self) -> None:
+        """Roll all histories (delayed scaling): the next step's scales come from them."""
+        n = len(self.fmts)
+        if n:
+            _cuda().fp8_scaling_update(self.hist[:n], self.amax[:n], self.scale[:n], self.inv[:n], self.fmax[:n],
+                                       self.cursor, False)
+        self.cursor = (self.cursor + 1) % self.history
+        self.first_step = False
+
+    def state_dict(self) -> dict:
+        n = len(self.fmts)
+        return {"names": dict(self.names), "fmts": list(self.fmts), "hist": self.hist[:n].cpu(),
+                "scale": self.scale[:n].cpu(), "cursor": self.cursor, "history": self.history}
+
+    def load_state_dict(self, sd: dict) -> None:
+        for name, fmt in zip(sorted(sd["names"], key=sd["names"].get), sd["fmts"]):
+            self.slot(name, fmt)
+        n = len(sd["fmts"])
+        self.hist[:n] = sd["hist"].to(self.device)
+        self.scale[:n] = sd["scale"].to(self.device)
+        self.inv[:n] = 1.0 / self.scale[:n]
+        self.cursor = sd["cursor"]
+        self.first_step = False
+
+
+__all__ = ["E4M3", "E5M2", "FMT_MAX", "quantize", "dequantize", "quantize_blocks", "gemm_fp8", "Fp8State"]

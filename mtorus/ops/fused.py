@@ -16,6 +16,7 @@ from typing import Optional
 import torch
 from torch.autograd import Function
 
+from . import fp8 as F8
 from . import kernels as K
 
 
@@ -148,22 +149,36 @@ class AttnBlockFn(Function):
     backward adds the residual gradient in the same kernel."""
 
     @staticmethod
-    def forward(ctx, x2d, ln, qkv_params, out_params, shape):
+    def forward(ctx, x2d, ln, qkv_params, out_params, shape, fp8=None):
         from .attention import causal_attention
 
         B, S, H, dh = shape
         h, mean, rstd = _ln_fwd(x2d, ln)
         wq, bq = qkv_params
-        qkv = K.gemm(h, wq.w16, bias=bq.data)
+        wo, bo = out_params
+        if fp8 is not None:
+            st, tag = fp8
+            h8, ih = st.quantize(h, tag + ".qkv_in", F8.E4M3)
+            qkv = F8.gemm_fp8(h8, F8.E4M3, wq.w8, F8.E4M3, bias=bq.data, alpha=ih, alpha2=wq.w8_inv)
+            h = h8
+        else:
+            qkv = K.gemm(h, wq.w16, bias=bq.data)
         with torch.enable_grad():
             qkv_leaf = qkv.detach().requires_grad_(True)
             o_graph = causal_attention(qkv_leaf, B, S, H, dh)
         o = o_graph.detach()
-        wo, bo = out_params
-        out = K.gemm(o, wo.w16, bias=bo.data, residual=x2d)
+        if fp8 is not None:
+            o8, io = st.quantize(o, tag + ".out_in", F8.E4M3)
+            out = F8.gemm_fp8(o8, F8.E4M3, wo.w8, F8.E4M3, bias=bo.data, residual=x2d, alpha=io,
+                              alpha2=wo.w8_inv)
+            o = o8
+            ctx.inv = (ih, io)
+        else:
+            out = K.gemm(o, wo.w16, bias=bo.data, residual=x2d)
         ctx.save_for_backward(x2d, mean, rstd, h, o)
         ctx.attn = (qkv_leaf, o_graph)
         ctx.params = (ln, qkv_params, out_params)
+        ctx.fp8 = fp8
         return out
 
     @staticmethod
@@ -173,18 +188,33 @@ class AttnBlockFn(Function):
         qkv_leaf, o_graph = ctx.attn
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
-        do = K.gemm(dout, wo.w16, b_mn=True)
-        K.gemm(dout, o, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        fp8 = ctx.fp8
+        if fp8 is not None:
+            st, tag = fp8
+            ih, io = ctx.inv
+            g8, ig = st.quantize(dout, tag + ".out_grad", F8.E5M2)
+            do = F8.gemm_fp8(g8, F8.E5M2, wo.w8, F8.E4M3, b_mn=True, alpha=ig, alpha2=wo.w8_inv)
+            F8.gemm_fp8(g8, F8.E5M2, o, F8.E4M3, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc,
+                        alpha=ig, alpha2=io)
+        else:
+            do = K.gemm(dout, wo.w16, b_mn=True)
+            K.gemm(dout, o, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc)
         K.colsum_(dout, bo.main_grad, acc)
         _grads_done(wo, bo)
         torch.autograd.backward(o_graph, do)
         dqkv = qkv_leaf.grad
         ctx.attn = None
-        K.gemm(dqkv, h, out=wq.main_grad, a_mn=True, b_mn=True, accumulate=acc)
         K.colsum_(dqkv, bq.main_grad, acc)
+        if fp8 is not None:
+            q8, iq = st.quantize(dqkv, tag + ".qkv_grad", F8.E5M2)
+            F8.gemm_fp8(q8, F8.E5M2, h, F8.E4M3, out=wq.main_grad, a_mn=True, b_mn=True, accumulate=acc,
+                        alpha=iq, alpha2=ih)
+            dh = F8.gemm_fp8(q8, F8.E5M2, wq.w8, F8.E4M3, b_mn=True, alpha=iq, alpha2=wq.w8_inv)
+        else:
+            K.gemm(dqkv, h, out=wq.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+            dh = K.gemm(dqkv, wq.w16, b_mn=True)
         _grads_done(wq, bq)
-        dh = K.gemm(dqkv, wq.w16, b_mn=True)
-        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None
 
 
 class MLPBlockFn(Function):
@@ -194,16 +224,28 @@ class MLPBlockFn(Function):
     adds the residual gradient."""
 
     @staticmethod
-    def forward(ctx, x2d, ln, params):
+    def forward(ctx, x2d, ln, params, fp8=None):
         w1, b1, w2, b2 = params
         h, mean, rstd = _ln_fwd(x2d, ln)
         T, F = h.shape[0], w1.shape[0]
         pre = torch.empty((T, F), dtype=torch.bfloat16, device=h.device)
         act = torch.empty_like(pre)
-        K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
-        out = K.gemm(act, w2.w16, bias=b2.data, residual=x2d)
+        if fp8 is not None:
+            st, tag = fp8
+            h8, ih = st.quantize(h, tag + ".ffn1_in", F8.E4M3)
+            F8.gemm_fp8(h8, F8.E4M3, w1.w8, F8.E4M3, out=pre, bias=b1.data, act=act, alpha=ih,
+                        alpha2=w1.w8_inv)
+            a8, ia = st.quantize(act, tag + ".ffn2_in", F8.E4M3)
+            out = F8.gemm_fp8(a8, F8.E4M3, w2.w8, F8.E4M3, bias=b2.data, residual=x2d, alpha=ia,
+                              alpha2=w2.w8_inv)
+            h, act = h8, a8
+            ctx.inv = (ih, ia)
+        else:
+            K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
+            out = K.gemm(act, w2.w16, bias=b2.data, residual=x2d)
         ctx.save_for_backward(x2d, mean, rstd, h, pre, act)
         ctx.params = (ln, params)
+        ctx.fp8 = fp8
         return out
 
     @staticmethod
@@ -212,15 +254,30 @@ class MLPBlockFn(Function):
         ln, (w1, b1, w2, b2) = ctx.params
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
-        dpre = K.gemm(dout, w2.w16, b_mn=True, aux=pre)
-        K.gemm(dout, act, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+        fp8 = ctx.fp8
+        if fp8 is not None:
+            st, tag = fp8
+            ih, ia = ctx.inv
+            g8, ig = st.quantize(dout, tag + ".ffn2_grad", F8.E5M2)
+            dpre = F8.gemm_fp8(g8, F8.E5M2, w2.w8, F8.E4M3, b_mn=True, aux=pre, alpha=ig, alpha2=w2.w8_inv)
+            F8.gemm_fp8(g8, F8.E5M2, act, F8.E4M3, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc,
+                        alpha=ig, alpha2=ia)
+        else:
+            dpre = K.gemm(dout, w2.w16, b_mn=True, aux=pre)
+            K.gemm(dout, act, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc)
         K.colsum_(dout, b2.main_grad, acc)
         _grads_done(w2, b2)
-        K.gemm(dpre, h, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc)
         K.colsum_(dpre, b1.main_grad, acc)
+        if fp8 is not None:
+            p8, ip = st.quantize(dpre, tag + ".ffn1_grad", F8.E5M2)
+            F8.gemm_fp8(p8, F8.E5M2, h, F8.E4M3, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc,
+                        alpha=ip, alpha2=ih)
+            dh = F8.gemm_fp8(p8, F8.E5M2, w1.w8, F8.E4M3, b_mn=True, alpha=ip, alpha2=w1.w8_inv)
+        else:
+            K.gemm(dpre, h, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+            dh = K.gemm(dpre, w1.w16, b_mn=True)
         _grads_done(w1, b1)
-        dh = K.gemm(dpre, w1.w16, b_mn=True)
-        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None
 
 
 class EmbeddingFn(Function):

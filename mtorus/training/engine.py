@@ -27,7 +27,8 @@ class GptTrainer:
     def __init__(self, config: GptConfig, device="cuda", lr: float = 3e-4, init: str = "normal",
                  seed: int = 0, dp_group=None, dp: str = "nccl", bucket_mb: float = 25.0,
                  loss_scale: Optional[DeviceLossScaleConfig] = None, max_grad_norm: float = 0.0,
-                 weight_decay: float = 0.0, warmup_steps: int = 0):
+                 weight_decay: float = 0.0, warmup_steps: int = 0, fp8: bool = False,
+                 fp8_history: int = 16):
         self.config = config
         self.device = torch.device(device)
         torch.manual_seed(seed)
@@ -45,6 +46,9 @@ class GptTrainer:
         self.global_step = 0
         self.reducer = None
         ls = loss_scale or DeviceLossScaleConfig()
+        self.fp8 = fp8
+        if fp8:
+            self.model.enable_fp8(fp8_history)
         if self.dp == "symm":
             from ..parallel.symm import SymmBucketReducer, ZeroAdam
 
@@ -73,6 +77,8 @@ class GptTrainer:
     def step_device(self, ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """One full training step on device tensors; returns the device loss (no sync)."""
         FusedGradState.accumulate = False
+        if self.fp8:
+            self.model.refresh_fp8_weights()
         FusedGradState.grad_ready_hook = self.reducer.on_ready if self.reducer is not None else None
         if hasattr(self.reducer, "begin_step"):
             self.reducer.begin_step()
@@ -82,6 +88,8 @@ class GptTrainer:
             self.reducer.finish()
         FusedGradState.grad_ready_hook = None
         self.opt.step(self.current_lr())
+        if self.fp8:
+            self.model.fp8_state.end_step()
         self.global_step += 1
         return loss.detach()
 

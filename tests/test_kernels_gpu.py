@@ -193,3 +193,72 @@ def test_overflow_skips_and_halves(K):
     torch.cuda.synchronize()
     assert torch.all(p == 1.0)
     assert st[2].item() == 2.0 and st[5].item() == 1.0
+
+
+# ---------------------------------------------------------------- FP8
+def _q(x, fmt, scale):
+    dt = torch.float8_e4m3fn if fmt == 0 else torch.float8_e5m2
+    mx = 448.0 if fmt == 0 else 57344.0
+    return (x.float() * scale).clamp(-mx, mx).to(dt)
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_fp8_quantize_matches_torch(fmt):
+    from mtorus.ops import fp8 as F8
+
+    x = (torch.randn(4099, 37, device="cuda") * 3).bfloat16()
+    scale = torch.tensor([17.0], device="cuda")
+    amax = torch.zeros(1, device="cuda")
+    q = F8.quantize(x, fmt, scale, amax)
+    ref = _q(x, fmt, 17.0).view(torch.uint8)
+    assert torch.equal(q, ref)
+    assert amax.item() == x.float().abs().max().item()
+
+
+@pytest.mark.parametrize("layout", ["tn", "dgrad", "wgrad"])
+@pytest.mark.parametrize("fa,fb", [(0, 0), (1, 0)])
+def test_gemm_fp8(layout, fa, fb):
+    from mtorus.ops import fp8 as F8
+
+    torch.manual_seed(7)
+    M, N, Kd = 512, 768, 384
+    A = torch.randn(M, Kd, device="cuda")
+    B = torch.randn(N, Kd, device="cuda")
+    sa, sb = 20.0, 30.0
+    A8, B8 = _q(A, fa, sa), _q(B, fb, sb)
+    ref = (A8.float() / sa) @ (B8.float() / sb).t()
+    ia = torch.tensor([1 / sa], device="cuda")
+    ib = torch.tensor([1 / sb], device="cuda")
+    if layout == "tn":
+        out = F8.gemm_fp8(A8.view(torch.uint8), fa, B8.view(torch.uint8), fb, alpha=ia, alpha2=ib)
+    elif layout == "dgrad":
+        out = F8.gemm_fp8(A8.view(torch.uint8), fa, B8.t().contiguous().view(torch.uint8), fb, b_mn=True,
+                          alpha=ia, alpha2=ib)
+    else:
+        out = F8.gemm_fp8(A8.t().contiguous().view(torch.uint8), fa, B8.t().contiguous().view(torch.uint8), fb,
+                          a_mn=True, b_mn=True, alpha=ia, alpha2=ib, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert K_status() == 0
+    assert _rel(out, ref) < 1e-2, _rel(out, ref)
+
+
+def K_status():
+    from mtorus.ops import kernels
+
+    return kernels.gemm_status()
+
+
+def test_fp8_state_delayed_scaling():
+    from mtorus.ops import fp8 as F8
+
+    st = F8.Fp8State("cuda", history=4)
+    x = torch.randn(1024, device="cuda").bfloat16()
+    q, inv = st.quantize(x, "a", F8.E4M3)
+    amax = x.float().abs().max().item()
+    assert abs(1.0 / inv.item() - 416.0 / amax) / (416.0 / amax) < 1e-6  # first step: current scaling
+    st.end_step()
+    q2, inv2 = st.quantize(x * 2, "a", F8.E4M3)
+    assert abs(1.0 / inv2.item() - 416.0 / amax) / (416.0 / amax) < 1e-6  # delayed: previous amax
+    st.end_step()
+    q3, inv3 = st.quantize(x, "a", F8.E4M3)
+    assert abs(1.0 / inv3.item() - 416.0 / (2 * amax)) / (416.0 / amax) < 1e-5

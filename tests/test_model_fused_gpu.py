@@ -46,3 +46,21 @@ def test_trainer_loss_decreases():
     x, y = t[:, :-1].contiguous().pin_memory(), t[:, 1:].contiguous().pin_memory()
     losses = [tr.train_step(x, y) for _ in range(30)]
     assert losses[-1] < losses[0] - 1.0, losses
+
+
+def test_fp8_training_tracks_bf16():
+    from mtorus.models.gpt import GptConfig
+    from mtorus.training.engine import GptTrainer
+
+    cfg = GptConfig(vocab_size=512, d_model=256, num_layers=2, num_heads=2, d_ff=1024, max_seq_len=128,
+                    dropout=0.0)
+    g = torch.Generator().manual_seed(0)
+    t = torch.randint(0, cfg.vocab_size, (4, 129), generator=g)
+    x, y = t[:, :-1].contiguous().pin_memory(), t[:, 1:].contiguous().pin_memory()
+    runs = {}
+    for fp8 in (False, True):
+        tr = GptTrainer(cfg, device="cuda", lr=2e-3, init="normal", seed=0, fp8=fp8)
+        runs[fp8] = [tr.train_step(x, y) for _ in range(20)]
+    a, b = runs[False], runs[True]
+    assert abs(a[0] - b[0]) < 0.05 * a[0]
+    assert b[-1] < b[0] - 1.0 and abs(a[-1] - b[-1]) < 0.15 * a[-1], (a, b)
