@@ -54,6 +54,12 @@ def main() -> int:
         print(json.dumps({"impl": "reference", "unavailable": REF_UNAVAILABLE}))
         return 0
 
+    # Libraries (NCCL's version banner, extension builds) may write to stdout; the
+    # contract is one JSON line there, so fd 1 goes to stderr until the result is out.
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+
     import torch
     import torch.distributed as dist
 
@@ -180,7 +186,7 @@ def main() -> int:
             "api": "mtorus.training.engine.GptTrainer.train_step",
         }
     if rank == 0:
-        print(json.dumps(out), flush=True)
+        os.write(json_fd, (json.dumps(out) + "\n").encode())
     if world > 1:
         barrier()
         dist.destroy_process_group()

@@ -52,6 +52,38 @@ def main():
         ("lm_wgrad", V, d, T, "wgrad"), ("square8k", 8192, 8192, 8192, "tn"),
     ]
     rows = []
+    from mtorus.ops import fp8 as F8
+
+    fp8_cases = [("qkv_fwd_fp8", T, 3 * d, d, "tn"), ("ffn1_fwd_fp8", T, F, d, "tn"), ("ffn2_fwd_fp8", T, d, F, "tn"),
+                 ("ffn2_dgrad_fp8", T, F, d, "dgrad"), ("ffn1_wgrad_fp8", F, d, T, "wgrad"),
+                 ("square8k_fp8", 8192, 8192, 8192, "tn")]
+    one = torch.ones(1, device="cuda")
+    for name, M, N, Kd, lay in fp8_cases:
+        A = (torch.randn(M, Kd, device="cuda") if lay != "wgrad" else torch.randn(Kd, M, device="cuda")).to(
+            torch.float8_e4m3fn).view(torch.uint8)
+        B = (torch.randn(N, Kd, device="cuda") if lay == "tn" else torch.randn(Kd, N, device="cuda")).to(
+            torch.float8_e4m3fn).view(torch.uint8)
+        if lay == "tn":
+            mine = lambda: F8.gemm_fp8(A, 0, B, 0, alpha=one)
+            ref = lambda: torch._scaled_mm(A.view(torch.float8_e4m3fn), B.view(torch.float8_e4m3fn).t(), one, one,
+                                           out_dtype=torch.bfloat16)
+        elif lay == "dgrad":
+            mine = lambda: F8.gemm_fp8(A, 1, B, 0, b_mn=True, alpha=one)
+            ref = None
+        else:
+            out = torch.empty(M, N, device="cuda")
+            mine = lambda: F8.gemm_fp8(A, 1, B, 0, out=out, a_mn=True, b_mn=True, alpha=one)
+            ref = None
+        flops = 2.0 * M * N * Kd
+        tm = timeit(mine, args.iters)
+        tr = timeit(ref, args.iters) if ref is not None else float("nan")
+        r = {"case": name, "M": M, "N": N, "K": Kd, "layout": lay, "mine_ms": round(tm, 4),
+             "cublas_ms": round(tr, 4), "mine_tflops": round(flops / tm / 1e9, 1),
+             "cublas_tflops": round(flops / tr / 1e9, 1) if tr == tr else None,
+             "mine_frac_of_2x_measured_bf16_peak": round(flops / tm / 1e9 / (2 * peak), 3)}
+        rows.append(r)
+        print(json.dumps(r), flush=True)
+        del A, B
     for name, M, N, Kd, lay in cases:
         A = torch.randn(M, Kd, device="cuda").bfloat16() if lay != "wgrad" else torch.randn(Kd, M, device="cuda").bfloat16()
         if lay == "tn":

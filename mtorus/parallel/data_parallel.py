@@ -57,9 +57,12 @@ class BucketPlan:
 class NcclBucketReducer:
     """Averages gradients across the DP group with NCCL, overlapped with backward."""
 
-    def __init__(self, flat, group=None, bucket_bytes: int = 25 * 1024 * 1024):
+    def __init__(self, flat, group=None, bucket_bytes: int = 25 * 1024 * 1024, reserve_sms: Optional[int] = None):
+        import os
+
         self.flat = flat
         self.group = group
+        self.reserve_sms = reserve_sms if reserve_sms is not None else int(os.environ.get("MTORUS_DP_RESERVE_SMS", "16"))
         self.world = dist.get_world_size(group)
         self.plan = BucketPlan(flat, bucket_bytes)
         self.on_cuda = flat.grad.is_cuda
@@ -84,6 +87,11 @@ class NcclBucketReducer:
 
     def _launch(self, b: int) -> None:
         s, e = self.plan.ranges[b]
+        if self.on_cuda and b == 0 and self.reserve_sms:
+            # NCCL kernels overlap the rest of backward: leave SMs free for them
+            from .._ext import cuda as _cuda
+
+            _cuda().gemm_set_reserved_sms(self.reserve_sms)
         if not self.on_cuda:
             self.reduce_range(s, e)
             self.launched[b] = True
@@ -104,4 +112,8 @@ class NcclBucketReducer:
             self.next_to_launch += 1
         if self.on_cuda:
             torch.cuda.current_stream().wait_stream(self.stream)
+            if self.reserve_sms:
+                from .._ext import cuda as _cuda
+
+                _cuda().gemm_set_reserved_sms(0)
         self._reset()

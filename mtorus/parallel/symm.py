@@ -84,8 +84,12 @@ def _chunk_len(n_elems: int, world: int) -> int:
 class SymmBucketReducer:
     """Reduce-scatter of the flat gradient buffer, bucket by bucket, over NVLink."""
 
-    def __init__(self, flat, group=None, bucket_bytes: int = 25 * 1024 * 1024, ctas: int = 24,
-                 ctx: Optional[SymmContext] = None):
+    def __init__(self, flat, group=None, bucket_bytes: int = 25 * 1024 * 1024, ctas: Optional[int] = None,
+                 ctx: Optional[SymmContext] = None, reserve_sms: Optional[int] = None):
+        import os
+
+        ctas = ctas if ctas is not None else int(os.environ.get("MTORUS_DP_CTAS", "16"))
+        self.reserve = reserve_sms if reserve_sms is not None else int(os.environ.get("MTORUS_DP_RESERVE_SMS", str(ctas)))
         if not getattr(flat, "symmetric", False):
             raise ValueError("SymmBucketReducer needs a FlatParams built with symmetric grad/w16 buffers")
         self.flat = flat
@@ -113,6 +117,7 @@ class SymmBucketReducer:
                 moff += (ln + 7) // 8 * 8
         self.shard_numel = moff
         self.ranges = torch.tensor(ranges, dtype=torch.int64, device=flat.device).reshape(-1, 3)
+        self._reserved = False
         self._reset()
 
     def _reset(self):
@@ -121,6 +126,7 @@ class SymmBucketReducer:
 
     def begin_step(self) -> None:
         self.epoch += 1
+        self._reserved = False
 
     def on_ready(self, params) -> None:
         for p in params:
@@ -133,6 +139,10 @@ class SymmBucketReducer:
             self.next_to_launch += 1
 
     def _launch(self, b: int) -> None:
+        if not self._reserved:
+            # from now on reduce kernels overlap backward: keep their SMs out of the GEMM grids
+            _cuda().gemm_set_reserved_sms(self.reserve)
+            self._reserved = True
         s, e = self.plan.ranges[b]
         ev = torch.cuda.Event()
         ev.record()
@@ -149,6 +159,8 @@ class SymmBucketReducer:
             _cuda().symm_scalars_ar(self.ctx.scalars.ptrs, self.ctx.flags.ptrs, self.me, self.slot_norm,
                                     self.epoch, self.state)
         torch.cuda.current_stream().wait_stream(self.stream)
+        _cuda().gemm_set_reserved_sms(0)
+        self._reserved = False
         self._reset()
 
     # the optimizer's state block is shared (norm partials land in it)
