@@ -123,6 +123,22 @@ def main() -> int:
     ms = t0.elapsed_time(t1)
     last_loss = float(loss)
 
+    # exposed communication: the same steps with no data-parallel traffic at all
+    comp_ms = None
+    if world > 1:
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(2):
+            trainer.step_device(dev_ids[i % nb], dev_tgt[i % nb], reduce=False)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for i in range(args.steps):
+            trainer.step_device(dev_ids[i % nb], dev_tgt[i % nb], reduce=False)
+        c1.record()
+        c1.synchronize()
+        comp_ms = c0.elapsed_time(c1)
+        barrier()
+
     e2e_ms = None
     if not args.no_e2e:
         barrier()
@@ -137,9 +153,9 @@ def main() -> int:
         barrier()
 
     if world > 1:
-        t = torch.tensor([ms, e2e_ms or 0.0], device=dev)
+        t = torch.tensor([ms, e2e_ms or 0.0, comp_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), (float(t[1]) if e2e_ms is not None else None)
+        ms, e2e_ms, comp_ms = float(t[0]), (float(t[1]) if e2e_ms is not None else None), float(t[2])
 
     tokens_per_step = B * S * world
     ms_step = ms / args.steps
@@ -171,6 +187,13 @@ def main() -> int:
             "l2": "per-step working set (activations, 1.4B-param optimizer state) >> 126 MB L2; no flush",
             "params": cfg.num_params(),
             "model_tflops_per_gpu": round(cfg.train_flops_per_token(S) * B * S / (ms_step / 1000.0) / 1e12, 1),
+        },
+        "exposed_comm": {
+            "ms_per_step": round(max(0.0, ms_step - comp_ms / args.steps), 3) if comp_ms is not None else 0.0,
+            "fraction_of_step": (round(max(0.0, ms_step - comp_ms / args.steps) / ms_step, 4)
+                                 if comp_ms is not None else 0.0),
+            "compute_only_ms_per_step": round(comp_ms / args.steps, 3) if comp_ms is not None else round(ms_step, 3),
+            "how": "device-timed step minus the same step with no data-parallel communication (max over ranks)",
         },
         "clocks": clocks,
         "gpu_launches": int(lc1 - lc0),

@@ -24,7 +24,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import List, Optional
+from typing import List, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -205,16 +205,26 @@ class TransformerBlock(nn.Module):
 class GptModel(nn.Module):
     """Reference: GptModel (examples/gpt-1b/src/model.rs:56-129)."""
 
-    def __init__(self, config: GptConfig, init: str = "reference"):
+    def __init__(self, config: GptConfig, init: str = "reference", layers: Optional[Tuple[int, int]] = None,
+                 embed: bool = True, head: bool = True):
+        """``layers=(lo, hi)`` / ``embed`` / ``head`` build one pipeline stage: blocks
+        lo..hi-1 of the full model, with the embeddings only on the first stage and
+        ln_f + lm_head only on the last (the reference splits its layer list the same
+        way, crates/mt-burn/src/module_ext.rs:40-79)."""
         super().__init__()
         c = config
         self.config = c
-        self.token_embedding = Embedding(c.vocab_size, c.d_model)
-        self.position_embedding = Embedding(c.max_seq_len, c.d_model)
+        lo, hi = layers if layers is not None else (0, c.num_layers)
+        self.layer_offset = lo
+        self.has_embed, self.has_head = embed, head
+        if embed:
+            self.token_embedding = Embedding(c.vocab_size, c.d_model)
+            self.position_embedding = Embedding(c.max_seq_len, c.d_model)
         self.blocks = nn.ModuleList(
-            [TransformerBlock(c.d_model, c.num_heads, c.d_ff, c.dropout) for _ in range(c.num_layers)])
-        self.ln_f = LayerNorm(c.d_model)
-        self.lm_head = Linear(c.d_model, c.vocab_size)
+            [TransformerBlock(c.d_model, c.num_heads, c.d_ff, c.dropout) for _ in range(lo, hi)])
+        if head:
+            self.ln_f = LayerNorm(c.d_model)
+            self.lm_head = Linear(c.d_model, c.vocab_size)
         self.dropout = nn.Dropout(c.dropout)
         self.d_model = c.d_model
         self.max_seq_len = c.max_seq_len
@@ -238,19 +248,30 @@ class GptModel(nn.Module):
         return len(self.blocks)
 
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
-        B, S = input_ids.shape
-        dev = input_ids.device
-        hidden = self.token_embedding(input_ids) + self.position_embedding(create_position_ids(B, S, dev))
-        hidden = self.dropout(hidden)
+        return self.forward_stage(input_ids)
+
+    def forward_stage(self, x: torch.Tensor) -> torch.Tensor:
+        """Reference path of a (possibly partial) model: token ids [B, S] on the first
+        stage, else the previous stage's [B, S, d] hidden; returns the hidden, or the
+        logits when this part holds the head."""
+        if self.has_embed:
+            B, S = x.shape
+            dev = x.device
+            hidden = self.token_embedding(x) + self.position_embedding(create_position_ids(B, S, dev))
+            hidden = self.dropout(hidden)
+        else:
+            hidden, S, dev = x, x.shape[1], x.device
         mask = create_causal_mask(S, dev).reshape(1, 1, S, S)
         for blk in self.blocks:
             hidden = blk(hidden, mask)
-        return self.lm_head(self.ln_f(hidden))
+        if self.has_head:
+            return self.lm_head(self.ln_f(hidden))
+        return hidden
 
     # ---------------------------------------------------------------- fused path
     def flat_groups(self) -> List[List[nn.Parameter]]:
         """Parameter layout for the flat buffers: q/k/v weights (and biases) back to back."""
-        groups = [[self.token_embedding.weight], [self.position_embedding.weight]]
+        groups = [[self.token_embedding.weight], [self.position_embedding.weight]] if self.has_embed else []
         for blk in self.blocks:
             a = blk.attention
             groups += [[blk.norm1.gamma, blk.norm1.beta],
@@ -260,7 +281,8 @@ class GptModel(nn.Module):
                        [blk.norm2.gamma, blk.norm2.beta],
                        [blk.ff.linear1.weight], [blk.ff.linear1.bias],
                        [blk.ff.linear2.weight], [blk.ff.linear2.bias]]
-        groups += [[self.ln_f.gamma, self.ln_f.beta], [self.lm_head.weight], [self.lm_head.bias]]
+        if self.has_head:
+            groups += [[self.ln_f.gamma, self.ln_f.beta], [self.lm_head.weight], [self.lm_head.bias]]
         return groups
 
     def flatten(self, device, grad_dtype=torch.float32, symmetric: bool = False, group=None):
@@ -278,22 +300,50 @@ class GptModel(nn.Module):
         return self.flat
 
     def fused_hidden(self, input_ids: torch.Tensor) -> torch.Tensor:
-        from ..ops.fused import EmbeddingFn, LayerNormFn, grad_anchor
+        from ..ops.fused import LayerNormFn
 
         assert self.flat is not None, "call flatten(device) before using the fused path"
         B, S = input_ids.shape
-        x = EmbeddingFn.apply(input_ids, grad_anchor(input_ids.device),
-                              (self.token_embedding.weight, self.position_embedding.weight), S)
+        x = self.fused_blocks(self.fused_embed(input_ids), B, S)
+        return LayerNormFn.apply(x, (self.ln_f.gamma, self.ln_f.beta), self.ln_f.eps)
+
+    def fused_embed(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """[B, S] token ids -> [B*S, d] bf16 hidden (token + learned position embedding)."""
+        from ..ops.fused import EmbeddingFn, grad_anchor
+
+        assert self.flat is not None, "call flatten(device) before using the fused path"
+        S = input_ids.shape[1]
+        return EmbeddingFn.apply(input_ids, grad_anchor(input_ids.device),
+                                 (self.token_embedding.weight, self.position_embedding.weight), S)
+
+    def fused_blocks(self, x: torch.Tensor, B: int, S: int) -> torch.Tensor:
+        """[B*S, d] -> [B*S, d] through this model's (or stage's) transformer blocks."""
         st = getattr(self, "fp8_state", None)
         for i, blk in enumerate(self.blocks):
-            x = blk.fused_forward(x, B, S, None if st is None else (st, f"L{i}"))
-        return LayerNormFn.apply(x, (self.ln_f.gamma, self.ln_f.beta), self.ln_f.eps)
+            x = blk.fused_forward(x, B, S, None if st is None else (st, f"L{self.layer_offset + i}"))
+        return x
+
+    def fused_stage(self, x: torch.Tensor, B: int, S: int) -> torch.Tensor:
+        """Pipeline-stage forward: token ids (first stage) or the previous stage's
+        [B*S, d] hidden in, this stage's [B*S, d] hidden out (before ln_f)."""
+        if self.has_embed:
+            x = self.fused_embed(x)
+        return self.fused_blocks(x, B, S)
+
+    def fused_head_loss(self, x: torch.Tensor, targets: torch.Tensor,
+                        grad_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Last-stage loss: ln_f -> lm_head -> mean CE, gradients into main_grad."""
+        from ..ops.fused import LayerNormFn, LMHeadLossFn
+
+        h = LayerNormFn.apply(x, (self.ln_f.gamma, self.ln_f.beta), self.ln_f.eps)
+        return LMHeadLossFn.apply(h, targets, (self.lm_head.weight, self.lm_head.bias), grad_scale)
 
     # ---------------------------------------------------------------- FP8
     def fp8_weights(self):
         """(name, weight-like) pairs whose GEMMs run in FP8 (the LM head stays bf16)."""
         out = []
-        for i, blk in enumerate(self.blocks):
+        for j, blk in enumerate(self.blocks):
+            i = self.layer_offset + j
             out += [(f"L{i}.qkv_w", blk._qkv_w), (f"L{i}.out_w", blk.attention.out_proj.weight),
                     (f"L{i}.ffn1_w", blk.ff.linear1.weight), (f"L{i}.ffn2_w", blk.ff.linear2.weight)]
         return out

@@ -81,6 +81,7 @@ class Fp8State:
         self.fmax = torch.zeros(capacity, device=d)
         self.cursor = 0
         self.first_step = True
+        self._measured = set()  # slots whose first-step scale is already set
 
     def slot(self, name: str, fmt: int) -> int:
         s = self.names.get(name)
@@ -97,10 +98,7 @@ class Fp8State:
         """-> (codes, inverse-scale view).  The inverse scale is the one this step used."""
         s = self.slot(name, fmt)
         sl = slice(s, s + 1)
-        if self.first_step:
-            _cuda().fp8_amax(x.contiguous(), self.amax[sl])
-            _cuda().fp8_scaling_update(self.hist[sl], self.amax[sl], self.scale[sl], self.inv[sl],
-                                       self.fmax[sl], self.cursor, True)
+        self._first_step_scale(x, s)
         q = quantize(x, fmt, self.scale[sl], self.amax[sl])
         # the inverse scale stays valid until end_step(), i.e. through this step's backward
         return q, self.inv[sl]
@@ -108,12 +106,21 @@ class Fp8State:
     def quantize_into(self, x: torch.Tensor, name: str, fmt: int, out: torch.Tensor):
         s = self.slot(name, fmt)
         sl = slice(s, s + 1)
-        if self.first_step:
-            _cuda().fp8_amax(x.contiguous(), self.amax[sl])
-            _cuda().fp8_scaling_update(self.hist[sl], self.amax[sl], self.scale[sl], self.inv[sl],
-                                       self.fmax[sl], self.cursor, True)
+        self._first_step_scale(x, s)
         quantize(x, fmt, self.scale[sl], self.amax[sl], out=out)
         return out, self.inv[sl]
+
+    def _first_step_scale(self, x: torch.Tensor, s: int) -> None:
+        """First step (empty history): scale from the tensor's own amax, measured on
+        its first use only -- later micro-batches of the step keep that scale, since
+        earlier micro-batches' saved codes are dequantised with it in backward."""
+        if not self.first_step or s in self._measured:
+            return
+        sl = slice(s, s + 1)
+        _cuda().fp8_amax(x.contiguous(), self.amax[sl])
+        _cuda().fp8_scaling_update(self.hist[sl], self.amax[sl], self.scale[sl], self.inv[sl],
+                                   self.fmax[sl], self.cursor, True)
+        self._measured.add(s)
 
     def end_step(self) -> None:
         """Roll all histories (delayed scaling): the next step's scales come from them."""

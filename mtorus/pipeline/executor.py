@@ -15,6 +15,8 @@ input of each in-flight micro-batch and recomputes the forward in backward.
 """
 from __future__ import annotations
 
+import os
+import sys
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional, Sequence
 
@@ -59,12 +61,34 @@ class DistributedPipelineExecutor:
     loss_fn     last stage only: loss_fn(output, target) -> scalar; the executor
                 divides it by the number of micro-batches
     act_shape   shape of the tensor exchanged between stages (per micro-batch)
+    stage_fn    optional forward callable used instead of ``module(x)``
+    pre_backward  called as pre_backward(microbatch, k) before the k-th backward of
+                the step (k = 0 .. M-1), e.g. to switch gradient accumulation on
+                after the first micro-batch or to arm the data-parallel reducer on
+                the last one
+    grad_group  process group for the backward (gradient) transfers; default
+                ``group``.  With NCCL, activations and gradients between the same
+                two ranks must travel on different communicators: one NCCL stream
+                per rank pair would serialise a send of activations behind a
+                receive of gradients and the two neighbours would wait on each
+                other
+    sync_losses True: ``run`` returns the per-micro-batch losses as floats (one
+                host sync each); False: it returns the mean loss as a device
+                scalar (last stage) without synchronising
+    timed       record CUDA events around every forward / backward; after ``run``
+                ``busy_ms`` / ``span_ms`` / ``bubble_fraction`` hold this rank's
+                compute time, first-to-last op span and idle share of that span
+
+    Receives for the next compute op are posted before the current one runs, so
+    transfers overlap compute; sends are asynchronous.
     """
 
     def __init__(self, module: torch.nn.Module, stage_ranks: Sequence[int], schedule_type=ScheduleType.OneF1B,
                  num_microbatches: int = 1, checkpoint: CheckpointStrategy = CheckpointStrategy.None_,
                  loss_fn: Optional[Callable] = None, act_shape: Sequence[int] = (), act_dtype=torch.float32,
-                 device=None, group=None, on_backward_done: Optional[Callable[[int], None]] = None):
+                 device=None, group=None, on_backward_done: Optional[Callable[[int], None]] = None,
+                 stage_fn: Optional[Callable] = None, pre_backward: Optional[Callable[[int, int], None]] = None,
+                 grad_group=None, sync_losses: bool = True, timed: bool = False):
         self.module = module
         self.stage_ranks = list(stage_ranks)
         self.S = len(self.stage_ranks)
@@ -78,40 +102,105 @@ class DistributedPipelineExecutor:
         self.act_dtype = act_dtype
         self.device = torch.device(device) if device is not None else torch.device("cpu")
         self.group = group
+        self.grad_group = grad_group if grad_group is not None else group
         self.on_backward_done = on_backward_done
+        self.stage_fn = stage_fn
+        self.pre_backward = pre_backward
+        self.sync_losses = sync_losses
+        self.timed = timed and self.device.type == "cuda"
         self.program = rank_program(schedule_type, self.stage, self.S, self.M)
         self.is_first = self.stage == 0
         self.is_last = self.stage == self.S - 1
+        self.busy_ms = self.span_ms = self.bubble_fraction = None
 
     def _peer(self, stage: int) -> int:
         return self.stage_ranks[stage]
 
+    def connect(self) -> None:
+        """Sets up the NCCL point-to-point connections to both neighbours, on both
+        groups, with one message of the real size in each direction.
+
+        NCCL connects a peer lazily, inside the first send / receive to it, and that
+        setup is a blocking host-side handshake with the peer.  If it first happened
+        in the middle of the schedule (a receive posted ahead of a forward), the
+        host would wait for a neighbour whose GPU may itself be waiting on a
+        transfer this host has not launched yet.  Done once, here, before any
+        transfer kernel runs, nothing later blocks the host.  The ops are the same
+        unbatched send / receive calls as the schedule's (a batched call may get a
+        communicator of its own), ordered as a chain that resolves from its end:
+        every stage sends downstream first and then receives from upstream."""
+        self._connected = True
+        if self.S == 1:
+            return
+        buf_out = torch.zeros(self.act_shape, dtype=self.act_dtype, device=self.device)
+        buf_in = torch.empty_like(buf_out)
+        works = []
+        for grp, nxt, prv in ((self.group, self.stage + 1, self.stage - 1),
+                              (self.grad_group, self.stage - 1, self.stage + 1)):
+            if 0 <= nxt < self.S:
+                works.append(dist.isend(buf_out, self._peer(nxt), group=grp))
+            if 0 <= prv < self.S:
+                works.append(dist.irecv(buf_in, self._peer(prv), group=grp))
+        for w in works:
+            w.wait()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
     def _stage_forward(self, x):
-        return self.module(x)
+        return self.stage_fn(x) if self.stage_fn is not None else self.module(x)
 
     def run(self, inputs: Optional[Sequence[torch.Tensor]] = None,
-            targets: Optional[Sequence[torch.Tensor]] = None) -> List[float]:
-        """Runs one step of the schedule; returns the per-micro-batch losses
-        (last stage) and leaves parameter gradients accumulated in the module."""
+            targets: Optional[Sequence[torch.Tensor]] = None):
+        """Runs one step of the schedule and leaves parameter gradients accumulated
+        in the module.  Returns the per-micro-batch losses (``sync_losses``) or the
+        mean loss as a device scalar (last stage; ``None`` elsewhere)."""
+        if not getattr(self, "_connected", False) and self.device.type == "cuda":
+            self.connect()
         K = PipeOp.Kind
+        prog = self.program
         stash_in: Dict[int, torch.Tensor] = {}
         stash_out: Dict[int, torch.Tensor] = {}
         recv_act: Dict[int, torch.Tensor] = {}
         recv_grad: Dict[int, torch.Tensor] = {}
+        posted: Dict[int, tuple] = {}
         pending_sends = []
-        losses: List[float] = []
+        losses: List = []
         peak = 0
-        for op in self.program:
+        n_bwd = 0
+        events = []
+        scan = 0
+
+        def post_until(limit: int) -> None:
+            nonlocal scan
+            while scan < min(limit, len(prog)):
+                op = prog[scan]
+                if op.kind in (K.RecvAct, K.RecvGrad):
+                    buf = torch.empty(self.act_shape, dtype=self.act_dtype, device=self.device)
+                    grp = self.group if op.kind == K.RecvAct else self.grad_group
+                    posted[scan] = (buf, dist.irecv(buf, self._peer(op.peer), group=grp))
+                scan += 1
+
+        compute_idx = [i for i, op in enumerate(prog) if op.kind in (K.Forward, K.Backward)]
+        next_compute = {a: b for a, b in zip(compute_idx, compute_idx[1:] + [len(prog)])}
+
+        trace = os.environ.get("MTORUS_PP_TRACE") == "1"
+        for i, op in enumerate(prog):
             m = op.microbatch
-            if op.kind == K.RecvAct:
-                buf = torch.empty(self.act_shape, dtype=self.act_dtype, device=self.device)
-                dist.recv(buf, self._peer(op.peer), group=self.group)
-                recv_act[m] = buf
-            elif op.kind == K.RecvGrad:
-                buf = torch.empty(self.act_shape, dtype=self.act_dtype, device=self.device)
-                dist.recv(buf, self._peer(op.peer), group=self.group)
-                recv_grad[m] = buf
-            elif op.kind == K.Forward:
+            if trace:
+                print(f"[pp rank {self.rank}] op {i} {op.kind} mb {m}", file=sys.stderr, flush=True)
+            if op.kind in (K.RecvAct, K.RecvGrad):
+                post_until(i + 1)
+                buf, work = posted.pop(i)
+                work.wait()
+                (recv_act if op.kind == K.RecvAct else recv_grad)[m] = buf
+                continue
+            if op.kind in (K.Forward, K.Backward):
+                # receives needed by the next compute op go out before this one runs
+                post_until(next_compute[i])
+                if self.timed:
+                    ev0 = torch.cuda.Event(enable_timing=True)
+                    ev0.record()
+            if op.kind == K.Forward:
                 x = inputs[m] if self.is_first else recv_act.pop(m)
                 if not self.is_first:
                     x.requires_grad_(True)
@@ -134,6 +223,9 @@ class DistributedPipelineExecutor:
                 y = stash_out[m]
                 pending_sends.append(dist.isend(y.detach().contiguous(), self._peer(op.peer), group=self.group))
             elif op.kind == K.Backward:
+                if self.pre_backward is not None:
+                    self.pre_backward(m, n_bwd)
+                n_bwd += 1
                 x = stash_in.pop(m)
                 y = stash_out.pop(m)
                 if self.checkpoint is CheckpointStrategy.Full:
@@ -143,23 +235,37 @@ class DistributedPipelineExecutor:
                         if self.is_last:
                             y = self.loss_fn(y, targets[m]) / self.M
                 if self.is_last:
-                    losses.append(float(y.detach()) * self.M)
+                    losses.append(y.detach())
                     torch.autograd.backward(y)
                 else:
                     torch.autograd.backward(y, recv_grad.pop(m))
+                del y
                 if self.on_backward_done is not None:
                     self.on_backward_done(m)
                 stash_in[m] = x  # keep for SendGrad
             elif op.kind == K.SendGrad:
                 x = stash_in.pop(m)
-                pending_sends.append(dist.isend(x.grad.contiguous(), self._peer(op.peer), group=self.group))
+                pending_sends.append(dist.isend(x.grad.contiguous(), self._peer(op.peer), group=self.grad_group))
+            if op.kind in (K.Forward, K.Backward) and self.timed:
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev1.record()
+                events.append((ev0, ev1))
             if len(pending_sends) > 8:
                 pending_sends.pop(0).wait()
         for w in pending_sends:
             w.wait()
         stash_in.clear()
         self.peak_inflight = peak
-        return losses
+        if self.timed and events:
+            events[-1][1].synchronize()
+            self.busy_ms = sum(a.elapsed_time(b) for a, b in events)
+            self.span_ms = events[0][0].elapsed_time(events[-1][1])
+            self.bubble_fraction = max(0.0, 1.0 - self.busy_ms / self.span_ms) if self.span_ms > 0 else 0.0
+        if self.sync_losses:
+            return [float(v) * self.M for v in losses]
+        if not losses:
+            return None
+        return torch.stack(losses).sum()
 
 
 __all__ = ["PipelineConfig", "PipelineExecutor", "DistributedPipelineExecutor", "ScheduleType"]

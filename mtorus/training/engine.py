@@ -74,24 +74,36 @@ class GptTrainer:
             return self.lr * (self.global_step + 1) / self.warmup_steps
         return self.lr
 
-    def step_device(self, ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
-        """One full training step on device tensors; returns the device loss (no sync)."""
+    def step_device(self, ids: torch.Tensor, targets: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        """One full training step on device tensors; returns the device loss (no sync).
+
+        ``reduce=False`` runs the same step with no data-parallel communication at
+        all (each rank updates its own replica with a local Adam): the compute-only
+        reference against which the exposed communication time of a real step is
+        measured.  Every rank must pass the same value."""
         FusedGradState.accumulate = False
         if self.fp8:
             self.model.refresh_fp8_weights()
-        FusedGradState.grad_ready_hook = self.reducer.on_ready if self.reducer is not None else None
-        if hasattr(self.reducer, "begin_step"):
-            self.reducer.begin_step()
-        loss = self.model.fused_loss(ids, targets, grad_scale=self.opt.loss_scale_tensor)
+        reducer = self.reducer if reduce else None
+        FusedGradState.grad_ready_hook = reducer.on_ready if reducer is not None else None
+        if hasattr(reducer, "begin_step"):
+            reducer.begin_step()
+        opt = self.opt if reduce or self.reducer is None else self._local_optimizer()
+        loss = self.model.fused_loss(ids, targets, grad_scale=opt.loss_scale_tensor)
         loss.backward()
-        if self.reducer is not None:
-            self.reducer.finish()
+        if reducer is not None:
+            reducer.finish()
         FusedGradState.grad_ready_hook = None
-        self.opt.step(self.current_lr())
+        opt.step(self.current_lr())
         if self.fp8:
             self.model.fp8_state.end_step()
         self.global_step += 1
         return loss.detach()
+
+    def _local_optimizer(self) -> FusedAdam:
+        if getattr(self, "_local_opt", None) is None:
+            self._local_opt = FusedAdam(self.flat, lr=self.lr)
+        return self._local_opt
 
     def train_step(self, input_ids: torch.Tensor, targets: torch.Tensor) -> float:
         """Host batch in (ideally pinned), host loss out."""

@@ -1,0 +1,265 @@
+"""PipelineTrainer: GPT training with data x pipeline parallelism on the fused path.
+
+The world of ``dp * pp`` ranks (one per GPU) is laid out as ``dp`` pipeline
+replicas of ``pp`` consecutive ranks: rank = replica * pp + stage.  Each rank
+builds only its stage of the model (``GptModel(layers=..., embed=..., head=...)``,
+the layer list split with ``split_evenly`` as in the reference's
+crates/mt-burn/src/module_ext.rs:40-79), flattens it into its own fp32 master /
+bf16 / fp32-grad buffers and runs:
+
+1. the per-rank GPipe or 1F1B program from the schedule builder
+   (``DistributedPipelineExecutor``; reference crates/mt-pipeline/src/schedule/
+   gpipe.rs, onef1b.rs) with NCCL point-to-point activations / gradients,
+   activations on one process group and gradients on another so that the two
+   directions between neighbours never share an NCCL stream;
+2. optional full activation checkpointing per stage (stage input kept, forward
+   recomputed in backward; reference crates/mt-pipeline/src/checkpoint.rs);
+3. gradient accumulation over the micro-batches straight into ``main_grad``
+   (the first backward overwrites, the rest add, in the wgrad GEMM epilogues);
+4. during the last micro-batch's backward, the data-parallel bucket all-reduce
+   over the ranks that hold the same stage, overlapped with that backward;
+5. the fused device optimizer, with the gradient-norm / overflow statistics
+   summed over the pipeline so that every stage takes the same skip / clip /
+   loss-scale decision (reference crates/mt-training/src/step.rs:114-180).
+
+Stage placement: on one NVSwitch node every GPU pair is one NVLink hop, so
+consecutive ranks per pipeline is already the topology-aware placement
+(``topology_aware_placement`` maps stages to torus nodes across nodes).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+from ..models.gpt import GptConfig, GptModel
+from ..ops.fused import FusedGradState
+from ..pipeline.checkpoint import CheckpointStrategy
+from ..pipeline.executor import DistributedPipelineExecutor
+from ..pipeline.schedule import ScheduleType, ideal_bubble_fraction
+from ..torch_ext.module_ext import split_evenly
+from .fused_optim import ST_NONFINITE, ST_SUMSQ, DeviceLossScaleConfig, FusedAdam
+
+
+@dataclass
+class PipelineLayout:
+    """Rank layout of a dp x pp job: ``stage_ranks[r]`` are the ranks of replica r
+    (stage order); ``dp_ranks[s]`` the ranks that hold stage s."""
+
+    dp: int
+    pp: int
+    stage_ranks: List[List[int]] = field(default_factory=list)
+    dp_ranks: List[List[int]] = field(default_factory=list)
+
+    def __post_init__(self):
+        self.stage_ranks = [[r * self.pp + s for s in range(self.pp)] for r in range(self.dp)]
+        self.dp_ranks = [[r * self.pp + s for r in range(self.dp)] for s in range(self.pp)]
+
+    def coords(self, rank: int):
+        """-> (replica, stage)."""
+        return divmod(rank, self.pp)
+
+
+class PipelineTrainer:
+    def __init__(self, config: GptConfig, pp: int, dp: int = 1, schedule=ScheduleType.OneF1B,
+                 num_microbatches: int = 8, micro_batch: int = 1, seq_len: Optional[int] = None,
+                 checkpoint: CheckpointStrategy = CheckpointStrategy.Full, fp8: bool = True,
+                 fp8_history: int = 16, lr: float = 3e-4, device=None, seed: int = 0,
+                 bucket_mb: float = 25.0, loss_scale: Optional[DeviceLossScaleConfig] = None,
+                 max_grad_norm: float = 0.0, timed: bool = False):
+        world = dist.get_world_size()
+        if world != dp * pp:
+            raise ValueError(f"world size {world} != dp {dp} x pp {pp}")
+        if pp > config.num_layers:
+            raise ValueError(f"pp {pp} exceeds the layer count {config.num_layers}")
+        self.config = config
+        self.dp, self.pp = dp, pp
+        self.M = num_microbatches
+        self.b = micro_batch
+        self.S = seq_len or config.max_seq_len
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.layout = PipelineLayout(dp, pp)
+        self.rank = dist.get_rank()
+        self.replica, self.stage = self.layout.coords(self.rank)
+        # every rank creates every group, in the same order
+        self.pipe_group = self.grad_group = self.dp_group = None
+        for ranks in self.layout.stage_ranks:
+            g_act = dist.new_group(ranks)
+            g_grad = dist.new_group(ranks)
+            if self.rank in ranks:
+                self.pipe_group, self.grad_group = g_act, g_grad
+        for ranks in self.layout.dp_ranks:
+            g = dist.new_group(ranks)
+            if self.rank in ranks:
+                self.dp_group = g
+        lo, hi = split_evenly(config.num_layers, pp)[self.stage]
+        self.layers = (lo, hi)
+        self.is_first, self.is_last = self.stage == 0, self.stage == pp - 1
+        torch.manual_seed(seed + self.stage)
+        with torch.device(self.device):
+            self.model = GptModel(config, init="reference", layers=(lo, hi), embed=self.is_first,
+                                  head=self.is_last)
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed * 1000 + self.stage)
+        self.model.init_normal_(0.02, generator=g)
+        self.flat = self.model.flatten(self.device)
+        self.fp8 = fp8
+        if fp8:
+            self.model.enable_fp8(fp8_history)
+        self.opt = FusedAdam(self.flat, lr=lr, max_grad_norm=max_grad_norm,
+                             loss_scale=loss_scale or DeviceLossScaleConfig())
+        self.reducer = None
+        if dp > 1:
+            from ..parallel.data_parallel import NcclBucketReducer
+
+            self.reducer = NcclBucketReducer(self.flat, self.dp_group, int(bucket_mb * 1024 * 1024))
+        b, S = self.b, self.S
+
+        def stage_fn(x):
+            return self.model.fused_stage(x, b, S)
+
+        def loss_fn(h, tgt):
+            return self.model.fused_head_loss(h, tgt, grad_scale=self.opt.loss_scale_tensor)
+
+        self.executor = DistributedPipelineExecutor(
+            self.model, self.layout.stage_ranks[self.replica], schedule, num_microbatches, checkpoint,
+            loss_fn=loss_fn, act_shape=(b * S, config.d_model), act_dtype=torch.bfloat16, device=self.device,
+            group=self.pipe_group, grad_group=self.grad_group, stage_fn=stage_fn,
+            pre_backward=self._pre_backward, sync_losses=False, timed=timed)
+        self.schedule = schedule
+        self.global_step = 0
+        self._loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def global_name(self, local: str) -> str:
+        """Stage parameter name -> the full model's name (``blocks.{j}`` -> ``blocks.{lo+j}``)."""
+        if local.startswith("blocks."):
+            j, rest = local[len("blocks."):].split(".", 1)
+            return f"blocks.{int(j) + self.layers[0]}.{rest}"
+        return local
+
+    def state_dict_global(self) -> dict:
+        """This stage's parameters under the full model's names (fp32 master copies)."""
+        return {self.global_name(k): v.detach() for k, v in self.model.state_dict().items()}
+
+    @torch.no_grad()
+    def load_global_state_dict(self, sd: dict) -> None:
+        """Load this stage's slice of a full-model state dict (names as in ``GptModel``)."""
+        own = self.model.state_dict()
+        for k, v in own.items():
+            v.copy_(sd[self.global_name(k)].to(v.device, v.dtype))
+        self.flat.sync_w16()
+
+    def ideal_bubble_fraction(self) -> float:
+        """(S-1)/(M+S-1) for both schedules (the reference's formula)."""
+        return ideal_bubble_fraction(self.pp, self.M)
+
+    def _pre_backward(self, m: int, k: int) -> None:
+        FusedGradState.accumulate = k > 0
+        last = k == self.M - 1
+        FusedGradState.grad_ready_hook = self.reducer.on_ready if (last and self.reducer is not None) else None
+
+    def step_device(self, ids: Optional[Sequence[torch.Tensor]], targets: Optional[Sequence[torch.Tensor]]):
+        """One optimizer step over M micro-batches (device tensors: ``ids`` on the first
+        stage, ``targets`` on the last, each a list of M [b, S] tensors).  Returns the
+        mean loss as a device scalar on the last stage, None elsewhere; no host sync."""
+        loss = self.forward_backward(ids, targets)
+        self.optimizer_step()
+        return loss
+
+    def warm_kernels(self) -> None:
+        """Runs this stage's forward, backward and optimizer kernels once on dummy data,
+        with no communication, and restores every piece of state they touch.
+
+        Why: under CUDA lazy module loading (torch's default) the first launch of a
+        kernel -- and cuDNN's first use of an attention plan -- may need a context
+        synchronisation, which waits for the NCCL receive kernels that this rank
+        already has spinning for a neighbour.  If that neighbour is in the same
+        situation, both ranks wait forever.  After this call every kernel of the
+        step is resident, so the pipelined step never loads code while an NCCL
+        kernel is in flight."""
+        self._warmed = True
+        b, S, d = self.b, self.S, self.config.d_model
+        st = self.model.fp8_state if self.fp8 else None
+        if st is not None:
+            saved = {k: getattr(st, k).clone() for k in ("hist", "amax", "scale", "inv")}
+            saved_meta = (st.first_step, set(st._measured), st.cursor)
+            self.model.refresh_fp8_weights()
+        opt_state = self.opt.state.clone()
+        FusedGradState.accumulate = False
+        FusedGradState.grad_ready_hook = None
+        dev = self.device
+        if self.is_first:
+            x = torch.zeros((b, S), dtype=torch.long, device=dev)
+        else:
+            x = torch.zeros((b * S, d), dtype=torch.bfloat16, device=dev, requires_grad=True)
+        with torch.no_grad():  # the checkpointed forward
+            self.model.fused_stage(x, b, S)
+        with torch.enable_grad():
+            y = self.model.fused_stage(x, b, S)
+            if self.is_last:
+                tgt = torch.zeros((b, S), dtype=torch.long, device=dev)
+                torch.autograd.backward(self.model.fused_head_loss(y, tgt, grad_scale=self.opt.loss_scale_tensor))
+            else:
+                torch.autograd.backward(y, torch.zeros_like(y))
+        del x, y
+        # zero gradients leave master weights and Adam moments unchanged
+        self.flat.grad.zero_()
+        self.opt.step()
+        if st is not None:
+            st.end_step()
+        with torch.no_grad():
+            self.opt.state.copy_(opt_state)
+            if st is not None:
+                for k, v in saved.items():
+                    getattr(st, k).copy_(v)
+                st.first_step, st._measured, st.cursor = saved_meta[0], saved_meta[1], saved_meta[2]
+        torch.cuda.synchronize(dev)
+
+    def forward_backward(self, ids, targets):
+        """The schedule's forwards / backwards and the data-parallel reduction: leaves
+        the step's averaged gradients in ``flat.grad``; returns the device loss (last
+        stage) or None."""
+        if not getattr(self, "_warmed", False):
+            self.warm_kernels()
+        if self.fp8:
+            self.model.refresh_fp8_weights()
+        loss = self.executor.run(ids if self.is_first else None, targets if self.is_last else None)
+        FusedGradState.grad_ready_hook = None
+        FusedGradState.accumulate = False
+        if self.reducer is not None:
+            self.reducer.finish()
+        return loss
+
+    def optimizer_step(self) -> None:
+        """Pipeline-wide norm / overflow, then the fused Adam update and the FP8 scale roll."""
+        self.opt.accumulate_norm()
+        if self.pp > 1:
+            # sum of squares and the non-finite count over the whole model
+            dist.all_reduce(self.opt.state[ST_SUMSQ:ST_NONFINITE + 1], group=self.pipe_group)
+        self.opt.finalize()
+        self.opt.update()
+        if self.fp8:
+            self.model.fp8_state.end_step()
+        self.global_step += 1
+
+    def train_step(self, ids_host: Optional[torch.Tensor], targets_host: Optional[torch.Tensor]) -> Optional[float]:
+        """Host batch [M, b, S] in (pinned; ids needed on the first stage, targets on the
+        last), host mean loss out on the last stage (None elsewhere)."""
+        ids = tgt = None
+        if self.is_first:
+            d = ids_host.to(self.device, non_blocking=True)
+            ids = list(d.unbind(0))
+        if self.is_last:
+            d = targets_host.to(self.device, non_blocking=True)
+            tgt = list(d.unbind(0))
+        loss = self.step_device(ids, tgt)
+        if loss is None:
+            return None
+        self._loss_host.copy_(loss, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return float(self._loss_host)
+
+
+__all__ = ["PipelineLayout", "PipelineTrainer"]

@@ -95,3 +95,62 @@ def test_fused_dp_matches_nccl_baseline():
         assert torch.allclose(a[r][1], b[r][1], atol=2e-2, rtol=2e-2)
     # every rank holds the same weights after the all-gather
     assert torch.equal(b[0][1], b[1][1])
+
+
+def _pp_body(rank, world, sched_name, ckpt_name):
+    import torch
+
+    from mtorus.models.gpt import GptConfig, GptModel
+    from mtorus.pipeline import CheckpointStrategy, ScheduleType
+    from mtorus.training.pipeline_engine import PipelineTrainer
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    cfg = GptConfig(vocab_size=512, d_model=256, num_layers=4, num_heads=2, d_ff=1024, max_seq_len=128,
+                    dropout=0.0)
+    M, b, S = 4, 2, 128
+    torch.manual_seed(0)
+    full = GptModel(cfg)
+    full.init_normal_(0.02)
+    sd = {k: v.clone() for k, v in full.state_dict().items()}
+    tr = PipelineTrainer(cfg, pp=world, dp=1, schedule=getattr(ScheduleType, sched_name), num_microbatches=M,
+                         micro_batch=b, seq_len=S, checkpoint=getattr(CheckpointStrategy, ckpt_name), fp8=False,
+                         lr=1e-3, device=dev)
+    tr.load_global_state_dict(sd)
+    g = torch.Generator().manual_seed(7)
+    t = torch.randint(0, cfg.vocab_size, (M, b, S + 1), generator=g)
+    ids, tgt = t[:, :, :-1].contiguous(), t[:, :, 1:].contiguous()
+    loss = tr.forward_backward(list(ids.to(dev).unbind(0)), list(tgt.to(dev).unbind(0)))
+    grads = {tr.global_name(n): p.main_grad.float().cpu().clone() for n, p in tr.model.named_parameters()}
+    out = {"loss": None if loss is None else float(loss), "grads": grads}
+    if rank == 0:
+        # single-GPU fused model on the whole batch: mean loss over all micro-batch tokens
+        ref = GptModel(cfg).to(dev)
+        ref.load_state_dict(sd)
+        ref.flatten(dev)
+        l_ref = ref.fused_loss(ids.reshape(M * b, S).to(dev), tgt.reshape(M * b, S).to(dev))
+        l_ref.backward()
+        out["ref_loss"] = float(l_ref)
+        out["ref_grads"] = {n: p.main_grad.float().cpu().clone() for n, p in ref.named_parameters()}
+    # a full optimizer step runs and the pipeline-wide overflow flag stays clear
+    tr.optimizer_step()
+    out["skip"] = float(tr.opt.state[5])
+    torch.cuda.synchronize()
+    return out
+
+
+@needs2
+@pytest.mark.parametrize("sched,ckpt", [("OneF1B", "Full"), ("Gpipe", "None_")])
+def test_pipeline_trainer_matches_single_gpu(sched, ckpt):
+    res = run_dist(_pp_body, 2, (sched, ckpt), backend="nccl")
+    ref_loss, ref_grads = res[0]["ref_loss"], res[0]["ref_grads"]
+    assert abs(res[1]["loss"] - ref_loss) < 2e-2 * abs(ref_loss)
+    checked = 0
+    for r in range(2):
+        assert res[r]["skip"] == 0.0
+        for name, gr in res[r]["grads"].items():
+            gref = ref_grads[name]
+            err = (gr - gref).norm() / max(gref.norm(), 1e-6)
+            assert err < 5e-2, (r, name, float(err))
+            checked += 1
+    assert checked == len(ref_grads)
