@@ -216,6 +216,17 @@ class PipelineTrainer:
                     getattr(st, k).copy_(v)
                 st.first_step, st._measured, st.cursor = saved_meta[0], saved_meta[1], saved_meta[2]
         torch.cuda.synchronize(dev)
+        # NCCL also connects collective rings / trees on their first use: do that now,
+        # at the sizes the step uses, for the data-parallel and the pipeline group
+        if self.reducer is not None:
+            s0, e0 = self.reducer.plan.ranges[0]
+            tmp = torch.zeros(max(e - s for s, e in self.reducer.plan.ranges), device=dev)
+            dist.all_reduce(tmp, group=self.dp_group)
+            dist.all_reduce(tmp[:e0 - s0], group=self.dp_group)
+            del tmp
+        if self.pp > 1:
+            dist.all_reduce(torch.zeros(2, device=dev), group=self.pipe_group)
+        torch.cuda.synchronize(dev)
 
     def forward_backward(self, ids, targets):
         """The schedule's forwards / backwards and the data-parallel reduction: leaves
