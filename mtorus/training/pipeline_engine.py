@@ -2,9 +2,10 @@
 
 The world of ``dp * pp`` ranks (one per GPU) is laid out as ``dp`` pipeline
 replicas of ``pp`` consecutive ranks: rank = replica * pp + stage.  Each rank
-builds only its stage of the model (``GptModel(layers=..., embed=..., head=...)``,
-the layer list split with ``split_evenly`` as in the reference's
-crates/mt-burn/src/module_ext.rs:40-79), flattens it into its own fp32 master /
+builds only its stage of the model (``GptModel(layers=..., embed=..., head=...)``;
+contiguous layer ranges as in the reference's crates/mt-burn/src/module_ext.rs:40-79,
+balanced by FLOPs with the LM head counted (``balanced_split``) or ``split_evenly``),
+flattens it into its own fp32 master /
 bf16 / fp32-grad buffers and runs:
 
 1. the per-rank GPipe or 1F1B program from the schedule builder
@@ -43,6 +44,47 @@ from ..torch_ext.module_ext import split_evenly
 from .fused_optim import ST_NONFINITE, ST_SUMSQ, DeviceLossScaleConfig, FusedAdam
 
 
+def stage_costs(config: GptConfig, seq_len: Optional[int] = None):
+    """Forward FLOPs per token of each transformer layer and of the LM head + loss."""
+    S = seq_len or config.max_seq_len
+    d, f, V = config.d_model, config.d_ff, config.vocab_size
+    layer = 2.0 * (4 * d * d + 2 * d * f) + 2.0 * S * d  # GEMMs + causal attention
+    head = 2.0 * d * V + 8.0 * V  # LM head GEMM + softmax cross-entropy
+    return layer, head
+
+
+def balanced_split(config: GptConfig, pp: int, seq_len: Optional[int] = None) -> List[tuple]:
+    """Contiguous layer ranges (lo, hi) for ``pp`` stages that minimise the slowest
+    stage, counting the LM head on the last stage (for GPT-1B it costs about two
+    layers).  Every stage gets at least one layer.  ``split_evenly`` (the reference's
+    rule) ignores the head, which leaves the last stage the bottleneck of the
+    schedule."""
+    L = config.num_layers
+    if pp < 1 or pp > L:
+        raise ValueError(f"cannot split {L} layers into {pp} stages")
+    layer, head = stage_costs(config, seq_len)
+    INF = float("inf")
+    # best[s][i]: min over splits of layers i..L-1 into stages s..pp-1 of the max stage cost
+    best = [[INF] * (L + 1) for _ in range(pp + 1)]
+    cut = [[0] * (L + 1) for _ in range(pp + 1)]
+    best[pp][L] = 0.0
+    for s in range(pp - 1, -1, -1):
+        for i in range(L - 1, -1, -1):
+            for j in range(i + 1, L - (pp - 1 - s) + 1):
+                c = (j - i) * layer + (head if s == pp - 1 else 0.0)
+                if s == pp - 1 and j != L:
+                    continue
+                v = max(c, best[s + 1][j])
+                if v < best[s][i]:
+                    best[s][i], cut[s][i] = v, j
+    out, i = [], 0
+    for s in range(pp):
+        j = cut[s][i]
+        out.append((i, j))
+        i = j
+    return out
+
+
 @dataclass
 class PipelineLayout:
     """Rank layout of a dp x pp job: ``stage_ranks[r]`` are the ranks of replica r
@@ -68,7 +110,7 @@ class PipelineTrainer:
                  checkpoint: CheckpointStrategy = CheckpointStrategy.Full, fp8: bool = True,
                  fp8_history: int = 16, lr: float = 3e-4, device=None, seed: int = 0,
                  bucket_mb: float = 25.0, loss_scale: Optional[DeviceLossScaleConfig] = None,
-                 max_grad_norm: float = 0.0, timed: bool = False):
+                 max_grad_norm: float = 0.0, timed: bool = False, split: str = "balanced"):
         world = dist.get_world_size()
         if world != dp * pp:
             raise ValueError(f"world size {world} != dp {dp} x pp {pp}")
@@ -94,7 +136,13 @@ class PipelineTrainer:
             g = dist.new_group(ranks)
             if self.rank in ranks:
                 self.dp_group = g
-        lo, hi = split_evenly(config.num_layers, pp)[self.stage]
+        if split == "balanced":
+            self.split = balanced_split(config, pp, self.S)
+        elif split == "even":
+            self.split = split_evenly(config.num_layers, pp)
+        else:
+            raise ValueError(f"unknown split {split!r}")
+        lo, hi = self.split[self.stage]
         self.layers = (lo, hi)
         self.is_first, self.is_last = self.stage == 0, self.stage == pp - 1
         torch.manual_seed(seed + self.stage)
@@ -273,4 +321,4 @@ class PipelineTrainer:
         return float(self._loss_host)
 
 
-__all__ = ["PipelineLayout", "PipelineTrainer"]
+__all__ = ["PipelineLayout", "PipelineTrainer", "balanced_split", "stage_costs"]

@@ -253,3 +253,26 @@ def test_distances():
                                 MeshTorusHybrid.new_2d(4, 4, 2)) == 2
     assert compute_hop_distance(TorusCoordinates.new_3d(0, 0, 0), TorusCoordinates.new_3d(1, 1, 1),
                                 MeshTorusHybrid.new_3d(4, 4, 4, 2)) == 3
+
+
+def test_balanced_split_counts_the_lm_head():
+    from mtorus.models.gpt import GptConfig
+    from mtorus.training.pipeline_engine import balanced_split, stage_costs
+
+    cfg = GptConfig.gpt_1b_bench()
+    layer, head = stage_costs(cfg)
+    split = balanced_split(cfg, 4)
+    assert split[0][0] == 0 and split[-1][1] == cfg.num_layers
+    assert all(a[1] == b[0] and a[1] > a[0] for a, b in zip(split, split[1:]))
+    cost = [(hi - lo) * layer + (head if i == 3 else 0) for i, (lo, hi) in enumerate(split)]
+    even_last = 6 * layer + head
+    assert max(cost) < even_last  # the even split's last stage is the bottleneck
+    # exhaustive check of optimality on a small case
+    import itertools
+
+    cfg.num_layers = 9
+    split = balanced_split(cfg, 3)
+    got = max((hi - lo) * layer + (head if i == 2 else 0) for i, (lo, hi) in enumerate(split))
+    best = min(max(a * layer, b * layer, (9 - a - b) * layer + head)
+               for a, b in itertools.product(range(1, 8), repeat=2) if a + b < 9)
+    assert abs(got - best) < 1e-6
