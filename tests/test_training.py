@@ -299,3 +299,22 @@ def test_training_loop_scaffold():
     assert t.total_steps == 3
     with pytest.raises(TrainingError.EmptyDataloader):
         training_loop(None, [], TrainingConfig())
+
+
+def test_gpt1b_cpu_example_runs_dp_pp_fp8(capsys):
+    """The CPU example (MockCommunicator x4 on a 2x2 torus, DP2 x PP2 1F1B, FP8
+    delayed scaling, dynamic loss scale) trains two steps with finite losses."""
+    import importlib.util
+    import json
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "examples", "gpt1b", "train.py")
+    spec = importlib.util.spec_from_file_location("gpt1b_example", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.main(["--steps", "2"]) == 0
+    out = capsys.readouterr().out.strip().splitlines()
+    assert out[0].startswith("Step   1 | loss = ")
+    summary = json.loads(out[-1])
+    assert summary["overflows"] == 0 and len(summary["loss_curve"]) == 2
+    assert all(6.0 < v < 8.0 for v in summary["loss_curve"])
