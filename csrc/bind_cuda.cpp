@@ -44,6 +44,11 @@ void gemm_fp8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B
               const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
               const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha,
               const c10::optional<at::Tensor>& alpha2, bool beta);
+// attention.cu
+std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H);
+at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
+                    int64_t B, int64_t S, int64_t H);
+int64_t attn_status(bool reset);
 // fp8.cu
 void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::Tensor>& scale,
                   const c10::optional<at::Tensor>& amax, int64_t fmt);
@@ -123,4 +128,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_halo", &symm_halo);
   m.def("install_segv_handler", &install_segv_handler);
   m.def("launch_count", []() { return mtorus::launch_counter(); });
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_status", &attn_status, py::arg("reset") = true);
 }

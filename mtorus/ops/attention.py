@@ -1,19 +1,69 @@
-"""Causal multi-head attention for the fused GPT path.
+"""Causal multi-head attention for the fused GPT path (sm_100a flash attention).
 
 Reference: scores = QK^T / sqrt(d_head) + mask -> softmax -> dropout -> PV
 (examples/gpt-1b/src/transformer.rs:51-85) with the [S,S] 0/-inf causal mask
-(transformer.rs:163-171).  The mask is applied by index here (no mask tensor)
-and the [B,H,S,S] score tensor is never materialised.
+(transformer.rs:163-171).  The mask is applied by index inside the kernels and
+the [B,H,S,S] score tensor is never materialised: ``csrc/kernels/attention.cu``
+runs the forward (O and the per-row log-sum-exp) and the backward (dQ, dK, dV
+straight into one [T, 3*H*d] gradient matrix) on tcgen05 with TMEM
+accumulators.  Head dim 128 and sequence lengths that are multiples of 128;
+no dropout.
 """
 from __future__ import annotations
 
+from typing import Tuple
+
 import torch
-import torch.nn.functional as F
+
+from .._ext import cuda as _cuda
+
+HEAD_DIM = 128
+TILE = 128
+
+
+def check_shape(S: int, dh: int) -> None:
+    if dh != HEAD_DIM or S % TILE != 0:
+        raise ValueError(f"fused attention needs head dim {HEAD_DIM} and seq len % {TILE} == 0 "
+                         f"(got head dim {dh}, seq len {S})")
+
+
+def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """qkv [B*S, 3*H*128] bf16 -> (out [B*S, H*128] bf16, lse [B, H, S] fp32)."""
+    out, lse = _cuda().attn_fwd(qkv, B, S, H)
+    return out, lse
+
+
+def attention_bwd(dout: torch.Tensor, qkv: torch.Tensor, out: torch.Tensor, lse: torch.Tensor,
+                  B: int, S: int, H: int) -> torch.Tensor:
+    """-> dqkv [B*S, 3*H*128] bf16 (dq | dk | dv)."""
+    return _cuda().attn_bwd(dout.contiguous(), qkv, out, lse, B, S, H)
+
+
+class CausalAttentionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, B, S, H):
+        out, lse = attention_fwd(qkv, B, S, H)
+        ctx.save_for_backward(qkv, out, lse)
+        ctx.dims = (B, S, H)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, out, lse = ctx.saved_tensors
+        return attention_bwd(dout, qkv, out, lse, *ctx.dims), None, None, None
 
 
 def causal_attention(qkv: torch.Tensor, B: int, S: int, H: int, dh: int) -> torch.Tensor:
     """qkv: [B*S, 3*H*dh] bf16 (q | k | v, heads contiguous) -> [B*S, H*dh]."""
-    q, k, v = qkv.view(B, S, 3, H, dh).unbind(2)
-    o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                       is_causal=True)
-    return o.transpose(1, 2).reshape(B * S, H * dh)
+    check_shape(S, dh)
+    return CausalAttentionFn.apply(qkv, B, S, H)
+
+
+def reference_attention(qkv: torch.Tensor, B: int, S: int, H: int, dh: int) -> torch.Tensor:
+    """Plain PyTorch fp32 oracle of the same op (tests only)."""
+    q, k, v = qkv.float().view(B, S, 3, H, dh).unbind(2)
+    q, k, v = (t.transpose(1, 2) for t in (q, k, v))
+    s = q @ k.transpose(-1, -2) / dh ** 0.5
+    mask = torch.ones(S, S, dtype=torch.bool, device=qkv.device).triu(1)
+    p = torch.softmax(s.masked_fill(mask, float("-inf")), dim=-1)
+    return (p @ v).transpose(1, 2).reshape(B * S, H * dh)

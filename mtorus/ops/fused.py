@@ -150,9 +150,10 @@ class AttnBlockFn(Function):
 
     @staticmethod
     def forward(ctx, x2d, ln, qkv_params, out_params, shape, fp8=None):
-        from .attention import causal_attention
+        from .attention import attention_fwd, check_shape
 
         B, S, H, dh = shape
+        check_shape(S, dh)
         h, mean, rstd = _ln_fwd(x2d, ln)
         wq, bq = qkv_params
         wo, bo = out_params
@@ -163,10 +164,8 @@ class AttnBlockFn(Function):
             h = h8
         else:
             qkv = K.gemm(h, wq.w16, bias=bq.data)
-        with torch.enable_grad():
-            qkv_leaf = qkv.detach().requires_grad_(True)
-            o_graph = causal_attention(qkv_leaf, B, S, H, dh)
-        o = o_graph.detach()
+        o, lse = attention_fwd(qkv, B, S, H)
+        attn_saved = (qkv, o, lse)
         if fp8 is not None:
             o8, io = st.quantize(o, tag + ".out_in", F8.E4M3)
             out = F8.gemm_fp8(o8, F8.E4M3, wo.w8, F8.E4M3, bias=bo.data, residual=x2d, alpha=io,
@@ -175,17 +174,18 @@ class AttnBlockFn(Function):
             ctx.inv = (ih, io)
         else:
             out = K.gemm(o, wo.w16, bias=bo.data, residual=x2d)
-        ctx.save_for_backward(x2d, mean, rstd, h, o)
-        ctx.attn = (qkv_leaf, o_graph)
+        ctx.save_for_backward(x2d, mean, rstd, h, o, *attn_saved)
+        ctx.shape = (B, S, H)
         ctx.params = (ln, qkv_params, out_params)
         ctx.fp8 = fp8
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        x2d, mean, rstd, h, o = ctx.saved_tensors
+        from .attention import attention_bwd
+
+        x2d, mean, rstd, h, o, qkv, o_bf16, lse = ctx.saved_tensors
         ln, (wq, bq), (wo, bo) = ctx.params
-        qkv_leaf, o_graph = ctx.attn
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
         fp8 = ctx.fp8
@@ -201,9 +201,7 @@ class AttnBlockFn(Function):
             K.gemm(dout, o, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc)
         K.colsum_(dout, bo.main_grad, acc)
         _grads_done(wo, bo)
-        torch.autograd.backward(o_graph, do)
-        dqkv = qkv_leaf.grad
-        ctx.attn = None
+        dqkv = attention_bwd(do, qkv, o_bf16, lse, *ctx.shape)
         K.colsum_(dqkv, bq.main_grad, acc)
         if fp8 is not None:
             q8, iq = st.quantize(dqkv, tag + ".qkv_grad", F8.E5M2)

@@ -262,3 +262,35 @@ def test_fp8_state_delayed_scaling():
     st.end_step()
     q3, inv3 = st.quantize(x, "a", F8.E4M3)
     assert abs(1.0 / inv3.item() - 416.0 / (2 * amax)) / (416.0 / amax) < 1e-5
+
+
+@pytest.mark.parametrize("B,S,H", [(1, 128, 1), (2, 256, 2), (1, 1024, 3)])
+def test_attention_forward_backward(B, S, H):
+    """tcgen05 flash attention (forward and backward) vs a plain fp32 PyTorch
+    causal softmax attention."""
+    from mtorus._ext import cuda as _cuda
+    from mtorus.ops.attention import attention_bwd, attention_fwd, reference_attention
+
+    torch.manual_seed(0)
+    dh = 128
+    qkv = (torch.randn(B * S, 3 * H * dh, device="cuda") * 1.5).bfloat16()
+    out, lse = attention_fwd(qkv, B, S, H)
+    torch.cuda.synchronize()
+    assert _cuda().attn_status(True) == 0
+    x = qkv.float().requires_grad_(True)
+    ref = reference_attention(x, B, S, H, dh)
+    assert _rel(out, ref) < 1e-2
+    # log-sum-exp of the scaled scores
+    q, k, _ = qkv.float().view(B, S, 3, H, dh).unbind(2)
+    s = (q.transpose(1, 2) @ k.transpose(1, 2).transpose(-1, -2)) / dh ** 0.5
+    s = s.masked_fill(torch.ones(S, S, dtype=torch.bool, device="cuda").triu(1), float("-inf"))
+    assert torch.allclose(lse, torch.logsumexp(s, -1), atol=2e-2, rtol=1e-3)
+    dout = torch.randn(B * S, H * dh, device="cuda").bfloat16()
+    ref.backward(dout.float())
+    dqkv = attention_bwd(dout, qkv, out, lse, B, S, H)
+    torch.cuda.synchronize()
+    assert _cuda().attn_status(True) == 0
+    g = x.grad.view(B * S, 3, H * dh)
+    d = dqkv.view(B * S, 3, H * dh)
+    for i, name in enumerate("qkv"):
+        assert _rel(d[:, i], g[:, i]) < 2e-2, (name, _rel(d[:, i], g[:, i]))

@@ -38,11 +38,11 @@ def test_trainer_loss_decreases():
     from mtorus.models.gpt import GptConfig
     from mtorus.training.engine import GptTrainer
 
-    cfg = GptConfig(vocab_size=256, d_model=256, num_layers=2, num_heads=2, d_ff=1024, max_seq_len=64,
+    cfg = GptConfig(vocab_size=256, d_model=256, num_layers=2, num_heads=2, d_ff=1024, max_seq_len=128,
                     dropout=0.0)
     tr = GptTrainer(cfg, device="cuda", lr=3e-3, init="normal", seed=0)
     g = torch.Generator().manual_seed(0)
-    t = torch.randint(0, cfg.vocab_size, (4, 65), generator=g)
+    t = torch.randint(0, cfg.vocab_size, (4, 129), generator=g)
     x, y = t[:, :-1].contiguous().pin_memory(), t[:, 1:].contiguous().pin_memory()
     losses = [tr.train_step(x, y) for _ in range(30)]
     assert losses[-1] < losses[0] - 1.0, losses
