@@ -88,40 +88,58 @@ __device__ __forceinline__ void named_sync_compute() {
 }
 
 // ================================================================== forward
+//
+// One CTA per (256 consecutive queries = tiles A (upper) and B (lower), batch, head).
+// TMEM: S_A | O_A | S_B | O_B (128 columns each).  Shared memory: Q_A, Q_B, a ring
+// of three 32 KB slots that receives K_0, V_0, K_1, V_1, ... in order, P_A, P_B.
+// MMA order: S_A0 S_B0 | PV_A0 S_A1 PV_B0 S_B1 | PV_A1 S_A2 ... so the tensor core
+// works on one tile while the other tile's softmax warps run.
+constexpr int kRing = 3;
+constexpr int kFwdThreads = 320;  // producer, MMA, 2 x 4 softmax warps
+
 struct FwdCtl {
-  uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full, o_done, drain;
+  uint64_t q_full, ring_full[kRing], ring_empty[kRing], s_full[2], p_full[2], o_done[2], drain;
   uint32_t tmem_base;
   int abort;
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tma_qkv, bf16* __restrict__ out, int ld_out,
                     float* __restrict__ lse, int B, int H, int S, float scale, int* status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sQ = smem;
-  uint8_t* sKV = smem + kTileBytes;             // stage s: K at +2s*32K, V at +(2s+1)*32K
-  uint8_t* sP = smem + 5 * kTileBytes;
-  FwdCtl* ctl = reinterpret_cast<FwdCtl*>(smem + 6 * kTileBytes);
+  uint8_t* sQ = smem;                        // tile g at g * 32K (g = 0: A, 1: B)
+  uint8_t* sRing = smem + 2 * kTileBytes;     // slot s at s * 32K
+  uint8_t* sP = smem + 5 * kTileBytes;        // tile g at g * 32K
+  FwdCtl* ctl = reinterpret_cast<FwdCtl*>(smem + 7 * kTileBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = S / kTile;
-  const int bh = blockIdx.x % (B * H);
-  const int qt = nq - 1 - blockIdx.x / (B * H);  // heaviest query tiles first
+  const int npair = (nq + 1) / 2;
+  const int bh = blockIdx.x / npair;
+  const int pair = blockIdx.x % npair;        // heaviest first within a head
   const int b = bh / H, h = bh % H;
-  const int nkv = qt + 1;
-  const int row0 = b * S + qt * kTile;
+  const int qtA = nq - 1 - 2 * pair, qtB = qtA - 1;  // qtB = -1: no tile B (odd tile count)
+  const int nkv = qtA + 1;                     // tile B uses tiles 0 .. nkv-2
 
   if (threadIdx.x == 0) {
     mbar_init(&ctl->q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&ctl->kv_full[s], 1);
-      mbar_init(&ctl->kv_empty[s], 1);
-      mbar_init(&ctl->s_full[s], 1);
+    for (int s = 0; s < kRing; ++s) {
+      mbar_init(&ctl->ring_full[s], 1);
+      mbar_init(&ctl->ring_empty[s], 1);
     }
-    mbar_init(&ctl->p_full, 128);
-    mbar_init(&ctl->o_done, 1);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&ctl->s_full[g], 1);
+      mbar_init(&ctl->p_full[g], 128);
+      mbar_init(&ctl->o_done[g], 1);
+    }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     fence_mbar_init();
@@ -135,36 +153,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO = tmem + 256;
   volatile int* abort = &ctl->abort;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
       const int qcol = h * kD, kcol = H * kD + h * kD, vcol = 2 * H * kD + h * kD;
-      mbar_arrive_expect_tx(&ctl->q_full, kTileBytes);
-      tma_load_2d(sQ, &tma_qkv, &ctl->q_full, qcol, row0);
-      tma_load_2d(sQ + kHalf, &tma_qkv, &ctl->q_full, qcol + 64, row0);
+      mbar_arrive_expect_tx(&ctl->q_full, 2 * kTileBytes);
+      for (int g = 0; g < 2; ++g) {
+        const int r0 = b * S + max(g == 0 ? qtA : qtB, 0) * kTile;  // an absent tile B loads tile 0, unused
+        tma_load_2d(sQ + g * kTileBytes, &tma_qkv, &ctl->q_full, qcol, r0);
+        tma_load_2d(sQ + g * kTileBytes + kHalf, &tma_qkv, &ctl->q_full, qcol + 64, r0);
+      }
       uint32_t issued = 0, par = 0;
-      for (int j = 0; j < nkv && !*abort; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&ctl->kv_empty[st], ((j >> 1) - 1) & 1, abort, status, 11)) break;
-        uint8_t* k = sKV + (2 * st) * kTileBytes;
-        uint8_t* v = k + kTileBytes;
-        const int kr = b * S + j * kTile;
-        issued |= 1u << st;
-        par = (par & ~(1u << st)) | (((uint32_t)(j >> 1) & 1u) << st);
-        mbar_arrive_expect_tx(&ctl->kv_full[st], 2 * kTileBytes);
-        tma_load_2d(k, &tma_qkv, &ctl->kv_full[st], kcol, kr);
-        tma_load_2d(k + kHalf, &tma_qkv, &ctl->kv_full[st], kcol + 64, kr);
-        tma_load_2d(v, &tma_qkv, &ctl->kv_full[st], vcol, kr);
-        tma_load_2d(v + kHalf, &tma_qkv, &ctl->kv_full[st], vcol + 64, kr);
+      for (int n = 0; n < 2 * nkv && !*abort; ++n) {  // n = 2j: K_j, 2j+1: V_j
+        const int s = n % kRing, use = n / kRing;
+        if (use > 0 && !mbar_wait(&ctl->ring_empty[s], (use - 1) & 1, abort, status, 11)) break;
+        const int col = (n & 1) ? vcol : kcol;
+        const int r0 = b * S + (n >> 1) * kTile;
+        uint8_t* dst = sRing + s * kTileBytes;
+        issued |= 1u << s;
+        par = (par & ~(1u << s)) | (((uint32_t)use & 1u) << s);
+        mbar_arrive_expect_tx(&ctl->ring_full[s], kTileBytes);
+        tma_load_2d(dst, &tma_qkv, &ctl->ring_full[s], col, r0);
+        tma_load_2d(dst + kHalf, &tma_qkv, &ctl->ring_full[s], col + 64, r0);
       }
       if (*abort) {
         bounded_drain(&ctl->q_full, 0);
-        for (int s = 0; s < 2; ++s)
-          if (issued >> s & 1u) bounded_drain(&ctl->kv_full[s], (par >> s) & 1u);
+        for (int s = 0; s < kRing; ++s)
+          if (issued >> s & 1u) bounded_drain(&ctl->ring_full[s], (par >> s) & 1u);
       }
     }
   } else if (warp == 1) {
@@ -172,31 +189,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------------- MMA issuer
       const uint32_t idS = make_idesc_bf16(kTile, kTile, 0, 0);
       const uint32_t idO = make_idesc_bf16(kTile, kD, 0, 1);
-      const uint32_t q = smem_u32(sQ), p = smem_u32(sP);
-      bool issued_any = false, ok = mbar_wait(&ctl->q_full, 0, abort, status, 12);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&ctl->kv_full[st], (j >> 1) & 1, abort, status, 13)) return false;
+      bool issued_any = false;
+      bool ok = mbar_wait(&ctl->q_full, 0, abort, status, 12);
+      auto ring_wait = [&](int n) -> bool {
+        const int s = n % kRing;
+        if (!mbar_wait(&ctl->ring_full[s], (n / kRing) & 1, abort, status, 13)) return false;
         tc_fence_after();
-        const uint32_t k = smem_u32(sKV + (2 * st) * kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          umma_f16(tS[st], desc_kmajor(q, kk), desc_kmajor(k, kk), idS, kk > 0 ? 1u : 0u);
-        umma_commit(&ctl->s_full[st]);
-        issued_any = true;
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < nkv && ok; ++j) {
-        if (j + 1 < nkv && !issue_s(j + 1)) break;
-        if (!mbar_wait(&ctl->p_full, j & 1, abort, status, 14)) break;
-        tc_fence_after();
-        const uint32_t v = smem_u32(sKV + (2 * (j & 1) + 1) * kTileBytes);
+      // S_g(j) = Q_g K_j^T; K_j's slot is released after the last tile that needs it
+      auto issue_s = [&](int g, int j) {
+        const uint32_t q = smem_u32(sQ + g * kTileBytes);
+        const uint32_t k = smem_u32(sRing + ((2 * j) % kRing) * kTileBytes);
+        const uint32_t d = tmem + g * 256;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          umma_f16(d, desc_kmajor(q, kk), desc_kmajor(k, kk), idS, kk > 0 ? 1u : 0u);
+        umma_commit(&ctl->s_full[g]);
+        issued_any = true;
+      };
+      auto issue_pv = [&](int g, int j) {
+        const uint32_t p = smem_u32(sP + g * kTileBytes);
+        const uint32_t v = smem_u32(sRing + ((2 * j + 1) % kRing) * kTileBytes);
+        const uint32_t d = tmem + g * 256 + 128;
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
-          umma_f16(tO, desc_kmajor(p, kk), desc_mnmajor(v, kk), idO, (j | kk) != 0 ? 1u : 0u);
-        umma_commit(&ctl->o_done);
-        umma_commit(&ctl->kv_empty[j & 1]);
+          umma_f16(d, desc_kmajor(p, kk), desc_mnmajor(v, kk), idO, (j | kk) != 0 ? 1u : 0u);
+        umma_commit(&ctl->o_done[g]);
+      };
+      // prologue: S_A(0), S_B(0)
+      if (ok && (ok = ring_wait(0))) {
+        issue_s(0, 0);
+        if (nkv - 1 > 0) issue_s(1, 0);
+        umma_commit(&ctl->ring_empty[0]);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const bool b_needs = j < nkv - 1;  // tile B uses KV tiles 0 .. nkv-2
+        if (!(ok = ring_wait(2 * j + 1))) break;  // V_j
+        // A: PV_A(j), then S_A(j+1)
+        if (!(ok = mbar_wait(&ctl->p_full[0], j & 1, abort, status, 14))) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        const bool more = j + 1 < nkv;
+        if (more) {
+          if (!(ok = ring_wait(2 * j + 2))) break;  // K_{j+1}
+          issue_s(0, j + 1);
+        }
+        // B: PV_B(j), then S_B(j+1)
+        if (b_needs) {
+          if (!(ok = mbar_wait(&ctl->p_full[1], j & 1, abort, status, 15))) break;
+          tc_fence_after();
+          issue_pv(1, j);
+          if (j + 1 < nkv - 1) issue_s(1, j + 1);
+        }
+        umma_commit(&ctl->ring_empty[(2 * j + 1) % kRing]);  // V_j
+        if (more) umma_commit(&ctl->ring_empty[(2 * j + 2) % kRing]);  // K_{j+1}
       }
       if (*abort && issued_any) {
         umma_commit(&ctl->drain);
@@ -205,71 +252,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax
+    const int g = (warp - 2) >> 2;            // 0: tile A (warps 2-5), 1: tile B (warps 6-9)
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // query row within the tile
+    const int r = quarter * 32 + lane;        // query row within the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + g * 256 + lane_off, tO = tS + 128;
+    const int qt = g == 0 ? qtA : qtB;
+    const int n = g == 0 ? nkv : nkv - 1;
+    uint8_t* myP = sP + g * kTileBytes;
     const float sl2 = scale * kLog2e;
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait(&ctl->s_full[st], (j >> 1) & 1, abort, status, 15)) {
+    for (int j = 0; j < n; ++j) {
+      if (!mbar_wait(&ctl->s_full[g], j & 1, abort, status, 16)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float t[kTile];
+      uint32_t t[kTile];  // raw scores, loaded straight into the row's registers
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tS[st] + lane_off + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) t[c * 32 + e] = __uint_as_float(v[e]) * sl2;
-      }
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&t[c * 32]));
+      tmem_wait_ld();
       if (j == qt) {  // diagonal tile: keys after the query are masked
 #pragma unroll
         for (int e = 0; e < kTile; ++e)
-          if (e > r) t[e] = -INFINITY;
+          if (e > r) t[e] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      float mx = __uint_as_float(t[0]);
 #pragma unroll
-      for (int e = 0; e < kTile; ++e) mx = fmaxf(mx, t[e]);
+      for (int e = 1; e < kTile; ++e) mx = fmaxf(mx, __uint_as_float(t[e]));
+      mx *= sl2;
       float alpha = 1.f;
       if (j == 0) {
         m_ref = mx;
       } else if (mx > m_ref + kRescale) {
-        alpha = exp2f(m_ref - mx);
+        alpha = ex2_approx(m_ref - mx);
         m_ref = mx;
       }
-      // O and the P buffer are free once the previous P V product has completed
-      if (j > 0) {
-        if (!mbar_wait(&ctl->o_done, (j - 1) & 1, abort, status, 16)) {
+      if (j > 0) {  // O and P_g are free once PV_g(j-1) has completed
+        if (!mbar_wait(&ctl->o_done[g], (j - 1) & 1, abort, status, 17)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32(tO + lane_off + c * 32, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
-            tmem_st32(tO + lane_off + c * 32, v);
-          }
-          tmem_wait_st();
-        }
       }
       l *= alpha;
       float sum = 0.f;
+      const float neg = -m_ref;
 #pragma unroll
       for (int c16 = 0; c16 < kTile / 8; ++c16) {
         float pv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          pv[e] = exp2f(t[c16 * 8 + e] - m_ref);
+          pv[e] = ex2_approx(fmaf(__uint_as_float(t[c16 * 8 + e]), sl2, neg));
           sum += pv[e];
         }
         uint4 w;
@@ -277,21 +312,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         w.y = pack_bf16x2(pv[2], pv[3]);
         w.z = pack_bf16x2(pv[4], pv[5]);
         w.w = pack_bf16x2(pv[6], pv[7]);
-        *reinterpret_cast<uint4*>(sP + sw128_chunk(r, c16)) = w;
+        *reinterpret_cast<uint4*>(myP + sw128_chunk(r, c16)) = w;
       }
       l += sum;
+      // rescale O (rows whose max grew) before PV_g(j) accumulates into it
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tO + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+          tmem_st32(tO + c * 32, v);
+        }
+        tmem_wait_st();
+      }
       fence_async_shared();
       tc_fence_before();
-      mbar_arrive(&ctl->p_full);
+      mbar_arrive(&ctl->p_full[g]);
     }
-    if (ok && mbar_wait(&ctl->o_done, (nkv - 1) & 1, abort, status, 17)) {
+    if (ok && n > 0 && mbar_wait(&ctl->o_done[g], (n - 1) & 1, abort, status, 18)) {
       tc_fence_after();
       const float inv = 1.f / l;
-      bf16* dst = out + (size_t)(row0 + r) * ld_out + h * kD;
+      const int row = b * S + qt * kTile + r;
+      bf16* dst = out + (size_t)row * ld_out + h * kD;
 #pragma unroll 1
       for (int c = 0; c < kD / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tO + lane_off + c * 32, v);
+        tmem_ld32(tO + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; e += 8) {
@@ -315,17 +364,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ================================================================== backward
+//
+// One CTA per (128-key tile j, batch, head) looping over query tiles i = j .. nt-1.
+// Shared memory: K, V, Q / dO of the current query tile, one tile that first holds
+// P^T (read by the dV MMA) and then dS^T (read by the dK and dQ MMAs), and a 64 KB
+// fp32 staging area from which dQ_i leaves as four [128 x 32] TMA reduce-adds into
+// the fp32 dQ buffer (full-line reductions in L2 instead of scattered atomics).
+// TMEM: S^T | dP^T | dV | dK; dQ_i reuses S^T.
 struct BwdCtl {
-  uint64_t kv_full, qdo_full, qdo_empty, st_full, pds_full, dq_full, dq_free, kv_done, drain;
+  uint64_t kv_full, qdo_full, qdo_empty, st_full, p_ready, pv_done, ds_ready, dq_full, dq_free,
+      kv_done, drain;
   uint32_t tmem_base;
   int abort;
   float lse[kTile];
   float dd[kTile];
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+constexpr int kBwdThreads = 320;  // producer, MMA, 2 x 4 compute warps (column halves)
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tma_qkv, const __grid_constant__ CUtensorMap tma_do,
-                    const float* __restrict__ lse, const float* __restrict__ dvec, float* __restrict__ dq,
+                    const __grid_constant__ CUtensorMap tma_dq,
+                    const float* __restrict__ lse, const float* __restrict__ dvec,
                     bf16* __restrict__ dqkv, int ld_dqkv, int B, int H, int S, float scale, int* status) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -334,14 +394,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sV = smem + kTileBytes;
   uint8_t* sQ = smem + 2 * kTileBytes;
   uint8_t* sDO = smem + 3 * kTileBytes;
-  uint8_t* sPT = smem + 4 * kTileBytes;
-  uint8_t* sDST = smem + 5 * kTileBytes;
-  BwdCtl* ctl = reinterpret_cast<BwdCtl*>(smem + 6 * kTileBytes);
+  uint8_t* sPS = smem + 4 * kTileBytes;    // P^T, then dS^T
+  uint8_t* sDQ = smem + 5 * kTileBytes;    // 4 x [128 rows x 128 B] fp32 boxes, SW128
+  BwdCtl* ctl = reinterpret_cast<BwdCtl*>(smem + 7 * kTileBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = S / kTile;
-  const int bh = blockIdx.x % (B * H);
-  const int kt = blockIdx.x / (B * H);  // key tile; tile 0 loops over every query tile
+  const int bh = blockIdx.x / nt;
+  const int kt = blockIdx.x % nt;        // key tile; tile 0 loops over every query tile
   const int b = bh / H, h = bh % H;
   const int nqi = nt - kt;               // query tiles i = kt .. nt-1
   const int krow0 = b * S + kt * kTile;
@@ -351,15 +411,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&ctl->qdo_full, 1);
     mbar_init(&ctl->qdo_empty, 1);
     mbar_init(&ctl->st_full, 1);
-    mbar_init(&ctl->pds_full, 128);
+    mbar_init(&ctl->p_ready, 256);
+    mbar_init(&ctl->pv_done, 1);
+    mbar_init(&ctl->ds_ready, 256);
     mbar_init(&ctl->dq_full, 1);
-    mbar_init(&ctl->dq_free, 128);
+    mbar_init(&ctl->dq_free, 256);
     mbar_init(&ctl->kv_done, 1);
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tma_qkv);
     tma_prefetch_desc(&tma_do);
+    tma_prefetch_desc(&tma_dq);
   }
   if (warp == 1) {
     tmem_alloc(&ctl->tmem_base, 512);
@@ -404,10 +467,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t id_kk = make_idesc_bf16(kTile, kTile, 0, 0);  // A, B K-major
       const uint32_t id_kn = make_idesc_bf16(kTile, kD, 0, 1);     // A K-major, B MN-major
       const uint32_t id_mn = make_idesc_bf16(kTile, kD, 1, 1);     // A, B MN-major
-      const uint32_t k = smem_u32(sK), v = smem_u32(sV), q = smem_u32(sQ), dO = smem_u32(sDO);
-      const uint32_t pT = smem_u32(sPT), dsT = smem_u32(sDST);
+      const uint32_t k = smem_u32(sK), v = smem_u32(sV), ps = smem_u32(sPS);
       bool issued_any = false;
       bool ok = mbar_wait(&ctl->kv_full, 0, abort, status, 22);
+      const uint32_t q = smem_u32(sQ), dO = smem_u32(sDO);
       for (int it = 0; it < nqi && ok; ++it) {
         if (!mbar_wait(&ctl->qdo_full, it & 1, abort, status, 23)) break;
         // the S^T columns hold dQ of the previous tile until the compute warps read it
@@ -421,17 +484,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16(tDP, desc_kmajor(v, kk), desc_kmajor(dO, kk), id_kk, kk > 0 ? 1u : 0u);
         umma_commit(&ctl->st_full);
         issued_any = true;
-        if (!mbar_wait(&ctl->pds_full, it & 1, abort, status, 25)) break;
+        if (!mbar_wait(&ctl->p_ready, it & 1, abort, status, 25)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dV += P^T dO
-          umma_f16(tDV, desc_kmajor(pT, kk), desc_mnmajor(dO, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
+          umma_f16(tDV, desc_kmajor(ps, kk), desc_mnmajor(dO, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
+        umma_commit(&ctl->pv_done);
+        if (!mbar_wait(&ctl->ds_ready, it & 1, abort, status, 29)) break;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dK += dS^T Q
-          umma_f16(tDK, desc_kmajor(dsT, kk), desc_mnmajor(q, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
+          umma_f16(tDK, desc_kmajor(ps, kk), desc_mnmajor(q, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dQ_i = dS K
-          umma_f16(tDQ, desc_mnmajor(dsT, kk), desc_mnmajor(k, kk), id_mn, kk > 0 ? 1u : 0u);
+          umma_f16(tDQ, desc_mnmajor(ps, kk), desc_mnmajor(k, kk), id_mn, kk > 0 ? 1u : 0u);
         umma_commit(&ctl->dq_full);
         umma_commit(&ctl->qdo_empty);
       }
@@ -445,84 +511,121 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------------ compute
     const int quarter = warp & 3;
+    const int ch = (warp - 2) >> 2;     // column half: 0 (warps 2-5) or 1 (warps 6-9)
     const int r = quarter * 32 + lane;  // key row (S^T, dP^T, dV, dK) or query row (dQ)
-    const int tid = threadIdx.x - 64;
+    const int tid = threadIdx.x - 64;   // 0 .. 255
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const float sl2 = scale * kLog2e;
     bool ok = true;
+    // the tile's log-sum-exp (log2 units; threads 0-127) and D (threads 128-255), fetched a tile ahead
+    const float* src = tid < kTile ? lse : dvec;
+    const float mul = tid < kTile ? kLog2e : 1.f;
+    float* dst = tid < kTile ? ctl->lse : ctl->dd;
+    const int ti = tid & (kTile - 1);
+    float next = src[(size_t)bh * S + kt * kTile + ti] * mul;
     for (int it = 0; it < nqi; ++it) {
       const int qi = kt + it;
-      // this tile's log-sum-exp (log2 units) and D, shared by all key rows
-      ctl->lse[tid] = lse[(size_t)bh * S + qi * kTile + tid] * kLog2e;
-      ctl->dd[tid] = dvec[(size_t)bh * S + qi * kTile + tid];
-      named_sync_compute();
+      // every thread read the previous tile's values before arriving on p_ready,
+      // which the MMA of that tile (and so dq_full, waited below) depends on
+      dst[ti] = next;
+      if (it + 1 < nqi) next = src[(size_t)bh * S + (qi + 1) * kTile + ti] * mul;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float* sl = ctl->lse;
+      const float* sd = ctl->dd;
       if (!mbar_wait(&ctl->st_full, it & 1, abort, status, 26)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const bool diag = qi == kt;
-#pragma unroll 1
-      for (int c = 0; c < kTile / 32; ++c) {
+      uint32_t dsp[32];  // this thread's 64 dS^T values as bf16 pairs, stored after the dV MMA
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = ch * 2 + cc;
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + lane_off + c * 32, sv);
         tmem_ld32(tDP + lane_off + c * 32, dv);
         tmem_wait_ld();
-        float p[32], ds[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int col = c * 32 + e;  // query within the tile
-          float pe = exp2f(__uint_as_float(sv[e]) * sl2 - ctl->lse[col]);
-          if (diag && col < r) pe = 0.f;  // query before key: masked in the forward
-          p[e] = pe;
-          ds[e] = pe * (__uint_as_float(dv[e]) - ctl->dd[col]) * scale;
-        }
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          uint4 wp, wd;
-          wp.x = pack_bf16x2(p[g * 8 + 0], p[g * 8 + 1]);
-          wp.y = pack_bf16x2(p[g * 8 + 2], p[g * 8 + 3]);
-          wp.z = pack_bf16x2(p[g * 8 + 4], p[g * 8 + 5]);
-          wp.w = pack_bf16x2(p[g * 8 + 6], p[g * 8 + 7]);
-          wd.x = pack_bf16x2(ds[g * 8 + 0], ds[g * 8 + 1]);
-          wd.y = pack_bf16x2(ds[g * 8 + 2], ds[g * 8 + 3]);
-          wd.z = pack_bf16x2(ds[g * 8 + 4], ds[g * 8 + 5]);
-          wd.w = pack_bf16x2(ds[g * 8 + 6], ds[g * 8 + 7]);
-          const uint32_t off = sw128_chunk(r, c * 4 + g);
-          *reinterpret_cast<uint4*>(sPT + off) = wp;
-          *reinterpret_cast<uint4*>(sDST + off) = wd;
+          float p[8], ds[8];
+#pragma unroll
+          for (int x = 0; x < 8; ++x) {
+            const int e = g * 8 + x, col = c * 32 + e;  // query within the tile
+            float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -sl[col]));
+            if (diag && col < r) pe = 0.f;  // query before key: masked in the forward
+            p[x] = pe;
+            ds[x] = pe * (__uint_as_float(dv[e]) - sd[col]) * scale;
+          }
+          uint4 wp;
+          wp.x = pack_bf16x2(p[0], p[1]);
+          wp.y = pack_bf16x2(p[2], p[3]);
+          wp.z = pack_bf16x2(p[4], p[5]);
+          wp.w = pack_bf16x2(p[6], p[7]);
+          *reinterpret_cast<uint4*>(sPS + sw128_chunk(r, c * 4 + g)) = wp;
+#pragma unroll
+          for (int x = 0; x < 4; ++x) dsp[(cc * 32 + g * 8) / 2 + x] = pack_bf16x2(ds[2 * x], ds[2 * x + 1]);
         }
       }
       fence_async_shared();
       tc_fence_before();
-      mbar_arrive(&ctl->pds_full);
+      mbar_arrive(&ctl->p_ready);
+      // dS^T replaces P^T once the dV MMA has read it
+      if (!mbar_wait(&ctl->pv_done, it & 1, abort, status, 30)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int c16 = 0; c16 < 8; ++c16) {
+        uint4 w;
+        w.x = dsp[c16 * 4 + 0];
+        w.y = dsp[c16 * 4 + 1];
+        w.z = dsp[c16 * 4 + 2];
+        w.w = dsp[c16 * 4 + 3];
+        *reinterpret_cast<uint4*>(sPS + sw128_chunk(r, ch * 8 + c16)) = w;
+      }
+      fence_async_shared();
+      tc_fence_before();
+      mbar_arrive(&ctl->ds_ready);
       if (!mbar_wait(&ctl->dq_full, it & 1, abort, status, 27)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float* dqrow = dq + (size_t)(b * S + qi * kTile + r) * (H * kD) + h * kD;
+      // the previous tile's reduce-adds must have read the staging boxes of this half
+      const bool leader = (quarter == 0 && lane == 0);  // one thread per column half
+      if (leader) bulk_wait_group_read<0>();
+      asm volatile("bar.sync %0, 128;" ::"r"(2 + ch) : "memory");
 #pragma unroll 1
-      for (int c = 0; c < kD / 32; ++c) {
+      for (int c = ch * 2; c < ch * 2 + 2; ++c) {
         uint32_t v[32];
         tmem_ld32(tDQ + lane_off + c * 32, v);
         tmem_wait_ld();
+        uint8_t* box = sDQ + c * kHalf;
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          atomicAdd(reinterpret_cast<float4*>(dqrow + c * 32 + e),
-                    make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]), __uint_as_float(v[e + 2]),
-                                __uint_as_float(v[e + 3])));
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<uint4*>(box + r * 128 + ((k ^ (r & 7)) << 4)) =
+              make_uint4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
       }
       tc_fence_before();
       mbar_arrive(&ctl->dq_free);
+      fence_async_shared();
+      asm volatile("bar.sync %0, 128;" ::"r"(2 + ch) : "memory");
+      if (leader) {
+        const int y = b * S + qi * kTile;
+        tma_reduce_add_2d(&tma_dq, sDQ + (ch * 2) * kHalf, h * kD + ch * 64, y);
+        tma_reduce_add_2d(&tma_dq, sDQ + (ch * 2 + 1) * kHalf, h * kD + ch * 64 + 32, y);
+        bulk_commit_group();
+      }
     }
+    if ((quarter == 0 && lane == 0)) bulk_wait_group<0>();  // dQ reductions complete before exit
     if (ok && mbar_wait(&ctl->kv_done, 0, abort, status, 28)) {
       tc_fence_after();
       // dK and dV rows of this key tile -> the k and v thirds of dqkv
       bf16* dk = dqkv + (size_t)(krow0 + r) * ld_dqkv + H * kD + h * kD;
       bf16* dvp = dqkv + (size_t)(krow0 + r) * ld_dqkv + 2 * H * kD + h * kD;
 #pragma unroll 1
-      for (int c = 0; c < kD / 32; ++c) {
+      for (int c = ch * 2; c < ch * 2 + 2; ++c) {
         uint32_t a[32], bb[32];
         tmem_ld32(tDK + lane_off + c * 32, a);
         tmem_ld32(tDV + lane_off + c * 32, bb);
@@ -592,8 +695,8 @@ __global__ void attn_dq_cast_kernel(const float* __restrict__ dq, bf16* __restri
   *reinterpret_cast<uint4*>(dqkv + t * ld_dqkv + c) = w;
 }
 
-constexpr size_t kFwdSmem = 6 * kTileBytes + sizeof(FwdCtl) + 1024;
-constexpr size_t kBwdSmem = 6 * kTileBytes + sizeof(BwdCtl) + 1024;
+constexpr size_t kFwdSmem = 7 * kTileBytes + sizeof(FwdCtl) + 1024;
+constexpr size_t kBwdSmem = 7 * kTileBytes + sizeof(BwdCtl) + 1024;
 
 void check_qkv(const at::Tensor& qkv, int B, int S, int H) {
   MT_CHECK_CUDA(qkv);
@@ -621,8 +724,8 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, in
                                         (int)kFwdSmem));
     attr = true;
   }
-  const int grid = (int)(B * H * (S / kTile));
-  attn_fwd_kernel<<<grid, kThreads, kFwdSmem, cur_stream()>>>(tm, (bf16*)out.data_ptr(), (int)(H * kD),
+  const int grid = (int)(B * H * ((S / kTile + 1) / 2));
+  attn_fwd_kernel<<<grid, kFwdThreads, kFwdSmem, cur_stream()>>>(tm, (bf16*)out.data_ptr(), (int)(H * kD),
                                                               lse.data_ptr<float>(), (int)B, (int)H, (int)S,
                                                               1.0f / sqrtf((float)kD), attn_status_ptr());
   MT_LAUNCH_CHECK();
@@ -654,6 +757,8 @@ at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Ten
                                      qkv.stride(0), 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap td = make_tma_2d(dout.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, T, HD, 64, kTile,
                                      CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tdq = make_tma_2d(dq.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, HD, T, HD, 32, kTile,
+                                      CU_TENSOR_MAP_SWIZZLE_128B);
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -661,8 +766,8 @@ at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Ten
     attr = true;
   }
   const int grid = (int)(B * H * (S / kTile));
-  attn_bwd_kernel<<<grid, kThreads, kBwdSmem, cur_stream()>>>(
-      tq, td, lse.data_ptr<float>(), dvec.data_ptr<float>(), dq.data_ptr<float>(), (bf16*)dqkv.data_ptr(),
+  attn_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, cur_stream()>>>(
+      tq, td, tdq, lse.data_ptr<float>(), dvec.data_ptr<float>(), (bf16*)dqkv.data_ptr(),
       (int)(3 * HD), (int)B, (int)H, (int)S, 1.0f / sqrtf((float)kD), attn_status_ptr());
   MT_LAUNCH_CHECK();
   {
