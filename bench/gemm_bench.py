@@ -38,6 +38,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--case", default=None, help="run only the named case (e.g. ffn1_fwd_fp8)")
     args = ap.parse_args()
     peak = 1607.9
     p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
@@ -58,6 +59,9 @@ def main():
                  ("ffn2_dgrad_fp8", T, F, d, "dgrad"), ("ffn1_wgrad_fp8", F, d, T, "wgrad"),
                  ("square8k_fp8", 8192, 8192, 8192, "tn")]
     one = torch.ones(1, device="cuda")
+    if args.case:
+        fp8_cases = [c for c in fp8_cases if c[0] == args.case]
+        cases = [c for c in cases if c[0] == args.case]
     for name, M, N, Kd, lay in fp8_cases:
         A = (torch.randn(M, Kd, device="cuda") if lay != "wgrad" else torch.randn(Kd, M, device="cuda")).to(
             torch.float8_e4m3fn).view(torch.uint8)

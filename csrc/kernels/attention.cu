@@ -654,27 +654,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-// D[bh, s] = sum_c dO[t, h*128 + c] * O[t, h*128 + c]; one warp per (token, head).
+// D[bh, s] = sum_c dO[t, h*128 + c] * O[t, h*128 + c], with 16 threads per (token,
+// head) row and 16-byte loads; the same threads zero that row's slice of the fp32
+// dQ accumulator, which the backward kernel then reduces into.
 __global__ void attn_bwd_dot_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ o, int ld,
-                                    float* __restrict__ dvec, int B, int H, int S) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const int total = B * S * H;
-  if (w >= total) return;
-  const int t = w / H, h = w % H;
-  const bf16* a = dout + (size_t)t * ld + h * kD + lane * 4;
-  const bf16* c = o + (size_t)t * ld + h * kD + lane * 4;
-  const uint2 ua = *reinterpret_cast<const uint2*>(a), uc = *reinterpret_cast<const uint2*>(c);
-  const bf162* ha = reinterpret_cast<const bf162*>(&ua);
-  const bf162* hc = reinterpret_cast<const bf162*>(&uc);
+                                    float* __restrict__ dvec, float* __restrict__ dq, int B, int H, int S) {
+  const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long row = g >> 4;  // (token, head)
+  const int sub = threadIdx.x & 15;
+  const long long total = (long long)B * S * H;
+  if (row >= total) return;
+  const long long t = row / H;
+  const int h = (int)(row % H);
+  const size_t off = (size_t)t * ld + h * kD + sub * 8;
+  const uint4 ua = *reinterpret_cast<const uint4*>(dout + off);
+  const uint4 uc = *reinterpret_cast<const uint4*>(o + off);
+  float fa[8], fc[8];
+  unpack8(*reinterpret_cast<const bf16x8*>(&ua), fa);
+  unpack8(*reinterpret_cast<const bf16x8*>(&uc), fc);
   float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float2 x = __bfloat1622float2(ha[i]), y = __bfloat1622float2(hc[i]);
-    acc += x.x * y.x + x.y * y.y;
-  }
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    const int b = t / S, s = t % S;
+  for (int i = 0; i < 8; ++i) acc += fa[i] * fc[i];
+#pragma unroll
+  for (int m = 8; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+  float4* z = reinterpret_cast<float4*>(dq + off);
+  z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (sub == 0) {
+    const long long b = t / S, s = t % S;
     dvec[((size_t)b * H + h) * S + s] = acc;
   }
 }
@@ -743,14 +750,14 @@ at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Ten
   ensure_context();
   const int64_t T = B * S, HD = H * kD;
   auto dvec = at::empty({B, H, S}, lse.options());
-  auto dq = at::zeros({T, HD}, lse.options());
+  auto dq = at::empty({T, HD}, lse.options());  // zeroed by the dot kernel
   auto dqkv = at::empty({T, 3 * HD}, qkv.options());
   {
-    const int64_t warps = T * H;
+    const int64_t threads_total = T * H * 16;
     const int threads = 256;
-    attn_bwd_dot_kernel<<<(unsigned)((warps * 32 + threads - 1) / threads), threads, 0, cur_stream()>>>(
-        (const bf16*)dout.data_ptr(), (const bf16*)out.data_ptr(), (int)HD, dvec.data_ptr<float>(), (int)B,
-        (int)H, (int)S);
+    attn_bwd_dot_kernel<<<(unsigned)((threads_total + threads - 1) / threads), threads, 0, cur_stream()>>>(
+        (const bf16*)dout.data_ptr(), (const bf16*)out.data_ptr(), (int)HD, dvec.data_ptr<float>(),
+        dq.data_ptr<float>(), (int)B, (int)H, (int)S);
     MT_LAUNCH_CHECK();
   }
   const CUtensorMap tq = make_tma_2d(qkv.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3 * HD, T,
