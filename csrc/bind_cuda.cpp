@@ -53,6 +53,11 @@ int64_t attn_status(bool reset);
 void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::Tensor>& scale,
                   const c10::optional<at::Tensor>& amax, int64_t fmt);
 void fp8_amax(const at::Tensor& x, at::Tensor amax);
+void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
+                     at::Tensor counter, const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
+                     int64_t slot, int64_t parity, int64_t epoch, int64_t fmt);
+void fp8_amax_gather(const at::Tensor& table, at::Tensor amax, int64_t world, int64_t cap, int64_t parity,
+                     int64_t epoch);
 void fp8_scaling_update(at::Tensor hist, at::Tensor amax, at::Tensor scale, at::Tensor inv,
                         const at::Tensor& fmax, int64_t cursor, bool current);
 void fp8_dequantize(const at::Tensor& q, at::Tensor out, const at::Tensor& inv_scale, int64_t fmt);
@@ -128,6 +133,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_halo", &symm_halo);
   m.def("install_segv_handler", &install_segv_handler);
   m.def("launch_count", []() { return mtorus::launch_counter(); });
+  m.def("fp8_quantize_ar", &fp8_quantize_ar);
+  m.def("fp8_amax_gather", &fp8_amax_gather);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
   m.def("attn_status", &attn_status, py::arg("reset") = true);

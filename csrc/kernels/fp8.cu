@@ -71,6 +71,92 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(const bf16* __restric
   }
 }
 
+// ---------------------------------------------------------------- amax all-reduce (fused)
+// Data parallel: every rank quantises its own activations / gradients, so the
+// delayed-scaling amax of a tensor role is the max over ranks.  The quantise
+// kernel below publishes its rank's running amax for the slot into every peer's
+// symmetric table, from its last block (a per-slot arrival counter finds it):
+//     table[parity][me][slot] = (epoch << 32) | float_bits(amax)     (one u64 store)
+// At the end of the step, after a flag barrier, fp8_amax_gather takes the max
+// over ranks of the entries stamped with this step's epoch.  The table is
+// double-buffered by step parity, so a peer that already runs the next step
+// writes the other half.
+constexpr int kAmaxMaxPeers = 8;
+struct AmaxPeers {
+  uint64_t p[kAmaxMaxPeers];
+};
+
+template <int FMT>
+__global__ void __launch_bounds__(256) fp8_quantize_ar_kernel(const bf16* __restrict__ x,
+                                                              uint8_t* __restrict__ out,
+                                                              const float* __restrict__ scale,
+                                                              float* __restrict__ amax, size_t n,
+                                                              unsigned int* __restrict__ counter,
+                                                              AmaxPeers table, int me, int world, int cap,
+                                                              int slot, int parity, unsigned int epoch) {
+  __shared__ float red[32];
+  __shared__ bool last;
+  const float s = scale ? *scale : 1.f;
+  float m = 0.f;
+  const size_t nv = n / 16;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < nv;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float f[16];
+    unpack8(reinterpret_cast<const bf16x8*>(x)[2 * i], f);
+    unpack8(reinterpret_cast<const bf16x8*>(x)[2 * i + 1], f + 8);
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(f[4 * k]), fabsf(f[4 * k + 1])),
+                         fmaxf(fabsf(f[4 * k + 2]), fabsf(f[4 * k + 3]))));
+      const uint16_t lo = FMT == 0 ? cvt2_e4m3(f[4 * k] * s, f[4 * k + 1] * s)
+                                   : cvt2_e5m2(f[4 * k] * s, f[4 * k + 1] * s);
+      const uint16_t hi = FMT == 0 ? cvt2_e4m3(f[4 * k + 2] * s, f[4 * k + 3] * s)
+                                   : cvt2_e5m2(f[4 * k + 2] * s, f[4 * k + 3] * s);
+      w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  for (size_t i = nv * 16 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const float f = __bfloat162float(x[i]);
+    m = fmaxf(m, fabsf(f));
+    const uint16_t c = FMT == 0 ? cvt2_e4m3(f * s, 0.f) : cvt2_e5m2(f * s, 0.f);
+    out[i] = (uint8_t)(c & 0xFF);
+  }
+  m = block_max(m, red);
+  if (threadIdx.x == 0) {
+    atomic_max_pos(amax, m);
+    __threadfence();
+    last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch on this slot
+  if (threadIdx.x < world) {
+    const float a = *reinterpret_cast<volatile float*>(amax);
+    const unsigned long long v = ((unsigned long long)epoch << 32) | __float_as_uint(a);
+    unsigned long long* t = reinterpret_cast<unsigned long long*>(table.p[threadIdx.x]) +
+                            ((size_t)parity * world + me) * cap + slot;
+    *reinterpret_cast<volatile unsigned long long*>(t) = v;
+    __threadfence_system();
+  }
+}
+
+// amax[s] = max over ranks r of table[parity][r][s] entries stamped with `epoch`.
+__global__ void fp8_amax_gather_kernel(const unsigned long long* __restrict__ table, float* __restrict__ amax,
+                                       int slots, int world, int cap, int parity, unsigned int epoch) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= slots) return;
+  float m = amax[s];
+  for (int r = 0; r < world; ++r) {
+    const unsigned long long v =
+        *reinterpret_cast<const volatile unsigned long long*>(table + ((size_t)parity * world + r) * cap + s);
+    if ((unsigned int)(v >> 32) == epoch) m = fmaxf(m, __uint_as_float((unsigned int)(v & 0xffffffffu)));
+  }
+  amax[s] = m;
+}
+
 __global__ void __launch_bounds__(256) amax_kernel(const bf16* __restrict__ x, float* __restrict__ amax,
                                                    size_t n) {
   __shared__ float red[32];
@@ -172,6 +258,47 @@ void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::T
     fp8_quantize_kernel<0><<<q_grid(n, 16), 256, 0, cur_stream()>>>(xp, op, sp, ap, n);
   else
     fp8_quantize_kernel<1><<<q_grid(n, 16), 256, 0, cur_stream()>>>(xp, op, sp, ap, n);
+  MT_LAUNCH_CHECK();
+}
+
+// Quantise with the amax all-reduce of fused path (b): see fp8_quantize_ar_kernel.
+void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
+                     at::Tensor counter, const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
+                     int64_t slot, int64_t parity, int64_t epoch, int64_t fmt) {
+  MT_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "fp8_quantize_ar: contiguous bf16 input");
+  MT_CHECK(out.element_size() == 1 && out.is_contiguous() && out.numel() == x.numel(), "fp8_quantize_ar: out");
+  MT_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+               reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+           "fp8_quantize_ar: 16-byte aligned buffers");
+  MT_CHECK(counter.scalar_type() == at::kInt && counter.numel() >= 1, "fp8_quantize_ar: int32 counter");
+  const int world = (int)table_ptrs.size();
+  MT_CHECK(world >= 1 && world <= kAmaxMaxPeers, "fp8_quantize_ar: 1..8 ranks");
+  AmaxPeers t{};
+  for (int i = 0; i < world; ++i) t.p[i] = (uint64_t)table_ptrs[i];
+  const size_t n = x.numel();
+  if (n == 0) return;
+  const auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto* op = reinterpret_cast<uint8_t*>(out.data_ptr());
+  auto* cp = reinterpret_cast<unsigned int*>(counter.data_ptr());
+  if (fmt == 0)
+    fp8_quantize_ar_kernel<0><<<q_grid(n, 16), 256, 0, cur_stream()>>>(
+        xp, op, scale.data_ptr<float>(), amax.data_ptr<float>(), n, cp, t, (int)me, world, (int)cap, (int)slot,
+        (int)parity, (unsigned int)epoch);
+  else
+    fp8_quantize_ar_kernel<1><<<q_grid(n, 16), 256, 0, cur_stream()>>>(
+        xp, op, scale.data_ptr<float>(), amax.data_ptr<float>(), n, cp, t, (int)me, world, (int)cap, (int)slot,
+        (int)parity, (unsigned int)epoch);
+  MT_LAUNCH_CHECK();
+}
+
+void fp8_amax_gather(const at::Tensor& table, at::Tensor amax, int64_t world, int64_t cap, int64_t parity,
+                     int64_t epoch) {
+  const int slots = amax.numel();
+  if (slots == 0) return;
+  MT_CHECK(table.element_size() == 8 && table.numel() >= 2 * world * cap, "fp8_amax_gather: table");
+  fp8_amax_gather_kernel<<<(slots + 127) / 128, 128, 0, cur_stream()>>>(
+      reinterpret_cast<const unsigned long long*>(table.data_ptr()), amax.data_ptr<float>(), slots, (int)world,
+      (int)cap, (int)parity, (unsigned int)epoch);
   MT_LAUNCH_CHECK();
 }
 

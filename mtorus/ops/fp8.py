@@ -63,6 +63,52 @@ def gemm_fp8(a, a_fmt: int, b, b_fmt: int, out=None, *, a_mn=False, b_mn=False, 
     return out
 
 
+class NcclAmaxSync:
+    """Cross-rank amax max for delayed scaling through one NCCL all-reduce (MAX) of
+    the step's amax vector before the scales roll (the baseline of the fused path)."""
+
+    def __init__(self, group=None):
+        self.group = group
+
+    def quantize(self, x, out, scale, amax, slot, fmt):
+        quantize(x, fmt, scale, amax, out=out)
+
+    def reduce(self, amax: torch.Tensor) -> None:
+        import torch.distributed as dist
+
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+
+
+class SymmAmaxSync:
+    """Fused path (b): the amax all-reduce runs inside the quantise kernels.  The
+    last block of each quantise launch stores the rank's running amax for that
+    tensor role into every peer's table (symmetric memory, NVLink stores, tagged
+    with the step's epoch, double-buffered by step parity); at the end of the step
+    a flag barrier and one gather kernel take the max over ranks.  No collective
+    library call and no extra pass over the data."""
+
+    def __init__(self, device, capacity: int, group=None):
+        from ..parallel.symm import SymmBuffer, SymmContext
+
+        self.ctx = SymmContext(device, group, num_slots=4)
+        self.me, self.world = self.ctx.rank, self.ctx.world
+        self.cap = capacity
+        self.table = SymmBuffer(2 * self.world * capacity, torch.int64, device, group)
+        self.counters = torch.zeros(capacity, dtype=torch.int32, device=device)
+        self.epoch = 1
+        self.table.barrier()
+
+    def quantize(self, x, out, scale, amax, slot, fmt):
+        _cuda().fp8_quantize_ar(x.contiguous(), out, scale, amax, self.counters[slot:slot + 1], self.table.ptrs,
+                                self.me, self.cap, slot, self.epoch & 1, self.epoch, int(fmt))
+
+    def reduce(self, amax: torch.Tensor) -> None:
+        # every rank has published this step's amaxes (its quantise kernels precede the barrier)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 0, self.epoch, 24)
+        _cuda().fp8_amax_gather(self.table.tensor, amax, self.world, self.cap, self.epoch & 1, self.epoch)
+        self.epoch += 1
+
+
 class Fp8State:
     """Amax histories, scales and inverse scales of every FP8 tensor role of a model."""
 
@@ -82,6 +128,21 @@ class Fp8State:
         self.cursor = 0
         self.first_step = True
         self._measured = set()  # slots whose first-step scale is already set
+        self.sync = None  # cross-rank amax reduction (data parallel), see set_amax_sync
+
+    def set_amax_sync(self, sync) -> None:
+        """Make every amax the max over the data-parallel ranks (``NcclAmaxSync`` or
+        ``SymmAmaxSync``); all ranks must quantise the same roles each step."""
+        self.sync = sync
+
+    def _quantize(self, x, fmt, s, out):
+        sl = slice(s, s + 1)
+        if self.sync is not None:
+            if out is None:
+                out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+            self.sync.quantize(x, out, self.scale[sl], self.amax[sl], s, fmt)
+            return out
+        return quantize(x, fmt, self.scale[sl], self.amax[sl], out=out)
 
     def slot(self, name: str, fmt: int) -> int:
         s = self.names.get(name)
@@ -99,7 +160,7 @@ class Fp8State:
         s = self.slot(name, fmt)
         sl = slice(s, s + 1)
         self._first_step_scale(x, s)
-        q = quantize(x, fmt, self.scale[sl], self.amax[sl])
+        q = self._quantize(x, fmt, s, None)
         # the inverse scale stays valid until end_step(), i.e. through this step's backward
         return q, self.inv[sl]
 
@@ -107,7 +168,7 @@ class Fp8State:
         s = self.slot(name, fmt)
         sl = slice(s, s + 1)
         self._first_step_scale(x, s)
-        quantize(x, fmt, self.scale[sl], self.amax[sl], out=out)
+        self._quantize(x, fmt, s, out)
         return out, self.inv[sl]
 
     def _first_step_scale(self, x: torch.Tensor, s: int) -> None:
@@ -125,6 +186,8 @@ class Fp8State:
     def end_step(self) -> None:
         """Roll all histories (delayed scaling): the next step's scales come from them."""
         n = len(self.fmts)
+        if n and self.sync is not None:
+            self.sync.reduce(self.amax[:n])
         if n:
             _cuda().fp8_scaling_update(self.hist[:n], self.amax[:n], self.scale[:n], self.inv[:n], self.fmax[:n],
                                        self.cursor, False)
@@ -147,4 +210,5 @@ class Fp8State:
         self.first_step = False
 
 
-__all__ = ["E4M3", "E5M2", "FMT_MAX", "quantize", "dequantize", "quantize_blocks", "gemm_fp8", "Fp8State"]
+__all__ = ["E4M3", "E5M2", "FMT_MAX", "quantize", "dequantize", "quantize_blocks", "gemm_fp8", "Fp8State",
+           "NcclAmaxSync", "SymmAmaxSync"]

@@ -48,7 +48,15 @@ class GptTrainer:
         ls = loss_scale or DeviceLossScaleConfig()
         self.fp8 = fp8
         if fp8:
-            self.model.enable_fp8(fp8_history)
+            st = self.model.enable_fp8(fp8_history)
+            if self.dp == "symm":
+                from ..ops.fp8 import SymmAmaxSync
+
+                st.set_amax_sync(SymmAmaxSync(self.device, st.cap, dp_group))
+            elif self.dp == "nccl":
+                from ..ops.fp8 import NcclAmaxSync
+
+                st.set_amax_sync(NcclAmaxSync(dp_group))
         if self.dp == "symm":
             from ..parallel.symm import SymmBucketReducer, ZeroAdam
 

@@ -155,7 +155,11 @@ class PipelineTrainer:
         self.flat = self.model.flatten(self.device)
         self.fp8 = fp8
         if fp8:
-            self.model.enable_fp8(fp8_history)
+            st = self.model.enable_fp8(fp8_history)
+            if dp > 1:
+                from ..ops.fp8 import NcclAmaxSync
+
+                st.set_amax_sync(NcclAmaxSync(self.dp_group))
         self.opt = FusedAdam(self.flat, lr=lr, max_grad_norm=max_grad_norm,
                              loss_scale=loss_scale or DeviceLossScaleConfig())
         self.reducer = None

@@ -154,3 +154,50 @@ def test_pipeline_trainer_matches_single_gpu(sched, ckpt):
             assert err < 5e-2, (r, name, float(err))
             checked += 1
     assert checked == len(ref_grads)
+
+
+def _amax_body(rank, world, kind):
+    import torch
+
+    from mtorus.ops import fp8 as F8
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    st = F8.Fp8State(dev, history=4, capacity=64)
+    st.set_amax_sync(F8.SymmAmaxSync(dev, st.cap) if kind == "symm" else F8.NcclAmaxSync())
+    out = {"scale": [], "codes_match": []}
+    for step in range(3):
+        torch.manual_seed(100 * step + rank)
+        xs = {"a": (torch.randn(4096, 256) * (rank + 1) * (step + 1)).to(dev),
+              "b": (torch.randn(1000, 8) * (2.0 - rank)).to(dev)}
+        for name, x in xs.items():
+            x = x.bfloat16()
+            q, _ = st.quantize(x, name, F8.E4M3 if name == "a" else F8.E5M2)
+            s = st.names[name]
+            ref = F8.quantize(x, st.fmts[s], st.scale[s:s + 1])
+            out["codes_match"].append(bool(torch.equal(q, ref)))
+        st.end_step()
+        out["scale"].append(st.scale[:2].cpu().clone())
+    torch.cuda.synchronize()
+    return out
+
+
+@needs2
+@pytest.mark.parametrize("kind", ["symm", "nccl"])
+def test_fp8_amax_allreduce_2gpu(kind):
+    """Delayed-scaling amax reduced over ranks: both ranks end every step with the
+    same scales, equal to fmax / (max over ranks and history of amax); the fused
+    quantise kernel writes the same codes as the plain one."""
+    res = run_dist(_amax_body, 2, (kind,), backend="nccl")
+    for o in res:
+        assert all(o["codes_match"])
+    for step in range(3):
+        assert torch.equal(res[0]["scale"][step], res[1]["scale"][step])
+    # step 3 (index 2): role "a" amax = max over ranks = 2 * 3 * max|randn|; scale = 416 / that (history 4)
+    a_amax = [0.0, 0.0]
+    for step in range(3):
+        for r in range(2):
+            torch.manual_seed(100 * step + r)
+            xa = (torch.randn(4096, 256) * (r + 1) * (step + 1)).bfloat16().float()
+            a_amax[0] = max(a_amax[0], float(xa.abs().max()))
+    assert abs(float(res[0]["scale"][2][0]) - 416.0 / a_amax[0]) < 1e-3 * 416.0 / a_amax[0]
