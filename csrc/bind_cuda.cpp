@@ -83,6 +83,8 @@ void symm_broadcast(const std::vector<int64_t>& bufs, int64_t root, int64_t byte
 void symm_halo(int64_t src, const std::vector<int64_t>& recv, const at::Tensor& nbr_rank,
                const at::Tensor& nbr_slot, int64_t bytes, int64_t ctas);
 void install_segv_handler();
+void wait_flag(const at::Tensor& flag, int64_t target, double limit_ms, at::Tensor status, int64_t code,
+               at::Tensor waited);
 }  // namespace mtorus
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -132,6 +134,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_broadcast", &symm_broadcast);
   m.def("symm_halo", &symm_halo);
   m.def("install_segv_handler", &install_segv_handler);
+  m.def("wait_flag", &wait_flag);
   m.def("launch_count", []() { return mtorus::launch_counter(); });
   m.def("fp8_quantize_ar", &fp8_quantize_ar);
   m.def("fp8_amax_gather", &fp8_amax_gather);

@@ -195,9 +195,13 @@ class Fp8State:
         self.first_step = False
 
     def state_dict(self) -> dict:
+        """Format, scale, amax history and cursor of every tensor role (the
+        reference's DelayedScaling{amax_history, history_length, cursor} per role)."""
         n = len(self.fmts)
         return {"names": dict(self.names), "fmts": list(self.fmts), "hist": self.hist[:n].cpu(),
-                "scale": self.scale[:n].cpu(), "cursor": self.cursor, "history": self.history}
+                "scale": self.scale[:n].cpu(), "inv": self.inv[:n].cpu(), "amax": self.amax[:n].cpu(),
+                "cursor": self.cursor, "history": self.history, "first_step": self.first_step,
+                "measured": sorted(self._measured)}
 
     def load_state_dict(self, sd: dict) -> None:
         for name, fmt in zip(sorted(sd["names"], key=sd["names"].get), sd["fmts"]):
@@ -205,9 +209,12 @@ class Fp8State:
         n = len(sd["fmts"])
         self.hist[:n] = sd["hist"].to(self.device)
         self.scale[:n] = sd["scale"].to(self.device)
-        self.inv[:n] = 1.0 / self.scale[:n]
+        self.inv[:n] = sd["inv"].to(self.device) if "inv" in sd else 1.0 / self.scale[:n]
+        if "amax" in sd:
+            self.amax[:n] = sd["amax"].to(self.device)
         self.cursor = sd["cursor"]
-        self.first_step = False
+        self.first_step = sd.get("first_step", False)
+        self._measured = set(sd.get("measured", []))
 
 
 __all__ = ["E4M3", "E5M2", "FMT_MAX", "quantize", "dequantize", "quantize_blocks", "gemm_fp8", "Fp8State",

@@ -82,6 +82,38 @@ class GptTrainer:
             return self.lr * (self.global_step + 1) / self.warmup_steps
         return self.lr
 
+    def step_device_accum(self, ids_list, targets_list) -> torch.Tensor:
+        """One optimizer step over several micro-batches (gradient accumulation:
+        the reference's GradientAccumulator, crates/mt-training/src/accumulator.rs).
+        The first micro-batch's backward overwrites ``main_grad``, the others add
+        into it in the wgrad epilogues; the data-parallel reduction runs during the
+        last backward.  Returns the mean loss as a device scalar."""
+        k = len(ids_list)
+        if k == 1:
+            return self.step_device(ids_list[0], targets_list[0])
+        if self.fp8:
+            self.model.refresh_fp8_weights()
+        if hasattr(self.reducer, "begin_step"):
+            self.reducer.begin_step()
+        gs = self.opt.loss_scale_tensor / k
+        total = None
+        for i, (ids, tgt) in enumerate(zip(ids_list, targets_list)):
+            FusedGradState.accumulate = i > 0
+            last = i == k - 1
+            FusedGradState.grad_ready_hook = self.reducer.on_ready if (last and self.reducer is not None) else None
+            loss = self.model.fused_loss(ids, tgt, grad_scale=gs)
+            loss.backward()
+            total = loss.detach() if total is None else total + loss.detach()
+        FusedGradState.accumulate = False
+        FusedGradState.grad_ready_hook = None
+        if self.reducer is not None:
+            self.reducer.finish()
+        self.opt.step(self.current_lr())
+        if self.fp8:
+            self.model.fp8_state.end_step()
+        self.global_step += 1
+        return total / k
+
     def step_device(self, ids: torch.Tensor, targets: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """One full training step on device tensors; returns the device loss (no sync).
 
@@ -107,6 +139,31 @@ class GptTrainer:
             self.model.fp8_state.end_step()
         self.global_step += 1
         return loss.detach()
+
+    # ---------------------------------------------------------------- checkpoints
+    def state_dict(self) -> dict:
+        """Everything this rank needs to resume bit for bit (see mtorus.training.checkpoint)."""
+        opt = self.opt
+        d = {"global_step": self.global_step, "dp": self.dp, "fp8": self.fp8,
+             "master": self.flat.master.detach().cpu(), "w16": self.flat.w16.detach().cpu(),
+             "opt": {"m": opt.m.detach().cpu(), "v": opt.v.detach().cpu(), "state": opt.state.detach().cpu()}}
+        if self.fp8:
+            d["fp8_state"] = self.model.fp8_state.state_dict()
+        return d
+
+    @torch.no_grad()
+    def load_state_dict(self, d: dict) -> None:
+        if d["dp"] != self.dp or bool(d["fp8"]) != bool(self.fp8):
+            raise ValueError(f"checkpoint was written with dp={d['dp']} fp8={d['fp8']}, "
+                             f"this trainer has dp={self.dp} fp8={self.fp8}")
+        self.flat.master.copy_(d["master"].to(self.device))
+        self.flat.w16.copy_(d["w16"].to(self.device))
+        self.opt.m.copy_(d["opt"]["m"].to(self.device))
+        self.opt.v.copy_(d["opt"]["v"].to(self.device))
+        self.opt.state.copy_(d["opt"]["state"].to(self.device))
+        if self.fp8:
+            self.model.fp8_state.load_state_dict(d["fp8_state"])
+        self.global_step = int(d["global_step"])
 
     def _local_optimizer(self) -> FusedAdam:
         if getattr(self, "_local_opt", None) is None:

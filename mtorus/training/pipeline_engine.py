@@ -203,6 +203,30 @@ class PipelineTrainer:
             v.copy_(sd[self.global_name(k)].to(v.device, v.dtype))
         self.flat.sync_w16()
 
+    def state_dict(self) -> dict:
+        """This rank's stage: weights, Adam state, FP8 state, step (see mtorus.training.checkpoint)."""
+        d = {"global_step": self.global_step, "stage": self.stage, "layers": self.layers, "fp8": self.fp8,
+             "master": self.flat.master.detach().cpu(), "w16": self.flat.w16.detach().cpu(),
+             "opt": {"m": self.opt.m.detach().cpu(), "v": self.opt.v.detach().cpu(),
+                     "state": self.opt.state.detach().cpu()}}
+        if self.fp8:
+            d["fp8_state"] = self.model.fp8_state.state_dict()
+        return d
+
+    @torch.no_grad()
+    def load_state_dict(self, d: dict) -> None:
+        if d["stage"] != self.stage or tuple(d["layers"]) != tuple(self.layers):
+            raise ValueError(f"checkpoint holds stage {d['stage']} layers {d['layers']}, "
+                             f"this rank runs stage {self.stage} layers {self.layers}")
+        self.flat.master.copy_(d["master"].to(self.device))
+        self.flat.w16.copy_(d["w16"].to(self.device))
+        self.opt.m.copy_(d["opt"]["m"].to(self.device))
+        self.opt.v.copy_(d["opt"]["v"].to(self.device))
+        self.opt.state.copy_(d["opt"]["state"].to(self.device))
+        if self.fp8:
+            self.model.fp8_state.load_state_dict(d["fp8_state"])
+        self.global_step = int(d["global_step"])
+
     def ideal_bubble_fraction(self) -> float:
         """(S-1)/(M+S-1) for both schedules (the reference's formula)."""
         return ideal_bubble_fraction(self.pp, self.M)

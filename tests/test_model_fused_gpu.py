@@ -64,3 +64,67 @@ def test_fp8_training_tracks_bf16():
     a, b = runs[False], runs[True]
     assert abs(a[0] - b[0]) < 0.05 * a[0]
     assert b[-1] < b[0] - 1.0 and abs(a[-1] - b[-1]) < 0.15 * a[-1], (a, b)
+
+
+def test_checkpoint_resume_is_bitwise(tmp_path):
+    """Train 3 steps, checkpoint, train 3 more.  A fresh trainer restored from the
+    checkpoint holds exactly the saved state (weights, Adam moments, loss scale,
+    FP8 scales and histories) and continues along the same trajectory; the steps
+    themselves match up to the fp32 summation order of the atomic reductions
+    (attention dQ, embedding gradients), which varies run to run."""
+    from mtorus.models.gpt import GptConfig
+    from mtorus.training.checkpoint import load_checkpoint, save_checkpoint
+    from mtorus.training.config import TrainingConfig
+    from mtorus.training.engine import GptTrainer
+
+    cfg = GptConfig(vocab_size=512, d_model=256, num_layers=2, num_heads=2, d_ff=1024, max_seq_len=128,
+                    dropout=0.0)
+    g = torch.Generator().manual_seed(3)
+    batches = []
+    for _ in range(6):
+        t = torch.randint(0, cfg.vocab_size, (2, 129), generator=g)
+        batches.append((t[:, :-1].contiguous().pin_memory(), t[:, 1:].contiguous().pin_memory()))
+    a = GptTrainer(cfg, device="cuda", lr=1e-3, init="normal", seed=0, fp8=True)
+    for x, y in batches[:3]:
+        a.train_step(x, y)
+    tc = TrainingConfig()
+    save_checkpoint(str(tmp_path / "ck"), a, tc)
+    la = [a.train_step(x, y) for x, y in batches[3:]]
+    b = GptTrainer(cfg, device="cuda", lr=1e-3, init="normal", seed=123, fp8=True)
+    cfg_back = load_checkpoint(str(tmp_path / "ck"), b)
+    assert cfg_back == tc and b.global_step == 3
+    saved = torch.load(str(tmp_path / "ck" / "rank0.pt"), weights_only=False)
+    got = b.state_dict()
+    for k in ("master", "w16"):
+        assert torch.equal(got[k], saved[k]), k
+    for k in ("m", "v", "state"):
+        assert torch.equal(got["opt"][k], saved["opt"][k]), k
+    for k in ("hist", "scale", "inv"):
+        assert torch.equal(got["fp8_state"][k], saved["fp8_state"][k]), k
+    lb = [b.train_step(x, y) for x, y in batches[3:]]
+    assert all(abs(p - q) < 1e-3 * abs(p) for p, q in zip(la, lb)), (la, lb)
+    assert torch.allclose(a.flat.master, b.flat.master, rtol=1e-3, atol=1e-5)
+
+
+def test_train_gpu_cli_accumulation_metrics_checkpoint(tmp_path):
+    """The GPU training entrypoint: 2 micro-batches per step, JSONL metrics,
+    a checkpoint at step 2, and a resumed run that continues from it."""
+    import importlib.util
+    import json
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "examples", "gpt1b",
+                        "train_gpu.py")
+    spec = importlib.util.spec_from_file_location("train_gpu", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    m = str(tmp_path / "m.jsonl")
+    common = ["--model", "small", "--seq", "128", "--set", "batch_size=4", "--set", "micro_batch_size=2",
+              "--set", "accumulation_steps=2", "--set", "checkpoint_interval=2", "--set", "log_interval=1"]
+    assert mod.main(common + ["--steps", "2", "--metrics", m, "--checkpoint-dir", str(tmp_path / "ck")]) == 0
+    recs = [json.loads(x) for x in open(m)]
+    assert [r["step"] for r in recs] == [1, 2] and all(5.0 < r["loss"] < 10.0 for r in recs)
+    assert os.path.exists(tmp_path / "ck" / "step00000002" / "rank0.pt")
+    m2 = str(tmp_path / "m2.jsonl")
+    assert mod.main(common + ["--steps", "1", "--metrics", m2, "--resume", str(tmp_path / "ck" / "step00000002")]) == 0
+    assert [json.loads(x)["step"] for x in open(m2)] == [3]

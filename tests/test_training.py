@@ -318,3 +318,63 @@ def test_gpt1b_cpu_example_runs_dp_pp_fp8(capsys):
     summary = json.loads(out[-1])
     assert summary["overflows"] == 0 and len(summary["loss_curve"]) == 2
     assert all(6.0 < v < 8.0 for v in summary["loss_curve"])
+
+
+def test_checkpoint_files_roundtrip_cpu(tmp_path):
+    """save / load on a host-only trainer: config TOML, per-rank file, meta, RNG state."""
+    import json
+
+    import torch
+
+    from mtorus.training.checkpoint import load_checkpoint, maybe_save, save_checkpoint
+    from mtorus.training.config import TrainingConfig
+
+    class Toy:
+        def __init__(self):
+            self.w = torch.zeros(4)
+            self.global_step = 0
+
+        def state_dict(self):
+            return {"w": self.w.clone(), "global_step": self.global_step}
+
+        def load_state_dict(self, d):
+            self.w = d["w"].clone()
+            self.global_step = d["global_step"]
+
+    t = Toy()
+    t.w += 3.0
+    t.global_step = 7
+    cfg = TrainingConfig(checkpoint_interval=7)
+    torch.manual_seed(5)
+    p = maybe_save(str(tmp_path), t, cfg)
+    assert p is not None and p.endswith("rank0.pt")
+    r1 = torch.rand(3)
+    u = Toy()
+    back = load_checkpoint(str(tmp_path / "step00000007"), u)
+    assert back == cfg and u.global_step == 7 and torch.equal(u.w, torch.full((4,), 3.0))
+    assert torch.equal(torch.rand(3), r1)  # RNG restored to the save point
+    meta = json.load(open(tmp_path / "step00000007" / "meta.json"))
+    assert meta == {"world_size": 1, "global_step": 7, "files": ["rank0.pt"]}
+    t.global_step = 8
+    assert maybe_save(str(tmp_path), t, cfg) is None
+    save_checkpoint(str(tmp_path / "x"), t)
+
+
+def test_train_cli_set_overrides():
+    import importlib.util
+    import os
+
+    from mtorus.training.config import PipelineScheduleConfig, TrainingConfig
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "examples", "gpt1b",
+                        "train_gpu.py")
+    spec = importlib.util.spec_from_file_location("train_gpu", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    d = mod.parse_set(["learning_rate=3e-4", "pipeline_schedule={OneF1B={num_stages=4}}",
+                       "mixed_precision.scaling_strategy=\"Dynamic\"", "checkpoint_interval=100"],
+                      TrainingConfig().to_dict())
+    tc = TrainingConfig.from_dict(d)
+    assert tc.learning_rate == 3e-4 and tc.checkpoint_interval == 100
+    assert tc.pipeline_schedule == PipelineScheduleConfig.OneF1B(4)
+    assert tc.mixed_precision.to_dict()["scaling_strategy"] == "Dynamic"
