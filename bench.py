@@ -112,8 +112,10 @@ def main() -> int:
     lc0 = ext.launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
+    h0 = time.perf_counter()
     for i in range(args.steps):
         loss = trainer.step_device(dev_ids[i % nb], dev_tgt[i % nb])
+    host_ms = (time.perf_counter() - h0) * 1000.0
     t1.record()
     t1.synchronize()
     lc1 = ext.launch_count()
@@ -195,6 +197,7 @@ def main() -> int:
             "compute_only_ms_per_step": round(comp_ms / args.steps, 3) if comp_ms is not None else round(ms_step, 3),
             "how": "device-timed step minus the same step with no data-parallel communication (max over ranks)",
         },
+        "host_enqueue_ms_per_step": round(host_ms / args.steps, 3),
         "clocks": clocks,
         "gpu_launches": int(lc1 - lc0),
         "final_loss": round(last_loss, 4),

@@ -58,6 +58,10 @@ void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scal
                      int64_t slot, int64_t parity, int64_t epoch, int64_t fmt);
 void fp8_amax_gather(const at::Tensor& table, at::Tensor amax, int64_t world, int64_t cap, int64_t parity,
                      int64_t epoch);
+void fp8_quantize_colsum(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
+                         at::Tensor colsum, bool accumulate, const c10::optional<at::Tensor>& counter,
+                         const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap, int64_t slot,
+                         int64_t parity, int64_t epoch, int64_t fmt);
 void fp8_scaling_update(at::Tensor hist, at::Tensor amax, at::Tensor scale, at::Tensor inv,
                         const at::Tensor& fmax, int64_t cursor, bool current);
 void fp8_dequantize(const at::Tensor& q, at::Tensor out, const at::Tensor& inv_scale, int64_t fmt);
@@ -138,6 +142,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", []() { return mtorus::launch_counter(); });
   m.def("fp8_quantize_ar", &fp8_quantize_ar);
   m.def("fp8_amax_gather", &fp8_amax_gather);
+  m.def("fp8_quantize_colsum", &fp8_quantize_colsum);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
   m.def("attn_status", &attn_status, py::arg("reset") = true);

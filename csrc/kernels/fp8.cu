@@ -86,6 +86,87 @@ struct AmaxPeers {
   uint64_t p[kAmaxMaxPeers];
 };
 
+// Block amax -> the slot's running amax (atomic); with a counter, the grid's last
+// block then stores the slot's amax into every peer's table (see above).
+__device__ __forceinline__ void publish_amax(float m, float* amax, unsigned int* counter, const AmaxPeers& table,
+                                             int me, int world, int cap, int slot, int parity, unsigned int epoch,
+                                             bool* last) {
+  if (threadIdx.x == 0) {
+    atomic_max_pos(amax, m);
+    if (counter) {
+      __threadfence();
+      *last = atomicAdd(counter, 1u) == gridDim.x * gridDim.y - 1;
+    }
+  }
+  if (!counter) return;
+  __syncthreads();
+  if (!*last) return;
+  if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch on this slot
+  if (threadIdx.x < world) {
+    const float a = *reinterpret_cast<volatile float*>(amax);
+    const unsigned long long v = ((unsigned long long)epoch << 32) | __float_as_uint(a);
+    unsigned long long* t = reinterpret_cast<unsigned long long*>(table.p[threadIdx.x]) +
+                            ((size_t)parity * world + me) * cap + slot;
+    *reinterpret_cast<volatile unsigned long long*>(t) = v;
+    __threadfence_system();
+  }
+}
+
+// Quantise a [rows, F] bf16 gradient and add its column sums into `colsum` (the
+// bias gradient) in the same pass: blocks of 32 column groups of 8 x 8 row lanes,
+// 16-byte loads, 8-byte code stores, per-block column partials in shared memory
+// and one atomic per column.  Amax / all-reduce publication as above.
+template <int FMT>
+__global__ void __launch_bounds__(256) fp8_quantize_colsum_kernel(
+    const bf16* __restrict__ x, uint8_t* __restrict__ out, const float* __restrict__ scale,
+    float* __restrict__ amax, float* __restrict__ colsum, int rows, int F, int rows_per_block,
+    unsigned int* __restrict__ counter, AmaxPeers table, int me, int world, int cap, int slot, int parity,
+    unsigned int epoch) {
+  __shared__ float red[8][257];
+  __shared__ float redm[32];
+  __shared__ bool last;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 256 + tx * 8;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  const float s = *scale;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float m = 0.f;
+  if (c0 < F) {
+    for (int r = r0 + ty; r < r1; r += 8) {
+      float f[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(x + (size_t)r * F + c0), f);
+      uint32_t w[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[4 * k + j] += f[4 * k + j];
+          m = fmaxf(m, fabsf(f[4 * k + j]));
+        }
+        const uint16_t lo = FMT == 0 ? cvt2_e4m3(f[4 * k] * s, f[4 * k + 1] * s)
+                                     : cvt2_e5m2(f[4 * k] * s, f[4 * k + 1] * s);
+        const uint16_t hi = FMT == 0 ? cvt2_e4m3(f[4 * k + 2] * s, f[4 * k + 3] * s)
+                                     : cvt2_e5m2(f[4 * k + 2] * s, f[4 * k + 3] * s);
+        w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+      }
+      *reinterpret_cast<uint2*>(out + (size_t)r * F + c0) = make_uint2(w[0], w[1]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) red[ty][tx * 8 + k] = acc[k];
+  __syncthreads();
+  const int col = threadIdx.x;
+  if (blockIdx.x * 256 + col < F) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][col];
+    atomicAdd(colsum + blockIdx.x * 256 + col, t);
+  }
+  m = block_max(m, redm);
+  publish_amax(m, amax, counter, table, me, world, cap, slot, parity, epoch, &last);
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(256) fp8_quantize_ar_kernel(const bf16* __restrict__ x,
                                                               uint8_t* __restrict__ out,
@@ -125,22 +206,7 @@ __global__ void __launch_bounds__(256) fp8_quantize_ar_kernel(const bf16* __rest
     out[i] = (uint8_t)(c & 0xFF);
   }
   m = block_max(m, red);
-  if (threadIdx.x == 0) {
-    atomic_max_pos(amax, m);
-    __threadfence();
-    last = atomicAdd(counter, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!last) return;
-  if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch on this slot
-  if (threadIdx.x < world) {
-    const float a = *reinterpret_cast<volatile float*>(amax);
-    const unsigned long long v = ((unsigned long long)epoch << 32) | __float_as_uint(a);
-    unsigned long long* t = reinterpret_cast<unsigned long long*>(table.p[threadIdx.x]) +
-                            ((size_t)parity * world + me) * cap + slot;
-    *reinterpret_cast<volatile unsigned long long*>(t) = v;
-    __threadfence_system();
-  }
+  publish_amax(m, amax, counter, table, me, world, cap, slot, parity, epoch, &last);
 }
 
 // amax[s] = max over ranks r of table[parity][r][s] entries stamped with `epoch`.
@@ -288,6 +354,46 @@ void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scal
     fp8_quantize_ar_kernel<1><<<q_grid(n, 16), 256, 0, cur_stream()>>>(
         xp, op, scale.data_ptr<float>(), amax.data_ptr<float>(), n, cp, t, (int)me, world, (int)cap, (int)slot,
         (int)parity, (unsigned int)epoch);
+  MT_LAUNCH_CHECK();
+}
+
+// Quantise a 2-D bf16 gradient and (+)= its column sums into `colsum` (fp32 [F]).
+// table_ptrs empty: local amax only; otherwise the amax all-reduce of path (b).
+void fp8_quantize_colsum(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
+                         at::Tensor colsum, bool accumulate, const c10::optional<at::Tensor>& counter,
+                         const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap, int64_t slot,
+                         int64_t parity, int64_t epoch, int64_t fmt) {
+  MT_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() >= 1, "fp8_quantize_colsum: bf16 x");
+  const int F = x.size(-1);
+  const int rows = x.numel() / std::max(F, 1);
+  MT_CHECK(F % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+               reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+           "fp8_quantize_colsum: F % 8 == 0 and 16-byte aligned buffers");
+  MT_CHECK(out.element_size() == 1 && out.numel() == x.numel() && out.is_contiguous(), "fp8_quantize_colsum: out");
+  MT_CHECK(colsum.scalar_type() == at::kFloat && colsum.numel() == F && colsum.is_contiguous(),
+           "fp8_quantize_colsum: fp32 colsum [F]");
+  if (!accumulate) colsum.zero_();
+  if (rows == 0) return;
+  const int world = (int)table_ptrs.size();
+  MT_CHECK(world <= kAmaxMaxPeers && (world == 0 || counter.has_value()), "fp8_quantize_colsum: peers");
+  AmaxPeers t{};
+  for (int i = 0; i < world; ++i) t.p[i] = (uint64_t)table_ptrs[i];
+  unsigned int* cp = world ? reinterpret_cast<unsigned int*>(counter->data_ptr()) : nullptr;
+  const int col_blocks = (F + 255) / 256;
+  int row_blocks = std::max(1, std::min((rows + 63) / 64, (num_sms() * 8 + col_blocks - 1) / col_blocks));
+  const int rpb = (rows + row_blocks - 1) / row_blocks;
+  row_blocks = (rows + rpb - 1) / rpb;
+  const dim3 grid(col_blocks, row_blocks);
+  const auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto* op = reinterpret_cast<uint8_t*>(out.data_ptr());
+  if (fmt == 0)
+    fp8_quantize_colsum_kernel<0><<<grid, 256, 0, cur_stream()>>>(
+        xp, op, scale.data_ptr<float>(), amax.data_ptr<float>(), colsum.data_ptr<float>(), rows, F, rpb, cp, t,
+        (int)me, world, (int)cap, (int)slot, (int)parity, (unsigned int)epoch);
+  else
+    fp8_quantize_colsum_kernel<1><<<grid, 256, 0, cur_stream()>>>(
+        xp, op, scale.data_ptr<float>(), amax.data_ptr<float>(), colsum.data_ptr<float>(), rows, F, rpb, cp, t,
+        (int)me, world, (int)cap, (int)slot, (int)parity, (unsigned int)epoch);
   MT_LAUNCH_CHECK();
 }
 

@@ -102,6 +102,10 @@ class SymmAmaxSync:
         _cuda().fp8_quantize_ar(x.contiguous(), out, scale, amax, self.counters[slot:slot + 1], self.table.ptrs,
                                 self.me, self.cap, slot, self.epoch & 1, self.epoch, int(fmt))
 
+    def publish_args(self, slot: int):
+        """(counter, table pointers, me, cap, slot, parity, epoch) for kernels that publish."""
+        return (self.counters[slot:slot + 1], self.table.ptrs, self.me, self.cap, slot, self.epoch & 1, self.epoch)
+
     def reduce(self, amax: torch.Tensor) -> None:
         # every rank has published this step's amaxes (its quantise kernels precede the barrier)
         _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 0, self.epoch, 24)
@@ -163,6 +167,22 @@ class Fp8State:
         q = self._quantize(x, fmt, s, None)
         # the inverse scale stays valid until end_step(), i.e. through this step's backward
         return q, self.inv[sl]
+
+    def quantize_colsum(self, x: torch.Tensor, name: str, fmt: int, colsum: torch.Tensor,
+                        accumulate: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Quantise a 2-D bf16 gradient and (+)= its column sums (the bias gradient)
+        into ``colsum`` in one pass over x -> (codes, inverse-scale view)."""
+        s = self.slot(name, fmt)
+        sl = slice(s, s + 1)
+        self._first_step_scale(x, s)
+        out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+        if isinstance(self.sync, SymmAmaxSync):
+            args = self.sync.publish_args(s)
+        else:
+            args = (None, [], 0, self.cap, s, 0, 0)
+        _cuda().fp8_quantize_colsum(x.contiguous(), out, self.scale[sl], self.amax[sl], colsum, bool(accumulate),
+                                    *args, int(fmt))
+        return out, self.inv[sl]
 
     def quantize_into(self, x: torch.Tensor, name: str, fmt: int, out: torch.Tensor):
         s = self.slot(name, fmt)

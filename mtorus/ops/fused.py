@@ -192,23 +192,24 @@ class AttnBlockFn(Function):
         if fp8 is not None:
             st, tag = fp8
             ih, io = ctx.inv
-            g8, ig = st.quantize(dout, tag + ".out_grad", F8.E5M2)
+            # E5M2 codes and the output-projection bias gradient in one pass over dout
+            g8, ig = st.quantize_colsum(dout, tag + ".out_grad", F8.E5M2, bo.main_grad, acc)
             do = F8.gemm_fp8(g8, F8.E5M2, wo.w8, F8.E4M3, b_mn=True, alpha=ig, alpha2=wo.w8_inv)
             F8.gemm_fp8(g8, F8.E5M2, o, F8.E4M3, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc,
                         alpha=ig, alpha2=io)
         else:
             do = K.gemm(dout, wo.w16, b_mn=True)
             K.gemm(dout, o, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc)
-        K.colsum_(dout, bo.main_grad, acc)
+            K.colsum_(dout, bo.main_grad, acc)
         _grads_done(wo, bo)
         dqkv = attention_bwd(do, qkv, o_bf16, lse, *ctx.shape)
-        K.colsum_(dqkv, bq.main_grad, acc)
         if fp8 is not None:
-            q8, iq = st.quantize(dqkv, tag + ".qkv_grad", F8.E5M2)
+            q8, iq = st.quantize_colsum(dqkv, tag + ".qkv_grad", F8.E5M2, bq.main_grad, acc)
             F8.gemm_fp8(q8, F8.E5M2, h, F8.E4M3, out=wq.main_grad, a_mn=True, b_mn=True, accumulate=acc,
                         alpha=iq, alpha2=ih)
             dh = F8.gemm_fp8(q8, F8.E5M2, wq.w8, F8.E4M3, b_mn=True, alpha=iq, alpha2=wq.w8_inv)
         else:
+            K.colsum_(dqkv, bq.main_grad, acc)
             K.gemm(dqkv, h, out=wq.main_grad, a_mn=True, b_mn=True, accumulate=acc)
             dh = K.gemm(dqkv, wq.w16, b_mn=True)
         _grads_done(wq, bq)
@@ -256,22 +257,22 @@ class MLPBlockFn(Function):
         if fp8 is not None:
             st, tag = fp8
             ih, ia = ctx.inv
-            g8, ig = st.quantize(dout, tag + ".ffn2_grad", F8.E5M2)
+            g8, ig = st.quantize_colsum(dout, tag + ".ffn2_grad", F8.E5M2, b2.main_grad, acc)
             dpre = F8.gemm_fp8(g8, F8.E5M2, w2.w8, F8.E4M3, b_mn=True, aux=pre, alpha=ig, alpha2=w2.w8_inv)
             F8.gemm_fp8(g8, F8.E5M2, act, F8.E4M3, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc,
                         alpha=ig, alpha2=ia)
         else:
             dpre = K.gemm(dout, w2.w16, b_mn=True, aux=pre)
             K.gemm(dout, act, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc)
-        K.colsum_(dout, b2.main_grad, acc)
+            K.colsum_(dout, b2.main_grad, acc)
         _grads_done(w2, b2)
-        K.colsum_(dpre, b1.main_grad, acc)
         if fp8 is not None:
-            p8, ip = st.quantize(dpre, tag + ".ffn1_grad", F8.E5M2)
+            p8, ip = st.quantize_colsum(dpre, tag + ".ffn1_grad", F8.E5M2, b1.main_grad, acc)
             F8.gemm_fp8(p8, F8.E5M2, h, F8.E4M3, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc,
                         alpha=ip, alpha2=ih)
             dh = F8.gemm_fp8(p8, F8.E5M2, w1.w8, F8.E4M3, b_mn=True, alpha=ip, alpha2=w1.w8_inv)
         else:
+            K.colsum_(dpre, b1.main_grad, acc)
             K.gemm(dpre, h, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc)
             dh = K.gemm(dpre, w1.w16, b_mn=True)
         _grads_done(w1, b1)

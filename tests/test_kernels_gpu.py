@@ -294,3 +294,24 @@ def test_attention_forward_backward(B, S, H):
     d = dqkv.view(B * S, 3, H * dh)
     for i, name in enumerate("qkv"):
         assert _rel(d[:, i], g[:, i]) < 2e-2, (name, _rel(d[:, i], g[:, i]))
+
+
+@pytest.mark.parametrize("rows,F", [(512, 256), (1000, 2048), (64, 8)])
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_fp8_quantize_colsum(rows, F, accumulate):
+    """Fused E5M2 quantisation + column sums == the separate quantise and fp32 column sums."""
+    from mtorus.ops import fp8 as F8
+
+    torch.manual_seed(0)
+    x = (torch.randn(rows, F, device="cuda") * 3).bfloat16()
+    st = F8.Fp8State("cuda", history=4, capacity=8)
+    st.first_step = False
+    s = st.slot("g", F8.E5M2)
+    st.scale[s] = 100.0
+    col = torch.full((F,), 0.5, device="cuda")
+    q, _ = st.quantize_colsum(x, "g", F8.E5M2, col, accumulate)
+    ref_q = F8.quantize(x, F8.E5M2, st.scale[s:s + 1])
+    assert torch.equal(q, ref_q)
+    ref_col = x.float().sum(0) + (0.5 if accumulate else 0.0)
+    assert torch.allclose(col, ref_col, rtol=1e-4, atol=1e-3)
+    assert abs(float(st.amax[s]) - float(x.float().abs().max())) < 1e-6
