@@ -46,6 +46,8 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=None,
                     help="override layer count (debug only; the metric is defined for 24)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--graph", default="on", choices=["on", "off"],
+                    help="replay the whole step as one CUDA graph (dp none / nccl)")
     ap.add_argument("--precision", default="fp8", choices=["fp8", "bf16"],
                     help="fp8: E4M3/E5M2 delayed-scaling GEMMs in the blocks; bf16: all GEMMs bf16")
     args = ap.parse_args()
@@ -106,6 +108,16 @@ def main() -> int:
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
+    use_graph = args.graph == "on" and trainer.dp in ("none", "nccl")
+    if use_graph:
+        torch.cuda.empty_cache()
+        trainer.capture(dev_ids[0], dev_tgt[0])
+        for i in range(2):  # the replays' own warm-up
+            trainer.graph_step(dev_ids[i % nb], dev_tgt[i % nb])
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+    step_fn = trainer.graph_step if use_graph else trainer.step_device
 
     sampler = ClockSampler(local_rank).start()
     time.sleep(0.3)
@@ -114,11 +126,13 @@ def main() -> int:
     t0.record()
     h0 = time.perf_counter()
     for i in range(args.steps):
-        loss = trainer.step_device(dev_ids[i % nb], dev_tgt[i % nb])
+        loss = step_fn(dev_ids[i % nb], dev_tgt[i % nb])
     host_ms = (time.perf_counter() - h0) * 1000.0
     t1.record()
     t1.synchronize()
     lc1 = ext.launch_count()
+    if use_graph:  # graph replays launch the captured kernels without host launches
+        lc1 += trainer.graph_launches * args.steps
     barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop()
@@ -132,10 +146,17 @@ def main() -> int:
         torch.cuda.synchronize()
         for i in range(2):
             trainer.step_device(dev_ids[i % nb], dev_tgt[i % nb], reduce=False)
+        comp_fn = lambda a, b: trainer.step_device(a, b, reduce=False)  # noqa: E731
+        if use_graph:
+            trainer.capture(dev_ids[0], dev_tgt[0], reduce=False)
+            trainer.graph_step(dev_ids[0], dev_tgt[0], reduce=False)
+            comp_fn = lambda a, b: trainer.graph_step(a, b, reduce=False)  # noqa: E731
+        torch.cuda.synchronize()
+        barrier()
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c0.record()
         for i in range(args.steps):
-            trainer.step_device(dev_ids[i % nb], dev_tgt[i % nb], reduce=False)
+            comp_fn(dev_ids[i % nb], dev_tgt[i % nb])
         c1.record()
         c1.synchronize()
         comp_ms = c0.elapsed_time(c1)
@@ -198,6 +219,7 @@ def main() -> int:
             "how": "device-timed step minus the same step with no data-parallel communication (max over ranks)",
         },
         "host_enqueue_ms_per_step": round(host_ms / args.steps, 3),
+        "cuda_graph": use_graph,
         "clocks": clocks,
         "gpu_launches": int(lc1 - lc0),
         "final_loss": round(last_loss, 4),

@@ -63,7 +63,8 @@ void fp8_quantize_colsum(const at::Tensor& x, at::Tensor out, const at::Tensor& 
                          const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap, int64_t slot,
                          int64_t parity, int64_t epoch, int64_t fmt);
 void fp8_scaling_update(at::Tensor hist, at::Tensor amax, at::Tensor scale, at::Tensor inv,
-                        const at::Tensor& fmax, int64_t cursor, bool current);
+                        const at::Tensor& fmax, int64_t cursor, bool current,
+                        const c10::optional<at::Tensor>& cursor_dev);
 void fp8_dequantize(const at::Tensor& q, at::Tensor out, const at::Tensor& inv_scale, int64_t fmt);
 void fp8_quantize_blocks(const at::Tensor& x, at::Tensor out, at::Tensor scales, int64_t block_size,
                          double fmax, int64_t fmt);
@@ -125,7 +126,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quantize", &fp8_quantize, py::arg("x"), py::arg("out"), py::arg("scale") = py::none(),
         py::arg("amax") = py::none(), py::arg("fmt") = 0);
   m.def("fp8_amax", &fp8_amax);
-  m.def("fp8_scaling_update", &fp8_scaling_update);
+  m.def("fp8_scaling_update", &fp8_scaling_update, py::arg("hist"), py::arg("amax"), py::arg("scale"),
+        py::arg("inv"), py::arg("fmax"), py::arg("cursor"), py::arg("current"), py::arg("cursor_dev") = py::none());
   m.def("fp8_dequantize", &fp8_dequantize);
   m.def("fp8_quantize_blocks", &fp8_quantize_blocks);
   m.def("symm_status", &symm_status, py::arg("reset") = true);

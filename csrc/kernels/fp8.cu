@@ -249,9 +249,10 @@ __global__ void __launch_bounds__(256) amax_kernel(const bf16* __restrict__ x, f
 __global__ void fp8_scaling_update_kernel(float* __restrict__ hist, float* __restrict__ amax,
                                           float* __restrict__ scale, float* __restrict__ inv,
                                           const float* __restrict__ fmax_per_slot, int slots,
-                                          int H, int cursor, int current) {
+                                          int H, int cursor, int current, const int* cursor_dev) {
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= slots) return;
+  if (cursor_dev) cursor = *cursor_dev;  // device-resident ring position (graph replay)
   const float a = amax[s];
   float* h = hist + (size_t)s * H;
   h[cursor] = a;
@@ -417,15 +418,25 @@ void fp8_amax(const at::Tensor& x, at::Tensor amax) {
   MT_LAUNCH_CHECK();
 }
 
+__global__ void fp8_cursor_advance_kernel(int* cursor, int H) { *cursor = (*cursor + 1) % H; }
+
+// cursor_dev (int32 [1], optional): read the ring position from the device and
+// advance it there, so a captured step replays correctly.
 void fp8_scaling_update(at::Tensor hist, at::Tensor amax, at::Tensor scale, at::Tensor inv,
-                        const at::Tensor& fmax, int64_t cursor, bool current) {
+                        const at::Tensor& fmax, int64_t cursor, bool current,
+                        const c10::optional<at::Tensor>& cursor_dev) {
   const int slots = amax.numel();
   const int H = hist.numel() / std::max(slots, 1);
   if (slots == 0) return;
+  const int* cd = cursor_dev.has_value() ? cursor_dev->data_ptr<int>() : nullptr;
   fp8_scaling_update_kernel<<<(slots + 127) / 128, 128, 0, cur_stream()>>>(
       hist.data_ptr<float>(), amax.data_ptr<float>(), scale.data_ptr<float>(), inv.data_ptr<float>(),
-      fmax.data_ptr<float>(), slots, H, (int)cursor, current ? 1 : 0);
+      fmax.data_ptr<float>(), slots, H, (int)cursor, current ? 1 : 0, cd);
   MT_LAUNCH_CHECK();
+  if (cd && !current) {
+    fp8_cursor_advance_kernel<<<1, 1, 0, cur_stream()>>>(cursor_dev->data_ptr<int>(), H);
+    MT_LAUNCH_CHECK();
+  }
 }
 
 void fp8_dequantize(const at::Tensor& q, at::Tensor out, const at::Tensor& inv_scale, int64_t fmt) {

@@ -130,6 +130,7 @@ class Fp8State:
         self.inv = torch.ones(capacity, device=d)
         self.fmax = torch.zeros(capacity, device=d)
         self.cursor = 0
+        self.cursor_dev = torch.zeros(1, dtype=torch.int32, device=d)  # ring position, advanced on device
         self.first_step = True
         self._measured = set()  # slots whose first-step scale is already set
         self.sync = None  # cross-rank amax reduction (data parallel), see set_amax_sync
@@ -210,8 +211,8 @@ class Fp8State:
             self.sync.reduce(self.amax[:n])
         if n:
             _cuda().fp8_scaling_update(self.hist[:n], self.amax[:n], self.scale[:n], self.inv[:n], self.fmax[:n],
-                                       self.cursor, False)
-        self.cursor = (self.cursor + 1) % self.history
+                                       self.cursor, False, self.cursor_dev)
+        self.cursor = (self.cursor + 1) % self.history  # host mirror (stale under graph replay)
         self.first_step = False
 
     def state_dict(self) -> dict:
@@ -220,7 +221,7 @@ class Fp8State:
         n = len(self.fmts)
         return {"names": dict(self.names), "fmts": list(self.fmts), "hist": self.hist[:n].cpu(),
                 "scale": self.scale[:n].cpu(), "inv": self.inv[:n].cpu(), "amax": self.amax[:n].cpu(),
-                "cursor": self.cursor, "history": self.history, "first_step": self.first_step,
+                "cursor": int(self.cursor_dev), "history": self.history, "first_step": self.first_step,
                 "measured": sorted(self._measured)}
 
     def load_state_dict(self, sd: dict) -> None:
@@ -233,6 +234,7 @@ class Fp8State:
         if "amax" in sd:
             self.amax[:n] = sd["amax"].to(self.device)
         self.cursor = sd["cursor"]
+        self.cursor_dev.fill_(int(sd["cursor"]))
         self.first_step = sd.get("first_step", False)
         self._measured = set(sd.get("measured", []))
 

@@ -170,14 +170,71 @@ class GptTrainer:
             self._local_opt = FusedAdam(self.flat, lr=self.lr)
         return self._local_opt
 
+    # ---------------------------------------------------------------- CUDA graph
+    def capture(self, ids: torch.Tensor, targets: torch.Tensor, reduce: bool = True) -> int:
+        """Captures one whole training step (forward, backward, data-parallel bucket
+        all-reduce, optimizer, FP8 scale roll) into a CUDA graph over static input
+        buffers shaped like ``ids`` / ``targets``; ``graph_step`` then replays it with
+        one launch instead of ~1000.  Call after at least one eager step (the FP8
+        first-step path and every kernel's one-time set-up must have run).  Data
+        parallel over NCCL or none (the symmetric-memory path carries per-step
+        epochs in kernel arguments).  Returns the number of this framework's kernels
+        in the graph."""
+        from .._ext import cuda as _cuda
+
+        if self.dp not in ("none", "nccl"):
+            raise ValueError("graph capture supports dp 'none' / 'nccl'")
+        if self.global_step == 0 or (self.fp8 and self.model.fp8_state.first_step):
+            raise RuntimeError("run one eager step before capturing")
+        if self.warmup_steps and self.global_step < self.warmup_steps:
+            raise RuntimeError("the learning rate is still warming up (it is baked into the graph)")
+        if not reduce:
+            self._local_optimizer()  # its state must exist outside the graph
+        if getattr(self, "_g_ids", None) is None or self._g_ids.shape != ids.shape:
+            self._g_ids = ids.detach().clone()
+            self._g_tgt = targets.detach().clone()
+        torch.cuda.synchronize()
+        lc0 = _cuda().launch_count()
+        g = torch.cuda.CUDAGraph()
+        step0 = self.global_step
+        cursor0 = self.model.fp8_state.cursor if self.fp8 else None
+        with torch.cuda.graph(g):
+            loss = self.step_device(self._g_ids, self._g_tgt, reduce=reduce)
+        self.global_step = step0  # capture records, it does not run a step
+        if self.fp8:
+            self.model.fp8_state.cursor = cursor0
+        n = int(_cuda().launch_count() - lc0)
+        if not hasattr(self, "_graphs"):
+            self._graphs = {}
+        self._graphs[reduce] = (g, loss, n)
+        if reduce:
+            self._graph, self._g_loss, self.graph_launches = g, loss, n
+        torch.cuda.synchronize()
+        return n
+
+    def graph_step(self, ids: torch.Tensor, targets: torch.Tensor, reduce: bool = True) -> torch.Tensor:
+        """One training step by replaying the captured graph; returns the device loss."""
+        g, loss, _ = self._graphs[reduce]
+        self._g_ids.copy_(ids, non_blocking=True)
+        self._g_tgt.copy_(targets, non_blocking=True)
+        g.replay()
+        self.global_step += 1
+        if self.fp8:
+            st = self.model.fp8_state
+            st.cursor = (st.cursor + 1) % st.history
+        return loss
+
     def train_step(self, input_ids: torch.Tensor, targets: torch.Tensor) -> float:
         """Host batch in (ideally pinned), host loss out."""
         if self._ids is None or self._ids.shape != input_ids.shape:
             self._ids = torch.empty(input_ids.shape, dtype=torch.long, device=self.device)
             self._tgt = torch.empty(targets.shape, dtype=torch.long, device=self.device)
-        self._ids.copy_(input_ids, non_blocking=True)
-        self._tgt.copy_(targets, non_blocking=True)
-        loss = self.step_device(self._ids, self._tgt)
+        if getattr(self, "_graph", None) is not None and input_ids.shape == self._g_ids.shape:
+            loss = self.graph_step(input_ids, targets)  # host -> static buffers, replay
+        else:
+            self._ids.copy_(input_ids, non_blocking=True)
+            self._tgt.copy_(targets, non_blocking=True)
+            loss = self.step_device(self._ids, self._tgt)
         self._loss_host.copy_(loss, non_blocking=True)
         torch.cuda.current_stream().synchronize()
         return float(self._loss_host)

@@ -128,3 +128,32 @@ def test_train_gpu_cli_accumulation_metrics_checkpoint(tmp_path):
     m2 = str(tmp_path / "m2.jsonl")
     assert mod.main(common + ["--steps", "1", "--metrics", m2, "--resume", str(tmp_path / "ck" / "step00000002")]) == 0
     assert [json.loads(x)["step"] for x in open(m2)] == [3]
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_cuda_graph_step_matches_eager(fp8):
+    """A whole training step captured once and replayed follows the eager run
+    (losses and weights, FP8 scale rolls included)."""
+    from mtorus.models.gpt import GptConfig
+    from mtorus.training.engine import GptTrainer
+
+    cfg = GptConfig(vocab_size=512, d_model=256, num_layers=2, num_heads=2, d_ff=1024, max_seq_len=128,
+                    dropout=0.0)
+    g = torch.Generator().manual_seed(11)
+    batches = []
+    for _ in range(5):
+        t = torch.randint(0, cfg.vocab_size, (2, 129), generator=g)
+        batches.append((t[:, :-1].contiguous().cuda(), t[:, 1:].contiguous().cuda()))
+    a = GptTrainer(cfg, device="cuda", lr=1e-3, init="normal", seed=0, fp8=fp8)
+    la = [float(a.step_device(x, y)) for x, y in batches]
+    b = GptTrainer(cfg, device="cuda", lr=1e-3, init="normal", seed=0, fp8=fp8)
+    lb = [float(b.step_device(*batches[0]))]
+    n = b.capture(*batches[0])
+    assert n > 10
+    lb += [float(b.graph_step(x, y)) for x, y in batches[1:]]
+    assert b.global_step == 5
+    assert all(abs(p - q) < 2e-3 * abs(p) for p, q in zip(la, lb)), (la, lb)
+    assert torch.allclose(a.flat.master, b.flat.master, rtol=1e-3, atol=1e-5)
+    if fp8:
+        assert int(b.model.fp8_state.cursor_dev) == int(a.model.fp8_state.cursor_dev)
+        assert torch.allclose(a.model.fp8_state.scale, b.model.fp8_state.scale, rtol=1e-2)
