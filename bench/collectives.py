@@ -4,9 +4,13 @@ kernels of mtorus.parallel.symm, one process per GPU.
 
     torchrun --nproc-per-node 8 bench/collectives.py [--max-mb 1024] [--min-kb 4]
 
-Operations: all-reduce (fp32, bf16), broadcast, all-gather and the 2-D torus
+Operations: all-reduce (fp32, bf16, fp8 E4M3), broadcast, all-gather and the 2-D torus
 (2 x N/2) nearest-neighbour halo exchange (NCCL: batched isend/irecv to the 4
 neighbours; mtorus: direct peer stores into per-direction receive slots).
+All-reduce and broadcast also run through NVLS when the fabric offers multicast
+(``mtorus_nvls_*``: multimem.ld_reduce / multimem.st through the switch); the
+FP8 all-reduce decodes peers' codes, sums in fp32 and re-encodes (NCCL: fp8
+tensors where the installed NCCL supports them, else reported unsupported).
 Message sizes are powers of two.  Each point is the median of CUDA-event timed
 iterations (max over ranks); bus bandwidth uses the usual factors
 (all-reduce 2(n-1)/n, all-gather (n-1)/n, broadcast 1, halo: bytes sent per
@@ -51,7 +55,7 @@ def main():
     ap.add_argument("--min-kb", type=int, default=4)
     ap.add_argument("--max-mb", type=int, default=1024)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--ops", default="allreduce_f32,allreduce_bf16,broadcast,allgather,halo")
+    ap.add_argument("--ops", default="allreduce_f32,allreduce_bf16,allreduce_fp8,broadcast,allgather,halo")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -77,21 +81,31 @@ def main():
         b *= 2
     for op in args.ops.split(","):
         for nbytes in sizes:
+            f_v = None
             if op == "allreduce_f32":
                 n = nbytes // 4
                 f_n = lambda: dist.all_reduce(nccl_buf[:n])
                 f_m = lambda: col.all_reduce(n, torch.float32)
+                f_v = (lambda: col.all_reduce_nvls(n, torch.float32)) if col.nvls else None
                 factor = 2 * (world - 1) / world
             elif op == "allreduce_bf16":
                 n = nbytes // 2
                 nb16 = nccl_buf.view(torch.bfloat16)
                 f_n = lambda: dist.all_reduce(nb16[:n])
                 f_m = lambda: col.all_reduce(n, torch.bfloat16)
+                f_v = (lambda: col.all_reduce_nvls(n, torch.bfloat16)) if col.nvls else None
+                factor = 2 * (world - 1) / world
+            elif op == "allreduce_fp8":
+                n = nbytes
+                nb8 = nccl_buf.view(torch.uint8)[:n].view(torch.float8_e4m3fn)
+                f_n = lambda: dist.all_reduce(nb8)
+                f_m = lambda: col.all_reduce_fp8(n, 0)
                 factor = 2 * (world - 1) / world
             elif op == "broadcast":
                 n = nbytes // 4
                 f_n = lambda: dist.broadcast(nccl_buf[:n], 0)
                 f_m = lambda: col.broadcast(nbytes, 0)
+                f_v = (lambda: col.broadcast_nvls(nbytes, 0)) if col.nvls else None
                 factor = 1.0
             elif op == "allgather":
                 if nbytes * world > max_bytes:
@@ -117,16 +131,27 @@ def main():
                 factor = len(nbrs)
             else:
                 continue
-            tn = timed(f_n, args.iters)
+            try:
+                tn = timed(f_n, args.iters)
+            except (RuntimeError, TypeError, ValueError) as e:  # dtype the NCCL build lacks
+                tn = None
+                nccl_err = str(e).splitlines()[0][:120]
             tm = timed(f_m, args.iters)
-            bus_n = nbytes * factor / (tn * 1e-3) / 1e9
-            bus_m = nbytes * factor / (tm * 1e-3) / 1e9
+            tv = timed(f_v, args.iters) if f_v is not None else None
+            bus = lambda t: nbytes * factor / (t * 1e-3) / 1e9  # noqa: E731
             if rank == 0:
-                print(json.dumps({"op": op, "bytes": nbytes, "world": world, "nccl_ms": round(tn, 4),
-                                  "mtorus_ms": round(tm, 4), "nccl_busbw_gbs": round(bus_n, 1),
-                                  "mtorus_busbw_gbs": round(bus_m, 1),
-                                  "mtorus_frac_of_link": round(bus_m / LINK_GBS, 3),
-                                  "status": col.ctx.status(False)}), flush=True)
+                rec = {"op": op, "bytes": nbytes, "world": world,
+                       "nccl_ms": round(tn, 4) if tn else None, "mtorus_ms": round(tm, 4),
+                       "nccl_busbw_gbs": round(bus(tn), 1) if tn else None,
+                       "mtorus_busbw_gbs": round(bus(tm), 1),
+                       "mtorus_frac_of_link": round(bus(tm) / LINK_GBS, 3)}
+                if tn is None:
+                    rec["nccl"] = "unsupported: " + nccl_err
+                if tv is not None:
+                    rec.update({"mtorus_nvls_ms": round(tv, 4), "mtorus_nvls_busbw_gbs": round(bus(tv), 1),
+                                "mtorus_nvls_frac_of_link": round(bus(tv) / LINK_GBS, 3)})
+                rec["status"] = col.ctx.status(False)
+                print(json.dumps(rec), flush=True)
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()

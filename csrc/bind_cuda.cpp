@@ -85,6 +85,9 @@ void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>
 void symm_allgather(int64_t src, const std::vector<int64_t>& dst, int64_t me, int64_t bytes,
                     int64_t ctas);
 void symm_broadcast(const std::vector<int64_t>& bufs, int64_t root, int64_t bytes, int64_t ctas);
+void symm_allreduce_mc(int64_t mc, const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags,
+                       int64_t me, int64_t numel, int64_t dtype, int64_t slot, int64_t epoch, int64_t ctas);
+void symm_broadcast_mc(int64_t src, int64_t mc, int64_t bytes, int64_t ctas);
 void symm_halo(int64_t src, const std::vector<int64_t>& recv, const at::Tensor& nbr_rank,
                const at::Tensor& nbr_slot, int64_t bytes, int64_t ctas);
 void install_segv_handler();
@@ -139,6 +142,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_allgather", &symm_allgather);
   m.def("symm_broadcast", &symm_broadcast);
   m.def("symm_halo", &symm_halo);
+  m.def("symm_allreduce_mc", &symm_allreduce_mc);
+  m.def("symm_broadcast_mc", &symm_broadcast_mc);
   m.def("install_segv_handler", &install_segv_handler);
   m.def("wait_flag", &wait_flag);
   m.def("launch_count", []() { return mtorus::launch_counter(); });

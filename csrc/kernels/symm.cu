@@ -100,21 +100,36 @@ __global__ void __launch_bounds__(512) rs_bucket_kernel(PeerPtrs grads, PeerPtrs
   float acc2 = 0.f;
   int bad = 0;
   const int64_t nvec = (c1 > c0) ? (c1 - c0) / 4 : 0;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t off = c0 + i * 4;
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  // two vectors per thread per trip: 2 x n independent 16-byte peer loads in flight
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < nvec; i0 += 2 * stride) {
+    float4 s[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int p = 0; p < kMaxPeers; ++p) {
       if (p < n) {
-        const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(grads.p[p]) + off);
-        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int64_t i = i0 + u * stride;
+          if (i < nvec) {
+            const float4 v =
+                *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(grads.p[p]) + c0 + i * 4);
+            s[u].x += v.x; s[u].y += v.y; s[u].z += v.z; s[u].w += v.w;
+          }
+        }
       }
     }
-    s.x *= inv_n; s.y *= inv_n; s.z *= inv_n; s.w *= inv_n;
-    *reinterpret_cast<float4*>(mine + off) = s;
-    acc2 += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
-    bad |= !(isfinite(s.x) && isfinite(s.y) && isfinite(s.z) && isfinite(s.w));
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= nvec) continue;
+      float4 t = s[u];
+      t.x *= inv_n; t.y *= inv_n; t.z *= inv_n; t.w *= inv_n;
+      *reinterpret_cast<float4*>(mine + c0 + i * 4) = t;
+      acc2 += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+      bad |= !(isfinite(t.x) && isfinite(t.y) && isfinite(t.z) && isfinite(t.w));
+    }
   }
   // scalar tail (len not a multiple of 4)
   for (int64_t off = c0 + nvec * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; off < c1;
@@ -230,27 +245,37 @@ __global__ void __launch_bounds__(512) allreduce_kernel(PeerPtrs bufs, PeerPtrs 
   const int64_t nvec = numel / V;
   const int64_t per = (nvec + n - 1) / n;
   const int64_t v0 = (int64_t)me * per, v1 = min(nvec, v0 + per);
-  for (int64_t i = v0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < v1;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    float acc[V];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = v0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < v1; i0 += 2 * stride) {
+    uint4 raw[2][kMaxPeers];
 #pragma unroll
-    for (int k = 0; k < V; ++k) acc[k] = 0.f;
+    for (int u = 0; u < 2; ++u)
 #pragma unroll
-    for (int p = 0; p < kMaxPeers; ++p) {
-      if (p < n) {
-        const uint4 raw = reinterpret_cast<const uint4*>(bufs.p[p])[i];
-        const T* e = reinterpret_cast<const T*>(&raw);
+      for (int p = 0; p < kMaxPeers; ++p)
+        if (p < n && i0 + u * stride < v1) raw[u][p] = reinterpret_cast<const uint4*>(bufs.p[p])[i0 + u * stride];
 #pragma unroll
-        for (int k = 0; k < V; ++k) acc[k] += to_f(e[k]);
+    for (int u = 0; u < 2; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= v1) continue;
+      float acc[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) acc[k] = 0.f;
+#pragma unroll
+      for (int p = 0; p < kMaxPeers; ++p) {
+        if (p < n) {
+          const T* e = reinterpret_cast<const T*>(&raw[u][p]);
+#pragma unroll
+          for (int k = 0; k < V; ++k) acc[k] += to_f(e[k]);
+        }
       }
+      uint4 outv;
+      T* o = reinterpret_cast<T*>(&outv);
+#pragma unroll
+      for (int k = 0; k < V; ++k) o[k] = from_f<T>(acc[k]);
+#pragma unroll
+      for (int p = 0; p < kMaxPeers; ++p)
+        if (p < n) reinterpret_cast<uint4*>(bufs.p[p])[i] = outv;
     }
-    uint4 outv;
-    T* o = reinterpret_cast<T*>(&outv);
-#pragma unroll
-    for (int k = 0; k < V; ++k) o[k] = from_f<T>(acc[k]);
-#pragma unroll
-    for (int p = 0; p < kMaxPeers; ++p)
-      if (p < n) reinterpret_cast<uint4*>(bufs.p[p])[i] = outv;
   }
 }
 
@@ -271,12 +296,19 @@ __global__ void __launch_bounds__(512) allgather_kernel(const uint4* __restrict_
 __global__ void __launch_bounds__(512) broadcast_kernel(PeerPtrs bufs, int root, int n,
                                                         int64_t nvec) {
   const uint4* src = reinterpret_cast<const uint4*>(bufs.p[root]);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const uint4 v = src[i];
+  constexpr int U = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < nvec; i0 += U * stride) {
+    uint4 v[U];
 #pragma unroll
-    for (int p = 0; p < kMaxPeers; ++p)
-      if (p < n && p != root) reinterpret_cast<uint4*>(bufs.p[p])[i] = v;
+    for (int u = 0; u < U; ++u)
+      if (i0 + u * stride < nvec) v[u] = src[i0 + u * stride];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int p = 0; p < kMaxPeers; ++p)
+        if (p < n && p != root && i0 + u * stride < nvec)
+          reinterpret_cast<uint4*>(bufs.p[p])[i0 + u * stride] = v[u];
   }
 }
 
@@ -294,6 +326,153 @@ __global__ void __launch_bounds__(512) halo_kernel(const uint4* __restrict__ src
       uint4* d = reinterpret_cast<uint4*>(recv.p[nbr_rank[k]]);
       d[(int64_t)nbr_slot[k] * nvec + i] = v;
     }
+  }
+}
+
+// ------------------------------------------------------------------ NVLS (multimem) collectives
+// The symmetric buffers are also bound to an NVLink multicast object: a
+// `multimem.ld_reduce` through the multicast address returns the sum of that
+// element over every GPU (the NVSwitch reduces in the switch), a `multimem.st`
+// writes one value into every GPU's copy.  All-reduce: each rank reduces its
+// 1/N slice in the switch and stores the result back to all ranks (each byte
+// crosses its link about twice, independent of N); broadcast: the root stores
+// once and the switch replicates.
+__device__ __forceinline__ void mc_ld_reduce_f32(uint64_t a, float4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(a)
+               : "memory");
+}
+__device__ __forceinline__ void mc_ld_reduce_bf16(uint64_t a, uint4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(a)
+               : "memory");
+}
+__device__ __forceinline__ void mc_st_16(uint64_t a, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
+__device__ __forceinline__ void mc_publish_fence() {
+  // multicast stores alias the unicast buffers the consumers read
+  asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+}
+
+template <int DT>  // 0: fp32, 1: bf16
+__global__ void __launch_bounds__(512) allreduce_mc_kernel(uint64_t mc, PeerPtrs flags, uint32_t* my_flags,
+                                                           int me, int n, int64_t numel, int slot,
+                                                           uint32_t epoch, int* status) {
+  if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 33)) return;
+  const int64_t nvec = numel / (DT == 0 ? 4 : 8);
+  const int64_t per = (nvec + n - 1) / n;
+  const int64_t v0 = (int64_t)me * per, v1 = min(nvec, v0 + per);
+  // four vectors per thread per trip: the switch round trip is long, keep many in flight
+  constexpr int U = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = v0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < v1; i0 += U * stride) {
+    uint4 r[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < v1) {
+        const uint64_t a = mc + (uint64_t)i * 16;
+        if (DT == 0) {
+          float4 f;
+          mc_ld_reduce_f32(a, f);
+          r[u] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z),
+                            __float_as_uint(f.w));
+        } else {
+          mc_ld_reduce_bf16(a, r[u]);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < v1) mc_st_16(mc + (uint64_t)i * 16, r[u]);
+    }
+  }
+  mc_publish_fence();
+}
+
+// Only the root stores; every rank's buffer receives the data.
+__global__ void __launch_bounds__(512) broadcast_mc_kernel(const uint4* __restrict__ src, uint64_t mc,
+                                                           int64_t nvec) {
+  constexpr int U = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < nvec; i0 += U * stride) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + u * stride < nvec) v[u] = src[i0 + u * stride];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + u * stride < nvec) mc_st_16(mc + (uint64_t)(i0 + u * stride) * 16, v[u]);
+  }
+  mc_publish_fence();
+}
+
+// ------------------------------------------------------------------ FP8 all-reduce (peer loads)
+// E4M3 / E5M2 codes: decode each peer's 16 codes to fp32, sum, re-encode with
+// saturation, store the result into every peer (reduce-scatter + all-gather).
+__device__ __forceinline__ void dec8x2(uint16_t c, int fmt, float& a, float& b) {
+  uint32_t h;
+  if (fmt == 0)
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(c));
+  else
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h) : "h"(c));
+  const __half2 hh = *reinterpret_cast<__half2*>(&h);
+  a = __low2float(hh);
+  b = __high2float(hh);
+}
+__device__ __forceinline__ uint16_t enc8x2(float a, float b, int fmt) {
+  uint16_t r;
+  if (fmt == 0)
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(a), "f"(b));
+  else
+    asm("cvt.rn.satfinite.e5m2x2.f32 %0, %2, %1;" : "=h"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__global__ void __launch_bounds__(512) allreduce_fp8_kernel(PeerPtrs bufs, PeerPtrs flags, uint32_t* my_flags,
+                                                            int me, int n, int64_t numel, int fmt, int slot,
+                                                            uint32_t epoch, int* status) {
+  if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 34)) return;
+  const int64_t nvec = numel / 16;
+  const int64_t per = (nvec + n - 1) / n;
+  const int64_t v0 = (int64_t)me * per, v1 = min(nvec, v0 + per);
+  for (int64_t i = v0 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < v1;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+    uint4 raw[kMaxPeers];
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p)
+      if (p < n) raw[p] = reinterpret_cast<const uint4*>(bufs.p[p])[i];
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p) {
+      if (p < n) {
+        const uint16_t* c = reinterpret_cast<const uint16_t*>(&raw[p]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float a, b;
+          dec8x2(c[k], fmt, a, b);
+          acc[2 * k] += a;
+          acc[2 * k + 1] += b;
+        }
+      }
+    }
+    uint4 outv;
+    uint16_t* o = reinterpret_cast<uint16_t*>(&outv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = enc8x2(acc[2 * k], acc[2 * k + 1], fmt);
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p)
+      if (p < n) reinterpret_cast<uint4*>(bufs.p[p])[i] = outv;
   }
 }
 
@@ -372,6 +551,39 @@ void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>
     allreduce_kernel<bf16><<<(int)ctas, 512, 0, cur_stream()>>>(
         to_peers(bufs), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, numel,
         (int)slot, (uint32_t)epoch, symm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+// NVLS all-reduce through the multicast address `mc` (fp32: dtype 0, bf16: 1), or
+// the FP8 all-reduce over peer loads (dtype 2: E4M3, 3: E5M2; `mc` unused).
+void symm_allreduce_mc(int64_t mc, const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags,
+                       int64_t me, int64_t numel, int64_t dtype, int64_t slot, int64_t epoch, int64_t ctas) {
+  const int n = flags.size();
+  auto* my = reinterpret_cast<uint32_t*>(flags[me]);
+  if (dtype == 0 || dtype == 1) {
+    MT_CHECK(mc != 0, "allreduce_mc: no multicast address");
+    MT_CHECK(mc % 16 == 0 && numel % (dtype == 0 ? 4 : 8) == 0, "allreduce_mc: 16-byte granularity");
+    if (dtype == 0)
+      allreduce_mc_kernel<0><<<(int)ctas, 512, 0, cur_stream()>>>((uint64_t)mc, to_peers(flags), my, (int)me, n,
+                                                                  numel, (int)slot, (uint32_t)epoch,
+                                                                  symm_status_ptr());
+    else
+      allreduce_mc_kernel<1><<<(int)ctas, 512, 0, cur_stream()>>>((uint64_t)mc, to_peers(flags), my, (int)me, n,
+                                                                  numel, (int)slot, (uint32_t)epoch,
+                                                                  symm_status_ptr());
+  } else {
+    MT_CHECK(numel % 16 == 0 && bufs.size() == flags.size(), "allreduce fp8: numel % 16, one buffer per rank");
+    allreduce_fp8_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(to_peers(bufs), to_peers(flags), my, (int)me, n,
+                                                              numel, (int)(dtype - 2), (int)slot, (uint32_t)epoch,
+                                                              symm_status_ptr());
+  }
+  MT_LAUNCH_CHECK();
+}
+
+void symm_broadcast_mc(int64_t src, int64_t mc, int64_t bytes, int64_t ctas) {
+  MT_CHECK(bytes % 16 == 0 && mc % 16 == 0 && mc != 0, "broadcast_mc: 16-byte granularity, multicast address");
+  broadcast_mc_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(reinterpret_cast<const uint4*>(src), (uint64_t)mc,
+                                                           bytes / 16);
   MT_LAUNCH_CHECK();
 }
 

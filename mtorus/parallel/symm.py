@@ -53,6 +53,12 @@ class SymmBuffer:
         base = self.handle.buffer_ptrs[self.rank]
         off = self.tensor.data_ptr() - base
         self.ptrs: List[int] = [int(p) + off for p in self.handle.buffer_ptrs]
+        # NVLink multicast (NVLS) address of the same bytes, 0 when the fabric has none
+        try:
+            mc = int(self.handle.multicast_ptr)  # 0 when the allocation has no multicast binding
+        except (AttributeError, RuntimeError):
+            mc = 0
+        self.mc = mc + off if mc else 0
 
     def barrier(self) -> None:
         self.handle.barrier()
@@ -215,7 +221,7 @@ class ZeroAdam:
 class SymmCollectives:
     """Standalone NVLink collectives on symmetric buffers (microbenchmark / halo)."""
 
-    def __init__(self, device, group=None, max_bytes: int = 1 << 30, ctas: int = 32):
+    def __init__(self, device, group=None, max_bytes: int = 1 << 30, ctas: int = 128):
         self.ctx = SymmContext(device, group)
         self.me, self.world = self.ctx.rank, self.ctx.world
         self.buf = SymmBuffer(max_bytes // 4, torch.float32, device, group)
@@ -234,6 +240,37 @@ class SymmCollectives:
                                0, ep, self.ctas)
         _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 1, ep, 32)
         return self.buf.tensor.view(dtype)[:numel]
+
+    @property
+    def nvls(self) -> bool:
+        """True when the buffers have an NVLink multicast address (NVSwitch reduction)."""
+        return self.buf.mc != 0
+
+    def all_reduce_nvls(self, numel: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """In-place sum over ranks through NVLS: each rank reduces its slice in the
+        switch (multimem.ld_reduce) and stores it to every rank (multimem.st)."""
+        ep = self._slot()
+        _cuda().symm_allreduce_mc(self.buf.mc, self.buf.ptrs, self.ctx.flags.ptrs, self.me, numel,
+                                  0 if dtype == torch.float32 else 1, 6, ep, self.ctas)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 7, ep, 37)
+        return self.buf.tensor.view(dtype)[:numel]
+
+    def all_reduce_fp8(self, numel: int, fmt: int = 0) -> torch.Tensor:
+        """In-place sum over ranks of ``numel`` FP8 codes (0: E4M3, 1: E5M2): fp32
+        accumulation, saturating re-encode, result in every rank's buffer."""
+        ep = self._slot()
+        _cuda().symm_allreduce_mc(0, self.buf.ptrs, self.ctx.flags.ptrs, self.me, numel, 2 + fmt, 8, ep, self.ctas)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 9, ep, 38)
+        return self.buf.tensor.view(torch.uint8)[:numel]
+
+    def broadcast_nvls(self, nbytes: int, root: int = 0) -> None:
+        """The root stores its bytes once into the multicast address; the switch
+        writes every rank's copy."""
+        ep = self._slot()
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 10, ep, 39)  # every rank is past its last read
+        if self.me == root:
+            _cuda().symm_broadcast_mc(self.buf.tensor.data_ptr(), self.buf.mc, nbytes, self.ctas)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 11, ep, 40)
 
     def all_gather(self, nbytes: int) -> None:
         """Each rank's first nbytes of ``buf`` land in slot rank of every peer's ``recv``."""

@@ -201,3 +201,43 @@ def test_fp8_amax_allreduce_2gpu(kind):
             xa = (torch.randn(4096, 256) * (r + 1) * (step + 1)).bfloat16().float()
             a_amax[0] = max(a_amax[0], float(xa.abs().max()))
     assert abs(float(res[0]["scale"][2][0]) - 416.0 / a_amax[0]) < 1e-3 * 416.0 / a_amax[0]
+
+
+def _nvls_body(rank, world):
+    import torch
+
+    from mtorus.parallel.symm import SymmCollectives
+
+    torch.cuda.set_device(rank)
+    c = SymmCollectives(f"cuda:{rank}", max_bytes=1 << 22)
+    out = {"nvls": c.nvls}
+    n = 4096
+    # FP8 all-reduce (peer loads): codes of small integers sum exactly
+    vals = torch.full((n,), float(rank + 1), device="cuda").to(torch.float8_e4m3fn)
+    c.buf.tensor.view(torch.uint8)[:n] = vals.view(torch.uint8)
+    r8 = c.all_reduce_fp8(n, 0).clone().view(torch.float8_e4m3fn).float().cpu()
+    out["fp8"] = r8
+    if c.nvls:
+        c.buf.tensor[:n] = torch.arange(n, device="cuda", dtype=torch.float32) * (rank + 1)
+        out["ar"] = c.all_reduce_nvls(n).clone().cpu()
+        c.buf.tensor.view(torch.bfloat16)[:n] = (torch.ones(n, device="cuda") * (rank + 1)).bfloat16()
+        out["ar16"] = c.all_reduce_nvls(n, torch.bfloat16).float().clone().cpu()
+        c.buf.tensor[:256] = 5.0 if rank == 1 else -1.0
+        c.broadcast_nvls(256 * 4, root=1)
+        out["bc"] = c.buf.tensor[:256].clone().cpu()
+    out["status"] = c.ctx.status()
+    torch.cuda.synchronize()
+    return out
+
+
+@needs2
+def test_nvls_and_fp8_collectives_2gpu():
+    res = run_dist(_nvls_body, 2, backend="nccl")
+    n = 4096
+    for o in res:
+        assert o["status"] == 0
+        assert torch.equal(o["fp8"], torch.full((n,), 3.0))
+        if o["nvls"]:
+            assert torch.allclose(o["ar"], torch.arange(n, dtype=torch.float32) * 3)
+            assert torch.allclose(o["ar16"], torch.full((n,), 3.0))
+            assert torch.equal(o["bc"], torch.full((256,), 5.0))
