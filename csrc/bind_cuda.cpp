@@ -7,6 +7,11 @@ namespace mtorus {
 // layernorm.cu
 std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gamma,
                                       const at::Tensor& beta, double eps);
+std::vector<at::Tensor> layernorm_fwd_fp8(const at::Tensor& x, const at::Tensor& gamma, const at::Tensor& beta,
+                                          double eps, at::Tensor y8, const at::Tensor& scale, at::Tensor amax,
+                                          int64_t fmt, const c10::optional<at::Tensor>& counter,
+                                          const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
+                                          int64_t slot, int64_t parity, int64_t epoch);
 at::Tensor layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& gamma,
                          const at::Tensor& mean, const at::Tensor& rstd, at::Tensor dgamma,
                          at::Tensor dbeta, bool accumulate, const c10::optional<at::Tensor>& dres);
@@ -148,6 +153,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wait_flag", &wait_flag);
   m.def("launch_count", []() { return mtorus::launch_counter(); });
   m.def("fp8_quantize_ar", &fp8_quantize_ar);
+  m.def("layernorm_fwd_fp8", &layernorm_fwd_fp8);
   m.def("fp8_amax_gather", &fp8_amax_gather);
   m.def("fp8_quantize_colsum", &fp8_quantize_colsum);
   m.def("attn_fwd", &attn_fwd);

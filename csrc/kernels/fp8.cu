@@ -11,25 +11,11 @@
 // 1-byte codes with 16-byte stores and folds max|x| into the slot's running
 // amax with one atomic per block.  After the step one tiny kernel rolls every
 // slot's ring buffer and recomputes scale / inverse scale for all slots at once.
-#include "common.cuh"
+#include "amax_publish.cuh"
 
 namespace mtorus {
 
-__device__ __forceinline__ uint16_t cvt2_e4m3(float a, float b) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ uint16_t cvt2_e5m2(float a, float b) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e5m2x2.f32 %0, %2, %1;" : "=h"(r) : "f"(a), "f"(b));
-  return r;
-}
 
-__device__ __forceinline__ void atomic_max_pos(float* addr, float v) {
-  // non-negative floats order like their bit patterns
-  atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
-}
 
 template <int FMT>  // 0 = E4M3, 1 = E5M2
 __global__ void __launch_bounds__(256) fp8_quantize_kernel(const bf16* __restrict__ x,
@@ -81,37 +67,6 @@ __global__ void __launch_bounds__(256) fp8_quantize_kernel(const bf16* __restric
 // over ranks of the entries stamped with this step's epoch.  The table is
 // double-buffered by step parity, so a peer that already runs the next step
 // writes the other half.
-constexpr int kAmaxMaxPeers = 8;
-struct AmaxPeers {
-  uint64_t p[kAmaxMaxPeers];
-};
-
-// Block amax -> the slot's running amax (atomic); with a counter, the grid's last
-// block then stores the slot's amax into every peer's table (see above).
-__device__ __forceinline__ void publish_amax(float m, float* amax, unsigned int* counter, const AmaxPeers& table,
-                                             int me, int world, int cap, int slot, int parity, unsigned int epoch,
-                                             bool* last) {
-  if (threadIdx.x == 0) {
-    atomic_max_pos(amax, m);
-    if (counter) {
-      __threadfence();
-      *last = atomicAdd(counter, 1u) == gridDim.x * gridDim.y - 1;
-    }
-  }
-  if (!counter) return;
-  __syncthreads();
-  if (!*last) return;
-  if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch on this slot
-  if (threadIdx.x < world) {
-    const float a = *reinterpret_cast<volatile float*>(amax);
-    const unsigned long long v = ((unsigned long long)epoch << 32) | __float_as_uint(a);
-    unsigned long long* t = reinterpret_cast<unsigned long long*>(table.p[threadIdx.x]) +
-                            ((size_t)parity * world + me) * cap + slot;
-    *reinterpret_cast<volatile unsigned long long*>(t) = v;
-    __threadfence_system();
-  }
-}
-
 // Quantise a [rows, F] bf16 gradient and add its column sums into `colsum` (the
 // bias gradient) in the same pass: blocks of 32 column groups of 8 x 8 row lanes,
 // 16-byte loads, 8-byte code stores, per-block column partials in shared memory

@@ -9,7 +9,7 @@
 // gamma/beta are the fp32 master parameters.  The backward writes dx and
 // accumulates dgamma/dbeta in per-warp shared-memory slices, reduced per block
 // into a [blocks, 2, d] partial buffer and finished by a column-sum kernel.
-#include "common.cuh"
+#include "amax_publish.cuh"
 
 namespace mtorus {
 
@@ -282,6 +282,82 @@ __global__ void __launch_bounds__(1024) ln_fwd_row(const bf16* __restrict__ x,
   }
 }
 
+// LayerNorm whose output goes straight to FP8 codes (the input of the next FP8
+// GEMM): y = LN(x) is rounded to bf16 as in the bf16 path, multiplied by the tensor
+// role's delayed scale and stored as E4M3 / E5M2; max|y| folds into the role's amax
+// (and, with a counter, is published to the data-parallel peers).  Saves the bf16
+// write of y and the separate quantise pass that would read it back.
+template <int FMT>
+__global__ void __launch_bounds__(1024) ln_fwd_row_fp8(const bf16* __restrict__ x,
+                                                       const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta,
+                                                       uint8_t* __restrict__ y8, float* __restrict__ mean_out,
+                                                       float* __restrict__ rstd_out, int rows, int d, float eps,
+                                                       const float* __restrict__ scale, float* __restrict__ amax,
+                                                       unsigned int* counter, AmaxPeers table, int me, int world,
+                                                       int cap, int slot, int parity, unsigned int epoch) {
+  __shared__ float red[4][32];
+  __shared__ float redm[32];
+  __shared__ bool last;
+  const int col = threadIdx.x * 8;
+  const float sc = *scale;
+  float g[8], b[8];
+  {
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + col);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + col + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(beta + col);
+    const float4 b1 = *reinterpret_cast<const float4*>(beta + col + 4);
+    g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+    b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+  }
+  float m = 0.f;
+  int par = 0;
+  bf16x8 nxt;
+  if (blockIdx.x < rows) nxt = *reinterpret_cast<const bf16x8*>(x + (size_t)blockIdx.x * d + col);
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    float v[8];
+    unpack8(nxt, v);
+    if (row + gridDim.x < rows)
+      nxt = *reinterpret_cast<const bf16x8*>(x + (size_t)(row + gridDim.x) * d + col);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[i];
+    const float mean = block_sum2(s, 0.f, red, par).x / d;
+    par ^= 1;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float t = v[i] - mean;
+      q += t * t;
+    }
+    const float rstd = rsqrtf(block_sum2(q, 0.f, red, par).x / d + eps);
+    par ^= 1;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = (v[i] - mean) * rstd * g[i] + b[i];
+    float r[8];
+    unpack8(pack8(o), r);  // the bf16 value the unfused path would quantise
+    uint32_t w[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) m = fmaxf(m, fabsf(r[4 * k + j]));
+      const uint16_t lo = FMT == 0 ? cvt2_e4m3(r[4 * k] * sc, r[4 * k + 1] * sc)
+                                   : cvt2_e5m2(r[4 * k] * sc, r[4 * k + 1] * sc);
+      const uint16_t hi = FMT == 0 ? cvt2_e4m3(r[4 * k + 2] * sc, r[4 * k + 3] * sc)
+                                   : cvt2_e5m2(r[4 * k + 2] * sc, r[4 * k + 3] * sc);
+      w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint2*>(y8 + (size_t)row * d + col) = make_uint2(w[0], w[1]);
+    if (threadIdx.x == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+  m = block_max(m, redm);
+  publish_amax(m, amax, counter, table, me, world, cap, slot, parity, epoch, &last);
+}
+
 // dx = LN backward (+ dres, the gradient of a residual branch that reads x);
 // part[block][0][:] / part[block][1][:] = this block's dgamma / dbeta sums.
 __global__ void __launch_bounds__(1024) ln_bwd_row(const bf16* __restrict__ dy,
@@ -400,6 +476,48 @@ static int pick_nch(int d) {
   if (d <= 2048) return 8;
   if (d <= 4096) return 16;
   return 0;
+}
+
+// LayerNorm straight to FP8 codes (see ln_fwd_row_fp8) -> (mean, rstd); y8 is the
+// uint8 [rows, d] output.  table_ptrs empty: local amax only.
+std::vector<at::Tensor> layernorm_fwd_fp8(const at::Tensor& x, const at::Tensor& gamma, const at::Tensor& beta,
+                                          double eps, at::Tensor y8, const at::Tensor& scale, at::Tensor amax,
+                                          int64_t fmt, const c10::optional<at::Tensor>& counter,
+                                          const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
+                                          int64_t slot, int64_t parity, int64_t epoch) {
+  MT_CHECK_CUDA(x);
+  MT_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "layernorm_fwd_fp8: contiguous bf16 x");
+  MT_CHECK(gamma.scalar_type() == at::kFloat && beta.scalar_type() == at::kFloat, "layernorm_fwd_fp8: fp32 params");
+  const int d = x.size(-1);
+  const int rows = x.numel() / d;
+  MT_CHECK(y8.element_size() == 1 && y8.numel() == x.numel() && y8.is_contiguous(), "layernorm_fwd_fp8: y8");
+  const auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  MT_CHECK(row_kernel_ok(d, xp, gamma.data_ptr(), beta.data_ptr()) &&
+               reinterpret_cast<uintptr_t>(y8.data_ptr()) % 16 == 0,
+           "layernorm_fwd_fp8: d must be a multiple of 8 up to 8192 with aligned buffers");
+  auto opts = x.options().dtype(at::kFloat);
+  auto mean = at::empty({rows}, opts), rstd = at::empty({rows}, opts);
+  if (rows == 0) return {mean, rstd};
+  const int world = (int)table_ptrs.size();
+  MT_CHECK(world <= kAmaxMaxPeers && (world == 0 || counter.has_value()), "layernorm_fwd_fp8: peers");
+  AmaxPeers t{};
+  for (int i = 0; i < world; ++i) t.p[i] = (uint64_t)table_ptrs[i];
+  unsigned int* cp = world ? reinterpret_cast<unsigned int*>(counter->data_ptr()) : nullptr;
+  const int threads = d / 8;
+  const int grid = std::min(rows, num_sms() * std::max(1, 2048 / threads));
+  auto* yp = reinterpret_cast<uint8_t*>(y8.data_ptr());
+  if (fmt == 0)
+    ln_fwd_row_fp8<0><<<grid, threads, 0, cur_stream()>>>(
+        xp, gamma.data_ptr<float>(), beta.data_ptr<float>(), yp, mean.data_ptr<float>(), rstd.data_ptr<float>(),
+        rows, d, (float)eps, scale.data_ptr<float>(), amax.data_ptr<float>(), cp, t, (int)me, world, (int)cap,
+        (int)slot, (int)parity, (unsigned int)epoch);
+  else
+    ln_fwd_row_fp8<1><<<grid, threads, 0, cur_stream()>>>(
+        xp, gamma.data_ptr<float>(), beta.data_ptr<float>(), yp, mean.data_ptr<float>(), rstd.data_ptr<float>(),
+        rows, d, (float)eps, scale.data_ptr<float>(), amax.data_ptr<float>(), cp, t, (int)me, world, (int)cap,
+        (int)slot, (int)parity, (unsigned int)epoch);
+  MT_LAUNCH_CHECK();
+  return {mean, rstd};
 }
 
 std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gamma,

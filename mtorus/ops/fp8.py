@@ -185,6 +185,28 @@ class Fp8State:
                                     *args, int(fmt))
         return out, self.inv[sl]
 
+    def layernorm_quantize(self, x2d: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float,
+                           name: str, fmt: int):
+        """LayerNorm(x) straight to FP8 codes of tensor role ``name`` ->
+        (codes, inverse-scale view, mean, rstd).  The first step, whose scale is
+        measured on the tensor itself, takes the unfused route (bf16 LN, then quantise)."""
+        if self.first_step:
+            from . import kernels as K
+
+            h, mean, rstd = K.layernorm_fwd(x2d, gamma, beta, eps)
+            q, inv = self.quantize(h, name, fmt)
+            return q, inv, mean, rstd
+        s = self.slot(name, fmt)
+        sl = slice(s, s + 1)
+        out = torch.empty(x2d.shape, dtype=torch.uint8, device=x2d.device)
+        if isinstance(self.sync, SymmAmaxSync):
+            args = self.sync.publish_args(s)
+        else:
+            args = (None, [], 0, self.cap, s, 0, 0)
+        mean, rstd = _cuda().layernorm_fwd_fp8(x2d.contiguous(), gamma, beta, float(eps), out, self.scale[sl],
+                                               self.amax[sl], int(fmt), *args)
+        return out, self.inv[sl], mean, rstd
+
     def quantize_into(self, x: torch.Tensor, name: str, fmt: int, out: torch.Tensor):
         s = self.slot(name, fmt)
         sl = slice(s, s + 1)

@@ -154,15 +154,17 @@ class AttnBlockFn(Function):
 
         B, S, H, dh = shape
         check_shape(S, dh)
-        h, mean, rstd = _ln_fwd(x2d, ln)
         wq, bq = qkv_params
         wo, bo = out_params
         if fp8 is not None:
             st, tag = fp8
-            h8, ih = st.quantize(h, tag + ".qkv_in", F8.E4M3)
+            gamma, beta, eps = ln
+            # LayerNorm writes the E4M3 codes of the QKV GEMM's input directly
+            h8, ih, mean, rstd = st.layernorm_quantize(x2d, gamma.data, beta.data, eps, tag + ".qkv_in", F8.E4M3)
             qkv = F8.gemm_fp8(h8, F8.E4M3, wq.w8, F8.E4M3, bias=bq.data, alpha=ih, alpha2=wq.w8_inv)
             h = h8
         else:
+            h, mean, rstd = _ln_fwd(x2d, ln)
             qkv = K.gemm(h, wq.w16, bias=bq.data)
         o, lse = attention_fwd(qkv, B, S, H)
         attn_saved = (qkv, o, lse)
@@ -225,13 +227,13 @@ class MLPBlockFn(Function):
     @staticmethod
     def forward(ctx, x2d, ln, params, fp8=None):
         w1, b1, w2, b2 = params
-        h, mean, rstd = _ln_fwd(x2d, ln)
-        T, F = h.shape[0], w1.shape[0]
-        pre = torch.empty((T, F), dtype=torch.bfloat16, device=h.device)
+        T, F = x2d.shape[0], w1.shape[0]
+        pre = torch.empty((T, F), dtype=torch.bfloat16, device=x2d.device)
         act = torch.empty_like(pre)
         if fp8 is not None:
             st, tag = fp8
-            h8, ih = st.quantize(h, tag + ".ffn1_in", F8.E4M3)
+            gamma, beta, eps = ln
+            h8, ih, mean, rstd = st.layernorm_quantize(x2d, gamma.data, beta.data, eps, tag + ".ffn1_in", F8.E4M3)
             F8.gemm_fp8(h8, F8.E4M3, w1.w8, F8.E4M3, out=pre, bias=b1.data, act=act, alpha=ih,
                         alpha2=w1.w8_inv)
             a8, ia = st.quantize(act, tag + ".ffn2_in", F8.E4M3)
@@ -240,6 +242,7 @@ class MLPBlockFn(Function):
             h, act = h8, a8
             ctx.inv = (ih, ia)
         else:
+            h, mean, rstd = _ln_fwd(x2d, ln)
             K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
             out = K.gemm(act, w2.w16, bias=b2.data, residual=x2d)
         ctx.save_for_backward(x2d, mean, rstd, h, pre, act)

@@ -315,3 +315,24 @@ def test_fp8_quantize_colsum(rows, F, accumulate):
     ref_col = x.float().sum(0) + (0.5 if accumulate else 0.0)
     assert torch.allclose(col, ref_col, rtol=1e-4, atol=1e-3)
     assert abs(float(st.amax[s]) - float(x.float().abs().max())) < 1e-6
+
+
+@pytest.mark.parametrize("rows,d", [(300, 256), (1024, 2048)])
+def test_layernorm_fp8_output_matches_unfused(K, rows, d):
+    """LayerNorm writing E4M3 codes == bf16 LayerNorm followed by the quantise kernel."""
+    from mtorus.ops import fp8 as F8
+
+    torch.manual_seed(0)
+    x = (torch.randn(rows, d, device="cuda") * 2 + 0.5).bfloat16()
+    gamma = torch.randn(d, device="cuda") * 0.2 + 1
+    beta = torch.randn(d, device="cuda") * 0.1
+    st = F8.Fp8State("cuda", history=4, capacity=8)
+    st.first_step = False
+    s = st.slot("h", F8.E4M3)
+    st.scale[s] = 50.0
+    q, _, mean, rstd = st.layernorm_quantize(x, gamma, beta, 1e-5, "h", F8.E4M3)
+    h, mean_r, rstd_r = K.layernorm_fwd(x, gamma, beta, 1e-5)
+    ref = F8.quantize(h, F8.E4M3, st.scale[s:s + 1])
+    assert torch.equal(q, ref)
+    assert torch.allclose(mean, mean_r) and torch.allclose(rstd, rstd_r)
+    assert float(st.amax[s]) == float(h.float().abs().max())
