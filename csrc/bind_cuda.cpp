@@ -49,6 +49,13 @@ void gemm_fp8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B
               const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
               const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha,
               const c10::optional<at::Tensor>& alpha2, bool beta);
+void gemm_fp8_act8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
+                   int64_t b_fmt, at::Tensor D, const c10::optional<at::Tensor>& bias,
+                   const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
+                   const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha,
+                   const c10::optional<at::Tensor>& alpha2, bool beta,
+                   const c10::optional<at::Tensor>& act8, const c10::optional<at::Tensor>& act8_scale,
+                   const c10::optional<at::Tensor>& act8_amax, int64_t act8_fmt);
 // attention.cu
 std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H);
 at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
@@ -154,6 +161,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", []() { return mtorus::launch_counter(); });
   m.def("fp8_quantize_ar", &fp8_quantize_ar);
   m.def("layernorm_fwd_fp8", &layernorm_fwd_fp8);
+  m.def("gemm_fp8_act8", &gemm_fp8_act8);
   m.def("fp8_amax_gather", &fp8_amax_gather);
   m.def("fp8_quantize_colsum", &fp8_quantize_colsum);
   m.def("attn_fwd", &attn_fwd);

@@ -20,6 +20,7 @@
 // All mbarrier waits are bounded (see sm100.cuh); a timeout raises the status word.
 #include <cstdlib>
 
+#include "amax_publish.cuh"
 #include "sm100.cuh"
 
 namespace mtorus {
@@ -40,6 +41,11 @@ struct GemmEpilogue {
   int64_t ldaux;
   const float* alpha;   // device scalar multiplier or null
   const float* alpha2;  // second device scalar multiplier (e.g. the other operand's 1/scale) or null
+  // FP8 GELU output (2-SM kernel): act8 = fp8(GELU(result) * act8_scale), max|GELU| -> act8_amax
+  uint8_t* act8;
+  const float* act8_scale;
+  float* act8_amax;
+  int act8_fmt;         // 0 = E4M3, 1 = E5M2
 };
 
 namespace {
@@ -504,6 +510,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* dstage = epi_smem + q * 2 * P_EPI_D_BYTES;
     uint8_t* astage = epi_smem + 4 * 2 * P_EPI_D_BYTES + q * 2 * P_EPI_ACT_BYTES;
     const bool f32out = ep.out_f32 != 0;
+    const float act_scale = ep.act8_scale ? *ep.act8_scale : 1.f;
+    float act_amax = 0.f;
     int chunk_count = 0;
     int local = 0;
     for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs, ++local) {
@@ -586,6 +594,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
               *reinterpret_cast<bf16x8*>(astage + sb * P_EPI_ACT_BYTES + lane * 64 +
                                          ((j ^ ((lane >> 1) & 3)) << 4)) = pack8(g8);
+            } else if (ep.act8) {
+              // FP8 GELU: the bf16-rounded GELU (as the bf16 path stores it) times the scale;
+              // 32 rows x 32 B, unswizzled
+              float p8[8], g8[8], r8[8];
+              unpack8(pk, p8);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
+              unpack8(pack8(g8), r8);
+              uint32_t w[2];
+#pragma unroll
+              for (int k = 0; k < 2; ++k) {
+                if (m < M) {  // rows past M hold GELU(bias) of zero-filled A rows
+#pragma unroll
+                  for (int t = 0; t < 4; ++t) act_amax = fmaxf(act_amax, fabsf(r8[4 * k + t]));
+                }
+                const uint16_t lo = ep.act8_fmt == 0 ? cvt2_e4m3(r8[4 * k] * act_scale, r8[4 * k + 1] * act_scale)
+                                                     : cvt2_e5m2(r8[4 * k] * act_scale, r8[4 * k + 1] * act_scale);
+                const uint16_t hi = ep.act8_fmt == 0
+                                        ? cvt2_e4m3(r8[4 * k + 2] * act_scale, r8[4 * k + 3] * act_scale)
+                                        : cvt2_e5m2(r8[4 * k + 2] * act_scale, r8[4 * k + 3] * act_scale);
+                w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+              }
+              *reinterpret_cast<uint2*>(astage + sb * P_EPI_ACT_BYTES + lane * 32 + j * 8) =
+                  make_uint2(w[0], w[1]);
             }
           }
         }
@@ -596,13 +628,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tma_reduce_add_2d(&tma_d, dstage + sb * P_EPI_D_BYTES, n0, row0);
           else
             tma_store_2d(&tma_d, dstage + sb * P_EPI_D_BYTES, n0, row0);
-          if (ep.act) tma_store_2d(&tma_act, astage + sb * P_EPI_ACT_BYTES, n0, row0);
+          if (ep.act || ep.act8) tma_store_2d(&tma_act, astage + sb * P_EPI_ACT_BYTES, n0, row0);
           bulk_commit_group();
         }
       }
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
+    if (ep.act8_amax) {
+      const float wm = warp_max(act_amax);
+      if (lane == 0) atomic_max_pos(ep.act8_amax, wm);
+    }
   }
 
   tc_fence_before();
@@ -762,7 +798,9 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
   CUtensorMap tact = act.has_value()
       ? make_tma_2d(act->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, act->stride(0), 32, 32,
                     CU_TENSOR_MAP_SWIZZLE_64B)
-      : td;
+      : ep.act8 ? make_tma_2d(ep.act8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, N, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_NONE)
+                : td;
   const int num_tiles = (int)(((M + 2 * P_BM - 1) / (2 * P_BM)) * ((N + P_BN - 1) / P_BN));
   const int avail_pairs = std::max(1, (num_sms() - g_reserved_sms) / 2);
   const int pairs = std::min(num_tiles, avail_pairs);
@@ -829,11 +867,32 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
 // FP8 GEMM (tcgen05 kind::f8f6f4, fp32 accumulate): A / B are 1-byte E4M3 (fmt 0)
 // or E5M2 (fmt 1) codes; the epilogue multiplies by alpha * alpha2 (the operands'
 // inverse scales) before bias / residual / GELU / dGELU / fp32 accumulate.
+void gemm_fp8_act8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
+                   int64_t b_fmt, at::Tensor D, const c10::optional<at::Tensor>& bias,
+                   const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
+                   const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha,
+                   const c10::optional<at::Tensor>& alpha2, bool beta,
+                   const c10::optional<at::Tensor>& act8, const c10::optional<at::Tensor>& act8_scale,
+                   const c10::optional<at::Tensor>& act8_amax, int64_t act8_fmt);
+
 void gemm_fp8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
               int64_t b_fmt, at::Tensor D, const c10::optional<at::Tensor>& bias,
               const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
               const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha,
               const c10::optional<at::Tensor>& alpha2, bool beta) {
+  gemm_fp8_act8(A, a_mn, a_fmt, B, b_mn, b_fmt, D, bias, residual, act, aux, alpha, alpha2, beta, c10::nullopt,
+                c10::nullopt, c10::nullopt, 0);
+}
+
+// gemm_fp8 whose epilogue may also write GELU(result) as FP8 codes (act8, uint8 [M, N]
+// contiguous) with the role's scale, folding max|GELU| into act8_amax.
+void gemm_fp8_act8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
+                   int64_t b_fmt, at::Tensor D, const c10::optional<at::Tensor>& bias,
+                   const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
+                   const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha,
+                   const c10::optional<at::Tensor>& alpha2, bool beta,
+                   const c10::optional<at::Tensor>& act8, const c10::optional<at::Tensor>& act8_scale,
+                   const c10::optional<at::Tensor>& act8_amax, int64_t act8_fmt) {
   check_operand(A, "A", 1);
   check_operand(B, "B", 1);
   TORCH_CHECK((a_fmt == 0 || a_fmt == 1) && (b_fmt == 0 || b_fmt == 1), "gemm_fp8: formats are 0 (E4M3) / 1 (E5M2)");
@@ -846,6 +905,17 @@ void gemm_fp8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B
   TORCH_CHECK(!a_mn || M % 16 == 0, "gemm_fp8: M must be a multiple of 16 for an MN-major A");
   TORCH_CHECK(!b_mn || N % 16 == 0, "gemm_fp8: N must be a multiple of 16 for an MN-major B");
   GemmEpilogue ep = build_epilogue(D, M, N, bias, residual, act, aux, alpha, alpha2, beta);
+  if (act8.has_value()) {
+    TORCH_CHECK(!act.has_value() && act8_scale.has_value() && act8_amax.has_value(),
+                "gemm_fp8: act8 needs act8_scale and act8_amax and excludes act");
+    TORCH_CHECK(act8->element_size() == 1 && act8->is_contiguous() && act8->numel() == M * N &&
+                    reinterpret_cast<uintptr_t>(act8->data_ptr()) % 16 == 0 && N % 16 == 0 && M >= 2 * P_BM,
+                "gemm_fp8: act8 must be a 16-byte aligned contiguous uint8 [M, N], N % 16 == 0, M >= 256");
+    ep.act8 = reinterpret_cast<uint8_t*>(act8->data_ptr());
+    ep.act8_scale = act8_scale->data_ptr<float>();
+    ep.act8_amax = act8_amax->data_ptr<float>();
+    ep.act8_fmt = (int)act8_fmt;
+  }
   if (M == 0 || N == 0) return;
   ensure_context();
   launch_pair<1>(A, a_mn, B, b_mn, D, act, ep, M, N, K,

@@ -16,6 +16,7 @@ multiplies by the two operands' inverse scales.
 """
 from __future__ import annotations
 
+import os
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -23,6 +24,9 @@ import torch
 from .._ext import cuda as _cuda
 
 E4M3, E5M2 = 0, 1
+# producers that write FP8 codes themselves (on by default; "0" selects the separate quantise pass)
+_FUSE_LN = os.environ.get("MTORUS_FP8_FUSE_LN", "1") != "0"
+_FUSE_GELU = os.environ.get("MTORUS_FP8_FUSE_GELU", "1") != "0"
 FMT_MAX = {E4M3: 416.0, E5M2: 49152.0}  # reference format maxima (float8 crate MAX)
 
 
@@ -50,6 +54,16 @@ def quantize_blocks(x: torch.Tensor, fmt: int, block_size: int) -> Tuple[torch.T
     scales = torch.empty(nb, dtype=torch.float32, device=x.device)
     _cuda().fp8_quantize_blocks(x, out, scales, int(block_size), FMT_MAX[fmt], int(fmt))
     return out, scales
+
+
+def gemm_fp8_gelu8(a, a_fmt: int, b, b_fmt: int, pre: torch.Tensor, act8: torch.Tensor, act_scale: torch.Tensor,
+                   act_amax: torch.Tensor, act_fmt: int, *, bias=None, alpha=None, alpha2=None):
+    """FP8 GEMM whose epilogue stores the pre-activation (bf16, for dGELU) and
+    GELU(pre) straight as FP8 codes of the next GEMM's input (scale ``act_scale``,
+    max|GELU| folded into ``act_amax``)."""
+    _cuda().gemm_fp8_act8(a, False, int(a_fmt), b, False, int(b_fmt), pre, bias, None, None, None, alpha, alpha2,
+                          False, act8, act_scale, act_amax, int(act_fmt))
+    return pre
 
 
 def gemm_fp8(a, a_fmt: int, b, b_fmt: int, out=None, *, a_mn=False, b_mn=False, bias=None, residual=None,
@@ -185,12 +199,22 @@ class Fp8State:
                                     *args, int(fmt))
         return out, self.inv[sl]
 
+    def epilogue_slot(self, name: str, fmt: int):
+        """(scale, amax, inverse scale) views for a producer kernel that writes the
+        role's FP8 codes itself, or None when it cannot: the first step (scale not
+        known yet) or a cross-rank sync that publishes from the quantise kernels."""
+        if self.first_step or isinstance(self.sync, SymmAmaxSync) or not _FUSE_GELU:
+            return None
+        s = self.slot(name, fmt)
+        sl = slice(s, s + 1)
+        return self.scale[sl], self.amax[sl], self.inv[sl]
+
     def layernorm_quantize(self, x2d: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float,
                            name: str, fmt: int):
         """LayerNorm(x) straight to FP8 codes of tensor role ``name`` ->
         (codes, inverse-scale view, mean, rstd).  The first step, whose scale is
         measured on the tensor itself, takes the unfused route (bf16 LN, then quantise)."""
-        if self.first_step:
+        if self.first_step or not _FUSE_LN:
             from . import kernels as K
 
             h, mean, rstd = K.layernorm_fwd(x2d, gamma, beta, eps)
@@ -261,5 +285,6 @@ class Fp8State:
         self._measured = set(sd.get("measured", []))
 
 
-__all__ = ["E4M3", "E5M2", "FMT_MAX", "quantize", "dequantize", "quantize_blocks", "gemm_fp8", "Fp8State",
+__all__ = ["E4M3", "E5M2", "FMT_MAX", "quantize", "dequantize", "quantize_blocks", "gemm_fp8", "gemm_fp8_gelu8",
+           "Fp8State",
            "NcclAmaxSync", "SymmAmaxSync"]

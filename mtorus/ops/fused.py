@@ -229,20 +229,29 @@ class MLPBlockFn(Function):
         w1, b1, w2, b2 = params
         T, F = x2d.shape[0], w1.shape[0]
         pre = torch.empty((T, F), dtype=torch.bfloat16, device=x2d.device)
-        act = torch.empty_like(pre)
         if fp8 is not None:
             st, tag = fp8
             gamma, beta, eps = ln
             h8, ih, mean, rstd = st.layernorm_quantize(x2d, gamma.data, beta.data, eps, tag + ".ffn1_in", F8.E4M3)
-            F8.gemm_fp8(h8, F8.E4M3, w1.w8, F8.E4M3, out=pre, bias=b1.data, act=act, alpha=ih,
-                        alpha2=w1.w8_inv)
-            a8, ia = st.quantize(act, tag + ".ffn2_in", F8.E4M3)
+            slot = st.epilogue_slot(tag + ".ffn2_in", F8.E4M3) if T >= 256 else None
+            if slot is not None:
+                # the FFN1 epilogue writes GELU straight as the FFN2 input's E4M3 codes
+                a8 = torch.empty((T, F), dtype=torch.uint8, device=x2d.device)
+                F8.gemm_fp8_gelu8(h8, F8.E4M3, w1.w8, F8.E4M3, pre, a8, slot[0], slot[1], F8.E4M3, bias=b1.data,
+                                  alpha=ih, alpha2=w1.w8_inv)
+                ia = slot[2]
+            else:
+                act = torch.empty_like(pre)
+                F8.gemm_fp8(h8, F8.E4M3, w1.w8, F8.E4M3, out=pre, bias=b1.data, act=act, alpha=ih,
+                            alpha2=w1.w8_inv)
+                a8, ia = st.quantize(act, tag + ".ffn2_in", F8.E4M3)
             out = F8.gemm_fp8(a8, F8.E4M3, w2.w8, F8.E4M3, bias=b2.data, residual=x2d, alpha=ia,
                               alpha2=w2.w8_inv)
             h, act = h8, a8
             ctx.inv = (ih, ia)
         else:
             h, mean, rstd = _ln_fwd(x2d, ln)
+            act = torch.empty_like(pre)
             K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
             out = K.gemm(act, w2.w16, bias=b2.data, residual=x2d)
         ctx.save_for_backward(x2d, mean, rstd, h, pre, act)

@@ -336,3 +336,27 @@ def test_layernorm_fp8_output_matches_unfused(K, rows, d):
     assert torch.equal(q, ref)
     assert torch.allclose(mean, mean_r) and torch.allclose(rstd, rstd_r)
     assert float(st.amax[s]) == float(h.float().abs().max())
+
+
+@pytest.mark.parametrize("M,N,Kd", [(256, 512, 256), (1000, 1024, 512)])
+def test_gemm_fp8_gelu_fp8_epilogue(M, N, Kd):
+    """FP8 GEMM writing GELU(x W^T + b) as E4M3 codes == the bf16-GELU epilogue followed
+    by the quantise kernel (codes and amax)."""
+    from mtorus.ops import fp8 as F8
+
+    torch.manual_seed(0)
+    a = (torch.randn(M, Kd, device="cuda") * 0.5).to(torch.float8_e4m3fn).view(torch.uint8)
+    b = (torch.randn(N, Kd, device="cuda") * 0.5).to(torch.float8_e4m3fn).view(torch.uint8)
+    bias = torch.randn(N, device="cuda") * 0.1
+    one = torch.full((1,), 0.05, device="cuda")
+    pre_r = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    act_r = torch.empty_like(pre_r)
+    F8.gemm_fp8(a, F8.E4M3, b, F8.E4M3, out=pre_r, bias=bias, act=act_r, alpha=one)
+    scale = torch.full((1,), 20.0, device="cuda")
+    amax = torch.zeros(1, device="cuda")
+    pre = torch.empty_like(pre_r)
+    a8 = torch.empty(M, N, dtype=torch.uint8, device="cuda")
+    F8.gemm_fp8_gelu8(a, F8.E4M3, b, F8.E4M3, pre, a8, scale, amax, F8.E4M3, bias=bias, alpha=one)
+    assert torch.equal(pre, pre_r)
+    assert torch.equal(a8, F8.quantize(act_r, F8.E4M3, scale))
+    assert float(amax) == float(act_r.float().abs().max())
