@@ -46,8 +46,8 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=None,
                     help="override layer count (debug only; the metric is defined for 24)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--graph", default="on", choices=["on", "off"],
-                    help="replay the whole step as one CUDA graph (dp none / nccl)")
+    ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
+                    help="replay the whole step as one CUDA graph (dp none / nccl); auto: on for 1 GPU")
     ap.add_argument("--precision", default="fp8", choices=["fp8", "bf16"],
                     help="fp8: E4M3/E5M2 delayed-scaling GEMMs in the blocks; bf16: all GEMMs bf16")
     args = ap.parse_args()
@@ -108,7 +108,7 @@ def main() -> int:
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    use_graph = args.graph == "on" and trainer.dp in ("none", "nccl")
+    use_graph = (args.graph == "on" or (args.graph == "auto" and world == 1)) and trainer.dp in ("none", "nccl")
     if use_graph:
         torch.cuda.empty_cache()
         trainer.capture(dev_ids[0], dev_tgt[0])
