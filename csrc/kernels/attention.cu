@@ -278,9 +278,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int e = 0; e < kTile; ++e)
           if (e > r) t[e] = __float_as_uint(-INFINITY);
       }
-      float mx = __uint_as_float(t[0]);
+      // row max as 8 independent chains (a single 128-long chain of dependent max
+      // operations costs ~4 cycles each on the critical path)
+      float m8[8];
 #pragma unroll
-      for (int e = 1; e < kTile; ++e) mx = fmaxf(mx, __uint_as_float(t[e]));
+      for (int k = 0; k < 8; ++k) m8[k] = __uint_as_float(t[k]);
+#pragma unroll
+      for (int e = 8; e < kTile; e += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], __uint_as_float(t[e + k]));
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= sl2;
       float alpha = 1.f;
       if (j == 0) {
@@ -297,7 +304,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
       }
       l *= alpha;
-      float sum = 0.f;
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent partial row sums
       const float neg = -m_ref;
 #pragma unroll
       for (int c16 = 0; c16 < kTile / 8; ++c16) {
@@ -305,7 +312,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           pv[e] = ex2_approx(fmaf(__uint_as_float(t[c16 * 8 + e]), sl2, neg));
-          sum += pv[e];
+          s8[e] += pv[e];
         }
         uint4 w;
         w.x = pack_bf16x2(pv[0], pv[1]);
@@ -314,7 +321,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         w.w = pack_bf16x2(pv[6], pv[7]);
         *reinterpret_cast<uint4*>(myP + sw128_chunk(r, c16)) = w;
       }
-      l += sum;
+      l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       // rescale O (rows whose max grew) before PV_g(j) accumulates into it
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
@@ -372,7 +379,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 // the fp32 dQ buffer (full-line reductions in L2 instead of scattered atomics).
 // TMEM: S^T | dP^T | dV | dK; dQ_i reuses S^T.
 struct BwdCtl {
-  uint64_t kv_full, qdo_full, qdo_empty, st_full, p_ready, pv_done, ds_ready, dq_full, dq_free,
+  uint64_t kv_full, q_full, q_empty, do_full, do_empty, st_full, p_ready, pv_done, ds_ready, dq_full, dq_free,
       kv_done, drain;
   uint32_t tmem_base;
   int abort;
@@ -408,8 +415,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&ctl->kv_full, 1);
-    mbar_init(&ctl->qdo_full, 1);
-    mbar_init(&ctl->qdo_empty, 1);
+    mbar_init(&ctl->q_full, 1);
+    mbar_init(&ctl->q_empty, 1);
+    mbar_init(&ctl->do_full, 1);
+    mbar_init(&ctl->do_empty, 1);
     mbar_init(&ctl->st_full, 1);
     mbar_init(&ctl->p_ready, 256);
     mbar_init(&ctl->pv_done, 1);
@@ -445,20 +454,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_load_2d(sK + kHalf, &tma_qkv, &ctl->kv_full, kcol + 64, krow0);
       tma_load_2d(sV, &tma_qkv, &ctl->kv_full, vcol, krow0);
       tma_load_2d(sV + kHalf, &tma_qkv, &ctl->kv_full, vcol + 64, krow0);
-      int issued = -1;
+      // dO of the next query tile loads as soon as the dV MMA has read this one, Q as
+      // soon as the dK MMA has: both overlap the dS math and the dQ MMA / read-out
+      int issued_q = -1, issued_do = -1;
       for (int it = 0; it < nqi && !*abort; ++it) {
-        if (it > 0 && !mbar_wait(&ctl->qdo_empty, (it - 1) & 1, abort, status, 21)) break;
         const int qr = b * S + (kt + it) * kTile;
-        issued = it;
-        mbar_arrive_expect_tx(&ctl->qdo_full, 2 * kTileBytes);
-        tma_load_2d(sQ, &tma_qkv, &ctl->qdo_full, qcol, qr);
-        tma_load_2d(sQ + kHalf, &tma_qkv, &ctl->qdo_full, qcol + 64, qr);
-        tma_load_2d(sDO, &tma_do, &ctl->qdo_full, h * kD, qr);
-        tma_load_2d(sDO + kHalf, &tma_do, &ctl->qdo_full, h * kD + 64, qr);
+        if (it > 0 && !mbar_wait(&ctl->do_empty, (it - 1) & 1, abort, status, 21)) break;
+        issued_do = it;
+        mbar_arrive_expect_tx(&ctl->do_full, kTileBytes);
+        tma_load_2d(sDO, &tma_do, &ctl->do_full, h * kD, qr);
+        tma_load_2d(sDO + kHalf, &tma_do, &ctl->do_full, h * kD + 64, qr);
+        if (it > 0 && !mbar_wait(&ctl->q_empty, (it - 1) & 1, abort, status, 20)) break;
+        issued_q = it;
+        mbar_arrive_expect_tx(&ctl->q_full, kTileBytes);
+        tma_load_2d(sQ, &tma_qkv, &ctl->q_full, qcol, qr);
+        tma_load_2d(sQ + kHalf, &tma_qkv, &ctl->q_full, qcol + 64, qr);
       }
       if (*abort) {
         bounded_drain(&ctl->kv_full, 0);
-        if (issued >= 0) bounded_drain(&ctl->qdo_full, issued & 1);
+        if (issued_q >= 0) bounded_drain(&ctl->q_full, issued_q & 1);
+        if (issued_do >= 0) bounded_drain(&ctl->do_full, issued_do & 1);
       }
     }
   } else if (warp == 1) {
@@ -472,7 +487,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = mbar_wait(&ctl->kv_full, 0, abort, status, 22);
       const uint32_t q = smem_u32(sQ), dO = smem_u32(sDO);
       for (int it = 0; it < nqi && ok; ++it) {
-        if (!mbar_wait(&ctl->qdo_full, it & 1, abort, status, 23)) break;
+        if (!mbar_wait(&ctl->q_full, it & 1, abort, status, 23)) break;
+        if (!mbar_wait(&ctl->do_full, it & 1, abort, status, 19)) break;
         // the S^T columns hold dQ of the previous tile until the compute warps read it
         if (it > 0 && !mbar_wait(&ctl->dq_free, (it - 1) & 1, abort, status, 24)) break;
         tc_fence_after();
@@ -490,16 +506,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int kk = 0; kk < kTile / 16; ++kk)  // dV += P^T dO
           umma_f16(tDV, desc_kmajor(ps, kk), desc_mnmajor(dO, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
         umma_commit(&ctl->pv_done);
+        umma_commit(&ctl->do_empty);  // dO is read by dP^T and dV only
         if (!mbar_wait(&ctl->ds_ready, it & 1, abort, status, 29)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dK += dS^T Q
           umma_f16(tDK, desc_kmajor(ps, kk), desc_mnmajor(q, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
+        umma_commit(&ctl->q_empty);  // Q is read by S^T and dK only
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dQ_i = dS K
           umma_f16(tDQ, desc_mnmajor(ps, kk), desc_mnmajor(k, kk), id_mn, kk > 0 ? 1u : 0u);
         umma_commit(&ctl->dq_full);
-        umma_commit(&ctl->qdo_empty);
       }
       if (!*abort) {
         umma_commit(&ctl->kv_done);
