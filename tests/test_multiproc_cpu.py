@@ -101,3 +101,81 @@ def test_bucket_reducer_averages_across_ranks():
     res = run_dist(_dp_body, 2)
     for g, nb in res:
         assert nb > 1 and torch.allclose(g[g != 0], torch.full_like(g[g != 0], 1.5))
+
+
+def _gpt_dppp_body(rank, world):
+    """2 replicas x 2 pipeline stages of the reference-path GPT on gloo: the layout of
+    PipelineLayout, activations and gradients on separate groups, DP averaging."""
+    import torch.distributed as dist
+
+    from mtorus.models.gpt import GptConfig, GptModel
+    from mtorus.pipeline import CheckpointStrategy, DistributedPipelineExecutor, ScheduleType
+    from mtorus.training.pipeline_engine import PipelineLayout
+
+    cfg = GptConfig(vocab_size=64, d_model=32, num_layers=2, num_heads=2, d_ff=64, max_seq_len=16, dropout=0.0)
+    lay = PipelineLayout(2, 2)
+    replica, stage = lay.coords(rank)
+    groups = {}
+    for ranks in lay.stage_ranks:
+        ga, gg = dist.new_group(ranks), dist.new_group(ranks)
+        if rank in ranks:
+            groups["act"], groups["grad"] = ga, gg
+    for ranks in lay.dp_ranks:
+        g = dist.new_group(ranks)
+        if rank in ranks:
+            groups["dp"] = g
+    torch.manual_seed(0)
+    full = GptModel(cfg)
+    sd = full.state_dict()
+    m = GptModel(cfg, layers=(stage, stage + 1), embed=stage == 0, head=stage == 1)
+    own = m.state_dict()
+    for k in own:
+        g = f"blocks.{int(k.split('.')[1]) + stage}.{k.split('.', 2)[2]}" if k.startswith("blocks.") else k
+        own[k].copy_(sd[g])
+    M, b, S = 4, 2, 16
+    gen = torch.Generator().manual_seed(10 + replica)
+    t = torch.randint(0, cfg.vocab_size, (M, b, S + 1), generator=gen)
+    ids, tgt = list(t[..., :-1].unbind(0)), list(t[..., 1:].unbind(0))
+
+    def loss_fn(logits, y):
+        return torch.nn.functional.cross_entropy(logits.reshape(-1, cfg.vocab_size), y.reshape(-1))
+
+    ex = DistributedPipelineExecutor(m, lay.stage_ranks[replica], ScheduleType.OneF1B, M, CheckpointStrategy.Full,
+                                     loss_fn=loss_fn, act_shape=(b, S, cfg.d_model), stage_fn=m.forward_stage,
+                                     group=groups["act"], grad_group=groups["grad"])
+    losses = ex.run(ids if stage == 0 else None, tgt if stage == 1 else None)
+    for p in m.parameters():
+        dist.all_reduce(p.grad, group=groups["dp"])
+        p.grad /= 2
+    names = {}
+    for k, p in m.named_parameters():
+        g = f"blocks.{int(k.split('.')[1]) + stage}.{k.split('.', 2)[2]}" if k.startswith("blocks.") else k
+        names[g] = p.grad.clone()
+    return {"losses": losses, "grads": names}
+
+
+def test_gpt_dp2_pp2_gloo_matches_single_process():
+    from mtorus.models.gpt import GptConfig, GptModel
+
+    res = run_dist(_gpt_dppp_body, 4)
+    cfg = GptConfig(vocab_size=64, d_model=32, num_layers=2, num_heads=2, d_ff=64, max_seq_len=16, dropout=0.0)
+    torch.manual_seed(0)
+    full = GptModel(cfg)
+    M, b, S = 4, 2, 16
+    total = 0.0
+    for replica in range(2):
+        gen = torch.Generator().manual_seed(10 + replica)
+        t = torch.randint(0, cfg.vocab_size, (M, b, S + 1), generator=gen)
+        logits = full(t[..., :-1].reshape(M * b, S))
+        loss = torch.nn.functional.cross_entropy(logits.reshape(-1, cfg.vocab_size), t[..., 1:].reshape(-1))
+        (loss / 2).backward()
+        total += float(loss)
+    got = {}
+    for r in res:
+        got.update(r["grads"])
+    assert set(got) == {n for n, _ in full.named_parameters()}
+    for n, p in full.named_parameters():
+        assert torch.allclose(got[n], p.grad, rtol=1e-4, atol=1e-6), n
+    # last stages (ranks 1 and 3) report each replica's micro-batch losses
+    mean_loss = (sum(res[1]["losses"]) + sum(res[3]["losses"])) / 8
+    assert abs(mean_loss - total / 2) < 1e-4
