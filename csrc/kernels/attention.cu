@@ -5,21 +5,27 @@
 // Layout: one [T, 3*H*128] bf16 matrix holds q | k | v for T = B*S tokens (heads
 // contiguous inside each third), the output is [T, H*128]; S is a multiple of 128.
 //
-// Forward, one CTA per (128-query tile, batch, head), heaviest tiles first:
-//   warp 0      TMA producer: Q once, then K_j / V_j into a 2-stage ring
-//   warp 1      MMA issuer: S_j = Q K_j^T into one of two TMEM buffers (issued one
-//               tile ahead), then O += P_j V_j into the TMEM accumulator
-//   warps 2..5  softmax: one query row per thread, read from TMEM; running max
-//               with lazy rescaling (O is rescaled only when a row max grows by
-//               more than 2^8), P written as bf16 into shared memory in the
-//               128B-swizzled K-major layout the MMA reads; the epilogue divides
-//               by the row sum and stores O and the log-sum-exp.
+// Forward, one CTA per (two 128-query tiles, batch, head), heaviest pairs first:
+//   warp 0      TMA producer: both Q tiles once, then K_0, V_0, K_1, ... into a
+//               3-slot ring
+//   warp 1      MMA issuer: S = Q K^T and O += P V for the two tiles in ping-pong
+//               order, so the tensor core works on one tile while the other
+//               tile's softmax runs
+//   warps 2..9  two softmax warpgroups (one per query tile), one query row per
+//               thread, read from TMEM; running max with lazy rescaling (O is
+//               rescaled only when a row max grows by more than 2^8); P is written
+//               as bf16 into shared memory in the 128B-swizzled K-major layout the
+//               MMA reads; the epilogue divides by the row sum and stores O and
+//               the log-sum-exp.
 // Backward, one CTA per (128-key tile, batch, head), looping over query tiles i >= j:
-//   S^T = K Q^T and dP^T = V dO^T into TMEM; P^T = exp(S^T*scale - lse) and
-//   dS^T = P^T (dP^T - D) * scale written to shared memory; dV += P^T dO,
-//   dK += dS^T Q accumulate in TMEM; dQ_i = dS K lands in TMEM (reusing the S^T
-//   columns) and is added to an fp32 dQ buffer with vector atomics.
-// D = rowsum(dO * O) comes from a small pre-kernel; a post-kernel casts dQ to bf16.
+//   S^T = K Q^T and dP^T = V dO^T into TMEM; two compute warpgroups (one column
+//   half each) form P^T = exp(S^T*scale - lse) and dS^T = P^T (dP^T - D) * scale
+//   in one shared-memory tile (P^T for the dV MMA, then dS^T for dK and dQ);
+//   dV, dK accumulate in TMEM; dQ_i = dS K lands in TMEM (reusing the S^T columns)
+//   and leaves through a shared staging area as TMA reduce-adds into an fp32 dQ
+//   buffer.  The next dO / Q tiles load as soon as the dV / dK MMAs release them.
+// D = rowsum(dO * O) (and the zeroing of dQ) comes from a small pre-kernel; a
+// post-kernel casts dQ to bf16.
 //
 // Every wait is bounded (2 s); on a timeout the kernel records a status code,
 // lets its in-flight copies and MMAs land, frees TMEM and returns.
@@ -42,7 +48,6 @@ constexpr int kD = 128;                 // head dim
 constexpr int kTile = 128;              // query / key tile
 constexpr int kTileBytes = kTile * kD * 2;  // 32 KB: two 64-column halves of [128 x 128 B]
 constexpr int kHalf = kTile * 128;          // 16 KB
-constexpr int kThreads = 192;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;        // lazy rescale threshold (log2 units)
 
@@ -81,10 +86,6 @@ __device__ __forceinline__ void bounded_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(smem_u32(bar), parity) && globaltimer_ns() - t0 < 100000000ull) {
   }
-}
-
-__device__ __forceinline__ void named_sync_compute() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
 // ================================================================== forward
