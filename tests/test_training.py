@@ -378,3 +378,21 @@ def test_train_cli_set_overrides():
     assert tc.learning_rate == 3e-4 and tc.checkpoint_interval == 100
     assert tc.pipeline_schedule == PipelineScheduleConfig.OneF1B(4)
     assert tc.mixed_precision.to_dict()["scaling_strategy"] == "Dynamic"
+
+
+def test_metrics_logger_jsonl_and_summary(tmp_path):
+    import json
+
+    from mtorus.utils.metrics import MetricsLogger, nvtx_range
+
+    p = tmp_path / "m.jsonl"
+    log = MetricsLogger(str(p), tokens_per_step=1000)
+    with nvtx_range("step"):
+        log.log(1, 7.0, 3e-4, grad_norm=1.5, overflow=False, loss_scale=65536.0)
+    log.log(2, 5.0, 3e-4, overflow=True, extra_key=3)
+    s = log.summary()
+    log.close()
+    recs = [json.loads(x) for x in open(p)]
+    assert [r["step"] for r in recs] == [1, 2] and recs[0]["grad_norm"] == 1.5 and recs[1]["extra_key"] == 3
+    assert recs[0]["loss_scale"] == 65536.0 and "tokens_per_s" in recs[0]
+    assert s["total_steps"] == 2 and s["avg_loss"] == 6.0 and s["overflow_count"] == 1
