@@ -85,6 +85,9 @@ int64_t symm_status(bool reset);
 void symm_rs_bucket(const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
                     int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot,
                     int64_t epoch, at::Tensor st, int64_t ctas, double inv_n);
+void symm_rs_bucket_mc(int64_t grads_mc, const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
+                       int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot, int64_t epoch,
+                       at::Tensor st, int64_t ctas, double inv_n);
 void symm_scalars_ar(const std::vector<int64_t>& scal, const std::vector<int64_t>& flags,
                      int64_t me, int64_t slot, int64_t epoch, at::Tensor st);
 void symm_adam_shard_ag(const at::Tensor& ranges, at::Tensor master, at::Tensor m, at::Tensor v,
@@ -147,6 +150,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quantize_blocks", &fp8_quantize_blocks);
   m.def("symm_status", &symm_status, py::arg("reset") = true);
   m.def("symm_rs_bucket", &symm_rs_bucket);
+  m.def("symm_rs_bucket_mc", &symm_rs_bucket_mc);
   m.def("symm_scalars_ar", &symm_scalars_ar);
   m.def("symm_adam_shard_ag", &symm_adam_shard_ag);
   m.def("symm_barrier", &symm_barrier);

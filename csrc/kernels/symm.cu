@@ -415,6 +415,49 @@ __global__ void __launch_bounds__(512) broadcast_mc_kernel(const uint4* __restri
   mc_publish_fence();
 }
 
+// ------------------------------------------------------------------ NVLS reduce-scatter (DP buckets)
+// rs_bucket with the per-peer loads replaced by one multimem.ld_reduce through the
+// gradient buffer's multicast address: the switch sums this rank's chunk over all
+// ranks, so each rank receives its chunk once instead of from n peers.  Same
+// outputs as rs_bucket (averaged chunk in the own buffer, sum of squares and the
+// non-finite count into st).
+__global__ void __launch_bounds__(512) rs_bucket_mc_kernel(uint64_t grads_mc, float* mine, PeerPtrs flags,
+                                                           uint32_t* my_flags, int me, int n, int64_t start,
+                                                           int64_t len, int64_t clen, int slot, uint32_t epoch,
+                                                           float inv_n, float* st, int* status) {
+  __shared__ float red[32];
+  if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 25)) return;
+  const int64_t c0 = start + (int64_t)me * clen;
+  const int64_t c1 = min(start + len, c0 + clen);
+  float acc2 = 0.f;
+  int bad = 0;
+  const int64_t nvec = (c1 > c0) ? (c1 - c0) / 4 : 0;
+  constexpr int U = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < nvec; i0 += U * stride) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (i0 + u * stride < nvec) mc_ld_reduce_f32(grads_mc + (uint64_t)(c0 + (i0 + u * stride) * 4) * 4, v[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= nvec) continue;
+      float4 t = v[u];
+      t.x *= inv_n; t.y *= inv_n; t.z *= inv_n; t.w *= inv_n;
+      *reinterpret_cast<float4*>(mine + c0 + i * 4) = t;
+      acc2 += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+      bad |= !(isfinite(t.x) && isfinite(t.y) && isfinite(t.z) && isfinite(t.w));
+    }
+  }
+  acc2 = block_sum(acc2, red);
+  const int anybad = __syncthreads_or(bad);
+  if (threadIdx.x == 0) {
+    atomicAdd(st + 0, acc2);
+    if (anybad) atomicAdd(st + 1, 1.f);
+  }
+}
+
 // ------------------------------------------------------------------ FP8 all-reduce (peer loads)
 // E4M3 / E5M2 codes: decode each peer's 16 codes to fp32, sum, re-encode with
 // saturation, store the result into every peer (reduce-scatter + all-gather).
@@ -507,6 +550,20 @@ void symm_rs_bucket(const std::vector<int64_t>& grads, const std::vector<int64_t
   rs_bucket_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(
       to_peers(grads), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, start,
       len, clen, (int)slot, (uint32_t)epoch, (float)inv_n, st.data_ptr<float>(), symm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+// NVLS variant of symm_rs_bucket (grads_mc: multicast address of the gradient buffer).
+void symm_rs_bucket_mc(int64_t grads_mc, const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
+                       int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot, int64_t epoch,
+                       at::Tensor st, int64_t ctas, double inv_n) {
+  MT_CHECK(grads_mc != 0 && grads_mc % 16 == 0, "rs_bucket_mc: no multicast address");
+  MT_CHECK(start % 4 == 0 && clen % 4 == 0 && len % 4 == 0, "rs_bucket_mc: 16-byte aligned bucket and chunks");
+  const int n = flags.size();
+  rs_bucket_mc_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(
+      (uint64_t)grads_mc, reinterpret_cast<float*>(grads[me]), to_peers(flags),
+      reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, start, len, clen, (int)slot, (uint32_t)epoch,
+      (float)inv_n, st.data_ptr<float>(), symm_status_ptr());
   MT_LAUNCH_CHECK();
 }
 

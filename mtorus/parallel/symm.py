@@ -124,6 +124,8 @@ class SymmBucketReducer:
         self.shard_numel = moff
         self.ranges = torch.tensor(ranges, dtype=torch.int64, device=flat.device).reshape(-1, 3)
         self._reserved = False
+        # NVLS reduce-scatter (multimem.ld_reduce) when asked for and the buffer has a multicast binding
+        self.nvls = os.environ.get("MTORUS_DP_NVLS") == "1" and self.flat.symm_grad.mc != 0
         self._reset()
 
     def _reset(self):
@@ -154,8 +156,13 @@ class SymmBucketReducer:
         ev.record()
         self.stream.wait_event(ev)
         with torch.cuda.stream(self.stream):
-            _cuda().symm_rs_bucket(self.flat.symm_grad.ptrs, self.ctx.flags.ptrs, self.me, s, e - s, self.clen[b],
-                                   b, self.epoch, self.state, self.ctas, 1.0 / self.world)
+            if self.nvls:
+                _cuda().symm_rs_bucket_mc(self.flat.symm_grad.mc, self.flat.symm_grad.ptrs, self.ctx.flags.ptrs,
+                                          self.me, s, e - s, self.clen[b], b, self.epoch, self.state, self.ctas,
+                                          1.0 / self.world)
+            else:
+                _cuda().symm_rs_bucket(self.flat.symm_grad.ptrs, self.ctx.flags.ptrs, self.me, s, e - s,
+                                       self.clen[b], b, self.epoch, self.state, self.ctas, 1.0 / self.world)
 
     def finish(self) -> None:
         while self.next_to_launch < len(self.plan):

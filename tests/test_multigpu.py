@@ -62,9 +62,13 @@ def test_symm_collectives_2gpu():
         assert torch.equal(o["halo"][:128], torch.full((128,), float(peer)))
 
 
-def _dp_body(rank, world, dp):
+def _dp_body(rank, world, dp, nvls=False):
+    import os
+
     import torch
 
+    if nvls:
+        os.environ["MTORUS_DP_NVLS"] = "1"
     from mtorus.models.gpt import GptConfig
     from mtorus.training.engine import GptTrainer
 
@@ -81,6 +85,8 @@ def _dp_body(rank, world, dp):
     st = 0
     if dp == "symm":
         st = tr.reducer.ctx.status()
+        if nvls and not tr.reducer.nvls:
+            st = -1  # no multicast binding on this fabric: nothing to compare
     return losses, w, st
 
 
@@ -95,6 +101,21 @@ def test_fused_dp_matches_nccl_baseline():
         assert torch.allclose(a[r][1], b[r][1], atol=2e-2, rtol=2e-2)
     # every rank holds the same weights after the all-gather
     assert torch.equal(b[0][1], b[1][1])
+
+
+@needs2
+def test_fused_dp_nvls_reduce_scatter_matches_peer_loads():
+    """The NVLS (multimem.ld_reduce) bucket reduce-scatter gives the same training
+    trajectory as the peer-load one."""
+    a = run_dist(_dp_body, 2, ("symm",), backend="nccl")
+    b = run_dist(_dp_body, 2, ("symm", True), backend="nccl")
+    if b[0][2] == -1:
+        pytest.skip("no NVLink multicast on this fabric")
+    for r in range(2):
+        assert b[r][2] == 0
+        for x, y in zip(a[r][0], b[r][0]):
+            assert abs(x - y) < 2e-2 * max(1.0, abs(x)), (a[r][0], b[r][0])
+        assert torch.allclose(a[r][1], b[r][1], atol=2e-2, rtol=2e-2)
 
 
 def _pp_body(rank, world, sched_name, ckpt_name):
