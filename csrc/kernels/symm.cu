@@ -366,6 +366,7 @@ __global__ void __launch_bounds__(512) allreduce_mc_kernel(uint64_t mc, PeerPtrs
                                                            int me, int n, int64_t numel, int slot,
                                                            uint32_t epoch, int* status) {
   if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 33)) return;
+  asm volatile("fence.proxy.alias;" ::: "memory");  // peers' unicast writes, read through the multicast alias
   const int64_t nvec = numel / (DT == 0 ? 4 : 8);
   const int64_t per = (nvec + n - 1) / n;
   const int64_t v0 = (int64_t)me * per, v1 = min(nvec, v0 + per);
@@ -427,6 +428,7 @@ __global__ void __launch_bounds__(512) rs_bucket_mc_kernel(uint64_t grads_mc, fl
                                                            float inv_n, float* st, int* status) {
   __shared__ float red[32];
   if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 25)) return;
+  asm volatile("fence.proxy.alias;" ::: "memory");  // peers' unicast writes, read through the multicast alias
   const int64_t c0 = start + (int64_t)me * clen;
   const int64_t c1 = min(start + len, c0 + clen);
   float acc2 = 0.f;
