@@ -88,6 +88,38 @@ def main():
         rows.append(r)
         print(json.dumps(r), flush=True)
         del A, B
+    # MXFP8 (1x32 UE8M0 block scales), K-major operands; cuBLAS through torch._scaled_mm with
+    # the same scale bytes (its MX scale layout is the tcgen05 atom layout mx_quantize writes)
+    from mtorus.ops import mxfp8 as MX
+
+    mx_cases = [("qkv_fwd_mx", T, 3 * d, d), ("out_fwd_mx", T, d, d), ("ffn1_fwd_mx", T, F, d),
+                ("ffn2_fwd_mx", T, d, F), ("square8k_mx", 8192, 8192, 8192)]
+    if args.case:
+        mx_cases = [c for c in mx_cases if c[0] == args.case]
+    for name, M, N, Kd in mx_cases:
+        a = MX.mx_quantize(torch.randn(M, Kd, device="cuda").bfloat16())
+        b = MX.mx_quantize(torch.randn(N, Kd, device="cuda").bfloat16())
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        mine = lambda: MX.gemm_mxfp8(a, b, out)
+        try:
+            sa = a.sf.view(torch.float8_e8m0fnu).reshape((M + 127) // 128 * 128, -1)
+            sb = b.sf.view(torch.float8_e8m0fnu).reshape((N + 127) // 128 * 128, -1)
+            ref = lambda: torch._scaled_mm(a.codes.view(torch.float8_e4m3fn), b.codes.view(torch.float8_e4m3fn).t(),
+                                           sa, sb, out_dtype=torch.bfloat16)
+            ref()
+        except (RuntimeError, AttributeError, TypeError) as e:
+            print(f"[{name}] torch._scaled_mm MX path unavailable: {e}", file=sys.stderr)
+            ref = None
+        flops = 2.0 * M * N * Kd
+        tm = timeit(mine, args.iters)
+        tr = timeit(ref, args.iters) if ref is not None else float("nan")
+        r = {"case": name, "M": M, "N": N, "K": Kd, "layout": "tn_mx", "mine_ms": round(tm, 4),
+             "cublas_ms": round(tr, 4) if tr == tr else None, "mine_tflops": round(flops / tm / 1e9, 1),
+             "cublas_tflops": round(flops / tr / 1e9, 1) if tr == tr else None,
+             "mine_frac_of_2x_measured_bf16_peak": round(flops / tm / 1e9 / (2 * peak), 3)}
+        rows.append(r)
+        print(json.dumps(r), flush=True)
+        del a, b, out
     for name, M, N, Kd, lay in cases:
         A = torch.randn(M, Kd, device="cuda").bfloat16() if lay != "wgrad" else torch.randn(Kd, M, device="cuda").bfloat16()
         if lay == "tn":

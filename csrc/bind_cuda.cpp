@@ -56,6 +56,11 @@ void gemm_fp8_act8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tens
                    const c10::optional<at::Tensor>& alpha2, bool beta,
                    const c10::optional<at::Tensor>& act8, const c10::optional<at::Tensor>& act8_scale,
                    const c10::optional<at::Tensor>& act8_amax, int64_t act8_fmt);
+void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const at::Tensor& B,
+                int64_t b_fmt, const at::Tensor& sfb, at::Tensor D, const c10::optional<at::Tensor>& bias,
+                const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
+                const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta);
+void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt, double fmax);
 // attention.cu
 std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H);
 at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
@@ -166,6 +171,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quantize_ar", &fp8_quantize_ar);
   m.def("layernorm_fwd_fp8", &layernorm_fwd_fp8);
   m.def("gemm_fp8_act8", &gemm_fp8_act8);
+  m.def("gemm_mxfp8", &gemm_mxfp8, py::arg("A"), py::arg("a_fmt"), py::arg("sfa"), py::arg("B"), py::arg("b_fmt"),
+        py::arg("sfb"), py::arg("D"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
+        py::arg("act") = py::none(), py::arg("aux") = py::none(), py::arg("alpha") = py::none(),
+        py::arg("beta") = false);
+  m.def("mx_quantize", &mx_quantize);
   m.def("fp8_amax_gather", &fp8_amax_gather);
   m.def("fp8_quantize_colsum", &fp8_quantize_colsum);
   m.def("attn_fwd", &attn_fwd);

@@ -11,6 +11,8 @@
 // 1-byte codes with 16-byte stores and folds max|x| into the slot's running
 // amax with one atomic per block.  After the step one tiny kernel rolls every
 // slot's ring buffer and recomputes scale / inverse scale for all slots at once.
+#include <cstring>
+
 #include "amax_publish.cuh"
 
 namespace mtorus {
@@ -259,6 +261,66 @@ __global__ void fp8_quantize_blocks_kernel(const float* __restrict__ x, uint8_t*
   }
 }
 
+// MXFP8 quantisation (OCP MX: 32-element blocks along a row, one UE8M0 scale each)
+// for the block-scaled GEMM.  The block's shared exponent X is the smallest integer
+// with amax <= fmax * 2^X, so no element saturates; codes = fp8(x * 2^-X) and the
+// scale byte is X + 127 (clamped to [0, 254]; 255 = NaN marks a block holding a
+// NaN or Inf, which the GEMM turns into NaN outputs).  An all-zero block gets X = 0.
+// X comes from the IEEE-754 fields: with amax = (1 + ma) 2^ea and fmax = (1 + mf) 2^ef,
+// X = ea - ef + (ma > mf).  Scales go to the tcgen05 atom layout (see gemm_mxfp8);
+// padding rows / K blocks of the last atoms get 127.  One thread per block of 32.
+template <int FMT>
+__global__ void __launch_bounds__(256) mx_quantize_kernel(const bf16* __restrict__ x, int64_t ldx,
+                                                          uint8_t* __restrict__ codes, uint8_t* __restrict__ sf,
+                                                          int R, int K, int nkb4, uint32_t fmax_bits) {
+  const int jper = nkb4 * 4;  // 32-blocks per padded row
+  const int64_t total = (int64_t)((R + 127) / 128) * 128 * jper;
+  const int kblocks = K / 32;
+  const int ef = (int)((fmax_bits >> 23) & 0xFF);
+  const uint32_t mf = fmax_bits & 0x7FFFFF;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(idx % jper);
+    const int r = (int)(idx / jper);
+    const int rr = r & 127;
+    const int64_t so = ((int64_t)(r >> 7) * nkb4 + (j >> 2)) * 512 + (rr & 31) * 16 + (rr >> 5) * 4 + (j & 3);
+    if (r >= R || j >= kblocks) {
+      sf[so] = 127;
+      continue;
+    }
+    const bf16x8* src = reinterpret_cast<const bf16x8*>(x + (int64_t)r * ldx + (int64_t)j * 32);
+    float v[32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) unpack8(src[q], v + 8 * q);
+    float amax = 0.f;
+    bool finite = true;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      amax = fmaxf(amax, fabsf(v[i]));
+      finite &= isfinite(v[i]);
+    }
+    int X = 0;
+    if (amax > 0.f) {
+      const uint32_t ua = __float_as_uint(amax);
+      X = (int)((ua >> 23) & 0xFF) - ef + ((ua & 0x7FFFFF) > mf ? 1 : 0);
+      X = max(-127, min(127, X));
+    }
+    const float inv = __uint_as_float((uint32_t)(127 - min(X, 126)) << 23);  // 2^-X (X <= 126 for finite fp32)
+    uint32_t w[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float* t = v + 4 * q;
+      const uint16_t lo = FMT == 0 ? cvt2_e4m3(t[0] * inv, t[1] * inv) : cvt2_e5m2(t[0] * inv, t[1] * inv);
+      const uint16_t hi = FMT == 0 ? cvt2_e4m3(t[2] * inv, t[3] * inv) : cvt2_e5m2(t[2] * inv, t[3] * inv);
+      w[q] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(codes + (int64_t)r * K + (int64_t)j * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    sf[so] = finite ? (uint8_t)(X + 127) : (uint8_t)255;
+  }
+}
+
 static int q_grid(size_t n, int per) {
   return (int)std::max<size_t>(1, std::min<size_t>((n / per + 255) / 256, (size_t)num_sms() * 8));
 }
@@ -405,6 +467,39 @@ void fp8_dequantize(const at::Tensor& q, at::Tensor out, const at::Tensor& inv_s
     fp8_dequantize_kernel<1><<<q_grid(n, 1), 256, 0, cur_stream()>>>(
         reinterpret_cast<const uint8_t*>(q.data_ptr()), out.data_ptr<float>(),
         inv_scale.data_ptr<float>(), n);
+  MT_LAUNCH_CHECK();
+}
+
+// x: bf16 [R, K] (unit inner stride, 16-byte aligned rows), codes: uint8 [R, K]
+// contiguous, sf: uint8 [ceil(R/128) * ceil(K/128) * 512]; fmax = the format maximum
+// the block amax is scaled to.
+void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt, double fmax) {
+  MT_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "mx_quantize: 2-D bf16 input");
+  const int64_t R = x.size(0), K = x.size(1);
+  MT_CHECK(K % 32 == 0, "mx_quantize: K must be a multiple of 32");
+  MT_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && (x.stride(0) * 2) % 16 == 0,
+           "mx_quantize: 16-byte aligned rows");
+  MT_CHECK(codes.element_size() == 1 && codes.is_contiguous() && codes.numel() == R * K &&
+               reinterpret_cast<uintptr_t>(codes.data_ptr()) % 16 == 0,
+           "mx_quantize: codes must be 16-byte aligned contiguous uint8 [R, K]");
+  const int64_t nkb4 = (K + 127) / 128;
+  MT_CHECK(sf.element_size() == 1 && sf.is_contiguous() && sf.numel() == (R + 127) / 128 * nkb4 * 512,
+           "mx_quantize: sf must be contiguous uint8 of ceil(R/128) * ceil(K/128) * 512 bytes");
+  MT_CHECK(fmt == 0 || fmt == 1, "mx_quantize: fmt 0 (E4M3) or 1 (E5M2)");
+  MT_CHECK(fmax > 0.0, "mx_quantize: fmax > 0");
+  if (R == 0 || K == 0) return;
+  const float fm = (float)fmax;
+  uint32_t fbits;
+  std::memcpy(&fbits, &fm, 4);
+  const int64_t total = (R + 127) / 128 * 128 * nkb4 * 4;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16));
+  const auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto* cp = reinterpret_cast<uint8_t*>(codes.data_ptr());
+  auto* sp = reinterpret_cast<uint8_t*>(sf.data_ptr());
+  if (fmt == 0)
+    mx_quantize_kernel<0><<<grid, 256, 0, cur_stream()>>>(xp, x.stride(0), cp, sp, (int)R, (int)K, (int)nkb4, fbits);
+  else
+    mx_quantize_kernel<1><<<grid, 256, 0, cur_stream()>>>(xp, x.stride(0), cp, sp, (int)R, (int)K, (int)nkb4, fbits);
   MT_LAUNCH_CHECK();
 }
 

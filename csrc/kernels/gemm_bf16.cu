@@ -347,12 +347,26 @@ constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 // 4 KB each) and two 32x32 bf16 GELU chunks, written to global memory by TMA.
 constexpr int P_EPI_D_BYTES = 4096, P_EPI_ACT_BYTES = 2048;
 constexpr int P_EPI_BYTES = 4 * 2 * (P_EPI_D_BYTES + P_EPI_ACT_BYTES);
+// MXFP8 (1x32 UE8M0 block scales) per stage: this CTA's 128-row SFA atom and the
+// pair tile's two 128-row SFB atoms (every CTA needs the scales of all 256 B rows,
+// since its tensor core multiplies its A rows with the whole B tile).  An atom holds
+// the scales of 128 rows x 4 K-blocks of 32 (one stage) in the tcgen05.cp layout:
+// byte (r % 32) * 16 + (r / 32) * 4 + k.
+constexpr int P_SF_ATOM = 512;
+constexpr int P_SF_BYTES = 3 * P_SF_ATOM;
+// TMEM in the MXFP8 kernel: the scale factors need 12 of the 512 columns, so the
+// second accumulator starts one 32-column chunk early and overlaps the first one's
+// last chunk; each epilogue reads the shared chunk first and signals "ovl" before the
+// next tile's MMAs may start.  Scales occupy the last 32 columns (SFA 4, SFB 8).
+constexpr int MX_ACC1_COL = P_BN - 32;
+constexpr int MX_SF_COL = 2 * P_BN - 32;
 
 struct PairSmem {
   uint64_t full[P_STAGES];   // leader: both CTAs' loads of a stage have landed
   uint64_t empty[P_STAGES];  // each CTA: the MMAs reading a stage are done
   uint64_t tfull[2];         // each CTA: accumulator buffer ready for the epilogue
   uint64_t tempty[2];        // leader: both epilogues finished with a buffer
+  uint64_t ovl;              // leader (MXFP8): both epilogues read the chunk shared by the two accumulators
   uint32_t tmem_base;
   int abort;
 };
@@ -372,13 +386,20 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n,
 // EB = operand element bytes: 2 (bf16, kind::f16) or 1 (fp8 E4M3/E5M2, kind::f8f6f4).
 // A k-block is always 128 bytes of K per row (64 bf16 / 128 fp8), so the stage
 // layout is identical and an fp8 stage carries twice the MMA work.
-template <int EB>
+// MX (EB == 1, K-major A and B only): kind::mxf8f6f4 with 1x32 UE8M0 block scales,
+// loaded per stage next to the operands and copied into TMEM by the MMA thread
+// (tcgen05.cp, ordered before the stage's MMAs, which read them); sf_kb = number of
+// 128-wide K blocks per 128-row block of the scale tensors.
+template <int EB, bool MX = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     const __grid_constant__ CUtensorMap tma_b,
                     const __grid_constant__ CUtensorMap tma_d,
-                    const __grid_constant__ CUtensorMap tma_act, int M, int N, int K, int a_mn,
-                    int b_mn, uint32_t idesc, GemmEpilogue ep, int* status) {
+                    const __grid_constant__ CUtensorMap tma_act,
+                    const __grid_constant__ CUtensorMap tma_sfa,
+                    const __grid_constant__ CUtensorMap tma_sfb, int M, int N, int K, int a_mn,
+                    int b_mn, int sf_kb, uint32_t idesc, GemmEpilogue ep, int* status) {
+  static_assert(!MX || EB == 1, "block scaling is for fp8 operands");
   constexpr int BK = 128 / EB;       // K elements per stage
   constexpr int MMA_K = 32 / EB;     // K elements per tcgen05.mma
   constexpr int MN_BOX = 128 / EB;   // MN elements per 128-byte swizzle row
@@ -387,7 +408,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* epi_smem = smem + P_STAGES * P_STAGE_BYTES;
-  PairSmem* ctl = reinterpret_cast<PairSmem*>(epi_smem + P_EPI_BYTES);
+  uint8_t* sf_smem = epi_smem + P_EPI_BYTES;
+  PairSmem* ctl = reinterpret_cast<PairSmem*>(sf_smem + (MX ? P_STAGES * P_SF_BYTES : 0));
+  constexpr uint32_t ACC1_COL = MX ? MX_ACC1_COL : P_BN;  // TMEM column of accumulator 1
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -406,6 +429,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(&ctl->tfull[b], 1);
       mbar_init(&ctl->tempty[b], 2 * 128);
     }
+    if constexpr (MX) mbar_init(&ctl->ovl, 2 * 128);
     ctl->abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
@@ -433,7 +457,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int n0 = nb * P_BN + (int)rank * (P_BN / 2);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort, status, 11)) break;
-          if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * P_STAGE_BYTES);
+          if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * (P_STAGE_BYTES + (MX ? P_SF_BYTES : 0)));
           uint8_t* sa = smem + stage * P_STAGE_BYTES;
           uint8_t* sb = sa + P_A_BYTES;
           if (!a_mn) {
@@ -449,6 +473,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < B_BOXES; ++j)
               tma_load_2d_pair(sb + j * (BK * 128), &tma_b, &ctl->full[stage], n0 + j * MN_BOX, kb * BK);
+          }
+          if constexpr (MX) {
+            // scale atoms: rows of 256 bytes, two rows per atom; boxes past the end read zeros
+            uint8_t* ssf = sf_smem + stage * P_SF_BYTES;
+            const int arb = m0 / 128, brb = (nb * P_BN) / 128;
+            tma_load_2d_pair(ssf, &tma_sfa, &ctl->full[stage], 0, (arb * sf_kb + kb) * 2);
+            tma_load_2d_pair(ssf + P_SF_ATOM, &tma_sfb, &ctl->full[stage], 0, (brb * sf_kb + kb) * 2);
+            tma_load_2d_pair(ssf + 2 * P_SF_ATOM, &tma_sfb, &ctl->full[stage], 0, ((brb + 1) * sf_kb + kb) * 2);
           }
           if (++stage == P_STAGES) {
             stage = 0;
@@ -467,8 +499,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int buf = local & 1;
         const uint32_t tphase = (local >> 1) & 1;
         if (!mbar_wait(&ctl->tempty[buf], tphase ^ 1, abort, status, 12)) break;
+        if constexpr (MX) {
+          // the previous tile's epilogue must have read the chunk both accumulators share
+          if (local > 0 && !mbar_wait(&ctl->ovl, (uint32_t)(local - 1) & 1, abort, status, 15)) break;
+        }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * P_BN;
+        const uint32_t d_tmem = tmem_base + buf * ACC1_COL;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&ctl->full[stage], phase, abort, status, 13)) {
@@ -478,13 +514,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
           const uint32_t sb = sa + P_A_BYTES;
+          if constexpr (MX) {
+            // stage scales -> TMEM (in order with the MMAs of this thread, so the previous
+            // stage's MMAs have read the old scales before these land)
+            const uint32_t ssf = smem_u32(sf_smem + stage * P_SF_BYTES);
+            tmem_cp_32x128b_x4_2sm(tmem_base + MX_SF_COL, make_sdesc(ssf, 0, 128, kSwizzleNone));
+            tmem_cp_32x128b_x4_2sm(tmem_base + MX_SF_COL + 4, make_sdesc(ssf + P_SF_ATOM, 0, 128, kSwizzleNone));
+            tmem_cp_32x128b_x4_2sm(tmem_base + MX_SF_COL + 8, make_sdesc(ssf + 2 * P_SF_ATOM, 0, 128, kSwizzleNone));
+          }
 #pragma unroll
           for (int k = 0; k < BK / MMA_K; ++k) {
             const uint64_t ad = a_mn ? make_sdesc(sa + k * MMA_K * 128, BK * 128, 1024, kSwizzle128B)
                                      : make_sdesc(sa + k * 32, 16, 1024, kSwizzle128B);
             const uint64_t bd = b_mn ? make_sdesc(sb + k * MMA_K * 128, BK * 128, 1024, kSwizzle128B)
                                      : make_sdesc(sb + k * 32, 16, 1024, kSwizzle128B);
-            if constexpr (EB == 2)
+            if constexpr (MX)
+              umma_mx_2sm(d_tmem, ad, bd, idesc_mx_sf_id(idesc, (uint32_t)k),
+                          (tmem_base + MX_SF_COL) | ((uint32_t)k << 30),
+                          (tmem_base + MX_SF_COL + 4) | ((uint32_t)k << 30), (kb | k) != 0 ? 1u : 0u);
+            else if constexpr (EB == 2)
               umma_f16_2sm(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
             else
               umma_f8_2sm(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
@@ -507,6 +555,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&ctl->tempty[0]), 0);
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&ctl->tempty[1]), 0);
+    const uint32_t ovl_leader = mapa_shared(smem_u32(&ctl->ovl), 0);
     uint8_t* dstage = epi_smem + q * 2 * P_EPI_D_BYTES;
     uint8_t* astage = epi_smem + 4 * 2 * P_EPI_D_BYTES + q * 2 * P_EPI_ACT_BYTES;
     const bool f32out = ep.out_f32 != 0;
@@ -525,11 +574,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int m = row0 + lane;
       const float alpha = (ep.alpha ? *ep.alpha : 1.f) * (ep.alpha2 ? *ep.alpha2 : 1.f);
 #pragma unroll 1
-      for (int c = 0; c < P_BN / 32; ++c, ++chunk_count) {
+      for (int i = 0; i < P_BN / 32; ++i, ++chunk_count) {
+        // MXFP8: accumulator 0 is read from its last chunk (the one accumulator 1 shares)
+        const int c = (MX && buf == 0) ? ((i + P_BN / 32 - 1) % (P_BN / 32)) : i;
         uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * P_BN + c * 32, r);
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC1_COL + c * 32, r);
         tmem_wait_ld();
-        if (c == P_BN / 32 - 1) {
+        if constexpr (MX) {
+          if (i == 0) {
+            tc_fence_before();
+            mbar_arrive_cluster(ovl_leader);
+          }
+        }
+        if (i == P_BN / 32 - 1) {
           // the whole accumulator buffer is in registers / smem now: release it
           tc_fence_before();
           mbar_arrive_cluster(buf ? tempty_leader1 : tempty_leader0);
@@ -777,10 +834,11 @@ static GemmEpilogue build_epilogue(at::Tensor& D, int64_t M, int64_t N,
   return ep;
 }
 
-template <int EB>
+template <int EB, bool MX = false>
 static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor& D,
                         const c10::optional<at::Tensor>& act, const GemmEpilogue& ep, int64_t M,
-                        int64_t N, int64_t K, uint32_t idesc) {
+                        int64_t N, int64_t K, uint32_t idesc, const at::Tensor* sfa = nullptr,
+                        const at::Tensor* sfb = nullptr) {
   const auto dt = EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const auto swz = CU_TENSOR_MAP_SWIZZLE_128B;
   constexpr uint32_t BK = 128 / EB, MN_BOX = 128 / EB;
@@ -801,19 +859,28 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
       : ep.act8 ? make_tma_2d(ep.act8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, N, 32, 32,
                               CU_TENSOR_MAP_SWIZZLE_NONE)
                 : td;
+  // scale tensors viewed as rows of 256 bytes (an atom is two rows); x is always 0
+  const int64_t sf_kb = (K + 127) / 128;
+  CUtensorMap tsfa = MX ? make_tma_2d(sfa->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256,
+                                      sfa->numel() / 256, 256, 256, 2, CU_TENSOR_MAP_SWIZZLE_NONE)
+                        : td;
+  CUtensorMap tsfb = MX ? make_tma_2d(sfb->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256,
+                                      sfb->numel() / 256, 256, 256, 2, CU_TENSOR_MAP_SWIZZLE_NONE)
+                        : td;
   const int num_tiles = (int)(((M + 2 * P_BM - 1) / (2 * P_BM)) * ((N + P_BN - 1) / P_BN));
   const int avail_pairs = std::max(1, (num_sms() - g_reserved_sms) / 2);
   const int pairs = std::min(num_tiles, avail_pairs);
-  const size_t smem = P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + sizeof(PairSmem) + 1024;
+  const size_t smem = P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + (MX ? P_STAGES * P_SF_BYTES : 0) +
+                      sizeof(PairSmem) + 1024;
   static bool attr_set = false;
   if (!attr_set) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB>,
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB, MX>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set = true;
   }
-  gemm_2sm_kernel<EB><<<2 * pairs, kThreads, smem, cur_stream()>>>(
-      ta, tb, td, tact, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, idesc, ep,
-      gemm_status_ptr());
+  gemm_2sm_kernel<EB, MX><<<2 * pairs, kThreads, smem, cur_stream()>>>(
+      ta, tb, td, tact, tsfa, tsfb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
+      idesc, ep, gemm_status_ptr());
   MT_LAUNCH_CHECK();
 }
 
@@ -920,6 +987,38 @@ void gemm_fp8_act8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tens
   ensure_context();
   launch_pair<1>(A, a_mn, B, b_mn, D, act, ep, M, N, K,
                  make_idesc_f8(2 * P_BM, P_BN, (int)a_fmt, (int)b_fmt, a_mn ? 1 : 0, b_mn ? 1 : 0));
+}
+
+// MXFP8 GEMM (tcgen05 kind::mxf8f6f4, 1x32 UE8M0 block scales, fp32 accumulate):
+// D = epilogue(alpha * sum_k (A[m,k] 2^sa[m,k/32]) (B[n,k] 2^sb[n,k/32])).  A [M, K] and
+// B [N, K] are K-major E4M3 / E5M2 codes; sfa / sfb hold one biased exponent byte
+// (UE8M0, 127 = 2^0) per 32-element K block in the tcgen05 atom layout written by
+// mx_quantize: [ceil(rows / 128)][ceil(K / 128)][512], byte (r % 32) * 16 + (r % 128 / 32) * 4
+// + (k / 32) % 4 of atom (r / 128, k / 128).
+void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const at::Tensor& B,
+                int64_t b_fmt, const at::Tensor& sfb, at::Tensor D, const c10::optional<at::Tensor>& bias,
+                const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
+                const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta) {
+  check_operand(A, "A", 1);
+  check_operand(B, "B", 1);
+  TORCH_CHECK((a_fmt == 0 || a_fmt == 1) && (b_fmt == 0 || b_fmt == 1), "gemm_mxfp8: formats are 0 (E4M3) / 1 (E5M2)");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K, "gemm_mxfp8: K mismatch ", K, " vs ", B.size(1));
+  TORCH_CHECK(K % 32 == 0, "gemm_mxfp8: K must be a multiple of 32 (one scale per 32 elements)");
+  const int64_t kb = (K + 127) / 128;
+  auto check_sf = [&](const at::Tensor& sf, int64_t rows, const char* name) {
+    TORCH_CHECK(sf.is_cuda() && sf.element_size() == 1 && sf.is_contiguous(), name, ": contiguous uint8 on the GPU");
+    TORCH_CHECK(sf.numel() == (rows + 127) / 128 * kb * P_SF_ATOM, name, ": expected ", (rows + 127) / 128 * kb * P_SF_ATOM,
+                " scale bytes (the mx_quantize layout), got ", sf.numel());
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(sf.data_ptr()) % 16 == 0, name, ": 16-byte aligned base required");
+  };
+  check_sf(sfa, M, "sfa");
+  check_sf(sfb, N, "sfb");
+  GemmEpilogue ep = build_epilogue(D, M, N, bias, residual, act, aux, alpha, c10::nullopt, beta);
+  if (M == 0 || N == 0) return;
+  ensure_context();
+  launch_pair<1, true>(A, false, B, false, D, act, ep, M, N, K, make_idesc_mx(2 * P_BM, P_BN, (int)a_fmt, (int)b_fmt),
+                       &sfa, &sfb);
 }
 
 }  // namespace mtorus

@@ -254,6 +254,41 @@ __host__ __device__ constexpr uint32_t make_idesc_f8(int M, int N, int a_fmt, in
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// kind::mxf8f6f4 with 1x32 block scaling: each 32-element K block of a row of A
+// (column of B) carries a UE8M0 scale read from TMEM.  sfa / sfb are TMEM column
+// addresses whose bits 31:30 select the byte of the 32-bit TMEM word (the scale
+// of the k-th MMA of a 4-MMA group); the same byte index goes into the
+// instruction descriptor's scale-factor ID fields (make_idesc_mx).
+__device__ __forceinline__ void umma_mx_2sm(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+// Shared memory -> TMEM copy of a 32-row x 16-byte matrix, replicated into all four
+// 32-lane sub-partitions (lane l, l+32, l+64, l+96 receive row l; 4 columns).  With
+// cta_group::2 each CTA of the pair copies from its own shared memory into its own
+// TMEM.  `sdesc` is a no-swizzle K-major descriptor (8-row core matrices, SBO 128).
+__device__ __forceinline__ void tmem_cp_32x128b_x4_2sm(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// Instruction descriptor for kind::mxf8f6f4 block-scaled MMAs (K-major A and B):
+// b_sf_id [4,6), a_format [7,10), b_format [10,13) (0 = E4M3, 1 = E5M2), N>>3 [17,23),
+// scale format [23] = 1 (UE8M0), M>>4 [24,29), a_sf_id [29,31).  There is no
+// accumulator-format field: block-scaled MMAs always accumulate in fp32.
+__host__ __device__ constexpr uint32_t make_idesc_mx(int M, int N, int a_fmt, int b_fmt) {
+  return ((uint32_t)a_fmt << 7) | ((uint32_t)b_fmt << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
+         ((uint32_t)(M >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_mx_sf_id(uint32_t idesc, uint32_t k) {
+  return idesc | (k << 29) | (k << 4);
+}
+
 // Arrive (once all prior tcgen05 ops of this thread finish) on the mbarrier at the
 // same shared offset in every CTA of `cta_mask`.
 __device__ __forceinline__ void umma_commit_2sm_mc(uint64_t* bar, uint16_t cta_mask) {

@@ -1,0 +1,152 @@
+"""MXFP8: FP8 with one power-of-two scale per 32-element block (OCP microscaling),
+for the tcgen05 ``kind::mxf8f6f4`` block-scaled GEMM.
+
+The reference's block quantiser (``to_fp8_per_block``, crates/mt-core/src/precision/
+quantize.rs:68-97) keeps one fp32 scale per block of any size on the host.  The
+hardware form kept here has 32-element blocks along the GEMM's K dimension and an
+8-bit biased exponent (UE8M0) per block, which the tensor core applies inside the
+MMA, so a GEMM over block-scaled operands needs no dequantise pass and no epilogue
+scale.
+
+Block rule: X = the smallest integer with ``amax <= fmax * 2**X`` (so no element
+saturates); the codes are ``fp8(x * 2**-X)`` rounded to nearest even, and the scale
+byte is ``X + 127`` (clamped to [0, 254]).  An all-zero block gets X = 0; a block
+holding a NaN or an Inf gets the UE8M0 NaN byte 255, which turns every output it
+touches into NaN (the overflow check downstream sees it).  ``fmax`` is the
+format's largest finite value, 448 (E4M3) or 57344 (E5M2).
+
+Scale layout (what ``tcgen05.cp`` copies into tensor memory): for an operand of
+R rows and K columns the scales form atoms of 128 rows x 4 K-blocks (512 bytes),
+stored row-block-major ``[ceil(R/128)][ceil(K/128)][512]``; inside an atom the
+scale of row r and K-block j sits at byte ``(r % 32) * 16 + (r % 128 // 32) * 4 + j % 4``.
+Padding rows and K-blocks hold 127 (a scale of 1).
+
+``mx_quantize_ref`` / ``mx_dequantize`` are plain PyTorch on any device (the oracle
+for the CUDA quantiser and GEMM); ``mx_quantize`` and ``gemm_mxfp8`` run the sm_100a
+kernels on CUDA tensors.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from .._ext import cuda as _cuda
+
+E4M3, E5M2 = 0, 1
+MX_FMT_MAX = {E4M3: 448.0, E5M2: 57344.0}
+_TORCH_FP8 = {E4M3: torch.float8_e4m3fn, E5M2: torch.float8_e5m2}
+BLOCK = 32
+
+
+def sf_numel(rows: int, k: int) -> int:
+    """Bytes of the scale tensor of a [rows, k] operand."""
+    return (rows + 127) // 128 * ((k + 127) // 128) * 512
+
+
+def sf_offsets(rows: int, k: int, device=None) -> torch.Tensor:
+    """int64 [rows, k // 32]: byte offset of each block's scale in the atom layout."""
+    nkb4 = (k + 127) // 128
+    r = torch.arange(rows, device=device, dtype=torch.int64)[:, None]
+    j = torch.arange(k // BLOCK, device=device, dtype=torch.int64)[None, :]
+    return ((r // 128) * nkb4 + j // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + j % 4
+
+
+@dataclass
+class MxTensor:
+    """Block-scaled FP8 operand: ``codes`` uint8 [R, K], ``sf`` uint8 atoms, format id."""
+    codes: torch.Tensor
+    sf: torch.Tensor
+    fmt: int
+
+    @property
+    def shape(self):
+        return tuple(self.codes.shape)
+
+    def dequantize(self) -> torch.Tensor:
+        return mx_dequantize(self)
+
+
+def _block_exponent(amax: torch.Tensor, fmax: float) -> torch.Tensor:
+    """Smallest integer X with amax <= fmax * 2**X, from the IEEE-754 fields (exact)."""
+    fbits = torch.tensor([fmax], dtype=torch.float32).view(torch.int32).item()
+    ef, mf = (fbits >> 23) & 0xFF, fbits & 0x7FFFFF
+    ua = amax.contiguous().view(torch.int32)
+    ea, ma = (ua >> 23) & 0xFF, ua & 0x7FFFFF
+    x = ea - ef + (ma > mf).to(torch.int32)
+    x = x.clamp(-127, 127)
+    return torch.where(amax > 0, x, torch.zeros_like(x))
+
+
+def mx_quantize_ref(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = None) -> MxTensor:
+    """Plain-PyTorch MXFP8 quantisation of a 2-D tensor (K a multiple of 32)."""
+    if x.dim() != 2 or x.shape[1] % BLOCK:
+        raise ValueError("mx_quantize: 2-D input with K a multiple of 32 expected")
+    fmax = float(MX_FMT_MAX[fmt] if fmax is None else fmax)
+    R, K = x.shape
+    xb = x.float().reshape(R, K // BLOCK, BLOCK)
+    amax = xb.abs().amax(-1)
+    finite = torch.isfinite(xb).all(-1)
+    amax = torch.where(finite, amax, torch.zeros_like(amax))
+    X = _block_exponent(amax, fmax)
+    inv = torch.ldexp(torch.ones_like(amax), (-X).float())
+    scaled = (xb * inv[..., None]).reshape(R, K)
+    codes = scaled.to(_TORCH_FP8[fmt]).view(torch.uint8)
+    sf = torch.full((sf_numel(R, K),), 127, dtype=torch.uint8, device=x.device)
+    byte = torch.where(finite, X + 127, torch.full_like(X, 255)).to(torch.uint8)
+    sf[sf_offsets(R, K, x.device).reshape(-1)] = byte.reshape(-1)
+    return MxTensor(codes.contiguous(), sf, int(fmt))
+
+
+def mx_dequantize(t: MxTensor) -> torch.Tensor:
+    """fp32 values of a block-scaled operand (NaN where the scale byte is 255)."""
+    R, K = t.codes.shape
+    vals = t.codes.view(_TORCH_FP8[t.fmt]).float().reshape(R, K // BLOCK, BLOCK)
+    byte = t.sf[sf_offsets(R, K, t.codes.device)].to(torch.int32)
+    scale = torch.ldexp(torch.ones(byte.shape, device=byte.device), (byte - 127).float())
+    scale = torch.where(byte == 255, torch.full_like(scale, float("nan")), scale)
+    return (vals * scale[..., None]).reshape(R, K)
+
+
+def mx_quantize(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = None) -> MxTensor:
+    """MXFP8 quantisation: the sm_100a kernel for CUDA tensors, the reference on the CPU."""
+    if not x.is_cuda:
+        return mx_quantize_ref(x, fmt, fmax)
+    if x.dim() != 2 or x.shape[1] % BLOCK:
+        raise ValueError("mx_quantize: 2-D input with K a multiple of 32 expected")
+    fmax = float(MX_FMT_MAX[fmt] if fmax is None else fmax)
+    x = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    R, K = x.shape
+    codes = torch.empty((R, K), dtype=torch.uint8, device=x.device)
+    sf = torch.empty(sf_numel(R, K), dtype=torch.uint8, device=x.device)
+    _cuda().mx_quantize(x, codes, sf, int(fmt), fmax)
+    return MxTensor(codes, sf, int(fmt))
+
+
+def gemm_mxfp8(a: MxTensor, b: MxTensor, out: Optional[torch.Tensor] = None, *, bias=None, residual=None,
+               act=None, aux=None, alpha=None, accumulate: bool = False,
+               out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """out[M, N] = epilogue(alpha * A . B^T) with A [M, K] and B [N, K] block-scaled
+    (both K-major); epilogue as in ``ops.kernels.gemm`` (bias, residual, GELU / dGELU,
+    fp32 accumulate)."""
+    M, K = a.codes.shape
+    N, Kb = b.codes.shape
+    if K != Kb:
+        raise ValueError(f"gemm_mxfp8: K mismatch {K} vs {Kb}")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.codes.device)
+    _cuda().gemm_mxfp8(a.codes, a.fmt, a.sf, b.codes, b.fmt, b.sf, out, bias, residual, act, aux, alpha,
+                       bool(accumulate))
+    return out
+
+
+def gemm_mxfp8_ref(a: MxTensor, b: MxTensor) -> torch.Tensor:
+    """fp32 oracle of ``gemm_mxfp8``: the product of the dequantised operands."""
+    return mx_dequantize(a) @ mx_dequantize(b).t()
+
+
+__all__ = ["E4M3", "E5M2", "MX_FMT_MAX", "MxTensor", "sf_numel", "sf_offsets", "mx_quantize", "mx_quantize_ref",
+           "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_ref"]

@@ -1,0 +1,147 @@
+"""MXFP8 block-scaled quantisation (1x32 blocks, UE8M0 scales) and the tcgen05
+block-scaled GEMM.
+
+CPU tests pin the reference quantiser: the block-exponent rule, the round trip,
+special blocks and the tensor-memory atom layout of the scales.  The GPU tests
+compare the CUDA quantiser with the reference byte for byte and the GEMM with an
+fp32 product of the dequantised operands.  The GPU tests of this file are opt-in
+(``MTORUS_MXFP8_GPU_TESTS=1``): the block-scaled GEMM has not been run on a B200
+yet, and the default GPU suite only holds kernels that have.
+"""
+import os
+
+import pytest
+import torch
+
+from mtorus.ops.mxfp8 import (E4M3, E5M2, MX_FMT_MAX, MxTensor, gemm_mxfp8, gemm_mxfp8_ref, mx_dequantize,
+                              mx_quantize, mx_quantize_ref, sf_numel, sf_offsets)
+
+
+def _blocky(R, K, seed=0):
+    """Rows whose 32-blocks span many magnitudes (2^-20 .. 2^20)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(R, K // 32, 32, generator=g)
+    mag = torch.ldexp(torch.ones(R, K // 32, 1), torch.randint(-20, 21, (R, K // 32, 1), generator=g).float())
+    return (x * mag).reshape(R, K)
+
+
+def test_sf_layout_is_a_permutation_of_the_valid_slots():
+    R, K = 300, 544  # partial row block and partial K atom
+    off = sf_offsets(R, K).reshape(-1)
+    assert off.unique().numel() == off.numel()
+    assert int(off.min()) >= 0 and int(off.max()) < sf_numel(R, K)
+    assert sf_numel(R, K) == 3 * 5 * 512
+    # row r, block j of atom (0, 0): (r % 32) * 16 + (r // 32) * 4 + j
+    assert int(sf_offsets(128, 128)[37, 2]) == 5 * 16 + 1 * 4 + 2
+    # next K atom of the same row block, then the next row block
+    assert int(sf_offsets(256, 256)[0, 4]) == 512
+    assert int(sf_offsets(256, 256)[128, 0]) == 2 * 512
+
+
+@pytest.mark.parametrize("fmt", [E4M3, E5M2])
+def test_block_exponent_rule_and_round_trip(fmt):
+    R, K = 160, 256
+    x = _blocky(R, K, seed=fmt)
+    t = mx_quantize_ref(x, fmt)
+    fmax = MX_FMT_MAX[fmt]
+    byte = t.sf[sf_offsets(R, K)].long()
+    X = byte - 127
+    amax = x.reshape(R, K // 32, 32).abs().amax(-1).double()
+    scaled_max = amax * torch.pow(2.0, -X.double())
+    # smallest X with amax <= fmax * 2^X: amax * 2^-X lies in (fmax / 2, fmax]
+    assert bool((scaled_max <= fmax).all()) and bool((scaled_max > fmax / 2).all())
+    y = mx_dequantize(t)
+    rel = 2.0 ** -4 if fmt == E4M3 else 2.0 ** -3  # half an ulp of a 3 / 2-bit mantissa
+    sub = (2.0 ** -9 if fmt == E4M3 else 2.0 ** -16) * torch.pow(2.0, X.double())  # subnormal spacing / 2
+    bound = rel * x.abs().double() + sub.repeat_interleave(32, dim=1)
+    assert bool(((y.double() - x.double()).abs() <= bound).all())
+
+
+def test_padding_zero_and_nonfinite_blocks():
+    R, K = 130, 96  # 2 row blocks (second mostly padding), 3 of the 4 K-blocks of the atom
+    x = torch.randn(R, K)
+    x[3, 32:64] = 0.0
+    x[5, 7] = float("nan")
+    x[6, 70] = float("inf")
+    t = mx_quantize_ref(x, E4M3)
+    off = sf_offsets(R, K)
+    assert int(t.sf[off[3, 1]]) == 127
+    assert int(t.codes[3, 32:64].count_nonzero()) == 0
+    assert int(t.sf[off[5, 0]]) == 255 and int(t.sf[off[6, 2]]) == 255
+    used = torch.zeros(sf_numel(R, K), dtype=torch.bool)
+    used[off.reshape(-1)] = True
+    assert bool((t.sf[~used] == 127).all())
+    y = mx_dequantize(t)
+    assert bool(torch.isnan(y[5, :32]).all()) and bool(torch.isfinite(y[4]).all())
+
+
+def test_cpu_entry_point_uses_the_reference():
+    x = _blocky(64, 128, seed=3)
+    a, b = mx_quantize(x, E4M3), mx_quantize_ref(x, E4M3)
+    assert torch.equal(a.codes, b.codes) and torch.equal(a.sf, b.sf)
+
+
+def test_reference_gemm_matches_fp32_product_of_dequantised_operands():
+    a = mx_quantize_ref(_blocky(64, 96, seed=4) * 1e-3, E4M3)
+    b = mx_quantize_ref(_blocky(48, 96, seed=5) * 1e-3, E4M3)
+    da, db = mx_dequantize(a).double(), mx_dequantize(b).double()
+    ref = da @ db.t()
+    mag = da.abs() @ db.abs().t()  # fp32 summation error is relative to this, not to |ref|
+    assert bool(((gemm_mxfp8_ref(a, b).double() - ref).abs() <= 1e-5 * mag).all())
+
+
+# ---------------------------------------------------------------- GPU (opt-in)
+_gpu = pytest.mark.skipif(os.environ.get("MTORUS_MXFP8_GPU_TESTS") != "1",
+                          reason="block-scaled GEMM not yet run on a B200 (MTORUS_MXFP8_GPU_TESTS=1 runs it)")
+
+
+@pytest.mark.gpu
+@_gpu
+@pytest.mark.parametrize("fmt", [E4M3, E5M2])
+def test_cuda_quantiser_matches_reference(fmt):
+    x = _blocky(300, 544, seed=7).to(torch.bfloat16)
+    x[11, 40] = float("nan")
+    ref = mx_quantize_ref(x.float(), fmt)
+    got = mx_quantize(x.cuda(), fmt)
+    assert torch.equal(got.sf.cpu(), ref.sf)
+    finite_rows = torch.isfinite(x.float()).all(1)
+    assert torch.equal(got.codes.cpu()[finite_rows], ref.codes[finite_rows])
+
+
+@pytest.mark.gpu
+@_gpu
+@pytest.mark.parametrize("shape,fmts", [((512, 512, 512), (E4M3, E4M3)), ((300, 264, 544), (E4M3, E4M3)),
+                                        ((256, 2048, 1024), (E5M2, E4M3))])
+def test_block_scaled_gemm_matches_fp32_oracle(shape, fmts):
+    M, N, K = shape
+    g = torch.Generator().manual_seed(M + N + K)
+    xa = (_blocky(M, K, seed=1) * 1e-4).to(torch.bfloat16)
+    xb = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    a, b = mx_quantize(xa.cuda(), fmts[0]), mx_quantize(xb.cuda(), fmts[1])
+    ref = gemm_mxfp8_ref(MxTensor(a.codes.cpu(), a.sf.cpu(), a.fmt), MxTensor(b.codes.cpu(), b.sf.cpu(), b.fmt))
+    da = mx_dequantize(MxTensor(a.codes.cpu(), a.sf.cpu(), a.fmt)).double()
+    db = mx_dequantize(MxTensor(b.codes.cpu(), b.sf.cpu(), b.fmt)).double()
+    mag = (da.abs() @ db.abs().t()).float()
+    out = gemm_mxfp8(a, b, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    err = (out.cpu() - ref).abs()
+    assert bool((err <= 1e-5 * mag + 1e-30).all()), float((err / mag.clamp_min(1e-30)).max())
+    out16 = gemm_mxfp8(a, b).float().cpu()
+    assert bool(((out16 - ref).abs() <= 1e-2 * ref.abs() + 1e-5 * mag + 1e-30).all())
+
+
+@pytest.mark.gpu
+@_gpu
+def test_block_scaled_gemm_agrees_with_cublas_mx():
+    """cuBLAS MX GEMM (torch._scaled_mm with e8m0 scales) reads the same scale layout."""
+    M, N, K = 512, 768, 1024
+    a = mx_quantize((torch.randn(M, K) * 3).to(torch.bfloat16).cuda())
+    b = mx_quantize((torch.randn(N, K) * 0.02).to(torch.bfloat16).cuda())
+    try:
+        lib = torch._scaled_mm(a.codes.view(torch.float8_e4m3fn), b.codes.view(torch.float8_e4m3fn).t(),
+                               a.sf.view(torch.float8_e8m0fnu).reshape(M, -1),
+                               b.sf.view(torch.float8_e8m0fnu).reshape(N, -1), out_dtype=torch.float32)
+    except (RuntimeError, AttributeError, TypeError) as e:
+        pytest.skip(f"torch._scaled_mm has no MX path here: {e}")
+    out = gemm_mxfp8(a, b, out_dtype=torch.float32)
+    assert torch.allclose(out, lib, rtol=1e-4, atol=1e-4 * float(lib.abs().max()))
