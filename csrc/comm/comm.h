@@ -20,6 +20,7 @@
 //   * TcpCommunicator   -- sockets (tcp.cpp).
 #pragma once
 
+#include <atomic>
 #include <chrono>
 #include <condition_variable>
 #include <cstdint>
@@ -223,8 +224,8 @@ class TcpCommunicator : public Communicator {
 
  private:
   struct Peer {
-    int fd = -1;
-    std::mutex send_mu, recv_mu;
+    std::atomic<int> fd{-1};
+    std::mutex send_mu, recv_mu;  // one sender / one receiver per socket at a time
   };
   Peer* peer(size_t r);
   void accept_loop();

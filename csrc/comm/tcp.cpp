@@ -170,12 +170,18 @@ void TcpCommunicator::close() {
   if (acceptor_ && acceptor_->joinable()) acceptor_->join();
   if (listen_fd_ >= 0) ::close(listen_fd_);
   listen_fd_ = -1;
-  for (auto& p : peers_)
-    if (p->fd >= 0) {
-      ::shutdown(p->fd, SHUT_RDWR);
-      ::close(p->fd);
-      p->fd = -1;
-    }
+  // Shut every socket down first: that wakes a thread of this rank blocked in
+  // send / recv on it (EOF or EPIPE).  Close the descriptor only once no thread is
+  // inside send / recv on it, so that no call can reach a reused descriptor.
+  for (auto& p : peers_) {
+    const int fd = p->fd.load();
+    if (fd >= 0) ::shutdown(fd, SHUT_RDWR);
+  }
+  for (auto& p : peers_) {
+    std::scoped_lock lk(p->send_mu, p->recv_mu);
+    const int fd = p->fd.exchange(-1);
+    if (fd >= 0) ::close(fd);
+  }
 }
 
 void TcpCommunicator::accept_loop() {
