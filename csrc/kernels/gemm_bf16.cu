@@ -19,6 +19,7 @@
 //     the main loop of tile i+1.
 // All mbarrier waits are bounded (see sm100.cuh); a timeout raises the status word.
 #include <cstdlib>
+#include <cstring>
 
 #include "amax_publish.cuh"
 #include "sm100.cuh"
@@ -361,6 +362,19 @@ constexpr int P_SF_BYTES = 3 * P_SF_ATOM;
 constexpr int MX_ACC1_COL = P_BN - 32;
 constexpr int MX_SF_COL = 2 * P_BN - 32;
 
+// Row-sharded B read straight from its owners' memory: the parameter all-gather
+// fused into the GEMM that consumes the parameters.  Rank p owns rows
+// [p * shard_rows, (p + 1) * shard_rows) of B's storage (N rows for a K-major B,
+// K rows for an MN-major one) in its symmetric buffer, and m[p] maps that buffer
+// with the local map's shape and box.  Each B tile is a plain TMA load from the
+// owner (never a multicast load), so a remote tile crosses NVLink once per CTA
+// that needs it and lands in this SM's shared memory.  n == 0: B is local.
+struct PeerMapsB {
+  CUtensorMap m[8];
+  int n;
+  int shard_rows;
+};
+
 struct PairSmem {
   uint64_t full[P_STAGES];   // leader: both CTAs' loads of a stage have landed
   uint64_t empty[P_STAGES];  // each CTA: the MMAs reading a stage are done
@@ -397,7 +411,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tma_d,
                     const __grid_constant__ CUtensorMap tma_act,
                     const __grid_constant__ CUtensorMap tma_sfa,
-                    const __grid_constant__ CUtensorMap tma_sfb, int M, int N, int K, int a_mn,
+                    const __grid_constant__ CUtensorMap tma_sfb,
+                    const __grid_constant__ PeerMapsB peer_b, int M, int N, int K, int a_mn,
                     int b_mn, int sf_kb, uint32_t idesc, GemmEpilogue ep, int* status) {
   static_assert(!MX || EB == 1, "block scaling is for fp8 operands");
   constexpr int BK = 128 / EB;       // K elements per stage
@@ -467,12 +482,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int j = 0; j < A_BOXES; ++j)
               tma_load_2d_pair(sa + j * (BK * 128), &tma_a, &ctl->full[stage], m0 + j * MN_BOX, kb * BK);
           }
+          const CUtensorMap* map_b = &tma_b;
+          if (peer_b.n > 0)  // owner of this CTA's B rows (K-major) or of this k-block (MN-major)
+            map_b = &peer_b.m[min(peer_b.n - 1, (b_mn ? kb * BK : n0) / peer_b.shard_rows)];
           if (!b_mn) {
-            tma_load_2d_pair(sb, &tma_b, &ctl->full[stage], kb * BK, n0);
+            tma_load_2d_pair(sb, map_b, &ctl->full[stage], kb * BK, n0);
           } else {
 #pragma unroll
             for (int j = 0; j < B_BOXES; ++j)
-              tma_load_2d_pair(sb + j * (BK * 128), &tma_b, &ctl->full[stage], n0 + j * MN_BOX, kb * BK);
+              tma_load_2d_pair(sb + j * (BK * 128), map_b, &ctl->full[stage], n0 + j * MN_BOX, kb * BK);
           }
           if constexpr (MX) {
             // scale atoms: rows of 256 bytes, two rows per atom; boxes past the end read zeros
@@ -838,15 +856,26 @@ template <int EB, bool MX = false>
 static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor& D,
                         const c10::optional<at::Tensor>& act, const GemmEpilogue& ep, int64_t M,
                         int64_t N, int64_t K, uint32_t idesc, const at::Tensor* sfa = nullptr,
-                        const at::Tensor* sfb = nullptr) {
+                        const at::Tensor* sfb = nullptr, const std::vector<int64_t>* b_peers = nullptr,
+                        int64_t shard_rows = 0) {
   const auto dt = EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const auto swz = CU_TENSOR_MAP_SWIZZLE_128B;
   constexpr uint32_t BK = 128 / EB, MN_BOX = 128 / EB;
   // per-CTA boxes: 128 rows of A and 128 rows of B (the pair covers 256 x 256)
   CUtensorMap ta = a_mn ? make_tma_2d(A.data_ptr(), dt, EB, M, K, A.stride(0), MN_BOX, BK, swz)
                         : make_tma_2d(A.data_ptr(), dt, EB, K, M, A.stride(0), BK, P_BM, swz);
-  CUtensorMap tb = b_mn ? make_tma_2d(B.data_ptr(), dt, EB, N, K, B.stride(0), MN_BOX, BK, swz)
-                        : make_tma_2d(B.data_ptr(), dt, EB, K, N, B.stride(0), BK, P_BN / 2, swz);
+  auto map_b = [&](const void* ptr) {
+    return b_mn ? make_tma_2d(ptr, dt, EB, N, K, B.stride(0), MN_BOX, BK, swz)
+                : make_tma_2d(ptr, dt, EB, K, N, B.stride(0), BK, P_BN / 2, swz);
+  };
+  CUtensorMap tb = map_b(B.data_ptr());
+  PeerMapsB pb;
+  std::memset(&pb, 0, sizeof(pb));
+  if (b_peers) {
+    pb.n = (int)b_peers->size();
+    pb.shard_rows = (int)shard_rows;
+    for (int p = 0; p < pb.n; ++p) pb.m[p] = map_b(reinterpret_cast<const void*>((*b_peers)[p]));
+  }
   const bool out_f32 = ep.out_f32 != 0;
   CUtensorMap td = out_f32
       ? make_tma_2d(D.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, D.stride(0), 32, 32,
@@ -879,7 +908,7 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
     attr_set = true;
   }
   gemm_2sm_kernel<EB, MX><<<2 * pairs, kThreads, smem, cur_stream()>>>(
-      ta, tb, td, tact, tsfa, tsfb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
+      ta, tb, td, tact, tsfa, tsfb, pb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
       idesc, ep, gemm_status_ptr());
   MT_LAUNCH_CHECK();
 }
@@ -987,6 +1016,39 @@ void gemm_fp8_act8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tens
   ensure_context();
   launch_pair<1>(A, a_mn, B, b_mn, D, act, ep, M, N, K,
                  make_idesc_f8(2 * P_BM, P_BN, (int)a_fmt, (int)b_fmt, a_mn ? 1 : 0, b_mn ? 1 : 0));
+}
+
+// FP8 GEMM whose B operand is sharded by storage rows over the ranks of a symmetric
+// buffer and read from each owner's memory inside the kernel (see PeerMapsB): the
+// all-gather of B fused into the GEMM.  B is this rank's view of the full buffer
+// (shape and strides of the gathered operand); b_peers[p] is rank p's address of the
+// same bytes; rank p's rows are [p * shard_rows, (p + 1) * shard_rows).  The caller
+// orders the owners' writes before the launch (a barrier over the ranks).
+void gemm_fp8_gather_b(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
+                       int64_t b_fmt, const std::vector<int64_t>& b_peers, int64_t shard_rows, at::Tensor D,
+                       const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+                       const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
+                       const c10::optional<at::Tensor>& alpha, const c10::optional<at::Tensor>& alpha2, bool beta) {
+  check_operand(A, "A", 1);
+  check_operand(B, "B", 1);
+  TORCH_CHECK((a_fmt == 0 || a_fmt == 1) && (b_fmt == 0 || b_fmt == 1), "gemm_fp8_gather_b: formats 0 / 1");
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  TORCH_CHECK((b_mn ? B.size(0) : B.size(1)) == K, "gemm_fp8_gather_b: K mismatch");
+  TORCH_CHECK(K % 16 == 0 && (!a_mn || M % 16 == 0) && (!b_mn || N % 16 == 0), "gemm_fp8_gather_b: alignment");
+  const int64_t n = (int64_t)b_peers.size();
+  TORCH_CHECK(n >= 1 && n <= 8, "gemm_fp8_gather_b: 1..8 owners");
+  // a CTA's B box (128 rows of a K-major B) or k-block (128 K of an MN-major B) has one owner
+  TORCH_CHECK(shard_rows > 0 && shard_rows % 128 == 0, "gemm_fp8_gather_b: shard_rows must be a multiple of 128");
+  TORCH_CHECK(B.size(0) <= n * shard_rows, "gemm_fp8_gather_b: the shards do not cover B's rows");
+  for (int64_t p : b_peers) TORCH_CHECK(p != 0 && p % 16 == 0, "gemm_fp8_gather_b: 16-byte aligned peer addresses");
+  GemmEpilogue ep = build_epilogue(D, M, N, bias, residual, act, aux, alpha, alpha2, beta);
+  if (M == 0 || N == 0) return;
+  ensure_context();
+  launch_pair<1>(A, a_mn, B, b_mn, D, act, ep, M, N, K,
+                 make_idesc_f8(2 * P_BM, P_BN, (int)a_fmt, (int)b_fmt, a_mn ? 1 : 0, b_mn ? 1 : 0), nullptr, nullptr,
+                 &b_peers, shard_rows);
 }
 
 // MXFP8 GEMM (tcgen05 kind::mxf8f6f4, 1x32 UE8M0 block scales, fp32 accumulate):

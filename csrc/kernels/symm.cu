@@ -591,6 +591,17 @@ void symm_adam_shard_ag(const at::Tensor& ranges, at::Tensor master, at::Tensor 
   MT_LAUNCH_CHECK();
 }
 
+// Copy-engine copy of `bytes` from src (any address in this process's unified
+// space: a peer's symmetric buffer included) to dst on the current stream: one
+// cudaMemcpyAsync per call, no SM involved, so it overlaps with kernels on other
+// streams.
+void copy_async(int64_t dst, int64_t src, int64_t bytes) {
+  MT_CHECK(bytes >= 0, "copy_async: bytes >= 0");
+  if (bytes == 0) return;
+  C10_CUDA_CHECK(cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), (size_t)bytes,
+                                 cudaMemcpyDeviceToDevice, cur_stream()));
+}
+
 void symm_barrier(const std::vector<int64_t>& flags, int64_t me, int64_t slot, int64_t epoch,
                   int64_t code) {
   barrier_kernel<<<1, 32, 0, cur_stream()>>>(to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]),

@@ -299,6 +299,138 @@ class SymmCollectives:
         _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 5, ep, 36)
 
 
+class GatheredOperand:
+    """An FP8 GEMM operand sharded by rows over the ranks of a group and read by the
+    GEMM straight from its owners: the parameter all-gather fused into the first GEMM
+    that consumes the parameters (``gemm_fp8_gather_b``).
+
+    The reference gathers with a blocking ``all_gather`` of whole byte buffers
+    (crates/mt-comm/src/topology_aware.rs:58-66).  Here each rank writes only its own
+    rows, ``[rank * shard_rows, (rank + 1) * shard_rows)``, into a symmetric buffer
+    (``local_shard()``), ``publish()`` orders those writes before any peer's read
+    (a barrier over the ranks), and a GEMM then reads the remote rows in one of two
+    ways:
+
+    * ``direct``: the GEMM's TMA producer loads each 128-row (K-major) or 128-deep
+      (MN-major) tile from the rank that owns it, over NVLink, with plain (never
+      multicast) loads.  Peer reads are cached in the owner's L2, not this GPU's, so
+      every output row block re-reads the remote tiles: right for small M (one or two
+      256-row blocks, e.g. a decode step), NVLink-bound for training-sized M.
+    * ``overlap``: shard by shard, starting with the own one, the GEMM runs on the
+      shards already local while the copy engine pulls the next shard from its owner
+      (one ``cudaMemcpyAsync`` per shard on a side stream): every remote byte crosses
+      NVLink once and the copies hide behind the math.
+
+    ``method="auto"`` picks ``direct`` when M spans at most two 256-row blocks.
+    shard_rows is rounded up to 128 so that no tile spans two owners.  A rank must
+    not rewrite its shard before every rank finished the GEMMs that read it
+    (``retire()``).
+    """
+
+    def __init__(self, rows: int, cols: int, device, group=None, ctx: "SymmContext" = None):
+        if cols % 16:
+            raise ValueError("GatheredOperand: cols must be a multiple of 16 (TMA row stride)")
+        self.ctx = ctx or SymmContext(device, group, num_slots=16)
+        self.me, self.world = self.ctx.rank, self.ctx.world
+        self.rows, self.cols = rows, cols
+        per = (rows + self.world - 1) // self.world
+        self.shard_rows = (per + 127) // 128 * 128
+        self.buf = SymmBuffer(self.shard_rows * self.world * cols, torch.uint8, device, group)
+        self.full = self.buf.tensor.view(self.shard_rows * self.world, cols)[:rows]
+        self.lo = min(rows, self.me * self.shard_rows)
+        self.hi = min(rows, self.lo + self.shard_rows)
+        self.epoch = 0
+        self.retired = 0
+        self._gathered: Optional[torch.Tensor] = None
+        self._copy_stream: Optional[torch.cuda.Stream] = None
+
+    def shard_range(self, p: int):
+        lo = min(self.rows, p * self.shard_rows)
+        return lo, min(self.rows, lo + self.shard_rows)
+
+    def local_shard(self) -> torch.Tensor:
+        """This rank's rows of the operand (uint8 codes) to write into."""
+        return self.full[self.lo:self.hi]
+
+    def publish(self) -> None:
+        """Every rank's shard writes (stream-ordered before this call) become visible
+        to all ranks' later GEMMs.  Call on every rank."""
+        self.epoch += 1
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 0, self.epoch, 37)
+
+    def retire(self) -> None:
+        """Every rank's GEMMs on the current shards are done (stream order), so owners
+        may rewrite them.  Call on every rank."""
+        self.retired += 1
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 1, self.retired, 38)
+
+    def gemm(self, a: torch.Tensor, a_fmt: int, b_fmt: int, out: Optional[torch.Tensor] = None, *,
+             a_mn: bool = False, b_mn: bool = False, bias=None, residual=None, act=None, aux=None, alpha=None,
+             alpha2=None, accumulate: bool = False, out_dtype: torch.dtype = torch.bfloat16,
+             method: str = "auto") -> torch.Tensor:
+        """out = epilogue(alpha * alpha2 * A . B^T) with B this operand: [N, K] = [rows, cols]
+        (b_mn=False) or [K, N] = [rows, cols] (b_mn=True, rows sharded along K)."""
+        M = a.shape[1] if a_mn else a.shape[0]
+        N = self.cols if b_mn else self.rows
+        if out is None:
+            out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+        if method == "auto":
+            method = "direct" if (M + 255) // 256 <= 2 else "overlap"
+        if method == "direct":
+            _cuda().gemm_fp8_gather_b(a, bool(a_mn), int(a_fmt), self.full, bool(b_mn), int(b_fmt), self.buf.ptrs,
+                                      self.shard_rows, out, bias, residual, act, aux, alpha, alpha2,
+                                      bool(accumulate))
+            return out
+        if method != "overlap":
+            raise ValueError(f"method must be auto, direct or overlap, not {method!r}")
+        return self._gemm_overlap(a, a_fmt, b_fmt, out, a_mn, b_mn, bias, residual, act, aux, alpha, alpha2,
+                                  accumulate)
+
+    def _gemm_overlap(self, a, a_fmt, b_fmt, out, a_mn, b_mn, bias, residual, act, aux, alpha, alpha2, accumulate):
+        from ..ops.fp8 import gemm_fp8
+
+        if b_mn and (out.dtype != torch.float32 or any(t is not None for t in (bias, residual, act, aux))):
+            raise ValueError("overlap with a K-sharded B sums per-shard partial products: fp32 output, "
+                             "no bias / residual / GELU epilogue")
+        cur = torch.cuda.current_stream()
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(device=a.device)
+            self._gathered = torch.empty((self.rows, self.cols), dtype=torch.uint8, device=a.device)
+        cs, g = self._copy_stream, self._gathered
+        order = [(self.me + i) % self.world for i in range(self.world)]
+        ready = {}
+        cs.wait_stream(cur)  # the owners' writes were published on this stream
+        with torch.cuda.stream(cs):
+            for p in order[1:]:
+                lo, hi = self.shard_range(p)
+                if hi > lo:
+                    _cuda().copy_async(g[lo:hi].data_ptr(), self.buf.ptrs[p] + lo * self.cols, (hi - lo) * self.cols)
+                ev = torch.cuda.Event()
+                ev.record(cs)
+                ready[p] = ev
+        first = True
+        for p in order:
+            lo, hi = self.shard_range(p)
+            if hi <= lo:
+                continue
+            if p != self.me:
+                cur.wait_event(ready[p])
+            src = (self.full if p == self.me else g)[lo:hi]
+            if not b_mn:  # this shard's rows of B are output columns lo..hi
+                sl = (slice(None), slice(lo, hi))
+                gemm_fp8(a, a_fmt, src, b_fmt, out[sl], a_mn=a_mn, alpha=alpha, alpha2=alpha2,
+                         bias=None if bias is None else bias[lo:hi],
+                         residual=None if residual is None else residual[sl], act=None if act is None else act[sl],
+                         aux=None if aux is None else aux[sl], accumulate=accumulate)
+            else:  # this shard is K rows lo..hi: add its partial product
+                a_k = a[lo:hi] if a_mn else a[:, lo:hi]
+                gemm_fp8(a_k, a_fmt, src, b_fmt, out, a_mn=a_mn, b_mn=True, alpha=alpha, alpha2=alpha2,
+                         accumulate=accumulate or not first)
+            first = False
+        cs.wait_stream(cur)  # the gathered copy stays untouched until these GEMMs ran
+        return out
+
+
 def halo_plan(topology, rank: int, device) -> tuple:
     """Neighbour ranks and receive slots for the torus exchange of ``rank``: the
     sender's k-th neighbour (+x, -x, +y, -y, ...) receives into its slot for the
@@ -313,4 +445,5 @@ def halo_plan(topology, rank: int, device) -> tuple:
             torch.tensor(slots, dtype=torch.int32, device=device))
 
 
-__all__ = ["SymmBuffer", "SymmContext", "SymmBucketReducer", "ZeroAdam", "SymmCollectives", "halo_plan"]
+__all__ = ["SymmBuffer", "SymmContext", "SymmBucketReducer", "ZeroAdam", "SymmCollectives", "GatheredOperand",
+           "halo_plan"]
