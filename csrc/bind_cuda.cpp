@@ -62,6 +62,8 @@ void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const
                 const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta);
 void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt, double fmax);
 void copy_async(int64_t dst, int64_t src, int64_t bytes);
+void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, int64_t fmt,
+                    double fmax);
 void gemm_fp8_gather_b(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
                        int64_t b_fmt, const std::vector<int64_t>& b_peers, int64_t shard_rows, at::Tensor D,
                        const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
@@ -183,6 +185,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("beta") = false);
   m.def("mx_quantize", &mx_quantize);
   m.def("copy_async", &copy_async);
+  m.def("mx_quantize_rc", &mx_quantize_rc);
   m.def("gemm_fp8_gather_b", &gemm_fp8_gather_b, py::arg("A"), py::arg("a_mn"), py::arg("a_fmt"), py::arg("B"),
         py::arg("b_mn"), py::arg("b_fmt"), py::arg("b_peers"), py::arg("shard_rows"), py::arg("D"),
         py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("act") = py::none(),

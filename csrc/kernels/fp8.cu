@@ -321,6 +321,99 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(const bf16* __restrict
   }
 }
 
+// Row- and column-wise MXFP8 in one pass (the operands of all three GEMMs of a
+// linear layer): x [R, C] bf16 -> row codes [R, C] with 32-blocks along C, and the
+// transposed column codes [C, R] with 32-blocks along R, each with its own scale
+// atoms (same rule and layout as mx_quantize_kernel).  A CTA stages a 32 x 256 tile
+// in shared memory; thread t quantises row block (t / 8, t % 8) of the tile and then
+// column t, whose 32 codes are one contiguous 32-byte run of the transposed output.
+// R and C multiples of 32; a tile may overhang C (columns past C are skipped).
+__device__ __forceinline__ void mx_block(const float (&v)[32], int ef, uint32_t mf, int fmt, uint32_t (&w)[8],
+                                         uint8_t& sfb) {
+  float amax = 0.f;
+  bool finite = true;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    amax = fmaxf(amax, fabsf(v[i]));
+    finite &= isfinite(v[i]);
+  }
+  int X = 0;
+  if (amax > 0.f) {
+    const uint32_t ua = __float_as_uint(amax);
+    X = (int)((ua >> 23) & 0xFF) - ef + ((ua & 0x7FFFFF) > mf ? 1 : 0);
+    X = max(-127, min(127, X));
+  }
+  const float inv = __uint_as_float((uint32_t)(127 - min(X, 126)) << 23);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float* t = v + 4 * q;
+    const uint16_t lo = fmt == 0 ? cvt2_e4m3(t[0] * inv, t[1] * inv) : cvt2_e5m2(t[0] * inv, t[1] * inv);
+    const uint16_t hi = fmt == 0 ? cvt2_e4m3(t[2] * inv, t[3] * inv) : cvt2_e5m2(t[2] * inv, t[3] * inv);
+    w[q] = (uint32_t)lo | ((uint32_t)hi << 16);
+  }
+  sfb = finite ? (uint8_t)(X + 127) : (uint8_t)255;
+}
+
+__device__ __forceinline__ int64_t mx_sf_offset(int r, int j, int nkb4) {
+  const int rr = r & 127;
+  return ((int64_t)(r >> 7) * nkb4 + (j >> 2)) * 512 + (rr & 31) * 16 + (rr >> 5) * 4 + (j & 3);
+}
+
+__global__ void __launch_bounds__(256) mx_quantize_rc_kernel(const bf16* __restrict__ x, int64_t ldx, int R, int C,
+                                                             int fmt, uint32_t fmax_bits, uint8_t* __restrict__ rc,
+                                                             uint8_t* __restrict__ rsf, uint8_t* __restrict__ cc,
+                                                             uint8_t* __restrict__ csf) {
+  __shared__ __align__(16) bf16 tile[32][256 + 8];
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 256, t = threadIdx.x;
+  const int ef = (int)((fmax_bits >> 23) & 0xFF);
+  const uint32_t mf = fmax_bits & 0x7FFFFF;
+  // stage 32 rows x 256 columns (16-byte loads; columns past C read as zero)
+  for (int i = t; i < 32 * 32; i += 256) {
+    const int rr = i / 32, cv = (i % 32) * 8;
+    bf16x8 val;
+    if (c0 + cv < C) {
+      val = *reinterpret_cast<const bf16x8*>(x + (int64_t)(r0 + rr) * ldx + c0 + cv);
+    } else {
+      float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      val = pack8(z);
+    }
+    *reinterpret_cast<bf16x8*>(&tile[rr][cv]) = val;
+  }
+  __syncthreads();
+  float v[32];
+  uint32_t w[8];
+  uint8_t sfb;
+  // row-wise: block (row t / 8, columns 32 * (t % 8) ..)
+  {
+    const int rr = t / 8, cb = (t % 8) * 32;
+    if (c0 + cb < C) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) unpack8(*reinterpret_cast<const bf16x8*>(&tile[rr][cb + 8 * q]), v + 8 * q);
+      mx_block(v, ef, mf, fmt, w, sfb);
+      uint4* dst = reinterpret_cast<uint4*>(rc + (int64_t)(r0 + rr) * C + c0 + cb);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      rsf[mx_sf_offset(r0 + rr, (c0 + cb) / 32, (C + 127) / 128)] = sfb;
+    }
+  }
+  // column-wise: column t of the tile = row (c0 + t) of the transposed output, K block r0 / 32
+  if (c0 + t < C) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(tile[i][t]);
+    mx_block(v, ef, mf, fmt, w, sfb);
+    uint4* dst = reinterpret_cast<uint4*>(cc + (int64_t)(c0 + t) * R + r0);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    csf[mx_sf_offset(c0 + t, r0 / 32, (R + 127) / 128)] = sfb;
+  }
+}
+
+// Fills every byte of a scale tensor with 127 (the value of padding slots).
+__global__ void fill_u8_kernel(uint8_t* p, int64_t n, uint8_t v) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
 static int q_grid(size_t n, int per) {
   return (int)std::max<size_t>(1, std::min<size_t>((n / per + 255) / 256, (size_t)num_sms() * 8));
 }
@@ -500,6 +593,40 @@ void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t f
     mx_quantize_kernel<0><<<grid, 256, 0, cur_stream()>>>(xp, x.stride(0), cp, sp, (int)R, (int)K, (int)nkb4, fbits);
   else
     mx_quantize_kernel<1><<<grid, 256, 0, cur_stream()>>>(xp, x.stride(0), cp, sp, (int)R, (int)K, (int)nkb4, fbits);
+  MT_LAUNCH_CHECK();
+}
+
+// x: bf16 [R, C] (R, C multiples of 32, 16-byte aligned rows) -> row codes [R, C] + rsf
+// (scales of [R, C]) and column codes [C, R] + csf (scales of [C, R]).
+void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, int64_t fmt,
+                    double fmax) {
+  MT_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "mx_quantize_rc: 2-D bf16 input");
+  const int64_t R = x.size(0), C = x.size(1);
+  MT_CHECK(R % 32 == 0 && C % 32 == 0, "mx_quantize_rc: R and C must be multiples of 32");
+  MT_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && (x.stride(0) * 2) % 16 == 0,
+           "mx_quantize_rc: 16-byte aligned rows");
+  auto chk = [](const at::Tensor& t, int64_t n, const char* what) {
+    MT_CHECK(t.element_size() == 1 && t.is_contiguous() && t.numel() == n &&
+                 reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+             what);
+  };
+  chk(rc, R * C, "mx_quantize_rc: rc must be 16-byte aligned contiguous uint8 [R, C]");
+  chk(cc, R * C, "mx_quantize_rc: cc must be 16-byte aligned contiguous uint8 [C, R]");
+  chk(rsf, (R + 127) / 128 * ((C + 127) / 128) * 512, "mx_quantize_rc: rsf size");
+  chk(csf, (C + 127) / 128 * ((R + 127) / 128) * 512, "mx_quantize_rc: csf size");
+  MT_CHECK((fmt == 0 || fmt == 1) && fmax > 0.0, "mx_quantize_rc: fmt 0 / 1, fmax > 0");
+  if (R == 0 || C == 0) return;
+  const float fm = (float)fmax;
+  uint32_t fbits;
+  std::memcpy(&fbits, &fm, 4);
+  const int fill_grid = num_sms() * 4;
+  fill_u8_kernel<<<fill_grid, 256, 0, cur_stream()>>>(reinterpret_cast<uint8_t*>(rsf.data_ptr()), rsf.numel(), 127);
+  fill_u8_kernel<<<fill_grid, 256, 0, cur_stream()>>>(reinterpret_cast<uint8_t*>(csf.data_ptr()), csf.numel(), 127);
+  dim3 grid((unsigned)((C + 255) / 256), (unsigned)(R / 32));
+  mx_quantize_rc_kernel<<<grid, 256, 0, cur_stream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), (int)R, (int)C, (int)fmt, fbits,
+      reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),
+      reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()));
   MT_LAUNCH_CHECK();
 }
 

@@ -143,10 +143,75 @@ def gemm_mxfp8(a: MxTensor, b: MxTensor, out: Optional[torch.Tensor] = None, *, 
     return out
 
 
+def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = None):
+    """Row-wise MXFP8 of x [R, C] (32-blocks along C) and of its transpose [C, R]
+    (32-blocks along R), in one pass on the GPU: the operands that contract over C
+    and over R.  R and C multiples of 32.  The reference on the CPU."""
+    if x.dim() != 2 or x.shape[0] % BLOCK or x.shape[1] % BLOCK:
+        raise ValueError("mx_quantize_rc: 2-D input with both sizes multiples of 32 expected")
+    if not x.is_cuda:
+        return mx_quantize_ref(x, fmt, fmax), mx_quantize_ref(x.t(), fmt, fmax)
+    fmax = float(MX_FMT_MAX[fmt] if fmax is None else fmax)
+    x = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    R, C = x.shape
+    rc = torch.empty((R, C), dtype=torch.uint8, device=x.device)
+    cc = torch.empty((C, R), dtype=torch.uint8, device=x.device)
+    rsf = torch.empty(sf_numel(R, C), dtype=torch.uint8, device=x.device)
+    csf = torch.empty(sf_numel(C, R), dtype=torch.uint8, device=x.device)
+    _cuda().mx_quantize_rc(x, rc, rsf, cc, csf, int(fmt), fmax)
+    return MxTensor(rc, rsf, int(fmt)), MxTensor(cc, csf, int(fmt))
+
+
+def _mm(a: MxTensor, b: MxTensor, out_dtype, bias=None) -> torch.Tensor:
+    if a.codes.is_cuda:
+        return gemm_mxfp8(a, b, bias=bias, out_dtype=out_dtype)
+    y = gemm_mxfp8_ref(a, b)
+    return (y if bias is None else y + bias).to(out_dtype)
+
+
+class MxLinearFn(torch.autograd.Function):
+    """y = x . W^T + b with all three GEMMs block-scaled (the MXFP8 training recipe):
+    E4M3 activations and weights, E5M2 output gradients, 1x32 UE8M0 scales along each
+    GEMM's contraction dimension, fp32 accumulation.  Forward: row-wise x and W.
+    dgrad: row-wise dY with column-wise W.  wgrad: column-wise dY with column-wise x.
+    Each tensor is quantised once, both ways, by ``mx_quantize_rc``.  CUDA tensors run
+    the sm_100a kernels; CPU tensors run the PyTorch oracle with the same numerics.
+    x [T, in], W [out, in] (T, in, out multiples of 32), b fp32 [out] or None."""
+
+    @staticmethod
+    def forward(ctx, x, w, b):
+        x2 = x.reshape(-1, x.shape[-1])
+        xr, xc = mx_quantize_rc(x2.to(torch.bfloat16), E4M3)
+        wr, wc = mx_quantize_rc(w.to(torch.bfloat16), E4M3)
+        y = _mm(xr, wr, torch.bfloat16, None if b is None else b.float())
+        ctx.save_for_backward(xc.codes, xc.sf, wc.codes, wc.sf)
+        ctx.has_bias = b is not None
+        ctx.x_shape, ctx.w_dtype = x.shape, w.dtype
+        return y.reshape(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        xc_codes, xc_sf, wc_codes, wc_sf = ctx.saved_tensors
+        xc, wc = MxTensor(xc_codes, xc_sf, E4M3), MxTensor(wc_codes, wc_sf, E4M3)
+        dy2 = dy.reshape(-1, dy.shape[-1]).to(torch.bfloat16)
+        dyr, dyc = mx_quantize_rc(dy2, E5M2)
+        dx = _mm(dyr, wc, torch.bfloat16).reshape(ctx.x_shape)
+        dw = _mm(dyc, xc, torch.float32).to(ctx.w_dtype)
+        db = dy2.float().sum(0) if ctx.has_bias else None
+        return dx, dw, db
+
+
+def mx_linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Block-scaled FP8 linear layer (see MxLinearFn)."""
+    return MxLinearFn.apply(x, w, b)
+
+
 def gemm_mxfp8_ref(a: MxTensor, b: MxTensor) -> torch.Tensor:
     """fp32 oracle of ``gemm_mxfp8``: the product of the dequantised operands."""
     return mx_dequantize(a) @ mx_dequantize(b).t()
 
 
 __all__ = ["E4M3", "E5M2", "MX_FMT_MAX", "MxTensor", "sf_numel", "sf_offsets", "mx_quantize", "mx_quantize_ref",
-           "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_ref"]
+           "mx_quantize_rc", "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_ref", "MxLinearFn", "mx_linear"]

@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from mtorus.ops.mxfp8 import (E4M3, E5M2, MX_FMT_MAX, MxTensor, gemm_mxfp8, gemm_mxfp8_ref, mx_dequantize,
-                              mx_quantize, mx_quantize_ref, sf_numel, sf_offsets)
+                              mx_linear, mx_quantize, mx_quantize_rc, mx_quantize_ref, sf_numel, sf_offsets)
 
 
 def _blocky(R, K, seed=0):
@@ -90,6 +90,39 @@ def test_reference_gemm_matches_fp32_product_of_dequantised_operands():
     assert bool(((gemm_mxfp8_ref(a, b).double() - ref).abs() <= 1e-5 * mag).all())
 
 
+def test_mx_linear_cpu_oracle_gradients():
+    """All three GEMMs of the MXFP8 linear: forward on row-wise x / W, dgrad on row-wise
+    dY with column-wise W, wgrad on column-wise dY and x (E5M2 gradients)."""
+    torch.manual_seed(0)
+    T, I, O = 64, 96, 128
+    x = (torch.randn(T, I) * 0.5).bfloat16().float().requires_grad_(True)
+    w = (torch.randn(O, I) * 0.05).requires_grad_(True)
+    b = torch.randn(O, requires_grad=True)
+    y = mx_linear(x, w, b)
+    dy = torch.randn(T, O) * 1e-2
+    y.backward(dy.bfloat16().float())
+    xr, xc = mx_quantize_rc(x.detach().bfloat16(), E4M3)
+    wr, wc = mx_quantize_rc(w.detach().bfloat16(), E4M3)
+    dyr, dyc = mx_quantize_rc(dy.bfloat16(), E5M2)
+    assert torch.equal(y.detach(), (mx_dequantize(xr) @ mx_dequantize(wr).t() + b.detach()).bfloat16())
+    assert torch.equal(x.grad, (mx_dequantize(dyr) @ mx_dequantize(wc).t()).bfloat16().float())
+    assert torch.allclose(w.grad, mx_dequantize(dyc) @ mx_dequantize(xc).t(), rtol=1e-6, atol=1e-9)
+    assert torch.allclose(b.grad, dy.bfloat16().float().sum(0), rtol=1e-6, atol=1e-6)
+    # and close to the unquantised layer (E4M3 / E5M2 with per-32 scales: a few percent)
+    ref_y = x.detach() @ w.detach().t() + b.detach()
+    assert float((y.detach().float() - ref_y).norm() / ref_y.norm()) < 0.05
+    ref_dw = dy.t() @ x.detach()
+    assert float((w.grad - ref_dw).norm() / ref_dw.norm()) < 0.1
+
+
+def test_mx_quantize_rc_cpu_is_row_and_transposed_reference():
+    x = _blocky(96, 64, seed=9)
+    r, c = mx_quantize_rc(x, E4M3)
+    assert torch.equal(r.codes, mx_quantize_ref(x, E4M3).codes)
+    assert torch.equal(c.codes, mx_quantize_ref(x.t().contiguous(), E4M3).codes)
+    assert torch.equal(c.sf, mx_quantize_ref(x.t().contiguous(), E4M3).sf)
+
+
 # ---------------------------------------------------------------- GPU (opt-in)
 _gpu = pytest.mark.skipif(os.environ.get("MTORUS_MXFP8_GPU_TESTS") != "1",
                           reason="block-scaled GEMM not yet run on a B200 (MTORUS_MXFP8_GPU_TESTS=1 runs it)")
@@ -145,3 +178,36 @@ def test_block_scaled_gemm_agrees_with_cublas_mx():
         pytest.skip(f"torch._scaled_mm has no MX path here: {e}")
     out = gemm_mxfp8(a, b, out_dtype=torch.float32)
     assert torch.allclose(out, lib, rtol=1e-4, atol=1e-4 * float(lib.abs().max()))
+
+
+@pytest.mark.gpu
+@_gpu
+@pytest.mark.parametrize("shape", [(256, 512), (96, 320)])
+def test_cuda_row_col_quantiser_matches_reference(shape):
+    R, C = shape
+    x = _blocky(R, C, seed=R).to(torch.bfloat16)
+    r, c = mx_quantize_rc(x.cuda(), E4M3)
+    rr, cr = mx_quantize_ref(x.float(), E4M3), mx_quantize_ref(x.float().t().contiguous(), E4M3)
+    assert torch.equal(r.codes.cpu(), rr.codes) and torch.equal(r.sf.cpu(), rr.sf)
+    assert torch.equal(c.codes.cpu(), cr.codes) and torch.equal(c.sf.cpu(), cr.sf)
+
+
+@pytest.mark.gpu
+@_gpu
+def test_mx_linear_cuda_matches_cpu_oracle():
+    torch.manual_seed(1)
+    T, I, O = 512, 256, 768
+    x = (torch.randn(T, I) * 0.5).bfloat16()
+    w = torch.randn(O, I) * 0.05
+    b = torch.randn(O)
+    dy = (torch.randn(T, O) * 1e-2).bfloat16()
+    outs = {}
+    for dev in ("cpu", "cuda"):
+        xv = x.float().to(dev).requires_grad_(True)
+        wv = w.to(dev).requires_grad_(True)
+        bv = b.to(dev).requires_grad_(True)
+        y = mx_linear(xv, wv, bv)
+        y.backward(dy.float().to(dev))
+        outs[dev] = [t.detach().float().cpu() for t in (y, xv.grad, wv.grad, bv.grad)]
+    for g, r in zip(outs["cuda"], outs["cpu"]):
+        assert torch.allclose(g, r, rtol=2e-2, atol=1e-3 * float(r.abs().max()))
