@@ -208,10 +208,38 @@ def mx_linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None
     return MxLinearFn.apply(x, w, b)
 
 
+def enable_mx_linears(module: torch.nn.Module) -> int:
+    """Run every Linear of ``module`` through ``mx_linear`` (the MXFP8 recipe: all three
+    GEMMs block-scaled).  A call whose token count, input or output width is not a
+    multiple of 32 runs the layer's own forward instead.  Works on any device (CUDA
+    kernels on the GPU, the oracle on the CPU).  Returns the number of layers converted."""
+    import torch.nn.functional as F
+
+    n = 0
+    for mod in module.modules():
+        w = getattr(mod, "weight", None)
+        if not isinstance(w, torch.nn.Parameter) or w.dim() != 2 or not hasattr(mod, "bias"):
+            continue
+        if isinstance(mod, torch.nn.Embedding) or type(mod).__name__ == "Embedding":
+            continue
+
+        def fwd(x, mod=mod):
+            T = x.numel() // x.shape[-1]
+            out_f, in_f = mod.weight.shape
+            b = None if mod.bias is None else mod.bias
+            if T % BLOCK or in_f % BLOCK or out_f % BLOCK:
+                return F.linear(x, mod.weight.to(x.dtype), None if b is None else b.to(x.dtype))
+            return mx_linear(x, mod.weight, b).to(x.dtype)
+
+        mod.forward = fwd
+        n += 1
+    return n
+
+
 def gemm_mxfp8_ref(a: MxTensor, b: MxTensor) -> torch.Tensor:
     """fp32 oracle of ``gemm_mxfp8``: the product of the dequantised operands."""
     return mx_dequantize(a) @ mx_dequantize(b).t()
 
 
 __all__ = ["E4M3", "E5M2", "MX_FMT_MAX", "MxTensor", "sf_numel", "sf_offsets", "mx_quantize", "mx_quantize_ref",
-           "mx_quantize_rc", "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_ref", "MxLinearFn", "mx_linear"]
+           "mx_quantize_rc", "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_ref", "MxLinearFn", "mx_linear", "enable_mx_linears"]

@@ -211,3 +211,33 @@ def test_mx_linear_cuda_matches_cpu_oracle():
         outs[dev] = [t.detach().float().cpu() for t in (y, xv.grad, wv.grad, bv.grad)]
     for g, r in zip(outs["cuda"], outs["cpu"]):
         assert torch.allclose(g, r, rtol=2e-2, atol=1e-3 * float(r.abs().max()))
+
+
+def test_gpt_trains_with_mx_linears_on_cpu():
+    """The reference GPT with every Linear on the MXFP8 recipe (CPU oracle) follows the
+    fp32 model's loss curve within a few percent."""
+    from mtorus.models.gpt import GptConfig, GptModel
+    from mtorus.ops.mxfp8 import enable_mx_linears
+
+    cfg = GptConfig(256, 64, 2, 2, 256, 32, 0.0)
+    losses = {}
+    for mx in (False, True):
+        torch.manual_seed(0)
+        m = GptModel(cfg, init="normal")
+        if mx:
+            assert enable_mx_linears(m) == 2 * 4 + 2 * 2 + 1  # q/k/v/out, ffn in/out per block, lm head
+        opt = torch.optim.Adam(m.parameters(), lr=3e-3)
+        g = torch.Generator().manual_seed(1)
+        data = torch.randint(0, 256, (8, 33), generator=g)
+        curve = []
+        for _ in range(6):
+            logits = m(data[:, :-1])
+            loss = torch.nn.functional.cross_entropy(logits.reshape(-1, 256).float(), data[:, 1:].reshape(-1))
+            opt.zero_grad()
+            loss.backward()
+            opt.step()
+            curve.append(float(loss.detach()))
+        losses[mx] = curve
+    assert losses[True][-1] < losses[True][0]
+    for a, b in zip(losses[True], losses[False]):
+        assert abs(a - b) / b < 0.05
