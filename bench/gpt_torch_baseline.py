@@ -4,7 +4,8 @@ and step in eager PyTorch -- nn.Linear / nn.LayerNorm (cuBLAS bf16 under autocas
 scaled_dot_product_attention (cuDNN / flash), torch.optim.Adam(fused=True), and
 DistributedDataParallel with 25 MB buckets over NCCL for N > 1.  None of this
 framework's kernels run on this path; it is the "PyTorch eager + cuBLAS + NCCL"
-comparison point for ``bench.py``.
+comparison point for ``bench.py``.  With ``--mx`` every Linear runs instead on mtorus'
+MXFP8 recipe (``enable_mx_linears``): the same eager model with only the GEMMs swapped.
 
     python bench/gpt_torch_baseline.py --steps 10 --warmup 3
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 bench/gpt_torch_baseline.py
@@ -66,6 +67,9 @@ def main() -> int:
     ap.add_argument("--micro-batch", type=int, default=8)
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=24)
+    ap.add_argument("--mx", action="store_true",
+                    help="run every Linear through mtorus' MXFP8 recipe (block-scaled tcgen05 GEMMs) instead of "
+                         "cuBLAS bf16: the eager model with only the GEMMs swapped")
     args = ap.parse_args()
     sys.stdout.flush()
     json_fd = os.dup(1)
@@ -82,6 +86,11 @@ def main() -> int:
     V, d, h, f, S, B = 50304, 2048, 16, 8192, args.seq, args.micro_batch
     torch.manual_seed(1234)
     model = GPT(V, d, args.layers, h, f, S).to(dev)
+    if args.mx:
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        from mtorus.ops.mxfp8 import enable_mx_linears
+
+        enable_mx_linears(model)
     if world > 1:
         model = nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=25,
                                                     gradient_as_bucket_view=True)
@@ -114,10 +123,12 @@ def main() -> int:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = float(ms)
     nparams = sum(p.numel() for p in model.parameters())
-    out = {"metric": "GPT-1B bf16 tokens/sec, plain PyTorch eager (cuBLAS, SDPA, fused Adam, DDP/NCCL)",
-           "impl": "torch_eager_baseline", "value": round(B * S * world / (ms / 1000.0), 1), "unit": "tokens/s",
+    out = {"metric": ("GPT-1B MXFP8-linear tokens/sec, PyTorch eager with mtorus block-scaled GEMMs" if args.mx else
+                      "GPT-1B bf16 tokens/sec, plain PyTorch eager (cuBLAS, SDPA, fused Adam, DDP/NCCL)"),
+           "impl": "torch_eager_mx_linears" if args.mx else "torch_eager_baseline",
+           "value": round(B * S * world / (ms / 1000.0), 1), "unit": "tokens/s",
            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-           "dtype": "bf16 autocast", "data": "synthetic uniform-random tokens, N(0,0.02) init",
+           "dtype": "mxfp8 linears (E4M3 / E5M2, 1x32 UE8M0), bf16 elsewhere" if args.mx else "bf16 autocast", "data": "synthetic uniform-random tokens, N(0,0.02) init",
            "config": {"layers": args.layers, "d_model": d, "heads": h, "d_ff": f, "vocab": V, "seq_len": S,
                       "micro_batch_per_gpu": B, "params": nparams},
            "final_loss": round(float(loss), 4), "loss_is_finite": bool(math.isfinite(float(loss)))}
