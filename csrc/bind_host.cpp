@@ -4,6 +4,7 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include "core/data_loader.h"
 #include "core/precision.h"
 #include "core/topology.h"
 
@@ -212,11 +213,34 @@ static void bind_precision(py::module_& m) {
       .def(py::self == py::self);
 }
 
+static void bind_data(py::module_& m) {
+  m.def("synthetic_token", &synthetic_token, py::arg("seed"), py::arg("batch_index"), py::arg("position"),
+        py::arg("per_batch"), py::arg("vocab"));
+  py::class_<TokenLoader>(m, "TokenLoader")
+      .def(py::init<int64_t, int64_t, int64_t, int64_t, uint64_t, bool, int, int>(), py::arg("batch"),
+           py::arg("seq_len"), py::arg("vocab"), py::arg("num_batches"), py::arg("seed"), py::arg("shift"),
+           py::arg("depth") = 4, py::arg("workers") = 1)
+      // inp / tgt: addresses of int64 [batch, seq_len] host buffers
+      .def(
+          "next_into",
+          [](TokenLoader& l, int64_t inp, int64_t tgt, double timeout_s) {
+            return l.next_into(reinterpret_cast<int64_t*>(inp), reinterpret_cast<int64_t*>(tgt), timeout_s);
+          },
+          py::arg("inp"), py::arg("tgt"), py::arg("timeout_s") = 60.0, py::call_guard<py::gil_scoped_release>())
+      .def("seek", &TokenLoader::seek, py::call_guard<py::gil_scoped_release>())
+      .def("reset", &TokenLoader::reset, py::call_guard<py::gil_scoped_release>())
+      .def("num_batches", &TokenLoader::num_batches)
+      .def("current_batch", &TokenLoader::current_batch)
+      .def_property_readonly("batch", &TokenLoader::batch)
+      .def_property_readonly("seq_len", &TokenLoader::seq_len);
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-  m.doc() = "mtorus host runtime (topology, FP8 codec, communicators, pipeline schedules)";
+  m.doc() = "mtorus host runtime (topology, FP8 codec, communicators, pipeline schedules, data loader)";
   m.attr("__version__") = "0.1.0";
   bind_topology(m);
   bind_precision(m);
   bind_comm(m);
   bind_pipeline(m);
+  bind_data(m);
 }

@@ -16,12 +16,15 @@
 //   * TcpCommunicator over 127.0.0.1: ring all_reduce / all_gather / broadcast from
 //     3 rank threads, then two threads per rank sending concurrently to one peer,
 //     and a ring in which one rank's fault plan kills it mid-collective;
+//   * the prefetching TokenLoader: 3 worker threads, a consumer that seeks back and
+//     forth while fills are in flight, every batch checked against synthetic_token;
 //   * single-threaded, for the undefined-behaviour checker: the FP8 codec over all
 //     256 codes and over special / extreme floats, the scaling and loss-scale state
 //     machines, the pipeline op lists, simulator and stage-data frames.
 //
 // Exit status 0 when every check passed; a sanitizer that finds an error makes
 // the process exit non-zero (halt_on_error / exitcode options set by the runner).
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -33,6 +36,7 @@
 #include <vector>
 
 #include "comm/comm.h"
+#include "core/data_loader.h"
 #include "core/precision.h"
 #include "core/topology.h"
 #include "pipeline/schedule.h"
@@ -238,6 +242,25 @@ void codec_and_schedules() {
   check(back.size() == vals.size(), "fp8 stage frame");
 }
 
+void token_loader(int rounds) {
+  const int64_t B = 3, S = 17, V = 1000, N = 40;
+  TokenLoader l(B, S, V, N, 9, true, 3, 3);
+  std::vector<int64_t> inp(B * S), tgt(B * S);
+  for (int it = 0; it < rounds; ++it) {
+    const int64_t start = (it * 7) % N;
+    l.seek(start);
+    for (int64_t i = start; i < std::min<int64_t>(N, start + 5); ++i) {
+      check(l.next_into(inp.data(), tgt.data(), 10.0), "loader batch available");
+      const uint64_t per = (uint64_t)(B * (S + 1));
+      check(inp[0] == synthetic_token(9, (uint64_t)i, 0, per, V), "loader batch content");
+      check(tgt[0] == synthetic_token(9, (uint64_t)i, 1, per, V), "loader shifted target");
+    }
+  }
+  l.seek(N - 1);
+  check(l.next_into(inp.data(), tgt.data(), 10.0) && !l.next_into(inp.data(), tgt.data(), 10.0),
+        "loader ends after num_batches");
+}
+
 // A rank killed by its fault plan in the middle of a ring all_reduce: its send
 // thread closes every socket while its receiving thread is inside recv.  Every
 // rank must leave with a CommError (EOF or timeout), none may hang.
@@ -277,6 +300,7 @@ void tcp_kill() {
 int main(int argc, char** argv) {
   const int rounds = argc > 1 ? std::atoi(argv[1]) : 50;
   codec_and_schedules();
+  token_loader(rounds);
   local_world(rounds);
   torus(rounds / 5 + 1);
   p2p(rounds);

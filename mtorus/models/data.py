@@ -64,4 +64,92 @@ class SyntheticDataLoader:
         return inp, tgt
 
 
-__all__ = ["SyntheticDataLoader"]
+_MASK = (1 << 64) - 1
+
+
+def _mix(z):
+    """SplitMix64 finaliser on uint64 numpy arrays (the native loader's mixer)."""
+    import numpy as np
+
+    z = np.asarray(z, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def synthetic_batch_ref(seed: int, index: int, batch: int, seq_len: int, vocab: int, shift: bool):
+    """Pure-Python/NumPy recomputation of batch ``index`` of ``NativeSyntheticDataLoader``."""
+    import numpy as np
+
+    n = seq_len + (1 if shift else 0)
+    per = batch * n
+    with np.errstate(over="ignore"):
+        key = _mix(np.uint64((seed + 0x9E3779B97F4A7C15) & _MASK))
+        ctr = np.uint64(index) * np.uint64(per) + np.arange(per, dtype=np.uint64)
+        r = _mix(key ^ _mix(ctr))
+    # (r * vocab) >> 64 without 128-bit integers: split r into 32-bit halves
+    hi, lo = r >> np.uint64(32), r & np.uint64(0xFFFFFFFF)
+    v = np.uint64(vocab)
+    with np.errstate(over="ignore"):
+        t = ((lo * v) >> np.uint64(32)) + hi * v
+    tok = (t >> np.uint64(32)).astype(np.int64).reshape(batch, n)
+    t = torch.from_numpy(tok)
+    return (t[:, :-1].contiguous(), t[:, 1:].contiguous()) if shift else (t, t.clone())
+
+
+class NativeSyntheticDataLoader:
+    """``SyntheticDataLoader`` produced by the C++ runtime (``mtorus._C.TokenLoader``):
+    worker threads generate batches ahead of the consumer into a ring, each batch a
+    pure function of (seed, index), so ``seek(i)`` resumes a run exactly.  Batches are
+    handed out in reusable (optionally pinned) host buffers -- copy or consume them
+    before the next call -- and moved to ``device`` when one is given."""
+
+    def __init__(self, batch_size: int, seq_len: int, vocab_size: int, num_batches: int, device=None,
+                 seed: int = 0, shift: bool = False, pin_memory: bool = False, depth: int = 4, workers: int = 1):
+        from .._ext import host as _host
+
+        self._l = _host().TokenLoader(batch_size, seq_len, vocab_size, num_batches, seed, shift, depth, workers)
+        self.batch_size, self.seq_len, self.vocab_size = batch_size, seq_len, vocab_size
+        self.device = torch.device(device) if device is not None else torch.device("cpu")
+        pin = pin_memory and torch.cuda.is_available()
+        self._inp = torch.empty((batch_size, seq_len), dtype=torch.long, pin_memory=pin)
+        self._tgt = torch.empty((batch_size, seq_len), dtype=torch.long, pin_memory=pin)
+        self._copied = None  # event after the last host-to-device copy out of the buffers
+
+    def num_batches(self) -> int:
+        return self._l.num_batches()
+
+    def current_batch(self) -> int:
+        return self._l.current_batch()
+
+    def reset(self) -> None:
+        self._l.reset()
+
+    def seek(self, index: int) -> None:
+        self._l.seek(index)
+
+    def __iter__(self):
+        return self
+
+    def __next__(self):
+        b = self.next()
+        if b is None:
+            raise StopIteration
+        return b
+
+    def next(self):
+        if self._copied is not None:
+            self._copied.synchronize()  # the previous asynchronous copy still reads the buffers
+            self._copied = None
+        if not self._l.next_into(self._inp.data_ptr(), self._tgt.data_ptr()):
+            return None
+        if self.device.type != "cpu":
+            out = (self._inp.to(self.device, non_blocking=True), self._tgt.to(self.device, non_blocking=True))
+            self._copied = torch.cuda.Event()
+            self._copied.record()
+            return out
+        return self._inp, self._tgt
+
+
+__all__ = ["SyntheticDataLoader", "NativeSyntheticDataLoader", "synthetic_batch_ref"]

@@ -2,7 +2,7 @@
 
 The reference has no race detection (its only shared state is the mock mailbox
 lock, crates/mt-comm/src/mock.rs:6-32).  Here the host library -- communicators,
-fault plan, topology-aware wrapper, FP8 codec, pipeline schedules
+fault plan, topology-aware wrapper, FP8 codec, pipeline schedules, token loader
 (``csrc/comm``, ``csrc/core``, ``csrc/pipeline``) -- is plain C++17 with no
 Python or CUDA dependency, so it can be compiled with a sanitizer into a native
 stress driver (``csrc/tests/comm_stress.cpp``) that runs its thread-shared parts
@@ -28,7 +28,8 @@ from typing import Optional, Tuple
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 SOURCES = ["csrc/tests/comm_stress.cpp", "csrc/comm/comm.cpp", "csrc/comm/tcp.cpp", "csrc/comm/topology_aware.cpp",
-           "csrc/core/topology.cpp", "csrc/core/precision.cpp", "csrc/pipeline/schedule.cpp"]
+           "csrc/core/topology.cpp", "csrc/core/precision.cpp", "csrc/core/data_loader.cpp",
+           "csrc/pipeline/schedule.cpp"]
 FLAGS = {
     "thread": ["-fsanitize=thread"],
     "address": ["-fsanitize=address,undefined", "-fno-omit-frame-pointer", "-fno-sanitize-recover=undefined"],

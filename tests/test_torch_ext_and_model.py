@@ -233,3 +233,34 @@ def test_cross_entropy_and_training_loss_decreases():
         losses.append(loss.item())
     assert abs(losses[0] - math.log(c.vocab_size)) < 1.0
     assert losses[-1] < losses[0] - 1.0
+
+
+def test_native_token_loader_matches_reference_and_resumes():
+    from mtorus.models.data import NativeSyntheticDataLoader, synthetic_batch_ref
+
+    for shift, workers in ((True, 3), (False, 1)):
+        dl = NativeSyntheticDataLoader(4, 16, 1000, 7, seed=5, shift=shift, depth=3, workers=workers)
+        got = [tuple(t.clone() for t in b) for b in dl]
+        assert len(got) == 7 and dl.next() is None and dl.current_batch() == 7
+        for i, (x, y) in enumerate(got):
+            rx, ry = synthetic_batch_ref(5, i, 4, 16, 1000, shift)
+            assert torch.equal(x, rx) and torch.equal(y, ry)
+            assert int(x.min()) >= 0 and int(x.max()) < 1000
+        if shift:
+            assert torch.equal(got[0][0][:, 1:], got[0][1][:, :-1])  # next-token targets
+        dl.seek(4)
+        x, y = dl.next()
+        assert torch.equal(x, got[4][0]) and dl.current_batch() == 5
+        dl.reset()
+        assert torch.equal(dl.next()[0], got[0][0])
+
+
+def test_native_token_loader_is_roughly_uniform():
+    from mtorus.models.data import NativeSyntheticDataLoader
+
+    dl = NativeSyntheticDataLoader(64, 256, 10, 4, seed=1)
+    counts = torch.zeros(10)
+    for x, _ in dl:
+        counts += torch.bincount(x.reshape(-1), minlength=10).float()
+    frac = counts / counts.sum()
+    assert float((frac - 0.1).abs().max()) < 0.01
