@@ -48,8 +48,9 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
                     help="replay the whole step as one CUDA graph (dp none / nccl); auto: on for 1 GPU")
-    ap.add_argument("--precision", default="fp8", choices=["fp8", "bf16"],
-                    help="fp8: E4M3/E5M2 delayed-scaling GEMMs in the blocks; bf16: all GEMMs bf16")
+    ap.add_argument("--precision", default="fp8", choices=["fp8", "bf16", "mxfp8"],
+                    help="fp8: E4M3/E5M2 delayed-scaling GEMMs in the blocks; mxfp8: the same formats with "
+                         "1x32 UE8M0 block scales (block-scaled tcgen05 GEMMs); bf16: all GEMMs bf16")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -85,7 +86,8 @@ def main() -> int:
         cfg.num_layers = args.layers
     B, S = args.micro_batch, args.seq
     trainer = GptTrainer(cfg, device=dev, lr=3e-4, init="normal", seed=1234, dp=args.dp,
-                         fp8=args.precision == "fp8")
+                         fp8=args.precision in ("fp8", "mxfp8"),
+                         fp8_recipe="mx" if args.precision == "mxfp8" else "tensor")
     ext = _cuda()
 
     # synthetic next-token data: uniform ids, targets shifted by one
@@ -194,8 +196,11 @@ def main() -> int:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": ("fp8 (E4M3 fwd / E5M2 grad block GEMMs, delayed scaling; bf16 LM head, attention, "
-                  "activations; fp32 master / Adam)") if args.precision == "fp8" else "bf16",
+        "dtype": {"fp8": "fp8 (E4M3 fwd / E5M2 grad block GEMMs, delayed scaling; bf16 LM head, attention, "
+                         "activations; fp32 master / Adam)",
+                  "mxfp8": "mxfp8 (E4M3 fwd / E5M2 grad block GEMMs, 1x32 UE8M0 block scales; bf16 LM head, "
+                           "attention, activations; fp32 master / Adam)",
+                  "bf16": "bf16"}[args.precision],
         "data": "synthetic uniform-random tokens, random-init N(0,0.02) weights",
         "config": {
             "model": f"GPT-1B ({cfg.num_layers} layers, d_model {cfg.d_model}, {cfg.num_heads} heads, "
@@ -205,8 +210,10 @@ def main() -> int:
             "micro_batch_per_gpu": B,
             "parallelism": f"dp{world}",
             "dp_reduce": args.dp if world > 1 else "none",
-            "gemm": ("tcgen05 kind::f8f6f4 fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, fp32 accumulate"
-                     if args.precision == "fp8" else "tcgen05 kind::f16 bf16, CTA-pair 256x256 tiles"),
+            "gemm": {"fp8": "tcgen05 kind::f8f6f4 fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, fp32 accumulate",
+                     "mxfp8": "tcgen05 kind::mxf8f6f4 block-scaled fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, "
+                              "fp32 accumulate",
+                     "bf16": "tcgen05 kind::f16 bf16, CTA-pair 256x256 tiles"}[args.precision],
             "l2": "per-step working set (activations, 1.4B-param optimizer state) >> 126 MB L2; no flush",
             "params": cfg.num_params(),
             "model_tflops_per_gpu": round(cfg.train_flops_per_token(S) * B * S / (ms_step / 1000.0) / 1e12, 1),

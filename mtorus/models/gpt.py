@@ -348,16 +348,23 @@ class GptModel(nn.Module):
                     (f"L{i}.ffn1_w", blk.ff.linear1.weight), (f"L{i}.ffn2_w", blk.ff.linear2.weight)]
         return out
 
-    def enable_fp8(self, history: int = 16):
-        """E4M3 weights / activations and E5M2 gradients with delayed scaling for the
-        block GEMMs; call ``refresh_fp8_weights()`` after every optimizer step and
-        ``fp8_state.end_step()`` at the end of every step."""
+    def enable_fp8(self, history: int = 16, recipe: str = "tensor"):
+        """E4M3 weights / activations and E5M2 gradients for the block GEMMs; call
+        ``refresh_fp8_weights()`` after every optimizer step and ``fp8_state.end_step()``
+        at the end of every step.  recipe "tensor": per-tensor scales with delayed
+        scaling (amax histories); "mx": MXFP8, one power-of-two scale per 32 values
+        along each GEMM's contraction dimension, for all three GEMMs of every block
+        linear (``mtorus.ops.mxfp8``)."""
         from ..ops.fp8 import Fp8State
 
         assert self.flat is not None, "flatten() first"
+        if recipe not in ("tensor", "mx"):
+            raise ValueError(f"fp8 recipe must be 'tensor' or 'mx', not {recipe!r}")
         self.fp8_state = Fp8State(self.flat.device, history)
+        self.fp8_state.recipe = recipe
         for name, w in self.fp8_weights():
-            w.w8 = torch.empty(w.shape, dtype=torch.uint8, device=self.flat.device)
+            if recipe == "tensor":
+                w.w8 = torch.empty(w.shape, dtype=torch.uint8, device=self.flat.device)
             w.fp8_name = name
         return self.fp8_state
 
@@ -365,6 +372,12 @@ class GptModel(nn.Module):
         from ..ops import fp8 as F8
 
         st = self.fp8_state
+        if st.recipe == "mx":
+            from ..ops.mxfp8 import E4M3, mx_quantize_rc
+
+            for _, w in self.fp8_weights():
+                w.mx = mx_quantize_rc(w.w16, E4M3)  # (row-wise: forward, column-wise: dgrad)
+            return
         for name, w in self.fp8_weights():
             _, w.w8_inv = st.quantize_into(w.w16, name, F8.E4M3, w.w8)
 

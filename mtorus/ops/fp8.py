@@ -148,6 +148,7 @@ class Fp8State:
         self.first_step = True
         self._measured = set()  # slots whose first-step scale is already set
         self.sync = None  # cross-rank amax reduction (data parallel), see set_amax_sync
+        self.recipe = "tensor"  # "mx": the block GEMMs run MXFP8 (set by GptModel.enable_fp8)
 
     def set_amax_sync(self, sync) -> None:
         """Make every amax the max over the data-parallel ranks (``NcclAmaxSync`` or

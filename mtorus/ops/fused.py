@@ -142,6 +142,17 @@ def _ln_bwd(dh, x2d, mean, rstd, ln, dres):
     return dx
 
 
+def _mx(fp8) -> bool:
+    """True when the block GEMMs run the MXFP8 recipe (GptModel.enable_fp8(recipe="mx"))."""
+    return fp8 is not None and getattr(fp8[0], "recipe", "tensor") == "mx"
+
+
+def _mx_t(codes, sf, fmt):
+    from .mxfp8 import MxTensor
+
+    return MxTensor(codes, sf, fmt)
+
+
 class AttnBlockFn(Function):
     """x + out_proj(attention(qkv(LN1(x)))) as one autograd node (reference
     TransformerBlock first half, transformer.rs:144-149).  LayerNorm, the QKV and
@@ -156,6 +167,22 @@ class AttnBlockFn(Function):
         check_shape(S, dh)
         wq, bq = qkv_params
         wo, bo = out_params
+        ctx.shape = (B, S, H)
+        ctx.params = (ln, qkv_params, out_params)
+        ctx.fp8 = fp8
+        if _mx(fp8):
+            # MXFP8: every GEMM operand carries 1x32 UE8M0 scales along its contraction dim;
+            # inputs are quantised both ways once (row-wise now, column-wise for wgrad)
+            from . import mxfp8 as MX
+
+            h, mean, rstd = _ln_fwd(x2d, ln)
+            hr, hc = MX.mx_quantize_rc(h, MX.E4M3)
+            qkv = MX.gemm_mxfp8(hr, wq.mx[0], bias=bq.data)
+            o, lse = attention_fwd(qkv, B, S, H)
+            orow, ocol = MX.mx_quantize_rc(o, MX.E4M3)
+            out = MX.gemm_mxfp8(orow, wo.mx[0], bias=bo.data, residual=x2d)
+            ctx.save_for_backward(x2d, mean, rstd, hc.codes, hc.sf, ocol.codes, ocol.sf, qkv, o, lse)
+            return out
         if fp8 is not None:
             st, tag = fp8
             gamma, beta, eps = ln
@@ -177,15 +204,14 @@ class AttnBlockFn(Function):
         else:
             out = K.gemm(o, wo.w16, bias=bo.data, residual=x2d)
         ctx.save_for_backward(x2d, mean, rstd, h, o, *attn_saved)
-        ctx.shape = (B, S, H)
-        ctx.params = (ln, qkv_params, out_params)
-        ctx.fp8 = fp8
         return out
 
     @staticmethod
     def backward(ctx, dout):
         from .attention import attention_bwd
 
+        if _mx(ctx.fp8):
+            return AttnBlockFn._backward_mx(ctx, dout)
         x2d, mean, rstd, h, o, qkv, o_bf16, lse = ctx.saved_tensors
         ln, (wq, bq), (wo, bo) = ctx.params
         dout = dout.contiguous()
@@ -217,6 +243,29 @@ class AttnBlockFn(Function):
         _grads_done(wq, bq)
         return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None
 
+    @staticmethod
+    def _backward_mx(ctx, dout):
+        from . import mxfp8 as MX
+        from .attention import attention_bwd
+
+        x2d, mean, rstd, hcc, hcs, occ, ocs, qkv, o_bf16, lse = ctx.saved_tensors
+        ln, (wq, bq), (wo, bo) = ctx.params
+        dout = dout.contiguous()
+        acc = FusedGradState.accumulate
+        hc, oc = _mx_t(hcc, hcs, MX.E4M3), _mx_t(occ, ocs, MX.E4M3)
+        grow, gcol = MX.mx_quantize_rc(dout, MX.E5M2)
+        K.colsum_(dout, bo.main_grad, acc)
+        do = MX.gemm_mxfp8(grow, wo.mx[1])  # dgrad: dY (row) x W (column-wise)
+        MX.gemm_mxfp8(gcol, oc, out=wo.main_grad, accumulate=acc)  # wgrad: dY^T x O, both column-wise
+        _grads_done(wo, bo)
+        dqkv = attention_bwd(do, qkv, o_bf16, lse, *ctx.shape)
+        qrow, qcol = MX.mx_quantize_rc(dqkv, MX.E5M2)
+        K.colsum_(dqkv, bq.main_grad, acc)
+        MX.gemm_mxfp8(qcol, hc, out=wq.main_grad, accumulate=acc)
+        dh = MX.gemm_mxfp8(qrow, wq.mx[1])
+        _grads_done(wq, bq)
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None
+
 
 class MLPBlockFn(Function):
     """x + W2 GELU(W1 LN2(x) + b1) + b2 as one autograd node (reference
@@ -229,6 +278,19 @@ class MLPBlockFn(Function):
         w1, b1, w2, b2 = params
         T, F = x2d.shape[0], w1.shape[0]
         pre = torch.empty((T, F), dtype=torch.bfloat16, device=x2d.device)
+        ctx.params = (ln, params)
+        ctx.fp8 = fp8
+        if _mx(fp8):
+            from . import mxfp8 as MX
+
+            h, mean, rstd = _ln_fwd(x2d, ln)
+            hr, hc = MX.mx_quantize_rc(h, MX.E4M3)
+            act = torch.empty_like(pre)
+            MX.gemm_mxfp8(hr, w1.mx[0], out=pre, bias=b1.data, act=act)  # pre-activation and GELU
+            ar, ac = MX.mx_quantize_rc(act, MX.E4M3)
+            out = MX.gemm_mxfp8(ar, w2.mx[0], bias=b2.data, residual=x2d)
+            ctx.save_for_backward(x2d, mean, rstd, hc.codes, hc.sf, pre, ac.codes, ac.sf)
+            return out
         if fp8 is not None:
             st, tag = fp8
             gamma, beta, eps = ln
@@ -255,12 +317,12 @@ class MLPBlockFn(Function):
             K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
             out = K.gemm(act, w2.w16, bias=b2.data, residual=x2d)
         ctx.save_for_backward(x2d, mean, rstd, h, pre, act)
-        ctx.params = (ln, params)
-        ctx.fp8 = fp8
         return out
 
     @staticmethod
     def backward(ctx, dout):
+        if _mx(ctx.fp8):
+            return MLPBlockFn._backward_mx(ctx, dout)
         x2d, mean, rstd, h, pre, act = ctx.saved_tensors
         ln, (w1, b1, w2, b2) = ctx.params
         dout = dout.contiguous()
@@ -287,6 +349,27 @@ class MLPBlockFn(Function):
             K.colsum_(dpre, b1.main_grad, acc)
             K.gemm(dpre, h, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc)
             dh = K.gemm(dpre, w1.w16, b_mn=True)
+        _grads_done(w1, b1)
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None
+
+    @staticmethod
+    def _backward_mx(ctx, dout):
+        from . import mxfp8 as MX
+
+        x2d, mean, rstd, hcc, hcs, pre, acc_codes, acs = ctx.saved_tensors
+        ln, (w1, b1, w2, b2) = ctx.params
+        dout = dout.contiguous()
+        acc = FusedGradState.accumulate
+        hc, ac = _mx_t(hcc, hcs, MX.E4M3), _mx_t(acc_codes, acs, MX.E4M3)
+        grow, gcol = MX.mx_quantize_rc(dout, MX.E5M2)
+        K.colsum_(dout, b2.main_grad, acc)
+        dpre = MX.gemm_mxfp8(grow, w2.mx[1], aux=pre)  # dgrad with dGELU in the epilogue
+        MX.gemm_mxfp8(gcol, ac, out=w2.main_grad, accumulate=acc)
+        _grads_done(w2, b2)
+        prow, pcol = MX.mx_quantize_rc(dpre, MX.E5M2)
+        K.colsum_(dpre, b1.main_grad, acc)
+        MX.gemm_mxfp8(pcol, hc, out=w1.main_grad, accumulate=acc)
+        dh = MX.gemm_mxfp8(prow, w1.mx[1])
         _grads_done(w1, b1)
         return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None
 

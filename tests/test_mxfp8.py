@@ -241,3 +241,26 @@ def test_gpt_trains_with_mx_linears_on_cpu():
     assert losses[True][-1] < losses[True][0]
     for a, b in zip(losses[True], losses[False]):
         assert abs(a - b) / b < 0.05
+
+
+@pytest.mark.gpu
+@_gpu
+def test_fused_trainer_mx_recipe_tracks_tensor_recipe():
+    """GptTrainer with the MXFP8 recipe (block-scaled forward, dgrad and wgrad in the
+    fused blocks) trains like the per-tensor FP8 recipe on a small model."""
+    from mtorus.models.gpt import GptConfig
+    from mtorus.training.engine import GptTrainer
+
+    cfg = GptConfig(vocab_size=512, d_model=256, num_layers=2, num_heads=2, d_ff=1024, max_seq_len=128, dropout=0.0)
+    g = torch.Generator().manual_seed(3)
+    data = [torch.randint(0, 512, (4, 129), generator=g) for _ in range(8)]
+    curves = {}
+    for recipe in ("tensor", "mx"):
+        tr = GptTrainer(cfg, device="cuda", lr=1e-3, init="normal", seed=0, fp8=True, fp8_recipe=recipe)
+        curve = []
+        for t in data:
+            curve.append(float(tr.train_step(t[:, :-1].contiguous(), t[:, 1:].contiguous())))
+        curves[recipe] = curve
+    assert curves["mx"][-1] < curves["mx"][0]
+    for a, b in zip(curves["mx"], curves["tensor"]):
+        assert abs(a - b) / b < 0.05
