@@ -592,19 +592,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int m = row0 + lane;
       const float alpha = (ep.alpha ? *ep.alpha : 1.f) * (ep.alpha2 ? *ep.alpha2 : 1.f);
 #pragma unroll 1
-      for (int i = 0; i < P_BN / 32; ++i, ++chunk_count) {
+      for (int step = 0; step < P_BN / 32; ++step, ++chunk_count) {
         // MXFP8: accumulator 0 is read from its last chunk (the one accumulator 1 shares)
-        const int c = (MX && buf == 0) ? ((i + P_BN / 32 - 1) % (P_BN / 32)) : i;
+        const int c = (MX && buf == 0) ? ((step + P_BN / 32 - 1) % (P_BN / 32)) : step;
         uint32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC1_COL + c * 32, r);
         tmem_wait_ld();
         if constexpr (MX) {
-          if (i == 0) {
+          if (step == 0) {
             tc_fence_before();
             mbar_arrive_cluster(ovl_leader);
           }
         }
-        if (i == P_BN / 32 - 1) {
+        if (step == P_BN / 32 - 1) {
           // the whole accumulator buffer is in registers / smem now: release it
           tc_fence_before();
           mbar_arrive_cluster(buf ? tempty_leader1 : tempty_leader0);
