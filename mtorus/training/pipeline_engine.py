@@ -110,7 +110,8 @@ class PipelineTrainer:
                  checkpoint: CheckpointStrategy = CheckpointStrategy.Full, fp8: bool = True,
                  fp8_history: int = 16, lr: float = 3e-4, device=None, seed: int = 0,
                  bucket_mb: float = 25.0, loss_scale: Optional[DeviceLossScaleConfig] = None,
-                 max_grad_norm: float = 0.0, timed: bool = False, split: str = "balanced"):
+                 max_grad_norm: float = 0.0, timed: bool = False, split: str = "balanced",
+                 fp8_recipe: str = "tensor"):
         world = dist.get_world_size()
         if world != dp * pp:
             raise ValueError(f"world size {world} != dp {dp} x pp {pp}")
@@ -155,7 +156,7 @@ class PipelineTrainer:
         self.flat = self.model.flatten(self.device)
         self.fp8 = fp8
         if fp8:
-            st = self.model.enable_fp8(fp8_history)
+            st = self.model.enable_fp8(fp8_history, recipe=fp8_recipe)
             if dp > 1:
                 from ..ops.fp8 import NcclAmaxSync
 
