@@ -1,5 +1,6 @@
 #!/usr/bin/env python
-"""FP8 quantise kernel with and without the fused amax all-reduce (fused path (b)).
+"""FP8 quantise kernel with and without the fused amax all-reduce (the amax is
+published to every rank by the last block of each quantise kernel).
 
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 bench/fp8_quant_bench.py
 

@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Weight all-gather + FP8 GEMM (fused path (c)) against the NCCL baseline.
+"""Weight all-gather fused into the FP8 GEMM that consumes the weights, against the NCCL baseline.
 
 Each rank owns 1/N of the rows of an E4M3 weight W [N_out, K] (the GPT-1B FFN1
 weight: 8192 x 2048) and computes Y = X . W^T for its own activations X [M, K]:

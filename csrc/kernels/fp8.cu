@@ -438,7 +438,7 @@ void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::T
   MT_LAUNCH_CHECK();
 }
 
-// Quantise with the amax all-reduce of fused path (b): see fp8_quantize_ar_kernel.
+// Quantise with the fused amax all-reduce: see fp8_quantize_ar_kernel.
 void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
                      at::Tensor counter, const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
                      int64_t slot, int64_t parity, int64_t epoch, int64_t fmt) {
@@ -469,7 +469,7 @@ void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scal
 }
 
 // Quantise a 2-D bf16 gradient and (+)= its column sums into `colsum` (fp32 [F]).
-// table_ptrs empty: local amax only; otherwise the amax all-reduce of path (b).
+// table_ptrs empty: local amax only; otherwise the fused amax all-reduce.
 void fp8_quantize_colsum(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
                          at::Tensor colsum, bool accumulate, const c10::optional<at::Tensor>& counter,
                          const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap, int64_t slot,

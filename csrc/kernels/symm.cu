@@ -7,14 +7,14 @@
 //   rs_bucket      reduce-scatter of one gradient bucket: rank r sums chunk r of
 //                  the bucket over all peers' buffers (fp32 accumulate), writes
 //                  it into its own buffer and accumulates the squared norm and
-//                  a non-finite flag (overflow detection) -- fused path (a),
-//                  the reduction half;
+//                  a non-finite flag (overflow detection): the reduction half of
+//                  the fused data-parallel gradient path;
 //   scalars_ar     all-reduce of the per-rank norm partials (tiny);
 //   adam_shard_ag  Adam on this rank's shard (skipped on overflow, unscaled and
 //                  clipped by the device multiplier) whose new bf16 weights are
 //                  stored straight into every peer's weight buffer: the update
-//                  and the parameter all-gather in one pass -- fused path (a),
-//                  the optimizer half, and the weight broadcast of (c);
+//                  and the parameter all-gather in one pass: the optimizer half of
+//                  the fused data-parallel path, broadcasting the new weights;
 //   wait_flags     makes a stream wait until all peers reached an epoch;
 //   allreduce / allgather / broadcast / halo: standalone collectives for the
 //                  microbenchmark and the torus neighbour exchange (path d).

@@ -94,7 +94,7 @@ class NcclAmaxSync:
 
 
 class SymmAmaxSync:
-    """Fused path (b): the amax all-reduce runs inside the quantise kernels.  The
+    """The amax all-reduce fused into the quantise kernels.  The
     last block of each quantise launch stores the rank's running amax for that
     tensor role into every peer's table (symmetric memory, NVLink stores, tagged
     with the step's epoch, double-buffered by step parity); at the end of the step

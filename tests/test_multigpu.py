@@ -304,7 +304,7 @@ def _gather_gemm_body(rank, world):
 @pytest.mark.skipif(__import__("os").environ.get("MTORUS_GATHER_GEMM_TESTS") != "1",
                     reason="gather GEMM not yet run on B200s (MTORUS_GATHER_GEMM_TESTS=1 runs it)")
 def test_gather_b_gemm_matches_local_gemm_2gpu():
-    """Fused path (c): a GEMM that reads each B tile from the rank owning it equals
+    """Weight all-gather fused into the GEMM: a GEMM that reads each B tile from the rank owning it equals
     the same GEMM on a locally gathered B, bit for bit (same kernel, same tiles)."""
     for o in run_dist(_gather_gemm_body, 2, backend="nccl"):
         assert o["status"] == 0
