@@ -60,6 +60,8 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--dp", default="nccl", choices=["nccl", "symm"])
     ap.add_argument("--bf16", action="store_true", help="bf16 block GEMMs instead of FP8")
+    ap.add_argument("--fp8-recipe", default="tensor", choices=["tensor", "mx"],
+                    help="tensor: per-tensor delayed scaling; mx: MXFP8 1x32 block scales in all block GEMMs")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--metrics", default=None, help="append per-step JSON lines here (rank 0)")
     ap.add_argument("--checkpoint-dir", default=None)
@@ -106,8 +108,9 @@ def main(argv=None) -> int:
         if world % pp:
             raise SystemExit(f"world size {world} is not a multiple of num_stages {pp}")
         tr = PipelineTrainer(cfg, pp=pp, dp=world // pp, schedule=ScheduleType.OneF1B, num_microbatches=M,
-                             micro_batch=b, seq_len=S, fp8=not args.bf16, fp8_history=history, lr=tc.learning_rate,
-                             device=dev, seed=args.seed, loss_scale=ls, max_grad_norm=tc.clip_grad_norm)
+                             micro_batch=b, seq_len=S, fp8=not args.bf16, fp8_history=history,
+                             fp8_recipe=args.fp8_recipe, lr=tc.learning_rate, device=dev, seed=args.seed,
+                             loss_scale=ls, max_grad_norm=tc.clip_grad_norm)
         replicas = world // pp
         replica = tr.replica
     else:
@@ -115,7 +118,7 @@ def main(argv=None) -> int:
 
         tr = GptTrainer(cfg, device=dev, lr=tc.learning_rate, init="normal", seed=args.seed, dp=args.dp,
                         loss_scale=ls, max_grad_norm=tc.clip_grad_norm, warmup_steps=tc.warmup_steps,
-                        fp8=not args.bf16, fp8_history=history)
+                        fp8=not args.bf16, fp8_history=history, fp8_recipe=args.fp8_recipe)
         replicas, replica = world, rank
     if args.resume:
         load_checkpoint(args.resume, tr)
