@@ -62,6 +62,9 @@ void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const
                 const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta);
 void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt, double fmax);
 void copy_async(int64_t dst, int64_t src, int64_t bytes);
+void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at::Tensor& beta, double eps,
+                         at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, at::Tensor mean,
+                         at::Tensor rstd, int64_t fmt, double fmax);
 void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, int64_t fmt,
                     double fmax);
 void gemm_fp8_gather_b(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
@@ -185,6 +188,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("beta") = false);
   m.def("mx_quantize", &mx_quantize);
   m.def("copy_async", &copy_async);
+  m.def("layernorm_fwd_mx_rc", &layernorm_fwd_mx_rc);
   m.def("mx_quantize_rc", &mx_quantize_rc);
   m.def("gemm_fp8_gather_b", &gemm_fp8_gather_b, py::arg("A"), py::arg("a_mn"), py::arg("a_fmt"), py::arg("B"),
         py::arg("b_mn"), py::arg("b_fmt"), py::arg("b_peers"), py::arg("shard_rows"), py::arg("D"),

@@ -14,6 +14,7 @@
 #include <cstring>
 
 #include "amax_publish.cuh"
+#include "mx.cuh"
 
 namespace mtorus {
 
@@ -328,37 +329,6 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(const bf16* __restrict
 // in shared memory; thread t quantises row block (t / 8, t % 8) of the tile and then
 // column t, whose 32 codes are one contiguous 32-byte run of the transposed output.
 // R and C multiples of 32; a tile may overhang C (columns past C are skipped).
-__device__ __forceinline__ void mx_block(const float (&v)[32], int ef, uint32_t mf, int fmt, uint32_t (&w)[8],
-                                         uint8_t& sfb) {
-  float amax = 0.f;
-  bool finite = true;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    amax = fmaxf(amax, fabsf(v[i]));
-    finite &= isfinite(v[i]);
-  }
-  int X = 0;
-  if (amax > 0.f) {
-    const uint32_t ua = __float_as_uint(amax);
-    X = (int)((ua >> 23) & 0xFF) - ef + ((ua & 0x7FFFFF) > mf ? 1 : 0);
-    X = max(-127, min(127, X));
-  }
-  const float inv = __uint_as_float((uint32_t)(127 - min(X, 126)) << 23);
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float* t = v + 4 * q;
-    const uint16_t lo = fmt == 0 ? cvt2_e4m3(t[0] * inv, t[1] * inv) : cvt2_e5m2(t[0] * inv, t[1] * inv);
-    const uint16_t hi = fmt == 0 ? cvt2_e4m3(t[2] * inv, t[3] * inv) : cvt2_e5m2(t[2] * inv, t[3] * inv);
-    w[q] = (uint32_t)lo | ((uint32_t)hi << 16);
-  }
-  sfb = finite ? (uint8_t)(X + 127) : (uint8_t)255;
-}
-
-__device__ __forceinline__ int64_t mx_sf_offset(int r, int j, int nkb4) {
-  const int rr = r & 127;
-  return ((int64_t)(r >> 7) * nkb4 + (j >> 2)) * 512 + (rr & 31) * 16 + (rr >> 5) * 4 + (j & 3);
-}
-
 __global__ void __launch_bounds__(256) mx_quantize_rc_kernel(const bf16* __restrict__ x, int64_t ldx, int R, int C,
                                                              int fmt, uint32_t fmax_bits, uint8_t* __restrict__ rc,
                                                              uint8_t* __restrict__ rsf, uint8_t* __restrict__ cc,
@@ -406,12 +376,6 @@ __global__ void __launch_bounds__(256) mx_quantize_rc_kernel(const bf16* __restr
     dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
     csf[mx_sf_offset(c0 + t, r0 / 32, (R + 127) / 128)] = sfb;
   }
-}
-
-// Fills every byte of a scale tensor with 127 (the value of padding slots).
-__global__ void fill_u8_kernel(uint8_t* p, int64_t n, uint8_t v) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    p[i] = v;
 }
 
 static int q_grid(size_t n, int per) {
@@ -619,9 +583,9 @@ void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tens
   const float fm = (float)fmax;
   uint32_t fbits;
   std::memcpy(&fbits, &fm, 4);
-  const int fill_grid = num_sms() * 4;
-  fill_u8_kernel<<<fill_grid, 256, 0, cur_stream()>>>(reinterpret_cast<uint8_t*>(rsf.data_ptr()), rsf.numel(), 127);
-  fill_u8_kernel<<<fill_grid, 256, 0, cur_stream()>>>(reinterpret_cast<uint8_t*>(csf.data_ptr()), csf.numel(), 127);
+  // padding slots of the scale atoms hold 127 (a scale of 1)
+  C10_CUDA_CHECK(cudaMemsetAsync(rsf.data_ptr(), 127, (size_t)rsf.numel(), cur_stream()));
+  C10_CUDA_CHECK(cudaMemsetAsync(csf.data_ptr(), 127, (size_t)csf.numel(), cur_stream()));
   dim3 grid((unsigned)((C + 255) / 256), (unsigned)(R / 32));
   mx_quantize_rc_kernel<<<grid, 256, 0, cur_stream()>>>(
       reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), (int)R, (int)C, (int)fmt, fbits,

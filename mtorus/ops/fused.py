@@ -175,8 +175,8 @@ class AttnBlockFn(Function):
             # inputs are quantised both ways once (row-wise now, column-wise for wgrad)
             from . import mxfp8 as MX
 
-            h, mean, rstd = _ln_fwd(x2d, ln)
-            hr, hc = MX.mx_quantize_rc(h, MX.E4M3)
+            gamma, beta, eps = ln
+            hr, hc, mean, rstd = MX.mx_layernorm_rc(x2d, gamma.data, beta.data, eps, MX.E4M3)
             qkv = MX.gemm_mxfp8(hr, wq.mx[0], bias=bq.data)
             o, lse = attention_fwd(qkv, B, S, H)
             orow, ocol = MX.mx_quantize_rc(o, MX.E4M3)
@@ -283,8 +283,8 @@ class MLPBlockFn(Function):
         if _mx(fp8):
             from . import mxfp8 as MX
 
-            h, mean, rstd = _ln_fwd(x2d, ln)
-            hr, hc = MX.mx_quantize_rc(h, MX.E4M3)
+            gamma, beta, eps = ln
+            hr, hc, mean, rstd = MX.mx_layernorm_rc(x2d, gamma.data, beta.data, eps, MX.E4M3)
             act = torch.empty_like(pre)
             MX.gemm_mxfp8(hr, w1.mx[0], out=pre, bias=b1.data, act=act)  # pre-activation and GELU
             ar, ac = MX.mx_quantize_rc(act, MX.E4M3)

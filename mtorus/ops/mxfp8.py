@@ -164,6 +164,34 @@ def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = Non
     return MxTensor(rc, rsf, int(fmt)), MxTensor(cc, csf, int(fmt))
 
 
+def mx_layernorm_rc(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+                    fmt: int = E4M3, fmax: Optional[float] = None):
+    """LayerNorm of x [R, d] straight into MXFP8, row-wise ([R, d]) and column-wise
+    ([d, R]), plus the fp32 mean / rstd rows for the backward: one kernel, no bf16
+    output (CUDA, R % 32 == 0, d a multiple of 256 up to 2048).  Elsewhere: LayerNorm,
+    rounded to bf16, then ``mx_quantize_rc``."""
+    R, d = x.shape
+    if x.is_cuda and x.dtype == torch.bfloat16 and R % 32 == 0 and d % 256 == 0 and d <= 2048:
+        fmax = float(MX_FMT_MAX[fmt] if fmax is None else fmax)
+        x = x.contiguous()
+        dev = x.device
+        rc = torch.empty((R, d), dtype=torch.uint8, device=dev)
+        cc = torch.empty((d, R), dtype=torch.uint8, device=dev)
+        rsf = torch.empty(sf_numel(R, d), dtype=torch.uint8, device=dev)
+        csf = torch.empty(sf_numel(d, R), dtype=torch.uint8, device=dev)
+        mean = torch.empty(R, dtype=torch.float32, device=dev)
+        rstd = torch.empty(R, dtype=torch.float32, device=dev)
+        _cuda().layernorm_fwd_mx_rc(x, gamma.float().contiguous(), beta.float().contiguous(), float(eps), rc, rsf,
+                                    cc, csf, mean, rstd, int(fmt), fmax)
+        return MxTensor(rc, rsf, int(fmt)), MxTensor(cc, csf, int(fmt)), mean, rstd
+    xf = x.float()
+    mean = xf.mean(-1)
+    rstd = torch.rsqrt(xf.var(-1, unbiased=False) + eps)
+    h = ((xf - mean[:, None]) * rstd[:, None] * gamma.float() + beta.float()).to(torch.bfloat16)
+    r, c = mx_quantize_rc(h, fmt, fmax)
+    return r, c, mean, rstd
+
+
 def _mm(a: MxTensor, b: MxTensor, out_dtype, bias=None) -> torch.Tensor:
     if a.codes.is_cuda:
         return gemm_mxfp8(a, b, bias=bias, out_dtype=out_dtype)
@@ -242,4 +270,4 @@ def gemm_mxfp8_ref(a: MxTensor, b: MxTensor) -> torch.Tensor:
 
 
 __all__ = ["E4M3", "E5M2", "MX_FMT_MAX", "MxTensor", "sf_numel", "sf_offsets", "mx_quantize", "mx_quantize_ref",
-           "mx_quantize_rc", "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_ref", "MxLinearFn", "mx_linear", "enable_mx_linears"]
+           "mx_quantize_rc", "mx_layernorm_rc", "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_ref", "MxLinearFn", "mx_linear", "enable_mx_linears"]

@@ -264,3 +264,37 @@ def test_fused_trainer_mx_recipe_tracks_tensor_recipe():
     assert curves["mx"][-1] < curves["mx"][0]
     for a, b in zip(curves["mx"], curves["tensor"]):
         assert abs(a - b) / b < 0.05
+
+
+def test_mx_layernorm_reference_path():
+    from mtorus.ops.mxfp8 import mx_layernorm_rc
+
+    torch.manual_seed(4)
+    x = (torch.randn(64, 256) * 3 + 1).bfloat16()
+    g, b = torch.rand(256) + 0.5, torch.randn(256) * 0.1
+    r, c, mean, rstd = mx_layernorm_rc(x, g, b, 1e-5)
+    h = torch.nn.functional.layer_norm(x.float(), (256,), g, b, 1e-5)
+    assert torch.allclose(mean, x.float().mean(-1), atol=1e-5)
+    assert float((mx_dequantize(r) - h).abs().max()) <= 2 ** -4 * float(h.abs().max()) + 1e-6
+    hb = ((x.float() - mean[:, None]) * rstd[:, None] * g + b).bfloat16().float()
+    assert torch.equal(c.codes, mx_quantize_ref(hb.t().contiguous(), E4M3).codes)
+
+
+@pytest.mark.gpu
+@_gpu
+def test_cuda_layernorm_mx_matches_reference():
+    from mtorus.ops.mxfp8 import mx_layernorm_rc
+
+    torch.manual_seed(5)
+    R, d = 256, 2048
+    x = (torch.randn(R, d) * 2 + 0.5).bfloat16()
+    g, b = torch.rand(d) + 0.5, torch.randn(d) * 0.1
+    r_ref, c_ref, m_ref, s_ref = mx_layernorm_rc(x, g, b, 1e-5)
+    r, c, m, s = mx_layernorm_rc(x.cuda(), g.cuda(), b.cuda(), 1e-5)
+    assert torch.allclose(m.cpu(), m_ref, atol=1e-4) and torch.allclose(s.cpu(), s_ref, rtol=1e-4)
+    # bf16 rounding of the normalised value may differ by one ulp: compare the decoded operands
+    for got, ref in ((r, r_ref), (c, c_ref)):
+        dg = mx_dequantize(MxTensor(got.codes.cpu(), got.sf.cpu(), got.fmt))
+        dr = mx_dequantize(ref)
+        assert float((dg - dr).abs().max()) <= 2 ** -3 * float(dr.abs().max())
+        assert float((got.sf.cpu() == ref.sf).float().mean()) > 0.99
