@@ -264,3 +264,16 @@ def test_native_token_loader_is_roughly_uniform():
         counts += torch.bincount(x.reshape(-1), minlength=10).float()
     frac = counts / counts.sum()
     assert float((frac - 0.1).abs().max()) < 0.01
+
+
+def test_native_token_loader_rejects_bad_arguments():
+    from mtorus._ext import host
+    from mtorus.models.data import NativeSyntheticDataLoader
+
+    with pytest.raises(Exception):
+        host().TokenLoader(0, 16, 100, 3, 0, False)
+    dl = NativeSyntheticDataLoader(2, 8, 100, 3)
+    with pytest.raises(Exception):
+        dl.seek(4)  # past num_batches
+    dl.seek(3)
+    assert dl.next() is None
