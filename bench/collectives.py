@@ -55,7 +55,8 @@ def main():
     ap.add_argument("--min-kb", type=int, default=4)
     ap.add_argument("--max-mb", type=int, default=1024)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--ops", default="allreduce_f32,allreduce_bf16,allreduce_fp8,broadcast,allgather,halo")
+    ap.add_argument("--ops", default="allreduce_f32,allreduce_bf16,allreduce_fp8,broadcast,broadcast_scatter,"
+                                      "allgather,halo")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -106,6 +107,14 @@ def main():
                 f_n = lambda: dist.broadcast(nccl_buf[:n], 0)
                 f_m = lambda: col.broadcast(nbytes, 0)
                 f_v = (lambda: col.broadcast_nvls(nbytes, 0)) if col.nvls else None
+                factor = 1.0
+            elif op == "broadcast_scatter":
+                # scatter from the root by copy engine, then every rank multicasts its chunk
+                if not col.nvls:
+                    continue
+                n = nbytes // 4
+                f_n = lambda: dist.broadcast(nccl_buf[:n], 0)
+                f_m = lambda: col.broadcast_scatter_nvls(nbytes, 0)
                 factor = 1.0
             elif op == "allgather":
                 if nbytes * world > max_bytes:

@@ -279,6 +279,33 @@ class SymmCollectives:
             _cuda().symm_broadcast_mc(self.buf.tensor.data_ptr(), self.buf.mc, nbytes, self.ctas)
         _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 11, ep, 40)
 
+    def broadcast_scatter_nvls(self, nbytes: int, root: int = 0) -> None:
+        """Broadcast as scatter + multicast: the root's copy engine sends chunk p of its
+        bytes to rank p (one ``cudaMemcpyAsync`` per peer over NVLink), then every rank
+        stores its chunk once into the multicast address (``multimem.st``) and the
+        switch writes it into every rank's buffer.  The root's link carries (n-1)/n of
+        the bytes once and the multicast stores run on all ranks at the same time,
+        instead of one GPU issuing every multicast store (``broadcast_nvls``)."""
+        if nbytes % 16:
+            raise ValueError("broadcast_scatter_nvls: nbytes must be a multiple of 16")
+        n = self.world
+        chunk = ((nbytes + n - 1) // n + 15) // 16 * 16
+        ep = self._slot()
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 12, ep, 41)  # every rank is past its last read
+        if self.me == root:
+            base = self.buf.tensor.data_ptr()
+            for p in range(n):
+                lo = min(nbytes, p * chunk)
+                ln = min(nbytes, lo + chunk) - lo
+                if p != root and ln > 0:
+                    _cuda().copy_async(self.buf.ptrs[p] + lo, base + lo, ln)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 13, ep, 42)  # chunk me has landed here
+        lo = min(nbytes, self.me * chunk)
+        ln = min(nbytes, lo + chunk) - lo
+        if ln > 0:
+            _cuda().symm_broadcast_mc(self.buf.tensor.data_ptr() + lo, self.buf.mc + lo, ln, self.ctas)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 14, ep, 43)
+
     def all_gather(self, nbytes: int) -> None:
         """Each rank's first nbytes of ``buf`` land in slot rank of every peer's ``recv``."""
         ep = self._slot()
@@ -356,13 +383,13 @@ class GatheredOperand:
         """Every rank's shard writes (stream-ordered before this call) become visible
         to all ranks' later GEMMs.  Call on every rank."""
         self.epoch += 1
-        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 0, self.epoch, 37)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 0, self.epoch, 44)
 
     def retire(self) -> None:
         """Every rank's GEMMs on the current shards are done (stream order), so owners
         may rewrite them.  Call on every rank."""
         self.retired += 1
-        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 1, self.retired, 38)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 1, self.retired, 45)
 
     def gemm(self, a: torch.Tensor, a_fmt: int, b_fmt: int, out: Optional[torch.Tensor] = None, *,
              a_mn: bool = False, b_mn: bool = False, bias=None, residual=None, act=None, aux=None, alpha=None,

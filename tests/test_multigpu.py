@@ -310,3 +310,31 @@ def test_gather_b_gemm_matches_local_gemm_2gpu():
         assert o["status"] == 0
         assert o["kmajor"] and o["mnmajor"] and o["kmajor_overlap"]
         assert o["mnmajor_overlap_err"] < 1e-5  # per-shard partial sums: fp32 summation order differs
+
+
+def _bc_scatter_body(rank, world):
+    import torch
+
+    from mtorus.parallel.symm import SymmCollectives
+
+    torch.cuda.set_device(rank)
+    c = SymmCollectives(f"cuda:{rank}", max_bytes=1 << 22)
+    out = {"nvls": c.nvls}
+    if c.nvls:
+        n = 1040 // 4  # two uneven chunks (528 + 512 bytes)
+        c.buf.tensor[:n] = (torch.arange(n, device="cuda", dtype=torch.float32) + 7) if rank == 1 else -1.0
+        c.broadcast_scatter_nvls(n * 4, root=1)
+        out["bc"] = c.buf.tensor[:n].clone().cpu()
+    out["status"] = c.ctx.status()
+    torch.cuda.synchronize()
+    return out
+
+
+@needs2
+@pytest.mark.skipif(__import__("os").environ.get("MTORUS_BCAST_SCATTER_TESTS") != "1",
+                    reason="scatter + multicast broadcast not yet run on B200s (MTORUS_BCAST_SCATTER_TESTS=1 runs it)")
+def test_broadcast_scatter_multicast_2gpu():
+    for o in run_dist(_bc_scatter_body, 2, backend="nccl"):
+        assert o["status"] == 0
+        if o["nvls"]:
+            assert torch.equal(o["bc"], torch.arange(260, dtype=torch.float32) + 7)
