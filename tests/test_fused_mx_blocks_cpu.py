@@ -170,3 +170,22 @@ def test_mlp_block_mx_branch_matches_fp32_autograd(cpu_kernels):
     assert _rel(xin.grad, xr.grad) < 0.1
     for name, p in dict(w1=w1, b1=b1, w2=w2, b2=b2, gamma=gamma, beta=beta).items():
         assert _rel(p.main_grad, P[name].grad) < 0.1, name
+
+
+def test_model_refreshes_mx_weights_both_ways():
+    """GptModel.enable_fp8(recipe="mx") + refresh_fp8_weights(): every block weight gets
+    its row-wise (forward) and column-wise (dgrad) encodings of the current bf16 copy."""
+    from mtorus.models.gpt import GptConfig, GptModel
+
+    m = GptModel(GptConfig(256, 128, 2, 1, 256, 128, 0.0), init="reference")
+    m.flatten(torch.device("cpu"))
+    assert m.enable_fp8(16, recipe="mx").recipe == "mx"
+    m.refresh_fp8_weights()
+    for name, w in m.fp8_weights():
+        r, c = w.mx
+        assert r.codes.shape == w.shape and c.codes.shape == w.shape[::-1], name
+        assert torch.equal(r.codes, MX.mx_quantize_ref(w.w16, MX.E4M3).codes)
+        assert torch.equal(c.codes, MX.mx_quantize_ref(w.w16.t().contiguous(), MX.E4M3).codes)
+        assert not hasattr(w, "w8")  # the per-tensor copies are not allocated under MX
+    with pytest.raises(ValueError):
+        m.enable_fp8(16, recipe="block")
