@@ -62,6 +62,10 @@ void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const
                 const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta);
 void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt, double fmax);
 void copy_async(int64_t dst, int64_t src, int64_t bytes);
+void dp_quant_e5m2(int64_t grad, int64_t codes, int64_t sf, int64_t nelem);
+void symm_rs_bucket_e5m2(const std::vector<int64_t>& codes, const std::vector<int64_t>& sfs,
+                         const std::vector<int64_t>& flags, int64_t me, int64_t start, int64_t len, int64_t clen,
+                         int64_t slot, int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t mine);
 void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at::Tensor& beta, double eps,
                          at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, at::Tensor mean,
                          at::Tensor rstd, int64_t fmt, double fmax);
@@ -188,6 +192,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("beta") = false);
   m.def("mx_quantize", &mx_quantize);
   m.def("copy_async", &copy_async);
+  m.def("dp_quant_e5m2", &dp_quant_e5m2);
+  m.def("symm_rs_bucket_e5m2", &symm_rs_bucket_e5m2);
   m.def("layernorm_fwd_mx_rc", &layernorm_fwd_mx_rc);
   m.def("mx_quantize_rc", &mx_quantize_rc);
   m.def("gemm_fp8_gather_b", &gemm_fp8_gather_b, py::arg("A"), py::arg("a_mn"), py::arg("a_fmt"), py::arg("B"),

@@ -25,7 +25,10 @@
 // by a wall-clock limit (globaltimer); on expiry the kernel records a status
 // code, skips the dependent work and returns, so a missing peer never hangs the
 // GPU.  No TMA, no cluster launches.
+#include <cstring>
+
 #include "common.cuh"
+#include "mx.cuh"
 
 namespace mtorus {
 
@@ -538,6 +541,97 @@ static int* symm_status_ptr() {
   return s;
 }
 
+// ------------------------------------------------------------------ E5M2 gradient transport (DP buckets)
+// Opt-in variant of rs_bucket that moves gradients over NVLink as E5M2 codes with
+// one power-of-two scale per 32 values (the MX block rule of mx.cuh: the block's
+// amax maps to at most the format maximum, 57344, so nothing saturates): 33 bytes
+// per 32 gradients instead of 128.  dp_quant_e5m2_kernel encodes this rank's
+// finished bucket into its symmetric code / scale buffers; rs_bucket_e5m2_kernel
+// then decodes chunk me of every peer's bucket, sums in fp32, averages, writes the
+// result into this rank's fp32 gradient buffer and accumulates the squared norm
+// and the non-finite count exactly like rs_bucket.  A block holding a NaN / Inf
+// carries the NaN scale byte and decodes to NaN, so overflow detection still sees it.
+__global__ void __launch_bounds__(256) dp_quant_e5m2_kernel(const float* __restrict__ g, uint8_t* __restrict__ codes,
+                                                            uint8_t* __restrict__ sf, int64_t nblocks,
+                                                            uint32_t fmax_bits) {
+  const int ef = (int)((fmax_bits >> 23) & 0xFF);
+  const uint32_t mf = fmax_bits & 0x7FFFFF;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    float v[32];
+    const float4* src = reinterpret_cast<const float4*>(g + b * 32);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 t = src[q];
+      v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+    }
+    uint32_t w[8];
+    uint8_t sfb;
+    mx_block(v, ef, mf, 1, w, sfb);
+    uint4* dst = reinterpret_cast<uint4*>(codes + b * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    sf[b] = sfb;
+  }
+}
+
+// 2^(s - 127) for a UE8M0 scale byte (0: 2^-127, a subnormal; 255: NaN).
+__device__ __forceinline__ float ue8m0_value(uint32_t s) {
+  if (s == 255u) return __uint_as_float(0x7FC00000u);
+  if (s == 0u) return __uint_as_float(0x00400000u);
+  return __uint_as_float(s << 23);
+}
+
+__global__ void __launch_bounds__(512) rs_bucket_e5m2_kernel(PeerPtrs codes, PeerPtrs sfs, PeerPtrs flags,
+                                                             uint32_t* my_flags, int me, int n, int64_t start,
+                                                             int64_t len, int64_t clen, int slot, uint32_t epoch,
+                                                             float inv_n, float* __restrict__ mine, float* st,
+                                                             int* status) {
+  __shared__ float red[32];
+  if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 26)) return;
+  const int64_t c0 = start + (int64_t)me * clen;
+  const int64_t c1 = min(start + len, c0 + clen);
+  const int64_t nb = (c1 > c0) ? (c1 - c0) / 32 : 0;
+  float acc2 = 0.f;
+  int bad = 0;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e0 = c0 + b * 32;
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p) {
+      if (p < n) {
+        const uint4* cp = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(codes.p[p]) + e0);
+        const uint4 c0v = cp[0], c1v = cp[1];
+        const uint32_t words[8] = {c0v.x, c0v.y, c0v.z, c0v.w, c1v.x, c1v.y, c1v.z, c1v.w};
+        const float scale = ue8m0_value(reinterpret_cast<const uint8_t*>(sfs.p[p])[e0 / 32]);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          float a, bb;
+          dec8x2((uint16_t)(words[k >> 1] >> ((k & 1) * 16)), 1, a, bb);
+          acc[2 * k] += a * scale;
+          acc[2 * k + 1] += bb * scale;
+        }
+      }
+    }
+    float4* dst = reinterpret_cast<float4*>(mine + e0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 t = make_float4(acc[4 * q] * inv_n, acc[4 * q + 1] * inv_n, acc[4 * q + 2] * inv_n, acc[4 * q + 3] * inv_n);
+      dst[q] = t;
+      acc2 += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+      bad |= !(isfinite(t.x) && isfinite(t.y) && isfinite(t.z) && isfinite(t.w));
+    }
+  }
+  acc2 = block_sum(acc2, red);
+  const int anybad = __syncthreads_or(bad);
+  if (threadIdx.x == 0) {
+    atomicAdd(st + 0, acc2);
+    if (anybad) atomicAdd(st + 1, 1.f);
+  }
+}
+
 int64_t symm_status(bool reset) {
   int h = 0;
   C10_CUDA_CHECK(cudaMemcpy(&h, symm_status_ptr(), sizeof(int), cudaMemcpyDeviceToHost));
@@ -566,6 +660,37 @@ void symm_rs_bucket_mc(int64_t grads_mc, const std::vector<int64_t>& grads, cons
       (uint64_t)grads_mc, reinterpret_cast<float*>(grads[me]), to_peers(flags),
       reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, start, len, clen, (int)slot, (uint32_t)epoch,
       (float)inv_n, st.data_ptr<float>(), symm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+// E5M2 gradient transport: encode this rank's bucket (fp32 at grad, nelem a multiple of 32)
+// into codes / sf (one scale byte per 32 values) on the current stream.
+void dp_quant_e5m2(int64_t grad, int64_t codes, int64_t sf, int64_t nelem) {
+  MT_CHECK(nelem % 32 == 0 && grad % 16 == 0 && codes % 16 == 0, "dp_quant_e5m2: 32-element blocks, aligned buffers");
+  if (nelem == 0) return;
+  const float fm = 57344.f;  // E5M2 largest finite value
+  uint32_t fbits;
+  std::memcpy(&fbits, &fm, 4);
+  const int64_t nblocks = nelem / 32;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nblocks + 255) / 256, (int64_t)num_sms() * 8));
+  dp_quant_e5m2_kernel<<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<const float*>(grad),
+                                                       reinterpret_cast<uint8_t*>(codes), reinterpret_cast<uint8_t*>(sf),
+                                                       nblocks, fbits);
+  MT_LAUNCH_CHECK();
+}
+
+// rs_bucket over E5M2-encoded buckets: codes / sfs are every rank's code and scale
+// buffers (element and block offsets match the fp32 gradient buffer), mine this
+// rank's fp32 gradient buffer that receives the averaged chunk.
+void symm_rs_bucket_e5m2(const std::vector<int64_t>& codes, const std::vector<int64_t>& sfs,
+                         const std::vector<int64_t>& flags, int64_t me, int64_t start, int64_t len, int64_t clen,
+                         int64_t slot, int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t mine) {
+  MT_CHECK(start % 32 == 0 && len % 32 == 0 && clen % 32 == 0, "rs_bucket_e5m2: 32-element aligned bucket and chunks");
+  MT_CHECK(codes.size() == flags.size() && sfs.size() == flags.size(), "rs_bucket_e5m2: one buffer per rank");
+  rs_bucket_e5m2_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(
+      to_peers(codes), to_peers(sfs), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me,
+      (int)flags.size(), start, len, clen, (int)slot, (uint32_t)epoch, (float)inv_n, reinterpret_cast<float*>(mine),
+      st.data_ptr<float>(), symm_status_ptr());
   MT_LAUNCH_CHECK();
 }
 

@@ -91,7 +91,8 @@ class SymmBucketReducer:
     """Reduce-scatter of the flat gradient buffer, bucket by bucket, over NVLink."""
 
     def __init__(self, flat, group=None, bucket_bytes: int = 25 * 1024 * 1024, ctas: Optional[int] = None,
-                 ctx: Optional[SymmContext] = None, reserve_sms: Optional[int] = None):
+                 ctx: Optional[SymmContext] = None, reserve_sms: Optional[int] = None,
+                 grad_fp8: Optional[bool] = None):
         import os
 
         ctas = ctas if ctas is not None else int(os.environ.get("MTORUS_DP_CTAS", "16"))
@@ -126,6 +127,14 @@ class SymmBucketReducer:
         self._reserved = False
         # NVLS reduce-scatter (multimem.ld_reduce) when asked for and the buffer has a multicast binding
         self.nvls = os.environ.get("MTORUS_DP_NVLS") == "1" and self.flat.symm_grad.mc != 0
+        # E5M2 gradient transport (opt-in): buckets cross NVLink as E5M2 codes with one
+        # power-of-two scale per 32 values, decoded and summed in fp32 by the reduce kernel
+        self.grad_fp8 = grad_fp8 if grad_fp8 is not None else os.environ.get("MTORUS_DP_GRAD_FP8") == "1"
+        if self.grad_fp8:
+            if flat.numel % 32:
+                raise ValueError("E5M2 gradient transport needs a flat buffer of whole 32-value blocks")
+            self.codes = SymmBuffer(flat.numel, torch.uint8, flat.device, group, zero=False)
+            self.gsf = SymmBuffer(flat.numel // 32, torch.uint8, flat.device, group, zero=False)
         self._reset()
 
     def _reset(self):
@@ -156,7 +165,14 @@ class SymmBucketReducer:
         ev.record()
         self.stream.wait_event(ev)
         with torch.cuda.stream(self.stream):
-            if self.nvls:
+            if self.grad_fp8:
+                g = self.flat.symm_grad
+                _cuda().dp_quant_e5m2(g.tensor.data_ptr() + 4 * s, self.codes.tensor.data_ptr() + s,
+                                      self.gsf.tensor.data_ptr() + s // 32, e - s)
+                _cuda().symm_rs_bucket_e5m2(self.codes.ptrs, self.gsf.ptrs, self.ctx.flags.ptrs, self.me, s, e - s,
+                                            self.clen[b], b, self.epoch, self.state, self.ctas, 1.0 / self.world,
+                                            g.tensor.data_ptr())
+            elif self.nvls:
                 _cuda().symm_rs_bucket_mc(self.flat.symm_grad.mc, self.flat.symm_grad.ptrs, self.ctx.flags.ptrs,
                                           self.me, s, e - s, self.clen[b], b, self.epoch, self.state, self.ctas,
                                           1.0 / self.world)
