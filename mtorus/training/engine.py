@@ -23,12 +23,23 @@ from ..ops.fused import FusedGradState
 from .fused_optim import DeviceLossScaleConfig, FusedAdam
 
 
+def require_no_dropout(config) -> None:
+    """The fused GPU blocks have no dropout (the reference applies p = 0.1 at four sites,
+    examples/gpt-1b/src/transformer.rs:77,108,148,154 and model.rs:118); reject a config
+    that asks for it instead of silently training without it.  The reference-semantics
+    model (``GptModel.forward``) keeps dropout."""
+    if getattr(config, "dropout", 0.0) > 0.0:
+        raise ValueError(f"the fused trainers run without dropout; this config asks for dropout={config.dropout} "
+                         "(use dropout=0.0, or the reference-semantics GptModel.forward path)")
+
+
 class GptTrainer:
     def __init__(self, config: GptConfig, device="cuda", lr: float = 3e-4, init: str = "normal",
                  seed: int = 0, dp_group=None, dp: str = "nccl", bucket_mb: float = 25.0,
                  loss_scale: Optional[DeviceLossScaleConfig] = None, max_grad_norm: float = 0.0,
                  weight_decay: float = 0.0, warmup_steps: int = 0, fp8: bool = False,
                  fp8_history: int = 16, fp8_recipe: str = "tensor"):
+        require_no_dropout(config)
         self.config = config
         self.device = torch.device(device)
         torch.manual_seed(seed)

@@ -112,6 +112,9 @@ class PipelineTrainer:
                  bucket_mb: float = 25.0, loss_scale: Optional[DeviceLossScaleConfig] = None,
                  max_grad_norm: float = 0.0, timed: bool = False, split: str = "balanced",
                  fp8_recipe: str = "tensor"):
+        from .engine import require_no_dropout
+
+        require_no_dropout(config)
         world = dist.get_world_size()
         if world != dp * pp:
             raise ValueError(f"world size {world} != dp {dp} x pp {pp}")

@@ -396,3 +396,11 @@ def test_metrics_logger_jsonl_and_summary(tmp_path):
     assert [r["step"] for r in recs] == [1, 2] and recs[0]["grad_norm"] == 1.5 and recs[1]["extra_key"] == 3
     assert recs[0]["loss_scale"] == 65536.0 and "tokens_per_s" in recs[0]
     assert s["total_steps"] == 2 and s["avg_loss"] == 6.0 and s["overflow_count"] == 1
+
+
+def test_fused_trainers_reject_dropout():
+    from mtorus.models.gpt import GptConfig
+    from mtorus.training.engine import GptTrainer
+
+    with pytest.raises(ValueError, match="dropout"):
+        GptTrainer(GptConfig.gpt_1b(), device="cpu")  # the reference config has dropout 0.1
