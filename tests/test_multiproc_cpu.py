@@ -179,3 +179,42 @@ def test_gpt_dp2_pp2_gloo_matches_single_process():
     # last stages (ranks 1 and 3) report each replica's micro-batch losses
     mean_loss = (sum(res[1]["losses"]) + sum(res[3]["losses"])) / 8
     assert abs(mean_loss - total / 2) < 1e-4
+
+
+def _dp_e5m2_body(rank, world):
+    from mtorus.parallel.data_parallel import NcclBucketReducer
+    from mtorus.parallel.flat import FlatParams
+
+    torch.manual_seed(0)
+    m = torch.nn.Sequential(torch.nn.Linear(16, 32), torch.nn.Linear(32, 40), torch.nn.Linear(40, 8))
+    flat = FlatParams([[p] for p in m.parameters()], "cpu", with_w16=False)
+    red = NcclBucketReducer(flat, None, bucket_bytes=1024, grad_fp8=True)
+    g = torch.Generator().manual_seed(10 + rank)
+    for p in m.parameters():
+        p.main_grad.copy_(torch.randn(p.main_grad.shape, generator=g) * 10.0 ** (rank - 2))
+    before = flat.grad.clone()
+    for p in reversed(list(m.parameters())):
+        red.on_ready([p])
+    red.finish()
+    return before, flat.grad.clone(), [tuple(r) for r in red.plan.ranges]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_bucket_reducer_e5m2_transport(world):
+    """E5M2 transport through the NCCL-style reducer (gloo here): every rank ends with
+    the same bytes, equal to the bf16-rounded mean of the E5M2-decoded gradients."""
+    from mtorus.parallel.data_parallel import e5m2_decode, e5m2_encode
+
+    res = run_dist(_dp_e5m2_body, world)
+    inputs = [r[0] for r in res]
+    for r in res[1:]:
+        assert torch.equal(r[1], res[0][1])  # identical on every rank
+    out = res[0][1]
+    for s, e in res[0][2]:
+        L = e - s
+        pad = (-L) % 32
+        dec = [e5m2_decode(*e5m2_encode(torch.cat([x[s:e], torch.zeros(pad)])))[:L] for x in inputs]
+        ref = (sum(dec) * (1.0 / world)).to(torch.bfloat16).float()
+        assert torch.equal(out[s:e], ref)
+        exact = sum(x[s:e] for x in inputs) / world
+        assert float((out[s:e] - exact).norm() / exact.norm()) < 0.1
