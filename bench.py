@@ -210,6 +210,8 @@ def main() -> int:
             "micro_batch_per_gpu": B,
             "parallelism": f"dp{world}",
             "dp_reduce": args.dp if world > 1 else "none",
+            "dp_grad_transport": ("e5m2 (1x32 power-of-two scales)" if os.environ.get("MTORUS_DP_GRAD_FP8") == "1"
+                                  else "fp32") if world > 1 else "none",
             "gemm": {"fp8": "tcgen05 kind::f8f6f4 fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, fp32 accumulate",
                      "mxfp8": "tcgen05 kind::mxf8f6f4 block-scaled fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, "
                               "fp32 accumulate",
