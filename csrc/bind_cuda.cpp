@@ -37,7 +37,7 @@ at::Tensor bias_gelu_fwd(at::Tensor pre, const c10::optional<at::Tensor>& bias);
 void gelu_bwd_(at::Tensor dact, const at::Tensor& pre);
 void colsum_(const at::Tensor& x, at::Tensor out, bool accumulate,
              const c10::optional<at::Tensor>& scale);
-// gemm_bf16.cu
+// gemm.cu
 void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor D,
                const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
                const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,

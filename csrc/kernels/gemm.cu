@@ -1,6 +1,11 @@
-// Persistent, warp-specialised bf16 GEMM on the 5th-generation tensor cores.
+// Persistent, warp-specialised GEMMs on the 5th-generation tensor cores.
 //
 //   D[M,N] = epilogue( alpha * A[M,K] . B[N,K]^T )
+//
+// Variants: bf16 (kind::f16; a 1-SM kernel for M < 256 and the CTA-pair kernel),
+// per-tensor-scaled FP8 E4M3 / E5M2 (kind::f8f6f4, CTA pair), MXFP8 with 1x32
+// UE8M0 block scales (kind::mxf8f6f4.block_scale, CTA pair), and a B operand
+// sharded by rows across ranks and read from its owners (gemm_fp8_gather_b).
 //
 // Replaces the Burn NdArray matmuls of every Linear layer of the GPT example
 // (examples/gpt-1b/src/transformer.rs:34-37,54-56,84,99-100,106,109; model.rs:89,128)
