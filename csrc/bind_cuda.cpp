@@ -63,6 +63,7 @@ void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const
 void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt, double fmax);
 void copy_async(int64_t dst, int64_t src, int64_t bytes);
 void dp_quant_e5m2(int64_t grad, int64_t codes, int64_t sf, int64_t nelem);
+void dp_decode_mean_e5m2(const at::Tensor& codes, const at::Tensor& sf, at::Tensor out);
 void symm_rs_bucket_e5m2(const std::vector<int64_t>& codes, const std::vector<int64_t>& sfs,
                          const std::vector<int64_t>& flags, int64_t me, int64_t start, int64_t len, int64_t clen,
                          int64_t slot, int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t mine);
@@ -193,6 +194,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mx_quantize", &mx_quantize);
   m.def("copy_async", &copy_async);
   m.def("dp_quant_e5m2", &dp_quant_e5m2);
+  m.def("dp_decode_mean_e5m2", &dp_decode_mean_e5m2);
   m.def("symm_rs_bucket_e5m2", &symm_rs_bucket_e5m2);
   m.def("layernorm_fwd_mx_rc", &layernorm_fwd_mx_rc);
   m.def("mx_quantize_rc", &mx_quantize_rc);

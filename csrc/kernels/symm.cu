@@ -632,6 +632,38 @@ __global__ void __launch_bounds__(512) rs_bucket_e5m2_kernel(PeerPtrs codes, Pee
   }
 }
 
+// E5M2 transport on the NCCL reducer: after an all-to-all, row p of codes / sf holds
+// this rank's chunk of rank p's encoded bucket.  out[i] = bf16(inv_n * sum_p decode(p, i)),
+// summed in rank order in fp32 (the same order and rounding as the CPU path).
+__global__ void __launch_bounds__(256) dp_decode_mean_e5m2_kernel(const uint8_t* __restrict__ codes,
+                                                                  const uint8_t* __restrict__ sf, int n, int64_t c,
+                                                                  float inv_n, bf16* __restrict__ out) {
+  const int64_t nb = c / 32;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    for (int p = 0; p < n; ++p) {
+      const uint4* cp = reinterpret_cast<const uint4*>(codes + (int64_t)p * c + b * 32);
+      const uint4 c0v = cp[0], c1v = cp[1];
+      const uint32_t words[8] = {c0v.x, c0v.y, c0v.z, c0v.w, c1v.x, c1v.y, c1v.z, c1v.w};
+      const float scale = ue8m0_value(sf[(int64_t)p * nb + b]);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        float a, bb;
+        dec8x2((uint16_t)(words[k >> 1] >> ((k & 1) * 16)), 1, a, bb);
+        acc[2 * k] += a * scale;
+        acc[2 * k + 1] += bb * scale;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] *= inv_n;
+    bf16x8* dst = reinterpret_cast<bf16x8*>(out + b * 32);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q] = pack8(acc + 8 * q);
+  }
+}
+
 int64_t symm_status(bool reset) {
   int h = 0;
   C10_CUDA_CHECK(cudaMemcpy(&h, symm_status_ptr(), sizeof(int), cudaMemcpyDeviceToHost));
@@ -691,6 +723,24 @@ void symm_rs_bucket_e5m2(const std::vector<int64_t>& codes, const std::vector<in
       to_peers(codes), to_peers(sfs), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me,
       (int)flags.size(), start, len, clen, (int)slot, (uint32_t)epoch, (float)inv_n, reinterpret_cast<float*>(mine),
       st.data_ptr<float>(), symm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+// codes [n, c] and sf [n, c / 32] (uint8, contiguous, c a multiple of 32) -> out bf16 [c].
+void dp_decode_mean_e5m2(const at::Tensor& codes, const at::Tensor& sf, at::Tensor out) {
+  MT_CHECK(codes.dim() == 2 && codes.element_size() == 1 && codes.is_contiguous(), "dp_decode_mean_e5m2: codes [n, c]");
+  const int64_t n = codes.size(0), c = codes.size(1);
+  MT_CHECK(c % 32 == 0 && sf.numel() == n * (c / 32) && sf.is_contiguous() && sf.element_size() == 1,
+           "dp_decode_mean_e5m2: sf [n, c / 32]");
+  MT_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == c, "dp_decode_mean_e5m2: out");
+  MT_CHECK(reinterpret_cast<uintptr_t>(codes.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+           "dp_decode_mean_e5m2: 16-byte aligned buffers");
+  if (c == 0) return;
+  const int64_t nb = c / 32;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nb + 255) / 256, (int64_t)num_sms() * 8));
+  dp_decode_mean_e5m2_kernel<<<grid, 256, 0, cur_stream()>>>(
+      reinterpret_cast<const uint8_t*>(codes.data_ptr()), reinterpret_cast<const uint8_t*>(sf.data_ptr()), (int)n, c,
+      1.f / (float)n, reinterpret_cast<bf16*>(out.data_ptr()));
   MT_LAUNCH_CHECK();
 }
 

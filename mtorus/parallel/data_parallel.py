@@ -169,7 +169,13 @@ class NcclBucketReducer:
         rs = torch.empty(n, c // 32, dtype=torch.uint8, device=g.device)
         dist.all_to_all_single(rc, codes.view(n, c), group=self.group)  # row p: my chunk of rank p's bucket
         dist.all_to_all_single(rs, sf.view(n, c // 32), group=self.group)
-        mine = (e5m2_decode(rc, rs).sum(0) * (1.0 / n)).to(torch.bfloat16)
+        if g.is_cuda:
+            from .._ext import cuda as _cuda
+
+            mine = torch.empty(c, dtype=torch.bfloat16, device=g.device)
+            _cuda().dp_decode_mean_e5m2(rc, rs, mine)  # decode, fp32 sum in rank order, scale, bf16
+        else:
+            mine = (e5m2_decode(rc, rs).sum(0) * (1.0 / n)).to(torch.bfloat16)
         gathered = torch.empty(n, c, dtype=torch.bfloat16, device=g.device)
         if g.is_cuda:
             dist.all_gather_into_tensor(gathered, mine, group=self.group)

@@ -386,3 +386,4 @@ def test_e5m2_gradient_reduce_scatter_2gpu():
         # and within E5M2 precision of the exact fp32 mean
         exact = sum(r["input"] for r in res)[o["lo"]:o["hi"]] / len(res)
         assert float((o["chunk"] - exact).norm() / exact.norm()) < 0.1
+
