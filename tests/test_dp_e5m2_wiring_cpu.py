@@ -96,3 +96,30 @@ def test_fp32_transport_stays_the_default(fakes, monkeypatch):
     r.on_ready(flat.params)
     names = [n for n, _ in _Rec.calls]
     assert "symm_rs_bucket" in names and "dp_quant_e5m2" not in names
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_rank_chunks_tile_every_bucket_once(fakes, monkeypatch, world):
+    """The shard map the sharded Adam uses: over all ranks, the (flat offset, length)
+    chunks cover every bucket exactly once; each rank's compact offsets are 8-aligned,
+    ascending and non-overlapping, and its shard size is their padded total."""
+    flat = _Flat([3000, 5000, 700, 9000, 64, 12345])
+    cover = torch.zeros(flat.numel, dtype=torch.int32)
+    for me in range(world):
+        class Ctx(_Ctx):
+            def __init__(self, *a, **k):
+                super().__init__(*a, **k)
+                self.rank, self.world = me, world
+
+        monkeypatch.setattr(symm, "SymmContext", Ctx)
+        r = symm.SymmBucketReducer(flat, bucket_bytes=4 * 6000, ctas=8, reserve_sms=0, grad_fp8=False)
+        end = 0
+        for off, ln, moff in r.ranges.tolist():
+            cover[off:off + ln] += 1
+            assert moff % 8 == 0 and moff >= end
+            end = moff + (ln + 7) // 8 * 8
+        assert r.shard_numel == end
+    covered = torch.zeros(flat.numel, dtype=torch.bool)
+    for s, e in symm.BucketPlan(flat, 4 * 6000).ranges:
+        covered[s:e] = True
+    assert bool((cover[covered] == 1).all()) and bool((cover[~covered] == 0).all())
