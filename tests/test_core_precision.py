@@ -273,3 +273,32 @@ def test_overflow_behavior_sequence():
 def test_scaler_clone_equality():
     s = LossScaler.new_dynamic(1024.0, 100)
     assert s == s.clone()
+
+
+def test_fp8_state_slots_capacity_and_checkpoint_round_trip():
+    """Host bookkeeping of the device delayed-scaling state (mtorus.ops.fp8.Fp8State),
+    on CPU tensors: one slot per tensor role in first-use order with the role's format
+    maximum, a clear error past the capacity, and a state_dict that restores roles,
+    formats, histories, scales and the ring cursor into a fresh state."""
+    from mtorus.ops import fp8 as F8
+
+    st = F8.Fp8State("cpu", history=4, capacity=3)
+    assert st.recipe == "tensor"
+    assert st.slot("L0.qkv_in", F8.E4M3) == 0 and st.slot("L0.out_grad", F8.E5M2) == 1
+    assert st.slot("L0.qkv_in", F8.E4M3) == 0  # idempotent
+    assert float(st.fmax[0]) == 416.0 and float(st.fmax[1]) == 49152.0
+    st.slot("L0.ffn1_in", F8.E4M3)
+    with pytest.raises(RuntimeError, match="capacity"):
+        st.slot("L0.one_too_many", F8.E4M3)
+    st.hist[:3] = torch.arange(12, dtype=torch.float32).view(3, 4)
+    st.scale[:3] = torch.tensor([2.0, 4.0, 8.0])
+    st.inv[:3] = 1.0 / st.scale[:3]
+    st.cursor_dev.fill_(2)
+    st.first_step = False
+    sd = st.state_dict()
+    fresh = F8.Fp8State("cpu", history=4, capacity=8)
+    fresh.load_state_dict(sd)
+    assert fresh.names == st.names and fresh.fmts == st.fmts
+    assert torch.equal(fresh.hist[:3], st.hist[:3]) and torch.equal(fresh.scale[:3], st.scale[:3])
+    assert torch.equal(fresh.inv[:3], st.inv[:3]) and int(fresh.cursor_dev) == 2 and fresh.cursor == 2
+    assert not fresh.first_step
