@@ -4,6 +4,8 @@ is encoded from its own fp32 range (byte offset 4 * start) into the code buffer 
 element offset start and the scale buffer at block offset start / 32, then reduced
 with the same bucket bounds, chunk length, flag slot and epoch as the fp32 path; the
 buckets launch in order as their parameters become ready."""
+import contextlib
+
 import pytest
 import torch
 
@@ -61,7 +63,7 @@ def fakes(monkeypatch):
     monkeypatch.setattr(symm, "SymmContext", _Ctx)
     monkeypatch.setattr(torch.cuda, "Stream", lambda *a, **k: type("S", (), {"wait_event": lambda s, e: None})())
     monkeypatch.setattr(torch.cuda, "Event", lambda *a, **k: type("E", (), {"record": lambda s, *x: None})())
-    monkeypatch.setattr(torch.cuda, "stream", lambda s: __import__("contextlib").nullcontext())
+    monkeypatch.setattr(torch.cuda, "stream", lambda s: contextlib.nullcontext())
     monkeypatch.setattr(symm, "_cuda", lambda: _Rec())
     _Rec.calls = []
 

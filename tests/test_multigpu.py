@@ -1,6 +1,8 @@
 """Multi-GPU tests (NCCL process group, one process per GPU; skipped with < 2 GPUs):
 the fused NVLink collectives and the fused data-parallel training step against
 the NCCL baseline."""
+import os
+
 import pytest
 import torch
 
@@ -301,7 +303,7 @@ def _gather_gemm_body(rank, world):
 
 
 @needs2
-@pytest.mark.skipif(__import__("os").environ.get("MTORUS_GATHER_GEMM_TESTS") != "1",
+@pytest.mark.skipif(os.environ.get("MTORUS_GATHER_GEMM_TESTS") != "1",
                     reason="gather GEMM not yet run on B200s (MTORUS_GATHER_GEMM_TESTS=1 runs it)")
 def test_gather_b_gemm_matches_local_gemm_2gpu():
     """Weight all-gather fused into the GEMM: a GEMM that reads each B tile from the rank owning it equals
@@ -331,7 +333,7 @@ def _bc_scatter_body(rank, world):
 
 
 @needs2
-@pytest.mark.skipif(__import__("os").environ.get("MTORUS_BCAST_SCATTER_TESTS") != "1",
+@pytest.mark.skipif(os.environ.get("MTORUS_BCAST_SCATTER_TESTS") != "1",
                     reason="scatter + multicast broadcast not yet run on B200s (MTORUS_BCAST_SCATTER_TESTS=1 runs it)")
 def test_broadcast_scatter_multicast_2gpu():
     for o in run_dist(_bc_scatter_body, 2, backend="nccl"):
@@ -368,7 +370,7 @@ def _e5m2_rs_body(rank, world):
 
 
 @needs2
-@pytest.mark.skipif(__import__("os").environ.get("MTORUS_DP_GRAD_FP8_TESTS") != "1",
+@pytest.mark.skipif(os.environ.get("MTORUS_DP_GRAD_FP8_TESTS") != "1",
                     reason="E5M2 gradient transport not yet run on B200s (MTORUS_DP_GRAD_FP8_TESTS=1 runs it)")
 def test_e5m2_gradient_reduce_scatter_2gpu():
     """Each rank's chunk is the mean over ranks of the E5M2-encoded gradients (the
