@@ -60,6 +60,8 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--dp", default="nccl", choices=["nccl", "symm"])
     ap.add_argument("--bf16", action="store_true", help="bf16 block GEMMs instead of FP8")
+    ap.add_argument("--numa-bind", action="store_true",
+                    help="pin each rank's host threads to the CPUs of its GPU's NUMA node")
     ap.add_argument("--fp8-recipe", default="tensor", choices=["tensor", "mx"],
                     help="tensor: per-tensor delayed scaling; mx: MXFP8 1x32 block scales in all block GEMMs")
     ap.add_argument("--seed", type=int, default=0)
@@ -88,6 +90,10 @@ def main(argv=None) -> int:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.numa_bind:
+        from mtorus.core.topology import bind_to_gpu_numa
+
+        bind_to_gpu_numa(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 

@@ -40,14 +40,73 @@ def discover_manual(config: Optional[DiscoveryConfig] = None) -> List[GPUDevice]
     return _C.discover_manual(config or DiscoveryConfig())
 
 
-def _numa_of(bus_id: str) -> Optional[int]:
-    path = f"/sys/bus/pci/devices/{bus_id.lower()}/numa_node"
+def _numa_of(bus_id: str, sysfs: str = "/sys") -> Optional[int]:
+    path = f"{sysfs}/bus/pci/devices/{bus_id.lower()}/numa_node"
     try:
         with open(path) as f:
             v = int(f.read().strip())
         return v if v >= 0 else None
     except (OSError, ValueError):
         return None
+
+
+def parse_cpulist(text: str) -> List[int]:
+    """Linux cpulist syntax ("0-15,32-47,64") -> sorted CPU ids."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        if "-" in part:
+            lo, hi = part.split("-")
+            cpus.update(range(int(lo), int(hi) + 1))
+        else:
+            cpus.add(int(part))
+    return sorted(cpus)
+
+
+def numa_cpus(node: int, sysfs: str = "/sys") -> List[int]:
+    """CPUs of NUMA node ``node`` (empty when sysfs does not list them)."""
+    try:
+        with open(f"{sysfs}/devices/system/node/node{node}/cpulist") as f:
+            return parse_cpulist(f.read())
+    except (OSError, ValueError):
+        return []
+
+
+def _cuda_bus_id(index: int) -> Optional[str]:
+    import torch
+
+    if not torch.cuda.is_available() or index >= torch.cuda.device_count():
+        return None
+    props = torch.cuda.get_device_properties(index)
+    bus = getattr(props, "pci_bus_id", None)
+    if isinstance(bus, int):
+        bus = f"{getattr(props, 'pci_domain_id', 0):04x}:{bus:02x}:{getattr(props, 'pci_device_id', 0):02x}.0"
+    return bus
+
+
+def bind_to_gpu_numa(device_index: int = 0, bus_id: Optional[str] = None, sysfs: str = "/sys",
+                     apply: bool = True) -> Optional[List[int]]:
+    """Pin this process's host threads to the CPUs of the NUMA node the GPU hangs off
+    (host-to-device copies, the data loader and kernel launches then stay on the
+    socket next to the GPU).  Only the process's own CPU affinity changes; nothing on
+    the GPU is touched.  The CPU set is intersected with the CPUs the process may use
+    now.  Returns the CPUs bound to, or None when the node, its CPU list or the
+    intersection is unknown or empty (then nothing changes)."""
+    import os
+
+    bus = bus_id or _cuda_bus_id(device_index)
+    node = _numa_of(bus, sysfs) if bus else None
+    if node is None:
+        return None
+    cpus = set(numa_cpus(node, sysfs))
+    allowed = set(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else cpus
+    cpus &= allowed
+    if not cpus:
+        return None
+    if apply and hasattr(os, "sched_setaffinity"):
+        os.sched_setaffinity(0, cpus)
+    return sorted(cpus)
 
 
 def discover_cuda(config: Optional[DiscoveryConfig] = None) -> List[GPUDevice]:
@@ -97,5 +156,6 @@ def discover_mesh(config: Optional[DiscoveryConfig] = None) -> IntraNodeMesh:
 __all__ = [
     "GPUDevice", "IntraNodeMesh", "TorusCoordinates", "TorusDimensions", "MeshTorusHybrid",
     "DiscoveryConfig", "discover_devices", "discover_mesh", "discover_manual", "discover_cuda",
-    "topology_aware_placement", "compute_hop_distance", "torus_distance",
+    "topology_aware_placement", "compute_hop_distance", "torus_distance", "parse_cpulist", "numa_cpus",
+    "bind_to_gpu_numa",
 ]

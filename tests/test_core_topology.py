@@ -234,3 +234,26 @@ def test_dummy_communicator():
     for op in (CollectiveOp.AllReduce, CollectiveOp.Broadcast, CollectiveOp.AllGather, CollectiveOp.ReduceScatter):
         assert DummyCommunicator(0, 2).route_collective(op, b"\x2a") == b"\x2a"
     assert len(DummyCommunicator(0, 2).nearest_neighbor_exchange(b"\x01", 0)) == 2
+
+
+def test_numa_binding_from_sysfs(tmp_path):
+    """NUMA-aware host affinity: the GPU's PCI device -> its NUMA node -> that node's
+    CPUs, read from a stand-in sysfs tree (nothing is applied in the test)."""
+    import os
+
+    from mtorus.core.topology import bind_to_gpu_numa, numa_cpus, parse_cpulist
+
+    assert parse_cpulist("0-3,8,10-11\n") == [0, 1, 2, 3, 8, 10, 11]
+    allowed = sorted(os.sched_getaffinity(0))
+    node = tmp_path / "devices/system/node/node1"
+    node.mkdir(parents=True)
+    (node / "cpulist").write_text(f"{allowed[0]}-{allowed[-1]}\n")
+    dev = tmp_path / "bus/pci/devices/0000:1b:00.0"
+    dev.mkdir(parents=True)
+    (dev / "numa_node").write_text("1\n")
+    assert numa_cpus(1, str(tmp_path)) == list(range(allowed[0], allowed[-1] + 1))
+    got = bind_to_gpu_numa(bus_id="0000:1B:00.0", sysfs=str(tmp_path), apply=False)
+    assert got == allowed  # intersected with what the process may use
+    (dev / "numa_node").write_text("-1\n")  # no NUMA information: no binding
+    assert bind_to_gpu_numa(bus_id="0000:1b:00.0", sysfs=str(tmp_path), apply=False) is None
+    assert bind_to_gpu_numa(bus_id="0000:99:00.0", sysfs=str(tmp_path), apply=False) is None
