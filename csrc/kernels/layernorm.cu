@@ -848,21 +848,31 @@ float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
 
 // Once per device, with that device current: the device address of the array
 // (the host-side name g_ln_noalloc_scratch is only a stand-in, not a device
-// address) and the shared-memory opt-in of the kernels it launches.
+// address).
 float* noalloc_setup(int dev) {
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (g_noalloc_ptr[dev]) return g_noalloc_ptr[dev];
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_ln_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
-  const int smem = 4 * 2 * MTORUS_LN_NOALLOC_MAX_D * (int)sizeof(float);
-  if (cudaFuncSetAttribute(ln_bwd_vec<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-      cudaFuncSetAttribute(ln_bwd_vec<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-      cudaFuncSetAttribute(ln_bwd_vec<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-      cudaFuncSetAttribute(ln_bwd_vec<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
-      cudaFuncSetAttribute(ln_bwd_vec<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return nullptr;
   g_noalloc_ptr[dev] = static_cast<float*>(p);
   return g_noalloc_ptr[dev];
+}
+
+// The dynamic shared-memory limit is a per-function attribute that other code
+// (the torch-facing layernorm_bwd sets it to each call's own size) may have
+// lowered since the last call, so every call raises it for the kernel it is about
+// to launch.  Setting an attribute allocates nothing.
+template <int N>
+int noalloc_launch_vec(const bf16* dyp, const bf16* xp, const float* gamma, const float* mean,
+                       const float* rstd, bf16* dxp, float* part, int rows, int d, int grid,
+                       int wpb, size_t smem, cudaStream_t stream) {
+  if (cudaFuncSetAttribute(ln_bwd_vec<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess) {
+    (void)cudaGetLastError();  // the failed call's own (non-sticky) error
+    return MTORUS_NOALLOC_ESETUP;
+  }
+  ln_bwd_vec<N><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d);
+  return cudaGetLastError() == cudaSuccess ? MTORUS_NOALLOC_OK : MTORUS_NOALLOC_ELAUNCH;
 }
 
 }  // namespace
@@ -880,6 +890,9 @@ extern "C" int mtorus_layernorm_bwd_noalloc(const uint16_t* dy, const uint16_t* 
   for (const void* p : {(const void*)dy, (const void*)x, (const void*)gamma, (const void*)dx})
     if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return MTORUS_NOALLOC_EARG;
   if (d > MTORUS_LN_NOALLOC_MAX_D) return MTORUS_NOALLOC_ESIZE;
+  // An error left pending by earlier work belongs to the caller: report it without
+  // launching, and leave it in place for whoever owns it.
+  if (cudaPeekAtLastError() != cudaSuccess) return MTORUS_NOALLOC_EPENDING;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
     return MTORUS_NOALLOC_ESETUP;
@@ -892,15 +905,16 @@ extern "C" int mtorus_layernorm_bwd_noalloc(const uint16_t* dy, const uint16_t* 
   const auto* dyp = reinterpret_cast<const bf16*>(dy);
   const auto* xp = reinterpret_cast<const bf16*>(x);
   auto* dxp = reinterpret_cast<bf16*>(dx);
+  int rc;
   switch (nch) {
-    case 1: ln_bwd_vec<1><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
-    case 2: ln_bwd_vec<2><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
-    case 4: ln_bwd_vec<4><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
-    case 8: ln_bwd_vec<8><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
-    case 16: ln_bwd_vec<16><<<grid, wpb * 32, smem, stream>>>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d); break;
+    case 1: rc = noalloc_launch_vec<1>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d, grid, wpb, smem, stream); break;
+    case 2: rc = noalloc_launch_vec<2>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d, grid, wpb, smem, stream); break;
+    case 4: rc = noalloc_launch_vec<4>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d, grid, wpb, smem, stream); break;
+    case 8: rc = noalloc_launch_vec<8>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d, grid, wpb, smem, stream); break;
+    case 16: rc = noalloc_launch_vec<16>(dyp, xp, gamma, mean, rstd, dxp, part, rows, d, grid, wpb, smem, stream); break;
     default: return MTORUS_NOALLOC_ESIZE;
   }
-  if (cudaGetLastError() != cudaSuccess) return MTORUS_NOALLOC_ELAUNCH;
+  if (rc != MTORUS_NOALLOC_OK) return rc;
   ln_bwd_finish<<<(2 * d + 255) / 256, 256, 0, stream>>>(part, dgamma, dbeta, grid, d,
                                                          accumulate ? 1 : 0);
   if (cudaGetLastError() != cudaSuccess) return MTORUS_NOALLOC_ELAUNCH;

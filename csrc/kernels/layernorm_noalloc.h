@@ -18,8 +18,12 @@
 //   * The scratch array holds MTORUS_LN_NOALLOC_MAX_BLOCKS x 2 x 4096 floats
 //     (5 MiB).  Every GPU that loads the library keeps it until the process exits.
 //   * The first call on a device does the set-up for that device (it looks up
-//     the array's device address and sets the kernel's shared-memory limit).
-//     Make that first call before any stream capture.
+//     the array's device address).  Make that first call before any stream
+//     capture.  Every call also raises the shared-memory limit of the kernel it
+//     launches (a function attribute, which other code may lower in between).
+//   * An error already pending on the calling thread (from earlier, unrelated
+//     work) is left in place and reported as MTORUS_NOALLOC_EPENDING; nothing
+//     is launched.
 //   * All calls share the one array, and it keeps the last call's contents
 //     (every call overwrites what it reads).  Calls that overlap on the GPU --
 //     on two streams, or from two threads -- race on it; serialise them.
@@ -38,6 +42,7 @@
 #define MTORUS_NOALLOC_ESIZE -2   // d above MTORUS_LN_NOALLOC_MAX_D
 #define MTORUS_NOALLOC_ESETUP -3  // device set-up failed (symbol lookup / attribute)
 #define MTORUS_NOALLOC_ELAUNCH -4 // kernel launch failed
+#define MTORUS_NOALLOC_EPENDING -5 // a CUDA error from earlier work was already pending
 
 #ifdef __cplusplus
 extern "C" {

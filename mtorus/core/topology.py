@@ -89,9 +89,12 @@ def bind_to_gpu_numa(device_index: int = 0, bus_id: Optional[str] = None, sysfs:
                      apply: bool = True) -> Optional[List[int]]:
     """Pin this process's host threads to the CPUs of the NUMA node the GPU hangs off
     (host-to-device copies, the data loader and kernel launches then stay on the
-    socket next to the GPU).  Only the process's own CPU affinity changes; nothing on
-    the GPU is touched.  The CPU set is intersected with the CPUs the process may use
-    now.  Returns the CPUs bound to, or None when the node, its CPU list or the
+    socket next to the GPU).  On Linux an affinity belongs to a thread, so the set is
+    applied to every thread the process has now (``/proc/self/task``: CUDA driver and
+    torch pool threads started before this call included); threads created later
+    inherit it from their creator.  Only CPU affinity changes; nothing on the GPU is
+    touched.  The CPU set is intersected with the CPUs the process may use now.
+    Returns the CPUs bound to, or None when the node, its CPU list or the
     intersection is unknown or empty (then nothing changes)."""
     import os
 
@@ -105,6 +108,16 @@ def bind_to_gpu_numa(device_index: int = 0, bus_id: Optional[str] = None, sysfs:
     if not cpus:
         return None
     if apply and hasattr(os, "sched_setaffinity"):
+        tids = []
+        try:
+            tids = [int(t) for t in os.listdir("/proc/self/task")]
+        except OSError:
+            pass
+        for tid in tids:
+            try:
+                os.sched_setaffinity(tid, cpus)
+            except OSError:  # the thread exited meanwhile
+                pass
         os.sched_setaffinity(0, cpus)
     return sorted(cpus)
 

@@ -330,6 +330,21 @@ class GptModel(nn.Module):
             x = self.fused_embed(x)
         return self.fused_blocks(x, B, S)
 
+    def fused_stage_segments(self, B: int, S: int) -> list:
+        """``fused_stage`` as one callable per transformer block (the embedding folded
+        into the first): the segments that selective activation checkpointing splits
+        at the midpoint."""
+        st = getattr(self, "fp8_state", None)
+
+        def block_fn(i, blk, embed):
+            def run(x):
+                if embed:
+                    x = self.fused_embed(x)
+                return blk.fused_forward(x, B, S, None if st is None else (st, f"L{self.layer_offset + i}"))
+            return run
+
+        return [block_fn(i, blk, self.has_embed and i == 0) for i, blk in enumerate(self.blocks)]
+
     def fused_head_loss(self, x: torch.Tensor, targets: torch.Tensor,
                         grad_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Last-stage loss: ln_f -> lm_head -> mean CE, gradients into main_grad."""

@@ -10,8 +10,14 @@ receive activations, forward, send, receive gradients, backward, send -- with
 point-to-point transfers through ``torch.distributed`` (NCCL on GPUs, gloo on
 CPU).  Sends are posted asynchronously so transfers overlap the next compute
 op; receives for the next op are posted before the current compute runs.
-Activation checkpointing (``CheckpointStrategy.Full``) keeps only the stage
-input of each in-flight micro-batch and recomputes the forward in backward.
+Activation checkpointing: ``Full`` keeps only the stage input of each
+in-flight micro-batch and recomputes the whole stage forward in backward;
+``Selective`` splits the stage's segments at the midpoint (the reference's
+split, crates/mt-pipeline/src/checkpoint.rs:43-60), keeps the activations of
+the first half and the midpoint output, and recomputes only the second half in
+backward (half of Full's recompute, about half of None's activation memory).
+A stage of one segment has no midpoint, so Selective runs it as Full, like the
+reference.
 """
 from __future__ import annotations
 
@@ -23,7 +29,7 @@ from typing import Callable, Dict, List, Optional, Sequence
 import torch
 import torch.distributed as dist
 
-from .checkpoint import CheckpointStrategy
+from .checkpoint import CheckpointStrategy, checkpoint_module
 from .communicator import PipelineComm
 from .schedule import GpipeSchedule, OneF1BSchedule, PipeOp, ScheduleKind, ScheduleType, rank_program
 from .stage import PipelineStage
@@ -62,6 +68,10 @@ class DistributedPipelineExecutor:
                 divides it by the number of micro-batches
     act_shape   shape of the tensor exchanged between stages (per micro-batch)
     stage_fn    optional forward callable used instead of ``module(x)``
+    stage_segments  optional list of callables whose composition is the stage
+                forward (e.g. one per layer); ``Selective`` checkpointing splits
+                it at the midpoint.  Default: the children of an
+                ``nn.Sequential`` module, else the single stage forward
     pre_backward  called as pre_backward(microbatch, k) before the k-th backward of
                 the step (k = 0 .. M-1), e.g. to switch gradient accumulation on
                 after the first micro-batch or to arm the data-parallel reducer on
@@ -88,7 +98,8 @@ class DistributedPipelineExecutor:
                  loss_fn: Optional[Callable] = None, act_shape: Sequence[int] = (), act_dtype=torch.float32,
                  device=None, group=None, on_backward_done: Optional[Callable[[int], None]] = None,
                  stage_fn: Optional[Callable] = None, pre_backward: Optional[Callable[[int, int], None]] = None,
-                 grad_group=None, sync_losses: bool = True, timed: bool = False):
+                 grad_group=None, sync_losses: bool = True, timed: bool = False,
+                 stage_segments: Optional[Sequence[Callable]] = None):
         self.module = module
         self.stage_ranks = list(stage_ranks)
         self.S = len(self.stage_ranks)
@@ -105,6 +116,15 @@ class DistributedPipelineExecutor:
         self.grad_group = grad_group if grad_group is not None else group
         self.on_backward_done = on_backward_done
         self.stage_fn = stage_fn
+        if stage_segments is None and stage_fn is None and isinstance(module, torch.nn.Sequential):
+            stage_segments = list(module.children())
+        self.segments = list(stage_segments) if stage_segments else []
+        if checkpoint not in (CheckpointStrategy.None_, CheckpointStrategy.Full, CheckpointStrategy.Selective):
+            raise ValueError(f"unknown checkpoint strategy {checkpoint!r}")
+        # Selective with fewer than two segments has no midpoint: the reference caches
+        # the input and runs the stage, which is Full
+        if checkpoint is CheckpointStrategy.Selective and len(self.segments) < 2:
+            self.checkpoint = CheckpointStrategy.Full
         self.pre_backward = pre_backward
         self.sync_losses = sync_losses
         self.timed = timed and self.device.type == "cuda"
@@ -148,6 +168,22 @@ class DistributedPipelineExecutor:
 
     def _stage_forward(self, x):
         return self.stage_fn(x) if self.stage_fn is not None else self.module(x)
+
+    def _selective_forward(self, x):
+        """First half of the segments with their activations kept; the second half
+        under ``checkpoint_module`` (only the midpoint output is kept, the second
+        half's forward runs again inside backward)."""
+        split = len(self.segments) // 2
+        for seg in self.segments[:split]:
+            x = seg(x)
+        tail = self.segments[split:]
+
+        def second_half(h):
+            for seg in tail:
+                h = seg(h)
+            return h
+
+        return checkpoint_module(second_half, x)
 
     def run(self, inputs: Optional[Sequence[torch.Tensor]] = None,
             targets: Optional[Sequence[torch.Tensor]] = None):
@@ -208,6 +244,8 @@ class DistributedPipelineExecutor:
                 if self.checkpoint is CheckpointStrategy.Full:
                     with torch.no_grad():
                         y = self._stage_forward(x)
+                elif self.checkpoint is CheckpointStrategy.Selective:
+                    y = self._selective_forward(x)
                 else:
                     y = self._stage_forward(x)
                 if self.is_last:

@@ -13,8 +13,10 @@ bf16 / fp32-grad buffers and runs:
    gpipe.rs, onef1b.rs) with NCCL point-to-point activations / gradients,
    activations on one process group and gradients on another so that the two
    directions between neighbours never share an NCCL stream;
-2. optional full activation checkpointing per stage (stage input kept, forward
-   recomputed in backward; reference crates/mt-pipeline/src/checkpoint.rs);
+2. optional activation checkpointing per stage: Full (stage input kept, forward
+   recomputed in backward) or Selective (the second half of the stage's blocks
+   recomputed from the midpoint output); reference
+   crates/mt-pipeline/src/checkpoint.rs;
 3. gradient accumulation over the micro-batches straight into ``main_grad``
    (the first backward overwrites, the rest add, in the wgrad GEMM epilogues);
 4. during the last micro-batch's backward, the data-parallel bucket all-reduce
@@ -183,7 +185,8 @@ class PipelineTrainer:
             self.model, self.layout.stage_ranks[self.replica], schedule, num_microbatches, checkpoint,
             loss_fn=loss_fn, act_shape=(b * S, config.d_model), act_dtype=torch.bfloat16, device=self.device,
             group=self.pipe_group, grad_group=self.grad_group, stage_fn=stage_fn,
-            pre_backward=self._pre_backward, sync_losses=False, timed=timed)
+            pre_backward=self._pre_backward, sync_losses=False, timed=timed,
+            stage_segments=self.model.fused_stage_segments(b, S))
         self.schedule = schedule
         self.global_step = 0
         self._loss_host = torch.empty((), dtype=torch.float32).pin_memory()

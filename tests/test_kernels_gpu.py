@@ -363,8 +363,6 @@ def test_gemm_fp8_gelu_fp8_epilogue(M, N, Kd):
     assert float(amax) == float(act_r.float().abs().max())
 
 
-@pytest.mark.skipif(os.environ.get("MTORUS_DP_GRAD_FP8_TESTS") != "1",
-                    reason="E5M2 gradient transport not yet run on B200s (MTORUS_DP_GRAD_FP8_TESTS=1 runs it)")
 def test_e5m2_encode_and_decode_mean_kernels_match_cpu_path():
     """One GPU: the E5M2 block encoder matches the PyTorch oracle byte for byte, and the
     fused decode-average (NCCL reducer path) matches the CPU path exactly."""

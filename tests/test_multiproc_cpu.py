@@ -61,7 +61,7 @@ def _pp_body(rank, world, sched_name, ckpt_name):
 
 
 @pytest.mark.parametrize("sched", ["OneF1B", "Gpipe"])
-@pytest.mark.parametrize("ckpt", ["None_", "Full"])
+@pytest.mark.parametrize("ckpt", ["None_", "Full", "Selective"])
 def test_pipeline_executor_matches_single_process(sched, ckpt):
     res = run_dist(_pp_body, 3, (sched, ckpt))
     stages = _make_stages()
@@ -79,6 +79,46 @@ def test_pipeline_executor_matches_single_process(sched, ckpt):
     for r in range(3):
         for gp, p in zip(res[r][1], stages[r].parameters()):
             assert torch.allclose(gp, p.grad, atol=1e-5), (r, (gp - p.grad).abs().max())
+
+
+class _Counting(torch.nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.lin = torch.nn.Linear(d, d)
+        self.calls = 0
+
+    def forward(self, x):
+        self.calls += 1
+        return torch.tanh(self.lin(x))
+
+
+def _selective_body(rank, world, ckpt_name):
+    from mtorus.pipeline import CheckpointStrategy, DistributedPipelineExecutor, ScheduleType
+
+    torch.manual_seed(3)
+    stage = torch.nn.Sequential(*[_Counting(8) for _ in range(4)])
+    M = 3
+    g = torch.Generator().manual_seed(4)
+    xs = [torch.randn(2, 8, generator=g) for _ in range(M)]
+    ys = [torch.randn(2, 8, generator=g) for _ in range(M)]
+    ex = DistributedPipelineExecutor(stage, [0], ScheduleType.OneF1B, M, getattr(CheckpointStrategy, ckpt_name),
+                                     loss_fn=torch.nn.functional.mse_loss, act_shape=(2, 8))
+    ex.run(xs, ys)
+    return [m.calls for m in stage], [p.grad.clone() for p in stage.parameters()]
+
+
+def test_selective_checkpointing_recomputes_only_the_second_half():
+    """Selective (reference checkpoint.rs:43-60 splits the stage's layers at len / 2):
+    the first half runs once per micro-batch, the second half once more in backward,
+    and the gradients are those of the plain stage."""
+    calls_sel, grads_sel = run_dist(_selective_body, 1, ("Selective",))[0]
+    calls_none, grads_none = run_dist(_selective_body, 1, ("None_",))[0]
+    calls_full, _ = run_dist(_selective_body, 1, ("Full",))[0]
+    assert calls_none == [3, 3, 3, 3]
+    assert calls_sel == [3, 3, 6, 6]
+    assert calls_full == [6, 6, 6, 6]
+    for a, b in zip(grads_sel, grads_none):
+        assert torch.allclose(a, b, atol=1e-6)
 
 
 def _dp_body(rank, world):
