@@ -124,6 +124,11 @@ void symm_broadcast(const std::vector<int64_t>& bufs, int64_t root, int64_t byte
 void symm_allreduce_mc(int64_t mc, const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags,
                        int64_t me, int64_t numel, int64_t dtype, int64_t slot, int64_t epoch, int64_t ctas);
 void symm_broadcast_mc(int64_t src, int64_t mc, int64_t bytes, int64_t ctas);
+void symm_pull_msgs(const std::vector<int64_t>& src, int64_t src_off, int64_t dst, int64_t slot_bytes,
+                    const std::vector<int64_t>& peers, const std::vector<int64_t>& slots, int64_t ctas_per_msg);
+void symm_allreduce_msgs(const std::vector<int64_t>& src, int64_t src_off, int64_t dst, int64_t dtype, int64_t op,
+                         int64_t cap, int64_t ctas);
+void symm_flag(int64_t signal_addr, int64_t signal_value, int64_t wait_addr, int64_t wait_value, int64_t code);
 void symm_halo(int64_t src, const std::vector<int64_t>& recv, const at::Tensor& nbr_rank,
                const at::Tensor& nbr_slot, int64_t bytes, int64_t ctas);
 void install_segv_handler();
@@ -179,6 +184,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_allgather", &symm_allgather);
   m.def("symm_broadcast", &symm_broadcast);
   m.def("symm_halo", &symm_halo);
+  m.def("symm_pull_msgs", &symm_pull_msgs);
+  m.def("symm_allreduce_msgs", &symm_allreduce_msgs);
+  m.def("symm_flag", &symm_flag);
   m.def("symm_allreduce_mc", &symm_allreduce_mc);
   m.def("symm_broadcast_mc", &symm_broadcast_mc);
   m.def("install_segv_handler", &install_segv_handler);

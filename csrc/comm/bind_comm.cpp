@@ -51,6 +51,17 @@ class PyCommunicator : public Communicator {
   size_t world_size() const override { PYBIND11_OVERRIDE_PURE(size_t, Communicator, world_size, ); }
   std::string backend() const override { PYBIND11_OVERRIDE(std::string, Communicator, backend, ); }
   void barrier() override { PYBIND11_OVERRIDE(void, Communicator, barrier, ); }
+  bool exchange(const Bytes& data, const std::vector<size_t>& peers, std::vector<Bytes>* out) override {
+    py::gil_scoped_acquire g;
+    py::function f = py::get_override(static_cast<const Communicator*>(this), "exchange");
+    if (!f) return false;
+    py::object r = f(py::bytes(data), peers);
+    if (r.is_none()) return false;
+    out->clear();
+    for (auto item : r) out->push_back(item.cast<std::string>());
+    if (out->size() != peers.size()) throw CommError("exchange returned the wrong number of messages");
+    return true;
+  }
 };
 
 py::bytes B(const Bytes& b) { return py::bytes(b); }

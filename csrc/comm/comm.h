@@ -71,6 +71,16 @@ class Communicator {
   virtual size_t world_size() const = 0;
   virtual std::string backend() const { return "abstract"; }
   virtual void barrier();
+  // Neighbour exchange in one operation: send `data` to every rank in `peers` and
+  // receive one message from each (out[i] from peers[i]).  Backends that move the
+  // whole exchange at once (the device communicator's peer-memory kernels) return
+  // true; the default returns false and callers fall back to send / recv.
+  virtual bool exchange(const Bytes& data, const std::vector<size_t>& peers, std::vector<Bytes>* out) {
+    (void)data;
+    (void)peers;
+    (void)out;
+    return false;
+  }
 };
 
 // ---------------------------------------------------------------- Mock

@@ -857,4 +857,155 @@ void symm_halo(int64_t src, const std::vector<int64_t>& recv, const at::Tensor& 
   MT_LAUNCH_CHECK();
 }
 
+
+// ------------------------------------------------------------------ byte-message communicator
+// Kernels behind the device Communicator (mtorus.comm.device.SymmCommunicator):
+// messages of any length live in symmetric byte buffers as [int64 length | 8 pad |
+// payload], and every collective is a pull of whole messages over NVLink.
+//
+//   pull_msgs        copies the messages of a list of peers (their staging buffers)
+//                    into local slots: all_gather (every peer), broadcast (the
+//                    root), the neighbour exchange (the torus neighbours) and a
+//                    point-to-point receive (one sender);
+//   allreduce_msgs   reads every peer's staged message and reduces it element by
+//                    element in rank order (Sum / Product / Min / Max / Mean over
+//                    u64, i64, f32, f64, i32, u8), which is the order the host
+//                    reduce_buffers uses, so float results agree bit for bit;
+//   flag_kernel      release-stores one flag into a peer and / or waits (bounded)
+//                    for one of its own flags: the handshake of point-to-point
+//                    messages.
+constexpr int kMaxMsgs = 16;
+constexpr int64_t kMsgHeader = 16;
+
+struct MsgList {
+  int peer[kMaxMsgs];
+  int slot[kMaxMsgs];
+  int n;
+};
+
+__global__ void __launch_bounds__(256) pull_msgs_kernel(PeerPtrs src, int64_t src_off, uint8_t* dst,
+                                                        int64_t slot_bytes, MsgList msgs, int* status) {
+  const int per_msg = gridDim.x / msgs.n;
+  const int k = blockIdx.x / per_msg, part = blockIdx.x % per_msg;
+  if (k >= msgs.n) return;
+  const uint8_t* s = reinterpret_cast<const uint8_t*>(src.p[msgs.peer[k]]) + src_off;
+  uint8_t* d = dst + (int64_t)msgs.slot[k] * slot_bytes;
+  int64_t len = *reinterpret_cast<const volatile int64_t*>(s);
+  if (len < 0 || len > slot_bytes - kMsgHeader) {
+    if (threadIdx.x == 0 && part == 0) atomicExch(status, 51);
+    len = 0;
+  }
+  const int64_t nvec = (kMsgHeader + len + 15) / 16;
+  const uint4* sv = reinterpret_cast<const uint4*>(s);
+  uint4* dv = reinterpret_cast<uint4*>(d);
+  for (int64_t i = (int64_t)part * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)per_msg * blockDim.x)
+    dv[i] = sv[i];
+}
+
+template <typename T>
+__device__ __forceinline__ T reduce_one(int op, T a, T b) {
+  switch (op) {
+    case 1: return a * b;
+    case 2: return b < a ? b : a;
+    case 3: return a < b ? b : a;
+    default: return a + b;  // Sum, Mean
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) allreduce_msgs_kernel(PeerPtrs src, int64_t src_off, uint8_t* dst, int n,
+                                                             int op, int64_t cap, int* status) {
+  // element count from rank 0's message (reference semantics); shorter messages read as zeros
+  const int64_t len0 = *reinterpret_cast<const volatile int64_t*>(reinterpret_cast<const uint8_t*>(src.p[0]) + src_off);
+  if (len0 < 0 || len0 > cap) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(status, 52);
+    return;
+  }
+  const int64_t count = len0 / (int64_t)sizeof(T);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<int64_t*>(dst) = count * (int64_t)sizeof(T);
+  __shared__ int64_t lens[kMaxPeers];
+  if (threadIdx.x < n)
+    lens[threadIdx.x] =
+        *reinterpret_cast<const volatile int64_t*>(reinterpret_cast<const uint8_t*>(src.p[threadIdx.x]) + src_off);
+  __syncthreads();
+  T* out = reinterpret_cast<T*>(dst + kMsgHeader);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    const T* s0 = reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(src.p[0]) + src_off + kMsgHeader);
+    T acc = s0[i];
+    for (int p = 1; p < n; ++p) {
+      const T* sp = reinterpret_cast<const T*>(reinterpret_cast<const uint8_t*>(src.p[p]) + src_off + kMsgHeader);
+      const T x = (i + 1) * (int64_t)sizeof(T) <= lens[p] ? sp[i] : T(0);
+      acc = reduce_one<T>(op, acc, x);
+    }
+    if (op == 4) acc = static_cast<T>(acc / static_cast<T>(n));
+    out[i] = acc;
+  }
+}
+
+__global__ void flag_kernel(uint32_t* signal_addr, uint32_t signal_value, const uint32_t* wait_addr,
+                            uint32_t wait_value, int* status, int code) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  if (signal_addr) {
+    __threadfence_system();
+    st_release_sys(signal_addr, signal_value);
+  }
+  if (wait_addr) {
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t)(ld_acquire_sys(wait_addr) - wait_value) < 0) {
+      if (globaltimer_ns() - t0 > kSymmSpinLimitNs) {
+        atomicExch(status, code);
+        return;
+      }
+      __nanosleep(128);
+    }
+  }
+}
+
+void symm_pull_msgs(const std::vector<int64_t>& src, int64_t src_off, int64_t dst, int64_t slot_bytes,
+                    const std::vector<int64_t>& peers, const std::vector<int64_t>& slots, int64_t ctas_per_msg) {
+  MT_CHECK(!peers.empty() && peers.size() == slots.size() && peers.size() <= (size_t)kMaxMsgs,
+           "pull_msgs: 1..16 (peer, slot) pairs");
+  MT_CHECK(slot_bytes % 16 == 0 && src_off % 16 == 0 && dst % 16 == 0, "pull_msgs: 16-byte alignment");
+  MsgList m{};
+  m.n = (int)peers.size();
+  for (int i = 0; i < m.n; ++i) {
+    MT_CHECK(peers[i] >= 0 && peers[i] < (int64_t)src.size(), "pull_msgs: peer out of range");
+    m.peer[i] = (int)peers[i];
+    m.slot[i] = (int)slots[i];
+  }
+  const int per = (int)std::max<int64_t>(1, ctas_per_msg);
+  pull_msgs_kernel<<<per * m.n, 256, 0, cur_stream()>>>(to_peers(src), src_off, reinterpret_cast<uint8_t*>(dst),
+                                                       slot_bytes, m, symm_status_ptr());
+  MT_LAUNCH_CHECK();
+}
+
+// dtype: 0 U64, 1 I64, 2 F32, 3 F64, 4 I32, 5 U8 (the host DType order); op: 0 Sum, 1 Product,
+// 2 Min, 3 Max, 4 Mean (the host ReduceOp order).
+void symm_allreduce_msgs(const std::vector<int64_t>& src, int64_t src_off, int64_t dst, int64_t dtype, int64_t op,
+                         int64_t cap, int64_t ctas) {
+  MT_CHECK(op >= 0 && op <= 4, "allreduce_msgs: op 0..4");
+  MT_CHECK(src_off % 16 == 0 && dst % 16 == 0, "allreduce_msgs: 16-byte alignment");
+  const int n = (int)src.size();
+  auto* d = reinterpret_cast<uint8_t*>(dst);
+  const PeerPtrs pp = to_peers(src);
+  const int g = (int)std::max<int64_t>(1, ctas);
+  switch (dtype) {
+    case 0: allreduce_msgs_kernel<uint64_t><<<g, 256, 0, cur_stream()>>>(pp, src_off, d, n, (int)op, cap, symm_status_ptr()); break;
+    case 1: allreduce_msgs_kernel<int64_t><<<g, 256, 0, cur_stream()>>>(pp, src_off, d, n, (int)op, cap, symm_status_ptr()); break;
+    case 2: allreduce_msgs_kernel<float><<<g, 256, 0, cur_stream()>>>(pp, src_off, d, n, (int)op, cap, symm_status_ptr()); break;
+    case 3: allreduce_msgs_kernel<double><<<g, 256, 0, cur_stream()>>>(pp, src_off, d, n, (int)op, cap, symm_status_ptr()); break;
+    case 4: allreduce_msgs_kernel<int32_t><<<g, 256, 0, cur_stream()>>>(pp, src_off, d, n, (int)op, cap, symm_status_ptr()); break;
+    case 5: allreduce_msgs_kernel<uint8_t><<<g, 256, 0, cur_stream()>>>(pp, src_off, d, n, (int)op, cap, symm_status_ptr()); break;
+    default: MT_CHECK(false, "allreduce_msgs: unknown dtype");
+  }
+  MT_LAUNCH_CHECK();
+}
+
+void symm_flag(int64_t signal_addr, int64_t signal_value, int64_t wait_addr, int64_t wait_value, int64_t code) {
+  flag_kernel<<<1, 32, 0, cur_stream()>>>(reinterpret_cast<uint32_t*>(signal_addr), (uint32_t)signal_value,
+                                          reinterpret_cast<const uint32_t*>(wait_addr), (uint32_t)wait_value,
+                                          symm_status_ptr(), (int)code);
+  MT_LAUNCH_CHECK();
+}
+
 }  // namespace mtorus

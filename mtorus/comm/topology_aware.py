@@ -7,8 +7,13 @@ the inner communicator (ReduceScatter = all-reduce + slice), ``reduce_on_mesh``
 ignores its group like the reference (``reduce_on_group`` honours it), and the
 ``TopologyAwareCommunicator`` methods fall back to the caller's data on errors.
 
-The device counterpart of the neighbour exchange (direct NVLink peer stores
-between GPUs) is ``mtorus.parallel.symm.HaloExchange``.
+Over the device backend (``mtorus.comm.device.SymmCommunicator``) the inner
+communicator implements ``exchange``, and ``exchange_with_neighbors`` /
+``nearest_neighbor_exchange`` move the whole exchange in one peer-memory kernel
+(every neighbour's message pulled over NVLink at once) instead of a send and a
+receive per neighbour.  For device tensors, ``SymmCommunicator.
+exchange_neighbors_tensor`` stores straight into each neighbour's receive slot
+(``halo_kernel``).
 """
 from .._ext import host as _host
 

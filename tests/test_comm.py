@@ -388,3 +388,24 @@ def test_fault_plan_drop_then_timeout():
     assert w[1].recv(0) == b"second"
     with pytest.raises(CommTimeout):
         w[1].recv(0)
+
+
+def test_comm_scenario_on_local_world_threads():
+    """The shared communicator workload (also run on the device backend on 2 GPUs)
+    runs on host ranks and gives the reference's results."""
+    import struct
+
+    from comm_scenario import host_results
+    from mtorus.core.topology import MeshTorusHybrid
+
+    res = host_results(2, MeshTorusHybrid.new_2d(2, 1, 1))
+    for r, o in enumerate(res):
+        assert o["ar_u64_sum"] == struct.pack("<3Q", 3, 12, (2 ** 64 + 1) % 2 ** 64)
+        assert o["ar_i32_mean"] == struct.pack("<3i", 4, -5, 100)
+        assert o["ar_u8_sum"] == bytes([144, 1, 254, 6])
+        assert o["bc"] == b"root says hi 1"
+        assert o["ag"] == [b"x\x00", b"xx\x01"]
+        assert o["p2p"] == [b"msg %d from %d" % (k, 1 - r) for k in range(3)]
+        # the 2 x 1 torus: both x neighbours are the other rank, both y neighbours this rank itself
+        assert o["exchange"] == [(1 - r, b"halo of %d" % (1 - r))] * 2 + [(r, b"halo of %d" % r)] * 2
+        assert o["pc_rs"] == struct.pack("<2Q", 1 + 4 * r, 3 + 4 * r)

@@ -389,3 +389,48 @@ def test_e5m2_gradient_reduce_scatter_2gpu():
         exact = sum(r["input"] for r in res)[o["lo"]:o["hi"]] / len(res)
         assert float((o["chunk"] - exact).norm() / exact.norm()) < 0.1
 
+
+
+def _device_comm_body(rank, world):
+    import torch
+
+    from comm_scenario import scenario
+    from mtorus.comm.device import SymmCommunicator
+    from mtorus.core.topology import MeshTorusHybrid
+
+    torch.cuda.set_device(rank)
+    comm = SymmCommunicator(device=f"cuda:{rank}", max_bytes=1 << 16, tensor_bytes=1 << 20)
+    out = scenario(comm, MeshTorusHybrid.new_2d(world, 1, 1))
+    # the tensor interface on device data
+    t = torch.arange(1000, device="cuda", dtype=torch.float32) * (rank + 1)
+    out["t_ar"] = comm.all_reduce_tensor(t).cpu()
+    g = torch.empty(world * 6, device="cuda", dtype=torch.bfloat16)
+    out["t_ag"] = comm.all_gather_tensor(g, torch.full((6,), rank + 1.0, device="cuda").bfloat16()).float().cpu()
+    b = torch.full((5,), float(rank), device="cuda")
+    out["t_bc"] = comm.broadcast_tensor(b, 1).cpu()
+    got = comm.exchange_neighbors_tensor(torch.full((3, 4), rank + 10.0, device="cuda"),
+                                         MeshTorusHybrid.new_2d(world, 1, 1))
+    out["t_x"] = [x.cpu() for x in got]
+    out["status"] = int(comm.ctx.status())
+    return out
+
+
+@needs2
+def test_device_communicator_matches_host_world_2gpu():
+    """The device backend (NVLink peer-memory kernels) runs the reference's collective,
+    point-to-point and neighbour-exchange cases with the host LocalWorld's results."""
+    from comm_scenario import host_results
+    from mtorus.core.topology import MeshTorusHybrid
+
+    ref = host_results(2, MeshTorusHybrid.new_2d(2, 1, 1))
+    got = run_dist(_device_comm_body, 2, backend="nccl")
+    for r in range(2):
+        for k, v in ref[r].items():
+            assert got[r][k] == v, (r, k, got[r][k], v)
+        assert got[r]["status"] == 0
+        assert torch.equal(got[r]["t_ar"], torch.arange(1000, dtype=torch.float32) * 3)
+        assert torch.equal(got[r]["t_ag"], torch.cat([torch.full((6,), 1.0), torch.full((6,), 2.0)]))
+        assert torch.equal(got[r]["t_bc"], torch.full((5,), 1.0))
+        # neighbours in +x, -x, +y, -y order: the other rank twice, then this rank twice
+        want = [1 - r, 1 - r, r, r]
+        assert [float(x[0, 0]) for x in got[r]["t_x"]] == [w + 10.0 for w in want]
