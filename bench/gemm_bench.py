@@ -57,20 +57,44 @@ def main():
 
     fp8_cases = [("qkv_fwd_fp8", T, 3 * d, d, "tn"), ("ffn1_fwd_fp8", T, F, d, "tn"), ("ffn2_fwd_fp8", T, d, F, "tn"),
                  ("ffn2_dgrad_fp8", T, F, d, "dgrad"), ("ffn1_wgrad_fp8", F, d, T, "wgrad"),
-                 ("square8k_fp8", 8192, 8192, 8192, "tn")]
+                 ("square8k_fp8", 8192, 8192, 8192, "tn"),
+                 # the same shapes with the epilogues the training step uses
+                 ("ffn1_fwd_fp8_gelu8", T, F, d, "tn_gelu8"), ("ffn2_fwd_fp8_bias_res", T, d, F, "tn_res"),
+                 ("ffn2_dgrad_fp8_dgelu", T, F, d, "dgrad_aux"), ("ffn1_wgrad_fp8_acc", F, d, T, "wgrad_acc")]
     one = torch.ones(1, device="cuda")
     if args.case:
         fp8_cases = [c for c in fp8_cases if c[0] == args.case]
         cases = [c for c in cases if c[0] == args.case]
     for name, M, N, Kd, lay in fp8_cases:
-        A = (torch.randn(M, Kd, device="cuda") if lay != "wgrad" else torch.randn(Kd, M, device="cuda")).to(
-            torch.float8_e4m3fn).view(torch.uint8)
-        B = (torch.randn(N, Kd, device="cuda") if lay == "tn" else torch.randn(Kd, N, device="cuda")).to(
-            torch.float8_e4m3fn).view(torch.uint8)
+        A = (torch.randn(M, Kd, device="cuda") if not lay.startswith("wgrad") else
+             torch.randn(Kd, M, device="cuda")).to(torch.float8_e4m3fn).view(torch.uint8)
+        B = (torch.randn(N, Kd, device="cuda") if lay.startswith("tn") else
+             torch.randn(Kd, N, device="cuda")).to(torch.float8_e4m3fn).view(torch.uint8)
         if lay == "tn":
             mine = lambda: F8.gemm_fp8(A, 0, B, 0, alpha=one)
             ref = lambda: torch._scaled_mm(A.view(torch.float8_e4m3fn), B.view(torch.float8_e4m3fn).t(), one, one,
                                            out_dtype=torch.bfloat16)
+        elif lay == "tn_gelu8":
+            pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            a8 = torch.empty(M, N, device="cuda", dtype=torch.uint8)
+            bias = torch.zeros(N, device="cuda")
+            amax = torch.zeros(1, device="cuda")
+            mine = lambda: F8.gemm_fp8_gelu8(A, 0, B, 0, pre, a8, one, amax, 0, bias=bias, alpha=one, alpha2=one)
+            ref = None
+        elif lay == "tn_res":
+            bias = torch.zeros(N, device="cuda")
+            res = torch.randn(M, N, device="cuda").bfloat16()
+            mine = lambda: F8.gemm_fp8(A, 0, B, 0, bias=bias, residual=res, alpha=one, alpha2=one)
+            ref = None
+        elif lay == "dgrad_aux":
+            aux = torch.randn(M, N, device="cuda").bfloat16()
+            mine = lambda: F8.gemm_fp8(A, 1, B, 0, b_mn=True, aux=aux, alpha=one, alpha2=one)
+            ref = None
+        elif lay == "wgrad_acc":
+            out = torch.zeros(M, N, device="cuda")
+            mine = lambda: F8.gemm_fp8(A, 1, B, 0, out=out, a_mn=True, b_mn=True, accumulate=True, alpha=one,
+                                       alpha2=one)
+            ref = None
         elif lay == "dgrad":
             mine = lambda: F8.gemm_fp8(A, 1, B, 0, b_mn=True, alpha=one)
             ref = None

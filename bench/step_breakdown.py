@@ -111,6 +111,7 @@ def main() -> int:
     count = defaultdict(int)
     per_kernel = defaultdict(float)
     intervals = []
+    gemm_seq = []  # (start, ms, name) of the block GEMM launches, in launch order
     t_lo, t_hi = None, None
     for ev in prof.events():
         if ev.device_type != torch.autograd.DeviceType.CUDA:
@@ -123,6 +124,8 @@ def main() -> int:
         t_lo = s if t_lo is None else min(t_lo, s)
         t_hi = s + dur_ms if t_hi is None else max(t_hi, s + dur_ms)
         c = classify(ev.name)
+        if c.startswith("gemm"):
+            gemm_seq.append((s, dur_ms, c))
         per_cls[c] += dur_ms
         count[c] += 1
         per_kernel[ev.name] += dur_ms
@@ -144,6 +147,16 @@ def main() -> int:
     print(f"{'class':32s} {'ms/step':>9s} {'share':>7s} {'launches':>9s}")
     for c, v, k in rows:
         print(f"{c:32s} {v:9.3f} {v / step_ms:7.1%} {k:9.1f}")
+    gemm_seq.sort()
+    fp8 = [d for _, d, c in gemm_seq if c.startswith("gemm fp8")]
+    per_step = len(fp8) // n if n else 0
+    if per_step >= 24:
+        first = fp8[:per_step]
+        bwd = first[per_step - 8:]
+        out["layer0_fwd_gemm_ms"] = [round(x, 4) for x in first[4:8]]
+        out["layer0_bwd_gemm_ms"] = [round(x, 4) for x in bwd]
+        print("one layer's forward GEMMs (qkv, out, ffn1, ffn2), ms:", out["layer0_fwd_gemm_ms"])
+        print("layer 0 backward GEMMs in launch order, ms:", out["layer0_bwd_gemm_ms"])
     print("top kernels:")
     for r in out["top_kernels"]:
         print(f"  {r['ms_per_step']:8.3f}  {r['name']}")

@@ -613,4 +613,110 @@ void fp8_quantize_blocks(const at::Tensor& x, at::Tensor out, at::Tensor scales,
   MT_LAUNCH_CHECK();
 }
 
+
+// ------------------------------------------------------------------ FP8 wire codec
+// Compressed transfer format for pipeline-stage activations and gradients: FP8
+// codes (E4M3 or E5M2) with one power-of-two scale per 32 consecutive values (the
+// MX block rule of mx.cuh, so no value saturates and a NaN / Inf block carries the
+// NaN scale), flat layout: codes[numel] then scales[ceil(numel / 32)].  1.03 bytes
+// per value instead of 2 (bf16) or 4 (fp32).  One thread per 32-value block; the
+// last block is zero-padded.
+__device__ __forceinline__ void wire_dec2(uint16_t c, int fmt, float& a, float& b) {
+  uint32_t h;
+  if (fmt == 0)
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(c));
+  else
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h) : "h"(c));
+  const __half2 hh = *reinterpret_cast<__half2*>(&h);
+  a = __low2float(hh);
+  b = __high2float(hh);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) wire_encode_kernel(const T* __restrict__ x, uint8_t* __restrict__ codes,
+                                                          uint8_t* __restrict__ sf, int64_t numel, int fmt,
+                                                          uint32_t fmax_bits) {
+  const int ef = (int)((fmax_bits >> 23) & 0xFF);
+  const uint32_t mf = fmax_bits & 0x7FFFFF;
+  const int64_t nb = (numel + 31) / 32;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+    float v[32];
+    const int64_t e0 = b * 32;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = e0 + i < numel ? to_f(x[e0 + i]) : 0.f;
+    uint32_t w[8];
+    uint8_t sfb;
+    mx_block(v, ef, mf, fmt, w, sfb);
+    if (e0 + 32 <= numel && (reinterpret_cast<uintptr_t>(codes + e0) & 15) == 0) {
+      uint4* dst = reinterpret_cast<uint4*>(codes + e0);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      for (int i = 0; i < 32 && e0 + i < numel; ++i) codes[e0 + i] = (uint8_t)(w[i >> 2] >> ((i & 3) * 8));
+    }
+    sf[b] = sfb;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) wire_decode_kernel(const uint8_t* __restrict__ codes,
+                                                          const uint8_t* __restrict__ sf, T* __restrict__ out,
+                                                          int64_t numel, int fmt) {
+  const int64_t nb = (numel + 31) / 32;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nb; b += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t s = sf[b];
+    const float scale = s == 255u ? __uint_as_float(0x7FC00000u)
+                                  : (s == 0u ? __uint_as_float(0x00400000u) : __uint_as_float(s << 23));
+    const int64_t e0 = b * 32;
+    for (int i = 0; i < 32 && e0 + i < numel; i += 2) {
+      const uint16_t c = (uint16_t)codes[e0 + i] | (e0 + i + 1 < numel ? (uint16_t)codes[e0 + i + 1] << 8 : 0);
+      float a, bb;
+      wire_dec2(c, fmt, a, bb);
+      out[e0 + i] = from_f<T>(a * scale);
+      if (e0 + i + 1 < numel) out[e0 + i + 1] = from_f<T>(bb * scale);
+    }
+  }
+}
+
+// x: bf16 or fp32, contiguous; codes: uint8 [numel]; sf: uint8 [ceil(numel / 32)].
+void fp8_wire_encode(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt) {
+  MT_CHECK(x.is_contiguous() && codes.is_contiguous() && sf.is_contiguous(), "wire_encode: contiguous tensors");
+  const int64_t n = x.numel();
+  MT_CHECK(codes.numel() >= n && sf.numel() >= (n + 31) / 32, "wire_encode: output sizes");
+  if (n == 0) return;
+  const float fmax = fmt == 0 ? 448.f : 57344.f;
+  uint32_t bits;
+  std::memcpy(&bits, &fmax, 4);
+  const int64_t nb = (n + 31) / 32;
+  const int grid = (int)std::min<int64_t>((nb + 255) / 256, 148 * 16);
+  auto* c = reinterpret_cast<uint8_t*>(codes.data_ptr());
+  auto* f = reinterpret_cast<uint8_t*>(sf.data_ptr());
+  if (x.scalar_type() == at::kBFloat16)
+    wire_encode_kernel<bf16><<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()), c, f, n,
+                                                           (int)fmt, bits);
+  else {
+    MT_CHECK(x.scalar_type() == at::kFloat, "wire_encode: bf16 or fp32 input");
+    wire_encode_kernel<float><<<grid, 256, 0, cur_stream()>>>(x.data_ptr<float>(), c, f, n, (int)fmt, bits);
+  }
+  MT_LAUNCH_CHECK();
+}
+
+void fp8_wire_decode(const at::Tensor& codes, const at::Tensor& sf, at::Tensor out, int64_t fmt) {
+  MT_CHECK(out.is_contiguous() && codes.is_contiguous() && sf.is_contiguous(), "wire_decode: contiguous tensors");
+  const int64_t n = out.numel();
+  if (n == 0) return;
+  const int64_t nb = (n + 31) / 32;
+  const int grid = (int)std::min<int64_t>((nb + 255) / 256, 148 * 16);
+  const auto* c = reinterpret_cast<const uint8_t*>(codes.data_ptr());
+  const auto* f = reinterpret_cast<const uint8_t*>(sf.data_ptr());
+  if (out.scalar_type() == at::kBFloat16)
+    wire_decode_kernel<bf16><<<grid, 256, 0, cur_stream()>>>(c, f, reinterpret_cast<bf16*>(out.data_ptr()), n,
+                                                           (int)fmt);
+  else {
+    MT_CHECK(out.scalar_type() == at::kFloat, "wire_decode: bf16 or fp32 output");
+    wire_decode_kernel<float><<<grid, 256, 0, cur_stream()>>>(c, f, out.data_ptr<float>(), n, (int)fmt);
+  }
+  MT_LAUNCH_CHECK();
+}
+
 }  // namespace mtorus

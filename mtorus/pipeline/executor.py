@@ -18,6 +18,12 @@ the first half and the midpoint output, and recomputes only the second half in
 backward (half of Full's recompute, about half of None's activation memory).
 A stage of one segment has no midpoint, so Selective runs it as Full, like the
 reference.
+
+``wire="fp8"`` compresses every stage transfer the way the reference's
+PipelineComm does (crates/mt-pipeline/src/communicator.rs:44-73): activations as
+E4M3 and gradients as E5M2 by default, in the block-scaled wire format of
+``mtorus.pipeline.wire`` (one power-of-two scale per 32 values, ~1.03 bytes per
+value), encoded just before the send and decoded right after the receive.
 """
 from __future__ import annotations
 
@@ -33,6 +39,7 @@ from .checkpoint import CheckpointStrategy, checkpoint_module
 from .communicator import PipelineComm
 from .schedule import GpipeSchedule, OneF1BSchedule, PipeOp, ScheduleKind, ScheduleType, rank_program
 from .stage import PipelineStage
+from . import wire as W
 
 
 @dataclass
@@ -68,6 +75,8 @@ class DistributedPipelineExecutor:
                 divides it by the number of micro-batches
     act_shape   shape of the tensor exchanged between stages (per micro-batch)
     stage_fn    optional forward callable used instead of ``module(x)``
+    wire        "native" (send act_dtype tensors) or "fp8" (block-scaled FP8 codes:
+                ``wire_act_fmt`` for activations, ``wire_grad_fmt`` for gradients)
     stage_segments  optional list of callables whose composition is the stage
                 forward (e.g. one per layer); ``Selective`` checkpointing splits
                 it at the midpoint.  Default: the children of an
@@ -99,7 +108,12 @@ class DistributedPipelineExecutor:
                  device=None, group=None, on_backward_done: Optional[Callable[[int], None]] = None,
                  stage_fn: Optional[Callable] = None, pre_backward: Optional[Callable[[int, int], None]] = None,
                  grad_group=None, sync_losses: bool = True, timed: bool = False,
-                 stage_segments: Optional[Sequence[Callable]] = None):
+                 stage_segments: Optional[Sequence[Callable]] = None, wire: str = "native",
+                 wire_act_fmt: int = W.E4M3, wire_grad_fmt: int = W.E5M2):
+        if wire not in ("native", "fp8"):
+            raise ValueError(f"wire must be 'native' or 'fp8', not {wire!r}")
+        self.wire = wire
+        self.wire_fmt = {True: wire_act_fmt, False: wire_grad_fmt}  # keyed by "is activation"
         self.module = module
         self.stage_ranks = list(stage_ranks)
         self.S = len(self.stage_ranks)
@@ -152,7 +166,8 @@ class DistributedPipelineExecutor:
         self._connected = True
         if self.S == 1:
             return
-        buf_out = torch.zeros(self.act_shape, dtype=self.act_dtype, device=self.device)
+        buf_out = self._wire_buffer()
+        buf_out.zero_()
         buf_in = torch.empty_like(buf_out)
         works = []
         for grp, nxt, prv in ((self.group, self.stage + 1, self.stage - 1),
@@ -168,6 +183,26 @@ class DistributedPipelineExecutor:
 
     def _stage_forward(self, x):
         return self.stage_fn(x) if self.stage_fn is not None else self.module(x)
+
+    def _wire_buffer(self) -> torch.Tensor:
+        """Receive buffer of one transfer in the wire format."""
+        if self.wire == "fp8":
+            n = 1
+            for d in self.act_shape:
+                n *= int(d)
+            return torch.empty(W.wire_bytes(n), dtype=torch.uint8, device=self.device)
+        return torch.empty(self.act_shape, dtype=self.act_dtype, device=self.device)
+
+    def _to_wire(self, t: torch.Tensor, activation: bool) -> torch.Tensor:
+        t = t.detach().contiguous()
+        if self.wire == "fp8":
+            return W.encode(t, self.wire_fmt[activation])
+        return t
+
+    def _from_wire(self, buf: torch.Tensor, activation: bool) -> torch.Tensor:
+        if self.wire == "fp8":
+            return W.decode(buf, self.act_shape, self.act_dtype, self.wire_fmt[activation])
+        return buf
 
     def _selective_forward(self, x):
         """First half of the segments with their activations kept; the second half
@@ -211,7 +246,7 @@ class DistributedPipelineExecutor:
             while scan < min(limit, len(prog)):
                 op = prog[scan]
                 if op.kind in (K.RecvAct, K.RecvGrad):
-                    buf = torch.empty(self.act_shape, dtype=self.act_dtype, device=self.device)
+                    buf = self._wire_buffer()
                     grp = self.group if op.kind == K.RecvAct else self.grad_group
                     posted[scan] = (buf, dist.irecv(buf, self._peer(op.peer), group=grp))
                 scan += 1
@@ -228,7 +263,7 @@ class DistributedPipelineExecutor:
                 post_until(i + 1)
                 buf, work = posted.pop(i)
                 work.wait()
-                (recv_act if op.kind == K.RecvAct else recv_grad)[m] = buf
+                (recv_act if op.kind == K.RecvAct else recv_grad)[m] = self._from_wire(buf, op.kind == K.RecvAct)
                 continue
             if op.kind in (K.Forward, K.Backward):
                 # receives needed by the next compute op go out before this one runs
@@ -258,8 +293,8 @@ class DistributedPipelineExecutor:
                     stash_out[m] = y
                 peak = max(peak, len(stash_in))
             elif op.kind == K.SendAct:
-                y = stash_out[m]
-                pending_sends.append(dist.isend(y.detach().contiguous(), self._peer(op.peer), group=self.group))
+                y = self._to_wire(stash_out[m], True)
+                pending_sends.append((dist.isend(y, self._peer(op.peer), group=self.group), y))
             elif op.kind == K.Backward:
                 if self.pre_backward is not None:
                     self.pre_backward(m, n_bwd)
@@ -283,14 +318,15 @@ class DistributedPipelineExecutor:
                 stash_in[m] = x  # keep for SendGrad
             elif op.kind == K.SendGrad:
                 x = stash_in.pop(m)
-                pending_sends.append(dist.isend(x.grad.contiguous(), self._peer(op.peer), group=self.grad_group))
+                gx = self._to_wire(x.grad, False)
+                pending_sends.append((dist.isend(gx, self._peer(op.peer), group=self.grad_group), gx))
             if op.kind in (K.Forward, K.Backward) and self.timed:
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev1.record()
                 events.append((ev0, ev1))
             if len(pending_sends) > 8:
-                pending_sends.pop(0).wait()
-        for w in pending_sends:
+                pending_sends.pop(0)[0].wait()
+        for w, _ in pending_sends:
             w.wait()
         stash_in.clear()
         self.peak_inflight = peak

@@ -388,3 +388,28 @@ def test_e5m2_encode_and_decode_mean_kernels_match_cpu_path():
     both_nan = torch.isnan(got.float()) & torch.isnan(ref.float())
     assert bool(both_nan[64:96].all())  # the block holding the Inf decodes to NaN
     assert torch.equal(got[~both_nan], ref[~both_nan])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fp8_wire_codec_kernels_match_reference(dtype):
+    """The pipeline's FP8 wire encoder / decoder kernels agree with the PyTorch
+    restatement byte for byte (ragged tail, zero block, NaN block included)."""
+    from mtorus.pipeline import wire as W
+
+    g = torch.Generator().manual_seed(5)
+    x = (torch.randn(4133, generator=g) * torch.logspace(-6, 6, 4133)).to(dtype)
+    x[96:128] = 0
+    x[300] = float("nan")
+    for fmt in (W.E4M3, W.E5M2):
+        ref = W.encode_ref(x, fmt)
+        got = W.encode(x.cuda(), fmt).cpu()
+        n = x.numel()
+        assert torch.equal(got[n:], ref[n:])  # every block's scale byte, the NaN block's 255 included
+        keep = torch.ones(n, dtype=torch.bool)
+        keep[288:320] = False  # the NaN block decodes to NaN whatever its codes
+        assert torch.equal(got[:n][keep], ref[:n][keep])
+        back = W.decode(got.cuda(), x.shape, dtype, fmt).cpu()
+        want = W.decode_ref(ref, x.shape, dtype, fmt)
+        assert torch.equal(torch.isnan(back), torch.isnan(want))
+        ok = ~torch.isnan(want)
+        assert torch.equal(back[ok], want[ok])

@@ -43,7 +43,7 @@ def _make_stages(seed=0):
             torch.nn.Sequential(torch.nn.Linear(16, 4))]
 
 
-def _pp_body(rank, world, sched_name, ckpt_name):
+def _pp_body(rank, world, sched_name, ckpt_name, wire="native"):
     from mtorus.pipeline import CheckpointStrategy, DistributedPipelineExecutor, ScheduleType
 
     stages = _make_stages()
@@ -54,7 +54,8 @@ def _pp_body(rank, world, sched_name, ckpt_name):
     shapes = [(2, 16), (2, 16), (2, 4)]
     ex = DistributedPipelineExecutor(stages[rank], list(range(world)), getattr(ScheduleType, sched_name), M,
                                      getattr(CheckpointStrategy, ckpt_name),
-                                     loss_fn=torch.nn.functional.mse_loss, act_shape=shapes[max(rank - 1, 0)])
+                                     loss_fn=torch.nn.functional.mse_loss, act_shape=shapes[max(rank - 1, 0)],
+                                     wire=wire)
     losses = ex.run(xs if rank == 0 else None, ys if rank == world - 1 else None)
     grads = [p.grad.clone() for p in stages[rank].parameters()]
     return losses, grads
@@ -79,6 +80,19 @@ def test_pipeline_executor_matches_single_process(sched, ckpt):
     for r in range(3):
         for gp, p in zip(res[r][1], stages[r].parameters()):
             assert torch.allclose(gp, p.grad, atol=1e-5), (r, (gp - p.grad).abs().max())
+
+
+def test_pipeline_executor_fp8_wire_tracks_full_precision():
+    """Stage transfers as block-scaled FP8 (E4M3 activations, E5M2 gradients; the
+    reference compresses them in PipelineComm, communicator.rs:44-73): losses and
+    gradients stay within FP8 rounding of the full-precision run."""
+    ref = run_dist(_pp_body, 3, ("OneF1B", "None_"))
+    got = run_dist(_pp_body, 3, ("OneF1B", "None_", "fp8"))
+    for a, b in zip(got[2][0], ref[2][0]):
+        assert abs(a - b) <= 0.05 * abs(b) + 1e-4
+    for r in range(3):
+        for ga, gb in zip(got[r][1], ref[r][1]):
+            assert float((ga - gb).norm()) <= 0.15 * float(gb.norm()) + 1e-6, r
 
 
 class _Counting(torch.nn.Module):

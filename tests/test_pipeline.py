@@ -276,3 +276,27 @@ def test_balanced_split_counts_the_lm_head():
     best = min(max(a * layer, b * layer, (9 - a - b) * layer + head)
                for a, b in itertools.product(range(1, 8), repeat=2) if a + b < 9)
     assert abs(got - best) < 1e-6
+
+
+def test_fp8_wire_reference_round_trip():
+    """Block-scaled FP8 wire format: codes || one UE8M0 scale per 32 values; the
+    decoded values are within half an ulp of the block-scaled format, zero blocks
+    stay zero, a NaN poisons its block, and a ragged tail round-trips."""
+    import torch
+
+    from mtorus.pipeline import wire as W
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1000, generator=g) * torch.logspace(-8, 8, 1000)
+    x[64:96] = 0.0
+    for fmt, rel in ((W.E4M3, 2.0 ** -4), (W.E5M2, 2.0 ** -3)):
+        buf = W.encode_ref(x, fmt)
+        assert buf.numel() == W.wire_bytes(1000) == 1000 + 32
+        y = W.decode_ref(buf, (1000,), torch.float32, fmt)
+        assert torch.equal(y[64:96], torch.zeros(32))
+        blk = x.reshape(-1)[: 992].reshape(31, 32).abs().amax(1).repeat_interleave(32)
+        err = (y[:992] - x[:992]).abs()
+        assert bool((err <= rel * x[:992].abs() + blk * 2.0 ** -9 + 1e-30).all())
+    x[5] = float("nan")
+    y = W.decode_ref(W.encode_ref(x, W.E4M3), (1000,), torch.float32, W.E4M3)
+    assert bool(torch.isnan(y[:32]).all()) and bool(torch.isfinite(y[32:]).all())
