@@ -344,15 +344,20 @@ namespace {
 
 constexpr int P_BM = 128;  // rows per CTA (pair tile M = 256)
 constexpr int P_BN = 256;  // pair tile N; each CTA stages 128 rows of B
-constexpr int P_STAGES = 5;
+constexpr int P_STAGES = 5;       // operand ring depth (the MXFP8 kernel: 4, its scales need the room)
+template <bool MX>
+constexpr int pair_stages() { return MX ? 4 : P_STAGES; }
 constexpr int P_GROUP_M = 8;  // pair tiles per raster group along M
 constexpr int P_A_BYTES = P_BM * 128;        // 128 rows x 128 bytes of K
 constexpr int P_B_BYTES = (P_BN / 2) * 128;  // 128 rows of B x 128 bytes of K
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-// Epilogue staging (per epilogue warp): two 32x32 output chunks (fp32 worst case,
-// 4 KB each) and two 32x32 bf16 GELU chunks, written to global memory by TMA.
-constexpr int P_EPI_D_BYTES = 4096, P_EPI_ACT_BYTES = 2048;
-constexpr int P_EPI_BYTES = 4 * 2 * (P_EPI_D_BYTES + P_EPI_ACT_BYTES);
+// Epilogue: eight warps, each with two 4 KB staging buffers; a buffer holds one
+// 32x32 output chunk (fp32, 4 KB) or a bf16 chunk (2 KB) plus its GELU output
+// (bf16 2 KB or FP8 1 KB at offset 2048), written to global memory by TMA.
+constexpr int P_EPI_WARPS = 8;
+constexpr int kPairThreads = 64 + 32 * P_EPI_WARPS;
+constexpr int P_EPI_BUF = 4096;
+constexpr int P_EPI_BYTES = P_EPI_WARPS * 2 * P_EPI_BUF;
 // MXFP8 (1x32 UE8M0 block scales) per stage: this CTA's 128-row SFA atom and the
 // pair tile's two 128-row SFB atoms (every CTA needs the scales of all 256 B rows,
 // since its tensor core multiplies its A rows with the whole B tile).  An atom holds
@@ -402,6 +407,131 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n,
 
 }  // namespace
 
+// Accumulator chunk (32 columns) processed i-th by epilogue warp half h; MXFP8
+// buffer 0 starts with the chunk it shares with buffer 1 (see MX_ACC1_COL).
+template <bool MX>
+__device__ __forceinline__ int epi_chunk(int buf, int h, int i) {
+  if (MX && buf == 0 && h == 1) return i == 0 ? 7 : 3 + i;
+  return h * 4 + i;
+}
+
+// The 64 bytes of row m, columns n0..n0+31 of the dGELU input (aux) or of the
+// residual, whichever the epilogue reads (never both: dGELU runs in dgrad GEMMs,
+// residual adds in forward GEMMs); zeros outside the matrix.
+__device__ __forceinline__ void epi_prefetch(const GemmEpilogue& ep, int m, int M, int N, int n0, uint4 (&x)[4]) {
+  const bf16* src = ep.aux ? ep.aux + (size_t)m * ep.ldaux + n0
+                           : (ep.residual ? ep.residual + (size_t)m * ep.ldr + n0 : nullptr);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    x[j] = (src && m < M && n0 + j * 8 + 8 <= N) ? reinterpret_cast<const uint4*>(src)[j] : make_uint4(0, 0, 0, 0);
+}
+
+// One 32 x 32 output chunk of an epilogue warp: registers -> staging buffer -> TMA store.
+// r: the lane's (row m) 32 accumulator values; x: its prefetched aux / residual;
+// stages: the warp's two 4 KB staging buffers (D at 0, the GELU output at 2048),
+// used in turn by the chunks that store (sb flips at each commit, so the buffer
+// written next is never the one the most recent store still reads).
+__device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const uint4 (&x)[4], int m, int M, int N,
+                                                int n0, int row0, float alpha, float act_scale, float& act_amax,
+                                                const GemmEpilogue& ep, bool f32out, uint8_t* stages, int& sb,
+                                                const CUtensorMap* tma_d, const CUtensorMap* tma_act, int lane) {
+  if (n0 >= N) return;  // warp-uniform
+  uint8_t* stage = stages + sb * P_EPI_BUF;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
+  if (ep.bias) {
+    if (n0 + 32 <= N) {
+      const float4* bp = reinterpret_cast<const float4*>(ep.bias + n0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 b = bp[j];
+        v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (n0 + i < N) v[i] += ep.bias[n0 + i];
+    }
+  }
+  if (ep.aux) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float a8[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(&x[j]), a8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[j * 8 + i] *= gelu_grad_f(a8[i]);
+    }
+  } else if (ep.residual) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float r8[8];
+      unpack8(*reinterpret_cast<const bf16x8*>(&x[j]), r8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[j * 8 + i] += r8[i];
+    }
+  }
+  if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer two chunks ago
+  __syncwarp();
+  if (f32out) {
+    // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row r sits at j ^ (r & 7)
+    uint8_t* base = stage + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(base + ((j ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    // 32 rows x 64 B, 64B swizzle: 16-byte chunk j of row r sits at j ^ ((r >> 1) & 3)
+    uint8_t* base = stage + lane * 64;
+    uint8_t* abase = stage + 2048;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bf16x8 pk = pack8(v + 8 * j);
+      *reinterpret_cast<bf16x8*>(base + ((j ^ ((lane >> 1) & 3)) << 4)) = pk;
+      if (ep.act) {
+        float p8[8], g8[8];
+        unpack8(pk, p8);  // GELU of the rounded pre-activation
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
+        *reinterpret_cast<bf16x8*>(abase + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = pack8(g8);
+      } else if (ep.act8) {
+        // FP8 GELU: the bf16-rounded GELU (as the bf16 path stores it) times the scale;
+        // 32 rows x 32 B, unswizzled
+        float p8[8], g8[8], r8[8];
+        unpack8(pk, p8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
+        unpack8(pack8(g8), r8);
+        uint32_t w[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (m < M) {  // rows past M hold GELU(bias) of zero-filled A rows
+#pragma unroll
+            for (int t = 0; t < 4; ++t) act_amax = fmaxf(act_amax, fabsf(r8[4 * k + t]));
+          }
+          const uint16_t lo = ep.act8_fmt == 0 ? cvt2_e4m3(r8[4 * k] * act_scale, r8[4 * k + 1] * act_scale)
+                                               : cvt2_e5m2(r8[4 * k] * act_scale, r8[4 * k + 1] * act_scale);
+          const uint16_t hi = ep.act8_fmt == 0 ? cvt2_e4m3(r8[4 * k + 2] * act_scale, r8[4 * k + 3] * act_scale)
+                                               : cvt2_e5m2(r8[4 * k + 2] * act_scale, r8[4 * k + 3] * act_scale);
+          w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+        }
+        *reinterpret_cast<uint2*>(abase + lane * 32 + j * 8) = make_uint2(w[0], w[1]);
+      }
+    }
+  }
+  fence_async_shared();
+  __syncwarp();
+  if (lane == 0) {
+    if (f32out && ep.beta)
+      tma_reduce_add_2d(tma_d, stage, n0, row0);
+    else
+      tma_store_2d(tma_d, stage, n0, row0);
+    if (ep.act || ep.act8) tma_store_2d(tma_act, stage + 2048, n0, row0);
+    bulk_commit_group();
+  }
+  sb ^= 1;
+}
+
 // EB = operand element bytes: 2 (bf16, kind::f16) or 1 (fp8 E4M3/E5M2, kind::f8f6f4).
 // A k-block is always 128 bytes of K per row (64 bf16 / 128 fp8), so the stage
 // layout is identical and an fp8 stage carries twice the MMA work.
@@ -410,7 +540,7 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n,
 // (tcgen05.cp, ordered before the stage's MMAs, which read them); sf_kb = number of
 // 128-wide K blocks per 128-row block of the scale tensors.
 template <int EB, bool MX = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     const __grid_constant__ CUtensorMap tma_b,
                     const __grid_constant__ CUtensorMap tma_d,
@@ -424,12 +554,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr int MMA_K = 32 / EB;     // K elements per tcgen05.mma
   constexpr int MN_BOX = 128 / EB;   // MN elements per 128-byte swizzle row
   constexpr int A_BOXES = P_BM * EB / 128, B_BOXES = (P_BN / 2) * EB / 128;
+  constexpr int NST = pair_stages<MX>();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* epi_smem = smem + P_STAGES * P_STAGE_BYTES;
+  uint8_t* epi_smem = smem + NST * P_STAGE_BYTES;
   uint8_t* sf_smem = epi_smem + P_EPI_BYTES;
-  PairSmem* ctl = reinterpret_cast<PairSmem*>(sf_smem + (MX ? P_STAGES * P_SF_BYTES : 0));
+  PairSmem* ctl = reinterpret_cast<PairSmem*>(sf_smem + (MX ? NST * P_SF_BYTES : 0));
   constexpr uint32_t ACC1_COL = MX ? MX_ACC1_COL : P_BN;  // TMEM column of accumulator 1
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -441,13 +572,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int num_kb = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P_STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&ctl->full[s], 1);
       mbar_init(&ctl->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ctl->tfull[b], 1);
-      mbar_init(&ctl->tempty[b], 2 * 128);
+      mbar_init(&ctl->tempty[b], 2 * 32 * P_EPI_WARPS);
     }
     if constexpr (MX) mbar_init(&ctl->ovl, 2 * 128);
     ctl->abort = 0;
@@ -505,7 +636,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tma_load_2d_pair(ssf + P_SF_ATOM, &tma_sfb, &ctl->full[stage], 0, (brb * sf_kb + kb) * 2);
             tma_load_2d_pair(ssf + 2 * P_SF_ATOM, &tma_sfb, &ctl->full[stage], 0, ((brb + 1) * sf_kb + kb) * 2);
           }
-          if (++stage == P_STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1;
           }
@@ -561,7 +692,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               umma_f8_2sm(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_2sm_mc(&ctl->empty[stage], 0x3);
-          if (++stage == P_STAGES) {
+          if (++stage == NST) {
             stage = 0;
             phase ^= 1;
           }
@@ -572,19 +703,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
-    // TMEM -> registers (alpha, bias, dGELU, residual) -> swizzled smem chunk ->
-    // TMA store (or TMA reduce-add for fp32 accumulation).  Two staging buffers
-    // per warp let the math of chunk c overlap the store of chunk c-1.
+    // Eight warps, two per TMEM lane quarter (a warp may only read the 32 lanes of
+    // quarter warp % 4): warp half h = 0 takes accumulator columns 0..127, h = 1
+    // columns 128..255, as four 32-column chunks.  TMEM -> registers (alpha, bias,
+    // dGELU, residual) -> swizzled smem chunk -> TMA store (or TMA reduce-add for
+    // fp32 accumulation).  The TMEM load of chunk i+1 and the global loads (aux,
+    // residual) it needs are issued before chunk i is processed, so their latency
+    // hides behind its math; two staging buffers per warp let the math of chunk i
+    // overlap the store of chunk i-1.
+    const int ew = warp - 2;
     const int q = warp & 3;
+    const int h = ew >> 2;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&ctl->tempty[0]), 0);
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&ctl->tempty[1]), 0);
     const uint32_t ovl_leader = mapa_shared(smem_u32(&ctl->ovl), 0);
-    uint8_t* dstage = epi_smem + q * 2 * P_EPI_D_BYTES;
-    uint8_t* astage = epi_smem + 4 * 2 * P_EPI_D_BYTES + q * 2 * P_EPI_ACT_BYTES;
+    uint8_t* stage_base = epi_smem + ew * 2 * P_EPI_BUF;
     const bool f32out = ep.out_f32 != 0;
     const float act_scale = ep.act8_scale ? *ep.act8_scale : 1.f;
     float act_amax = 0.f;
-    int chunk_count = 0;
+    int sb = 0;
     int local = 0;
     for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs, ++local) {
       int mb, nb;
@@ -596,121 +733,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int row0 = mb * 2 * P_BM + (int)rank * P_BM + q * 32;
       const int m = row0 + lane;
       const float alpha = (ep.alpha ? *ep.alpha : 1.f) * (ep.alpha2 ? *ep.alpha2 : 1.f);
+      // MXFP8: the chunk the two accumulators share (columns 224..255 of accumulator 0
+      // = columns 0..31 of accumulator 1) is read first, and its readers signal "ovl"
+      const bool shared_first = MX && ((buf == 0 && h == 1) || (buf == 1 && h == 0));
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC1_COL;
+      uint32_t ra[32], rb[32];
+      uint4 xa[4], xb[4];  // aux (dGELU input) or residual of the chunk, prefetched
+      tmem_ld32(tbase + epi_chunk<MX>(buf, h, 0) * 32, ra);
+      epi_prefetch(ep, m, M, N, nb * P_BN + epi_chunk<MX>(buf, h, 0) * 32, xa);
+      tmem_wait_ld();
+      if (shared_first) {
+        tc_fence_before();
+        mbar_arrive_cluster(ovl_leader);
+      }
 #pragma unroll 1
-      for (int step = 0; step < P_BN / 32; ++step, ++chunk_count) {
-        // MXFP8: accumulator 0 is read from its last chunk (the one accumulator 1 shares)
-        const int c = (MX && buf == 0) ? ((step + P_BN / 32 - 1) % (P_BN / 32)) : step;
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC1_COL + c * 32, r);
+      for (int i = 0; i < 4; i += 2) {
+        const int c0 = epi_chunk<MX>(buf, h, i), c1 = epi_chunk<MX>(buf, h, i + 1);
+        tmem_ld32(tbase + c1 * 32, rb);
+        epi_prefetch(ep, m, M, N, nb * P_BN + c1 * 32, xb);
+        epi_chunk_store(ra, xa, m, M, N, nb * P_BN + c0 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
+                        stage_base, sb, &tma_d, &tma_act, lane);
         tmem_wait_ld();
-        if constexpr (MX) {
-          if (step == 0) {
-            tc_fence_before();
-            mbar_arrive_cluster(ovl_leader);
-          }
-        }
-        if (step == P_BN / 32 - 1) {
-          // the whole accumulator buffer is in registers / smem now: release it
+        if (i + 1 == 3) {
+          // every column of this warp's share of the buffer is in registers: release it
           tc_fence_before();
           mbar_arrive_cluster(buf ? tempty_leader1 : tempty_leader0);
-        }
-        const int n0 = nb * P_BN + c * 32;
-        if (n0 >= N) continue;  // warp-uniform
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
-        if (ep.bias) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (n0 + i < N) v[i] += ep.bias[n0 + i];
-        }
-        if (m < M) {
-          if (ep.aux) {
-            const bf16* ax = ep.aux + (size_t)m * ep.ldaux + n0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (n0 + j * 8 + 8 <= N) {
-                float a8[8];
-                unpack8(reinterpret_cast<const bf16x8*>(ax)[j], a8);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[j * 8 + i] *= gelu_grad_f(a8[i]);
-              }
-            }
-          }
-          if (ep.residual) {
-            const bf16* rp = ep.residual + (size_t)m * ep.ldr + n0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (n0 + j * 8 + 8 <= N) {
-                float r8[8];
-                unpack8(reinterpret_cast<const bf16x8*>(rp)[j], r8);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[j * 8 + i] += r8[i];
-              }
-            }
-          }
-        }
-        const int sb = chunk_count & 1;
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        if (f32out) {
-          // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row r sits at j ^ (r & 7)
-          uint8_t* base = dstage + sb * P_EPI_D_BYTES + lane * 128;
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<float4*>(base + ((j ^ (lane & 7)) << 4)) =
-                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         } else {
-          // 32 rows x 64 B, 64B swizzle: 16-byte chunk j of row r sits at j ^ ((r >> 1) & 3)
-          uint8_t* base = dstage + sb * P_EPI_D_BYTES + lane * 64;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const bf16x8 pk = pack8(v + 8 * j);
-            *reinterpret_cast<bf16x8*>(base + ((j ^ ((lane >> 1) & 3)) << 4)) = pk;
-            if (ep.act) {
-              float p8[8], g8[8];
-              unpack8(pk, p8);  // GELU of the rounded pre-activation
-#pragma unroll
-              for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
-              *reinterpret_cast<bf16x8*>(astage + sb * P_EPI_ACT_BYTES + lane * 64 +
-                                         ((j ^ ((lane >> 1) & 3)) << 4)) = pack8(g8);
-            } else if (ep.act8) {
-              // FP8 GELU: the bf16-rounded GELU (as the bf16 path stores it) times the scale;
-              // 32 rows x 32 B, unswizzled
-              float p8[8], g8[8], r8[8];
-              unpack8(pk, p8);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
-              unpack8(pack8(g8), r8);
-              uint32_t w[2];
-#pragma unroll
-              for (int k = 0; k < 2; ++k) {
-                if (m < M) {  // rows past M hold GELU(bias) of zero-filled A rows
-#pragma unroll
-                  for (int t = 0; t < 4; ++t) act_amax = fmaxf(act_amax, fabsf(r8[4 * k + t]));
-                }
-                const uint16_t lo = ep.act8_fmt == 0 ? cvt2_e4m3(r8[4 * k] * act_scale, r8[4 * k + 1] * act_scale)
-                                                     : cvt2_e5m2(r8[4 * k] * act_scale, r8[4 * k + 1] * act_scale);
-                const uint16_t hi = ep.act8_fmt == 0
-                                        ? cvt2_e4m3(r8[4 * k + 2] * act_scale, r8[4 * k + 3] * act_scale)
-                                        : cvt2_e5m2(r8[4 * k + 2] * act_scale, r8[4 * k + 3] * act_scale);
-                w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
-              }
-              *reinterpret_cast<uint2*>(astage + sb * P_EPI_ACT_BYTES + lane * 32 + j * 8) =
-                  make_uint2(w[0], w[1]);
-            }
-          }
+          const int c2 = epi_chunk<MX>(buf, h, i + 2);
+          tmem_ld32(tbase + c2 * 32, ra);
+          epi_prefetch(ep, m, M, N, nb * P_BN + c2 * 32, xa);
         }
-        fence_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          if (f32out && ep.beta)
-            tma_reduce_add_2d(&tma_d, dstage + sb * P_EPI_D_BYTES, n0, row0);
-          else
-            tma_store_2d(&tma_d, dstage + sb * P_EPI_D_BYTES, n0, row0);
-          if (ep.act || ep.act8) tma_store_2d(&tma_act, astage + sb * P_EPI_ACT_BYTES, n0, row0);
-          bulk_commit_group();
-        }
+        epi_chunk_store(rb, xb, m, M, N, nb * P_BN + c1 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
+                        stage_base, sb, &tma_d, &tma_act, lane);
+        if (i + 1 != 3) tmem_wait_ld();
       }
     }
     if (lane == 0) bulk_wait_group<0>();
@@ -904,15 +959,17 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
   const int num_tiles = (int)(((M + 2 * P_BM - 1) / (2 * P_BM)) * ((N + P_BN - 1) / P_BN));
   const int avail_pairs = std::max(1, (num_sms() - g_reserved_sms) / 2);
   const int pairs = std::min(num_tiles, avail_pairs);
-  const size_t smem = P_STAGES * P_STAGE_BYTES + P_EPI_BYTES + (MX ? P_STAGES * P_SF_BYTES : 0) +
-                      sizeof(PairSmem) + 1024;
+  constexpr int NST = pair_stages<MX>();
+  const size_t smem = NST * P_STAGE_BYTES + P_EPI_BYTES + (MX ? NST * P_SF_BYTES : 0) + sizeof(PairSmem) + 1024;
+  static_assert(NST * P_STAGE_BYTES + P_EPI_BYTES + (MX ? NST * P_SF_BYTES : 0) + sizeof(PairSmem) + 1024 <= 232448,
+                "CTA-pair GEMM: shared memory above the 227 KB per-CTA limit");
   static bool attr_set = false;
   if (!attr_set) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB, MX>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set = true;
   }
-  gemm_2sm_kernel<EB, MX><<<2 * pairs, kThreads, smem, cur_stream()>>>(
+  gemm_2sm_kernel<EB, MX><<<2 * pairs, kPairThreads, smem, cur_stream()>>>(
       ta, tb, td, tact, tsfa, tsfb, pb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
       idesc, ep, gemm_status_ptr());
   MT_LAUNCH_CHECK();
