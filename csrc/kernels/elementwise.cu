@@ -9,6 +9,7 @@
 // straight into the fp32 master-gradient buffer with vectorised fp32 atomics
 // (red.global.add.v4.f32) and sums position rows over the batch without atomics.
 #include "common.cuh"
+#include "gelu.cuh"
 
 namespace mtorus {
 
@@ -69,14 +70,8 @@ __global__ void embed_bwd_pos_kernel(const bf16* __restrict__ dy, float* __restr
   }
 }
 
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
-}
-__device__ __forceinline__ float gelu_erf_grad(float x) {
-  const float cdf = 0.5f * (1.f + erff(x * 0.70710678118654752f));
-  const float pdf = 0.39894228040143268f * __expf(-0.5f * x * x);
-  return cdf + x * pdf;
-}
+__device__ __forceinline__ float gelu_erf(float x) { return gelu_fwd(x); }
+__device__ __forceinline__ float gelu_erf_grad(float x) { return gelu_grad(x); }
 
 // pre[t, j] += bias[j] (in place, optional); act = gelu(pre)
 __global__ void bias_gelu_fwd_kernel(bf16* __restrict__ pre, const float* __restrict__ bias,

@@ -27,6 +27,7 @@
 #include <cstring>
 
 #include "amax_publish.cuh"
+#include "gelu.cuh"
 #include "sm100.cuh"
 
 namespace mtorus {
@@ -62,13 +63,8 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
 constexpr int kThreads = 192;
 
-__device__ __forceinline__ float gelu_f(float x) {
-  return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
-}
-__device__ __forceinline__ float gelu_grad_f(float x) {
-  const float cdf = 0.5f * (1.f + erff(x * 0.70710678118654752f));
-  return cdf + x * 0.39894228040143268f * __expf(-0.5f * x * x);
-}
+__device__ __forceinline__ float gelu_f(float x) { return gelu_fwd(x); }
+__device__ __forceinline__ float gelu_grad_f(float x) { return gelu_grad(x); }
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;

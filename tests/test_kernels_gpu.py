@@ -413,3 +413,18 @@ def test_fp8_wire_codec_kernels_match_reference(dtype):
         assert torch.equal(torch.isnan(back), torch.isnan(want))
         ok = ~torch.isnan(want)
         assert torch.equal(back[ok], want[ok])
+
+
+def test_gelu_kernels_match_fp32_erf_gelu_elementwise(K):
+    """The epilogues' GELU / GELU' (erf from Abramowitz & Stegun 7.1.26, |error| <=
+    1.5e-7) agree with PyTorch's fp32 erf GELU to bf16 rounding, element by element,
+    over [-8, 8] (both tails included)."""
+    x = torch.linspace(-8, 8, 4096 * 8, device="cuda").reshape(-1, 4096).bfloat16()
+    ref = F.gelu(x.float())
+    act = K.bias_gelu_fwd(x.clone(), None)
+    assert bool(((act.float() - ref).abs() <= 2.0 ** -8 * ref.abs() + 2e-6).all())
+    xg = x.float().requires_grad_(True)
+    F.gelu(xg).backward(torch.ones_like(xg))
+    d = torch.ones_like(x)
+    K.gelu_bwd_(d, x)
+    assert bool(((d.float() - xg.grad).abs() <= 2.0 ** -8 * xg.grad.abs() + 2e-6).all())
