@@ -5,6 +5,9 @@ Workload: GPT-1B decoder (24 layers, d_model 2048, 16 heads, d_ff 8192, vocab
 50304, seq 2048), micro-batch 8 sequences per GPU, pure data parallel over
 NCCL process groups, uniform-random synthetic tokens, N(0, 0.02) random-init
 weights, Adam.  One step = forward + backward + gradient reduction + optimizer.
+The transformer-layer GEMMs run the FP8 recipe with 1x32 block scales (MXFP8:
+E4M3 forward, E5M2 gradients, one UE8M0 scale per 32 values) unless
+``--precision`` says otherwise.
 
     python bench.py --gpus 1 --steps 10 --warmup 3
     torchrun --nproc-per-node 8 bench.py --gpus 8 ...
@@ -48,9 +51,10 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
                     help="replay the whole step as one CUDA graph (dp none / nccl); auto: on for 1 GPU")
-    ap.add_argument("--precision", default="fp8", choices=["fp8", "bf16", "mxfp8"],
-                    help="fp8: E4M3/E5M2 delayed-scaling GEMMs in the blocks; mxfp8: the same formats with "
-                         "1x32 UE8M0 block scales (block-scaled tcgen05 GEMMs); bf16: all GEMMs bf16")
+    ap.add_argument("--precision", default="mxfp8", choices=["mxfp8", "fp8", "bf16"],
+                    help="mxfp8 (default): E4M3 / E5M2 with one UE8M0 scale per 1x32 block in every "
+                         "transformer-layer GEMM (block-scaled tcgen05 GEMMs); fp8: the same formats with one "
+                         "per-tensor delayed-scaling scale; bf16: all GEMMs bf16")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -196,10 +200,12 @@ def main() -> int:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": {"fp8": "fp8 (E4M3 fwd / E5M2 grad block GEMMs, delayed scaling; bf16 LM head, attention, "
-                         "activations; fp32 master / Adam)",
-                  "mxfp8": "mxfp8 (E4M3 fwd / E5M2 grad block GEMMs, 1x32 UE8M0 block scales; bf16 LM head, "
-                           "attention, activations; fp32 master / Adam)",
+        "dtype": {"fp8": "fp8 (transformer-layer GEMMs: E4M3 forward / E5M2 gradients, one per-tensor "
+                         "delayed-scaling scale per operand; bf16 LM head, attention, activations; fp32 master "
+                         "weights / Adam)",
+                  "mxfp8": "mxfp8 (transformer-layer GEMMs: E4M3 forward / E5M2 gradients, one UE8M0 scale per "
+                           "1x32 block along each GEMM's contraction dimension; bf16 LM head, attention, "
+                           "activations; fp32 master weights / Adam)",
                   "bf16": "bf16"}[args.precision],
         "data": "synthetic uniform-random tokens, random-init N(0,0.02) weights",
         "config": {
@@ -212,6 +218,7 @@ def main() -> int:
             "dp_reduce": args.dp if world > 1 else "none",
             "dp_grad_transport": ("e5m2 (1x32 power-of-two scales)" if os.environ.get("MTORUS_DP_GRAD_FP8") == "1"
                                   else "fp32") if world > 1 else "none",
+            "precision": args.precision,
             "gemm": {"fp8": "tcgen05 kind::f8f6f4 fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, fp32 accumulate",
                      "mxfp8": "tcgen05 kind::mxf8f6f4 block-scaled fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, "
                               "fp32 accumulate",

@@ -117,7 +117,7 @@ def main():
     from mtorus.ops import mxfp8 as MX
 
     mx_cases = [("qkv_fwd_mx", T, 3 * d, d), ("out_fwd_mx", T, d, d), ("ffn1_fwd_mx", T, F, d),
-                ("ffn2_fwd_mx", T, d, F), ("square8k_mx", 8192, 8192, 8192)]
+                ("ffn2_fwd_mx", T, d, F), ("ffn1_wgrad_mx", F, d, T), ("square8k_mx", 8192, 8192, 8192)]
     if args.case:
         mx_cases = [c for c in mx_cases if c[0] == args.case]
     for name, M, N, Kd in mx_cases:

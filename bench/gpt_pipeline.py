@@ -45,7 +45,13 @@ def main(argv=None, defaults=None) -> int:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--no-checkpoint", action="store_true")
-    ap.add_argument("--precision", default="fp8", choices=["fp8", "bf16"])
+    ap.add_argument("--precision", default="fp8", choices=["fp8", "mxfp8", "bf16"])
+    ap.add_argument("--dp-mode", default="symm", choices=["symm", "nccl"],
+                    help="symm: fused NVLink reduce-scatter + sharded Adam + amax all-reduce in the quantise "
+                         "kernels; nccl: NCCL bucket all-reduce (the baseline)")
+    ap.add_argument("--checkpoint", default="full", choices=["full", "selective", "none"])
+    ap.add_argument("--wire", default="native", choices=["native", "fp8"],
+                    help="stage transfers as bf16 or as block-scaled FP8 codes")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="override layer count (debug only)")
     if defaults:
@@ -83,10 +89,13 @@ def main(argv=None, defaults=None) -> int:
     if args.layers is not None:
         cfg.num_layers = args.layers
     sched = ScheduleType.OneF1B if args.schedule == "1f1b" else ScheduleType.Gpipe
-    ckpt = CheckpointStrategy.None_ if args.no_checkpoint else CheckpointStrategy.Full
+    ckpt = {"full": CheckpointStrategy.Full, "selective": CheckpointStrategy.Selective,
+            "none": CheckpointStrategy.None_}["none" if args.no_checkpoint else args.checkpoint]
     M, b, S = args.micro_batches, args.micro_batch, args.seq
     tr = PipelineTrainer(cfg, pp=args.pp, dp=args.dp, schedule=sched, num_microbatches=M, micro_batch=b,
-                         seq_len=S, checkpoint=ckpt, fp8=args.precision == "fp8", lr=3e-4, device=dev, seed=1234)
+                         seq_len=S, checkpoint=ckpt, fp8=args.precision in ("fp8", "mxfp8"), lr=3e-4, device=dev,
+                         seed=1234, fp8_recipe="mx" if args.precision == "mxfp8" else "tensor",
+                         dp_mode=args.dp_mode if args.dp > 1 else "nccl", wire=args.wire)
     ext = _cuda()
 
     gen = torch.Generator().manual_seed(1000 + tr.replica)
@@ -172,8 +181,11 @@ def main(argv=None, defaults=None) -> int:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": ("fp8 (E4M3 fwd / E5M2 grad block GEMMs, delayed scaling; bf16 LM head, attention, "
-                  "activations and stage transfers; fp32 master / Adam)") if args.precision == "fp8" else "bf16",
+        "dtype": {"fp8": "fp8 (transformer-layer GEMMs: E4M3 forward / E5M2 gradients, per-tensor delayed "
+                         "scaling; bf16 LM head, attention, activations; fp32 master weights / Adam)",
+                  "mxfp8": "mxfp8 (transformer-layer GEMMs: E4M3 forward / E5M2 gradients, one UE8M0 scale per "
+                           "1x32 block; bf16 LM head, attention, activations; fp32 master weights / Adam)",
+                  "bf16": "bf16"}[args.precision],
         "data": "synthetic uniform-random tokens, random-init N(0,0.02) weights",
         "config": {
             "model": f"{name} ({cfg.num_layers} layers, d_model {cfg.d_model}, {cfg.num_heads} heads, "
@@ -184,8 +196,11 @@ def main(argv=None, defaults=None) -> int:
             "micro_batch": b,
             "parallelism": f"dp{args.dp}xpp{args.pp}",
             "schedule": args.schedule,
-            "activation_checkpointing": "none" if args.no_checkpoint else "full per stage",
-            "stage_transfer": "NCCL p2p, bf16 activations / gradients, separate groups per direction",
+            "activation_checkpointing": "none" if args.no_checkpoint else f"{args.checkpoint} per stage",
+            "dp_reduce": (args.dp_mode if args.dp > 1 else "none"),
+            "stage_transfer": ("NCCL p2p, " + ("block-scaled FP8 (E4M3 activations / E5M2 gradients)"
+                                               if args.wire == "fp8" else "bf16 activations / gradients")
+                               + ", separate groups per direction"),
             "l2": "per-step working set >> 126 MB L2; no flush",
             "model_tflops_per_gpu": round(cfg.train_flops_per_token(S) * tokens_per_step / world
                                           / (ms_step / 1000.0) / 1e12, 1),

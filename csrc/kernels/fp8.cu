@@ -322,60 +322,143 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(const bf16* __restrict
   }
 }
 
-// Row- and column-wise MXFP8 in one pass (the operands of all three GEMMs of a
-// linear layer): x [R, C] bf16 -> row codes [R, C] with 32-blocks along C, and the
-// transposed column codes [C, R] with 32-blocks along R, each with its own scale
-// atoms (same rule and layout as mx_quantize_kernel).  A CTA stages a 32 x 256 tile
-// in shared memory; thread t quantises row block (t / 8, t % 8) of the tile and then
-// column t, whose 32 codes are one contiguous 32-byte run of the transposed output.
-// R and C multiples of 32; a tile may overhang C (columns past C are skipped).
-__global__ void __launch_bounds__(256) mx_quantize_rc_kernel(const bf16* __restrict__ x, int64_t ldx, int R, int C,
-                                                             int fmt, uint32_t fmax_bits, uint8_t* __restrict__ rc,
-                                                             uint8_t* __restrict__ rsf, uint8_t* __restrict__ cc,
-                                                             uint8_t* __restrict__ csf) {
-  __shared__ __align__(16) bf16 tile[32][256 + 8];
-  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 256, t = threadIdx.x;
+// MXFP8 of a [R, C] bf16 tensor row-wise (32-blocks along C: the operand that
+// contracts over C) and column-wise (its transpose, 32-blocks along R), one
+// 128 x 128 tile per CTA.  A tile is exactly one 512-byte scale atom of each
+// output (128 rows x 4 K-blocks), so each CTA assembles both atoms in shared
+// memory and stores them whole; padding rows / columns read as zero and get the
+// scale byte 127, so no fill of the scale tensors is needed.  Both code tiles
+// (row-wise [128][128] and transposed [128][128]) are also assembled in shared
+// memory and stored as whole 128-byte rows, so every global store is coalesced.
+// LN: the tile is LayerNorm'd on load, bf16((x - mean[r]) * rstd[r] * gamma[c] +
+// beta[c]) (the MXFP8 input of the QKV / FFN1 GEMMs straight from the residual
+// stream).  colsum (optional): colsum[c] += sum over r of the tile's values (one
+// atomic per column per CTA).
+constexpr int kRcTileStride = 128 + 8;  // bf16 elements per staged row (16-byte rows, bank spread)
+constexpr int kRcSmem = 128 * kRcTileStride * 2 + 2 * 128 * 128 + 2 * 512 + 2 * 4 * 128;
+
+template <bool LN>
+__global__ void __launch_bounds__(256, 3) mx_rc_tile_kernel(const bf16* __restrict__ x, int64_t ldx, int R, int C, int fmt,
+                                                         uint32_t fmax_bits, const float* __restrict__ mean,
+                                                         const float* __restrict__ rstd,
+                                                         const float* __restrict__ gamma,
+                                                         const float* __restrict__ beta, float* __restrict__ colsum,
+                                                         uint8_t* __restrict__ rc, uint8_t* __restrict__ rsf,
+                                                         uint8_t* __restrict__ cc, uint8_t* __restrict__ csf) {
+  extern __shared__ __align__(16) uint8_t rc_smem[];
+  bf16 (*tile)[kRcTileStride] = reinterpret_cast<bf16 (*)[kRcTileStride]>(rc_smem);
+  uint8_t* rcode = rc_smem + 128 * kRcTileStride * 2;  // [128 rows][128 codes]
+  uint8_t* ccode = rcode + 128 * 128;                  // [128 columns][128 codes]
+  uint8_t* sfr = ccode + 128 * 128;
+  uint8_t* sfc = sfr + 512;
+  float* csum = reinterpret_cast<float*>(sfc + 512);  // [4][128]
+  const int rt = blockIdx.y, ct = blockIdx.x, t = threadIdx.x;
+  const int r0 = rt * 128, c0 = ct * 128;
   const int ef = (int)((fmax_bits >> 23) & 0xFF);
   const uint32_t mf = fmax_bits & 0x7FFFFF;
-  // stage 32 rows x 256 columns (16-byte loads; columns past C read as zero)
-  for (int i = t; i < 32 * 32; i += 256) {
-    const int rr = i / 32, cv = (i % 32) * 8;
-    bf16x8 val;
-    if (c0 + cv < C) {
-      val = *reinterpret_cast<const bf16x8*>(x + (int64_t)(r0 + rr) * ldx + c0 + cv);
-    } else {
-      float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      val = pack8(z);
+  {
+    // 128 rows x 16 vectors: all eight 16-byte loads of a thread in flight at once
+    uint4 raw[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
+      const int r = r0 + rr, c = c0 + cv;
+      raw[k] = (r < R && c < C) ? *reinterpret_cast<const uint4*>(x + (int64_t)r * ldx + c) : make_uint4(0, 0, 0, 0);
     }
-    *reinterpret_cast<bf16x8*>(&tile[rr][cv]) = val;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
+      if (LN) {
+        const int r = r0 + rr, c = c0 + cv;
+        float f[8];
+        unpack8(*reinterpret_cast<const bf16x8*>(&raw[k]), f);
+        if (r < R && c < C) {
+          const float mu = mean[r], rs = rstd[r];
+          const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+          const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+          const float4 b0 = *reinterpret_cast<const float4*>(beta + c);
+          const float4 b1 = *reinterpret_cast<const float4*>(beta + c + 4);
+          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+          for (int q = 0; q < 8; ++q) f[q] = (f[q] - mu) * rs * g[q] + b[q];
+        }
+        *reinterpret_cast<bf16x8*>(&tile[rr][cv]) = pack8(f);
+      } else {
+        *reinterpret_cast<uint4*>(&tile[rr][cv]) = raw[k];
+      }
+    }
   }
   __syncthreads();
   float v[32];
   uint32_t w[8];
   uint8_t sfb;
-  // row-wise: block (row t / 8, columns 32 * (t % 8) ..)
+  // row-wise: row t & 127, K-blocks 2 * (t >> 7) and 2 * (t >> 7) + 1
   {
-    const int rr = t / 8, cb = (t % 8) * 32;
-    if (c0 + cb < C) {
+    const int row = t & 127, half = t >> 7;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) unpack8(*reinterpret_cast<const bf16x8*>(&tile[rr][cb + 8 * q]), v + 8 * q);
+    for (int b = 0; b < 2; ++b) {
+      const int blk = 2 * half + b;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) unpack8(*reinterpret_cast<const bf16x8*>(&tile[row][blk * 32 + 8 * q]), v + 8 * q);
       mx_block(v, ef, mf, fmt, w, sfb);
-      uint4* dst = reinterpret_cast<uint4*>(rc + (int64_t)(r0 + rr) * C + c0 + cb);
+      uint4* dst = reinterpret_cast<uint4*>(rcode + row * 128 + blk * 32);
       dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
       dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      rsf[mx_sf_offset(r0 + rr, (c0 + cb) / 32, (C + 127) / 128)] = sfb;
+      sfr[(row & 31) * 16 + (row >> 5) * 4 + blk] = sfb;
     }
   }
-  // column-wise: column t of the tile = row (c0 + t) of the transposed output, K block r0 / 32
-  if (c0 + t < C) {
+  // column-wise: columns 2 (t & 63), 2 (t & 63) + 1, K-block (rows) t >> 6; 32-bit loads
+  {
+    const int cp = t & 63, blk = t >> 6;
+    float v1[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(tile[i][t]);
-    mx_block(v, ef, mf, fmt, w, sfb);
-    uint4* dst = reinterpret_cast<uint4*>(cc + (int64_t)(c0 + t) * R + r0);
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    csf[mx_sf_offset(c0 + t, r0 / 32, (R + 127) / 128)] = sfb;
+    for (int i = 0; i < 32; ++i) {
+      const __nv_bfloat162 pr = *reinterpret_cast<const __nv_bfloat162*>(&tile[blk * 32 + i][2 * cp]);
+      v[i] = __low2float(pr);
+      v1[i] = __high2float(pr);
+    }
+    if (colsum) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        s0 += v[i];
+        s1 += v1[i];
+      }
+      csum[blk * 128 + 2 * cp] = s0;
+      csum[blk * 128 + 2 * cp + 1] = s1;
+    }
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int col = 2 * cp + e;
+      mx_block(e ? v1 : v, ef, mf, fmt, w, sfb);
+      uint4* dst = reinterpret_cast<uint4*>(ccode + col * 128 + blk * 32);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      sfc[(col & 31) * 16 + (col >> 5) * 4 + blk] = sfb;
+    }
   }
+  __syncthreads();
+  // coalesced stores: 128 rows of 128 codes each way (8 threads x 16 bytes per row)
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = t + k * 256, row = i >> 3, seg = (i & 7) * 16;
+    if (r0 + row < R && c0 + seg < C)
+      *reinterpret_cast<uint4*>(rc + (int64_t)(r0 + row) * C + c0 + seg) =
+          *reinterpret_cast<const uint4*>(rcode + row * 128 + seg);
+    if (c0 + row < C && r0 + seg < R)
+      *reinterpret_cast<uint4*>(cc + (int64_t)(c0 + row) * R + r0 + seg) =
+          *reinterpret_cast<const uint4*>(ccode + row * 128 + seg);
+  }
+  if (t < 32) {
+    reinterpret_cast<uint4*>(rsf + ((int64_t)rt * ((C + 127) / 128) + ct) * 512)[t] =
+        reinterpret_cast<const uint4*>(sfr)[t];
+  } else if (t < 64) {
+    reinterpret_cast<uint4*>(csf + ((int64_t)ct * ((R + 127) / 128) + rt) * 512)[t - 32] =
+        reinterpret_cast<const uint4*>(sfc)[t - 32];
+  }
+  if (colsum && t < 128 && c0 + t < C)
+    atomicAdd(colsum + c0 + t, (csum[t] + csum[128 + t]) + (csum[256 + t] + csum[384 + t]));
 }
 
 static int q_grid(size_t n, int per) {
@@ -562,8 +645,33 @@ void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t f
 
 // x: bf16 [R, C] (R, C multiples of 32, 16-byte aligned rows) -> row codes [R, C] + rsf
 // (scales of [R, C]) and column codes [C, R] + csf (scales of [C, R]).
+// Launches mx_rc_tile_kernel over [R, C] (see there); ln_* non-null: LayerNorm on load.
+void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, double fmax, const float* ln_mean,
+                 const float* ln_rstd, const float* ln_gamma, const float* ln_beta, float* colsum, uint8_t* rc,
+                 uint8_t* rsf, uint8_t* cc, uint8_t* csf, cudaStream_t st) {
+  const float fm = (float)fmax;
+  uint32_t fbits;
+  std::memcpy(&fbits, &fm, 4);
+  dim3 grid((unsigned)((C + 127) / 128), (unsigned)((R + 127) / 128));
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));
+    attr = true;
+  }
+  if (ln_mean)
+    mx_rc_tile_kernel<true><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, ln_mean, ln_rstd,
+                                                   ln_gamma, ln_beta, colsum, rc, rsf, cc, csf);
+  else
+    mx_rc_tile_kernel<false><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, nullptr, nullptr,
+                                                    nullptr, nullptr, colsum, rc, rsf, cc, csf);
+  MT_LAUNCH_CHECK();
+}
+
+// colsum (optional fp32 [C]): += the column sums of x (the bias gradient of the layer
+// whose output gradient x is), in the same pass.
 void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, int64_t fmt,
-                    double fmax) {
+                    double fmax, const c10::optional<at::Tensor>& colsum) {
   MT_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "mx_quantize_rc: 2-D bf16 input");
   const int64_t R = x.size(0), C = x.size(1);
   MT_CHECK(R % 32 == 0 && C % 32 == 0, "mx_quantize_rc: R and C must be multiples of 32");
@@ -579,19 +687,14 @@ void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tens
   chk(rsf, (R + 127) / 128 * ((C + 127) / 128) * 512, "mx_quantize_rc: rsf size");
   chk(csf, (C + 127) / 128 * ((R + 127) / 128) * 512, "mx_quantize_rc: csf size");
   MT_CHECK((fmt == 0 || fmt == 1) && fmax > 0.0, "mx_quantize_rc: fmt 0 / 1, fmax > 0");
+  if (colsum.has_value())
+    MT_CHECK(colsum->scalar_type() == at::kFloat && colsum->is_contiguous() && colsum->numel() == C,
+             "mx_quantize_rc: colsum must be fp32 [C]");
   if (R == 0 || C == 0) return;
-  const float fm = (float)fmax;
-  uint32_t fbits;
-  std::memcpy(&fbits, &fm, 4);
-  // padding slots of the scale atoms hold 127 (a scale of 1)
-  C10_CUDA_CHECK(cudaMemsetAsync(rsf.data_ptr(), 127, (size_t)rsf.numel(), cur_stream()));
-  C10_CUDA_CHECK(cudaMemsetAsync(csf.data_ptr(), 127, (size_t)csf.numel(), cur_stream()));
-  dim3 grid((unsigned)((C + 255) / 256), (unsigned)(R / 32));
-  mx_quantize_rc_kernel<<<grid, 256, 0, cur_stream()>>>(
-      reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), (int)R, (int)C, (int)fmt, fbits,
-      reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),
-      reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()));
-  MT_LAUNCH_CHECK();
+  mx_rc_tiles(reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), R, C, fmt, fmax, nullptr, nullptr, nullptr,
+              nullptr, colsum.has_value() ? colsum->data_ptr<float>() : nullptr,
+              reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),
+              reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()), cur_stream());
 }
 
 void fp8_quantize_blocks(const at::Tensor& x, at::Tensor out, at::Tensor scales, int64_t block_size,

@@ -361,10 +361,11 @@ constexpr int P_EPI_BYTES = P_EPI_WARPS * 2 * P_EPI_BUF;
 // byte (r % 32) * 16 + (r / 32) * 4 + k.
 constexpr int P_SF_ATOM = 512;
 constexpr int P_SF_BYTES = 3 * P_SF_ATOM;
-// TMEM in the MXFP8 kernel: the scale factors need 12 of the 512 columns, so the
-// second accumulator starts one 32-column chunk early and overlaps the first one's
-// last chunk; each epilogue reads the shared chunk first and signals "ovl" before the
-// next tile's MMAs may start.  Scales occupy the last 32 columns (SFA 4, SFB 8).
+// TMEM in the MXFP8 kernel: the scale factors need 2 x 12 of the 512 columns (two
+// sets, used by alternate stages), so the second accumulator starts one 32-column
+// chunk early and overlaps the first one's last chunk; each epilogue reads the shared
+// chunk first and signals "ovl" before the next tile's MMAs may start.  Scales occupy
+// the last 32 columns: set s at 480 + 16 s (SFA 4 columns, SFB 8).
 constexpr int MX_ACC1_COL = P_BN - 32;
 constexpr int MX_SF_COL = 2 * P_BN - 32;
 
@@ -664,13 +665,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
           const uint32_t sb = sa + P_A_BYTES;
+          // MXFP8 scales of consecutive stages alternate between two TMEM column sets, so a
+          // stage's copy never overwrites scales the previous stage's MMAs may still read
+          const uint32_t sf_tmem = tmem_base + MX_SF_COL + (uint32_t)(stage & 1) * 16;
           if constexpr (MX) {
             // stage scales -> TMEM (in order with the MMAs of this thread, so the previous
             // stage's MMAs have read the old scales before these land)
             const uint32_t ssf = smem_u32(sf_smem + stage * P_SF_BYTES);
-            tmem_cp_32x128b_x4_2sm(tmem_base + MX_SF_COL, make_sdesc(ssf, 0, 128, kSwizzleNone));
-            tmem_cp_32x128b_x4_2sm(tmem_base + MX_SF_COL + 4, make_sdesc(ssf + P_SF_ATOM, 0, 128, kSwizzleNone));
-            tmem_cp_32x128b_x4_2sm(tmem_base + MX_SF_COL + 8, make_sdesc(ssf + 2 * P_SF_ATOM, 0, 128, kSwizzleNone));
+            tmem_cp_32x128b_x4_2sm(sf_tmem, make_sdesc(ssf, 0, 128, kSwizzleNone));
+            tmem_cp_32x128b_x4_2sm(sf_tmem + 4, make_sdesc(ssf + P_SF_ATOM, 0, 128, kSwizzleNone));
+            tmem_cp_32x128b_x4_2sm(sf_tmem + 8, make_sdesc(ssf + 2 * P_SF_ATOM, 0, 128, kSwizzleNone));
           }
 #pragma unroll
           for (int k = 0; k < BK / MMA_K; ++k) {
@@ -680,8 +684,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                      : make_sdesc(sb + k * 32, 16, 1024, kSwizzle128B);
             if constexpr (MX)
               umma_mx_2sm(d_tmem, ad, bd, idesc_mx_sf_id(idesc, (uint32_t)k),
-                          (tmem_base + MX_SF_COL) | ((uint32_t)k << 30),
-                          (tmem_base + MX_SF_COL + 4) | ((uint32_t)k << 30), (kb | k) != 0 ? 1u : 0u);
+                          sf_tmem | ((uint32_t)k << 30), (sf_tmem + 4) | ((uint32_t)k << 30), (kb | k) != 0 ? 1u : 0u);
             else if constexpr (EB == 2)
               umma_f16_2sm(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
             else

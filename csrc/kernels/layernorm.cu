@@ -523,112 +523,53 @@ std::vector<at::Tensor> layernorm_fwd_fp8(const at::Tensor& x, const at::Tensor&
   return {mean, rstd};
 }
 
-// LayerNorm whose output goes straight to MXFP8, row-wise and column-wise (the
-// operands of the forward GEMM and of the wgrad GEMM under the MX recipe); the bf16
-// output itself is never written.  A CTA owns 32 rows: each of its 8 warps
-// normalises 4 rows (statistics as in ln_fwd_vec: the row in registers, sum then
-// centred sum of squares, fp32) into a bf16 tile of 32 x d in shared memory; the
-// tile is then quantised in 32-element blocks along its rows (row codes [R, d]) and
-// down its columns (column codes [d, R], the transpose), with the mx_block rule.
-// mean / rstd go to global memory for the backward.
-template <int NCH>
-__global__ void __launch_bounds__(256) ln_fwd_mx_rc_kernel(const bf16* __restrict__ x, const float* __restrict__ gamma,
-                                                           const float* __restrict__ beta, float* __restrict__ mean_out,
-                                                           float* __restrict__ rstd_out, int R, int d, float eps,
-                                                           int fmt, uint32_t fmax_bits, uint8_t* __restrict__ rc,
-                                                           uint8_t* __restrict__ rsf, uint8_t* __restrict__ cc,
-                                                           uint8_t* __restrict__ csf) {
-  extern __shared__ __align__(16) uint8_t ln_mx_smem[];
-  bf16* tile = reinterpret_cast<bf16*>(ln_mx_smem);
-  const int ld = d + 8;  // padded row (bf16 elements), 16-byte multiple
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int r0 = blockIdx.x * 32;
-  for (int rr = warp; rr < 32; rr += 8) {
-    const bf16* xr = x + (int64_t)(r0 + rr) * d;
-    float v[NCH][8];
-    float s = 0.f;
+// LayerNorm straight to MXFP8, row-wise and column-wise (the operands of the
+// forward GEMM and of the wgrad GEMM under the MX recipe); the bf16 output itself
+// is never written.  Two launches: ln_row_stats (one warp per row: sum, then the
+// centred sum of squares, fp32, over a second, cache-resident read of the row)
+// writes mean / rstd, which the backward needs anyway; then the 128 x 128 tile
+// quantiser (mx_rc_tile_kernel in fp8.cu) normalises each tile on load and
+// quantises it along its rows and down its columns.
+__global__ void __launch_bounds__(256) ln_row_stats_kernel(const bf16* __restrict__ x, float* __restrict__ mean_out,
+                                                           float* __restrict__ rstd_out, int R, int d, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= R) return;
+  const bf16* row = x + (int64_t)warp * d;
+  float s = 0.f;
+  for (int c = lane * 8; c < d; c += 256) {
+    float f[8];
+    unpack8(*reinterpret_cast<const bf16x8*>(row + c), f);
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      const int col = c * 256 + lane * 8;
-      if (col < d) {
-        unpack8(*reinterpret_cast<const bf16x8*>(xr + col), v[c]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[c][i] = 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) s += v[c][i];
-    }
-    const float mean = warp_sum(s) / d;
-    float q = 0.f;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      if (c * 256 + lane * 8 < d) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float t = v[c][i] - mean;
-          q += t * t;
-        }
-      }
-    }
-    const float rstd = rsqrtf(warp_sum(q) / d + eps);
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      const int col = c * 256 + lane * 8;
-      if (col < d) {
-        const float4 g0 = *reinterpret_cast<const float4*>(gamma + col);
-        const float4 g1 = *reinterpret_cast<const float4*>(gamma + col + 4);
-        const float4 b0 = *reinterpret_cast<const float4*>(beta + col);
-        const float4 b1 = *reinterpret_cast<const float4*>(beta + col + 4);
-        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-        float o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = (v[c][i] - mean) * rstd * g[i] + b[i];
-        *reinterpret_cast<bf16x8*>(tile + rr * ld + col) = pack8(o);
-      }
-    }
-    if (lane == 0) {
-      mean_out[r0 + rr] = mean;
-      rstd_out[r0 + rr] = rstd;
-    }
+    for (int k = 0; k < 8; ++k) s += f[k];
   }
-  __syncthreads();
-  const int ef = (int)((fmax_bits >> 23) & 0xFF);
-  const uint32_t mf = fmax_bits & 0x7FFFFF;
-  const int kb = d / 32;
-  float v[32];
-  uint32_t w[8];
-  uint8_t sfb;
-  for (int idx = threadIdx.x; idx < 32 * kb; idx += 256) {  // row-wise blocks
-    const int rr = idx / kb, j = idx % kb;
+  s = warp_sum(s);
+  const float mu = s / (float)d;
+  float q = 0.f;
+  for (int c = lane * 8; c < d; c += 256) {
+    float f[8];
+    unpack8(*reinterpret_cast<const bf16x8*>(row + c), f);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) unpack8(*reinterpret_cast<const bf16x8*>(tile + rr * ld + j * 32 + 8 * q), v + 8 * q);
-    mx_block(v, ef, mf, fmt, w, sfb);
-    uint4* dst = reinterpret_cast<uint4*>(rc + (int64_t)(r0 + rr) * d + j * 32);
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    rsf[mx_sf_offset(r0 + rr, j, (d + 127) / 128)] = sfb;
+    for (int k = 0; k < 8; ++k) q += (f[k] - mu) * (f[k] - mu);
   }
-  for (int col = threadIdx.x; col < d; col += 256) {  // column-wise: 32 rows of one column
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(tile[i * ld + col]);
-    mx_block(v, ef, mf, fmt, w, sfb);
-    uint4* dst = reinterpret_cast<uint4*>(cc + (int64_t)col * R + r0);
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    csf[mx_sf_offset(col, r0 / 32, (R + 127) / 128)] = sfb;
+  q = warp_sum(q);
+  if (lane == 0) {
+    mean_out[warp] = mu;
+    rstd_out[warp] = rsqrtf(q / (float)d + eps);
   }
 }
 
 // x bf16 [R, d] contiguous (R % 32 == 0, d % 256 == 0, d <= 2048) -> row codes rc [R, d] +
 // rsf, column codes cc [d, R] + csf (scale atoms as mx_quantize_rc), mean / rstd [R].
+void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, double fmax, const float* ln_mean,
+                 const float* ln_rstd, const float* ln_gamma, const float* ln_beta, float* colsum, uint8_t* rc,
+                 uint8_t* rsf, uint8_t* cc, uint8_t* csf, cudaStream_t st);
+
 void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at::Tensor& beta, double eps,
                          at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, at::Tensor mean,
                          at::Tensor rstd, int64_t fmt, double fmax) {
   MT_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous(), "ln_mx: contiguous bf16 [R, d]");
   const int64_t R = x.size(0), d = x.size(1);
-  MT_CHECK(R % 32 == 0 && d % 256 == 0 && d <= 2048, "ln_mx: R % 32 == 0, d a multiple of 256 up to 2048");
+  MT_CHECK(R % 32 == 0 && d % 32 == 0, "ln_mx: R and d multiples of 32");
   MT_CHECK(gamma.scalar_type() == at::kFloat && beta.scalar_type() == at::kFloat && gamma.numel() == d &&
                beta.numel() == d && reinterpret_cast<uintptr_t>(gamma.data_ptr()) % 16 == 0 &&
                reinterpret_cast<uintptr_t>(beta.data_ptr()) % 16 == 0 &&
@@ -648,40 +589,15 @@ void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at:
            "ln_mx: fp32 mean / rstd [R]");
   MT_CHECK((fmt == 0 || fmt == 1) && fmax > 0.0, "ln_mx: fmt 0 / 1, fmax > 0");
   if (R == 0) return;
-  const float fm = (float)fmax;
-  uint32_t fbits;
-  std::memcpy(&fbits, &fm, 4);
   auto st = cur_stream();
-  C10_CUDA_CHECK(cudaMemsetAsync(rsf.data_ptr(), 127, (size_t)rsf.numel(), st));
-  C10_CUDA_CHECK(cudaMemsetAsync(csf.data_ptr(), 127, (size_t)csf.numel(), st));
-  const size_t smem = (size_t)32 * (d + 8) * sizeof(bf16);
-  const int nch = (int)(d / 256);
-#define LNMX(N)                                                                                               \
-  do {                                                                                                        \
-    static bool attr = false;                                                                                 \
-    if (!attr) {                                                                                              \
-      C10_CUDA_CHECK(cudaFuncSetAttribute(ln_fwd_mx_rc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                          32 * (2048 + 8) * (int)sizeof(bf16)));                             \
-      attr = true;                                                                                            \
-    }                                                                                                         \
-    ln_fwd_mx_rc_kernel<N><<<(unsigned)(R / 32), 256, smem, st>>>(                                            \
-        reinterpret_cast<const bf16*>(x.data_ptr()), gamma.data_ptr<float>(), beta.data_ptr<float>(),         \
-        mean.data_ptr<float>(), rstd.data_ptr<float>(), (int)R, (int)d, (float)eps, (int)fmt, fbits,          \
-        reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),               \
-        reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()));              \
-  } while (0)
-  switch (nch) {
-    case 1: LNMX(1); break;
-    case 2: LNMX(2); break;
-    case 4: LNMX(4); break;
-    case 8: LNMX(8); break;
-    default:
-      // 3, 5, 6, 7 chunks: round up to the next instantiation (extra chunks are skipped by col < d)
-      if (nch < 4) LNMX(4);
-      else LNMX(8);
-  }
-#undef LNMX
+  ln_row_stats_kernel<<<(unsigned)((R + 7) / 8), 256, 0, st>>>(reinterpret_cast<const bf16*>(x.data_ptr()),
+                                                               mean.data_ptr<float>(), rstd.data_ptr<float>(),
+                                                               (int)R, (int)d, (float)eps);
   MT_LAUNCH_CHECK();
+  mx_rc_tiles(reinterpret_cast<const bf16*>(x.data_ptr()), d, R, d, fmt, fmax, mean.data_ptr<float>(),
+              rstd.data_ptr<float>(), gamma.data_ptr<float>(), beta.data_ptr<float>(), nullptr,
+              reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),
+              reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()), st);
 }
 
 std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gamma,

@@ -253,14 +253,12 @@ class AttnBlockFn(Function):
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
         hc, oc = _mx_t(hcc, hcs, MX.E4M3), _mx_t(occ, ocs, MX.E4M3)
-        grow, gcol = MX.mx_quantize_rc(dout, MX.E5M2)
-        K.colsum_(dout, bo.main_grad, acc)
+        grow, gcol = MX.mx_quantize_rc(dout, MX.E5M2, colsum=bo.main_grad, accumulate=acc)
         do = MX.gemm_mxfp8(grow, wo.mx[1])  # dgrad: dY (row) x W (column-wise)
         MX.gemm_mxfp8(gcol, oc, out=wo.main_grad, accumulate=acc)  # wgrad: dY^T x O, both column-wise
         _grads_done(wo, bo)
         dqkv = attention_bwd(do, qkv, o_bf16, lse, *ctx.shape)
-        qrow, qcol = MX.mx_quantize_rc(dqkv, MX.E5M2)
-        K.colsum_(dqkv, bq.main_grad, acc)
+        qrow, qcol = MX.mx_quantize_rc(dqkv, MX.E5M2, colsum=bq.main_grad, accumulate=acc)
         MX.gemm_mxfp8(qcol, hc, out=wq.main_grad, accumulate=acc)
         dh = MX.gemm_mxfp8(qrow, wq.mx[1])
         _grads_done(wq, bq)
@@ -361,13 +359,11 @@ class MLPBlockFn(Function):
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
         hc, ac = _mx_t(hcc, hcs, MX.E4M3), _mx_t(acc_codes, acs, MX.E4M3)
-        grow, gcol = MX.mx_quantize_rc(dout, MX.E5M2)
-        K.colsum_(dout, b2.main_grad, acc)
+        grow, gcol = MX.mx_quantize_rc(dout, MX.E5M2, colsum=b2.main_grad, accumulate=acc)
         dpre = MX.gemm_mxfp8(grow, w2.mx[1], aux=pre)  # dgrad with dGELU in the epilogue
         MX.gemm_mxfp8(gcol, ac, out=w2.main_grad, accumulate=acc)
         _grads_done(w2, b2)
-        prow, pcol = MX.mx_quantize_rc(dpre, MX.E5M2)
-        K.colsum_(dpre, b1.main_grad, acc)
+        prow, pcol = MX.mx_quantize_rc(dpre, MX.E5M2, colsum=b1.main_grad, accumulate=acc)
         MX.gemm_mxfp8(pcol, hc, out=w1.main_grad, accumulate=acc)
         dh = MX.gemm_mxfp8(prow, w1.mx[1])
         _grads_done(w1, b1)

@@ -143,13 +143,24 @@ def gemm_mxfp8(a: MxTensor, b: MxTensor, out: Optional[torch.Tensor] = None, *, 
     return out
 
 
-def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = None):
+def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = None,
+                   colsum: Optional[torch.Tensor] = None, accumulate: bool = True):
     """Row-wise MXFP8 of x [R, C] (32-blocks along C) and of its transpose [C, R]
     (32-blocks along R), in one pass on the GPU: the operands that contract over C
-    and over R.  R and C multiples of 32.  The reference on the CPU."""
+    and over R.  R and C multiples of 32.  The reference on the CPU.
+
+    colsum (fp32 [C], optional): receives the column sums of x in the same pass (the
+    bias gradient when x is a layer's output gradient), added to its contents when
+    ``accumulate``, else overwriting them."""
     if x.dim() != 2 or x.shape[0] % BLOCK or x.shape[1] % BLOCK:
         raise ValueError("mx_quantize_rc: 2-D input with both sizes multiples of 32 expected")
     if not x.is_cuda:
+        if colsum is not None:
+            cs = x.float().sum(0)
+            if accumulate:
+                colsum += cs
+            else:
+                colsum.copy_(cs)
         return mx_quantize_ref(x, fmt, fmax), mx_quantize_ref(x.t(), fmt, fmax)
     fmax = float(MX_FMT_MAX[fmt] if fmax is None else fmax)
     x = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
@@ -160,18 +171,21 @@ def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = Non
     cc = torch.empty((C, R), dtype=torch.uint8, device=x.device)
     rsf = torch.empty(sf_numel(R, C), dtype=torch.uint8, device=x.device)
     csf = torch.empty(sf_numel(C, R), dtype=torch.uint8, device=x.device)
-    _cuda().mx_quantize_rc(x, rc, rsf, cc, csf, int(fmt), fmax)
+    if colsum is not None and not accumulate:
+        colsum.zero_()
+    _cuda().mx_quantize_rc(x, rc, rsf, cc, csf, int(fmt), fmax, colsum)
     return MxTensor(rc, rsf, int(fmt)), MxTensor(cc, csf, int(fmt))
 
 
 def mx_layernorm_rc(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
                     fmt: int = E4M3, fmax: Optional[float] = None):
     """LayerNorm of x [R, d] straight into MXFP8, row-wise ([R, d]) and column-wise
-    ([d, R]), plus the fp32 mean / rstd rows for the backward: one kernel, no bf16
-    output (CUDA, R % 32 == 0, d a multiple of 256 up to 2048).  Elsewhere: LayerNorm,
-    rounded to bf16, then ``mx_quantize_rc``."""
+    ([d, R]), plus the fp32 mean / rstd rows for the backward; no bf16 output (CUDA,
+    R and d multiples of 32: a row-statistics kernel, then the tile quantiser with
+    the normalisation applied on load).  Elsewhere: LayerNorm, rounded to bf16, then
+    ``mx_quantize_rc``."""
     R, d = x.shape
-    if x.is_cuda and x.dtype == torch.bfloat16 and R % 32 == 0 and d % 256 == 0 and d <= 2048:
+    if x.is_cuda and x.dtype == torch.bfloat16 and R % 32 == 0 and d % 32 == 0:
         fmax = float(MX_FMT_MAX[fmt] if fmax is None else fmax)
         x = x.contiguous()
         dev = x.device

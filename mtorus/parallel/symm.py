@@ -225,10 +225,21 @@ class ZeroAdam:
 
         return self.state[ST_SCALE:ST_SCALE + 1]
 
-    def step(self, lr: Optional[float] = None) -> None:
+    def finalize(self) -> None:
+        """Overflow / loss-scale / clip decision from the norm partials the reduce
+        kernels summed over the data-parallel ranks (a pipeline sums them over its
+        stages first)."""
         from ..ops import kernels as K
 
         K.optim_finalize(self.state, self.ls.dynamic, self.ls.growth_interval, self.max_grad_norm, True)
+
+    def step(self, lr: Optional[float] = None) -> None:
+        self.finalize()
+        self.update(lr)
+
+    def update(self, lr: Optional[float] = None) -> None:
+        """Adam on this rank's shard; the new bf16 weights go into every peer's weight
+        buffer, then a flag barrier orders them before any rank's next forward."""
         r = self.reducer
         _cuda().symm_adam_shard_ag(r.ranges, self.flat.master, self.m, self.v, self.flat.grad,
                                    self.flat.symm_w16.ptrs, self.state, self.lr if lr is None else lr,

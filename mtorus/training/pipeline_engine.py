@@ -19,8 +19,13 @@ bf16 / fp32-grad buffers and runs:
    crates/mt-pipeline/src/checkpoint.rs;
 3. gradient accumulation over the micro-batches straight into ``main_grad``
    (the first backward overwrites, the rest add, in the wgrad GEMM epilogues);
-4. during the last micro-batch's backward, the data-parallel bucket all-reduce
-   over the ranks that hold the same stage, overlapped with that backward;
+4. during the last micro-batch's backward, the data-parallel gradient reduction
+   over the ranks that hold the same stage, overlapped with that backward: NCCL
+   bucket all-reduces (``dp="nccl"``) or the fused NVLink path (``dp="symm"``:
+   per-bucket reduce-scatter kernels over symmetric memory with the norm /
+   overflow partials fused, then the sharded Adam that stores the new weights
+   into every peer, and the delayed-scaling amax all-reduce fused into the FP8
+   quantise kernels);
 5. the fused device optimizer, with the gradient-norm / overflow statistics
    summed over the pipeline so that every stage takes the same skip / clip /
    loss-scale decision (reference crates/mt-training/src/step.rs:114-180).
@@ -113,7 +118,7 @@ class PipelineTrainer:
                  fp8_history: int = 16, lr: float = 3e-4, device=None, seed: int = 0,
                  bucket_mb: float = 25.0, loss_scale: Optional[DeviceLossScaleConfig] = None,
                  max_grad_norm: float = 0.0, timed: bool = False, split: str = "balanced",
-                 fp8_recipe: str = "tensor"):
+                 fp8_recipe: str = "tensor", dp_mode: str = "nccl", wire: str = "native"):
         from .engine import require_no_dropout
 
         require_no_dropout(config)
@@ -158,21 +163,35 @@ class PipelineTrainer:
         g = torch.Generator(device=self.device)
         g.manual_seed(seed * 1000 + self.stage)
         self.model.init_normal_(0.02, generator=g)
-        self.flat = self.model.flatten(self.device)
+        if dp_mode not in ("nccl", "symm"):
+            raise ValueError(f"dp_mode must be 'nccl' or 'symm', not {dp_mode!r}")
+        self.dp_mode = dp_mode if dp > 1 else "none"
+        symm = self.dp_mode == "symm"
+        self.flat = self.model.flatten(self.device, symmetric=symm, group=self.dp_group if symm else None)
         self.fp8 = fp8
         if fp8:
             st = self.model.enable_fp8(fp8_history, recipe=fp8_recipe)
-            if dp > 1:
+            if symm:
+                from ..ops.fp8 import SymmAmaxSync
+
+                st.set_amax_sync(SymmAmaxSync(self.device, st.cap, self.dp_group))
+            elif dp > 1:
                 from ..ops.fp8 import NcclAmaxSync
 
                 st.set_amax_sync(NcclAmaxSync(self.dp_group))
-        self.opt = FusedAdam(self.flat, lr=lr, max_grad_norm=max_grad_norm,
-                             loss_scale=loss_scale or DeviceLossScaleConfig())
+        ls = loss_scale or DeviceLossScaleConfig()
         self.reducer = None
-        if dp > 1:
-            from ..parallel.data_parallel import NcclBucketReducer
+        if symm:
+            from ..parallel.symm import SymmBucketReducer, ZeroAdam
 
-            self.reducer = NcclBucketReducer(self.flat, self.dp_group, int(bucket_mb * 1024 * 1024))
+            self.reducer = SymmBucketReducer(self.flat, self.dp_group, int(bucket_mb * 1024 * 1024))
+            self.opt = ZeroAdam(self.flat, self.reducer, lr=lr, max_grad_norm=max_grad_norm, loss_scale=ls)
+        else:
+            self.opt = FusedAdam(self.flat, lr=lr, max_grad_norm=max_grad_norm, loss_scale=ls)
+            if dp > 1:
+                from ..parallel.data_parallel import NcclBucketReducer
+
+                self.reducer = NcclBucketReducer(self.flat, self.dp_group, int(bucket_mb * 1024 * 1024))
         b, S = self.b, self.S
 
         def stage_fn(x):
@@ -186,7 +205,7 @@ class PipelineTrainer:
             loss_fn=loss_fn, act_shape=(b * S, config.d_model), act_dtype=torch.bfloat16, device=self.device,
             group=self.pipe_group, grad_group=self.grad_group, stage_fn=stage_fn,
             pre_backward=self._pre_backward, sync_losses=False, timed=timed,
-            stage_segments=self.model.fused_stage_segments(b, S))
+            stage_segments=self.model.fused_stage_segments(b, S), wire=wire)
         self.schedule = schedule
         self.global_step = 0
         self._loss_host = torch.empty((), dtype=torch.float32).pin_memory()
@@ -301,7 +320,7 @@ class PipelineTrainer:
         torch.cuda.synchronize(dev)
         # NCCL also connects collective rings / trees on their first use: do that now,
         # at the sizes the step uses, for the data-parallel and the pipeline group
-        if self.reducer is not None:
+        if self.reducer is not None and self.dp_mode == "nccl":
             s0, e0 = self.reducer.plan.ranges[0]
             tmp = torch.zeros(max(e - s for s, e in self.reducer.plan.ranges), device=dev)
             dist.all_reduce(tmp, group=self.dp_group)
@@ -319,6 +338,8 @@ class PipelineTrainer:
             self.warm_kernels()
         if self.fp8:
             self.model.refresh_fp8_weights()
+        if hasattr(self.reducer, "begin_step"):
+            self.reducer.begin_step()
         loss = self.executor.run(ids if self.is_first else None, targets if self.is_last else None)
         FusedGradState.grad_ready_hook = None
         FusedGradState.accumulate = False
@@ -328,7 +349,8 @@ class PipelineTrainer:
 
     def optimizer_step(self) -> None:
         """Pipeline-wide norm / overflow, then the fused Adam update and the FP8 scale roll."""
-        self.opt.accumulate_norm()
+        if self.dp_mode != "symm":  # the symmetric reduce kernels already summed this stage's norm partials
+            self.opt.accumulate_norm()
         if self.pp > 1:
             # sum of squares and the non-finite count over the whole model
             dist.all_reduce(self.opt.state[ST_SUMSQ:ST_NONFINITE + 1], group=self.pipe_group)

@@ -176,10 +176,14 @@ def test_block_scaled_gemm_agrees_with_cublas_mx():
 def test_cuda_row_col_quantiser_matches_reference(shape):
     R, C = shape
     x = _blocky(R, C, seed=R).to(torch.bfloat16)
-    r, c = mx_quantize_rc(x.cuda(), E4M3)
+    cs = torch.full((C,), 5.0, device="cuda")
+    r, c = mx_quantize_rc(x.cuda(), E4M3, colsum=cs, accumulate=True)
     rr, cr = mx_quantize_ref(x.float(), E4M3), mx_quantize_ref(x.float().t().contiguous(), E4M3)
     assert torch.equal(r.codes.cpu(), rr.codes) and torch.equal(r.sf.cpu(), rr.sf)
     assert torch.equal(c.codes.cpu(), cr.codes) and torch.equal(c.sf.cpu(), cr.sf)
+    # the bias-gradient column sums of the same pass (fp32, added to the buffer)
+    want = x.double().sum(0) + 5.0
+    assert torch.allclose(cs.cpu().double(), want, rtol=1e-5, atol=1e-5 * float(x.double().abs().sum(0).max()))
 
 
 @pytest.mark.gpu
