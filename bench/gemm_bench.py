@@ -18,6 +18,27 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from mtorus.ops import kernels as K  # noqa: E402
 
 
+STALLS = False
+
+
+def stalls(fn, n=5):
+    """Shares of the MMA issuer's time spent waiting for operands / for a free accumulator,
+    and of the producer's time waiting for a free stage (gemm_profile counters)."""
+    from mtorus._ext import cuda
+
+    torch.cuda.synchronize()
+    cuda().gemm_profile(True)
+    for _ in range(n):
+        fn()
+    torch.cuda.synchronize()
+    p = cuda().gemm_profile_read()
+    cuda().gemm_profile(False)
+    if p[4] == 0:
+        return None
+    return {"mma_wait_operands": round(p[2] / p[4], 3), "mma_wait_accumulator": round(p[3] / p[4], 3),
+            "producer_wait_free_stage": round(p[0] / max(1, p[1]), 3)}
+
+
 def timeit(fn, iters=20, warmup=5):
     for _ in range(warmup):
         fn()
@@ -39,7 +60,12 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--json", default=None)
     ap.add_argument("--case", default=None, help="run only the named case (e.g. ffn1_fwd_fp8)")
+    ap.add_argument("--stalls", action="store_true",
+                    help="also report, per case, where the CTA-pair kernel's MMA issuer waited (for loaded "
+                         "operand stages vs for the epilogue to free an accumulator) over 5 extra launches")
     args = ap.parse_args()
+    global STALLS
+    STALLS = args.stalls
     peak = 1607.9
     p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -109,6 +135,8 @@ def main():
              "cublas_ms": round(tr, 4), "mine_tflops": round(flops / tm / 1e9, 1),
              "cublas_tflops": round(flops / tr / 1e9, 1) if tr == tr else None,
              "mine_frac_of_2x_measured_bf16_peak": round(flops / tm / 1e9 / (2 * peak), 3)}
+        if STALLS:
+            r["stalls"] = stalls(mine)
         rows.append(r)
         print(json.dumps(r), flush=True)
         del A, B
@@ -141,6 +169,8 @@ def main():
              "cublas_ms": round(tr, 4) if tr == tr else None, "mine_tflops": round(flops / tm / 1e9, 1),
              "cublas_tflops": round(flops / tr / 1e9, 1) if tr == tr else None,
              "mine_frac_of_2x_measured_bf16_peak": round(flops / tm / 1e9 / (2 * peak), 3)}
+        if STALLS:
+            r["stalls"] = stalls(mine)
         rows.append(r)
         print(json.dumps(r), flush=True)
         del a, b, out
@@ -165,6 +195,8 @@ def main():
         r = {"case": name, "M": M, "N": N, "K": Kd, "layout": lay, "mine_ms": round(tm, 4),
              "cublas_ms": round(tr, 4), "mine_tflops": round(flops / tm / 1e9, 1),
              "cublas_tflops": round(flops / tr / 1e9, 1), "mine_frac_of_measured_peak": round(flops / tm / 1e9 / peak, 3)}
+        if STALLS:
+            r["stalls"] = stalls(mine)
         rows.append(r)
         print(json.dumps(r), flush=True)
         del A, B

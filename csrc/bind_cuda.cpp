@@ -124,6 +124,8 @@ void symm_broadcast(const std::vector<int64_t>& bufs, int64_t root, int64_t byte
 void symm_allreduce_mc(int64_t mc, const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags,
                        int64_t me, int64_t numel, int64_t dtype, int64_t slot, int64_t epoch, int64_t ctas);
 void symm_broadcast_mc(int64_t src, int64_t mc, int64_t bytes, int64_t ctas);
+void gemm_profile(bool on);
+std::vector<int64_t> gemm_profile_read();
 void fp8_wire_encode(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt);
 void fp8_wire_decode(const at::Tensor& codes, const at::Tensor& sf, at::Tensor out, int64_t fmt);
 void symm_pull_msgs(const std::vector<int64_t>& src, int64_t src_off, int64_t dst, int64_t slot_bytes,
@@ -188,6 +190,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_halo", &symm_halo);
   m.def("symm_pull_msgs", &symm_pull_msgs);
   m.def("fp8_wire_encode", &fp8_wire_encode);
+  m.def("gemm_profile", &gemm_profile);
+  m.def("gemm_profile_read", &gemm_profile_read);
   m.def("fp8_wire_decode", &fp8_wire_decode);
   m.def("symm_allreduce_msgs", &symm_allreduce_msgs);
   m.def("symm_flag", &symm_flag);

@@ -335,7 +335,16 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(const bf16* __restrict
 // stream).  colsum (optional): colsum[c] += sum over r of the tile's values (one
 // atomic per column per CTA).
 constexpr int kRcTileStride = 128 + 8;  // bf16 elements per staged row (16-byte rows, bank spread)
-constexpr int kRcSmem = 128 * kRcTileStride * 2 + 2 * 128 * 128 + 2 * 512 + 2 * 4 * 128;
+// dynamic shared memory: bf16 tile | row codes | column codes | two scale atoms | fp32 column sums [4][128]
+constexpr int kRcOffRcode = 128 * kRcTileStride * 2;
+constexpr int kRcOffCcode = kRcOffRcode + 128 * 128;
+constexpr int kRcOffSfr = kRcOffCcode + 128 * 128;
+constexpr int kRcOffSfc = kRcOffSfr + 512;
+constexpr int kRcOffCsum = kRcOffSfc + 512;
+constexpr int kRcSmem = kRcOffCsum + 4 * 128 * (int)sizeof(float);
+static_assert(kRcOffRcode % 16 == 0 && kRcOffCcode % 16 == 0 && kRcOffSfr % 16 == 0 && kRcOffSfc % 16 == 0 &&
+                  kRcOffCsum % 16 == 0,
+              "mx_rc_tile_kernel: 16-byte aligned shared-memory regions");
 
 template <bool LN>
 __global__ void __launch_bounds__(256, 3) mx_rc_tile_kernel(const bf16* __restrict__ x, int64_t ldx, int R, int C, int fmt,
@@ -347,11 +356,11 @@ __global__ void __launch_bounds__(256, 3) mx_rc_tile_kernel(const bf16* __restri
                                                          uint8_t* __restrict__ cc, uint8_t* __restrict__ csf) {
   extern __shared__ __align__(16) uint8_t rc_smem[];
   bf16 (*tile)[kRcTileStride] = reinterpret_cast<bf16 (*)[kRcTileStride]>(rc_smem);
-  uint8_t* rcode = rc_smem + 128 * kRcTileStride * 2;  // [128 rows][128 codes]
-  uint8_t* ccode = rcode + 128 * 128;                  // [128 columns][128 codes]
-  uint8_t* sfr = ccode + 128 * 128;
-  uint8_t* sfc = sfr + 512;
-  float* csum = reinterpret_cast<float*>(sfc + 512);  // [4][128]
+  uint8_t* rcode = rc_smem + kRcOffRcode;  // [128 rows][128 codes]
+  uint8_t* ccode = rc_smem + kRcOffCcode;  // [128 columns][128 codes]
+  uint8_t* sfr = rc_smem + kRcOffSfr;
+  uint8_t* sfc = rc_smem + kRcOffSfc;
+  float* csum = reinterpret_cast<float*>(rc_smem + kRcOffCsum);  // [4][128]
   const int rt = blockIdx.y, ct = blockIdx.x, t = threadIdx.x;
   const int r0 = rt * 128, c0 = ct * 128;
   const int ef = (int)((fmax_bits >> 23) & 0xFF);

@@ -388,6 +388,7 @@ struct PairSmem {
   uint64_t tfull[2];         // each CTA: accumulator buffer ready for the epilogue
   uint64_t tempty[2];        // leader: both epilogues finished with a buffer
   uint64_t ovl;              // leader (MXFP8): both epilogues read the chunk shared by the two accumulators
+  long long prof[3];         // stall accounting (GemmEpilogue::prof): empty, full, tempty waits
   uint32_t tmem_base;
   int abort;
 };
@@ -545,7 +546,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     const __grid_constant__ CUtensorMap tma_sfa,
                     const __grid_constant__ CUtensorMap tma_sfb,
                     const __grid_constant__ PeerMapsB peer_b, int M, int N, int K, int a_mn,
-                    int b_mn, int sf_kb, uint32_t idesc, GemmEpilogue ep, int* status) {
+                    int b_mn, int sf_kb, uint32_t idesc, GemmEpilogue ep, int* status,
+                    unsigned long long* prof) {
+  // prof (optional, gemm_profile): stall accounting summed over CTAs: cycles the
+  // producer waited for free stages [0] and ran [1], the MMA issuer waited for
+  // loaded stages [2] / free accumulators [3] and ran [4]; CTA pairs [7].
   static_assert(!MX || EB == 1, "block scaling is for fp8 operands");
   constexpr int BK = 128 / EB;       // K elements per stage
   constexpr int MMA_K = 32 / EB;     // K elements per tcgen05.mma
@@ -578,6 +583,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       mbar_init(&ctl->tempty[b], 2 * 32 * P_EPI_WARPS);
     }
     if constexpr (MX) mbar_init(&ctl->ovl, 2 * 128);
+    for (int i = 0; i < 3; ++i) ctl->prof[i] = 0;
     ctl->abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
@@ -592,10 +598,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int* abort = &ctl->abort;
-
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------- producer (both CTAs)
+      const long long prof_t0 = prof ? clock64() : 0;
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
@@ -604,7 +610,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const int m0 = mb * 2 * P_BM + (int)rank * P_BM;
         const int n0 = nb * P_BN + (int)rank * (P_BN / 2);
         for (int kb = 0; kb < num_kb; ++kb) {
+          const long long pw0 = prof ? clock64() : 0;
           if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort, status, 11)) break;
+          if (prof) ctl->prof[0] += clock64() - pw0;
           if (leader) mbar_arrive_expect_tx(&ctl->full[stage], 2 * (P_STAGE_BYTES + (MX ? P_SF_BYTES : 0)));
           uint8_t* sa = smem + stage * P_STAGE_BYTES;
           uint8_t* sb = sa + P_A_BYTES;
@@ -639,17 +647,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           }
         }
       }
+      if (prof) {
+        atomicAdd(prof + 0, (unsigned long long)ctl->prof[0]);
+        atomicAdd(prof + 1, (unsigned long long)(clock64() - prof_t0));
+      }
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
       // ---------------------------------------------------------- MMA issuer (leader)
+      const long long prof_t0 = prof ? clock64() : 0;
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs, ++local) {
         const int buf = local & 1;
         const uint32_t tphase = (local >> 1) & 1;
+        const long long tw0 = prof ? clock64() : 0;
         if (!mbar_wait(&ctl->tempty[buf], tphase ^ 1, abort, status, 12)) break;
+        if (prof) ctl->prof[2] += clock64() - tw0;
         if constexpr (MX) {
           // the previous tile's epilogue must have read the chunk both accumulators share
           if (local > 0 && !mbar_wait(&ctl->ovl, (uint32_t)(local - 1) & 1, abort, status, 15)) break;
@@ -658,7 +673,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const uint32_t d_tmem = tmem_base + buf * ACC1_COL;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&ctl->full[stage], phase, abort, status, 13)) {
+          const long long fw0 = prof ? clock64() : 0;
+          const bool got = mbar_wait(&ctl->full[stage], phase, abort, status, 13);
+          if (prof) ctl->prof[1] += clock64() - fw0;
+          if (!got) {
             ok = false;
             break;
           }
@@ -698,6 +716,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         }
         if (!ok) break;
         umma_commit_2sm_mc(&ctl->tfull[buf], 0x3);
+      }
+      if (prof) {
+        atomicAdd(prof + 7, 1ull);
+        atomicAdd(prof + 2, (unsigned long long)ctl->prof[1]);
+        atomicAdd(prof + 3, (unsigned long long)ctl->prof[2]);
+        atomicAdd(prof + 4, (unsigned long long)(clock64() - prof_t0));
       }
     }
   } else {
@@ -861,6 +885,26 @@ static void check_operand(const at::Tensor& t, const char* name, int elem_bytes)
 static int g_reserved_sms = 0;
 void gemm_set_reserved_sms(int64_t n) { g_reserved_sms = (int)std::max<int64_t>(0, n); }
 
+// Stall accounting of the CTA-pair kernels (see GemmEpilogue::prof): off unless
+// gemm_profile(true) was called; gemm_profile_read() returns the eight sums.
+static unsigned long long* g_gemm_prof = nullptr;
+static bool g_gemm_prof_on = false;
+
+void gemm_profile(bool on) {
+  if (on && !g_gemm_prof) C10_CUDA_CHECK(cudaMalloc(&g_gemm_prof, 8 * sizeof(unsigned long long)));
+  if (g_gemm_prof) C10_CUDA_CHECK(cudaMemset(g_gemm_prof, 0, 8 * sizeof(unsigned long long)));
+  g_gemm_prof_on = on;
+}
+
+std::vector<int64_t> gemm_profile_read() {
+  std::vector<int64_t> out(8, 0);
+  if (!g_gemm_prof) return out;
+  unsigned long long h[8];
+  C10_CUDA_CHECK(cudaMemcpy(h, g_gemm_prof, sizeof(h), cudaMemcpyDeviceToHost));
+  for (int i = 0; i < 8; ++i) out[i] = (int64_t)h[i];
+  return out;
+}
+
 static GemmEpilogue build_epilogue(at::Tensor& D, int64_t M, int64_t N,
                                    const c10::optional<at::Tensor>& bias,
                                    const c10::optional<at::Tensor>& residual,
@@ -970,7 +1014,7 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
   }
   gemm_2sm_kernel<EB, MX><<<2 * pairs, kPairThreads, smem, cur_stream()>>>(
       ta, tb, td, tact, tsfa, tsfb, pb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
-      idesc, ep, gemm_status_ptr());
+      idesc, ep, gemm_status_ptr(), g_gemm_prof_on ? g_gemm_prof : nullptr);
   MT_LAUNCH_CHECK();
 }
 
