@@ -36,6 +36,7 @@ def stalls(fn, n=5):
     if p[4] == 0:
         return None
     return {"mma_wait_operands": round(p[2] / p[4], 3), "mma_wait_accumulator": round(p[3] / p[4], 3),
+            "mma_wait_shared_chunk": round(p[5] / p[4], 3),
             "producer_wait_free_stage": round(p[0] / max(1, p[1]), 3)}
 
 

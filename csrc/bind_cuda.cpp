@@ -29,8 +29,12 @@ void adam_step(at::Tensor p, at::Tensor m, at::Tensor v, const at::Tensor& g,
 void sgd_step(at::Tensor p, const at::Tensor& g, c10::optional<at::Tensor> w16,
               const at::Tensor& st, double lr);
 // elementwise.cu
-at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& wte, const at::Tensor& wpe,
-                     int64_t S);
+at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& wte, const at::Tensor& wpe, int64_t S,
+                     const c10::optional<at::Tensor>& drop_rng, int64_t drop_site, int64_t drop_thr16,
+                     double drop_scale);
+void dropout_apply(const at::Tensor& x, at::Tensor out, const at::Tensor& rng, int64_t site, int64_t thr16,
+                   double scale);
+void dropout_advance(at::Tensor rng, int64_t base);
 void embed_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor dwte, at::Tensor dwpe,
                int64_t S, bool accumulate);
 at::Tensor bias_gelu_fwd(at::Tensor pre, const c10::optional<at::Tensor>& bias);
@@ -78,9 +82,12 @@ void gemm_fp8_gather_b(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::
                        const c10::optional<at::Tensor>& act, const c10::optional<at::Tensor>& aux,
                        const c10::optional<at::Tensor>& alpha, const c10::optional<at::Tensor>& alpha2, bool beta);
 // attention.cu
-std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H);
+std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H,
+                                 const c10::optional<at::Tensor>& drop_rng, int64_t drop_site, int64_t drop_thr16,
+                                 double drop_scale);
 at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
-                    int64_t B, int64_t S, int64_t H);
+                    int64_t B, int64_t S, int64_t H, const c10::optional<at::Tensor>& drop_rng, int64_t drop_site,
+                    int64_t drop_thr16, double drop_scale);
 int64_t attn_status(bool reset);
 // fp8.cu
 void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::Tensor>& scale,
@@ -125,6 +132,7 @@ void symm_allreduce_mc(int64_t mc, const std::vector<int64_t>& bufs, const std::
                        int64_t me, int64_t numel, int64_t dtype, int64_t slot, int64_t epoch, int64_t ctas);
 void symm_broadcast_mc(int64_t src, int64_t mc, int64_t bytes, int64_t ctas);
 void gemm_profile(bool on);
+void gemm_set_dropout(const c10::optional<at::Tensor>& rng, int64_t site, int64_t thr16, double scale, int64_t mode);
 std::vector<int64_t> gemm_profile_read();
 void fp8_wire_encode(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt);
 void fp8_wire_decode(const at::Tensor& codes, const at::Tensor& sf, at::Tensor out, int64_t fmt);
@@ -155,7 +163,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("optim_finalize", &optim_finalize);
   m.def("adam_step", &adam_step);
   m.def("sgd_step", &sgd_step);
-  m.def("embed_fwd", &embed_fwd);
+  m.def("embed_fwd", &embed_fwd, py::arg("ids"), py::arg("wte"), py::arg("wpe"), py::arg("S"),
+        py::arg("drop_rng") = py::none(), py::arg("drop_site") = 0, py::arg("drop_thr16") = 0,
+        py::arg("drop_scale") = 1.0);
+  m.def("dropout_apply", &dropout_apply);
+  m.def("dropout_advance", &dropout_advance);
   m.def("embed_bwd", &embed_bwd);
   m.def("bias_gelu_fwd", &bias_gelu_fwd);
   m.def("gelu_bwd_", &gelu_bwd_);
@@ -191,6 +203,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_pull_msgs", &symm_pull_msgs);
   m.def("fp8_wire_encode", &fp8_wire_encode);
   m.def("gemm_profile", &gemm_profile);
+  m.def("gemm_set_dropout", &gemm_set_dropout);
   m.def("gemm_profile_read", &gemm_profile_read);
   m.def("fp8_wire_decode", &fp8_wire_decode);
   m.def("symm_allreduce_msgs", &symm_allreduce_msgs);
@@ -222,7 +235,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("beta") = false);
   m.def("fp8_amax_gather", &fp8_amax_gather);
   m.def("fp8_quantize_colsum", &fp8_quantize_colsum);
-  m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_fwd", &attn_fwd, py::arg("qkv"), py::arg("B"), py::arg("S"), py::arg("H"),
+        py::arg("drop_rng") = py::none(), py::arg("drop_site") = 0, py::arg("drop_thr16") = 0,
+        py::arg("drop_scale") = 1.0);
+  m.def("attn_bwd", &attn_bwd, py::arg("dout"), py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
+        py::arg("S"), py::arg("H"), py::arg("drop_rng") = py::none(), py::arg("drop_site") = 0,
+        py::arg("drop_thr16") = 0, py::arg("drop_scale") = 1.0);
   m.def("attn_status", &attn_status, py::arg("reset") = true);
 }

@@ -1,7 +1,15 @@
 // Causal multi-head attention (flash attention) on tcgen05 for the fused GPT path.
 //
-// Reference semantics: scores = Q K^T / sqrt(d_head) + causal mask -> softmax -> P V
-// (examples/gpt-1b/src/transformer.rs:51-85, mask :163-171); dropout is not applied.
+// Reference semantics: scores = Q K^T / sqrt(d_head) + causal mask -> softmax ->
+// dropout -> P V (examples/gpt-1b/src/transformer.rs:51-85, mask :163-171).  The
+// dropout variant (DROP) draws the keep mask of probability (q, k) from Philox
+// (philox.cuh; element ((b*H + h) * S + q) * S + k of the site) in the forward's
+// softmax warps, which scale kept probabilities by 1 / (1 - p) in the P they hand
+// to the PV MMA (the row sum and the log-sum-exp stay those of the undropped
+// softmax), and draws it again in the backward: dV takes the dropped P^T and
+// dS = P * (mask * dP / (1 - p) - D).  In the backward a thread owns a key and 64
+// queries, so each lane of a warp computes the Philox block of one (query,
+// 8-key group) and the warp exchanges the bits with shuffles.
 // Layout: one [T, 3*H*128] bf16 matrix holds q | k | v for T = B*S tokens (heads
 // contiguous inside each third), the output is [T, H*128]; S is a multiple of 128.
 //
@@ -30,6 +38,7 @@
 // Every wait is bounded (2 s); on a timeout the kernel records a status code,
 // lets its in-flight copies and MMAs land, frees TMEM and returns.
 #include "common.cuh"
+#include "philox.cuh"
 #include "sm100.cuh"
 
 #include <ATen/ops/zeros.h>
@@ -110,9 +119,10 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+template <bool DROP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tma_qkv, bf16* __restrict__ out, int ld_out,
-                    float* __restrict__ lse, int B, int H, int S, float scale, int* status) {
+                    float* __restrict__ lse, int B, int H, int S, float scale, int* status, DropoutArgs drop) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -265,6 +275,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
+      // dropout keep bits of this row's 128 keys of tile j (bit 8*c16 + e of word c16/4),
+      // drawn before the scores arrive so the Philox rounds overlap the S MMA
+      uint32_t keepw[4] = {0u, 0u, 0u, 0u};
+      if constexpr (DROP) {
+        const uint64_t grp0 = ((uint64_t)bh * S + qt * kTile + r) * (uint64_t)(S / 8) + j * (kTile / 8);
+#pragma unroll
+        for (int c16 = 0; c16 < kTile / 8; ++c16)
+          keepw[c16 >> 2] |= dropout_keep8(drop.rng[0], drop.rng[1], drop.site, grp0 + c16, drop.thr16)
+                             << ((c16 & 3) * 8);
+      }
       if (!mbar_wait(&ctl->s_full[g], j & 1, abort, status, 16)) {
         ok = false;
         break;
@@ -314,6 +334,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int e = 0; e < 8; ++e) {
           pv[e] = ex2_approx(fmaf(__uint_as_float(t[c16 * 8 + e]), sl2, neg));
           s8[e] += pv[e];
+        }
+        if constexpr (DROP) {  // keys j*128 + 8*c16 .. +7 of query row qt*128 + r
+          const uint32_t keep = keepw[c16 >> 2] >> ((c16 & 3) * 8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pv[e] = (keep >> e & 1u) ? pv[e] * drop.scale : 0.f;
         }
         uint4 w;
         w.x = pack_bf16x2(pv[0], pv[1]);
@@ -390,11 +415,13 @@ struct BwdCtl {
 
 constexpr int kBwdThreads = 320;  // producer, MMA, 2 x 4 compute warps (column halves)
 
+template <bool DROP>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tma_qkv, const __grid_constant__ CUtensorMap tma_do,
                     const __grid_constant__ CUtensorMap tma_dq,
                     const float* __restrict__ lse, const float* __restrict__ dvec,
-                    bf16* __restrict__ dqkv, int ld_dqkv, int B, int H, int S, float scale, int* status) {
+                    bf16* __restrict__ dqkv, int ld_dqkv, int B, int H, int S, float scale, int* status,
+                    DropoutArgs drop) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -567,13 +594,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           float p[8], ds[8];
+          uint32_t kb = 0;
+          if constexpr (DROP) {
+            // this lane's Philox block: query c*32 + 8g + lane/4, keys of 8-group (warp's 32 keys)/8 + lane%4
+            const int qq = qi * kTile + c * 32 + g * 8 + (lane >> 2);
+            const uint64_t grp = ((uint64_t)bh * S + qq) * (uint64_t)(S / 8) + (kt * kTile + quarter * 32) / 8 +
+                                 (lane & 3);
+            kb = dropout_keep8(drop.rng[0], drop.rng[1], drop.site, grp, drop.thr16);
+          }
 #pragma unroll
           for (int x = 0; x < 8; ++x) {
             const int e = g * 8 + x, col = c * 32 + e;  // query within the tile
             float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -sl[col]));
             if (diag && col < r) pe = 0.f;  // query before key: masked in the forward
-            p[x] = pe;
-            ds[x] = pe * (__uint_as_float(dv[e]) - sd[col]) * scale;
+            if constexpr (DROP) {
+              // the key bit of query e sits in the block of lane 4x + (key's 8-group within the warp)
+              const bool keep = (__shfl_sync(0xffffffffu, kb, x * 4 + (lane >> 3)) >> (lane & 7)) & 1u;
+              p[x] = keep ? pe * drop.scale : 0.f;
+              ds[x] = pe * ((keep ? __uint_as_float(dv[e]) * drop.scale : 0.f) - sd[col]) * scale;
+            } else {
+              p[x] = pe;
+              ds[x] = pe * (__uint_as_float(dv[e]) - sd[col]) * scale;
+            }
           }
           uint4 wp;
           wp.x = pack_bf16x2(p[0], p[1]);
@@ -736,7 +778,11 @@ void check_qkv(const at::Tensor& qkv, int B, int S, int H) {
 }  // namespace
 
 // qkv [B*S, 3*H*128] bf16 -> (out [B*S, H*128] bf16, lse [B, H, S] fp32)
-std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H) {
+DropoutArgs make_dropout_args(const c10::optional<at::Tensor>& rng, int64_t site, int64_t thr16, double scale);
+
+std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H,
+                                 const c10::optional<at::Tensor>& drop_rng, int64_t drop_site, int64_t drop_thr16,
+                                 double drop_scale) {
   check_qkv(qkv, (int)B, (int)S, (int)H);
   ensure_context();
   auto out = at::empty({B * S, H * kD}, qkv.options());
@@ -745,21 +791,30 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, in
                                      qkv.stride(0), 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B);
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)kFwdSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)kFwdSmem));
     attr = true;
   }
+  const DropoutArgs drop = make_dropout_args(drop_rng, drop_site, drop_thr16, drop_scale);
   const int grid = (int)(B * H * ((S / kTile + 1) / 2));
-  attn_fwd_kernel<<<grid, kFwdThreads, kFwdSmem, cur_stream()>>>(tm, (bf16*)out.data_ptr(), (int)(H * kD),
-                                                              lse.data_ptr<float>(), (int)B, (int)H, (int)S,
-                                                              1.0f / sqrtf((float)kD), attn_status_ptr());
+  if (drop.rng)
+    attn_fwd_kernel<true><<<grid, kFwdThreads, kFwdSmem, cur_stream()>>>(
+        tm, (bf16*)out.data_ptr(), (int)(H * kD), lse.data_ptr<float>(), (int)B, (int)H, (int)S,
+        1.0f / sqrtf((float)kD), attn_status_ptr(), drop);
+  else
+    attn_fwd_kernel<false><<<grid, kFwdThreads, kFwdSmem, cur_stream()>>>(
+        tm, (bf16*)out.data_ptr(), (int)(H * kD), lse.data_ptr<float>(), (int)B, (int)H, (int)S,
+        1.0f / sqrtf((float)kD), attn_status_ptr(), drop);
   MT_LAUNCH_CHECK();
   return {out, lse};
 }
 
 // -> dqkv [B*S, 3*H*128] bf16 (dq | dk | dv)
 at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
-                    int64_t B, int64_t S, int64_t H) {
+                    int64_t B, int64_t S, int64_t H, const c10::optional<at::Tensor>& drop_rng, int64_t drop_site,
+                    int64_t drop_thr16, double drop_scale) {
   check_qkv(qkv, (int)B, (int)S, (int)H);
   TORCH_CHECK(dout.is_contiguous() && out.is_contiguous() && dout.sizes() == out.sizes() &&
                   dout.size(0) == B * S && dout.size(1) == H * kD && dout.scalar_type() == at::kBFloat16,
@@ -786,14 +841,22 @@ at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Ten
                                       CU_TENSOR_MAP_SWIZZLE_128B);
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)kBwdSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)kBwdSmem));
     attr = true;
   }
+  const DropoutArgs drop = make_dropout_args(drop_rng, drop_site, drop_thr16, drop_scale);
   const int grid = (int)(B * H * (S / kTile));
-  attn_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, cur_stream()>>>(
-      tq, td, tdq, lse.data_ptr<float>(), dvec.data_ptr<float>(), (bf16*)dqkv.data_ptr(),
-      (int)(3 * HD), (int)B, (int)H, (int)S, 1.0f / sqrtf((float)kD), attn_status_ptr());
+  if (drop.rng)
+    attn_bwd_kernel<true><<<grid, kBwdThreads, kBwdSmem, cur_stream()>>>(
+        tq, td, tdq, lse.data_ptr<float>(), dvec.data_ptr<float>(), (bf16*)dqkv.data_ptr(),
+        (int)(3 * HD), (int)B, (int)H, (int)S, 1.0f / sqrtf((float)kD), attn_status_ptr(), drop);
+  else
+    attn_bwd_kernel<false><<<grid, kBwdThreads, kBwdSmem, cur_stream()>>>(
+        tq, td, tdq, lse.data_ptr<float>(), dvec.data_ptr<float>(), (bf16*)dqkv.data_ptr(),
+        (int)(3 * HD), (int)B, (int)H, (int)S, 1.0f / sqrtf((float)kD), attn_status_ptr(), drop);
   MT_LAUNCH_CHECK();
   {
     const int64_t n8 = T * HD / 8;

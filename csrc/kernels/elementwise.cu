@@ -10,13 +10,15 @@
 // (red.global.add.v4.f32) and sums position rows over the batch without atomics.
 #include "common.cuh"
 #include "gelu.cuh"
+#include "philox.cuh"
 
 namespace mtorus {
 
 // x[t, :] = wte[ids[t], :] + wpe[t % S, :]   (bf16 tables, bf16 output)
 __global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const bf16* __restrict__ wte,
                                  const bf16* __restrict__ wpe, bf16* __restrict__ out, int T,
-                                 int S, int d, int V) {
+                                 int S, int d, int V, DropoutArgs drop) {
+  const uint32_t k0 = drop.rng ? drop.rng[0] : 0u, k1 = drop.rng ? drop.rng[1] : 0u;
   const int nv = d / 8;
   const size_t total = (size_t)T * nv;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -29,8 +31,44 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const bf16* __
     unpack8(reinterpret_cast<const bf16x8*>(wpe + (size_t)(t % S) * d)[c], b);
 #pragma unroll
     for (int k = 0; k < 8; ++k) a[k] += b[k];
+    if (drop.rng) {  // embedding dropout (element t * d + 8c + k; its 8-group is (t * d) / 8 + c)
+      const uint32_t keep = dropout_keep8(k0, k1, drop.site, (uint64_t)t * (d / 8) + c, drop.thr16);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] = (keep >> k & 1u) ? a[k] * drop.scale : 0.f;
+    }
     reinterpret_cast<bf16x8*>(out + (size_t)t * d)[c] = pack8(a);
   }
+}
+
+// out = x * keep * scale over the site's mask (the backward of a dropout: the same
+// mask applied to the incoming gradient); out may alias x.  n a multiple of 8.
+__global__ void dropout_apply_kernel(const bf16* __restrict__ x, bf16* __restrict__ out, size_t n8,
+                                     DropoutArgs drop) {
+  const uint32_t k0 = drop.rng[0], k1 = drop.rng[1];
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    float a[8];
+    unpack8(reinterpret_cast<const bf16x8*>(x)[i], a);
+    const uint32_t keep = dropout_keep8(k0, k1, drop.site, i, drop.thr16);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = (keep >> k & 1u) ? a[k] * drop.scale : 0.f;
+    reinterpret_cast<bf16x8*>(out)[i] = pack8(a);
+  }
+}
+
+// rng = {key lo, key hi, step lo, step hi}: step += 1, key = SplitMix64 finaliser
+// (G. L. Steele, D. Lea, C. H. Flood, "Fast splittable pseudorandom number
+// generators", OOPSLA 2014) of base * golden-ratio increment + step + 1.
+__global__ void dropout_advance_kernel(int32_t* rng, uint64_t base) {
+  if (threadIdx.x || blockIdx.x) return;
+  const uint64_t step = ((uint64_t)(uint32_t)rng[2] | ((uint64_t)(uint32_t)rng[3] << 32)) + 1;
+  uint64_t z = base * 0x9E3779B97F4A7C15ull + step + 1;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  rng[0] = (int32_t)(uint32_t)z;
+  rng[1] = (int32_t)(uint32_t)(z >> 32);
+  rng[2] = (int32_t)(uint32_t)step;
+  rng[3] = (int32_t)(uint32_t)(step >> 32);
 }
 
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
@@ -160,8 +198,41 @@ static int ew_grid(size_t n) {
   return (int)std::max<size_t>(1, std::min<size_t>((n + 255) / 256, (size_t)num_sms() * 16));
 }
 
+DropoutArgs make_dropout_args(const c10::optional<at::Tensor>& rng, int64_t site, int64_t thr16, double scale) {
+  DropoutArgs a{};
+  if (rng.has_value()) {
+    MT_CHECK(rng->is_cuda() && rng->scalar_type() == at::kInt && rng->numel() >= 2, "dropout: int32 rng key on the GPU");
+    MT_CHECK(thr16 >= 0 && thr16 < 65536 && scale >= 1.0, "dropout: 0 <= p < 1");
+    a.rng = reinterpret_cast<const uint32_t*>(rng->data_ptr<int32_t>());
+    a.site = (uint32_t)site;
+    a.thr16 = (uint32_t)thr16;
+    a.scale = (float)scale;
+  }
+  return a;
+}
+
+void dropout_apply(const at::Tensor& x, at::Tensor out, const at::Tensor& rng, int64_t site, int64_t thr16,
+                   double scale) {
+  MT_CHECK(x.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
+               out.is_contiguous() && x.numel() == out.numel() && x.numel() % 8 == 0,
+           "dropout_apply: contiguous bf16 of equal size, numel % 8 == 0");
+  const size_t n8 = x.numel() / 8;
+  if (n8 == 0) return;
+  dropout_apply_kernel<<<ew_grid(n8), 256, 0, cur_stream()>>>(reinterpret_cast<const bf16*>(x.data_ptr()),
+                                                              reinterpret_cast<bf16*>(out.data_ptr()), n8,
+                                                              make_dropout_args(rng, site, thr16, scale));
+  MT_LAUNCH_CHECK();
+}
+
+void dropout_advance(at::Tensor rng, int64_t base) {
+  MT_CHECK(rng.is_cuda() && rng.scalar_type() == at::kInt && rng.numel() == 4, "dropout_advance: int32 [4] on the GPU");
+  dropout_advance_kernel<<<1, 32, 0, cur_stream()>>>(rng.data_ptr<int32_t>(), (uint64_t)base);
+  MT_LAUNCH_CHECK();
+}
+
 at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& wte, const at::Tensor& wpe,
-                     int64_t S) {
+                     int64_t S, const c10::optional<at::Tensor>& drop_rng, int64_t drop_site, int64_t drop_thr16,
+                     double drop_scale) {
   MT_CHECK(ids.scalar_type() == at::kLong, "embed: ids must be int64");
   MT_CHECK(wte.scalar_type() == at::kBFloat16 && wpe.scalar_type() == at::kBFloat16,
            "embed: bf16 tables");
@@ -173,7 +244,7 @@ at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& wte, const at::Ten
   embed_fwd_kernel<<<ew_grid((size_t)T * d / 8), 256, 0, cur_stream()>>>(
       ids.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(wte.data_ptr()),
       reinterpret_cast<const bf16*>(wpe.data_ptr()), reinterpret_cast<bf16*>(out.data_ptr()), T,
-      (int)S, d, V);
+      (int)S, d, V, make_dropout_args(drop_rng, drop_site, drop_thr16, drop_scale));
   MT_LAUNCH_CHECK();
   return out;
 }

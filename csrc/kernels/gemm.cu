@@ -28,6 +28,7 @@
 
 #include "amax_publish.cuh"
 #include "gelu.cuh"
+#include "philox.cuh"
 #include "sm100.cuh"
 
 namespace mtorus {
@@ -388,7 +389,7 @@ struct PairSmem {
   uint64_t tfull[2];         // each CTA: accumulator buffer ready for the epilogue
   uint64_t tempty[2];        // leader: both epilogues finished with a buffer
   uint64_t ovl;              // leader (MXFP8): both epilogues read the chunk shared by the two accumulators
-  long long prof[3];         // stall accounting (GemmEpilogue::prof): empty, full, tempty waits
+  long long prof[4];         // stall accounting (gemm_profile): empty, full, tempty, ovl waits
   uint32_t tmem_base;
   int abort;
 };
@@ -429,12 +430,26 @@ __device__ __forceinline__ void epi_prefetch(const GemmEpilogue& ep, int m, int 
 // stages: the warp's two 4 KB staging buffers (D at 0, the GELU output at 2048),
 // used in turn by the chunks that store (sb flips at each commit, so the buffer
 // written next is never the one the most recent store still reads).
+// DROP: dropout drawn in the epilogue (philox.cuh; element index m * N + n): mode 1
+// drops the GEMM result before the residual add (a branch output), mode 2 drops
+// GELU(result) in the act / act8 output (the FFN hidden), mode 3 applies the same
+// mask to the incoming gradient before the dGELU multiply (its backward).
+template <bool DROP>
 __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const uint4 (&x)[4], int m, int M, int N,
                                                 int n0, int row0, float alpha, float act_scale, float& act_amax,
                                                 const GemmEpilogue& ep, bool f32out, uint8_t* stages, int& sb,
-                                                const CUtensorMap* tma_d, const CUtensorMap* tma_act, int lane) {
+                                                const CUtensorMap* tma_d, const CUtensorMap* tma_act, int lane,
+                                                const DropoutArgs& drop, int drop_mode) {
   if (n0 >= N) return;  // warp-uniform
   uint8_t* stage = stages + sb * P_EPI_BUF;
+  uint32_t keep = 0xFFFFFFFFu;
+  if constexpr (DROP) {
+    const uint32_t k0 = drop.rng[0], k1 = drop.rng[1];
+    const uint64_t g0 = ((uint64_t)m * N + n0) >> 3;
+    keep = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) keep |= dropout_keep8(k0, k1, drop.site, g0 + q, drop.thr16) << (8 * q);
+  }
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
@@ -450,6 +465,12 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
 #pragma unroll
       for (int i = 0; i < 32; ++i)
         if (n0 + i < N) v[i] += ep.bias[n0 + i];
+    }
+  }
+  if constexpr (DROP) {
+    if (drop_mode == 1 || drop_mode == 3) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = (keep >> i & 1u) ? v[i] * drop.scale : 0.f;
     }
   }
   if (ep.aux) {
@@ -491,6 +512,14 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
         unpack8(pk, p8);  // GELU of the rounded pre-activation
 #pragma unroll
         for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
+        if constexpr (DROP) {
+          if (drop_mode == 2) {
+            float r8[8];
+            unpack8(pack8(g8), r8);  // the bf16 GELU, then the dropout (as dropout_apply does)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) g8[i] = (keep >> (8 * j + i) & 1u) ? r8[i] * drop.scale : 0.f;
+          }
+        }
         *reinterpret_cast<bf16x8*>(abase + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = pack8(g8);
       } else if (ep.act8) {
         // FP8 GELU: the bf16-rounded GELU (as the bf16 path stores it) times the scale;
@@ -500,6 +529,13 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
 #pragma unroll
         for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
         unpack8(pack8(g8), r8);
+        if constexpr (DROP) {
+          if (drop_mode == 2) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) g8[i] = (keep >> (8 * j + i) & 1u) ? r8[i] * drop.scale : 0.f;
+            unpack8(pack8(g8), r8);
+          }
+        }
         uint32_t w[2];
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
@@ -537,7 +573,7 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
 // loaded per stage next to the operands and copied into TMEM by the MMA thread
 // (tcgen05.cp, ordered before the stage's MMAs, which read them); sf_kb = number of
 // 128-wide K blocks per 128-row block of the scale tensors.
-template <int EB, bool MX = false>
+template <int EB, bool MX = false, bool DROP = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     const __grid_constant__ CUtensorMap tma_b,
@@ -547,10 +583,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     const __grid_constant__ CUtensorMap tma_sfb,
                     const __grid_constant__ PeerMapsB peer_b, int M, int N, int K, int a_mn,
                     int b_mn, int sf_kb, uint32_t idesc, GemmEpilogue ep, int* status,
-                    unsigned long long* prof) {
+                    unsigned long long* prof, DropoutArgs drop, int drop_mode) {
   // prof (optional, gemm_profile): stall accounting summed over CTAs: cycles the
   // producer waited for free stages [0] and ran [1], the MMA issuer waited for
-  // loaded stages [2] / free accumulators [3] and ran [4]; CTA pairs [7].
+  // loaded stages [2] / free accumulators [3] and ran [4], waited for the MXFP8
+  // epilogue to read the chunk both accumulators share [5]; CTA pairs [7].
   static_assert(!MX || EB == 1, "block scaling is for fp8 operands");
   constexpr int BK = 128 / EB;       // K elements per stage
   constexpr int MMA_K = 32 / EB;     // K elements per tcgen05.mma
@@ -583,7 +620,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       mbar_init(&ctl->tempty[b], 2 * 32 * P_EPI_WARPS);
     }
     if constexpr (MX) mbar_init(&ctl->ovl, 2 * 128);
-    for (int i = 0; i < 3; ++i) ctl->prof[i] = 0;
+    for (int i = 0; i < 4; ++i) ctl->prof[i] = 0;
     ctl->abort = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tma_a);
@@ -667,7 +704,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (prof) ctl->prof[2] += clock64() - tw0;
         if constexpr (MX) {
           // the previous tile's epilogue must have read the chunk both accumulators share
+          const long long ow0 = prof ? clock64() : 0;
           if (local > 0 && !mbar_wait(&ctl->ovl, (uint32_t)(local - 1) & 1, abort, status, 15)) break;
+          if (prof) ctl->prof[3] += clock64() - ow0;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * ACC1_COL;
@@ -719,6 +758,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       }
       if (prof) {
         atomicAdd(prof + 7, 1ull);
+        atomicAdd(prof + 5, (unsigned long long)ctl->prof[3]);
         atomicAdd(prof + 2, (unsigned long long)ctl->prof[1]);
         atomicAdd(prof + 3, (unsigned long long)ctl->prof[2]);
         atomicAdd(prof + 4, (unsigned long long)(clock64() - prof_t0));
@@ -774,8 +814,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const int c0 = epi_chunk<MX>(buf, h, i), c1 = epi_chunk<MX>(buf, h, i + 1);
         tmem_ld32(tbase + c1 * 32, rb);
         epi_prefetch(ep, m, M, N, nb * P_BN + c1 * 32, xb);
-        epi_chunk_store(ra, xa, m, M, N, nb * P_BN + c0 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
-                        stage_base, sb, &tma_d, &tma_act, lane);
+        epi_chunk_store<DROP>(ra, xa, m, M, N, nb * P_BN + c0 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
+                              stage_base, sb, &tma_d, &tma_act, lane, drop, drop_mode);
         tmem_wait_ld();
         if (i + 1 == 3) {
           // every column of this warp's share of the buffer is in registers: release it
@@ -786,8 +826,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           tmem_ld32(tbase + c2 * 32, ra);
           epi_prefetch(ep, m, M, N, nb * P_BN + c2 * 32, xa);
         }
-        epi_chunk_store(rb, xb, m, M, N, nb * P_BN + c1 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
-                        stage_base, sb, &tma_d, &tma_act, lane);
+        epi_chunk_store<DROP>(rb, xb, m, M, N, nb * P_BN + c1 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
+                              stage_base, sb, &tma_d, &tma_act, lane, drop, drop_mode);
         if (i + 1 != 3) tmem_wait_ld();
       }
     }
@@ -955,6 +995,27 @@ static GemmEpilogue build_epilogue(at::Tensor& D, int64_t M, int64_t N,
   return ep;
 }
 
+// Dropout for the next CTA-pair GEMM launch only (gemm_set_dropout; consumed and
+// cleared by that launch): the epilogue draws the mask of a site (see DROP in
+// epi_chunk_store).  Setting it for one call keeps every GEMM entry point's
+// signature unchanged.
+static DropoutArgs g_next_drop{};
+static int g_next_drop_mode = 0;
+
+void gemm_set_dropout(const c10::optional<at::Tensor>& rng, int64_t site, int64_t thr16, double scale,
+                      int64_t mode) {
+  g_next_drop = DropoutArgs{};
+  g_next_drop_mode = 0;
+  if (!rng.has_value()) return;
+  TORCH_CHECK(rng->is_cuda() && rng->scalar_type() == at::kInt && rng->numel() >= 2, "gemm dropout: int32 rng key");
+  TORCH_CHECK(mode >= 1 && mode <= 3 && thr16 >= 0 && thr16 < 65536 && scale >= 1.0, "gemm dropout: mode 1..3, 0 <= p < 1");
+  g_next_drop.rng = reinterpret_cast<const uint32_t*>(rng->data_ptr<int32_t>());
+  g_next_drop.site = (uint32_t)site;
+  g_next_drop.thr16 = (uint32_t)thr16;
+  g_next_drop.scale = (float)scale;
+  g_next_drop_mode = (int)mode;
+}
+
 template <int EB, bool MX = false>
 static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, at::Tensor& D,
                         const c10::optional<at::Tensor>& act, const GemmEpilogue& ep, int64_t M,
@@ -1006,6 +1067,25 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
   const size_t smem = NST * P_STAGE_BYTES + P_EPI_BYTES + (MX ? NST * P_SF_BYTES : 0) + sizeof(PairSmem) + 1024;
   static_assert(NST * P_STAGE_BYTES + P_EPI_BYTES + (MX ? NST * P_SF_BYTES : 0) + sizeof(PairSmem) + 1024 <= 232448,
                 "CTA-pair GEMM: shared memory above the 227 KB per-CTA limit");
+  const DropoutArgs drop = g_next_drop;
+  const int drop_mode = g_next_drop_mode;
+  g_next_drop = DropoutArgs{};
+  g_next_drop_mode = 0;
+  if (drop.rng) {
+    TORCH_CHECK((drop_mode != 1 || ep.residual) && (drop_mode != 2 || ep.act || ep.act8) && (drop_mode != 3 || ep.aux),
+                "gemm dropout: mode 1 needs a residual, 2 a GELU output, 3 a dGELU input");
+    static bool attr_set_d = false;
+    if (!attr_set_d) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB, MX, true>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      attr_set_d = true;
+    }
+    gemm_2sm_kernel<EB, MX, true><<<2 * pairs, kPairThreads, smem, cur_stream()>>>(
+        ta, tb, td, tact, tsfa, tsfb, pb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
+        idesc, ep, gemm_status_ptr(), g_gemm_prof_on ? g_gemm_prof : nullptr, drop, drop_mode);
+    MT_LAUNCH_CHECK();
+    return;
+  }
   static bool attr_set = false;
   if (!attr_set) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB, MX>,
@@ -1014,7 +1094,7 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
   }
   gemm_2sm_kernel<EB, MX><<<2 * pairs, kPairThreads, smem, cur_stream()>>>(
       ta, tb, td, tact, tsfa, tsfb, pb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
-      idesc, ep, gemm_status_ptr(), g_gemm_prof_on ? g_gemm_prof : nullptr);
+      idesc, ep, gemm_status_ptr(), g_gemm_prof_on ? g_gemm_prof : nullptr, drop, 0);
   MT_LAUNCH_CHECK();
 }
 
@@ -1039,6 +1119,7 @@ void gemm_bf16(const at::Tensor& A, bool a_mn, const at::Tensor& B, bool b_mn, a
     return;
   }
   static const bool force_1sm = std::getenv("MTORUS_GEMM_1SM") != nullptr;
+  TORCH_CHECK(!g_next_drop.rng || (M >= 2 * P_BM && !force_1sm), "gemm dropout needs M >= 256 (the CTA-pair kernel)");
   if (M >= 2 * P_BM && !force_1sm) {
     launch_pair<2>(A, a_mn, B, b_mn, D, act, ep, M, N, K,
                    make_idesc_bf16(2 * P_BM, P_BN, a_mn ? 1 : 0, b_mn ? 1 : 0));

@@ -190,16 +190,25 @@ class TransformerBlock(nn.Module):
         return self.dropout(self.ff(self.norm2(x))) + x
 
     # ---------------------------------------------------------------- fused path
-    def fused_forward(self, x2d, B: int, S: int, fp8=None):
+    def fused_forward(self, x2d, B: int, S: int, fp8=None, drop=None):
+        """drop: optional (DropoutState, layer index) -- the layer's four dropout sites
+        (attention probabilities, attention output, FFN hidden, FFN output) drawn in the
+        producing kernels."""
+        from ..ops.dropout import SITE_ATTN_OUT, SITE_ATTN_PROBS, SITE_FFN_ACT, SITE_FFN_OUT
         from ..ops.fused import AttnBlockFn, MLPBlockFn
 
         a = self.attention
+        da = dm = None
+        if drop is not None:
+            st, layer = drop
+            da = (st.layer_args(layer, SITE_ATTN_PROBS), st.layer_args(layer, SITE_ATTN_OUT))
+            dm = (st.layer_args(layer, SITE_FFN_ACT), st.layer_args(layer, SITE_FFN_OUT))
         x2d = AttnBlockFn.apply(x2d, (self.norm1.gamma, self.norm1.beta, self.norm1.eps),
                                 (self._qkv_w, self._qkv_b), (a.out_proj.weight, a.out_proj.bias),
-                                (B, S, a.num_heads, a.d_head), fp8)
+                                (B, S, a.num_heads, a.d_head), fp8, da)
         return MLPBlockFn.apply(x2d, (self.norm2.gamma, self.norm2.beta, self.norm2.eps),
                                 (self.ff.linear1.weight, self.ff.linear1.bias,
-                                 self.ff.linear2.weight, self.ff.linear2.bias), fp8)
+                                 self.ff.linear2.weight, self.ff.linear2.bias), fp8, dm)
 
 
 class GptModel(nn.Module):
@@ -308,19 +317,41 @@ class GptModel(nn.Module):
         return LayerNormFn.apply(x, (self.ln_f.gamma, self.ln_f.beta), self.ln_f.eps)
 
     def fused_embed(self, input_ids: torch.Tensor) -> torch.Tensor:
-        """[B, S] token ids -> [B*S, d] bf16 hidden (token + learned position embedding)."""
+        """[B, S] token ids -> [B*S, d] bf16 hidden (token + learned position embedding,
+        then the embedding dropout when enabled)."""
+        from ..ops.dropout import SITE_EMBED
         from ..ops.fused import EmbeddingFn, grad_anchor
 
         assert self.flat is not None, "call flatten(device) before using the fused path"
         S = input_ids.shape[1]
+        ds = self.dropout_state
         return EmbeddingFn.apply(input_ids, grad_anchor(input_ids.device),
-                                 (self.token_embedding.weight, self.position_embedding.weight), S)
+                                 (self.token_embedding.weight, self.position_embedding.weight), S,
+                                 None if ds is None else ds.args(SITE_EMBED))
+
+    dropout_state = None
+
+    def enable_dropout(self, seed: int = 0):
+        """Dropout with the config's probability in the fused path (all five reference
+        sites, masks drawn by Philox inside the kernels); no-op for p = 0.  The trainer
+        calls ``dropout_state.advance()`` once per step and sets
+        ``dropout_state.micro`` before each micro-batch's forward."""
+        from ..ops.dropout import DropoutState
+
+        p = float(getattr(self.config, "dropout", 0.0))
+        self.dropout_state = DropoutState(p, self.flat.device, seed) if p > 0.0 else None
+        return self.dropout_state
+
+    def _layer_drop(self, i: int):
+        ds = self.dropout_state
+        return None if ds is None else (ds, self.layer_offset + i)
 
     def fused_blocks(self, x: torch.Tensor, B: int, S: int) -> torch.Tensor:
         """[B*S, d] -> [B*S, d] through this model's (or stage's) transformer blocks."""
         st = getattr(self, "fp8_state", None)
         for i, blk in enumerate(self.blocks):
-            x = blk.fused_forward(x, B, S, None if st is None else (st, f"L{self.layer_offset + i}"))
+            x = blk.fused_forward(x, B, S, None if st is None else (st, f"L{self.layer_offset + i}"),
+                                  self._layer_drop(i))
         return x
 
     def fused_stage(self, x: torch.Tensor, B: int, S: int) -> torch.Tensor:
@@ -340,7 +371,8 @@ class GptModel(nn.Module):
             def run(x):
                 if embed:
                     x = self.fused_embed(x)
-                return blk.fused_forward(x, B, S, None if st is None else (st, f"L{self.layer_offset + i}"))
+                return blk.fused_forward(x, B, S, None if st is None else (st, f"L{self.layer_offset + i}"),
+                                         self._layer_drop(i))
             return run
 
         return [block_fn(i, blk, self.has_embed and i == 0) for i, blk in enumerate(self.blocks)]

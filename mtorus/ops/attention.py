@@ -6,8 +6,10 @@ Reference: scores = QK^T / sqrt(d_head) + mask -> softmax -> dropout -> PV
 the [B,H,S,S] score tensor is never materialised: ``csrc/kernels/attention.cu``
 runs the forward (O and the per-row log-sum-exp) and the backward (dQ, dK, dV
 straight into one [T, 3*H*d] gradient matrix) on tcgen05 with TMEM
-accumulators.  Head dim 128 and sequence lengths that are multiples of 128;
-no dropout.
+accumulators.  Head dim 128 and sequence lengths that are multiples of 128.
+Attention-probability dropout (``drop``) draws its Philox mask inside both
+kernels (``csrc/kernels/philox.cuh``): element (q, k) of head (b, h) is element
+((b*H + h) * S + q) * S + k of the site.
 """
 from __future__ import annotations
 
@@ -27,16 +29,22 @@ def check_shape(S: int, dh: int) -> None:
                          f"(got head dim {dh}, seq len {S})")
 
 
-def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int) -> Tuple[torch.Tensor, torch.Tensor]:
-    """qkv [B*S, 3*H*128] bf16 -> (out [B*S, H*128] bf16, lse [B, H, S] fp32)."""
-    out, lse = _cuda().attn_fwd(qkv, B, S, H)
-    return out, lse
+def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, drop=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """qkv [B*S, 3*H*128] bf16 -> (out [B*S, H*128] bf16, lse [B, H, S] fp32).
+    drop: optional (rng, site, thr16, scale) of the attention-probability dropout."""
+    if drop is None:
+        return tuple(_cuda().attn_fwd(qkv, B, S, H))
+    rng, site, thr, scale = drop
+    return tuple(_cuda().attn_fwd(qkv, B, S, H, rng, int(site), int(thr), float(scale)))
 
 
 def attention_bwd(dout: torch.Tensor, qkv: torch.Tensor, out: torch.Tensor, lse: torch.Tensor,
-                  B: int, S: int, H: int) -> torch.Tensor:
+                  B: int, S: int, H: int, drop=None) -> torch.Tensor:
     """-> dqkv [B*S, 3*H*128] bf16 (dq | dk | dv)."""
-    return _cuda().attn_bwd(dout.contiguous(), qkv, out, lse, B, S, H)
+    if drop is None:
+        return _cuda().attn_bwd(dout.contiguous(), qkv, out, lse, B, S, H)
+    rng, site, thr, scale = drop
+    return _cuda().attn_bwd(dout.contiguous(), qkv, out, lse, B, S, H, rng, int(site), int(thr), float(scale))
 
 
 class CausalAttentionFn(torch.autograd.Function):
@@ -59,11 +67,15 @@ def causal_attention(qkv: torch.Tensor, B: int, S: int, H: int, dh: int) -> torc
     return CausalAttentionFn.apply(qkv, B, S, H)
 
 
-def reference_attention(qkv: torch.Tensor, B: int, S: int, H: int, dh: int) -> torch.Tensor:
-    """Plain PyTorch fp32 oracle of the same op (tests only)."""
+def reference_attention(qkv: torch.Tensor, B: int, S: int, H: int, dh: int,
+                        keep: torch.Tensor = None, p_drop: float = 0.0) -> torch.Tensor:
+    """Plain PyTorch fp32 oracle of the same op (tests only); keep: optional bool
+    [B, H, S, S] dropout mask of the probabilities."""
     q, k, v = qkv.float().view(B, S, 3, H, dh).unbind(2)
     q, k, v = (t.transpose(1, 2) for t in (q, k, v))
     s = q @ k.transpose(-1, -2) / dh ** 0.5
     mask = torch.ones(S, S, dtype=torch.bool, device=qkv.device).triu(1)
     p = torch.softmax(s.masked_fill(mask, float("-inf")), dim=-1)
+    if keep is not None:
+        p = torch.where(keep, p / (1.0 - p_drop), torch.zeros_like(p))
     return (p @ v).transpose(1, 2).reshape(B * S, H * dh)

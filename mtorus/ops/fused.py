@@ -160,7 +160,9 @@ class AttnBlockFn(Function):
     backward adds the residual gradient in the same kernel."""
 
     @staticmethod
-    def forward(ctx, x2d, ln, qkv_params, out_params, shape, fp8=None):
+    def forward(ctx, x2d, ln, qkv_params, out_params, shape, fp8=None, drop=None):
+        """drop: optional (attention-probability dropout args, attention-output dropout
+        args), each (rng, site, thr16, scale)."""
         from .attention import attention_fwd, check_shape
 
         B, S, H, dh = shape
@@ -170,6 +172,8 @@ class AttnBlockFn(Function):
         ctx.shape = (B, S, H)
         ctx.params = (ln, qkv_params, out_params)
         ctx.fp8 = fp8
+        d_probs, d_out = drop if drop is not None else (None, None)
+        ctx.drop = (d_probs, d_out)
         if _mx(fp8):
             # MXFP8: every GEMM operand carries 1x32 UE8M0 scales along its contraction dim;
             # inputs are quantised both ways once (row-wise now, column-wise for wgrad)
@@ -178,9 +182,10 @@ class AttnBlockFn(Function):
             gamma, beta, eps = ln
             hr, hc, mean, rstd = MX.mx_layernorm_rc(x2d, gamma.data, beta.data, eps, MX.E4M3)
             qkv = MX.gemm_mxfp8(hr, wq.mx[0], bias=bq.data)
-            o, lse = attention_fwd(qkv, B, S, H)
+            o, lse = attention_fwd(qkv, B, S, H, d_probs)
             orow, ocol = MX.mx_quantize_rc(o, MX.E4M3)
-            out = MX.gemm_mxfp8(orow, wo.mx[0], bias=bo.data, residual=x2d)
+            with K.gemm_dropout(d_out, 1):
+                out = MX.gemm_mxfp8(orow, wo.mx[0], bias=bo.data, residual=x2d)
             ctx.save_for_backward(x2d, mean, rstd, hc.codes, hc.sf, ocol.codes, ocol.sf, qkv, o, lse)
             return out
         if fp8 is not None:
@@ -193,16 +198,18 @@ class AttnBlockFn(Function):
         else:
             h, mean, rstd = _ln_fwd(x2d, ln)
             qkv = K.gemm(h, wq.w16, bias=bq.data)
-        o, lse = attention_fwd(qkv, B, S, H)
+        o, lse = attention_fwd(qkv, B, S, H, d_probs)
         attn_saved = (qkv, o, lse)
         if fp8 is not None:
             o8, io = st.quantize(o, tag + ".out_in", F8.E4M3)
-            out = F8.gemm_fp8(o8, F8.E4M3, wo.w8, F8.E4M3, bias=bo.data, residual=x2d, alpha=io,
-                              alpha2=wo.w8_inv)
+            with K.gemm_dropout(d_out, 1):
+                out = F8.gemm_fp8(o8, F8.E4M3, wo.w8, F8.E4M3, bias=bo.data, residual=x2d, alpha=io,
+                                  alpha2=wo.w8_inv)
             o = o8
             ctx.inv = (ih, io)
         else:
-            out = K.gemm(o, wo.w16, bias=bo.data, residual=x2d)
+            with K.gemm_dropout(d_out, 1):
+                out = K.gemm(o, wo.w16, bias=bo.data, residual=x2d)
         ctx.save_for_backward(x2d, mean, rstd, h, o, *attn_saved)
         return out
 
@@ -217,20 +224,24 @@ class AttnBlockFn(Function):
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
         fp8 = ctx.fp8
+        d_probs, d_out = ctx.drop
+        # the attention branch's gradient: dout through the output dropout's mask (the
+        # residual path keeps dout itself)
+        dbr = K.dropout_apply(dout, d_out) if d_out is not None else dout
         if fp8 is not None:
             st, tag = fp8
             ih, io = ctx.inv
-            # E5M2 codes and the output-projection bias gradient in one pass over dout
-            g8, ig = st.quantize_colsum(dout, tag + ".out_grad", F8.E5M2, bo.main_grad, acc)
+            # E5M2 codes and the output-projection bias gradient in one pass over the branch gradient
+            g8, ig = st.quantize_colsum(dbr, tag + ".out_grad", F8.E5M2, bo.main_grad, acc)
             do = F8.gemm_fp8(g8, F8.E5M2, wo.w8, F8.E4M3, b_mn=True, alpha=ig, alpha2=wo.w8_inv)
             F8.gemm_fp8(g8, F8.E5M2, o, F8.E4M3, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc,
                         alpha=ig, alpha2=io)
         else:
-            do = K.gemm(dout, wo.w16, b_mn=True)
-            K.gemm(dout, o, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc)
-            K.colsum_(dout, bo.main_grad, acc)
+            do = K.gemm(dbr, wo.w16, b_mn=True)
+            K.gemm(dbr, o, out=wo.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+            K.colsum_(dbr, bo.main_grad, acc)
         _grads_done(wo, bo)
-        dqkv = attention_bwd(do, qkv, o_bf16, lse, *ctx.shape)
+        dqkv = attention_bwd(do, qkv, o_bf16, lse, *ctx.shape, drop=d_probs)
         if fp8 is not None:
             q8, iq = st.quantize_colsum(dqkv, tag + ".qkv_grad", F8.E5M2, bq.main_grad, acc)
             F8.gemm_fp8(q8, F8.E5M2, h, F8.E4M3, out=wq.main_grad, a_mn=True, b_mn=True, accumulate=acc,
@@ -241,7 +252,7 @@ class AttnBlockFn(Function):
             K.gemm(dqkv, h, out=wq.main_grad, a_mn=True, b_mn=True, accumulate=acc)
             dh = K.gemm(dqkv, wq.w16, b_mn=True)
         _grads_done(wq, bq)
-        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None, None
 
     @staticmethod
     def _backward_mx(ctx, dout):
@@ -252,17 +263,19 @@ class AttnBlockFn(Function):
         ln, (wq, bq), (wo, bo) = ctx.params
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
+        d_probs, d_out = ctx.drop
+        dbr = K.dropout_apply(dout, d_out) if d_out is not None else dout
         hc, oc = _mx_t(hcc, hcs, MX.E4M3), _mx_t(occ, ocs, MX.E4M3)
-        grow, gcol = MX.mx_quantize_rc(dout, MX.E5M2, colsum=bo.main_grad, accumulate=acc)
+        grow, gcol = MX.mx_quantize_rc(dbr, MX.E5M2, colsum=bo.main_grad, accumulate=acc)
         do = MX.gemm_mxfp8(grow, wo.mx[1])  # dgrad: dY (row) x W (column-wise)
         MX.gemm_mxfp8(gcol, oc, out=wo.main_grad, accumulate=acc)  # wgrad: dY^T x O, both column-wise
         _grads_done(wo, bo)
-        dqkv = attention_bwd(do, qkv, o_bf16, lse, *ctx.shape)
+        dqkv = attention_bwd(do, qkv, o_bf16, lse, *ctx.shape, drop=d_probs)
         qrow, qcol = MX.mx_quantize_rc(dqkv, MX.E5M2, colsum=bq.main_grad, accumulate=acc)
         MX.gemm_mxfp8(qcol, hc, out=wq.main_grad, accumulate=acc)
         dh = MX.gemm_mxfp8(qrow, wq.mx[1])
         _grads_done(wq, bq)
-        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None, None
 
 
 class MLPBlockFn(Function):
@@ -272,21 +285,26 @@ class MLPBlockFn(Function):
     adds the residual gradient."""
 
     @staticmethod
-    def forward(ctx, x2d, ln, params, fp8=None):
+    def forward(ctx, x2d, ln, params, fp8=None, drop=None):
+        """drop: optional (FFN-hidden dropout args, FFN-output dropout args)."""
         w1, b1, w2, b2 = params
         T, F = x2d.shape[0], w1.shape[0]
         pre = torch.empty((T, F), dtype=torch.bfloat16, device=x2d.device)
         ctx.params = (ln, params)
         ctx.fp8 = fp8
+        d_act, d_out = drop if drop is not None else (None, None)
+        ctx.drop = (d_act, d_out)
         if _mx(fp8):
             from . import mxfp8 as MX
 
             gamma, beta, eps = ln
             hr, hc, mean, rstd = MX.mx_layernorm_rc(x2d, gamma.data, beta.data, eps, MX.E4M3)
             act = torch.empty_like(pre)
-            MX.gemm_mxfp8(hr, w1.mx[0], out=pre, bias=b1.data, act=act)  # pre-activation and GELU
+            with K.gemm_dropout(d_act, 2):
+                MX.gemm_mxfp8(hr, w1.mx[0], out=pre, bias=b1.data, act=act)  # pre-activation and GELU
             ar, ac = MX.mx_quantize_rc(act, MX.E4M3)
-            out = MX.gemm_mxfp8(ar, w2.mx[0], bias=b2.data, residual=x2d)
+            with K.gemm_dropout(d_out, 1):
+                out = MX.gemm_mxfp8(ar, w2.mx[0], bias=b2.data, residual=x2d)
             ctx.save_for_backward(x2d, mean, rstd, hc.codes, hc.sf, pre, ac.codes, ac.sf)
             return out
         if fp8 is not None:
@@ -297,23 +315,28 @@ class MLPBlockFn(Function):
             if slot is not None:
                 # the FFN1 epilogue writes GELU straight as the FFN2 input's E4M3 codes
                 a8 = torch.empty((T, F), dtype=torch.uint8, device=x2d.device)
-                F8.gemm_fp8_gelu8(h8, F8.E4M3, w1.w8, F8.E4M3, pre, a8, slot[0], slot[1], F8.E4M3, bias=b1.data,
-                                  alpha=ih, alpha2=w1.w8_inv)
+                with K.gemm_dropout(d_act, 2):
+                    F8.gemm_fp8_gelu8(h8, F8.E4M3, w1.w8, F8.E4M3, pre, a8, slot[0], slot[1], F8.E4M3,
+                                      bias=b1.data, alpha=ih, alpha2=w1.w8_inv)
                 ia = slot[2]
             else:
                 act = torch.empty_like(pre)
-                F8.gemm_fp8(h8, F8.E4M3, w1.w8, F8.E4M3, out=pre, bias=b1.data, act=act, alpha=ih,
-                            alpha2=w1.w8_inv)
+                with K.gemm_dropout(d_act, 2):
+                    F8.gemm_fp8(h8, F8.E4M3, w1.w8, F8.E4M3, out=pre, bias=b1.data, act=act, alpha=ih,
+                                alpha2=w1.w8_inv)
                 a8, ia = st.quantize(act, tag + ".ffn2_in", F8.E4M3)
-            out = F8.gemm_fp8(a8, F8.E4M3, w2.w8, F8.E4M3, bias=b2.data, residual=x2d, alpha=ia,
-                              alpha2=w2.w8_inv)
+            with K.gemm_dropout(d_out, 1):
+                out = F8.gemm_fp8(a8, F8.E4M3, w2.w8, F8.E4M3, bias=b2.data, residual=x2d, alpha=ia,
+                                  alpha2=w2.w8_inv)
             h, act = h8, a8
             ctx.inv = (ih, ia)
         else:
             h, mean, rstd = _ln_fwd(x2d, ln)
             act = torch.empty_like(pre)
-            K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
-            out = K.gemm(act, w2.w16, bias=b2.data, residual=x2d)
+            with K.gemm_dropout(d_act, 2):
+                K.gemm(h, w1.w16, out=pre, bias=b1.data, act=act)
+            with K.gemm_dropout(d_out, 1):
+                out = K.gemm(act, w2.w16, bias=b2.data, residual=x2d)
         ctx.save_for_backward(x2d, mean, rstd, h, pre, act)
         return out
 
@@ -326,17 +349,21 @@ class MLPBlockFn(Function):
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
         fp8 = ctx.fp8
+        d_act, d_out = ctx.drop
+        dbr = K.dropout_apply(dout, d_out) if d_out is not None else dout
         if fp8 is not None:
             st, tag = fp8
             ih, ia = ctx.inv
-            g8, ig = st.quantize_colsum(dout, tag + ".ffn2_grad", F8.E5M2, b2.main_grad, acc)
-            dpre = F8.gemm_fp8(g8, F8.E5M2, w2.w8, F8.E4M3, b_mn=True, aux=pre, alpha=ig, alpha2=w2.w8_inv)
+            g8, ig = st.quantize_colsum(dbr, tag + ".ffn2_grad", F8.E5M2, b2.main_grad, acc)
+            with K.gemm_dropout(d_act, 3):  # the hidden dropout's mask, then dGELU
+                dpre = F8.gemm_fp8(g8, F8.E5M2, w2.w8, F8.E4M3, b_mn=True, aux=pre, alpha=ig, alpha2=w2.w8_inv)
             F8.gemm_fp8(g8, F8.E5M2, act, F8.E4M3, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc,
                         alpha=ig, alpha2=ia)
         else:
-            dpre = K.gemm(dout, w2.w16, b_mn=True, aux=pre)
-            K.gemm(dout, act, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc)
-            K.colsum_(dout, b2.main_grad, acc)
+            with K.gemm_dropout(d_act, 3):
+                dpre = K.gemm(dbr, w2.w16, b_mn=True, aux=pre)
+            K.gemm(dbr, act, out=w2.main_grad, a_mn=True, b_mn=True, accumulate=acc)
+            K.colsum_(dbr, b2.main_grad, acc)
         _grads_done(w2, b2)
         if fp8 is not None:
             p8, ip = st.quantize_colsum(dpre, tag + ".ffn1_grad", F8.E5M2, b1.main_grad, acc)
@@ -348,7 +375,7 @@ class MLPBlockFn(Function):
             K.gemm(dpre, h, out=w1.main_grad, a_mn=True, b_mn=True, accumulate=acc)
             dh = K.gemm(dpre, w1.w16, b_mn=True)
         _grads_done(w1, b1)
-        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None
 
     @staticmethod
     def _backward_mx(ctx, dout):
@@ -358,38 +385,44 @@ class MLPBlockFn(Function):
         ln, (w1, b1, w2, b2) = ctx.params
         dout = dout.contiguous()
         acc = FusedGradState.accumulate
+        d_act, d_out = ctx.drop
+        dbr = K.dropout_apply(dout, d_out) if d_out is not None else dout
         hc, ac = _mx_t(hcc, hcs, MX.E4M3), _mx_t(acc_codes, acs, MX.E4M3)
-        grow, gcol = MX.mx_quantize_rc(dout, MX.E5M2, colsum=b2.main_grad, accumulate=acc)
-        dpre = MX.gemm_mxfp8(grow, w2.mx[1], aux=pre)  # dgrad with dGELU in the epilogue
+        grow, gcol = MX.mx_quantize_rc(dbr, MX.E5M2, colsum=b2.main_grad, accumulate=acc)
+        with K.gemm_dropout(d_act, 3):
+            dpre = MX.gemm_mxfp8(grow, w2.mx[1], aux=pre)  # dgrad: hidden-dropout mask, then dGELU
         MX.gemm_mxfp8(gcol, ac, out=w2.main_grad, accumulate=acc)
         _grads_done(w2, b2)
         prow, pcol = MX.mx_quantize_rc(dpre, MX.E5M2, colsum=b1.main_grad, accumulate=acc)
         MX.gemm_mxfp8(pcol, hc, out=w1.main_grad, accumulate=acc)
         dh = MX.gemm_mxfp8(prow, w1.mx[1])
         _grads_done(w1, b1)
-        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None
+        return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None
 
 
 class EmbeddingFn(Function):
     """x = wte[ids] + wpe[pos] (reference model.rs:113-118)."""
 
     @staticmethod
-    def forward(ctx, ids, anchor, params, seq_len):
+    def forward(ctx, ids, anchor, params, seq_len, drop=None):
         wte, wpe = params
-        x = K.embed_fwd(ids.reshape(-1), wte.w16, wpe.w16, seq_len)
+        x = K.embed_fwd(ids.reshape(-1), wte.w16, wpe.w16, seq_len, drop)
         ctx.save_for_backward(ids)
         ctx.params = params
         ctx.seq_len = seq_len
+        ctx.drop = drop
         return x
 
     @staticmethod
     def backward(ctx, dx):
         (ids,) = ctx.saved_tensors
         wte, wpe = ctx.params
+        if ctx.drop is not None:
+            dx = K.dropout_apply(dx.contiguous(), ctx.drop)
         K.embed_bwd(ids.reshape(-1), dx, wte.main_grad, wpe.main_grad, ctx.seq_len,
                     FusedGradState.accumulate)
         _grads_done(wte, wpe)
-        return None, None, None, None
+        return None, None, None, None, None
 
 
 class LMHeadLossFn(Function):

@@ -63,8 +63,44 @@ def gemm_status(reset: bool = True) -> int:
     return int(_cuda().gemm_status(reset))
 
 
-def embed_fwd(ids, wte16, wpe16, seq_len: int):
-    return _cuda().embed_fwd(ids, wte16, wpe16, int(seq_len))
+def embed_fwd(ids, wte16, wpe16, seq_len: int, drop=None):
+    """drop: optional (rng, site, thr16, scale) of the embedding dropout (``DropoutState.args``)."""
+    if drop is None:
+        return _cuda().embed_fwd(ids, wte16, wpe16, int(seq_len))
+    rng, site, thr, scale = drop
+    return _cuda().embed_fwd(ids, wte16, wpe16, int(seq_len), rng, int(site), int(thr), float(scale))
+
+
+def dropout_apply(x, drop, out=None):
+    """x * keep * scale with the site's Philox mask (the backward of a dropout); bf16."""
+    rng, site, thr, scale = drop
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    _cuda().dropout_apply(x, out, rng, int(site), int(thr), float(scale))
+    return out
+
+
+class gemm_dropout:
+    """``with gemm_dropout(drop, mode): <one GEMM call>`` -- dropout drawn in that GEMM's
+    epilogue (drop = (rng, site, thr16, scale) or None for none): mode 1 drops the result
+    before the residual add, 2 drops the GELU output, 3 masks the incoming gradient before
+    the dGELU.  The setting is consumed by the next GEMM launch and cleared on exit in
+    any case, so it never leaks into a later GEMM."""
+
+    def __init__(self, drop, mode: int):
+        self.drop, self.mode = drop, mode
+
+    def __enter__(self):
+        if self.drop is not None:
+            rng, site, thr, scale = self.drop
+            _cuda().gemm_set_dropout(rng, int(site), int(thr), float(scale), int(self.mode))
+        return self
+
+    def __exit__(self, *exc):
+        if self.drop is not None:
+            _cuda().gemm_set_dropout(None, 0, 0, 1.0, 0)
+        return False
 
 
 def embed_bwd(ids, dy, dwte, dwpe, seq_len: int, accumulate: bool):

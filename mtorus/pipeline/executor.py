@@ -81,6 +81,9 @@ class DistributedPipelineExecutor:
                 forward (e.g. one per layer); ``Selective`` checkpointing splits
                 it at the midpoint.  Default: the children of an
                 ``nn.Sequential`` module, else the single stage forward
+    pre_forward called as pre_forward(microbatch) before each forward (e.g. to select
+                the micro-batch's dropout masks; a recomputing backward is preceded
+                by pre_backward, which can do the same)
     pre_backward  called as pre_backward(microbatch, k) before the k-th backward of
                 the step (k = 0 .. M-1), e.g. to switch gradient accumulation on
                 after the first micro-batch or to arm the data-parallel reducer on
@@ -109,7 +112,8 @@ class DistributedPipelineExecutor:
                  stage_fn: Optional[Callable] = None, pre_backward: Optional[Callable[[int, int], None]] = None,
                  grad_group=None, sync_losses: bool = True, timed: bool = False,
                  stage_segments: Optional[Sequence[Callable]] = None, wire: str = "native",
-                 wire_act_fmt: int = W.E4M3, wire_grad_fmt: int = W.E5M2):
+                 wire_act_fmt: int = W.E4M3, wire_grad_fmt: int = W.E5M2,
+                 pre_forward: Optional[Callable[[int], None]] = None):
         if wire not in ("native", "fp8"):
             raise ValueError(f"wire must be 'native' or 'fp8', not {wire!r}")
         self.wire = wire
@@ -140,6 +144,7 @@ class DistributedPipelineExecutor:
         if checkpoint is CheckpointStrategy.Selective and len(self.segments) < 2:
             self.checkpoint = CheckpointStrategy.Full
         self.pre_backward = pre_backward
+        self.pre_forward = pre_forward
         self.sync_losses = sync_losses
         self.timed = timed and self.device.type == "cuda"
         self.program = rank_program(schedule_type, self.stage, self.S, self.M)
@@ -272,6 +277,8 @@ class DistributedPipelineExecutor:
                     ev0 = torch.cuda.Event(enable_timing=True)
                     ev0.record()
             if op.kind == K.Forward:
+                if self.pre_forward is not None:
+                    self.pre_forward(m)
                 x = inputs[m] if self.is_first else recv_act.pop(m)
                 if not self.is_first:
                     x.requires_grad_(True)

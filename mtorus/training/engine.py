@@ -23,23 +23,12 @@ from ..ops.fused import FusedGradState
 from .fused_optim import DeviceLossScaleConfig, FusedAdam
 
 
-def require_no_dropout(config) -> None:
-    """The fused GPU blocks have no dropout (the reference applies p = 0.1 at four sites,
-    examples/gpt-1b/src/transformer.rs:77,108,148,154 and model.rs:118); reject a config
-    that asks for it instead of silently training without it.  The reference-semantics
-    model (``GptModel.forward``) keeps dropout."""
-    if getattr(config, "dropout", 0.0) > 0.0:
-        raise ValueError(f"the fused trainers run without dropout; this config asks for dropout={config.dropout} "
-                         "(use dropout=0.0, or the reference-semantics GptModel.forward path)")
-
-
 class GptTrainer:
     def __init__(self, config: GptConfig, device="cuda", lr: float = 3e-4, init: str = "normal",
                  seed: int = 0, dp_group=None, dp: str = "nccl", bucket_mb: float = 25.0,
                  loss_scale: Optional[DeviceLossScaleConfig] = None, max_grad_norm: float = 0.0,
                  weight_decay: float = 0.0, warmup_steps: int = 0, fp8: bool = False,
                  fp8_history: int = 16, fp8_recipe: str = "tensor"):
-        require_no_dropout(config)
         self.config = config
         self.device = torch.device(device)
         torch.manual_seed(seed)
@@ -52,6 +41,10 @@ class GptTrainer:
         multi = dp_group is not None or (torch.distributed.is_initialized() and torch.distributed.get_world_size() > 1)
         self.dp = dp if multi else "none"
         self.flat = self.model.flatten(self.device, symmetric=self.dp == "symm", group=dp_group)
+        # the reference GPT's dropout (p = config.dropout at its five sites), drawn in the kernels;
+        # ranks draw different masks (the seed folds in the data-parallel rank)
+        dp_rank = torch.distributed.get_rank(dp_group) if multi else 0
+        self.model.enable_dropout(seed * 1000003 + dp_rank)
         self.lr = lr
         self.warmup_steps = warmup_steps
         self.global_step = 0
@@ -108,7 +101,10 @@ class GptTrainer:
             self.reducer.begin_step()
         gs = self.opt.loss_scale_tensor / k
         total = None
+        ds = self.model.dropout_state
         for i, (ids, tgt) in enumerate(zip(ids_list, targets_list)):
+            if ds is not None:
+                ds.micro = i
             FusedGradState.accumulate = i > 0
             last = i == k - 1
             FusedGradState.grad_ready_hook = self.reducer.on_ready if (last and self.reducer is not None) else None
@@ -122,6 +118,9 @@ class GptTrainer:
         self.opt.step(self.current_lr())
         if self.fp8:
             self.model.fp8_state.end_step()
+        if ds is not None:
+            ds.micro = 0
+            ds.advance()
         self.global_step += 1
         return total / k
 
@@ -148,6 +147,8 @@ class GptTrainer:
         opt.step(self.current_lr())
         if self.fp8:
             self.model.fp8_state.end_step()
+        if self.model.dropout_state is not None:
+            self.model.dropout_state.advance()  # next step's masks (on the device: graph-safe)
         self.global_step += 1
         return loss.detach()
 
@@ -160,6 +161,8 @@ class GptTrainer:
              "opt": {"m": opt.m.detach().cpu(), "v": opt.v.detach().cpu(), "state": opt.state.detach().cpu()}}
         if self.fp8:
             d["fp8_state"] = self.model.fp8_state.state_dict()
+        if self.model.dropout_state is not None:
+            d["dropout_rng"] = self.model.dropout_state.rng.detach().cpu()
         return d
 
     @torch.no_grad()
@@ -174,6 +177,10 @@ class GptTrainer:
         self.opt.state.copy_(d["opt"]["state"].to(self.device))
         if self.fp8:
             self.model.fp8_state.load_state_dict(d["fp8_state"])
+        if self.model.dropout_state is not None and "dropout_rng" in d:
+            ds = self.model.dropout_state
+            ds.rng.copy_(d["dropout_rng"].to(ds.rng.device))
+            ds.step = (int(d["dropout_rng"][2]) & 0xFFFFFFFF) | ((int(d["dropout_rng"][3]) & 0xFFFFFFFF) << 32)
         self.global_step = int(d["global_step"])
 
     def _local_optimizer(self) -> FusedAdam:
@@ -214,6 +221,8 @@ class GptTrainer:
         self.global_step = step0  # capture records, it does not run a step
         if self.fp8:
             self.model.fp8_state.cursor = cursor0
+        if self.model.dropout_state is not None:
+            self.model.dropout_state.step -= 1
         n = int(_cuda().launch_count() - lc0)
         if not hasattr(self, "_graphs"):
             self._graphs = {}
@@ -233,6 +242,8 @@ class GptTrainer:
         if self.fp8:
             st = self.model.fp8_state
             st.cursor = (st.cursor + 1) % st.history
+        if self.model.dropout_state is not None:
+            self.model.dropout_state.step += 1
         return loss
 
     def train_step(self, input_ids: torch.Tensor, targets: torch.Tensor) -> float:

@@ -119,9 +119,6 @@ class PipelineTrainer:
                  bucket_mb: float = 25.0, loss_scale: Optional[DeviceLossScaleConfig] = None,
                  max_grad_norm: float = 0.0, timed: bool = False, split: str = "balanced",
                  fp8_recipe: str = "tensor", dp_mode: str = "nccl", wire: str = "native"):
-        from .engine import require_no_dropout
-
-        require_no_dropout(config)
         world = dist.get_world_size()
         if world != dp * pp:
             raise ValueError(f"world size {world} != dp {dp} x pp {pp}")
@@ -168,6 +165,9 @@ class PipelineTrainer:
         self.dp_mode = dp_mode if dp > 1 else "none"
         symm = self.dp_mode == "symm"
         self.flat = self.model.flatten(self.device, symmetric=symm, group=self.dp_group if symm else None)
+        # the reference GPT's dropout in the kernels; replicas draw different masks, stages
+        # differ by their layers' site ids
+        self.model.enable_dropout(seed * 1000003 + self.replica)
         self.fp8 = fp8
         if fp8:
             st = self.model.enable_fp8(fp8_history, recipe=fp8_recipe)
@@ -205,7 +205,7 @@ class PipelineTrainer:
             loss_fn=loss_fn, act_shape=(b * S, config.d_model), act_dtype=torch.bfloat16, device=self.device,
             group=self.pipe_group, grad_group=self.grad_group, stage_fn=stage_fn,
             pre_backward=self._pre_backward, sync_losses=False, timed=timed,
-            stage_segments=self.model.fused_stage_segments(b, S), wire=wire)
+            stage_segments=self.model.fused_stage_segments(b, S), wire=wire, pre_forward=self._pre_forward)
         self.schedule = schedule
         self.global_step = 0
         self._loss_host = torch.empty((), dtype=torch.float32).pin_memory()
@@ -257,7 +257,12 @@ class PipelineTrainer:
         """(S-1)/(M+S-1) for both schedules (the reference's formula)."""
         return ideal_bubble_fraction(self.pp, self.M)
 
+    def _pre_forward(self, m: int) -> None:
+        if self.model.dropout_state is not None:
+            self.model.dropout_state.micro = m
+
     def _pre_backward(self, m: int, k: int) -> None:
+        self._pre_forward(m)  # a recomputed forward draws micro-batch m's masks again
         FusedGradState.accumulate = k > 0
         last = k == self.M - 1
         FusedGradState.grad_ready_hook = self.reducer.on_ready if (last and self.reducer is not None) else None
@@ -358,6 +363,9 @@ class PipelineTrainer:
         self.opt.update()
         if self.fp8:
             self.model.fp8_state.end_step()
+        if self.model.dropout_state is not None:
+            self.model.dropout_state.micro = 0
+            self.model.dropout_state.advance()
         self.global_step += 1
 
     def train_step(self, ids_host: Optional[torch.Tensor], targets_host: Optional[torch.Tensor]) -> Optional[float]:

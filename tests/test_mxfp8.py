@@ -156,6 +156,23 @@ def test_block_scaled_gemm_matches_fp32_oracle(shape, fmts):
 
 
 @pytest.mark.gpu
+def test_block_scaled_gemm_both_operands_blocky():
+    """Block exponents spread over 2^-20..2^20 in A and B: every B row's scales (the
+    CTA pair's 256 rows live in two scale atoms per CTA) must reach the right rows."""
+    M, N, K = 512, 768, 512
+    xa = (_blocky(M, K, seed=11) * 1e-4).to(torch.bfloat16)
+    xb = (_blocky(N, K, seed=12) * 1e-4).to(torch.bfloat16)
+    a, b = mx_quantize(xa.cuda(), E4M3), mx_quantize(xb.cuda(), E4M3)
+    ref = gemm_mxfp8_ref(MxTensor(a.codes.cpu(), a.sf.cpu(), a.fmt), MxTensor(b.codes.cpu(), b.sf.cpu(), b.fmt))
+    da = mx_dequantize(MxTensor(a.codes.cpu(), a.sf.cpu(), a.fmt)).double()
+    db = mx_dequantize(MxTensor(b.codes.cpu(), b.sf.cpu(), b.fmt)).double()
+    mag = (da.abs() @ db.abs().t()).float()
+    out = gemm_mxfp8(a, b, out_dtype=torch.float32)
+    err = (out.cpu() - ref).abs()
+    assert bool((err <= 1e-5 * mag + 1e-30).all()), float((err / mag.clamp_min(1e-30)).max())
+
+
+@pytest.mark.gpu
 def test_block_scaled_gemm_agrees_with_cublas_mx():
     """cuBLAS MX GEMM (torch._scaled_mm with e8m0 scales) reads the same scale layout."""
     M, N, K = 512, 768, 1024

@@ -398,9 +398,17 @@ def test_metrics_logger_jsonl_and_summary(tmp_path):
     assert s["total_steps"] == 2 and s["avg_loss"] == 6.0 and s["overflow_count"] == 1
 
 
-def test_fused_trainers_reject_dropout():
-    from mtorus.models.gpt import GptConfig
-    from mtorus.training.engine import GptTrainer
+def test_fused_model_builds_the_reference_dropout_state():
+    """The reference config's p = 0.1 gives the fused path a Philox dropout state (the
+    GPU tests in test_dropout.py check the masks); p = 0 gives none."""
+    from mtorus.models.gpt import GptConfig, GptModel
 
-    with pytest.raises(ValueError, match="dropout"):
-        GptTrainer(GptConfig.gpt_1b(), device="cpu")  # the reference config has dropout 0.1
+    cfg = GptConfig(vocab_size=64, d_model=32, num_layers=1, num_heads=2, d_ff=64, max_seq_len=16, dropout=0.1)
+    m = GptModel(cfg)
+    m.flatten("cpu")
+    st = m.enable_dropout(seed=4)
+    assert st is not None and st.p == 0.1 and st.thr16 == 6554
+    cfg.dropout = 0.0
+    m2 = GptModel(cfg)
+    m2.flatten("cpu")
+    assert m2.enable_dropout() is None
