@@ -50,7 +50,7 @@ def main() -> int:
                     help="override layer count (debug only; the metric is defined for 24)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
-                    help="replay the whole step as one CUDA graph (dp none / nccl); auto: on for 1 GPU")
+                    help="replay the whole step as one CUDA graph (any --dp); auto: on for 1 GPU")
     ap.add_argument("--precision", default="mxfp8", choices=["mxfp8", "fp8", "bf16"],
                     help="mxfp8 (default): E4M3 / E5M2 with one UE8M0 scale per 1x32 block in every "
                          "transformer-layer GEMM (block-scaled tcgen05 GEMMs); fp8: the same formats with one "
@@ -114,7 +114,7 @@ def main() -> int:
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    use_graph = (args.graph == "on" or (args.graph == "auto" and world == 1)) and trainer.dp in ("none", "nccl")
+    use_graph = args.graph == "on" or (args.graph == "auto" and world == 1)
     if use_graph:
         torch.cuda.empty_cache()
         trainer.capture(dev_ids[0], dev_tgt[0])

@@ -11,7 +11,7 @@ std::vector<at::Tensor> layernorm_fwd_fp8(const at::Tensor& x, const at::Tensor&
                                           double eps, at::Tensor y8, const at::Tensor& scale, at::Tensor amax,
                                           int64_t fmt, const c10::optional<at::Tensor>& counter,
                                           const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
-                                          int64_t slot, int64_t parity, int64_t epoch);
+                                          int64_t slot, int64_t parity, int64_t epoch, int64_t ep_ptr);
 at::Tensor layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& gamma,
                          const at::Tensor& mean, const at::Tensor& rstd, at::Tensor dgamma,
                          at::Tensor dbeta, bool accumulate, const c10::optional<at::Tensor>& dres);
@@ -70,7 +70,8 @@ void dp_quant_e5m2(int64_t grad, int64_t codes, int64_t sf, int64_t nelem);
 void dp_decode_mean_e5m2(const at::Tensor& codes, const at::Tensor& sf, at::Tensor out);
 void symm_rs_bucket_e5m2(const std::vector<int64_t>& codes, const std::vector<int64_t>& sfs,
                          const std::vector<int64_t>& flags, int64_t me, int64_t start, int64_t len, int64_t clen,
-                         int64_t slot, int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t mine);
+                         int64_t slot, int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t mine,
+                         int64_t ep_ptr);
 void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at::Tensor& beta, double eps,
                          at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, at::Tensor mean,
                          at::Tensor rstd, int64_t fmt, double fmax);
@@ -95,13 +96,15 @@ void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::T
 void fp8_amax(const at::Tensor& x, at::Tensor amax);
 void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
                      at::Tensor counter, const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
-                     int64_t slot, int64_t parity, int64_t epoch, int64_t fmt);
+                     int64_t slot, int64_t parity, int64_t epoch, int64_t fmt, int64_t ep_ptr);
 void fp8_amax_gather(const at::Tensor& table, at::Tensor amax, int64_t world, int64_t cap, int64_t parity,
-                     int64_t epoch);
+                     int64_t epoch, int64_t ep_ptr);
+void fp8_amax_publish(const at::Tensor& amax, const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
+                      int64_t parity, int64_t epoch, int64_t ep_ptr);
 void fp8_quantize_colsum(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
                          at::Tensor colsum, bool accumulate, const c10::optional<at::Tensor>& counter,
                          const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap, int64_t slot,
-                         int64_t parity, int64_t epoch, int64_t fmt);
+                         int64_t parity, int64_t epoch, int64_t fmt, int64_t ep_ptr);
 void fp8_scaling_update(at::Tensor hist, at::Tensor amax, at::Tensor scale, at::Tensor inv,
                         const at::Tensor& fmax, int64_t cursor, bool current,
                         const c10::optional<at::Tensor>& cursor_dev);
@@ -112,17 +115,18 @@ void fp8_quantize_blocks(const at::Tensor& x, at::Tensor out, at::Tensor scales,
 int64_t symm_status(bool reset);
 void symm_rs_bucket(const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
                     int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot,
-                    int64_t epoch, at::Tensor st, int64_t ctas, double inv_n);
+                    int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t ep_ptr);
 void symm_rs_bucket_mc(int64_t grads_mc, const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
                        int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot, int64_t epoch,
-                       at::Tensor st, int64_t ctas, double inv_n);
+                       at::Tensor st, int64_t ctas, double inv_n, int64_t ep_ptr);
 void symm_scalars_ar(const std::vector<int64_t>& scal, const std::vector<int64_t>& flags,
-                     int64_t me, int64_t slot, int64_t epoch, at::Tensor st);
+                     int64_t me, int64_t slot, int64_t epoch, at::Tensor st, int64_t ep_ptr);
+void symm_epoch_advance(at::Tensor ep);
 void symm_adam_shard_ag(const at::Tensor& ranges, at::Tensor master, at::Tensor m, at::Tensor v,
                         const at::Tensor& grad, const std::vector<int64_t>& w16, const at::Tensor& st,
                         double lr, double beta1, double beta2, double eps, double wd);
 void symm_barrier(const std::vector<int64_t>& flags, int64_t me, int64_t slot, int64_t epoch,
-                  int64_t code);
+                  int64_t code, int64_t ep_ptr);
 void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t me,
                     int64_t numel, int64_t dtype, int64_t slot, int64_t epoch, int64_t ctas);
 void symm_allgather(int64_t src, const std::vector<int64_t>& dst, int64_t me, int64_t bytes,
@@ -191,11 +195,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_dequantize", &fp8_dequantize);
   m.def("fp8_quantize_blocks", &fp8_quantize_blocks);
   m.def("symm_status", &symm_status, py::arg("reset") = true);
-  m.def("symm_rs_bucket", &symm_rs_bucket);
-  m.def("symm_rs_bucket_mc", &symm_rs_bucket_mc);
-  m.def("symm_scalars_ar", &symm_scalars_ar);
+  // ep_ptr: address of a device-resident uint32 step counter added to `epoch` in the
+  // kernels (0: none), which lets a captured CUDA graph replay with fresh epochs
+  m.def("symm_rs_bucket", &symm_rs_bucket, py::arg("grads"), py::arg("flags"), py::arg("me"), py::arg("start"),
+        py::arg("len"), py::arg("clen"), py::arg("slot"), py::arg("epoch"), py::arg("st"), py::arg("ctas"),
+        py::arg("inv_n"), py::arg("ep_ptr") = 0);
+  m.def("symm_rs_bucket_mc", &symm_rs_bucket_mc, py::arg("grads_mc"), py::arg("grads"), py::arg("flags"),
+        py::arg("me"), py::arg("start"), py::arg("len"), py::arg("clen"), py::arg("slot"), py::arg("epoch"),
+        py::arg("st"), py::arg("ctas"), py::arg("inv_n"), py::arg("ep_ptr") = 0);
+  m.def("symm_scalars_ar", &symm_scalars_ar, py::arg("scal"), py::arg("flags"), py::arg("me"), py::arg("slot"),
+        py::arg("epoch"), py::arg("st"), py::arg("ep_ptr") = 0);
   m.def("symm_adam_shard_ag", &symm_adam_shard_ag);
-  m.def("symm_barrier", &symm_barrier);
+  m.def("symm_barrier", &symm_barrier, py::arg("flags"), py::arg("me"), py::arg("slot"), py::arg("epoch"),
+        py::arg("code"), py::arg("ep_ptr") = 0);
+  m.def("symm_epoch_advance", &symm_epoch_advance);
   m.def("symm_allreduce", &symm_allreduce);
   m.def("symm_allgather", &symm_allgather);
   m.def("symm_broadcast", &symm_broadcast);
@@ -213,8 +226,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("install_segv_handler", &install_segv_handler);
   m.def("wait_flag", &wait_flag);
   m.def("launch_count", []() { return mtorus::launch_counter(); });
-  m.def("fp8_quantize_ar", &fp8_quantize_ar);
-  m.def("layernorm_fwd_fp8", &layernorm_fwd_fp8);
+  m.def("fp8_quantize_ar", &fp8_quantize_ar, py::arg("x"), py::arg("out"), py::arg("scale"), py::arg("amax"),
+        py::arg("counter"), py::arg("table_ptrs"), py::arg("me"), py::arg("cap"), py::arg("slot"), py::arg("parity"),
+        py::arg("epoch"), py::arg("fmt"), py::arg("ep_ptr") = 0);
+  m.def("layernorm_fwd_fp8", &layernorm_fwd_fp8, py::arg("x"), py::arg("gamma"), py::arg("beta"), py::arg("eps"),
+        py::arg("y8"), py::arg("scale"), py::arg("amax"), py::arg("fmt"), py::arg("counter"), py::arg("table_ptrs"),
+        py::arg("me"), py::arg("cap"), py::arg("slot"), py::arg("parity"), py::arg("epoch"), py::arg("ep_ptr") = 0);
   m.def("gemm_fp8_act8", &gemm_fp8_act8);
   m.def("gemm_mxfp8", &gemm_mxfp8, py::arg("A"), py::arg("a_fmt"), py::arg("sfa"), py::arg("B"), py::arg("b_fmt"),
         py::arg("sfb"), py::arg("D"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
@@ -224,7 +241,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("copy_async", &copy_async);
   m.def("dp_quant_e5m2", &dp_quant_e5m2);
   m.def("dp_decode_mean_e5m2", &dp_decode_mean_e5m2);
-  m.def("symm_rs_bucket_e5m2", &symm_rs_bucket_e5m2);
+  m.def("symm_rs_bucket_e5m2", &symm_rs_bucket_e5m2, py::arg("codes"), py::arg("sfs"), py::arg("flags"),
+        py::arg("me"), py::arg("start"), py::arg("len"), py::arg("clen"), py::arg("slot"), py::arg("epoch"),
+        py::arg("st"), py::arg("ctas"), py::arg("inv_n"), py::arg("mine"), py::arg("ep_ptr") = 0);
   m.def("layernorm_fwd_mx_rc", &layernorm_fwd_mx_rc);
   m.def("mx_quantize_rc", &mx_quantize_rc, py::arg("x"), py::arg("rc"), py::arg("rsf"), py::arg("cc"),
         py::arg("csf"), py::arg("fmt"), py::arg("fmax"), py::arg("colsum") = py::none());
@@ -233,8 +252,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("act") = py::none(),
         py::arg("aux") = py::none(), py::arg("alpha") = py::none(), py::arg("alpha2") = py::none(),
         py::arg("beta") = false);
-  m.def("fp8_amax_gather", &fp8_amax_gather);
-  m.def("fp8_quantize_colsum", &fp8_quantize_colsum);
+  m.def("fp8_amax_gather", &fp8_amax_gather, py::arg("table"), py::arg("amax"), py::arg("world"), py::arg("cap"),
+        py::arg("parity"), py::arg("epoch"), py::arg("ep_ptr") = 0);
+  m.def("fp8_amax_publish", &fp8_amax_publish, py::arg("amax"), py::arg("table_ptrs"), py::arg("me"), py::arg("cap"),
+        py::arg("parity"), py::arg("epoch"), py::arg("ep_ptr") = 0);
+  m.def("fp8_quantize_colsum", &fp8_quantize_colsum, py::arg("x"), py::arg("out"), py::arg("scale"), py::arg("amax"),
+        py::arg("colsum"), py::arg("accumulate"), py::arg("counter"), py::arg("table_ptrs"), py::arg("me"),
+        py::arg("cap"), py::arg("slot"), py::arg("parity"), py::arg("epoch"), py::arg("fmt"), py::arg("ep_ptr") = 0);
   m.def("attn_fwd", &attn_fwd, py::arg("qkv"), py::arg("B"), py::arg("S"), py::arg("H"),
         py::arg("drop_rng") = py::none(), py::arg("drop_site") = 0, py::arg("drop_thr16") = 0,
         py::arg("drop_scale") = 1.0);

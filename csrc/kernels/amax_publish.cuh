@@ -29,6 +29,10 @@ __device__ __forceinline__ uint16_t cvt2_e5m2(float a, float b) {
 constexpr int kAmaxMaxPeers = 8;
 struct AmaxPeers {
   uint64_t p[kAmaxMaxPeers];
+  // device-resident step counter (nullptr: none).  When set, the stamp is
+  // epoch + *ep and the parity its low bit, so a captured CUDA graph replays
+  // with a new stamp every step.
+  const unsigned int* ep;
 };
 
 // Block amax -> the slot's running amax (atomic); with a counter, the grid's last
@@ -48,6 +52,10 @@ __device__ __forceinline__ void publish_amax(float m, float* amax, unsigned int*
   if (!*last) return;
   if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch on this slot
   if (threadIdx.x < world) {
+    if (table.ep) {
+      epoch += *reinterpret_cast<const volatile unsigned int*>(table.ep);
+      parity = (int)(epoch & 1u);
+    }
     const float a = *reinterpret_cast<volatile float*>(amax);
     const unsigned long long v = ((unsigned long long)epoch << 32) | __float_as_uint(a);
     unsigned long long* t = reinterpret_cast<unsigned long long*>(table.p[threadIdx.x]) +

@@ -167,11 +167,17 @@ __global__ void __launch_bounds__(256) fp8_quantize_ar_kernel(const bf16* __rest
   publish_amax(m, amax, counter, table, me, world, cap, slot, parity, epoch, &last);
 }
 
-// amax[s] = max over ranks r of table[parity][r][s] entries stamped with `epoch`.
+// amax[s] = max over ranks r of table[parity][r][s] entries stamped with `epoch`
+// (plus *ep when a device step counter is given; parity is then its low bit).
 __global__ void fp8_amax_gather_kernel(const unsigned long long* __restrict__ table, float* __restrict__ amax,
-                                       int slots, int world, int cap, int parity, unsigned int epoch) {
+                                       int slots, int world, int cap, int parity, unsigned int epoch,
+                                       const unsigned int* ep) {
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= slots) return;
+  if (ep) {
+    epoch += *ep;
+    parity = (int)(epoch & 1u);
+  }
   float m = amax[s];
   for (int r = 0; r < world; ++r) {
     const unsigned long long v =
@@ -497,7 +503,7 @@ void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::T
 // Quantise with the fused amax all-reduce: see fp8_quantize_ar_kernel.
 void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
                      at::Tensor counter, const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
-                     int64_t slot, int64_t parity, int64_t epoch, int64_t fmt) {
+                     int64_t slot, int64_t parity, int64_t epoch, int64_t fmt, int64_t ep_ptr) {
   MT_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "fp8_quantize_ar: contiguous bf16 input");
   MT_CHECK(out.element_size() == 1 && out.is_contiguous() && out.numel() == x.numel(), "fp8_quantize_ar: out");
   MT_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
@@ -508,6 +514,7 @@ void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scal
   MT_CHECK(world >= 1 && world <= kAmaxMaxPeers, "fp8_quantize_ar: 1..8 ranks");
   AmaxPeers t{};
   for (int i = 0; i < world; ++i) t.p[i] = (uint64_t)table_ptrs[i];
+  t.ep = reinterpret_cast<const unsigned int*>(ep_ptr);
   const size_t n = x.numel();
   if (n == 0) return;
   const auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
@@ -529,7 +536,7 @@ void fp8_quantize_ar(const at::Tensor& x, at::Tensor out, const at::Tensor& scal
 void fp8_quantize_colsum(const at::Tensor& x, at::Tensor out, const at::Tensor& scale, at::Tensor amax,
                          at::Tensor colsum, bool accumulate, const c10::optional<at::Tensor>& counter,
                          const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap, int64_t slot,
-                         int64_t parity, int64_t epoch, int64_t fmt) {
+                         int64_t parity, int64_t epoch, int64_t fmt, int64_t ep_ptr) {
   MT_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() >= 1, "fp8_quantize_colsum: bf16 x");
   const int F = x.size(-1);
   const int rows = x.numel() / std::max(F, 1);
@@ -545,6 +552,7 @@ void fp8_quantize_colsum(const at::Tensor& x, at::Tensor out, const at::Tensor& 
   MT_CHECK(world <= kAmaxMaxPeers && (world == 0 || counter.has_value()), "fp8_quantize_colsum: peers");
   AmaxPeers t{};
   for (int i = 0; i < world; ++i) t.p[i] = (uint64_t)table_ptrs[i];
+  t.ep = reinterpret_cast<const unsigned int*>(ep_ptr);
   unsigned int* cp = world ? reinterpret_cast<unsigned int*>(counter->data_ptr()) : nullptr;
   const int col_blocks = (F + 255) / 256;
   int row_blocks = std::max(1, std::min((rows + 63) / 64, (num_sms() * 8 + col_blocks - 1) / col_blocks));
@@ -565,13 +573,48 @@ void fp8_quantize_colsum(const at::Tensor& x, at::Tensor out, const at::Tensor& 
 }
 
 void fp8_amax_gather(const at::Tensor& table, at::Tensor amax, int64_t world, int64_t cap, int64_t parity,
-                     int64_t epoch) {
+                     int64_t epoch, int64_t ep_ptr) {
   const int slots = amax.numel();
   if (slots == 0) return;
   MT_CHECK(table.element_size() == 8 && table.numel() >= 2 * world * cap, "fp8_amax_gather: table");
   fp8_amax_gather_kernel<<<(slots + 127) / 128, 128, 0, cur_stream()>>>(
       reinterpret_cast<const unsigned long long*>(table.data_ptr()), amax.data_ptr<float>(), slots, (int)world,
-      (int)cap, (int)parity, (unsigned int)epoch);
+      (int)cap, (int)parity, (unsigned int)epoch, reinterpret_cast<const unsigned int*>(ep_ptr));
+  MT_LAUNCH_CHECK();
+}
+
+// Store amax[s] (this rank's running amax of slot s, s < slots) into every peer's
+// table with this step's stamp: the publication for roles whose FP8 codes come
+// from a producer that does not publish itself (a GEMM epilogue writing codes).
+__global__ void fp8_amax_publish_kernel(const float* __restrict__ amax, AmaxPeers table, int me, int world, int cap,
+                                        int slots, int parity, unsigned int epoch) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= slots) return;
+  if (table.ep) {
+    epoch += *table.ep;
+    parity = (int)(epoch & 1u);
+  }
+  const unsigned long long v = ((unsigned long long)epoch << 32) | __float_as_uint(amax[s]);
+  for (int r = 0; r < world; ++r) {
+    unsigned long long* t = reinterpret_cast<unsigned long long*>(table.p[r]) + ((size_t)parity * world + me) * cap + s;
+    *reinterpret_cast<volatile unsigned long long*>(t) = v;
+  }
+  __threadfence_system();
+}
+
+void fp8_amax_publish(const at::Tensor& amax, const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
+                      int64_t parity, int64_t epoch, int64_t ep_ptr) {
+  const int slots = amax.numel();
+  const int world = (int)table_ptrs.size();
+  MT_CHECK(world >= 1 && world <= kAmaxMaxPeers && slots <= cap, "fp8_amax_publish: 1..8 ranks, slots <= cap");
+  MT_CHECK(amax.scalar_type() == at::kFloat && amax.is_contiguous(), "fp8_amax_publish: fp32 amax");
+  if (slots == 0) return;
+  AmaxPeers t{};
+  for (int i = 0; i < world; ++i) t.p[i] = (uint64_t)table_ptrs[i];
+  t.ep = reinterpret_cast<const unsigned int*>(ep_ptr);
+  fp8_amax_publish_kernel<<<(slots + 127) / 128, 128, 0, cur_stream()>>>(amax.data_ptr<float>(), t, (int)me, world,
+                                                                          (int)cap, slots, (int)parity,
+                                                                          (unsigned int)epoch);
   MT_LAUNCH_CHECK();
 }
 

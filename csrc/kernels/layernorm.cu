@@ -487,7 +487,7 @@ std::vector<at::Tensor> layernorm_fwd_fp8(const at::Tensor& x, const at::Tensor&
                                           double eps, at::Tensor y8, const at::Tensor& scale, at::Tensor amax,
                                           int64_t fmt, const c10::optional<at::Tensor>& counter,
                                           const std::vector<int64_t>& table_ptrs, int64_t me, int64_t cap,
-                                          int64_t slot, int64_t parity, int64_t epoch) {
+                                          int64_t slot, int64_t parity, int64_t epoch, int64_t ep_ptr) {
   MT_CHECK_CUDA(x);
   MT_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "layernorm_fwd_fp8: contiguous bf16 x");
   MT_CHECK(gamma.scalar_type() == at::kFloat && beta.scalar_type() == at::kFloat, "layernorm_fwd_fp8: fp32 params");
@@ -505,6 +505,7 @@ std::vector<at::Tensor> layernorm_fwd_fp8(const at::Tensor& x, const at::Tensor&
   MT_CHECK(world <= kAmaxMaxPeers && (world == 0 || counter.has_value()), "layernorm_fwd_fp8: peers");
   AmaxPeers t{};
   for (int i = 0; i < world; ++i) t.p[i] = (uint64_t)table_ptrs[i];
+  t.ep = reinterpret_cast<const unsigned int*>(ep_ptr);
   unsigned int* cp = world ? reinterpret_cast<unsigned int*>(counter->data_ptr()) : nullptr;
   const int threads = d / 8;
   const int grid = std::min(rows, num_sms() * std::max(1, 2048 / threads));

@@ -88,14 +88,24 @@ __device__ __forceinline__ bool block_barrier(const PeerPtrs& flags, const uint3
   return ok != 0;
 }
 
+// A context's device-resident step counter: with ep set, a kernel's effective epoch
+// is the host value plus *ep, so a CUDA graph that advances the counter (one
+// epoch_advance launch per step) replays with fresh epochs.
+__device__ __forceinline__ uint32_t resolve_epoch(uint32_t epoch, const uint32_t* ep) {
+  return ep ? epoch + *reinterpret_cast<const volatile uint32_t*>(ep) : epoch;
+}
+
+__global__ void epoch_advance_kernel(uint32_t* ep) { *ep += 1u; }
+
 // ------------------------------------------------------------------ reduce-scatter
 // Bucket [start, start+len) (elements, fp32).  Chunk c = [start + c*clen, ...).
 __global__ void __launch_bounds__(512) rs_bucket_kernel(PeerPtrs grads, PeerPtrs flags,
                                                         uint32_t* my_flags, int me, int n,
                                                         int64_t start, int64_t len, int64_t clen,
                                                         int slot, uint32_t epoch, float inv_n,
-                                                        float* st, int* status) {
+                                                        float* st, int* status, const uint32_t* ep) {
   __shared__ float red[32];
+  epoch = resolve_epoch(epoch, ep);
   if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 21)) return;
   const int64_t c0 = start + (int64_t)me * clen;
   const int64_t c1 = min(start + len, c0 + clen);
@@ -155,8 +165,9 @@ __global__ void __launch_bounds__(512) rs_bucket_kernel(PeerPtrs grads, PeerPtrs
 // ------------------------------------------------------------------ scalars all-reduce
 // scal[me * 2 + k] of every peer <- st[k] (k = 0: Σg², 1: non-finite count); then sum.
 __global__ void scalars_ar_kernel(PeerPtrs scal, PeerPtrs flags, uint32_t* my_flags, int me, int n,
-                                  int slot, uint32_t epoch, float* st, int* status) {
+                                  int slot, uint32_t epoch, float* st, int* status, const uint32_t* ep) {
   if (threadIdx.x != 0) return;
+  epoch = resolve_epoch(epoch, ep);
   for (int p = 0; p < n; ++p) {
     float* d = reinterpret_cast<float*>(scal.p[p]) + me * 2;
     d[0] = st[0];
@@ -229,8 +240,9 @@ __global__ void __launch_bounds__(256) adam_shard_ag_kernel(
 
 // Signal (this rank finished writing into peers) then wait for everyone.
 __global__ void barrier_kernel(PeerPtrs flags, uint32_t* my_flags, int me, int n, int slot,
-                               uint32_t epoch, int* status, int code) {
+                               uint32_t epoch, int* status, int code, const uint32_t* ep) {
   if (threadIdx.x != 0) return;
+  epoch = resolve_epoch(epoch, ep);
   signal_peers(flags, me, n, slot, epoch);
   wait_peers(my_flags, n, slot, epoch, status, code);
 }
@@ -428,8 +440,9 @@ __global__ void __launch_bounds__(512) broadcast_mc_kernel(const uint4* __restri
 __global__ void __launch_bounds__(512) rs_bucket_mc_kernel(uint64_t grads_mc, float* mine, PeerPtrs flags,
                                                            uint32_t* my_flags, int me, int n, int64_t start,
                                                            int64_t len, int64_t clen, int slot, uint32_t epoch,
-                                                           float inv_n, float* st, int* status) {
+                                                           float inv_n, float* st, int* status, const uint32_t* ep) {
   __shared__ float red[32];
+  epoch = resolve_epoch(epoch, ep);
   if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 25)) return;
   asm volatile("fence.proxy.alias;" ::: "memory");  // peers' unicast writes, read through the multicast alias
   const int64_t c0 = start + (int64_t)me * clen;
@@ -586,8 +599,9 @@ __global__ void __launch_bounds__(512) rs_bucket_e5m2_kernel(PeerPtrs codes, Pee
                                                              uint32_t* my_flags, int me, int n, int64_t start,
                                                              int64_t len, int64_t clen, int slot, uint32_t epoch,
                                                              float inv_n, float* __restrict__ mine, float* st,
-                                                             int* status) {
+                                                             int* status, const uint32_t* ep) {
   __shared__ float red[32];
+  epoch = resolve_epoch(epoch, ep);
   if (!block_barrier(flags, my_flags, me, n, slot, epoch, blockIdx.x == 0, status, 26)) return;
   const int64_t c0 = start + (int64_t)me * clen;
   const int64_t c1 = min(start + len, c0 + clen);
@@ -673,25 +687,26 @@ int64_t symm_status(bool reset) {
 
 void symm_rs_bucket(const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
                     int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot,
-                    int64_t epoch, at::Tensor st, int64_t ctas, double inv_n) {
+                    int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t ep_ptr) {
   const int n = grads.size();
   rs_bucket_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(
       to_peers(grads), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, start,
-      len, clen, (int)slot, (uint32_t)epoch, (float)inv_n, st.data_ptr<float>(), symm_status_ptr());
+      len, clen, (int)slot, (uint32_t)epoch, (float)inv_n, st.data_ptr<float>(), symm_status_ptr(),
+      reinterpret_cast<const uint32_t*>(ep_ptr));
   MT_LAUNCH_CHECK();
 }
 
 // NVLS variant of symm_rs_bucket (grads_mc: multicast address of the gradient buffer).
 void symm_rs_bucket_mc(int64_t grads_mc, const std::vector<int64_t>& grads, const std::vector<int64_t>& flags,
                        int64_t me, int64_t start, int64_t len, int64_t clen, int64_t slot, int64_t epoch,
-                       at::Tensor st, int64_t ctas, double inv_n) {
+                       at::Tensor st, int64_t ctas, double inv_n, int64_t ep_ptr) {
   MT_CHECK(grads_mc != 0 && grads_mc % 16 == 0, "rs_bucket_mc: no multicast address");
   MT_CHECK(start % 4 == 0 && clen % 4 == 0 && len % 4 == 0, "rs_bucket_mc: 16-byte aligned bucket and chunks");
   const int n = flags.size();
   rs_bucket_mc_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(
       (uint64_t)grads_mc, reinterpret_cast<float*>(grads[me]), to_peers(flags),
       reinterpret_cast<uint32_t*>(flags[me]), (int)me, n, start, len, clen, (int)slot, (uint32_t)epoch,
-      (float)inv_n, st.data_ptr<float>(), symm_status_ptr());
+      (float)inv_n, st.data_ptr<float>(), symm_status_ptr(), reinterpret_cast<const uint32_t*>(ep_ptr));
   MT_LAUNCH_CHECK();
 }
 
@@ -716,13 +731,14 @@ void dp_quant_e5m2(int64_t grad, int64_t codes, int64_t sf, int64_t nelem) {
 // rank's fp32 gradient buffer that receives the averaged chunk.
 void symm_rs_bucket_e5m2(const std::vector<int64_t>& codes, const std::vector<int64_t>& sfs,
                          const std::vector<int64_t>& flags, int64_t me, int64_t start, int64_t len, int64_t clen,
-                         int64_t slot, int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t mine) {
+                         int64_t slot, int64_t epoch, at::Tensor st, int64_t ctas, double inv_n, int64_t mine,
+                         int64_t ep_ptr) {
   MT_CHECK(start % 32 == 0 && len % 32 == 0 && clen % 32 == 0, "rs_bucket_e5m2: 32-element aligned bucket and chunks");
   MT_CHECK(codes.size() == flags.size() && sfs.size() == flags.size(), "rs_bucket_e5m2: one buffer per rank");
   rs_bucket_e5m2_kernel<<<(int)ctas, 512, 0, cur_stream()>>>(
       to_peers(codes), to_peers(sfs), to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]), (int)me,
       (int)flags.size(), start, len, clen, (int)slot, (uint32_t)epoch, (float)inv_n, reinterpret_cast<float*>(mine),
-      st.data_ptr<float>(), symm_status_ptr());
+      st.data_ptr<float>(), symm_status_ptr(), reinterpret_cast<const uint32_t*>(ep_ptr));
   MT_LAUNCH_CHECK();
 }
 
@@ -745,11 +761,12 @@ void dp_decode_mean_e5m2(const at::Tensor& codes, const at::Tensor& sf, at::Tens
 }
 
 void symm_scalars_ar(const std::vector<int64_t>& scal, const std::vector<int64_t>& flags,
-                     int64_t me, int64_t slot, int64_t epoch, at::Tensor st) {
+                     int64_t me, int64_t slot, int64_t epoch, at::Tensor st, int64_t ep_ptr) {
   scalars_ar_kernel<<<1, 32, 0, cur_stream()>>>(to_peers(scal), to_peers(flags),
                                                 reinterpret_cast<uint32_t*>(flags[me]), (int)me,
                                                 (int)scal.size(), (int)slot, (uint32_t)epoch,
-                                                st.data_ptr<float>(), symm_status_ptr());
+                                                st.data_ptr<float>(), symm_status_ptr(),
+                                                reinterpret_cast<const uint32_t*>(ep_ptr));
   MT_LAUNCH_CHECK();
 }
 
@@ -778,10 +795,17 @@ void copy_async(int64_t dst, int64_t src, int64_t bytes) {
 }
 
 void symm_barrier(const std::vector<int64_t>& flags, int64_t me, int64_t slot, int64_t epoch,
-                  int64_t code) {
+                  int64_t code, int64_t ep_ptr) {
   barrier_kernel<<<1, 32, 0, cur_stream()>>>(to_peers(flags), reinterpret_cast<uint32_t*>(flags[me]),
                                              (int)me, (int)flags.size(), (int)slot, (uint32_t)epoch,
-                                             symm_status_ptr(), (int)code);
+                                             symm_status_ptr(), (int)code, reinterpret_cast<const uint32_t*>(ep_ptr));
+  MT_LAUNCH_CHECK();
+}
+
+// Advance a device-resident step counter (uint32 [1]) on the current stream.
+void symm_epoch_advance(at::Tensor ep) {
+  MT_CHECK(ep.is_cuda() && ep.element_size() == 4 && ep.numel() >= 1, "symm_epoch_advance: int32 [1] on the GPU");
+  epoch_advance_kernel<<<1, 1, 0, cur_stream()>>>(reinterpret_cast<uint32_t*>(ep.data_ptr()));
   MT_LAUNCH_CHECK();
 }
 

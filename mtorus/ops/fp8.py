@@ -109,22 +109,30 @@ class SymmAmaxSync:
         self.cap = capacity
         self.table = SymmBuffer(2 * self.world * capacity, torch.int64, device, group)
         self.counters = torch.zeros(capacity, dtype=torch.int32, device=device)
+        # stamps are 1 + the context's device step counter (advanced at the end of
+        # every reduce, on the stream): graph replays publish with fresh stamps
         self.epoch = 1
+        self.ep_ptr = self.ctx.ep_ptr
         self.table.barrier()
 
     def quantize(self, x, out, scale, amax, slot, fmt):
         _cuda().fp8_quantize_ar(x.contiguous(), out, scale, amax, self.counters[slot:slot + 1], self.table.ptrs,
-                                self.me, self.cap, slot, self.epoch & 1, self.epoch, int(fmt))
+                                self.me, self.cap, slot, self.epoch & 1, self.epoch, int(fmt), self.ep_ptr)
 
     def publish_args(self, slot: int):
-        """(counter, table pointers, me, cap, slot, parity, epoch) for kernels that publish."""
+        """(counter, table pointers, me, cap, slot, parity, epoch) for kernels that publish;
+        pass ``ep_ptr=self.ep_ptr`` with them."""
         return (self.counters[slot:slot + 1], self.table.ptrs, self.me, self.cap, slot, self.epoch & 1, self.epoch)
 
     def reduce(self, amax: torch.Tensor) -> None:
-        # every rank has published this step's amaxes (its quantise kernels precede the barrier)
-        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 0, self.epoch, 24)
-        _cuda().fp8_amax_gather(self.table.tensor, amax, self.world, self.cap, self.epoch & 1, self.epoch)
-        self.epoch += 1
+        # roles whose codes a GEMM epilogue wrote were not published by a quantise
+        # kernel: publish every used slot's running amax (the same value for the rest)
+        _cuda().fp8_amax_publish(amax, self.table.ptrs, self.me, self.cap, self.epoch & 1, self.epoch, self.ep_ptr)
+        # every rank has published this step's amaxes (its publishing kernels precede the barrier)
+        _cuda().symm_barrier(self.ctx.flags.ptrs, self.me, 0, self.epoch, 24, self.ep_ptr)
+        _cuda().fp8_amax_gather(self.table.tensor, amax, self.world, self.cap, self.epoch & 1, self.epoch,
+                                self.ep_ptr)
+        self.ctx.advance_epoch()
 
 
 class Fp8State:
@@ -196,15 +204,17 @@ class Fp8State:
             args = self.sync.publish_args(s)
         else:
             args = (None, [], 0, self.cap, s, 0, 0)
+        ep = self.sync.ep_ptr if isinstance(self.sync, SymmAmaxSync) else 0
         _cuda().fp8_quantize_colsum(x.contiguous(), out, self.scale[sl], self.amax[sl], colsum, bool(accumulate),
-                                    *args, int(fmt))
+                                    *args, int(fmt), ep)
         return out, self.inv[sl]
 
     def epilogue_slot(self, name: str, fmt: int):
         """(scale, amax, inverse scale) views for a producer kernel that writes the
         role's FP8 codes itself, or None when it cannot: the first step (scale not
-        known yet) or a cross-rank sync that publishes from the quantise kernels."""
-        if self.first_step or isinstance(self.sync, SymmAmaxSync) or not _FUSE_GELU:
+        known yet).  Under ``SymmAmaxSync`` the role's amax is published with the
+        rest at the end of the step."""
+        if self.first_step or not _FUSE_GELU:
             return None
         s = self.slot(name, fmt)
         sl = slice(s, s + 1)
@@ -228,8 +238,9 @@ class Fp8State:
             args = self.sync.publish_args(s)
         else:
             args = (None, [], 0, self.cap, s, 0, 0)
+        ep = self.sync.ep_ptr if isinstance(self.sync, SymmAmaxSync) else 0
         mean, rstd = _cuda().layernorm_fwd_fp8(x2d.contiguous(), gamma, beta, float(eps), out, self.scale[sl],
-                                               self.amax[sl], int(fmt), *args)
+                                               self.amax[sl], int(fmt), *args, ep)
         return out, self.inv[sl], mean, rstd
 
     def quantize_into(self, x: torch.Tensor, name: str, fmt: int, out: torch.Tensor):

@@ -75,7 +75,16 @@ class SymmContext:
         self.rank = self.flags.rank
         self.world = self.flags.world
         self.num_slots = num_slots
+        # device-resident step counter: kernels given its address (ep_ptr) stamp and
+        # wait on host epoch + counter, so a CUDA graph that advances it replays
+        # every step with fresh epochs
+        self.epoch_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.ep_ptr = self.epoch_dev.data_ptr()
         self.flags.barrier()
+
+    def advance_epoch(self) -> None:
+        """+1 on the device step counter, in stream order on the current stream."""
+        _cuda().symm_epoch_advance(self.epoch_dev)
 
     def status(self, reset: bool = True) -> int:
         """Non-zero when a fused kernel gave up waiting for a peer (its wait code)."""
@@ -107,7 +116,10 @@ class SymmBucketReducer:
             raise ValueError("too many buckets for the flag area")
         self.me, self.world = self.ctx.rank, self.ctx.world
         self.ctas = ctas
+        # flags are stamped with the context's device step counter (advanced by
+        # begin_step on the stream), so the step can be captured in a CUDA graph
         self.epoch = 0
+        self.ep_ptr = self.ctx.ep_ptr
         self.stream = torch.cuda.Stream(priority=-1)
         self.slot_norm = nb
         self.slot_ag = nb + 1
@@ -142,7 +154,9 @@ class SymmBucketReducer:
         self.next_to_launch = 0
 
     def begin_step(self) -> None:
-        self.epoch += 1
+        """Start a step: advance the device step counter on the current stream
+        (every rank takes the same number of steps, so the counters agree)."""
+        self.ctx.advance_epoch()
         self._reserved = False
 
     def on_ready(self, params) -> None:
@@ -171,14 +185,15 @@ class SymmBucketReducer:
                                       self.gsf.tensor.data_ptr() + s // 32, e - s)
                 _cuda().symm_rs_bucket_e5m2(self.codes.ptrs, self.gsf.ptrs, self.ctx.flags.ptrs, self.me, s, e - s,
                                             self.clen[b], b, self.epoch, self.state, self.ctas, 1.0 / self.world,
-                                            g.tensor.data_ptr())
+                                            g.tensor.data_ptr(), self.ep_ptr)
             elif self.nvls:
                 _cuda().symm_rs_bucket_mc(self.flat.symm_grad.mc, self.flat.symm_grad.ptrs, self.ctx.flags.ptrs,
                                           self.me, s, e - s, self.clen[b], b, self.epoch, self.state, self.ctas,
-                                          1.0 / self.world)
+                                          1.0 / self.world, self.ep_ptr)
             else:
                 _cuda().symm_rs_bucket(self.flat.symm_grad.ptrs, self.ctx.flags.ptrs, self.me, s, e - s,
-                                       self.clen[b], b, self.epoch, self.state, self.ctas, 1.0 / self.world)
+                                       self.clen[b], b, self.epoch, self.state, self.ctas, 1.0 / self.world,
+                                       self.ep_ptr)
 
     def finish(self) -> None:
         while self.next_to_launch < len(self.plan):
@@ -186,7 +201,7 @@ class SymmBucketReducer:
             self.next_to_launch += 1
         with torch.cuda.stream(self.stream):
             _cuda().symm_scalars_ar(self.ctx.scalars.ptrs, self.ctx.flags.ptrs, self.me, self.slot_norm,
-                                    self.epoch, self.state)
+                                    self.epoch, self.state, self.ep_ptr)
         torch.cuda.current_stream().wait_stream(self.stream)
         _cuda().gemm_set_reserved_sms(0)
         self._reserved = False
@@ -245,7 +260,7 @@ class ZeroAdam:
                                    self.flat.symm_w16.ptrs, self.state, self.lr if lr is None else lr,
                                    self.betas[0], self.betas[1], self.eps, self.weight_decay)
         # every rank has written its shard into every peer: order the next forward after it
-        _cuda().symm_barrier(r.ctx.flags.ptrs, r.me, r.slot_ag, r.epoch, 23)
+        _cuda().symm_barrier(r.ctx.flags.ptrs, r.me, r.slot_ag, r.epoch, 23, r.ep_ptr)
 
     def stats(self) -> dict:
         s = self.state.tolist()

@@ -194,14 +194,13 @@ class GptTrainer:
         all-reduce, optimizer, FP8 scale roll) into a CUDA graph over static input
         buffers shaped like ``ids`` / ``targets``; ``graph_step`` then replays it with
         one launch instead of ~1000.  Call after at least one eager step (the FP8
-        first-step path and every kernel's one-time set-up must have run).  Data
-        parallel over NCCL or none (the symmetric-memory path carries per-step
-        epochs in kernel arguments).  Returns the number of this framework's kernels
-        in the graph."""
+        first-step path and every kernel's one-time set-up must have run).  Any
+        data-parallel mode: NCCL buckets, or the symmetric-memory path, whose flag
+        epochs and amax stamps come from device step counters that the captured
+        step advances itself.  Returns the number of this framework's kernels in
+        the graph."""
         from .._ext import cuda as _cuda
 
-        if self.dp not in ("none", "nccl"):
-            raise ValueError("graph capture supports dp 'none' / 'nccl'")
         if self.global_step == 0 or (self.fp8 and self.model.fp8_state.first_step):
             raise RuntimeError("run one eager step before capturing")
         if self.warmup_steps and self.global_step < self.warmup_steps:

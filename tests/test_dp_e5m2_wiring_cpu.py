@@ -2,7 +2,8 @@
 the CPU with recording stand-ins for the symmetric buffers and kernels: every bucket
 is encoded from its own fp32 range (byte offset 4 * start) into the code buffer at
 element offset start and the scale buffer at block offset start / 32, then reduced
-with the same bucket bounds, chunk length, flag slot and epoch as the fp32 path; the
+with the same bucket bounds, chunk length, flag slot and epoch (the context's device
+step counter, advanced by begin_step) as the fp32 path; the
 buckets launch in order as their parameters become ready."""
 import contextlib
 
@@ -24,6 +25,11 @@ class _Ctx:
     def __init__(self, device, group=None, num_slots=1024):
         self.flags = _Buf(num_slots * 8, torch.int32)
         self.rank, self.world, self.num_slots = 1, 2, num_slots
+        self.ep_ptr = 4242
+        self.advanced = 0
+
+    def advance_epoch(self):
+        self.advanced += 1
 
 
 class _P:
@@ -82,9 +88,12 @@ def test_e5m2_transport_encodes_and_reduces_every_bucket(fakes):
     for b, ((s, e), q, rd) in enumerate(zip(r.plan.ranges, quant, reduce)):
         assert s % 64 == 0 and (e - s) % 32 == 0
         assert q == (gbase + 4 * s, cbase + s, sbase + s // 32, e - s)
-        codes, sfs, flags, me, start, ln, clen, slot, epoch, st, ctas, inv_n, mine = rd
+        codes, sfs, flags, me, start, ln, clen, slot, epoch, st, ctas, inv_n, mine, ep = rd
         assert (codes, sfs) == (r.codes.ptrs, r.gsf.ptrs) and me == 1
-        assert (start, ln, clen, slot, epoch, ctas, inv_n, mine) == (s, e - s, r.clen[b], b, 1, 8, 0.5, gbase)
+        # host epoch 0 + the context's device step counter (advanced once by begin_step)
+        assert (start, ln, clen, slot, epoch, ctas, inv_n, mine, ep) == (s, e - s, r.clen[b], b, 0, 8, 0.5, gbase,
+                                                                         4242)
+    assert r.ctx.advanced == 1
     assert not any(n in ("symm_rs_bucket", "symm_rs_bucket_mc") for n, _ in _Rec.calls)
 
 

@@ -120,6 +120,55 @@ def test_fused_dp_nvls_reduce_scatter_matches_peer_loads():
         assert torch.allclose(a[r][1], b[r][1], atol=2e-2, rtol=2e-2)
 
 
+def _dp_graph_body(rank, world, dp, fp8):
+    import gc
+
+    import torch
+
+    from mtorus.models.gpt import GptConfig
+    from mtorus.training.engine import GptTrainer
+
+    torch.cuda.set_device(rank)
+    dev = f"cuda:{rank}"
+    cfg = GptConfig(vocab_size=512, d_model=256, num_layers=2, num_heads=2, d_ff=1024, max_seq_len=128,
+                    dropout=0.0)
+    g = torch.Generator().manual_seed(300 + rank)
+    data = [torch.randint(0, cfg.vocab_size, (2, 129), generator=g) for _ in range(6)]
+    ids = [t[:, :-1].contiguous().to(dev) for t in data]
+    tgt = [t[:, 1:].contiguous().to(dev) for t in data]
+    out = {}
+    for graph in (False, True):
+        tr = GptTrainer(cfg, device=dev, lr=1e-3, init="normal", seed=0, dp=dp, bucket_mb=0.5, fp8=fp8)
+        losses = []
+        for i in range(6):
+            if graph and i == 2:
+                tr.capture(ids[i], tgt[i])
+            loss = tr.graph_step(ids[i], tgt[i]) if graph and i >= 2 else tr.step_device(ids[i], tgt[i])
+            losses.append(float(loss))
+        torch.cuda.synchronize()
+        st = tr.reducer.ctx.status() if dp == "symm" else 0
+        out[graph] = (losses, tr.flat.w16[:4096].float().cpu(), st)
+        del tr  # a graph holding NCCL calls is released before the group is destroyed
+        gc.collect()
+    return out
+
+
+@needs2
+@pytest.mark.parametrize("dp,fp8", [("symm", False), ("symm", True), ("nccl", True)])
+def test_captured_dp_step_replays_like_eager(dp, fp8):
+    """The whole data-parallel step captured once as a CUDA graph and replayed: the
+    fused path's flag epochs and amax stamps come from device step counters, so
+    four replays follow the eager trajectory."""
+    res = run_dist(_dp_graph_body, 2, (dp, fp8), backend="nccl")
+    for o in res:
+        (le, we, se), (lg, wg, sg) = o[False], o[True]
+        assert se == 0 and sg == 0
+        for x, y in zip(le, lg):
+            assert abs(x - y) < 1e-2 * max(1.0, abs(x)), (le, lg)
+        assert torch.allclose(we, wg, atol=1e-2, rtol=1e-2)
+    assert torch.equal(res[0][True][1], res[1][True][1])
+
+
 def _pp_body(rank, world, sched_name, ckpt_name):
     import torch
 
