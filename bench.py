@@ -45,12 +45,14 @@ def main() -> int:
     ap.add_argument("--impl", default="mtorus", choices=["mtorus", "reference"])
     ap.add_argument("--micro-batch", type=int, default=8)
     ap.add_argument("--seq", type=int, default=2048)
-    ap.add_argument("--dp", default="nccl", choices=["nccl", "symm"])
+    ap.add_argument("--dp", default="symm", choices=["nccl", "symm"],
+                    help="symm (default): fused NVLink reduce-scatter + sharded Adam + weight all-gather over "
+                         "symmetric memory; nccl: NCCL bucket all-reduce + full Adam on every rank (the baseline)")
     ap.add_argument("--layers", type=int, default=None,
                     help="override layer count (debug only; the metric is defined for 24)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
-                    help="replay the whole step as one CUDA graph (any --dp); auto: on for 1 GPU")
+                    help="replay the whole step as one CUDA graph (any --dp); auto: on")
     ap.add_argument("--precision", default="mxfp8", choices=["mxfp8", "fp8", "bf16"],
                     help="mxfp8 (default): E4M3 / E5M2 with one UE8M0 scale per 1x32 block in every "
                          "transformer-layer GEMM (block-scaled tcgen05 GEMMs); fp8: the same formats with one "
@@ -114,7 +116,7 @@ def main() -> int:
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    use_graph = args.graph == "on" or (args.graph == "auto" and world == 1)
+    use_graph = args.graph in ("on", "auto")
     if use_graph:
         torch.cuda.empty_cache()
         trainer.capture(dev_ids[0], dev_tgt[0])
@@ -251,6 +253,7 @@ def main() -> int:
         }
     if rank == 0:
         os.write(json_fd, (json.dumps(out) + "\n").encode())
+    trainer.release_graphs()  # a graph holding NCCL calls must go before the process group
     if world > 1:
         barrier()
         dist.destroy_process_group()

@@ -329,65 +329,89 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(const bf16* __restrict
 }
 
 // MXFP8 of a [R, C] bf16 tensor row-wise (32-blocks along C: the operand that
-// contracts over C) and column-wise (its transpose, 32-blocks along R), one
-// 128 x 128 tile per CTA.  A tile is exactly one 512-byte scale atom of each
-// output (128 rows x 4 K-blocks), so each CTA assembles both atoms in shared
-// memory and stores them whole; padding rows / columns read as zero and get the
-// scale byte 127, so no fill of the scale tensors is needed.  Both code tiles
-// (row-wise [128][128] and transposed [128][128]) are also assembled in shared
-// memory and stored as whole 128-byte rows, so every global store is coalesced.
-// LN: the tile is LayerNorm'd on load, bf16((x - mean[r]) * rstd[r] * gamma[c] +
-// beta[c]) (the MXFP8 input of the QKV / FFN1 GEMMs straight from the residual
-// stream).  colsum (optional): colsum[c] += sum over r of the tile's values (one
-// atomic per column per CTA).
+// contracts over C) and column-wise (its transpose, 32-blocks along R), over
+// 128 x 128 tiles.  A tile is exactly one 512-byte scale atom of each output
+// (128 rows x 4 K-blocks), assembled in shared memory and stored whole; padding
+// rows / columns read as zero (cp.async zero fill) and get the scale byte 127, so
+// no fill of the scale tensors is needed.  Persistent CTAs walk the tiles with two
+// shared-memory tile buffers: the cp.async copy of the next tile is in flight
+// while the current one is quantised, which hides the load latency that a
+// load-then-compute CTA exposes.  Codes go from registers straight to global
+// memory as whole 32-byte sectors (a row block of 32 codes, or a column block of
+// 32 codes of the transpose).
+// LN: the tile is LayerNorm'd in shared memory after it lands,
+// bf16((x - mean[r]) * rstd[r] * gamma[c] + beta[c]) (the MXFP8 input of the QKV /
+// FFN1 GEMMs straight from the residual stream).  colsum (optional):
+// colsum[c] += sum over r of the tile's values (one atomic per column per tile).
 constexpr int kRcTileStride = 128 + 8;  // bf16 elements per staged row (16-byte rows, bank spread)
-// dynamic shared memory: bf16 tile | row codes | column codes | two scale atoms | fp32 column sums [4][128]
-constexpr int kRcOffRcode = 128 * kRcTileStride * 2;
-constexpr int kRcOffCcode = kRcOffRcode + 128 * 128;
-constexpr int kRcOffSfr = kRcOffCcode + 128 * 128;
+constexpr int kRcTileBytes = 128 * kRcTileStride * 2;
+// dynamic shared memory: two bf16 tiles | two scale atoms | fp32 column sums [4][128]
+constexpr int kRcOffSfr = 2 * kRcTileBytes;
 constexpr int kRcOffSfc = kRcOffSfr + 512;
 constexpr int kRcOffCsum = kRcOffSfc + 512;
 constexpr int kRcSmem = kRcOffCsum + 4 * 128 * (int)sizeof(float);
-static_assert(kRcOffRcode % 16 == 0 && kRcOffCcode % 16 == 0 && kRcOffSfr % 16 == 0 && kRcOffSfc % 16 == 0 &&
-                  kRcOffCsum % 16 == 0,
+constexpr int kRcCtasPerSm = 3;
+static_assert(kRcTileBytes % 16 == 0 && kRcOffSfr % 16 == 0 && kRcOffSfc % 16 == 0 && kRcOffCsum % 16 == 0,
               "mx_rc_tile_kernel: 16-byte aligned shared-memory regions");
+static_assert(kRcCtasPerSm * (kRcSmem + 1024) <= 233472, "mx_rc_tile_kernel: CTAs per SM must fit in shared memory");
+
+// 16-byte cp.async global -> shared; src_bytes 0 zero-fills the destination
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, int src_bytes) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 template <bool LN>
-__global__ void __launch_bounds__(256, 3) mx_rc_tile_kernel(const bf16* __restrict__ x, int64_t ldx, int R, int C, int fmt,
-                                                         uint32_t fmax_bits, const float* __restrict__ mean,
-                                                         const float* __restrict__ rstd,
-                                                         const float* __restrict__ gamma,
-                                                         const float* __restrict__ beta, float* __restrict__ colsum,
-                                                         uint8_t* __restrict__ rc, uint8_t* __restrict__ rsf,
-                                                         uint8_t* __restrict__ cc, uint8_t* __restrict__ csf) {
+__global__ void __launch_bounds__(256, kRcCtasPerSm) mx_rc_tile_kernel(
+    const bf16* __restrict__ x, int64_t ldx, int R, int C, int fmt, uint32_t fmax_bits,
+    const float* __restrict__ mean, const float* __restrict__ rstd, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float* __restrict__ colsum, uint8_t* __restrict__ rc, uint8_t* __restrict__ rsf,
+    uint8_t* __restrict__ cc, uint8_t* __restrict__ csf) {
   extern __shared__ __align__(16) uint8_t rc_smem[];
-  bf16 (*tile)[kRcTileStride] = reinterpret_cast<bf16 (*)[kRcTileStride]>(rc_smem);
-  uint8_t* rcode = rc_smem + kRcOffRcode;  // [128 rows][128 codes]
-  uint8_t* ccode = rc_smem + kRcOffCcode;  // [128 columns][128 codes]
   uint8_t* sfr = rc_smem + kRcOffSfr;
   uint8_t* sfc = rc_smem + kRcOffSfc;
   float* csum = reinterpret_cast<float*>(rc_smem + kRcOffCsum);  // [4][128]
-  const int rt = blockIdx.y, ct = blockIdx.x, t = threadIdx.x;
-  const int r0 = rt * 128, c0 = ct * 128;
+  const int t = threadIdx.x;
+  const int ntc = (C + 127) / 128, ntr = (R + 127) / 128;
+  const int ntiles = ntc * ntr;
   const int ef = (int)((fmax_bits >> 23) & 0xFF);
   const uint32_t mf = fmax_bits & 0x7FFFFF;
-  {
-    // 128 rows x 16 vectors: all eight 16-byte loads of a thread in flight at once
-    uint4 raw[8];
+  // this thread's eight 16-byte pieces of a tile: row i >> 4, columns (i & 15) * 8 .. + 8
+  auto issue = [&](int tile, int buf) {
+    bf16(*tl)[kRcTileStride] = reinterpret_cast<bf16(*)[kRcTileStride]>(rc_smem + buf * kRcTileBytes);
+    const int r0 = (tile / ntc) * 128, c0 = (tile % ntc) * 128;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
       const int r = r0 + rr, c = c0 + cv;
-      raw[k] = (r < R && c < C) ? *reinterpret_cast<const uint4*>(x + (int64_t)r * ldx + c) : make_uint4(0, 0, 0, 0);
+      const bool ok = r < R && c < C;
+      cp_async16_zfill(&tl[rr][cv], ok ? (const void*)(x + (int64_t)r * ldx + c) : (const void*)x, ok ? 16 : 0);
     }
+  };
+  int tile = blockIdx.x;
+  if (tile < ntiles) issue(tile, 0);
+  cp_async_commit_group();
+  for (int it = 0; tile < ntiles; tile += gridDim.x, ++it) {
+    const int buf = it & 1;
+    // prefetch the next tile into the other buffer (read by the previous iteration,
+    // which every thread finished before its closing barrier)
+    if (tile + (int)gridDim.x < ntiles) issue(tile + gridDim.x, buf ^ 1);
+    cp_async_commit_group();
+    cp_async_wait_one();
+    __syncthreads();
+    bf16(*tl)[kRcTileStride] = reinterpret_cast<bf16(*)[kRcTileStride]>(rc_smem + buf * kRcTileBytes);
+    const int rt = tile / ntc, ct = tile % ntc;
+    const int r0 = rt * 128, c0 = ct * 128;
+    if (LN) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
-      if (LN) {
+      for (int k = 0; k < 8; ++k) {
+        const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
         const int r = r0 + rr, c = c0 + cv;
-        float f[8];
-        unpack8(*reinterpret_cast<const bf16x8*>(&raw[k]), f);
         if (r < R && c < C) {
+          float f[8];
+          unpack8(*reinterpret_cast<const bf16x8*>(&tl[rr][cv]), f);
           const float mu = mean[r], rs = rstd[r];
           const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
           const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
@@ -397,83 +421,79 @@ __global__ void __launch_bounds__(256, 3) mx_rc_tile_kernel(const bf16* __restri
           const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
           for (int q = 0; q < 8; ++q) f[q] = (f[q] - mu) * rs * g[q] + b[q];
+          *reinterpret_cast<bf16x8*>(&tl[rr][cv]) = pack8(f);
         }
-        *reinterpret_cast<bf16x8*>(&tile[rr][cv]) = pack8(f);
-      } else {
-        *reinterpret_cast<uint4*>(&tile[rr][cv]) = raw[k];
+      }
+      __syncthreads();
+    }
+    float v[32];
+    uint32_t w[8];
+    uint8_t sfb;
+    // row-wise: row t & 127, K-blocks 2 * (t >> 7) and 2 * (t >> 7) + 1 (64 codes)
+    {
+      const int row = t & 127, half = t >> 7;
+      const bool rok = r0 + row < R;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        const int blk = 2 * half + b;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) unpack8(*reinterpret_cast<const bf16x8*>(&tl[row][blk * 32 + 8 * q]), v + 8 * q);
+        mx_block(v, ef, mf, fmt, w, sfb);
+        if (rok && c0 + blk * 32 < C) {
+          uint4* dst = reinterpret_cast<uint4*>(rc + (int64_t)(r0 + row) * C + c0 + blk * 32);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        sfr[(row & 31) * 16 + (row >> 5) * 4 + blk] = sfb;
       }
     }
-  }
-  __syncthreads();
-  float v[32];
-  uint32_t w[8];
-  uint8_t sfb;
-  // row-wise: row t & 127, K-blocks 2 * (t >> 7) and 2 * (t >> 7) + 1
-  {
-    const int row = t & 127, half = t >> 7;
-#pragma unroll
-    for (int b = 0; b < 2; ++b) {
-      const int blk = 2 * half + b;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) unpack8(*reinterpret_cast<const bf16x8*>(&tile[row][blk * 32 + 8 * q]), v + 8 * q);
-      mx_block(v, ef, mf, fmt, w, sfb);
-      uint4* dst = reinterpret_cast<uint4*>(rcode + row * 128 + blk * 32);
-      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      sfr[(row & 31) * 16 + (row >> 5) * 4 + blk] = sfb;
-    }
-  }
-  // column-wise: columns 2 (t & 63), 2 (t & 63) + 1, K-block (rows) t >> 6; 32-bit loads
-  {
-    const int cp = t & 63, blk = t >> 6;
-    float v1[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const __nv_bfloat162 pr = *reinterpret_cast<const __nv_bfloat162*>(&tile[blk * 32 + i][2 * cp]);
-      v[i] = __low2float(pr);
-      v1[i] = __high2float(pr);
-    }
-    if (colsum) {
-      float s0 = 0.f, s1 = 0.f;
+    // column-wise: columns 2 (t & 63), 2 (t & 63) + 1, K-block (rows) t >> 6; 32-bit loads
+    {
+      const int cp = t & 63, blk = t >> 6;
+      float v1[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        s0 += v[i];
-        s1 += v1[i];
+        const __nv_bfloat162 pr = *reinterpret_cast<const __nv_bfloat162*>(&tl[blk * 32 + i][2 * cp]);
+        v[i] = __low2float(pr);
+        v1[i] = __high2float(pr);
       }
-      csum[blk * 128 + 2 * cp] = s0;
-      csum[blk * 128 + 2 * cp + 1] = s1;
-    }
+      if (colsum) {
+        float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int col = 2 * cp + e;
-      mx_block(e ? v1 : v, ef, mf, fmt, w, sfb);
-      uint4* dst = reinterpret_cast<uint4*>(ccode + col * 128 + blk * 32);
-      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      sfc[(col & 31) * 16 + (col >> 5) * 4 + blk] = sfb;
-    }
-  }
-  __syncthreads();
-  // coalesced stores: 128 rows of 128 codes each way (8 threads x 16 bytes per row)
+        for (int i = 0; i < 32; ++i) {
+          s0 += v[i];
+          s1 += v1[i];
+        }
+        csum[blk * 128 + 2 * cp] = s0;
+        csum[blk * 128 + 2 * cp + 1] = s1;
+      }
+      const bool kok = r0 + blk * 32 < R;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int i = t + k * 256, row = i >> 3, seg = (i & 7) * 16;
-    if (r0 + row < R && c0 + seg < C)
-      *reinterpret_cast<uint4*>(rc + (int64_t)(r0 + row) * C + c0 + seg) =
-          *reinterpret_cast<const uint4*>(rcode + row * 128 + seg);
-    if (c0 + row < C && r0 + seg < R)
-      *reinterpret_cast<uint4*>(cc + (int64_t)(c0 + row) * R + r0 + seg) =
-          *reinterpret_cast<const uint4*>(ccode + row * 128 + seg);
+      for (int e = 0; e < 2; ++e) {
+        const int col = 2 * cp + e;
+        mx_block(e ? v1 : v, ef, mf, fmt, w, sfb);
+        if (kok && c0 + col < C) {
+          uint4* dst = reinterpret_cast<uint4*>(cc + (int64_t)(c0 + col) * R + r0 + blk * 32);
+          dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        sfc[(col & 31) * 16 + (col >> 5) * 4 + blk] = sfb;
+      }
+    }
+    __syncthreads();  // scale atoms and column sums complete; the tile buffer is free
+    if (t < 32) {
+      reinterpret_cast<uint4*>(rsf + ((int64_t)rt * ntc + ct) * 512)[t] = reinterpret_cast<const uint4*>(sfr)[t];
+    } else if (t < 64) {
+      reinterpret_cast<uint4*>(csf + ((int64_t)ct * ntr + rt) * 512)[t - 32] =
+          reinterpret_cast<const uint4*>(sfc)[t - 32];
+    }
+    if (colsum && t >= 128 && c0 + (t - 128) < C) {
+      const int c = t - 128;
+      atomicAdd(colsum + c0 + c, (csum[c] + csum[128 + c]) + (csum[256 + c] + csum[384 + c]));
+    }
+    // the next iteration's first barrier orders these reads before sfr / sfc / csum are rewritten
   }
-  if (t < 32) {
-    reinterpret_cast<uint4*>(rsf + ((int64_t)rt * ((C + 127) / 128) + ct) * 512)[t] =
-        reinterpret_cast<const uint4*>(sfr)[t];
-  } else if (t < 64) {
-    reinterpret_cast<uint4*>(csf + ((int64_t)ct * ((R + 127) / 128) + rt) * 512)[t - 32] =
-        reinterpret_cast<const uint4*>(sfc)[t - 32];
-  }
-  if (colsum && t < 128 && c0 + t < C)
-    atomicAdd(colsum + c0 + t, (csum[t] + csum[128 + t]) + (csum[256 + t] + csum[384 + t]));
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 static int q_grid(size_t n, int per) {
@@ -704,7 +724,8 @@ void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, 
   const float fm = (float)fmax;
   uint32_t fbits;
   std::memcpy(&fbits, &fm, 4);
-  dim3 grid((unsigned)((C + 127) / 128), (unsigned)((R + 127) / 128));
+  const int64_t tiles = ((C + 127) / 128) * ((R + 127) / 128);
+  const int grid = (int)std::min<int64_t>(tiles, (int64_t)num_sms() * kRcCtasPerSm);
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));

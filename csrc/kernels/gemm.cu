@@ -573,6 +573,14 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
 // loaded per stage next to the operands and copied into TMEM by the MMA thread
 // (tcgen05.cp, ordered before the stage's MMAs, which read them); sf_kb = number of
 // 128-wide K blocks per 128-row block of the scale tensors.
+// MXFP8: the three scale atoms of a stage (A's 128 rows; B's two 128-row halves)
+// from shared memory into TMEM columns sf_tmem .. sf_tmem + 11 of both CTAs.
+__device__ __forceinline__ void mx_copy_scales(uint32_t sf_tmem, uint32_t ssf) {
+  tmem_cp_32x128b_x4_2sm(sf_tmem, make_sdesc(ssf, 0, 128, kSwizzleNone));
+  tmem_cp_32x128b_x4_2sm(sf_tmem + 4, make_sdesc(ssf + P_SF_ATOM, 0, 128, kSwizzleNone));
+  tmem_cp_32x128b_x4_2sm(sf_tmem + 8, make_sdesc(ssf + 2 * P_SF_ATOM, 0, 128, kSwizzleNone));
+}
+
 template <int EB, bool MX = false, bool DROP = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -711,6 +719,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * ACC1_COL;
         bool ok = true;
+        bool sf_ahead = false;  // MXFP8: this stage's scales were copied during the previous k-block
         for (int kb = 0; kb < num_kb; ++kb) {
           const long long fw0 = prof ? clock64() : 0;
           const bool got = mbar_wait(&ctl->full[stage], phase, abort, status, 13);
@@ -726,12 +735,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           // stage's copy never overwrites scales the previous stage's MMAs may still read
           const uint32_t sf_tmem = tmem_base + MX_SF_COL + (uint32_t)(stage & 1) * 16;
           if constexpr (MX) {
-            // stage scales -> TMEM (in order with the MMAs of this thread, so the previous
-            // stage's MMAs have read the old scales before these land)
-            const uint32_t ssf = smem_u32(sf_smem + stage * P_SF_BYTES);
-            tmem_cp_32x128b_x4_2sm(sf_tmem, make_sdesc(ssf, 0, 128, kSwizzleNone));
-            tmem_cp_32x128b_x4_2sm(sf_tmem + 4, make_sdesc(ssf + P_SF_ATOM, 0, 128, kSwizzleNone));
-            tmem_cp_32x128b_x4_2sm(sf_tmem + 8, make_sdesc(ssf + 2 * P_SF_ATOM, 0, 128, kSwizzleNone));
+            // stage scales -> TMEM, in issue order after the MMAs that last read this set
+            // (those of stage - 2), unless the previous k-block already copied them
+            if (!sf_ahead) mx_copy_scales(sf_tmem, smem_u32(sf_smem + stage * P_SF_BYTES));
+            // copy the next stage's scales now when its operands have already landed, so the
+            // copy is not the last tensor-pipe op before that stage's MMAs
+            sf_ahead = false;
+            if (kb + 1 < num_kb) {
+              const int ns = stage + 1 == NST ? 0 : stage + 1;
+              const uint32_t nph = stage + 1 == NST ? phase ^ 1u : phase;
+              if (mbar_try_wait(smem_u32(&ctl->full[ns]), nph)) {
+                tc_fence_after();
+                mx_copy_scales(tmem_base + MX_SF_COL + (uint32_t)(ns & 1) * 16,
+                               smem_u32(sf_smem + ns * P_SF_BYTES));
+                sf_ahead = true;
+              }
+            }
           }
 #pragma unroll
           for (int k = 0; k < BK / MMA_K; ++k) {

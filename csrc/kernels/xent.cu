@@ -4,14 +4,20 @@
 // (examples/gpt-1b/src/main.rs:32-41).
 //
 // Design (B200): one CTA per row of the [T, V] bf16 logits.  Pass 1 streams the
-// row once with 16-byte loads and an online max / sum-exp; pass 2 re-reads the
+// row once with 16-byte loads and an online max / sum-exp (one rescale per
+// 8-value vector, base-2 exponentials of pre-scaled logits); pass 2 re-reads the
 // row (an L2 hit: the row was touched microseconds earlier) and overwrites it
-// in place with dlogits = grad_scale * (softmax - onehot).  grad_scale is a
+// in place with dlogits = grad_scale * (softmax - onehot).  Half of the
+// exponentials of the 16-byte vectors run as ex2_poly on the FMA pipe, so the
+// special-function unit (two exponentials per logit) does not bound the kernel.  grad_scale is a
 // device scalar (1/T times the loss scale), so the backward needs no host sync
 // and fp32 logits are never materialised.
 #include "common.cuh"
+#include "ex2poly.cuh"
 
 namespace mtorus {
+
+constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void online_update(float& m, float& s, float x) {
   if (x > m) {
@@ -40,13 +46,26 @@ __global__ void __launch_bounds__(512) xent_fwd_bwd(bf16* __restrict__ logits,
   bf16* lr = logits + (size_t)row * V;
   float m = -INFINITY, s = 0.f;
   if (VEC) {
+    // m, s in log2 units of the scaled logits x * log2e
     const int nv = V / 8;
     for (int j = threadIdx.x; j < nv; j += blockDim.x) {
       float f[8];
       unpack8(reinterpret_cast<const bf16x8*>(lr)[j], f);
+      float vm = f[0];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) online_update(m, s, f[i]);
+      for (int i = 1; i < 8; ++i) vm = fmaxf(vm, f[i]);
+      vm *= kLog2e;
+      if (vm > m) {
+        s *= exp2f(m - vm);
+        m = vm;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float xe = fmaf(f[i], kLog2e, -m);
+        s += i < 4 ? exp2f(xe) : ex2_poly(xe);
+      }
     }
+    m *= 1.f / kLog2e;  // back to natural units for the merge below
   } else {
     for (int j = threadIdx.x; j < V; j += blockDim.x) online_update(m, s, __bfloat162float(lr[j]));
   }
@@ -83,14 +102,16 @@ __global__ void __launch_bounds__(512) xent_fwd_bwd(bf16* __restrict__ logits,
   const float inv_s = 1.f / s;
   if (VEC) {
     const int nv = V / 8;
+    const float nm = -m * kLog2e, ps = gs * inv_s;
     for (int j = threadIdx.x; j < nv; j += blockDim.x) {
       float f[8];
       unpack8(reinterpret_cast<const bf16x8*>(lr)[j], f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float p = __expf(f[i] - m) * inv_s;
-        if (j * 8 + i == tgt) p -= 1.f;
-        f[i] = p * gs;
+        const float xe = fmaf(f[i], kLog2e, nm);
+        float g = (i < 4 ? exp2f(xe) : ex2_poly(xe)) * ps;
+        if (j * 8 + i == tgt) g -= gs;
+        f[i] = g;
       }
       reinterpret_cast<bf16x8*>(lr)[j] = pack8(f);
     }

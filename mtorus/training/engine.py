@@ -231,6 +231,13 @@ class GptTrainer:
         torch.cuda.synchronize()
         return n
 
+    def release_graphs(self) -> None:
+        """Drop the captured step graphs (call before destroying a process group
+        whose NCCL calls a graph holds)."""
+        torch.cuda.synchronize()
+        self._graphs = {}
+        self._graph = self._g_loss = None
+
     def graph_step(self, ids: torch.Tensor, targets: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         """One training step by replaying the captured graph; returns the device loss."""
         g, loss, _ = self._graphs[reduce]
