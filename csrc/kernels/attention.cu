@@ -38,7 +38,6 @@
 // Every wait is bounded (2 s); on a timeout the kernel records a status code,
 // lets its in-flight copies and MMAs land, frees TMEM and returns.
 #include "common.cuh"
-#include "ex2poly.cuh"
 #include "philox.cuh"
 #include "sm100.cuh"
 
@@ -120,8 +119,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// of the 8 exponentials of a 16-byte P chunk, this many (the last ones) use ex2_poly
-constexpr int kPolyPerChunk = 2;
 
 template <bool DROP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -336,8 +333,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         float pv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float xe = fmaf(__uint_as_float(t[c16 * 8 + e]), sl2, neg);
-          pv[e] = e < 8 - kPolyPerChunk ? ex2_approx(xe) : ex2_poly(xe);
+          pv[e] = ex2_approx(fmaf(__uint_as_float(t[c16 * 8 + e]), sl2, neg));
           s8[e] += pv[e];
         }
         if constexpr (DROP) {  // keys j*128 + 8*c16 .. +7 of query row qt*128 + r

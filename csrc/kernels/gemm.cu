@@ -719,7 +719,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * ACC1_COL;
         bool ok = true;
-        bool sf_ahead = false;  // MXFP8: this stage's scales were copied during the previous k-block
         for (int kb = 0; kb < num_kb; ++kb) {
           const long long fw0 = prof ? clock64() : 0;
           const bool got = mbar_wait(&ctl->full[stage], phase, abort, status, 13);
@@ -735,22 +734,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           // stage's copy never overwrites scales the previous stage's MMAs may still read
           const uint32_t sf_tmem = tmem_base + MX_SF_COL + (uint32_t)(stage & 1) * 16;
           if constexpr (MX) {
-            // stage scales -> TMEM, in issue order after the MMAs that last read this set
-            // (those of stage - 2), unless the previous k-block already copied them
-            if (!sf_ahead) mx_copy_scales(sf_tmem, smem_u32(sf_smem + stage * P_SF_BYTES));
-            // copy the next stage's scales now when its operands have already landed, so the
-            // copy is not the last tensor-pipe op before that stage's MMAs
-            sf_ahead = false;
-            if (kb + 1 < num_kb) {
-              const int ns = stage + 1 == NST ? 0 : stage + 1;
-              const uint32_t nph = stage + 1 == NST ? phase ^ 1u : phase;
-              if (mbar_try_wait(smem_u32(&ctl->full[ns]), nph)) {
-                tc_fence_after();
-                mx_copy_scales(tmem_base + MX_SF_COL + (uint32_t)(ns & 1) * 16,
-                               smem_u32(sf_smem + ns * P_SF_BYTES));
-                sf_ahead = true;
-              }
-            }
+            // stage scales -> TMEM (in order with the MMAs of this thread, so the MMAs of
+            // stage - 2, the last readers of this column set, have read them before these land)
+            mx_copy_scales(sf_tmem, smem_u32(sf_smem + stage * P_SF_BYTES));
           }
 #pragma unroll
           for (int k = 0; k < BK / MMA_K; ++k) {

@@ -153,7 +153,11 @@ def test_cuda_graph_step_matches_eager(fp8):
     lb += [float(b.graph_step(x, y)) for x, y in batches[1:]]
     assert b.global_step == 5
     assert all(abs(p - q) < 2e-3 * abs(p) for p, q in zip(la, lb)), (la, lb)
-    assert torch.allclose(a.flat.master, b.flat.master, rtol=1e-3, atol=1e-5)
+    # atomics (bias-gradient column sums, attention dQ reduce-adds) sum in a different order
+    # from run to run, and an FP8 rounding flip can follow from a last-bit difference: the
+    # weights agree in norm, not bit for bit
+    rel = float((a.flat.master - b.flat.master).norm() / a.flat.master.norm())
+    assert rel < 1e-3, rel
     if fp8:
         assert int(b.model.fp8_state.cursor_dev) == int(a.model.fp8_state.cursor_dev)
         assert torch.allclose(a.model.fp8_state.scale, b.model.fp8_state.scale, rtol=1e-2)
