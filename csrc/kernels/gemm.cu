@@ -341,20 +341,24 @@ namespace {
 
 constexpr int P_BM = 128;  // rows per CTA (pair tile M = 256)
 constexpr int P_BN = 256;  // pair tile N; each CTA stages 128 rows of B
-constexpr int P_STAGES = 5;       // operand ring depth (the MXFP8 kernel: 4, its scales need the room)
+constexpr int P_STAGES = 5;       // operand ring depth
 template <bool MX>
-constexpr int pair_stages() { return MX ? 4 : P_STAGES; }
+constexpr int pair_stages() { return P_STAGES; }
 constexpr int P_GROUP_M = 8;  // pair tiles per raster group along M
 constexpr int P_A_BYTES = P_BM * 128;        // 128 rows x 128 bytes of K
 constexpr int P_B_BYTES = (P_BN / 2) * 128;  // 128 rows of B x 128 bytes of K
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-// Epilogue: eight warps, each with two 4 KB staging buffers; a buffer holds one
-// 32x32 output chunk (fp32, 4 KB) or a bf16 chunk (2 KB) plus its GELU output
-// (bf16 2 KB or FP8 1 KB at offset 2048), written to global memory by TMA.
+// Epilogue: eight warps, each with two 4 KB staging buffers (one in the MXFP8
+// kernel, whose per-stage scales would otherwise cost it an operand stage); a
+// buffer holds one 32x32 output chunk (fp32, 4 KB) or a bf16 chunk (2 KB) plus its
+// GELU output (bf16 2 KB or FP8 1 KB at offset 2048), written to global memory by TMA.
 constexpr int P_EPI_WARPS = 8;
 constexpr int kPairThreads = 64 + 32 * P_EPI_WARPS;
 constexpr int P_EPI_BUF = 4096;
-constexpr int P_EPI_BYTES = P_EPI_WARPS * 2 * P_EPI_BUF;
+template <bool MX>
+constexpr int epi_nbuf() { return MX ? 1 : 2; }
+template <bool MX>
+constexpr int epi_bytes() { return P_EPI_WARPS * epi_nbuf<MX>() * P_EPI_BUF; }
 // MXFP8 (1x32 UE8M0 block scales) per stage: this CTA's 128-row SFA atom and the
 // pair tile's two 128-row SFB atoms (every CTA needs the scales of all 256 B rows,
 // since its tensor core multiplies its A rows with the whole B tile).  An atom holds
@@ -434,7 +438,7 @@ __device__ __forceinline__ void epi_prefetch(const GemmEpilogue& ep, int m, int 
 // drops the GEMM result before the residual add (a branch output), mode 2 drops
 // GELU(result) in the act / act8 output (the FFN hidden), mode 3 applies the same
 // mask to the incoming gradient before the dGELU multiply (its backward).
-template <bool DROP>
+template <bool DROP, int NB>
 __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const uint4 (&x)[4], int m, int M, int N,
                                                 int n0, int row0, float alpha, float act_scale, float& act_amax,
                                                 const GemmEpilogue& ep, bool f32out, uint8_t* stages, int& sb,
@@ -490,7 +494,7 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
       for (int i = 0; i < 8; ++i) v[j * 8 + i] += r8[i];
     }
   }
-  if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer two chunks ago
+  if (lane == 0) bulk_wait_group_read<NB - 1>();  // the store that last used this buffer has read it
   __syncwarp();
   if (f32out) {
     // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row r sits at j ^ (r & 7)
@@ -563,7 +567,7 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
     if (ep.act || ep.act8) tma_store_2d(tma_act, stage + 2048, n0, row0);
     bulk_commit_group();
   }
-  sb ^= 1;
+  if (NB == 2) sb ^= 1;
 }
 
 // EB = operand element bytes: 2 (bf16, kind::f16) or 1 (fp8 E4M3/E5M2, kind::f8f6f4).
@@ -606,7 +610,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* epi_smem = smem + NST * P_STAGE_BYTES;
-  uint8_t* sf_smem = epi_smem + P_EPI_BYTES;
+  uint8_t* sf_smem = epi_smem + epi_bytes<MX>();
   PairSmem* ctl = reinterpret_cast<PairSmem*>(sf_smem + (MX ? NST * P_SF_BYTES : 0));
   constexpr uint32_t ACC1_COL = MX ? MX_ACC1_COL : P_BN;  // TMEM column of accumulator 1
 
@@ -785,7 +789,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&ctl->tempty[0]), 0);
     const uint32_t tempty_leader1 = mapa_shared(smem_u32(&ctl->tempty[1]), 0);
     const uint32_t ovl_leader = mapa_shared(smem_u32(&ctl->ovl), 0);
-    uint8_t* stage_base = epi_smem + ew * 2 * P_EPI_BUF;
+    uint8_t* stage_base = epi_smem + ew * epi_nbuf<MX>() * P_EPI_BUF;
     const bool f32out = ep.out_f32 != 0;
     const float act_scale = ep.act8_scale ? *ep.act8_scale : 1.f;
     float act_amax = 0.f;
@@ -819,7 +823,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const int c0 = epi_chunk<MX>(buf, h, i), c1 = epi_chunk<MX>(buf, h, i + 1);
         tmem_ld32(tbase + c1 * 32, rb);
         epi_prefetch(ep, m, M, N, nb * P_BN + c1 * 32, xb);
-        epi_chunk_store<DROP>(ra, xa, m, M, N, nb * P_BN + c0 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
+        epi_chunk_store<DROP, epi_nbuf<MX>()>(ra, xa, m, M, N, nb * P_BN + c0 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
                               stage_base, sb, &tma_d, &tma_act, lane, drop, drop_mode);
         tmem_wait_ld();
         if (i + 1 == 3) {
@@ -831,7 +835,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           tmem_ld32(tbase + c2 * 32, ra);
           epi_prefetch(ep, m, M, N, nb * P_BN + c2 * 32, xa);
         }
-        epi_chunk_store<DROP>(rb, xb, m, M, N, nb * P_BN + c1 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
+        epi_chunk_store<DROP, epi_nbuf<MX>()>(rb, xb, m, M, N, nb * P_BN + c1 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
                               stage_base, sb, &tma_d, &tma_act, lane, drop, drop_mode);
         if (i + 1 != 3) tmem_wait_ld();
       }
@@ -1069,8 +1073,8 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
   const int avail_pairs = std::max(1, (num_sms() - g_reserved_sms) / 2);
   const int pairs = std::min(num_tiles, avail_pairs);
   constexpr int NST = pair_stages<MX>();
-  const size_t smem = NST * P_STAGE_BYTES + P_EPI_BYTES + (MX ? NST * P_SF_BYTES : 0) + sizeof(PairSmem) + 1024;
-  static_assert(NST * P_STAGE_BYTES + P_EPI_BYTES + (MX ? NST * P_SF_BYTES : 0) + sizeof(PairSmem) + 1024 <= 232448,
+  const size_t smem = NST * P_STAGE_BYTES + epi_bytes<MX>() + (MX ? NST * P_SF_BYTES : 0) + sizeof(PairSmem) + 1024;
+  static_assert(NST * P_STAGE_BYTES + epi_bytes<MX>() + (MX ? NST * P_SF_BYTES : 0) + sizeof(PairSmem) + 1024 <= 232448,
                 "CTA-pair GEMM: shared memory above the 227 KB per-CTA limit");
   const DropoutArgs drop = g_next_drop;
   const int drop_mode = g_next_drop_mode;

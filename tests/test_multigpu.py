@@ -352,8 +352,6 @@ def _gather_gemm_body(rank, world):
 
 
 @needs2
-@pytest.mark.skipif(os.environ.get("MTORUS_GATHER_GEMM_TESTS") != "1",
-                    reason="gather GEMM not yet run on B200s (MTORUS_GATHER_GEMM_TESTS=1 runs it)")
 def test_gather_b_gemm_matches_local_gemm_2gpu():
     """Weight all-gather fused into the GEMM: a GEMM that reads each B tile from the rank owning it equals
     the same GEMM on a locally gathered B, bit for bit (same kernel, same tiles)."""
@@ -382,8 +380,6 @@ def _bc_scatter_body(rank, world):
 
 
 @needs2
-@pytest.mark.skipif(os.environ.get("MTORUS_BCAST_SCATTER_TESTS") != "1",
-                    reason="scatter + multicast broadcast not yet run on B200s (MTORUS_BCAST_SCATTER_TESTS=1 runs it)")
 def test_broadcast_scatter_multicast_2gpu():
     for o in run_dist(_bc_scatter_body, 2, backend="nccl"):
         assert o["status"] == 0
@@ -419,8 +415,6 @@ def _e5m2_rs_body(rank, world):
 
 
 @needs2
-@pytest.mark.skipif(os.environ.get("MTORUS_DP_GRAD_FP8_TESTS") != "1",
-                    reason="E5M2 gradient transport not yet run on B200s (MTORUS_DP_GRAD_FP8_TESTS=1 runs it)")
 def test_e5m2_gradient_reduce_scatter_2gpu():
     """Each rank's chunk is the mean over ranks of the E5M2-encoded gradients (the
     MX block rule with 32-value blocks), decoded exactly as the PyTorch oracle does."""
