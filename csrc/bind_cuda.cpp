@@ -63,7 +63,10 @@ void gemm_fp8_act8(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tens
 void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const at::Tensor& B,
                 int64_t b_fmt, const at::Tensor& sfb, at::Tensor D, const c10::optional<at::Tensor>& bias,
                 const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
-                const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta);
+                const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta,
+                const c10::optional<at::Tensor>& out_rc, const c10::optional<at::Tensor>& out_rsf,
+                const c10::optional<at::Tensor>& out_cc, const c10::optional<at::Tensor>& out_csf, int64_t out_fmt,
+                double out_fmax, const c10::optional<at::Tensor>& out_colsum, bool out_gelu, bool store_d);
 void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t fmt, double fmax);
 void copy_async(int64_t dst, int64_t src, int64_t bytes);
 void dp_quant_e5m2(int64_t grad, int64_t codes, int64_t sf, int64_t nelem);
@@ -236,7 +239,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_mxfp8", &gemm_mxfp8, py::arg("A"), py::arg("a_fmt"), py::arg("sfa"), py::arg("B"), py::arg("b_fmt"),
         py::arg("sfb"), py::arg("D"), py::arg("bias") = py::none(), py::arg("residual") = py::none(),
         py::arg("act") = py::none(), py::arg("aux") = py::none(), py::arg("alpha") = py::none(),
-        py::arg("beta") = false);
+        py::arg("beta") = false, py::arg("out_rc") = py::none(), py::arg("out_rsf") = py::none(),
+        py::arg("out_cc") = py::none(), py::arg("out_csf") = py::none(), py::arg("out_fmt") = 0,
+        py::arg("out_fmax") = 448.0, py::arg("out_colsum") = py::none(), py::arg("out_gelu") = false,
+        py::arg("store_d") = true);
   m.def("mx_quantize", &mx_quantize);
   m.def("copy_async", &copy_async);
   m.def("dp_quant_e5m2", &dp_quant_e5m2);

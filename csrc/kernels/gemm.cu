@@ -25,9 +25,11 @@
 // All mbarrier waits are bounded (see sm100.cuh); a timeout raises the status word.
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 
 #include "amax_publish.cuh"
 #include "gelu.cuh"
+#include "mx.cuh"
 #include "philox.cuh"
 #include "sm100.cuh"
 
@@ -54,6 +56,21 @@ struct GemmEpilogue {
   const float* act8_scale;
   float* act8_amax;
   int act8_fmt;         // 0 = E4M3, 1 = E5M2
+};
+
+// MXFP8 output of the 2-SM block-scaled GEMM's epilogue: the tile's values (or its
+// GELU) as row-wise codes [M, N] (32-blocks along N; stored through the act tensor
+// map) and column-wise codes [N, M] (32-blocks along M; its own tensor map), with the
+// scale atoms of both in the mx_quantize layout, optionally summing the columns
+// (the bias gradient when the tile is an output gradient).  M and N multiples of 128.
+struct MxOutArgs {
+  uint8_t* rsf;        // scales of the row codes: [ceil(M/128)][ceil(N/128)][512]
+  uint8_t* csf;        // scales of the column codes: [ceil(N/128)][ceil(M/128)][512]
+  float* colsum;       // += column sums of the quantised (bf16-rounded) values, or null
+  uint32_t fmax_bits;  // largest finite value of the code format (fp32 bits)
+  int fmt;             // 0 = E4M3, 1 = E5M2
+  int src_act;         // 1: quantise GELU(result) (D keeps the pre-activation); 0: the result itself
+  int store_d;         // 1: also store D in bf16
 };
 
 namespace {
@@ -438,12 +455,13 @@ __device__ __forceinline__ void epi_prefetch(const GemmEpilogue& ep, int m, int 
 // drops the GEMM result before the residual add (a branch output), mode 2 drops
 // GELU(result) in the act / act8 output (the FFN hidden), mode 3 applies the same
 // mask to the incoming gradient before the dGELU multiply (its backward).
-template <bool DROP, int NB>
+template <bool DROP, int NB, bool MXO>
 __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const uint4 (&x)[4], int m, int M, int N,
                                                 int n0, int row0, float alpha, float act_scale, float& act_amax,
                                                 const GemmEpilogue& ep, bool f32out, uint8_t* stages, int& sb,
                                                 const CUtensorMap* tma_d, const CUtensorMap* tma_act, int lane,
-                                                const DropoutArgs& drop, int drop_mode) {
+                                                const DropoutArgs& drop, int drop_mode, const MxOutArgs& mxo,
+                                                const CUtensorMap* tma_cc) {
   if (n0 >= N) return;  // warp-uniform
   uint8_t* stage = stages + sb * P_EPI_BUF;
   uint32_t keep = 0xFFFFFFFFu;
@@ -496,7 +514,79 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
   }
   if (lane == 0) bulk_wait_group_read<NB - 1>();  // the store that last used this buffer has read it
   __syncwarp();
-  if (f32out) {
+  if constexpr (MXO) {
+    // The chunk is 32 rows (one per lane) x 32 columns: one row block per lane and,
+    // read back through shared memory, one column block per lane.  Bytes 0..2047 of
+    // the staging buffer: D (bf16, 64B swizzle); 2048..4095: first the bf16 values to
+    // quantise (same swizzle), then the row codes [32 x 32 B] and the column codes.
+    uint8_t* base = stage + lane * 64;
+    uint8_t* sbase = stage + 2048;
+    float sv[32];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bf16x8 pk = pack8(v + 8 * j);
+      if (mxo.store_d) *reinterpret_cast<bf16x8*>(base + ((j ^ ((lane >> 1) & 3)) << 4)) = pk;
+      bf16x8 src = pk;
+      if (mxo.src_act) {
+        float p8[8], g8[8];
+        unpack8(pk, p8);  // GELU of the rounded pre-activation, as the bf16 path stores it
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
+        if constexpr (DROP) {
+          if (drop_mode == 2) {
+            float r8[8];
+            unpack8(pack8(g8), r8);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) g8[i] = (keep >> (8 * j + i) & 1u) ? r8[i] * drop.scale : 0.f;
+          }
+        }
+        src = pack8(g8);
+      }
+      if (m >= M) {  // rows past M hold the epilogue of zero-filled A rows: they pad the column blocks as zeros
+        const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        src = pack8(z);
+      }
+      unpack8(src, sv + 8 * j);
+      *reinterpret_cast<bf16x8*>(sbase + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = src;
+    }
+    const int ef = (int)((mxo.fmax_bits >> 23) & 0xFF);
+    const uint32_t mf = mxo.fmax_bits & 0x7FFFFF;
+    uint32_t rw[8], cw[8];
+    uint8_t rsb, csb;
+    mx_block(sv, ef, mf, mxo.fmt, rw, rsb);  // this lane's row block (sv is dead afterwards)
+    __syncwarp();
+    float cv[32];  // column n0 + lane, rows row0 .. row0 + 31
+#pragma unroll
+    for (int rr = 0; rr < 32; ++rr)
+      cv[rr] = __bfloat162float(*reinterpret_cast<const bf16*>(
+          sbase + rr * 64 + ((((lane >> 3) ^ ((rr >> 1) & 3))) << 4) + (lane & 7) * 2));
+    mx_block(cv, ef, mf, mxo.fmt, cw, csb);
+    if (mxo.colsum) {
+      float cs = 0.f;
+#pragma unroll
+      for (int rr = 0; rr < 32; ++rr) cs += cv[rr];
+      atomicAdd(mxo.colsum + n0 + lane, cs);
+    }
+    __syncwarp();  // every lane has read the bf16 values
+    uint4* rdst = reinterpret_cast<uint4*>(sbase + lane * 32);
+    rdst[0] = make_uint4(rw[0], rw[1], rw[2], rw[3]);
+    rdst[1] = make_uint4(rw[4], rw[5], rw[6], rw[7]);
+    uint4* cdst = reinterpret_cast<uint4*>(sbase + 1024 + lane * 32);
+    cdst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+    cdst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+    // scale bytes in the mx_quantize atom layout ((r / 128) * nkb4 + k / 4) * 512 + (r % 32) * 16 +
+    // (r % 128 / 32) * 4 + k % 4, r the operand row, k the 32-block along its K
+    if (m < M) {
+      const int nkb = N >> 7;
+      mxo.rsf[((int64_t)(m >> 7) * nkb + (n0 >> 7)) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 + ((n0 & 127) >> 5)] =
+          rsb;
+    }
+    if (row0 < M) {
+      const int c = n0 + lane, mkb = M >> 7;
+      mxo.csf[((int64_t)(c >> 7) * mkb + (row0 >> 7)) * 512 + (c & 31) * 16 + ((c & 127) >> 5) * 4 +
+              ((row0 & 127) >> 5)] = csb;
+    }
+  } else if (f32out) {
     // 32 rows x 128 B, 128B swizzle: 16-byte chunk j of row r sits at j ^ (r & 7)
     uint8_t* base = stage + lane * 128;
 #pragma unroll
@@ -560,11 +650,17 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
   fence_async_shared();
   __syncwarp();
   if (lane == 0) {
-    if (f32out && ep.beta)
-      tma_reduce_add_2d(tma_d, stage, n0, row0);
-    else
-      tma_store_2d(tma_d, stage, n0, row0);
-    if (ep.act || ep.act8) tma_store_2d(tma_act, stage + 2048, n0, row0);
+    if constexpr (MXO) {
+      if (mxo.store_d) tma_store_2d(tma_d, stage, n0, row0);
+      tma_store_2d(tma_act, stage + 2048, n0, row0);         // row codes [M, N]
+      tma_store_2d(tma_cc, stage + 3072, row0, n0);          // column codes [N, M]
+    } else {
+      if (f32out && ep.beta)
+        tma_reduce_add_2d(tma_d, stage, n0, row0);
+      else
+        tma_store_2d(tma_d, stage, n0, row0);
+      if (ep.act || ep.act8) tma_store_2d(tma_act, stage + 2048, n0, row0);
+    }
     bulk_commit_group();
   }
   if (NB == 2) sb ^= 1;
@@ -585,7 +681,7 @@ __device__ __forceinline__ void mx_copy_scales(uint32_t sf_tmem, uint32_t ssf) {
   tmem_cp_32x128b_x4_2sm(sf_tmem + 8, make_sdesc(ssf + 2 * P_SF_ATOM, 0, 128, kSwizzleNone));
 }
 
-template <int EB, bool MX = false, bool DROP = false>
+template <int EB, bool MX = false, bool DROP = false, bool MXO = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_2sm_kernel(const __grid_constant__ CUtensorMap tma_a,
                     const __grid_constant__ CUtensorMap tma_b,
@@ -595,12 +691,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     const __grid_constant__ CUtensorMap tma_sfb,
                     const __grid_constant__ PeerMapsB peer_b, int M, int N, int K, int a_mn,
                     int b_mn, int sf_kb, uint32_t idesc, GemmEpilogue ep, int* status,
-                    unsigned long long* prof, DropoutArgs drop, int drop_mode) {
+                    unsigned long long* prof, DropoutArgs drop, int drop_mode,
+                    const __grid_constant__ CUtensorMap tma_cc, MxOutArgs mxo) {
   // prof (optional, gemm_profile): stall accounting summed over CTAs: cycles the
   // producer waited for free stages [0] and ran [1], the MMA issuer waited for
   // loaded stages [2] / free accumulators [3] and ran [4], waited for the MXFP8
   // epilogue to read the chunk both accumulators share [5]; CTA pairs [7].
   static_assert(!MX || EB == 1, "block scaling is for fp8 operands");
+  static_assert(!MXO || MX, "MXFP8 output is an epilogue of the block-scaled kernel");
   constexpr int BK = 128 / EB;       // K elements per stage
   constexpr int MMA_K = 32 / EB;     // K elements per tcgen05.mma
   constexpr int MN_BOX = 128 / EB;   // MN elements per 128-byte swizzle row
@@ -823,8 +921,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const int c0 = epi_chunk<MX>(buf, h, i), c1 = epi_chunk<MX>(buf, h, i + 1);
         tmem_ld32(tbase + c1 * 32, rb);
         epi_prefetch(ep, m, M, N, nb * P_BN + c1 * 32, xb);
-        epi_chunk_store<DROP, epi_nbuf<MX>()>(ra, xa, m, M, N, nb * P_BN + c0 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
-                              stage_base, sb, &tma_d, &tma_act, lane, drop, drop_mode);
+        epi_chunk_store<DROP, epi_nbuf<MX>(), MXO>(ra, xa, m, M, N, nb * P_BN + c0 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
+                              stage_base, sb, &tma_d, &tma_act, lane, drop, drop_mode, mxo, &tma_cc);
         tmem_wait_ld();
         if (i + 1 == 3) {
           // every column of this warp's share of the buffer is in registers: release it
@@ -835,8 +933,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
           tmem_ld32(tbase + c2 * 32, ra);
           epi_prefetch(ep, m, M, N, nb * P_BN + c2 * 32, xa);
         }
-        epi_chunk_store<DROP, epi_nbuf<MX>()>(rb, xb, m, M, N, nb * P_BN + c1 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
-                              stage_base, sb, &tma_d, &tma_act, lane, drop, drop_mode);
+        epi_chunk_store<DROP, epi_nbuf<MX>(), MXO>(rb, xb, m, M, N, nb * P_BN + c1 * 32, row0, alpha, act_scale, act_amax, ep, f32out,
+                              stage_base, sb, &tma_d, &tma_act, lane, drop, drop_mode, mxo, &tma_cc);
         if (i + 1 != 3) tmem_wait_ld();
       }
     }
@@ -1030,7 +1128,8 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
                         const c10::optional<at::Tensor>& act, const GemmEpilogue& ep, int64_t M,
                         int64_t N, int64_t K, uint32_t idesc, const at::Tensor* sfa = nullptr,
                         const at::Tensor* sfb = nullptr, const std::vector<int64_t>* b_peers = nullptr,
-                        int64_t shard_rows = 0) {
+                        int64_t shard_rows = 0, const MxOutArgs* mxo = nullptr, const at::Tensor* mx_rc = nullptr,
+                        const at::Tensor* mx_cc = nullptr) {
   const auto dt = EB == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const auto swz = CU_TENSOR_MAP_SWIZZLE_128B;
   constexpr uint32_t BK = 128 / EB, MN_BOX = 128 / EB;
@@ -1060,7 +1159,14 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
                     CU_TENSOR_MAP_SWIZZLE_64B)
       : ep.act8 ? make_tma_2d(ep.act8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, N, 32, 32,
                               CU_TENSOR_MAP_SWIZZLE_NONE)
+      : mx_rc   ? make_tma_2d(mx_rc->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, M, N, 32, 32,
+                              CU_TENSOR_MAP_SWIZZLE_NONE)
                 : td;
+  // MXFP8 output: column codes [N, M], one 32 x 32-byte box per epilogue chunk
+  CUtensorMap tcc = mx_cc ? make_tma_2d(mx_cc->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, N, M, 32, 32,
+                                        CU_TENSOR_MAP_SWIZZLE_NONE)
+                          : td;
+  const MxOutArgs mo = mxo ? *mxo : MxOutArgs{};
   // scale tensors viewed as rows of 256 bytes (an atom is two rows); x is always 0
   const int64_t sf_kb = (K + 127) / 128;
   CUtensorMap tsfa = MX ? make_tma_2d(sfa->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256,
@@ -1080,31 +1186,33 @@ static void launch_pair(const at::Tensor& A, bool a_mn, const at::Tensor& B, boo
   const int drop_mode = g_next_drop_mode;
   g_next_drop = DropoutArgs{};
   g_next_drop_mode = 0;
-  if (drop.rng) {
-    TORCH_CHECK((drop_mode != 1 || ep.residual) && (drop_mode != 2 || ep.act || ep.act8) && (drop_mode != 3 || ep.aux),
+  if (drop.rng)
+    TORCH_CHECK((drop_mode != 1 || ep.residual) && (drop_mode != 2 || ep.act || ep.act8 || (mxo && mo.src_act)) &&
+                    (drop_mode != 3 || ep.aux),
                 "gemm dropout: mode 1 needs a residual, 2 a GELU output, 3 a dGELU input");
-    static bool attr_set_d = false;
-    if (!attr_set_d) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB, MX, true>,
+  // one instance per (dropout, MXFP8 output); each sets its shared-memory limit once
+  auto go = [&](auto drop_c, auto mxo_c) {
+    constexpr bool kDrop = decltype(drop_c)::value;
+    constexpr bool kMxo = decltype(mxo_c)::value && MX;
+    static bool attr_set = false;
+    if (!attr_set) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB, MX, kDrop, kMxo>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      attr_set_d = true;
+      attr_set = true;
     }
-    gemm_2sm_kernel<EB, MX, true><<<2 * pairs, kPairThreads, smem, cur_stream()>>>(
+    gemm_2sm_kernel<EB, MX, kDrop, kMxo><<<2 * pairs, kPairThreads, smem, cur_stream()>>>(
         ta, tb, td, tact, tsfa, tsfb, pb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
-        idesc, ep, gemm_status_ptr(), g_gemm_prof_on ? g_gemm_prof : nullptr, drop, drop_mode);
+        idesc, ep, gemm_status_ptr(), g_gemm_prof_on ? g_gemm_prof : nullptr, drop, kDrop ? drop_mode : 0, tcc,
+        mo);
     MT_LAUNCH_CHECK();
-    return;
+  };
+  using T = std::true_type;
+  using F = std::false_type;
+  if (mxo) {
+    if (drop.rng) go(T{}, T{}); else go(F{}, T{});
+  } else {
+    if (drop.rng) go(T{}, F{}); else go(F{}, F{});
   }
-  static bool attr_set = false;
-  if (!attr_set) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_2sm_kernel<EB, MX>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_set = true;
-  }
-  gemm_2sm_kernel<EB, MX><<<2 * pairs, kPairThreads, smem, cur_stream()>>>(
-      ta, tb, td, tact, tsfa, tsfb, pb, (int)M, (int)N, (int)K, a_mn ? 1 : 0, b_mn ? 1 : 0, (int)sf_kb,
-      idesc, ep, gemm_status_ptr(), g_gemm_prof_on ? g_gemm_prof : nullptr, drop, 0);
-  MT_LAUNCH_CHECK();
 }
 
 // A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] (b_mn=false) or [K,N] (b_mn=true).
@@ -1255,7 +1363,10 @@ void gemm_fp8_gather_b(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::
 void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const at::Tensor& B,
                 int64_t b_fmt, const at::Tensor& sfb, at::Tensor D, const c10::optional<at::Tensor>& bias,
                 const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& act,
-                const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta) {
+                const c10::optional<at::Tensor>& aux, const c10::optional<at::Tensor>& alpha, bool beta,
+                const c10::optional<at::Tensor>& out_rc, const c10::optional<at::Tensor>& out_rsf,
+                const c10::optional<at::Tensor>& out_cc, const c10::optional<at::Tensor>& out_csf, int64_t out_fmt,
+                double out_fmax, const c10::optional<at::Tensor>& out_colsum, bool out_gelu, bool store_d) {
   check_operand(A, "A", 1);
   check_operand(B, "B", 1);
   TORCH_CHECK((a_fmt == 0 || a_fmt == 1) && (b_fmt == 0 || b_fmt == 1), "gemm_mxfp8: formats are 0 (E4M3) / 1 (E5M2)");
@@ -1272,10 +1383,42 @@ void gemm_mxfp8(const at::Tensor& A, int64_t a_fmt, const at::Tensor& sfa, const
   check_sf(sfa, M, "sfa");
   check_sf(sfb, N, "sfb");
   GemmEpilogue ep = build_epilogue(D, M, N, bias, residual, act, aux, alpha, c10::nullopt, beta);
+  const bool mx_out = out_rc.has_value();
+  MxOutArgs mo{};
+  if (mx_out) {
+    // MXFP8 output (row and column codes with their scale atoms) written by the epilogue
+    TORCH_CHECK(out_rsf.has_value() && out_cc.has_value() && out_csf.has_value(),
+                "gemm_mxfp8: MX output needs rc, rsf, cc and csf");
+    TORCH_CHECK(M % 128 == 0 && N % 128 == 0, "gemm_mxfp8: MX output needs M and N multiples of 128");
+    TORCH_CHECK(D.scalar_type() == at::kBFloat16 && !beta && !act.has_value() && !residual.has_value(),
+                "gemm_mxfp8: MX output with a bf16 D, no accumulate, no bf16 GELU output and no residual");
+    TORCH_CHECK(out_fmt == 0 || out_fmt == 1, "gemm_mxfp8: MX output format 0 (E4M3) / 1 (E5M2)");
+    auto chk = [](const at::Tensor& t, int64_t n, const char* what) {
+      TORCH_CHECK(t.is_cuda() && t.element_size() == 1 && t.is_contiguous() && t.numel() == n &&
+                      reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+                  what);
+    };
+    chk(*out_rc, M * N, "gemm_mxfp8: rc must be 16-byte aligned contiguous uint8 [M, N]");
+    chk(*out_cc, M * N, "gemm_mxfp8: cc must be 16-byte aligned contiguous uint8 [N, M]");
+    chk(*out_rsf, (M / 128) * (N / 128) * P_SF_ATOM, "gemm_mxfp8: rsf size");
+    chk(*out_csf, (M / 128) * (N / 128) * P_SF_ATOM, "gemm_mxfp8: csf size");
+    if (out_colsum.has_value())
+      TORCH_CHECK(out_colsum->scalar_type() == at::kFloat && out_colsum->is_contiguous() && out_colsum->numel() == N,
+                  "gemm_mxfp8: colsum must be fp32 [N]");
+    const float fm = (float)out_fmax;
+    std::memcpy(&mo.fmax_bits, &fm, 4);
+    mo.rsf = reinterpret_cast<uint8_t*>(out_rsf->data_ptr());
+    mo.csf = reinterpret_cast<uint8_t*>(out_csf->data_ptr());
+    mo.colsum = out_colsum.has_value() ? out_colsum->data_ptr<float>() : nullptr;
+    mo.fmt = (int)out_fmt;
+    mo.src_act = out_gelu ? 1 : 0;
+    mo.store_d = store_d ? 1 : 0;
+  }
   if (M == 0 || N == 0) return;
   ensure_context();
   launch_pair<1, true>(A, false, B, false, D, act, ep, M, N, K, make_idesc_mx(2 * P_BM, P_BN, (int)a_fmt, (int)b_fmt),
-                       &sfa, &sfb);
+                       &sfa, &sfb, nullptr, 0, mx_out ? &mo : nullptr, mx_out ? &*out_rc : nullptr,
+                       mx_out ? &*out_cc : nullptr);
 }
 
 }  // namespace mtorus

@@ -278,6 +278,26 @@ class AttnBlockFn(Function):
         return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None, None
 
 
+def _mx_gemm_quant(MX, a, b, fmt, out=None, *, bias=None, aux=None, gelu=False, colsum=None, accumulate=True,
+                   store_d=True):
+    """Block-scaled GEMM whose output (or its GELU) leaves as MXFP8 row and column
+    codes: fused into the epilogue when M and N are multiples of 128, else the GEMM
+    followed by the row / column quantiser.  Returns (D or None, rows, cols)."""
+    M, N = a.codes.shape[0], b.codes.shape[0]
+    if M % 128 == 0 and N % 128 == 0:
+        return MX.gemm_mxfp8_mx_out(a, b, fmt, out, bias=bias, aux=aux, gelu=gelu, colsum=colsum,
+                                    accumulate=accumulate, store_d=store_d)
+    if gelu:
+        act = torch.empty((M, N), dtype=torch.bfloat16, device=a.codes.device)
+        d = MX.gemm_mxfp8(a, b, out=out, bias=bias, act=act)
+        src = act
+    else:
+        d = MX.gemm_mxfp8(a, b, out=out, bias=bias, aux=aux)
+        src = d
+    rows, cols = MX.mx_quantize_rc(src, fmt, colsum=colsum, accumulate=accumulate)
+    return (d if store_d else None), rows, cols
+
+
 class MLPBlockFn(Function):
     """x + W2 GELU(W1 LN2(x) + b1) + b2 as one autograd node (reference
     TransformerBlock second half and FeedForward, transformer.rs:89-110,151-155);
@@ -299,10 +319,9 @@ class MLPBlockFn(Function):
 
             gamma, beta, eps = ln
             hr, hc, mean, rstd = MX.mx_layernorm_rc(x2d, gamma.data, beta.data, eps, MX.E4M3)
-            act = torch.empty_like(pre)
+            # the FFN1 epilogue stores the pre-activation and quantises GELU of it both ways
             with K.gemm_dropout(d_act, 2):
-                MX.gemm_mxfp8(hr, w1.mx[0], out=pre, bias=b1.data, act=act)  # pre-activation and GELU
-            ar, ac = MX.mx_quantize_rc(act, MX.E4M3)
+                _, ar, ac = _mx_gemm_quant(MX, hr, w1.mx[0], MX.E4M3, out=pre, bias=b1.data, gelu=True)
             with K.gemm_dropout(d_out, 1):
                 out = MX.gemm_mxfp8(ar, w2.mx[0], bias=b2.data, residual=x2d)
             ctx.save_for_backward(x2d, mean, rstd, hc.codes, hc.sf, pre, ac.codes, ac.sf)
@@ -389,11 +408,13 @@ class MLPBlockFn(Function):
         dbr = K.dropout_apply(dout, d_out) if d_out is not None else dout
         hc, ac = _mx_t(hcc, hcs, MX.E4M3), _mx_t(acc_codes, acs, MX.E4M3)
         grow, gcol = MX.mx_quantize_rc(dbr, MX.E5M2, colsum=b2.main_grad, accumulate=acc)
+        # dgrad: hidden-dropout mask, then dGELU; the epilogue quantises the result both ways and
+        # sums its columns into the FFN1 bias gradient
         with K.gemm_dropout(d_act, 3):
-            dpre = MX.gemm_mxfp8(grow, w2.mx[1], aux=pre)  # dgrad: hidden-dropout mask, then dGELU
+            _, prow, pcol = _mx_gemm_quant(MX, grow, w2.mx[1], MX.E5M2, aux=pre, colsum=b1.main_grad,
+                                           accumulate=acc, store_d=False)
         MX.gemm_mxfp8(gcol, ac, out=w2.main_grad, accumulate=acc)
         _grads_done(w2, b2)
-        prow, pcol = MX.mx_quantize_rc(dpre, MX.E5M2, colsum=b1.main_grad, accumulate=acc)
         MX.gemm_mxfp8(pcol, hc, out=w1.main_grad, accumulate=acc)
         dh = MX.gemm_mxfp8(prow, w1.mx[1])
         _grads_done(w1, b1)

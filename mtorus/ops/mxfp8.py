@@ -143,6 +143,61 @@ def gemm_mxfp8(a: MxTensor, b: MxTensor, out: Optional[torch.Tensor] = None, *, 
     return out
 
 
+def gemm_mxfp8_mx_out(a: MxTensor, b: MxTensor, fmt: int, out: Optional[torch.Tensor] = None, *, bias=None,
+                      aux=None, alpha=None, gelu: bool = False, colsum: Optional[torch.Tensor] = None,
+                      accumulate: bool = True, store_d: bool = True, fmax: Optional[float] = None):
+    """The block-scaled GEMM whose epilogue quantises its own output: D = epilogue(alpha
+    * A . B^T) (bias, dGELU with ``aux``), then the bf16-rounded D -- or GELU of it when
+    ``gelu`` -- as MXFP8 row codes [M, N] and column codes [N, M], exactly what
+    ``mx_quantize_rc`` makes of that bf16 tensor, without writing it.  ``colsum``
+    (fp32 [N], optional) receives its column sums (added when ``accumulate``).  D is
+    stored in bf16 only when ``store_d`` (the pre-activation a dGELU needs later).
+    M and N multiples of 128.  Returns (D or None, rows, cols).  The CPU path is the
+    unfused oracle."""
+    M, K = a.codes.shape
+    N, Kb = b.codes.shape
+    if K != Kb:
+        raise ValueError(f"gemm_mxfp8_mx_out: K mismatch {K} vs {Kb}")
+    if M % 128 or N % 128:
+        raise ValueError("gemm_mxfp8_mx_out: M and N must be multiples of 128")
+    fmax = float(MX_FMT_MAX[fmt] if fmax is None else fmax)
+    dev = a.codes.device
+    if not a.codes.is_cuda:
+        d = gemm_mxfp8_ref(a, b)
+        if alpha is not None:
+            d = d * alpha.float()
+        if bias is not None:
+            d = d + bias.float()
+        if aux is not None:  # dGELU: d * GELU'(aux), the erf GELU's derivative
+            x = aux.float()
+            d = d * (0.5 * (1.0 + torch.erf(x * 0.7071067811865476)) + x * torch.exp(-0.5 * x * x) * 0.3989422804014327)
+        d16 = d.to(torch.bfloat16)
+        src = d16
+        if gelu:
+            src = torch.nn.functional.gelu(d16.float()).to(torch.bfloat16)
+        if colsum is not None:
+            cs = src.float().sum(0)
+            if accumulate:
+                colsum += cs
+            else:
+                colsum.copy_(cs)
+        if out is not None and store_d:
+            out.copy_(d16)
+        return (out if store_d else None), mx_quantize_ref(src, fmt, fmax), mx_quantize_ref(src.t(), fmt, fmax)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    rc = torch.empty((M, N), dtype=torch.uint8, device=dev)
+    cc = torch.empty((N, M), dtype=torch.uint8, device=dev)
+    rsf = torch.empty(sf_numel(M, N), dtype=torch.uint8, device=dev)
+    csf = torch.empty(sf_numel(N, M), dtype=torch.uint8, device=dev)
+    if colsum is not None and not accumulate:
+        colsum.zero_()
+    _cuda().gemm_mxfp8(a.codes, a.fmt, a.sf, b.codes, b.fmt, b.sf, out, bias, None, None, aux, alpha, False,
+                       out_rc=rc, out_rsf=rsf, out_cc=cc, out_csf=csf, out_fmt=int(fmt), out_fmax=fmax,
+                       out_colsum=colsum, out_gelu=bool(gelu), store_d=bool(store_d))
+    return (out if store_d else None), MxTensor(rc, rsf, int(fmt)), MxTensor(cc, csf, int(fmt))
+
+
 def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = None,
                    colsum: Optional[torch.Tensor] = None, accumulate: bool = True):
     """Row-wise MXFP8 of x [R, C] (32-blocks along C) and of its transpose [C, R]
@@ -284,4 +339,4 @@ def gemm_mxfp8_ref(a: MxTensor, b: MxTensor) -> torch.Tensor:
 
 
 __all__ = ["E4M3", "E5M2", "MX_FMT_MAX", "MxTensor", "sf_numel", "sf_offsets", "mx_quantize", "mx_quantize_ref",
-           "mx_quantize_rc", "mx_layernorm_rc", "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_ref", "MxLinearFn", "mx_linear", "enable_mx_linears"]
+           "mx_quantize_rc", "mx_layernorm_rc", "mx_dequantize", "gemm_mxfp8", "gemm_mxfp8_mx_out", "gemm_mxfp8_ref", "MxLinearFn", "mx_linear", "enable_mx_linears"]

@@ -9,8 +9,9 @@ fp32 product of the dequantised operands (and with cuBLAS's MX GEMM).
 import pytest
 import torch
 
-from mtorus.ops.mxfp8 import (E4M3, E5M2, MX_FMT_MAX, MxTensor, gemm_mxfp8, gemm_mxfp8_ref, mx_dequantize,
-                              mx_linear, mx_quantize, mx_quantize_rc, mx_quantize_ref, sf_numel, sf_offsets)
+from mtorus.ops.mxfp8 import (E4M3, E5M2, MX_FMT_MAX, MxTensor, gemm_mxfp8, gemm_mxfp8_mx_out, gemm_mxfp8_ref,
+                              mx_dequantize, mx_linear, mx_quantize, mx_quantize_rc, mx_quantize_ref, sf_numel,
+                              sf_offsets)
 
 
 def _blocky(R, K, seed=0):
@@ -201,6 +202,44 @@ def test_cuda_row_col_quantiser_matches_reference(shape):
     # the bias-gradient column sums of the same pass (fp32, added to the buffer)
     want = x.double().sum(0) + 5.0
     assert torch.allclose(cs.cpu().double(), want, rtol=1e-5, atol=1e-5 * float(x.double().abs().sum(0).max()))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N", [(512, 768), (384, 384)])
+def test_gemm_epilogue_mx_output_matches_unfused_quantiser(M, N):
+    """The GEMM epilogue that quantises its own output (row and column MXFP8 codes,
+    both scale atoms, column sums) writes exactly what the separate quantiser makes
+    of the bf16 tensor the unfused epilogue would store: GELU of the FFN1
+    pre-activation (E4M3) and the dGELU'd FFN2 dgrad (E5M2).  M = 384 leaves the
+    second CTA of the last pair entirely past M."""
+    K = 256
+    g = torch.Generator().manual_seed(M + N)
+    a = mx_quantize((torch.randn(M, K, generator=g) * 0.5).to(torch.bfloat16).cuda())
+    b = mx_quantize((torch.randn(N, K, generator=g) * 0.1).to(torch.bfloat16).cuda())
+    bias = (torch.randn(N, generator=g) * 0.1).cuda()
+    # FFN1: pre-activation stored, GELU quantised
+    pre_ref = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    act_ref = torch.empty_like(pre_ref)
+    gemm_mxfp8(a, b, out=pre_ref, bias=bias, act=act_ref)
+    r_ref, c_ref = mx_quantize_rc(act_ref, E4M3)
+    pre = torch.empty_like(pre_ref)
+    d, r, c = gemm_mxfp8_mx_out(a, b, E4M3, out=pre, bias=bias, gelu=True)
+    torch.cuda.synchronize()
+    assert torch.equal(d, pre_ref)
+    for got, want in ((r, r_ref), (c, c_ref)):
+        assert torch.equal(got.codes, want.codes) and torch.equal(got.sf, want.sf)
+    # FFN2 dgrad: dGELU with the pre-activation as aux, E5M2 codes, bias-gradient sums, no bf16 store
+    gd = mx_quantize((torch.randn(M, K, generator=g) * 1e-3).to(torch.bfloat16).cuda(), E5M2)
+    dpre_ref = gemm_mxfp8(gd, b, aux=pre_ref)
+    cs_ref = torch.full((N,), 0.5, device="cuda")
+    r_ref, c_ref = mx_quantize_rc(dpre_ref, E5M2, colsum=cs_ref, accumulate=True)
+    cs = torch.full((N,), 0.5, device="cuda")
+    d, r, c = gemm_mxfp8_mx_out(gd, b, E5M2, aux=pre_ref, colsum=cs, accumulate=True, store_d=False)
+    torch.cuda.synchronize()
+    assert d is None
+    for got, want in ((r, r_ref), (c, c_ref)):
+        assert torch.equal(got.codes, want.codes) and torch.equal(got.sf, want.sf)
+    assert torch.allclose(cs, cs_ref, rtol=1e-5, atol=1e-5 * float(dpre_ref.float().abs().sum(0).max()))
 
 
 @pytest.mark.gpu
