@@ -53,6 +53,9 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
                     help="replay the whole step as one CUDA graph (any --dp); auto: on")
+    ap.add_argument("--lm-head", default="fp8", choices=["fp8", "bf16"],
+                    help="LM-head GEMMs in FP8 (per-tensor delayed scaling, E4M3 / E5M2) or bf16 "
+                         "(ignored with --precision bf16)")
     ap.add_argument("--precision", default="mxfp8", choices=["mxfp8", "fp8", "bf16"],
                     help="mxfp8 (default): E4M3 / E5M2 with one UE8M0 scale per 1x32 block in every "
                          "transformer-layer GEMM (block-scaled tcgen05 GEMMs); fp8: the same formats with one "
@@ -93,7 +96,8 @@ def main() -> int:
     B, S = args.micro_batch, args.seq
     trainer = GptTrainer(cfg, device=dev, lr=3e-4, init="normal", seed=1234, dp=args.dp,
                          fp8=args.precision in ("fp8", "mxfp8"),
-                         fp8_recipe="mx" if args.precision == "mxfp8" else "tensor")
+                         fp8_recipe="mx" if args.precision == "mxfp8" else "tensor",
+                         fp8_head=args.lm_head == "fp8")
     ext = _cuda()
 
     # synthetic next-token data: uniform ids, targets shifted by one
@@ -191,6 +195,8 @@ def main() -> int:
     tokens_per_step = B * S * world
     ms_step = ms / args.steps
     value = tokens_per_step / (ms_step / 1000.0)
+    head = ("LM-head GEMMs FP8 (E4M3 h / weight, E5M2 dlogits, per-tensor delayed scaling)"
+            if args.lm_head == "fp8" else "bf16 LM head")
     out = {
         "metric": "GPT-1B FP8 tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; exposed comm/step",
         "value": round(value, 1),
@@ -203,14 +209,15 @@ def main() -> int:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": {"fp8": "fp8 (transformer-layer GEMMs: E4M3 forward / E5M2 gradients, one per-tensor "
-                         "delayed-scaling scale per operand; bf16 LM head, attention, activations; fp32 master "
-                         "weights / Adam)",
+                         "delayed-scaling scale per operand; " + head + "; bf16 attention, activations; fp32 "
+                         "master weights / Adam)",
                   "mxfp8": "mxfp8 (transformer-layer GEMMs: E4M3 forward / E5M2 gradients, one UE8M0 scale per "
-                           "1x32 block along each GEMM's contraction dimension; bf16 LM head, attention, "
+                           "1x32 block along each GEMM's contraction dimension; " + head + "; bf16 attention, "
                            "activations; fp32 master weights / Adam)",
                   "bf16": "bf16"}[args.precision],
         "data": "synthetic uniform-random tokens, random-init N(0,0.02) weights",
         "config": {
+            "lm_head": args.lm_head if args.precision != "bf16" else "bf16",
             "model": f"GPT-1B ({cfg.num_layers} layers, d_model {cfg.d_model}, {cfg.num_heads} heads, "
                      f"d_ff {cfg.d_ff}, vocab {cfg.vocab_size})",
             "global_batch": B * world,

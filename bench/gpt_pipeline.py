@@ -46,6 +46,8 @@ def main(argv=None, defaults=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--no-checkpoint", action="store_true")
     ap.add_argument("--precision", default="fp8", choices=["fp8", "mxfp8", "bf16"])
+    ap.add_argument("--lm-head", default="fp8", choices=["fp8", "bf16"],
+                    help="LM-head GEMMs in FP8 (per-tensor delayed scaling) or bf16")
     ap.add_argument("--dp-mode", default="symm", choices=["symm", "nccl"],
                     help="symm: fused NVLink reduce-scatter + sharded Adam + amax all-reduce in the quantise "
                          "kernels; nccl: NCCL bucket all-reduce (the baseline)")
@@ -95,6 +97,7 @@ def main(argv=None, defaults=None) -> int:
     tr = PipelineTrainer(cfg, pp=args.pp, dp=args.dp, schedule=sched, num_microbatches=M, micro_batch=b,
                          seq_len=S, checkpoint=ckpt, fp8=args.precision in ("fp8", "mxfp8"), lr=3e-4, device=dev,
                          seed=1234, fp8_recipe="mx" if args.precision == "mxfp8" else "tensor",
+                         fp8_head=args.lm_head == "fp8",
                          dp_mode=args.dp_mode if args.dp > 1 else "nccl", wire=args.wire)
     ext = _cuda()
 
@@ -182,9 +185,10 @@ def main(argv=None, defaults=None) -> int:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": {"fp8": "fp8 (transformer-layer GEMMs: E4M3 forward / E5M2 gradients, per-tensor delayed "
-                         "scaling; bf16 LM head, attention, activations; fp32 master weights / Adam)",
+                         "scaling; LM head " + args.lm_head + "; bf16 attention, activations; fp32 master weights / Adam)",
                   "mxfp8": "mxfp8 (transformer-layer GEMMs: E4M3 forward / E5M2 gradients, one UE8M0 scale per "
-                           "1x32 block; bf16 LM head, attention, activations; fp32 master weights / Adam)",
+                           "1x32 block; LM head " + args.lm_head + " (per-tensor); bf16 attention, activations; "
+                           "fp32 master weights / Adam)",
                   "bf16": "bf16"}[args.precision],
         "data": "synthetic uniform-random tokens, random-init N(0,0.02) weights",
         "config": {

@@ -383,11 +383,13 @@ class GptModel(nn.Module):
         from ..ops.fused import LayerNormFn, LMHeadLossFn
 
         h = LayerNormFn.apply(x, (self.ln_f.gamma, self.ln_f.beta), self.ln_f.eps)
-        return LMHeadLossFn.apply(h, targets, (self.lm_head.weight, self.lm_head.bias), grad_scale)
+        return LMHeadLossFn.apply(h, targets, (self.lm_head.weight, self.lm_head.bias), grad_scale,
+                                  self._head_fp8())
 
     # ---------------------------------------------------------------- FP8
     def fp8_weights(self):
-        """(name, weight-like) pairs whose GEMMs run in FP8 (the LM head stays bf16)."""
+        """(name, weight-like) pairs of the transformer blocks' GEMMs (the block recipe;
+        the LM head, when in FP8, uses per-tensor scales, see ``enable_fp8``)."""
         out = []
         for j, blk in enumerate(self.blocks):
             i = self.layer_offset + j
@@ -395,13 +397,14 @@ class GptModel(nn.Module):
                     (f"L{i}.ffn1_w", blk.ff.linear1.weight), (f"L{i}.ffn2_w", blk.ff.linear2.weight)]
         return out
 
-    def enable_fp8(self, history: int = 16, recipe: str = "tensor"):
+    def enable_fp8(self, history: int = 16, recipe: str = "tensor", head: bool = True):
         """E4M3 weights / activations and E5M2 gradients for the block GEMMs; call
         ``refresh_fp8_weights()`` after every optimizer step and ``fp8_state.end_step()``
         at the end of every step.  recipe "tensor": per-tensor scales with delayed
         scaling (amax histories); "mx": MXFP8, one power-of-two scale per 32 values
         along each GEMM's contraction dimension, for all three GEMMs of every block
-        linear (``mtorus.ops.mxfp8``)."""
+        linear (``mtorus.ops.mxfp8``).  head: the LM head's three GEMMs in FP8 as well
+        (per-tensor delayed scaling in both recipes), else bf16."""
         from ..ops.fp8 import Fp8State
 
         assert self.flat is not None, "flatten() first"
@@ -413,12 +416,19 @@ class GptModel(nn.Module):
             if recipe == "tensor":
                 w.w8 = torch.empty(w.shape, dtype=torch.uint8, device=self.flat.device)
             w.fp8_name = name
+        self.fp8_head = bool(head) and self.has_head and self.flat.device.type == "cuda"  # per-tensor kernels
+        if self.fp8_head:
+            w = self.lm_head.weight
+            w.w8 = torch.empty(w.shape, dtype=torch.uint8, device=self.flat.device)
         return self.fp8_state
 
     def refresh_fp8_weights(self):
         from ..ops import fp8 as F8
 
         st = self.fp8_state
+        if getattr(self, "fp8_head", False):
+            w = self.lm_head.weight
+            _, w.w8_inv = st.quantize_into(w.w16, "lm_head.w", F8.E4M3, w.w8)
         if st.recipe == "mx":
             from ..ops.mxfp8 import E4M3, mx_quantize_rc
 
@@ -434,7 +444,12 @@ class GptModel(nn.Module):
         from ..ops.fused import LMHeadLossFn
 
         h = self.fused_hidden(input_ids)
-        return LMHeadLossFn.apply(h, targets, (self.lm_head.weight, self.lm_head.bias), grad_scale)
+        return LMHeadLossFn.apply(h, targets, (self.lm_head.weight, self.lm_head.bias), grad_scale,
+                                  self._head_fp8())
+
+    def _head_fp8(self):
+        """The FP8 state when the LM head runs in FP8, else None."""
+        return getattr(self, "fp8_state", None) if getattr(self, "fp8_head", False) else None
 
 
 def cross_entropy_loss(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:

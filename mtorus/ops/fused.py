@@ -451,26 +451,43 @@ class LMHeadLossFn(Function):
     (reference cross_entropy_loss, examples/gpt-1b/src/main.rs:32-41).
 
     grad_scale (device fp32 scalar, optional) multiplies the gradients, e.g. the
-    dynamic loss scale; the returned loss is unscaled."""
+    dynamic loss scale; the returned loss is unscaled.  fp8 (an ``Fp8State``,
+    optional): the three LM-head GEMMs run in FP8 with per-tensor delayed scaling --
+    h and the weight as E4M3, dlogits as E5M2 -- instead of bf16."""
 
     @staticmethod
-    def forward(ctx, h, targets, params, grad_scale):
+    def forward(ctx, h, targets, params, grad_scale, fp8=None):
         w, b = params
         T = h.shape[0]
-        logits = K.gemm(h, w.w16, bias=b.data)
+        ctx.fp8 = fp8
+        if fp8 is not None:
+            h8, ih = fp8.quantize(h, "lm_head.in", F8.E4M3)
+            logits = F8.gemm_fp8(h8, F8.E4M3, w.w8, F8.E4M3, bias=b.data, alpha=ih, alpha2=w.w8_inv)
+            saved = (h8, ih)
+        else:
+            logits = K.gemm(h, w.w16, bias=b.data)
+            saved = (h,)
         rows = K.xent_fused(logits, targets.reshape(-1), grad_scale, 1.0 / T, True)
-        ctx.save_for_backward(h, logits)
+        ctx.save_for_backward(*saved, logits)
         ctx.params = params
         return rows.mean()
 
     @staticmethod
     def backward(ctx, gloss):
-        h, dlogits = ctx.saved_tensors
         w, b = ctx.params
         acc = FusedGradState.accumulate
         g = gloss.reshape(1).float().contiguous()
-        dh = K.gemm(dlogits, w.w16, b_mn=True, alpha=g)
-        K.gemm(dlogits, h, out=w.main_grad, a_mn=True, b_mn=True, accumulate=acc, alpha=g)
+        if ctx.fp8 is not None:
+            h8, ih, dlogits = ctx.saved_tensors
+            g8, igd = ctx.fp8.quantize(dlogits, "lm_head.grad", F8.E5M2)
+            a = igd * g  # the E5M2 inverse scale times the incoming loss gradient
+            dh = F8.gemm_fp8(g8, F8.E5M2, w.w8, F8.E4M3, b_mn=True, alpha=a, alpha2=w.w8_inv)
+            F8.gemm_fp8(g8, F8.E5M2, h8, F8.E4M3, out=w.main_grad, a_mn=True, b_mn=True, accumulate=acc,
+                        alpha=a, alpha2=ih, out_dtype=torch.float32)
+        else:
+            h, dlogits = ctx.saved_tensors
+            dh = K.gemm(dlogits, w.w16, b_mn=True, alpha=g)
+            K.gemm(dlogits, h, out=w.main_grad, a_mn=True, b_mn=True, accumulate=acc, alpha=g)
         K.colsum_(dlogits, b.main_grad, acc, scale=g)
         _grads_done(w, b)
-        return dh, None, None, None
+        return dh, None, None, None, None

@@ -28,7 +28,7 @@ class GptTrainer:
                  seed: int = 0, dp_group=None, dp: str = "nccl", bucket_mb: float = 25.0,
                  loss_scale: Optional[DeviceLossScaleConfig] = None, max_grad_norm: float = 0.0,
                  weight_decay: float = 0.0, warmup_steps: int = 0, fp8: bool = False,
-                 fp8_history: int = 16, fp8_recipe: str = "tensor"):
+                 fp8_history: int = 16, fp8_recipe: str = "tensor", fp8_head: bool = True):
         self.config = config
         self.device = torch.device(device)
         torch.manual_seed(seed)
@@ -52,7 +52,7 @@ class GptTrainer:
         ls = loss_scale or DeviceLossScaleConfig()
         self.fp8 = fp8
         if fp8:
-            st = self.model.enable_fp8(fp8_history, recipe=fp8_recipe)
+            st = self.model.enable_fp8(fp8_history, recipe=fp8_recipe, head=fp8_head)
             if self.dp == "symm":
                 from ..ops.fp8 import SymmAmaxSync
 

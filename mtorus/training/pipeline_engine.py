@@ -118,7 +118,7 @@ class PipelineTrainer:
                  fp8_history: int = 16, lr: float = 3e-4, device=None, seed: int = 0,
                  bucket_mb: float = 25.0, loss_scale: Optional[DeviceLossScaleConfig] = None,
                  max_grad_norm: float = 0.0, timed: bool = False, split: str = "balanced",
-                 fp8_recipe: str = "tensor", dp_mode: str = "nccl", wire: str = "native"):
+                 fp8_recipe: str = "tensor", dp_mode: str = "nccl", wire: str = "native", fp8_head: bool = True):
         world = dist.get_world_size()
         if world != dp * pp:
             raise ValueError(f"world size {world} != dp {dp} x pp {pp}")
@@ -170,7 +170,7 @@ class PipelineTrainer:
         self.model.enable_dropout(seed * 1000003 + self.replica)
         self.fp8 = fp8
         if fp8:
-            st = self.model.enable_fp8(fp8_history, recipe=fp8_recipe)
+            st = self.model.enable_fp8(fp8_history, recipe=fp8_recipe, head=fp8_head)
             if symm:
                 from ..ops.fp8 import SymmAmaxSync
 
