@@ -175,6 +175,43 @@ def main():
         rows.append(r)
         print(json.dumps(r), flush=True)
         del a, b, out
+    # the MXFP8 epilogues of the fused path: FFN1 forward (bias, GELU, pre-activation stored, GELU
+    # quantised to row + column MX codes) and FFN2 dgrad (dGELU, E5M2 row + column codes, bias-gradient
+    # column sums, no bf16 store), against the same GEMM followed by the separate quantiser
+    epi_cases = [("ffn1_fwd_mx_gelu_mxout", T, F, d), ("ffn2_dgrad_mx_dgelu_mxout", T, F, d)]
+    if args.case:
+        epi_cases = [c for c in epi_cases if c[0] == args.case]
+    for name, M, N, Kd in epi_cases:
+        dgrad = "dgrad" in name
+        a = MX.mx_quantize(torch.randn(M, Kd, device="cuda").bfloat16(), MX.E5M2 if dgrad else MX.E4M3)
+        b = MX.mx_quantize((torch.randn(N, Kd, device="cuda") * 0.02).bfloat16())
+        bias = torch.randn(N, device="cuda") * 0.1
+        pre = torch.randn(M, N, device="cuda").bfloat16()
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        cs = torch.zeros(N, device="cuda")
+        if dgrad:
+            mine = lambda: MX.gemm_mxfp8_mx_out(a, b, MX.E5M2, aux=pre, colsum=cs, store_d=False)
+
+            def unfused():
+                d_ = MX.gemm_mxfp8(a, b, out, aux=pre)
+                MX.mx_quantize_rc(d_, MX.E5M2, colsum=cs)
+        else:
+            mine = lambda: MX.gemm_mxfp8_mx_out(a, b, MX.E4M3, out, bias=bias, gelu=True)
+            act = torch.empty_like(out)
+
+            def unfused():
+                MX.gemm_mxfp8(a, b, out, bias=bias, act=act)
+                MX.mx_quantize_rc(act, MX.E4M3)
+        flops = 2.0 * M * N * Kd
+        tm = timeit(mine, args.iters)
+        tu = timeit(unfused, args.iters)
+        r = {"case": name, "M": M, "N": N, "K": Kd, "layout": "tn_mx", "mine_ms": round(tm, 4),
+             "unfused_ms": round(tu, 4), "mine_tflops": round(flops / tm / 1e9, 1)}
+        if STALLS:
+            r["stalls"] = stalls(mine)
+        rows.append(r)
+        print(json.dumps(r), flush=True)
+        del a, b, out, pre
     for name, M, N, Kd, lay in cases:
         A = torch.randn(M, Kd, device="cuda").bfloat16() if lay != "wgrad" else torch.randn(Kd, M, device="cuda").bfloat16()
         if lay == "tn":
