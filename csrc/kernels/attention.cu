@@ -400,13 +400,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 // ================================================================== backward
 //
 // One CTA per (128-key tile j, batch, head) looping over query tiles i = j .. nt-1.
-// Shared memory: K, V, Q / dO of the current query tile, one tile that first holds
-// P^T (read by the dV MMA) and then dS^T (read by the dK and dQ MMAs), and a 64 KB
-// fp32 staging area from which dQ_i leaves as four [128 x 32] TMA reduce-adds into
-// the fp32 dQ buffer (full-line reductions in L2 instead of scattered atomics).
+// Shared memory: K, V, Q / dO of the current query tile, P^T (read by the dV MMA),
+// dS^T (read by the dK and dQ MMAs) and a 32 KB fp32 box.  P^T and dS^T have tiles of
+// their own, so the compute warps write both in one pass and the dV, dK and dQ MMAs
+// issue back to back.  dQ_i leaves as four [128 x 32] fp32 TMA reduce-adds into the
+// fp32 dQ buffer (full-line reductions in L2 instead of scattered atomics), staged by
+// one column half in the box and by the other in the P^T tile, which the dV MMA has
+// read by then; the next P^T is written after that reduce-add has read the tile.
 // TMEM: S^T | dP^T | dV | dK; dQ_i reuses S^T.
 struct BwdCtl {
-  uint64_t kv_full, q_full, q_empty, do_full, do_empty, st_full, p_ready, pv_done, ds_ready, dq_full, dq_free,
+  uint64_t kv_full, q_full, q_empty, do_full, do_empty, st_full, p_ready, ds_ready, dq_full, dq_free,
       kv_done, drain;
   uint32_t tmem_base;
   int abort;
@@ -430,8 +433,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = smem + kTileBytes;
   uint8_t* sQ = smem + 2 * kTileBytes;
   uint8_t* sDO = smem + 3 * kTileBytes;
-  uint8_t* sPS = smem + 4 * kTileBytes;    // P^T, then dS^T
-  uint8_t* sDQ = smem + 5 * kTileBytes;    // 4 x [128 rows x 128 B] fp32 boxes, SW128
+  uint8_t* sP = smem + 4 * kTileBytes;     // P^T; then dQ boxes 0, 1 of column half 0
+  uint8_t* sDS = smem + 5 * kTileBytes;    // dS^T
+  uint8_t* sDQ = smem + 6 * kTileBytes;    // dQ boxes 2, 3 ([128 rows x 128 B] fp32, SW128) of column half 1
   BwdCtl* ctl = reinterpret_cast<BwdCtl*>(smem + 7 * kTileBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -450,7 +454,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&ctl->do_empty, 1);
     mbar_init(&ctl->st_full, 1);
     mbar_init(&ctl->p_ready, 256);
-    mbar_init(&ctl->pv_done, 1);
     mbar_init(&ctl->ds_ready, 256);
     mbar_init(&ctl->dq_full, 1);
     mbar_init(&ctl->dq_free, 256);
@@ -511,7 +514,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t id_kk = make_idesc_bf16(kTile, kTile, 0, 0);  // A, B K-major
       const uint32_t id_kn = make_idesc_bf16(kTile, kD, 0, 1);     // A K-major, B MN-major
       const uint32_t id_mn = make_idesc_bf16(kTile, kD, 1, 1);     // A, B MN-major
-      const uint32_t k = smem_u32(sK), v = smem_u32(sV), ps = smem_u32(sPS);
+      const uint32_t k = smem_u32(sK), v = smem_u32(sV), ps = smem_u32(sP), dss = smem_u32(sDS);
       bool issued_any = false;
       bool ok = mbar_wait(&ctl->kv_full, 0, abort, status, 22);
       const uint32_t q = smem_u32(sQ), dO = smem_u32(sDO);
@@ -534,17 +537,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dV += P^T dO
           umma_f16(tDV, desc_kmajor(ps, kk), desc_mnmajor(dO, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
-        umma_commit(&ctl->pv_done);
         umma_commit(&ctl->do_empty);  // dO is read by dP^T and dV only
         if (!mbar_wait(&ctl->ds_ready, it & 1, abort, status, 29)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dK += dS^T Q
-          umma_f16(tDK, desc_kmajor(ps, kk), desc_mnmajor(q, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
+          umma_f16(tDK, desc_kmajor(dss, kk), desc_mnmajor(q, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
         umma_commit(&ctl->q_empty);  // Q is read by S^T and dK only
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dQ_i = dS K
-          umma_f16(tDQ, desc_mnmajor(ps, kk), desc_mnmajor(k, kk), id_mn, kk > 0 ? 1u : 0u);
+          umma_f16(tDQ, desc_mnmajor(dss, kk), desc_mnmajor(k, kk), id_mn, kk > 0 ? 1u : 0u);
         umma_commit(&ctl->dq_full);
       }
       if (!*abort) {
@@ -575,6 +577,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // which the MMA of that tile (and so dq_full, waited below) depends on
       dst[ti] = next;
       if (it + 1 < nqi) next = src[(size_t)bh * S + (qi + 1) * kTile + ti] * mul;
+      // column half 0 staged the previous dQ in the P^T tile: its reduce-adds must have read it
+      if (it > 0 && ch == 0 && quarter == 0 && lane == 0) bulk_wait_group_read<0>();
       asm volatile("bar.sync 1, 256;" ::: "memory");
       const float* sl = ctl->lse;
       const float* sd = ctl->dd;
@@ -584,7 +588,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
       const bool diag = qi == kt;
-      uint32_t dsp[32];  // this thread's 64 dS^T values as bf16 pairs, stored after the dV MMA
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c = ch * 2 + cc;
@@ -623,30 +626,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           wp.y = pack_bf16x2(p[2], p[3]);
           wp.z = pack_bf16x2(p[4], p[5]);
           wp.w = pack_bf16x2(p[6], p[7]);
-          *reinterpret_cast<uint4*>(sPS + sw128_chunk(r, c * 4 + g)) = wp;
-#pragma unroll
-          for (int x = 0; x < 4; ++x) dsp[(cc * 32 + g * 8) / 2 + x] = pack_bf16x2(ds[2 * x], ds[2 * x + 1]);
+          *reinterpret_cast<uint4*>(sP + sw128_chunk(r, c * 4 + g)) = wp;
+          uint4 wd;
+          wd.x = pack_bf16x2(ds[0], ds[1]);
+          wd.y = pack_bf16x2(ds[2], ds[3]);
+          wd.z = pack_bf16x2(ds[4], ds[5]);
+          wd.w = pack_bf16x2(ds[6], ds[7]);
+          *reinterpret_cast<uint4*>(sDS + sw128_chunk(r, c * 4 + g)) = wd;
         }
       }
       fence_async_shared();
       tc_fence_before();
       mbar_arrive(&ctl->p_ready);
-      // dS^T replaces P^T once the dV MMA has read it
-      if (!mbar_wait(&ctl->pv_done, it & 1, abort, status, 30)) {
-        ok = false;
-        break;
-      }
-#pragma unroll
-      for (int c16 = 0; c16 < 8; ++c16) {
-        uint4 w;
-        w.x = dsp[c16 * 4 + 0];
-        w.y = dsp[c16 * 4 + 1];
-        w.z = dsp[c16 * 4 + 2];
-        w.w = dsp[c16 * 4 + 3];
-        *reinterpret_cast<uint4*>(sPS + sw128_chunk(r, ch * 8 + c16)) = w;
-      }
-      fence_async_shared();
-      tc_fence_before();
       mbar_arrive(&ctl->ds_ready);
       if (!mbar_wait(&ctl->dq_full, it & 1, abort, status, 27)) {
         ok = false;
@@ -657,12 +648,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const bool leader = (quarter == 0 && lane == 0);  // one thread per column half
       if (leader) bulk_wait_group_read<0>();
       asm volatile("bar.sync %0, 128;" ::"r"(2 + ch) : "memory");
+      // half 0 stages into the P^T tile (read by the dV MMA before dq_full), half 1 into its box
+      uint8_t* boxes = ch == 0 ? sP : sDQ;
 #pragma unroll 1
       for (int c = ch * 2; c < ch * 2 + 2; ++c) {
         uint32_t v[32];
         tmem_ld32(tDQ + lane_off + c * 32, v);
         tmem_wait_ld();
-        uint8_t* box = sDQ + c * kHalf;
+        uint8_t* box = boxes + (c - ch * 2) * kHalf;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           *reinterpret_cast<uint4*>(box + r * 128 + ((k ^ (r & 7)) << 4)) =
@@ -674,8 +667,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       asm volatile("bar.sync %0, 128;" ::"r"(2 + ch) : "memory");
       if (leader) {
         const int y = b * S + qi * kTile;
-        tma_reduce_add_2d(&tma_dq, sDQ + (ch * 2) * kHalf, h * kD + ch * 64, y);
-        tma_reduce_add_2d(&tma_dq, sDQ + (ch * 2 + 1) * kHalf, h * kD + ch * 64 + 32, y);
+        tma_reduce_add_2d(&tma_dq, boxes, h * kD + ch * 64, y);
+        tma_reduce_add_2d(&tma_dq, boxes + kHalf, h * kD + ch * 64 + 32, y);
         bulk_commit_group();
       }
     }

@@ -415,6 +415,30 @@ def test_fp8_wire_codec_kernels_match_reference(dtype):
         assert torch.equal(back[ok], want[ok])
 
 
+def test_gemm_epilogue_gelu_matches_fp32_erf_gelu(K):
+    """The CTA-pair GEMM epilogue's GELU (alternating the special-function-unit and the
+    FMA-pipe forms over its values) and its dGELU agree with PyTorch's fp32 erf GELU
+    to bf16 rounding: D = X . I reproduces X exactly, so act = GELU(X); with A = 1 and
+    aux = X the dGELU epilogue yields GELU'(X)."""
+    M = N = 256
+    x = (torch.rand(M, N, device="cuda") * 16 - 8).bfloat16()
+    eye = torch.eye(N, device="cuda").bfloat16()
+    pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    act = torch.empty_like(pre)
+    K.gemm(x, eye, out=pre, act=act)
+    assert torch.equal(pre, x)
+    ref = F.gelu(x.float())
+    assert bool(((act.float() - ref).abs() <= 2.0 ** -8 * ref.abs() + 2e-6).all())
+    xg = x.float().requires_grad_(True)
+    F.gelu(xg).backward(torch.ones_like(xg))
+    ones = torch.zeros(M, N, device="cuda").bfloat16()
+    ones[:, 0] = 1.0
+    e0 = torch.zeros(N, N, device="cuda").bfloat16()
+    e0[:, 0] = 1.0  # D[m, n] = sum_k ones[m, k] e0[n, k] = 1
+    d = K.gemm(ones, e0, aux=x)
+    assert bool(((d.float() - xg.grad).abs() <= 2.0 ** -8 * xg.grad.abs() + 2e-6).all())
+
+
 def test_gelu_kernels_match_fp32_erf_gelu_elementwise(K):
     """The epilogues' GELU / GELU' (erf from Abramowitz & Stegun 7.1.26, |error| <=
     1.5e-7) agree with PyTorch's fp32 erf GELU to bf16 rounding, element by element,
