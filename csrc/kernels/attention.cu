@@ -413,8 +413,8 @@ struct BwdCtl {
       kv_done, drain;
   uint32_t tmem_base;
   int abort;
-  float lse[kTile];
-  float dd[kTile];
+  alignas(16) float lse[kTile];  // 16-byte aligned: the compute warps read them as vectors
+  alignas(16) float dd[kTile];
 };
 
 constexpr int kBwdThreads = 320;  // producer, MMA, 2 x 4 compute warps (column halves)
@@ -577,8 +577,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // which the MMA of that tile (and so dq_full, waited below) depends on
       dst[ti] = next;
       if (it + 1 < nqi) next = src[(size_t)bh * S + (qi + 1) * kTile + ti] * mul;
-      // column half 0 staged the previous dQ in the P^T tile: its reduce-adds must have read it
-      if (it > 0 && ch == 0 && quarter == 0 && lane == 0) bulk_wait_group_read<0>();
       asm volatile("bar.sync 1, 256;" ::: "memory");
       const float* sl = ctl->lse;
       const float* sd = ctl->dd;
@@ -587,6 +585,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         break;
       }
       tc_fence_after();
+      if (it > 0) {
+        // column half 0 staged the previous dQ in the P^T tile: its reduce-adds must have read
+        // it before any thread writes P^T (waited here, behind this tile's S^T / dP^T MMAs)
+        if (ch == 0 && quarter == 0 && lane == 0) bulk_wait_group_read<0>();
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+      }
       const bool diag = qi == kt;
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {

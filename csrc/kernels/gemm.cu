@@ -83,9 +83,6 @@ constexpr int kThreads = 192;
 
 __device__ __forceinline__ float gelu_f(float x) { return gelu_fwd(x); }
 __device__ __forceinline__ float gelu_grad_f(float x) { return gelu_grad(x); }
-// The CTA-pair epilogue alternates GELU forms over its values (odd ones on the FMA
-// pipe, see gelu.cuh): the special-function unit, also busy with the FP8 and bf16
-// conversions, then carries half of the exponentials and reciprocals.
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
@@ -504,7 +501,7 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
       float a8[8];
       unpack8(*reinterpret_cast<const bf16x8*>(&x[j]), a8);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[j * 8 + i] *= (i & 1 ? gelu_grad_fma(a8[i]) : gelu_grad(a8[i]));
+      for (int i = 0; i < 8; ++i) v[j * 8 + i] *= gelu_grad_f(a8[i]);
     }
   } else if (ep.residual) {
 #pragma unroll
@@ -534,7 +531,7 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
         float p8[8], g8[8];
         unpack8(pk, p8);  // GELU of the rounded pre-activation, as the bf16 path stores it
 #pragma unroll
-        for (int i = 0; i < 8; ++i) g8[i] = (i & 1 ? gelu_fwd_fma(p8[i]) : gelu_fwd(p8[i]));
+        for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
         if constexpr (DROP) {
           if (drop_mode == 2) {
             float r8[8];
@@ -608,7 +605,7 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
         float p8[8], g8[8];
         unpack8(pk, p8);  // GELU of the rounded pre-activation
 #pragma unroll
-        for (int i = 0; i < 8; ++i) g8[i] = (i & 1 ? gelu_fwd_fma(p8[i]) : gelu_fwd(p8[i]));
+        for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
         if constexpr (DROP) {
           if (drop_mode == 2) {
             float r8[8];
@@ -624,7 +621,7 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
         float p8[8], g8[8], r8[8];
         unpack8(pk, p8);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) g8[i] = (i & 1 ? gelu_fwd_fma(p8[i]) : gelu_fwd(p8[i]));
+        for (int i = 0; i < 8; ++i) g8[i] = gelu_f(p8[i]);
         unpack8(pack8(g8), r8);
         if constexpr (DROP) {
           if (drop_mode == 2) {
