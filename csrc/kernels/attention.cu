@@ -119,6 +119,36 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two values).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 
 template <bool DROP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
@@ -326,15 +356,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
       }
       l *= alpha;
-      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent partial row sums
+      // 8 independent partial row sums as 4 packed pairs; scores scaled on pairs (f32x2)
+      uint64_t s8[4] = {0ull, 0ull, 0ull, 0ull};
       const float neg = -m_ref;
+      const uint64_t sl2p = f2pack(sl2, sl2), negp = f2pack(neg, neg);
 #pragma unroll
       for (int c16 = 0; c16 < kTile / 8; ++c16) {
         float pv[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = ex2_approx(fmaf(__uint_as_float(t[c16 * 8 + e]), sl2, neg));
-          s8[e] += pv[e];
+        for (int e = 0; e < 8; e += 2) {
+          float a0, a1;
+          f2unpack(fma2(f2pack(__uint_as_float(t[c16 * 8 + e]), __uint_as_float(t[c16 * 8 + e + 1])), sl2p, negp),
+                   a0, a1);
+          pv[e] = ex2_approx(a0);
+          pv[e + 1] = ex2_approx(a1);
+          s8[e / 2] = add2(s8[e / 2], f2pack(pv[e], pv[e + 1]));
         }
         if constexpr (DROP) {  // keys j*128 + 8*c16 .. +7 of query row qt*128 + r
           const uint32_t keep = keepw[c16 >> 2] >> ((c16 & 3) * 8);
@@ -348,7 +384,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         w.w = pack_bf16x2(pv[6], pv[7]);
         *reinterpret_cast<uint4*>(myP + sw128_chunk(r, c16)) = w;
       }
-      l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      float sp[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) f2unpack(s8[k], sp[2 * k], sp[2 * k + 1]);
+      l += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       // rescale O (rows whose max grew) before PV_g(j) accumulates into it
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
@@ -400,20 +439,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 // ================================================================== backward
 //
 // One CTA per (128-key tile j, batch, head) looping over query tiles i = j .. nt-1.
-// Shared memory: K, V, Q / dO of the current query tile, P^T (read by the dV MMA),
-// dS^T (read by the dK and dQ MMAs) and a 32 KB fp32 box.  P^T and dS^T have tiles of
-// their own, so the compute warps write both in one pass and the dV, dK and dQ MMAs
-// issue back to back.  dQ_i leaves as four [128 x 32] fp32 TMA reduce-adds into the
-// fp32 dQ buffer (full-line reductions in L2 instead of scattered atomics), staged by
-// one column half in the box and by the other in the P^T tile, which the dV MMA has
-// read by then; the next P^T is written after that reduce-add has read the tile.
+// Shared memory: K, V, Q / dO of the current query tile, one tile that first holds
+// P^T (read by the dV MMA) and then dS^T (read by the dK and dQ MMAs), and a 64 KB
+// fp32 staging area from which dQ_i leaves as four [128 x 32] TMA reduce-adds into
+// the fp32 dQ buffer (full-line reductions in L2 instead of scattered atomics).
 // TMEM: S^T | dP^T | dV | dK; dQ_i reuses S^T.
 struct BwdCtl {
-  uint64_t kv_full, q_full, q_empty, do_full, do_empty, st_full, p_ready, ds_ready, dq_full, dq_free,
+  uint64_t kv_full, q_full, q_empty, do_full, do_empty, st_full, p_ready, pv_done, ds_ready, dq_full, dq_free,
       kv_done, drain;
   uint32_t tmem_base;
   int abort;
-  alignas(16) float lse[kTile];  // 16-byte aligned: the compute warps read them as vectors
+  alignas(16) float lse[kTile];
   alignas(16) float dd[kTile];
 };
 
@@ -433,9 +469,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = smem + kTileBytes;
   uint8_t* sQ = smem + 2 * kTileBytes;
   uint8_t* sDO = smem + 3 * kTileBytes;
-  uint8_t* sP = smem + 4 * kTileBytes;     // P^T; then dQ boxes 0, 1 of column half 0
-  uint8_t* sDS = smem + 5 * kTileBytes;    // dS^T
-  uint8_t* sDQ = smem + 6 * kTileBytes;    // dQ boxes 2, 3 ([128 rows x 128 B] fp32, SW128) of column half 1
+  uint8_t* sPS = smem + 4 * kTileBytes;    // P^T, then dS^T
+  uint8_t* sDQ = smem + 5 * kTileBytes;    // 4 x [128 rows x 128 B] fp32 boxes, SW128
   BwdCtl* ctl = reinterpret_cast<BwdCtl*>(smem + 7 * kTileBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -454,6 +489,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&ctl->do_empty, 1);
     mbar_init(&ctl->st_full, 1);
     mbar_init(&ctl->p_ready, 256);
+    mbar_init(&ctl->pv_done, 1);
     mbar_init(&ctl->ds_ready, 256);
     mbar_init(&ctl->dq_full, 1);
     mbar_init(&ctl->dq_free, 256);
@@ -514,7 +550,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t id_kk = make_idesc_bf16(kTile, kTile, 0, 0);  // A, B K-major
       const uint32_t id_kn = make_idesc_bf16(kTile, kD, 0, 1);     // A K-major, B MN-major
       const uint32_t id_mn = make_idesc_bf16(kTile, kD, 1, 1);     // A, B MN-major
-      const uint32_t k = smem_u32(sK), v = smem_u32(sV), ps = smem_u32(sP), dss = smem_u32(sDS);
+      const uint32_t k = smem_u32(sK), v = smem_u32(sV), ps = smem_u32(sPS);
       bool issued_any = false;
       bool ok = mbar_wait(&ctl->kv_full, 0, abort, status, 22);
       const uint32_t q = smem_u32(sQ), dO = smem_u32(sDO);
@@ -537,16 +573,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dV += P^T dO
           umma_f16(tDV, desc_kmajor(ps, kk), desc_mnmajor(dO, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
+        umma_commit(&ctl->pv_done);
         umma_commit(&ctl->do_empty);  // dO is read by dP^T and dV only
         if (!mbar_wait(&ctl->ds_ready, it & 1, abort, status, 29)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dK += dS^T Q
-          umma_f16(tDK, desc_kmajor(dss, kk), desc_mnmajor(q, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
+          umma_f16(tDK, desc_kmajor(ps, kk), desc_mnmajor(q, kk), id_kn, (it | kk) != 0 ? 1u : 0u);
         umma_commit(&ctl->q_empty);  // Q is read by S^T and dK only
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)  // dQ_i = dS K
-          umma_f16(tDQ, desc_mnmajor(dss, kk), desc_mnmajor(k, kk), id_mn, kk > 0 ? 1u : 0u);
+          umma_f16(tDQ, desc_mnmajor(ps, kk), desc_mnmajor(k, kk), id_mn, kk > 0 ? 1u : 0u);
         umma_commit(&ctl->dq_full);
       }
       if (!*abort) {
@@ -567,7 +604,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     // the tile's log-sum-exp (log2 units; threads 0-127) and D (threads 128-255), fetched a tile ahead
     const float* src = tid < kTile ? lse : dvec;
-    const float mul = tid < kTile ? kLog2e : 1.f;
+    const float mul = tid < kTile ? -kLog2e : 1.f;  // smem holds -lse (log2 units) and D
     float* dst = tid < kTile ? ctl->lse : ctl->dd;
     const int ti = tid & (kTile - 1);
     float next = src[(size_t)bh * S + kt * kTile + ti] * mul;
@@ -585,13 +622,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         break;
       }
       tc_fence_after();
-      if (it > 0) {
-        // column half 0 staged the previous dQ in the P^T tile: its reduce-adds must have read
-        // it before any thread writes P^T (waited here, behind this tile's S^T / dP^T MMAs)
-        if (ch == 0 && quarter == 0 && lane == 0) bulk_wait_group_read<0>();
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-      }
       const bool diag = qi == kt;
+      uint32_t dsp[32];  // this thread's 64 dS^T values as bf16 pairs, stored after the dV MMA
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c = ch * 2 + cc;
@@ -610,19 +642,43 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                  (lane & 3);
             kb = dropout_keep8(drop.rng[0], drop.rng[1], drop.site, grp, drop.thr16);
           }
+          if constexpr (DROP) {
 #pragma unroll
-          for (int x = 0; x < 8; ++x) {
-            const int e = g * 8 + x, col = c * 32 + e;  // query within the tile
-            float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, -sl[col]));
-            if (diag && col < r) pe = 0.f;  // query before key: masked in the forward
-            if constexpr (DROP) {
+            for (int x = 0; x < 8; ++x) {
+              const int e = g * 8 + x, col = c * 32 + e;  // query within the tile
+              float pe = ex2_approx(fmaf(__uint_as_float(sv[e]), sl2, sl[col]));
+              if (diag && col < r) pe = 0.f;  // query before key: masked in the forward
               // the key bit of query e sits in the block of lane 4x + (key's 8-group within the warp)
               const bool keep = (__shfl_sync(0xffffffffu, kb, x * 4 + (lane >> 3)) >> (lane & 7)) & 1u;
               p[x] = keep ? pe * drop.scale : 0.f;
               ds[x] = pe * ((keep ? __uint_as_float(dv[e]) * drop.scale : 0.f) - sd[col]) * scale;
-            } else {
-              p[x] = pe;
-              ds[x] = pe * (__uint_as_float(dv[e]) - sd[col]) * scale;
+            }
+          } else {
+            // the same on value pairs: vector loads of -lse / D, packed f32x2 arithmetic
+            const int col0 = c * 32 + g * 8;
+            const float4 la = *reinterpret_cast<const float4*>(sl + col0);
+            const float4 lb = *reinterpret_cast<const float4*>(sl + col0 + 4);
+            const float4 da = *reinterpret_cast<const float4*>(sd + col0);
+            const float4 db = *reinterpret_cast<const float4*>(sd + col0 + 4);
+            const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+            const float dd8[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+            const uint64_t s2 = f2pack(sl2, sl2), sc2 = f2pack(scale, scale);
+#pragma unroll
+            for (int x = 0; x < 8; x += 2) {
+              const int e = g * 8 + x, col = col0 + x;
+              float a0, a1;
+              f2unpack(fma2(f2pack(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), s2, f2pack(lv[x], lv[x + 1])),
+                       a0, a1);
+              float pe0 = ex2_approx(a0), pe1 = ex2_approx(a1);
+              if (diag) {  // queries before the key: masked in the forward
+                if (col < r) pe0 = 0.f;
+                if (col + 1 < r) pe1 = 0.f;
+              }
+              p[x] = pe0;
+              p[x + 1] = pe1;
+              const uint64_t q = sub2(f2pack(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])),
+                                      f2pack(dd8[x], dd8[x + 1]));
+              f2unpack(mul2(mul2(f2pack(pe0, pe1), sc2), q), ds[x], ds[x + 1]);
             }
           }
           uint4 wp;
@@ -630,18 +686,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           wp.y = pack_bf16x2(p[2], p[3]);
           wp.z = pack_bf16x2(p[4], p[5]);
           wp.w = pack_bf16x2(p[6], p[7]);
-          *reinterpret_cast<uint4*>(sP + sw128_chunk(r, c * 4 + g)) = wp;
-          uint4 wd;
-          wd.x = pack_bf16x2(ds[0], ds[1]);
-          wd.y = pack_bf16x2(ds[2], ds[3]);
-          wd.z = pack_bf16x2(ds[4], ds[5]);
-          wd.w = pack_bf16x2(ds[6], ds[7]);
-          *reinterpret_cast<uint4*>(sDS + sw128_chunk(r, c * 4 + g)) = wd;
+          *reinterpret_cast<uint4*>(sPS + sw128_chunk(r, c * 4 + g)) = wp;
+#pragma unroll
+          for (int x = 0; x < 4; ++x) dsp[(cc * 32 + g * 8) / 2 + x] = pack_bf16x2(ds[2 * x], ds[2 * x + 1]);
         }
       }
       fence_async_shared();
       tc_fence_before();
       mbar_arrive(&ctl->p_ready);
+      // dS^T replaces P^T once the dV MMA has read it
+      if (!mbar_wait(&ctl->pv_done, it & 1, abort, status, 30)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int c16 = 0; c16 < 8; ++c16) {
+        uint4 w;
+        w.x = dsp[c16 * 4 + 0];
+        w.y = dsp[c16 * 4 + 1];
+        w.z = dsp[c16 * 4 + 2];
+        w.w = dsp[c16 * 4 + 3];
+        *reinterpret_cast<uint4*>(sPS + sw128_chunk(r, ch * 8 + c16)) = w;
+      }
+      fence_async_shared();
+      tc_fence_before();
       mbar_arrive(&ctl->ds_ready);
       if (!mbar_wait(&ctl->dq_full, it & 1, abort, status, 27)) {
         ok = false;
@@ -652,14 +720,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const bool leader = (quarter == 0 && lane == 0);  // one thread per column half
       if (leader) bulk_wait_group_read<0>();
       asm volatile("bar.sync %0, 128;" ::"r"(2 + ch) : "memory");
-      // half 0 stages into the P^T tile (read by the dV MMA before dq_full), half 1 into its box
-      uint8_t* boxes = ch == 0 ? sP : sDQ;
 #pragma unroll 1
       for (int c = ch * 2; c < ch * 2 + 2; ++c) {
         uint32_t v[32];
         tmem_ld32(tDQ + lane_off + c * 32, v);
         tmem_wait_ld();
-        uint8_t* box = boxes + (c - ch * 2) * kHalf;
+        uint8_t* box = sDQ + c * kHalf;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           *reinterpret_cast<uint4*>(box + r * 128 + ((k ^ (r & 7)) << 4)) =
@@ -671,8 +737,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       asm volatile("bar.sync %0, 128;" ::"r"(2 + ch) : "memory");
       if (leader) {
         const int y = b * S + qi * kTile;
-        tma_reduce_add_2d(&tma_dq, boxes, h * kD + ch * 64, y);
-        tma_reduce_add_2d(&tma_dq, boxes + kHalf, h * kD + ch * 64 + 32, y);
+        tma_reduce_add_2d(&tma_dq, sDQ + (ch * 2) * kHalf, h * kD + ch * 64, y);
+        tma_reduce_add_2d(&tma_dq, sDQ + (ch * 2 + 1) * kHalf, h * kD + ch * 64 + 32, y);
         bulk_commit_group();
       }
     }
