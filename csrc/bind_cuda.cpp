@@ -127,7 +127,7 @@ void symm_scalars_ar(const std::vector<int64_t>& scal, const std::vector<int64_t
 void symm_epoch_advance(at::Tensor ep);
 void symm_adam_shard_ag(const at::Tensor& ranges, at::Tensor master, at::Tensor m, at::Tensor v,
                         const at::Tensor& grad, const std::vector<int64_t>& w16, const at::Tensor& st,
-                        double lr, double beta1, double beta2, double eps, double wd);
+                        double lr, double beta1, double beta2, double eps, double wd, int64_t w16_mc);
 void symm_barrier(const std::vector<int64_t>& flags, int64_t me, int64_t slot, int64_t epoch,
                   int64_t code, int64_t ep_ptr);
 void symm_allreduce(const std::vector<int64_t>& bufs, const std::vector<int64_t>& flags, int64_t me,
@@ -208,7 +208,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("st"), py::arg("ctas"), py::arg("inv_n"), py::arg("ep_ptr") = 0);
   m.def("symm_scalars_ar", &symm_scalars_ar, py::arg("scal"), py::arg("flags"), py::arg("me"), py::arg("slot"),
         py::arg("epoch"), py::arg("st"), py::arg("ep_ptr") = 0);
-  m.def("symm_adam_shard_ag", &symm_adam_shard_ag);
+  m.def("symm_adam_shard_ag", &symm_adam_shard_ag, py::arg("ranges"), py::arg("master"), py::arg("m"),
+        py::arg("v"), py::arg("grad"), py::arg("w16"), py::arg("st"), py::arg("lr"), py::arg("beta1"),
+        py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("w16_mc") = 0);
   m.def("symm_barrier", &symm_barrier, py::arg("flags"), py::arg("me"), py::arg("slot"), py::arg("epoch"),
         py::arg("code"), py::arg("ep_ptr") = 0);
   m.def("symm_epoch_advance", &symm_epoch_advance);

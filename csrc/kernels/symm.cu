@@ -88,6 +88,38 @@ __device__ __forceinline__ bool block_barrier(const PeerPtrs& flags, const uint3
   return ok != 0;
 }
 
+// ------------------------------------------------------------------ NVLS (multimem) collectives
+// The symmetric buffers are also bound to an NVLink multicast object: a
+// `multimem.ld_reduce` through the multicast address returns the sum of that
+// element over every GPU (the NVSwitch reduces in the switch), a `multimem.st`
+// writes one value into every GPU's copy.  All-reduce: each rank reduces its
+// 1/N slice in the switch and stores the result back to all ranks (each byte
+// crosses its link about twice, independent of N); broadcast: the root stores
+// once and the switch replicates.
+__device__ __forceinline__ void mc_ld_reduce_f32(uint64_t a, float4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(a)
+               : "memory");
+}
+__device__ __forceinline__ void mc_ld_reduce_bf16(uint64_t a, uint4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(a)
+               : "memory");
+}
+__device__ __forceinline__ void mc_st_16(uint64_t a, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
+__device__ __forceinline__ void mc_publish_fence() {
+  // multicast stores alias the unicast buffers the consumers read
+  asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+}
+
 // A context's device-resident step counter: with ep set, a kernel's effective epoch
 // is the host value plus *ep, so a CUDA graph that advances the counter (one
 // epoch_advance launch per step) replays with fresh epochs.
@@ -190,10 +222,13 @@ __global__ void scalars_ar_kernel(PeerPtrs scal, PeerPtrs flags, uint32_t* my_fl
 
 // ------------------------------------------------------------------ sharded Adam + all-gather
 // ranges[r] = {flat offset, length, compact (m/v) offset}; blockIdx.y = range.
+// w16_mc (non-zero): the multicast address of the bf16 weight buffer; each new weight
+// vector is then stored once through the switch, which writes it into every rank's copy
+// (one store instead of n, so the all-gather costs 1/n of the NVLink bytes).
 __global__ void __launch_bounds__(256) adam_shard_ag_kernel(
     const int64_t* __restrict__ ranges, float* __restrict__ master, float* __restrict__ m,
     float* __restrict__ v, const float* __restrict__ grad, PeerPtrs w16, int n,
-    const float* __restrict__ st, float lr, float beta1, float beta2, float eps, float wd) {
+    const float* __restrict__ st, float lr, float beta1, float beta2, float eps, float wd, uint64_t w16_mc) {
   const int64_t off = ranges[blockIdx.y * 3], len = ranges[blockIdx.y * 3 + 1],
                 moff = ranges[blockIdx.y * 3 + 2];
   const bool skip = st[5] > 0.f;  // kStSkip
@@ -232,10 +267,15 @@ __global__ void __launch_bounds__(256) adam_shard_ag_kernel(
       *reinterpret_cast<float4*>(v + mo + 4) = *reinterpret_cast<float4*>(vf + 4);
     }
     const bf16x8 w = pack8(pf);
+    if (w16_mc) {
+      mc_st_16(w16_mc + (uint64_t)o * 2, *reinterpret_cast<const uint4*>(&w));
+    } else {
 #pragma unroll
-    for (int p = 0; p < kMaxPeers; ++p)
-      if (p < n) reinterpret_cast<bf16x8*>(reinterpret_cast<bf16*>(w16.p[p]) + o)[0] = w;
+      for (int p = 0; p < kMaxPeers; ++p)
+        if (p < n) reinterpret_cast<bf16x8*>(reinterpret_cast<bf16*>(w16.p[p]) + o)[0] = w;
+    }
   }
+  if (w16_mc) mc_publish_fence();  // the multicast stores before the barrier that publishes them
 }
 
 // Signal (this rank finished writing into peers) then wait for everyone.
@@ -245,6 +285,9 @@ __global__ void barrier_kernel(PeerPtrs flags, uint32_t* my_flags, int me, int n
   epoch = resolve_epoch(epoch, ep);
   signal_peers(flags, me, n, slot, epoch);
   wait_peers(my_flags, n, slot, epoch, status, code);
+  // peers may have written this rank's buffers through a multicast alias: order those
+  // before the unicast reads of the kernels that follow
+  asm volatile("fence.proxy.alias;" ::: "memory");
 }
 
 // ------------------------------------------------------------------ standalone collectives
@@ -344,37 +387,6 @@ __global__ void __launch_bounds__(512) halo_kernel(const uint4* __restrict__ src
   }
 }
 
-// ------------------------------------------------------------------ NVLS (multimem) collectives
-// The symmetric buffers are also bound to an NVLink multicast object: a
-// `multimem.ld_reduce` through the multicast address returns the sum of that
-// element over every GPU (the NVSwitch reduces in the switch), a `multimem.st`
-// writes one value into every GPU's copy.  All-reduce: each rank reduces its
-// 1/N slice in the switch and stores the result back to all ranks (each byte
-// crosses its link about twice, independent of N); broadcast: the root stores
-// once and the switch replicates.
-__device__ __forceinline__ void mc_ld_reduce_f32(uint64_t a, float4& v) {
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(a)
-               : "memory");
-}
-__device__ __forceinline__ void mc_ld_reduce_bf16(uint64_t a, uint4& v) {
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(a)
-               : "memory");
-}
-__device__ __forceinline__ void mc_st_16(uint64_t a, const uint4& v) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a),
-               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
-               "f"(__uint_as_float(v.w))
-               : "memory");
-}
-__device__ __forceinline__ void mc_publish_fence() {
-  // multicast stores alias the unicast buffers the consumers read
-  asm volatile("fence.proxy.alias;" ::: "memory");
-  __threadfence_system();
-}
 
 template <int DT>  // 0: fp32, 1: bf16
 __global__ void __launch_bounds__(512) allreduce_mc_kernel(uint64_t mc, PeerPtrs flags, uint32_t* my_flags,
@@ -772,14 +784,15 @@ void symm_scalars_ar(const std::vector<int64_t>& scal, const std::vector<int64_t
 
 void symm_adam_shard_ag(const at::Tensor& ranges, at::Tensor master, at::Tensor m, at::Tensor v,
                         const at::Tensor& grad, const std::vector<int64_t>& w16, const at::Tensor& st,
-                        double lr, double beta1, double beta2, double eps, double wd) {
+                        double lr, double beta1, double beta2, double eps, double wd, int64_t w16_mc) {
+  MT_CHECK(w16_mc % 16 == 0, "symm_adam_shard_ag: 16-byte aligned multicast address");
   const int nr = ranges.size(0);
   if (nr == 0) return;
   dim3 grid(std::max(1, num_sms() * 4 / std::max(nr, 1)), nr);
   adam_shard_ag_kernel<<<grid, 256, 0, cur_stream()>>>(
       ranges.data_ptr<int64_t>(), master.data_ptr<float>(), m.data_ptr<float>(),
       v.data_ptr<float>(), grad.data_ptr<float>(), to_peers(w16), (int)w16.size(),
-      st.data_ptr<float>(), (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd);
+      st.data_ptr<float>(), (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, (uint64_t)w16_mc);
   MT_LAUNCH_CHECK();
 }
 

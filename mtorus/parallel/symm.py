@@ -91,6 +91,15 @@ class SymmContext:
         return int(_cuda().symm_status(reset))
 
 
+def _mc_choice(env: str, world: int) -> bool:
+    """A multicast (NVLS) variant: the environment variable forces it on ("1") or off ("0");
+    unset, it is on from 4 ranks up."""
+    import os
+
+    v = os.environ.get(env)
+    return v == "1" if v in ("0", "1") else world >= 4
+
+
 def _chunk_len(n_elems: int, world: int) -> int:
     c = (n_elems + world - 1) // world
     return (c + _ALIGN - 1) // _ALIGN * _ALIGN
@@ -137,8 +146,11 @@ class SymmBucketReducer:
         self.shard_numel = moff
         self.ranges = torch.tensor(ranges, dtype=torch.int64, device=flat.device).reshape(-1, 3)
         self._reserved = False
-        # NVLS reduce-scatter (multimem.ld_reduce) when asked for and the buffer has a multicast binding
-        self.nvls = os.environ.get("MTORUS_DP_NVLS") == "1" and self.flat.symm_grad.mc != 0
+        # NVLS reduce-scatter (multimem.ld_reduce: the switch sums a chunk over all ranks, so each rank
+        # receives its chunk once instead of n - 1 times) when the buffer has a multicast binding:
+        # by default from 4 ranks up (with 2 the switch round trip buys nothing); MTORUS_DP_NVLS=1 / 0
+        # forces it on / off
+        self.nvls = _mc_choice("MTORUS_DP_NVLS", self.world) and self.flat.symm_grad.mc != 0
         # E5M2 gradient transport (opt-in): buckets cross NVLink as E5M2 codes with one
         # power-of-two scale per 32 values, decoded and summed in fp32 by the reduce kernel
         self.grad_fp8 = grad_fp8 if grad_fp8 is not None else os.environ.get("MTORUS_DP_GRAD_FP8") == "1"
@@ -233,6 +245,11 @@ class ZeroAdam:
         self.state = torch.zeros(16, dtype=torch.float32, device=dev)
         self.state[ST_SCALE] = self.ls.init_scale
         reducer.state = self.state
+        # the new bf16 weights leave through the weight buffer's multicast address (one store,
+        # replicated by the switch) when it has one: by default from 4 ranks up
+        # (MTORUS_DP_AG_MC=1 / 0 forces it on / off)
+        mc = flat.symm_w16.mc
+        self.w16_mc = mc if mc and _mc_choice("MTORUS_DP_AG_MC", reducer.world) else 0
 
     @property
     def loss_scale_tensor(self) -> torch.Tensor:
@@ -258,7 +275,7 @@ class ZeroAdam:
         r = self.reducer
         _cuda().symm_adam_shard_ag(r.ranges, self.flat.master, self.m, self.v, self.flat.grad,
                                    self.flat.symm_w16.ptrs, self.state, self.lr if lr is None else lr,
-                                   self.betas[0], self.betas[1], self.eps, self.weight_decay)
+                                   self.betas[0], self.betas[1], self.eps, self.weight_decay, self.w16_mc)
         # every rank has written its shard into every peer: order the next forward after it
         _cuda().symm_barrier(r.ctx.flags.ptrs, r.me, r.slot_ag, r.epoch, 23, r.ep_ptr)
 

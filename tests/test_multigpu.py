@@ -64,13 +64,15 @@ def test_symm_collectives_2gpu():
         assert torch.equal(o["halo"][:128], torch.full((128,), float(peer)))
 
 
-def _dp_body(rank, world, dp, nvls=False):
+def _dp_body(rank, world, dp, nvls=False, ag_mc=False):
     import os
 
     import torch
 
     if nvls:
         os.environ["MTORUS_DP_NVLS"] = "1"
+    if ag_mc:
+        os.environ["MTORUS_DP_AG_MC"] = "1"
     from mtorus.models.gpt import GptConfig
     from mtorus.training.engine import GptTrainer
 
@@ -87,7 +89,7 @@ def _dp_body(rank, world, dp, nvls=False):
     st = 0
     if dp == "symm":
         st = tr.reducer.ctx.status()
-        if nvls and not tr.reducer.nvls:
+        if (nvls and not tr.reducer.nvls) or (ag_mc and not tr.opt.w16_mc):
             st = -1  # no multicast binding on this fabric: nothing to compare
     return losses, w, st
 
@@ -226,6 +228,23 @@ def test_pipeline_trainer_matches_single_gpu(sched, ckpt):
             assert err < 5e-2, (r, name, float(err))
             checked += 1
     assert checked == len(ref_grads)
+
+
+@needs2
+def test_fused_dp_multicast_weight_allgather_matches_peer_stores():
+    """The sharded Adam storing the new weights once through the multicast address (the
+    default from 4 ranks up) gives the same trajectory and bit-identical weights on every
+    rank as storing them into each peer."""
+    a = run_dist(_dp_body, 2, ("symm",), backend="nccl")
+    b = run_dist(_dp_body, 2, ("symm", False, True), backend="nccl")
+    if b[0][2] == -1:
+        pytest.skip("no NVLink multicast on this fabric")
+    for r in range(2):
+        assert b[r][2] == 0
+        for x, y in zip(a[r][0], b[r][0]):
+            assert abs(x - y) < 2e-2 * max(1.0, abs(x)), (a[r][0], b[r][0])
+        assert torch.allclose(a[r][1], b[r][1], atol=2e-2, rtol=2e-2)
+    assert torch.equal(b[0][1], b[1][1])
 
 
 def _amax_body(rank, world, kind):
