@@ -5,9 +5,11 @@ every precision, so the curves differ only by the GEMM arithmetic.
 
     python bench/convergence.py --steps 60 --precisions bf16,fp8,mxfp8,mxfp8/head-bf16
 
-Data: a fixed random first-order Markov chain over the vocabulary in which every
-token has ``--branching`` equally likely successors, so the achievable loss is
-ln(branching) (1.39 nats for 4) while a fresh model starts near ln(V).  Each step
+Data: a fixed random first-order Markov chain over the first ``--active-vocab``
+token ids (of the model's full vocabulary) in which every token has ``--branching``
+equally likely successors, so the achievable loss is ln(branching) (1.39 nats for 4)
+while a fresh model starts near ln(V): within a few steps it learns which ids occur
+(ln(active-vocab)), then the transitions.  Each step
 draws a new batch from the chain (host RNG, seeded), copies it in, and runs one
 ``GptTrainer.step_device``.  A precision with the suffix ``/head-bf16`` keeps the LM
 head in bf16 (the FP8 precisions run it in FP8 by default).  Prints one JSON line per
@@ -26,7 +28,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
 def markov_batches(vocab: int, branching: int, batch: int, seq: int, steps: int, seed: int):
-    """steps batches of [batch, seq + 1] tokens from a fixed random Markov chain."""
+    """steps batches of [batch, seq + 1] tokens in [0, vocab) from a fixed random Markov chain."""
     import torch
 
     g = torch.Generator().manual_seed(seed)
@@ -48,6 +50,7 @@ def main(argv=None) -> int:
     ap.add_argument("--micro-batch", type=int, default=8)
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--branching", type=int, default=4)
+    ap.add_argument("--active-vocab", type=int, default=1024, help="token ids the chain uses (<= the vocabulary)")
     ap.add_argument("--lr", type=float, default=3e-4)
     ap.add_argument("--warmup", type=int, default=10, help="linear learning-rate warmup steps")
     ap.add_argument("--seed", type=int, default=1234)
@@ -60,7 +63,8 @@ def main(argv=None) -> int:
 
     cfg = GptConfig.gpt_1b_bench()
     cfg.num_layers = args.layers
-    batches = markov_batches(cfg.vocab_size, args.branching, args.micro_batch, args.seq, args.steps, args.seed)
+    batches = markov_batches(min(args.active_vocab, cfg.vocab_size), args.branching, args.micro_batch, args.seq,
+                             args.steps, args.seed)
     curves = {}
     for prec in args.precisions.split(","):
         base_prec, _, opt = prec.partition("/")
@@ -80,7 +84,8 @@ def main(argv=None) -> int:
     base = curves.get("bf16")
     tail = max(1, args.steps // 4)
     summary = {"model": f"GPT-1B shape, {cfg.num_layers} layers", "tokens_per_step": args.micro_batch * args.seq,
-               "data": f"random Markov chain, {args.branching} successors per token (floor ln {args.branching} = "
+               "data": f"random Markov chain over {min(args.active_vocab, cfg.vocab_size)} token ids, "
+                       f"{args.branching} successors per token (floor ln {args.branching} = "
                        f"{torch.log(torch.tensor(float(args.branching))).item():.3f})",
                "final_loss": {p: round(c[-1], 4) for p, c in curves.items()}}
     if base is not None:
