@@ -79,7 +79,7 @@ void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at:
                          at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, at::Tensor mean,
                          at::Tensor rstd, int64_t fmt, double fmax);
 void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, int64_t fmt,
-                    double fmax, const c10::optional<at::Tensor>& colsum);
+                    double fmax, const c10::optional<at::Tensor>& colsum, const c10::optional<at::Tensor>& xq);
 void gemm_fp8_gather_b(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
                        int64_t b_fmt, const std::vector<int64_t>& b_peers, int64_t shard_rows, at::Tensor D,
                        const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
@@ -91,7 +91,7 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, in
                                  double drop_scale);
 at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
                     int64_t B, int64_t S, int64_t H, const c10::optional<at::Tensor>& drop_rng, int64_t drop_site,
-                    int64_t drop_thr16, double drop_scale);
+                    int64_t drop_thr16, double drop_scale, const c10::optional<at::Tensor>& dq_out);
 int64_t attn_status(bool reset);
 // fp8.cu
 void fp8_quantize(const at::Tensor& x, at::Tensor out, const c10::optional<at::Tensor>& scale,
@@ -254,7 +254,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("st"), py::arg("ctas"), py::arg("inv_n"), py::arg("mine"), py::arg("ep_ptr") = 0);
   m.def("layernorm_fwd_mx_rc", &layernorm_fwd_mx_rc);
   m.def("mx_quantize_rc", &mx_quantize_rc, py::arg("x"), py::arg("rc"), py::arg("rsf"), py::arg("cc"),
-        py::arg("csf"), py::arg("fmt"), py::arg("fmax"), py::arg("colsum") = py::none());
+        py::arg("csf"), py::arg("fmt"), py::arg("fmax"), py::arg("colsum") = py::none(), py::arg("xq") = py::none());
   m.def("gemm_fp8_gather_b", &gemm_fp8_gather_b, py::arg("A"), py::arg("a_mn"), py::arg("a_fmt"), py::arg("B"),
         py::arg("b_mn"), py::arg("b_fmt"), py::arg("b_peers"), py::arg("shard_rows"), py::arg("D"),
         py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("act") = py::none(),
@@ -272,6 +272,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("drop_scale") = 1.0);
   m.def("attn_bwd", &attn_bwd, py::arg("dout"), py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("H"), py::arg("drop_rng") = py::none(), py::arg("drop_site") = 0,
-        py::arg("drop_thr16") = 0, py::arg("drop_scale") = 1.0);
+        py::arg("drop_thr16") = 0, py::arg("drop_scale") = 1.0, py::arg("dq_out") = py::none());
   m.def("attn_status", &attn_status, py::arg("reset") = true);
 }

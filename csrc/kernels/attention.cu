@@ -876,9 +876,12 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, in
 }
 
 // -> dqkv [B*S, 3*H*128] bf16 (dq | dk | dv)
+// dq_out (optional fp32 [B*S, H*128]): receives the fp32 dQ accumulator, and the q third
+// of the returned dqkv is left unwritten (for a consumer that reads dQ in fp32, e.g. the
+// MXFP8 row / column quantiser); without it dQ is cast into that third.
 at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
                     int64_t B, int64_t S, int64_t H, const c10::optional<at::Tensor>& drop_rng, int64_t drop_site,
-                    int64_t drop_thr16, double drop_scale) {
+                    int64_t drop_thr16, double drop_scale, const c10::optional<at::Tensor>& dq_out) {
   check_qkv(qkv, (int)B, (int)S, (int)H);
   TORCH_CHECK(dout.is_contiguous() && out.is_contiguous() && dout.sizes() == out.sizes() &&
                   dout.size(0) == B * S && dout.size(1) == H * kD && dout.scalar_type() == at::kBFloat16,
@@ -887,7 +890,11 @@ at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Ten
   ensure_context();
   const int64_t T = B * S, HD = H * kD;
   auto dvec = at::empty({B, H, S}, lse.options());
-  auto dq = at::empty({T, HD}, lse.options());  // zeroed by the dot kernel
+  if (dq_out.has_value())
+    TORCH_CHECK(dq_out->scalar_type() == at::kFloat && dq_out->is_contiguous() && dq_out->numel() == T * HD &&
+                    reinterpret_cast<uintptr_t>(dq_out->data_ptr()) % 16 == 0,
+                "attention backward: dq_out must be contiguous fp32 [B*S, H*128]");
+  auto dq = dq_out.has_value() ? *dq_out : at::empty({T, HD}, lse.options());  // zeroed by the dot kernel
   auto dqkv = at::empty({T, 3 * HD}, qkv.options());
   {
     const int64_t threads_total = T * H * 16;
@@ -922,7 +929,7 @@ at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Ten
         tq, td, tdq, lse.data_ptr<float>(), dvec.data_ptr<float>(), (bf16*)dqkv.data_ptr(),
         (int)(3 * HD), (int)B, (int)H, (int)S, 1.0f / sqrtf((float)kD), attn_status_ptr(), drop);
   MT_LAUNCH_CHECK();
-  {
+  if (!dq_out.has_value()) {
     const int64_t n8 = T * HD / 8;
     attn_dq_cast_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, cur_stream()>>>(
         dq.data_ptr<float>(), (bf16*)dqkv.data_ptr(), (int)(3 * HD), (int)T, (int)HD);

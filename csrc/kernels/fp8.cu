@@ -368,7 +368,10 @@ __global__ void __launch_bounds__(256, kRcCtasPerSm) mx_rc_tile_kernel(
     const bf16* __restrict__ x, int64_t ldx, int R, int C, int fmt, uint32_t fmax_bits,
     const float* __restrict__ mean, const float* __restrict__ rstd, const float* __restrict__ gamma,
     const float* __restrict__ beta, float* __restrict__ colsum, uint8_t* __restrict__ rc, uint8_t* __restrict__ rsf,
-    uint8_t* __restrict__ cc, uint8_t* __restrict__ csf) {
+    uint8_t* __restrict__ cc, uint8_t* __restrict__ csf, const float* __restrict__ xq, int64_t ldq, int qcols) {
+  // xq (optional): columns [0, qcols) of the tensor come from this fp32 matrix instead of x
+  // (rounded to bf16 on load; qcols a multiple of 128), e.g. the attention's dQ accumulator
+  // beside the dK / dV it wrote into x
   extern __shared__ __align__(16) uint8_t rc_smem[];
   uint8_t* sfr = rc_smem + kRcOffSfr;
   uint8_t* sfc = rc_smem + kRcOffSfc;
@@ -382,6 +385,7 @@ __global__ void __launch_bounds__(256, kRcCtasPerSm) mx_rc_tile_kernel(
   auto issue = [&](int tile, int buf) {
     bf16(*tl)[kRcTileStride] = reinterpret_cast<bf16(*)[kRcTileStride]>(rc_smem + buf * kRcTileBytes);
     const int r0 = (tile / ntc) * 128, c0 = (tile % ntc) * 128;
+    if (xq && c0 < qcols) return;  // an fp32 tile: converted when it is processed
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
@@ -404,6 +408,21 @@ __global__ void __launch_bounds__(256, kRcCtasPerSm) mx_rc_tile_kernel(
     bf16(*tl)[kRcTileStride] = reinterpret_cast<bf16(*)[kRcTileStride]>(rc_smem + buf * kRcTileBytes);
     const int rt = tile / ntc, ct = tile % ntc;
     const int r0 = rt * 128, c0 = ct * 128;
+    if (xq && c0 < qcols) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
+        const int r = r0 + rr;
+        float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (r < R) {
+          const float4 a = *reinterpret_cast<const float4*>(xq + (int64_t)r * ldq + c0 + cv);
+          const float4 b = *reinterpret_cast<const float4*>(xq + (int64_t)r * ldq + c0 + cv + 4);
+          f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+        }
+        *reinterpret_cast<bf16x8*>(&tl[rr][cv]) = pack8(f);
+      }
+      __syncthreads();
+    }
     if (LN) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -720,7 +739,8 @@ void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t f
 // Launches mx_rc_tile_kernel over [R, C] (see there); ln_* non-null: LayerNorm on load.
 void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, double fmax, const float* ln_mean,
                  const float* ln_rstd, const float* ln_gamma, const float* ln_beta, float* colsum, uint8_t* rc,
-                 uint8_t* rsf, uint8_t* cc, uint8_t* csf, cudaStream_t st) {
+                 uint8_t* rsf, uint8_t* cc, uint8_t* csf, cudaStream_t st, const float* xq, int64_t ldq,
+                 int64_t qcols) {
   const float fm = (float)fmax;
   uint32_t fbits;
   std::memcpy(&fbits, &fm, 4);
@@ -734,17 +754,18 @@ void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, 
   }
   if (ln_mean)
     mx_rc_tile_kernel<true><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, ln_mean, ln_rstd,
-                                                   ln_gamma, ln_beta, colsum, rc, rsf, cc, csf);
+                                                   ln_gamma, ln_beta, colsum, rc, rsf, cc, csf, nullptr, 0, 0);
   else
     mx_rc_tile_kernel<false><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, nullptr, nullptr,
-                                                    nullptr, nullptr, colsum, rc, rsf, cc, csf);
+                                                    nullptr, nullptr, colsum, rc, rsf, cc, csf, xq, ldq, (int)qcols);
   MT_LAUNCH_CHECK();
 }
 
 // colsum (optional fp32 [C]): += the column sums of x (the bias gradient of the layer
-// whose output gradient x is), in the same pass.
+// whose output gradient x is), in the same pass.  xq (optional fp32 [R, Q], Q a multiple
+// of 128): columns [0, Q) of the tensor are taken from xq (rounded to bf16) instead of x.
 void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, int64_t fmt,
-                    double fmax, const c10::optional<at::Tensor>& colsum) {
+                    double fmax, const c10::optional<at::Tensor>& colsum, const c10::optional<at::Tensor>& xq) {
   MT_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "mx_quantize_rc: 2-D bf16 input");
   const int64_t R = x.size(0), C = x.size(1);
   MT_CHECK(R % 32 == 0 && C % 32 == 0, "mx_quantize_rc: R and C must be multiples of 32");
@@ -763,11 +784,23 @@ void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tens
   if (colsum.has_value())
     MT_CHECK(colsum->scalar_type() == at::kFloat && colsum->is_contiguous() && colsum->numel() == C,
              "mx_quantize_rc: colsum must be fp32 [C]");
+  const float* xqp = nullptr;
+  int64_t ldq = 0, qcols = 0;
+  if (xq.has_value()) {
+    MT_CHECK(xq->scalar_type() == at::kFloat && xq->dim() == 2 && xq->size(0) == R && xq->stride(1) == 1 &&
+                 xq->size(1) % 128 == 0 && xq->size(1) <= C && xq->stride(0) % 4 == 0 &&
+                 reinterpret_cast<uintptr_t>(xq->data_ptr()) % 16 == 0,
+             "mx_quantize_rc: xq must be fp32 [R, Q] with Q a multiple of 128, 16-byte aligned rows");
+    xqp = xq->data_ptr<float>();
+    ldq = xq->stride(0);
+    qcols = xq->size(1);
+  }
   if (R == 0 || C == 0) return;
   mx_rc_tiles(reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), R, C, fmt, fmax, nullptr, nullptr, nullptr,
               nullptr, colsum.has_value() ? colsum->data_ptr<float>() : nullptr,
               reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),
-              reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()), cur_stream());
+              reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()), cur_stream(), xqp,
+              ldq, qcols);
 }
 
 void fp8_quantize_blocks(const at::Tensor& x, at::Tensor out, at::Tensor scales, int64_t block_size,

@@ -563,7 +563,8 @@ __global__ void __launch_bounds__(256) ln_row_stats_kernel(const bf16* __restric
 // rsf, column codes cc [d, R] + csf (scale atoms as mx_quantize_rc), mean / rstd [R].
 void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, double fmax, const float* ln_mean,
                  const float* ln_rstd, const float* ln_gamma, const float* ln_beta, float* colsum, uint8_t* rc,
-                 uint8_t* rsf, uint8_t* cc, uint8_t* csf, cudaStream_t st);
+                 uint8_t* rsf, uint8_t* cc, uint8_t* csf, cudaStream_t st, const float* xq, int64_t ldq,
+                 int64_t qcols);
 
 void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at::Tensor& beta, double eps,
                          at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, at::Tensor mean,
@@ -598,7 +599,8 @@ void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at:
   mx_rc_tiles(reinterpret_cast<const bf16*>(x.data_ptr()), d, R, d, fmt, fmax, mean.data_ptr<float>(),
               rstd.data_ptr<float>(), gamma.data_ptr<float>(), beta.data_ptr<float>(), nullptr,
               reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),
-              reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()), st);
+              reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()), st, nullptr, 0,
+              0);
 }
 
 std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gamma,

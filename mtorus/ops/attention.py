@@ -13,7 +13,7 @@ kernels (``csrc/kernels/philox.cuh``): element (q, k) of head (b, h) is element
 """
 from __future__ import annotations
 
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 
@@ -39,12 +39,14 @@ def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, drop=None) -> Tuple
 
 
 def attention_bwd(dout: torch.Tensor, qkv: torch.Tensor, out: torch.Tensor, lse: torch.Tensor,
-                  B: int, S: int, H: int, drop=None) -> torch.Tensor:
-    """-> dqkv [B*S, 3*H*128] bf16 (dq | dk | dv)."""
+                  B: int, S: int, H: int, drop=None, dq_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """-> dqkv [B*S, 3*H*128] bf16 (dq | dk | dv).  With dq_out (fp32 [B*S, H*128]) dQ is
+    left there in fp32 and the dq third of dqkv is not written."""
     if drop is None:
-        return _cuda().attn_bwd(dout.contiguous(), qkv, out, lse, B, S, H)
+        return _cuda().attn_bwd(dout.contiguous(), qkv, out, lse, B, S, H, dq_out=dq_out)
     rng, site, thr, scale = drop
-    return _cuda().attn_bwd(dout.contiguous(), qkv, out, lse, B, S, H, rng, int(site), int(thr), float(scale))
+    return _cuda().attn_bwd(dout.contiguous(), qkv, out, lse, B, S, H, rng, int(site), int(thr), float(scale),
+                            dq_out=dq_out)
 
 
 class CausalAttentionFn(torch.autograd.Function):

@@ -199,16 +199,25 @@ def gemm_mxfp8_mx_out(a: MxTensor, b: MxTensor, fmt: int, out: Optional[torch.Te
 
 
 def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = None,
-                   colsum: Optional[torch.Tensor] = None, accumulate: bool = True):
+                   colsum: Optional[torch.Tensor] = None, accumulate: bool = True,
+                   xq: Optional[torch.Tensor] = None):
     """Row-wise MXFP8 of x [R, C] (32-blocks along C) and of its transpose [C, R]
     (32-blocks along R), in one pass on the GPU: the operands that contract over C
     and over R.  R and C multiples of 32.  The reference on the CPU.
 
     colsum (fp32 [C], optional): receives the column sums of x in the same pass (the
     bias gradient when x is a layer's output gradient), added to its contents when
-    ``accumulate``, else overwriting them."""
+    ``accumulate``, else overwriting them.  xq (fp32 [R, Q], Q a multiple of 128, optional):
+    the first Q columns are taken from xq rounded to bf16 instead of from x."""
     if x.dim() != 2 or x.shape[0] % BLOCK or x.shape[1] % BLOCK:
         raise ValueError("mx_quantize_rc: 2-D input with both sizes multiples of 32 expected")
+    if xq is not None:
+        if xq.shape[0] != x.shape[0] or xq.shape[1] % 128 or xq.shape[1] > x.shape[1]:
+            raise ValueError("mx_quantize_rc: xq must be [R, Q] with Q a multiple of 128, Q <= C")
+        if not x.is_cuda:
+            x = x.clone()
+            x[:, :xq.shape[1]] = xq.to(x.dtype)
+            xq = None
     if not x.is_cuda:
         if colsum is not None:
             cs = x.float().sum(0)
@@ -228,7 +237,7 @@ def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = Non
     csf = torch.empty(sf_numel(C, R), dtype=torch.uint8, device=x.device)
     if colsum is not None and not accumulate:
         colsum.zero_()
-    _cuda().mx_quantize_rc(x, rc, rsf, cc, csf, int(fmt), fmax, colsum)
+    _cuda().mx_quantize_rc(x, rc, rsf, cc, csf, int(fmt), fmax, colsum, xq)
     return MxTensor(rc, rsf, int(fmt)), MxTensor(cc, csf, int(fmt))
 
 

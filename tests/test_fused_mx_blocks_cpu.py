@@ -57,11 +57,16 @@ def _attn_fwd(qkv, b, s, h, drop=None):
     return A.reference_attention(qkv, b, s, h, DH).to(torch.bfloat16), torch.zeros(b, h, s)
 
 
-def _attn_bwd(do, qkv, o, lse, b, s, h, drop=None):
+def _attn_bwd(do, qkv, o, lse, b, s, h, drop=None, dq_out=None):
     with torch.enable_grad():  # called from inside a custom Function's backward
         q = qkv.float().detach().requires_grad_(True)
         A.reference_attention(q, b, s, h, DH).backward(do.float())
-    return q.grad.to(torch.bfloat16)
+    g = q.grad
+    if dq_out is not None:  # the kernel's contract: dQ in fp32 there, the dq third unwritten
+        dq_out.copy_(g[:, :dq_out.shape[1]])
+        g = g.clone()
+        g[:, :dq_out.shape[1]] = float("nan")
+    return g.to(torch.bfloat16)
 
 
 def _colsum(x, out, accumulate, scale=None):

@@ -243,6 +243,26 @@ def test_gemm_epilogue_mx_output_matches_unfused_quantiser(M, N):
 
 
 @pytest.mark.gpu
+def test_row_col_quantiser_reads_leading_columns_from_fp32():
+    """xq: the first 128 columns come from an fp32 matrix (rounded to bf16 on load), the
+    rest from the bf16 tensor -- the attention backward's fp32 dQ beside its bf16 dK / dV."""
+    R, C = 256, 384
+    x = _blocky(R, C, seed=3).to(torch.bfloat16)
+    xq = _blocky(R, 128, seed=4).float() * 1.37
+    x_nan = x.clone()
+    x_nan[:, :128] = float("nan")  # must not be read
+    cs = torch.zeros(C, device="cuda")
+    r, c = mx_quantize_rc(x_nan.cuda(), E5M2, colsum=cs, xq=xq.cuda())
+    full = x.clone()
+    full[:, :128] = xq.to(torch.bfloat16)
+    rr, cr = mx_quantize_ref(full.float(), E5M2), mx_quantize_ref(full.float().t().contiguous(), E5M2)
+    assert torch.equal(r.codes.cpu(), rr.codes) and torch.equal(r.sf.cpu(), rr.sf)
+    assert torch.equal(c.codes.cpu(), cr.codes) and torch.equal(c.sf.cpu(), cr.sf)
+    assert torch.allclose(cs.cpu().double(), full.double().sum(0), rtol=1e-5,
+                          atol=1e-5 * float(full.double().abs().sum(0).max()))
+
+
+@pytest.mark.gpu
 def test_mx_linear_cuda_matches_cpu_oracle():
     torch.manual_seed(1)
     T, I, O = 512, 256, 768
