@@ -88,7 +88,9 @@ void gemm_fp8_gather_b(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::
 // attention.cu
 std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H,
                                  const c10::optional<at::Tensor>& drop_rng, int64_t drop_site, int64_t drop_thr16,
-                                 double drop_scale);
+                                 double drop_scale, const c10::optional<at::Tensor>& mx_rc,
+                                 const c10::optional<at::Tensor>& mx_rsf, const c10::optional<at::Tensor>& mx_cc,
+                                 const c10::optional<at::Tensor>& mx_csf, int64_t mx_fmt, double mx_fmax);
 at::Tensor attn_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& lse,
                     int64_t B, int64_t S, int64_t H, const c10::optional<at::Tensor>& drop_rng, int64_t drop_site,
                     int64_t drop_thr16, double drop_scale, const c10::optional<at::Tensor>& dq_out);
@@ -269,7 +271,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("cap"), py::arg("slot"), py::arg("parity"), py::arg("epoch"), py::arg("fmt"), py::arg("ep_ptr") = 0);
   m.def("attn_fwd", &attn_fwd, py::arg("qkv"), py::arg("B"), py::arg("S"), py::arg("H"),
         py::arg("drop_rng") = py::none(), py::arg("drop_site") = 0, py::arg("drop_thr16") = 0,
-        py::arg("drop_scale") = 1.0);
+        py::arg("drop_scale") = 1.0, py::arg("mx_rc") = py::none(), py::arg("mx_rsf") = py::none(),
+        py::arg("mx_cc") = py::none(), py::arg("mx_csf") = py::none(), py::arg("mx_fmt") = 0,
+        py::arg("mx_fmax") = 448.0);
   m.def("attn_bwd", &attn_bwd, py::arg("dout"), py::arg("qkv"), py::arg("out"), py::arg("lse"), py::arg("B"),
         py::arg("S"), py::arg("H"), py::arg("drop_rng") = py::none(), py::arg("drop_site") = 0,
         py::arg("drop_thr16") = 0, py::arg("drop_scale") = 1.0, py::arg("dq_out") = py::none());

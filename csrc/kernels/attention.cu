@@ -38,10 +38,13 @@
 // Every wait is bounded (2 s); on a timeout the kernel records a status code,
 // lets its in-flight copies and MMAs land, frees TMEM and returns.
 #include "common.cuh"
+#include "mx.cuh"
 #include "philox.cuh"
 #include "sm100.cuh"
 
 #include <ATen/ops/zeros.h>
+
+#include <cstring>
 
 namespace mtorus {
 
@@ -107,6 +110,18 @@ __device__ __forceinline__ void bounded_drain(uint64_t* bar, uint32_t parity) {
 constexpr int kRing = 3;
 constexpr int kFwdThreads = 320;  // producer, MMA, 2 x 4 softmax warps
 
+// MXFP8 copy of the attention output (the out-projection's operand both ways): row codes
+// [T, H*128] and column codes [H*128, T] with their scale atoms (the mx_quantize layout),
+// written by the forward's epilogue beside the bf16 output.  rc == nullptr: none.
+struct AttnMxOut {
+  uint8_t* rc;
+  uint8_t* rsf;
+  uint8_t* cc;
+  uint8_t* csf;
+  uint32_t fmax_bits;
+  int fmt;
+};
+
 struct FwdCtl {
   uint64_t q_full, ring_full[kRing], ring_empty[kRing], s_full[2], p_full[2], o_done[2], drain;
   uint32_t tmem_base;
@@ -153,7 +168,8 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
 template <bool DROP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tma_qkv, bf16* __restrict__ out, int ld_out,
-                    float* __restrict__ lse, int B, int H, int S, float scale, int* status, DropoutArgs drop) {
+                    float* __restrict__ lse, int B, int H, int S, float scale, int* status, DropoutArgs drop,
+                    AttnMxOut mxo) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -410,11 +426,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float inv = 1.f / l;
       const int row = b * S + qt * kTile + r;
       bf16* dst = out + (size_t)row * ld_out + h * kD;
+      // MX output: this warp's 32 rows x 32 columns per chunk go through a 2 KB staging
+      // area in the warpgroup's P tile (free: every PV MMA of the tile has completed)
+      uint8_t* stg = myP + quarter * 2048;
+      const int T = B * S, row0w = b * S + qt * kTile + quarter * 32;
 #pragma unroll 1
       for (int c = 0; c < kD / 32; ++c) {
         uint32_t v[32];
         tmem_ld32(tO + c * 32, v);
         tmem_wait_ld();
+        uint4 wv[4];
 #pragma unroll
         for (int e = 0; e < 32; e += 8) {
           uint4 w;
@@ -423,6 +444,39 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           w.z = pack_bf16x2(__uint_as_float(v[e + 4]) * inv, __uint_as_float(v[e + 5]) * inv);
           w.w = pack_bf16x2(__uint_as_float(v[e + 6]) * inv, __uint_as_float(v[e + 7]) * inv);
           *reinterpret_cast<uint4*>(dst + c * 32 + e) = w;
+          wv[e / 8] = w;
+        }
+        if (mxo.rc) {
+          const int ef = (int)((mxo.fmax_bits >> 23) & 0xFF);
+          const uint32_t mf = mxo.fmax_bits & 0x7FFFFF;
+          const int col0 = h * kD + c * 32;  // first column of the chunk in [T, H*128]
+          float f[32];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) unpack8(*reinterpret_cast<const bf16x8*>(&wv[q]), f + 8 * q);
+          uint32_t cw[8];
+          uint8_t sb;
+          mx_block(f, ef, mf, mxo.fmt, cw, sb);  // this row's block (the bf16 values just stored)
+          uint4* rdst = reinterpret_cast<uint4*>(mxo.rc + (size_t)row * ld_out + col0);
+          rdst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+          rdst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+          mxo.rsf[((int64_t)(row >> 7) * H + h) * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 + c] = sb;
+          // column block: stage the 32 x 32 bf16 chunk, then each lane quantises column col0 + lane
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(stg + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = wv[q];
+          __syncwarp();
+#pragma unroll
+          for (int rr = 0; rr < 32; ++rr)
+            f[rr] = __bfloat162float(*reinterpret_cast<const bf16*>(
+                stg + rr * 64 + ((((lane >> 3) ^ ((rr >> 1) & 3))) << 4) + (lane & 7) * 2));
+          __syncwarp();  // the staging area is rewritten by the next chunk
+          mx_block(f, ef, mf, mxo.fmt, cw, sb);
+          const int col = col0 + lane;
+          uint4* cdst = reinterpret_cast<uint4*>(mxo.cc + (size_t)col * T + row0w);
+          cdst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+          cdst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+          mxo.csf[((int64_t)(col >> 7) * (T >> 7) + (row0w >> 7)) * 512 + (col & 31) * 16 + ((col & 127) >> 5) * 4 +
+                  ((row0w & 127) >> 5)] = sb;
         }
       }
       // natural-log log-sum-exp of the scaled scores
@@ -844,11 +898,36 @@ void check_qkv(const at::Tensor& qkv, int B, int S, int H) {
 // qkv [B*S, 3*H*128] bf16 -> (out [B*S, H*128] bf16, lse [B, H, S] fp32)
 DropoutArgs make_dropout_args(const c10::optional<at::Tensor>& rng, int64_t site, int64_t thr16, double scale);
 
+// mx_* (optional, all four or none): also write the output's MXFP8 row codes [B*S, H*128] /
+// mx_rsf and column codes [H*128, B*S] / mx_csf in format mx_fmt (largest value mx_fmax).
 std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, int64_t H,
                                  const c10::optional<at::Tensor>& drop_rng, int64_t drop_site, int64_t drop_thr16,
-                                 double drop_scale) {
+                                 double drop_scale, const c10::optional<at::Tensor>& mx_rc,
+                                 const c10::optional<at::Tensor>& mx_rsf, const c10::optional<at::Tensor>& mx_cc,
+                                 const c10::optional<at::Tensor>& mx_csf, int64_t mx_fmt, double mx_fmax) {
   check_qkv(qkv, (int)B, (int)S, (int)H);
   ensure_context();
+  AttnMxOut mxo{};
+  if (mx_rc.has_value()) {
+    const int64_t n = B * S * H * kD, atoms = (B * S / kTile) * H * 512;
+    auto chk = [](const c10::optional<at::Tensor>& t, int64_t numel, const char* what) {
+      TORCH_CHECK(t.has_value() && t->is_cuda() && t->element_size() == 1 && t->is_contiguous() &&
+                      t->numel() == numel && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+                  what);
+    };
+    chk(mx_rc, n, "attention MX output: rc must be 16-byte aligned contiguous uint8 [B*S, H*128]");
+    chk(mx_cc, n, "attention MX output: cc must be 16-byte aligned contiguous uint8 [H*128, B*S]");
+    chk(mx_rsf, atoms, "attention MX output: rsf size");
+    chk(mx_csf, atoms, "attention MX output: csf size");
+    TORCH_CHECK(mx_fmt == 0 || mx_fmt == 1, "attention MX output: format 0 (E4M3) / 1 (E5M2)");
+    const float fm = (float)mx_fmax;
+    std::memcpy(&mxo.fmax_bits, &fm, 4);
+    mxo.rc = reinterpret_cast<uint8_t*>(mx_rc->data_ptr());
+    mxo.rsf = reinterpret_cast<uint8_t*>(mx_rsf->data_ptr());
+    mxo.cc = reinterpret_cast<uint8_t*>(mx_cc->data_ptr());
+    mxo.csf = reinterpret_cast<uint8_t*>(mx_csf->data_ptr());
+    mxo.fmt = (int)mx_fmt;
+  }
   auto out = at::empty({B * S, H * kD}, qkv.options());
   auto lse = at::empty({B, H, S}, qkv.options().dtype(at::kFloat));
   const CUtensorMap tm = make_tma_2d(qkv.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3 * H * kD, B * S,
@@ -866,11 +945,11 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& qkv, int64_t B, int64_t S, in
   if (drop.rng)
     attn_fwd_kernel<true><<<grid, kFwdThreads, kFwdSmem, cur_stream()>>>(
         tm, (bf16*)out.data_ptr(), (int)(H * kD), lse.data_ptr<float>(), (int)B, (int)H, (int)S,
-        1.0f / sqrtf((float)kD), attn_status_ptr(), drop);
+        1.0f / sqrtf((float)kD), attn_status_ptr(), drop, mxo);
   else
     attn_fwd_kernel<false><<<grid, kFwdThreads, kFwdSmem, cur_stream()>>>(
         tm, (bf16*)out.data_ptr(), (int)(H * kD), lse.data_ptr<float>(), (int)B, (int)H, (int)S,
-        1.0f / sqrtf((float)kD), attn_status_ptr(), drop);
+        1.0f / sqrtf((float)kD), attn_status_ptr(), drop, mxo);
   MT_LAUNCH_CHECK();
   return {out, lse};
 }

@@ -29,13 +29,31 @@ def check_shape(S: int, dh: int) -> None:
                          f"(got head dim {dh}, seq len {S})")
 
 
-def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, drop=None) -> Tuple[torch.Tensor, torch.Tensor]:
+def attention_fwd(qkv: torch.Tensor, B: int, S: int, H: int, drop=None, mx_fmt: Optional[int] = None):
     """qkv [B*S, 3*H*128] bf16 -> (out [B*S, H*128] bf16, lse [B, H, S] fp32).
-    drop: optional (rng, site, thr16, scale) of the attention-probability dropout."""
+    drop: optional (rng, site, thr16, scale) of the attention-probability dropout.
+    mx_fmt (optional MXFP8 format): the epilogue also writes the output's MXFP8 row and
+    column codes (what ``mx_quantize_rc`` makes of ``out``) and the call returns
+    (out, lse, rows, cols)."""
+    kw = {}
+    rows = cols = None
+    if mx_fmt is not None:
+        from .mxfp8 import MX_FMT_MAX, MxTensor, sf_numel
+
+        T, HD = B * S, H * 128
+        dev = qkv.device
+        rows = MxTensor(torch.empty((T, HD), dtype=torch.uint8, device=dev),
+                        torch.empty(sf_numel(T, HD), dtype=torch.uint8, device=dev), int(mx_fmt))
+        cols = MxTensor(torch.empty((HD, T), dtype=torch.uint8, device=dev),
+                        torch.empty(sf_numel(HD, T), dtype=torch.uint8, device=dev), int(mx_fmt))
+        kw = dict(mx_rc=rows.codes, mx_rsf=rows.sf, mx_cc=cols.codes, mx_csf=cols.sf, mx_fmt=int(mx_fmt),
+                  mx_fmax=float(MX_FMT_MAX[mx_fmt]))
     if drop is None:
-        return tuple(_cuda().attn_fwd(qkv, B, S, H))
-    rng, site, thr, scale = drop
-    return tuple(_cuda().attn_fwd(qkv, B, S, H, rng, int(site), int(thr), float(scale)))
+        out, lse = _cuda().attn_fwd(qkv, B, S, H, **kw)
+    else:
+        rng, site, thr, scale = drop
+        out, lse = _cuda().attn_fwd(qkv, B, S, H, rng, int(site), int(thr), float(scale), **kw)
+    return (out, lse) if mx_fmt is None else (out, lse, rows, cols)
 
 
 def attention_bwd(dout: torch.Tensor, qkv: torch.Tensor, out: torch.Tensor, lse: torch.Tensor,

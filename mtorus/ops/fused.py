@@ -182,8 +182,8 @@ class AttnBlockFn(Function):
             gamma, beta, eps = ln
             hr, hc, mean, rstd = MX.mx_layernorm_rc(x2d, gamma.data, beta.data, eps, MX.E4M3)
             qkv = MX.gemm_mxfp8(hr, wq.mx[0], bias=bq.data)
-            o, lse = attention_fwd(qkv, B, S, H, d_probs)
-            orow, ocol = MX.mx_quantize_rc(o, MX.E4M3)
+            # the attention epilogue writes the output's MX codes both ways beside the bf16 copy
+            o, lse, orow, ocol = _attn_fwd_mx(attention_fwd, MX, qkv, B, S, H, d_probs)
             with K.gemm_dropout(d_out, 1):
                 out = MX.gemm_mxfp8(orow, wo.mx[0], bias=bo.data, residual=x2d)
             ctx.save_for_backward(x2d, mean, rstd, hc.codes, hc.sf, ocol.codes, ocol.sf, qkv, o, lse)
@@ -279,6 +279,16 @@ class AttnBlockFn(Function):
         dh = MX.gemm_mxfp8(qrow, wq.mx[1])
         _grads_done(wq, bq)
         return _ln_bwd(dh, x2d, mean, rstd, ln, dout), None, None, None, None, None, None
+
+
+def _attn_fwd_mx(attention_fwd, MX, qkv, B, S, H, drop):
+    """Attention forward plus its output's MXFP8 row / column codes (E4M3): from the kernel's
+    epilogue on the GPU, from the separate quantiser where the kernel is replaced."""
+    if qkv.is_cuda:
+        return attention_fwd(qkv, B, S, H, drop, mx_fmt=MX.E4M3)
+    o, lse = attention_fwd(qkv, B, S, H, drop)
+    orow, ocol = MX.mx_quantize_rc(o, MX.E4M3)
+    return o, lse, orow, ocol
 
 
 def _mx_gemm_quant(MX, a, b, fmt, out=None, *, bias=None, aux=None, gelu=False, colsum=None, accumulate=True,

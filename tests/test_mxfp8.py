@@ -243,6 +243,23 @@ def test_gemm_epilogue_mx_output_matches_unfused_quantiser(M, N):
 
 
 @pytest.mark.gpu
+def test_attention_epilogue_mx_output_matches_quantiser():
+    """The attention forward's MX-output epilogue writes exactly what the row / column
+    quantiser makes of the bf16 output it stores (codes and both scale atoms)."""
+    from mtorus.ops.attention import attention_fwd
+
+    B, S, H = 2, 256, 2
+    g = torch.Generator().manual_seed(5)
+    qkv = (torch.randn(B * S, 3 * H * 128, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    out, lse, rows, cols = attention_fwd(qkv, B, S, H, mx_fmt=E4M3)
+    plain, _ = attention_fwd(qkv, B, S, H)
+    assert torch.equal(out, plain)
+    r_ref, c_ref = mx_quantize_rc(out, E4M3)
+    for got, want in ((rows, r_ref), (cols, c_ref)):
+        assert torch.equal(got.codes, want.codes) and torch.equal(got.sf, want.sf)
+
+
+@pytest.mark.gpu
 def test_row_col_quantiser_reads_leading_columns_from_fp32():
     """xq: the first 128 columns come from an fp32 matrix (rounded to bf16 on load), the
     rest from the bf16 tensor -- the attention backward's fp32 dQ beside its bf16 dK / dV."""
