@@ -18,7 +18,8 @@ at::Tensor layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Te
 // xent.cu
 at::Tensor xent_fused(at::Tensor logits, const at::Tensor& targets,
                       const c10::optional<at::Tensor>& grad_scale, double scale_mul,
-                      bool write_grad);
+                      bool write_grad, const c10::optional<at::Tensor>& out8,
+                      const c10::optional<at::Tensor>& out8_scale, const c10::optional<at::Tensor>& out8_amax);
 // optim.cu
 void optim_grad_sumsq(const at::Tensor& g, at::Tensor st);
 void optim_finalize(at::Tensor st, bool dynamic, int64_t growth_interval, double max_norm,
@@ -39,6 +40,8 @@ void embed_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor dwte, at:
                int64_t S, bool accumulate);
 at::Tensor bias_gelu_fwd(at::Tensor pre, const c10::optional<at::Tensor>& bias);
 void gelu_bwd_(at::Tensor dact, const at::Tensor& pre);
+void colsum_e5m2_(const at::Tensor& codes, at::Tensor out, bool accumulate, const c10::optional<at::Tensor>& scale,
+                  const c10::optional<at::Tensor>& scale2);
 void colsum_(const at::Tensor& x, at::Tensor out, bool accumulate,
              const c10::optional<at::Tensor>& scale);
 // gemm.cu
@@ -167,7 +170,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dres") = py::none());
   m.def("xent_fused", &xent_fused, py::arg("logits"), py::arg("targets"),
         py::arg("grad_scale") = py::none(), py::arg("scale_mul") = 1.0,
-        py::arg("write_grad") = true);
+        py::arg("write_grad") = true, py::arg("out8") = py::none(), py::arg("out8_scale") = py::none(),
+        py::arg("out8_amax") = py::none());
   m.def("optim_grad_sumsq", &optim_grad_sumsq);
   m.def("optim_finalize", &optim_finalize);
   m.def("adam_step", &adam_step);
@@ -180,6 +184,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &embed_bwd);
   m.def("bias_gelu_fwd", &bias_gelu_fwd);
   m.def("gelu_bwd_", &gelu_bwd_);
+  m.def("colsum_e5m2_", &colsum_e5m2_, py::arg("codes"), py::arg("out"), py::arg("accumulate"),
+        py::arg("scale") = py::none(), py::arg("scale2") = py::none());
   m.def("colsum_", &colsum_, py::arg("x"), py::arg("out"), py::arg("accumulate"),
         py::arg("scale") = py::none());
   m.def("gemm_bf16", &gemm_bf16, py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"),

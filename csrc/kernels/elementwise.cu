@@ -9,6 +9,8 @@
 // straight into the fp32 master-gradient buffer with vectorised fp32 atomics
 // (red.global.add.v4.f32) and sums position rows over the batch without atomics.
 #include "common.cuh"
+
+#include <cuda_fp16.h>
 #include "gelu.cuh"
 #include "philox.cuh"
 
@@ -181,6 +183,41 @@ __global__ void __launch_bounds__(256) colsum_vec_kernel(const bf16* __restrict_
   }
 }
 
+// Column sums of E5M2 codes [rows, F] (F % 8 == 0): an E5M2 code is the high byte of the
+// fp16 with the same value, so decoding is a shift.  out (+)= sum * (*scale) * (*scale2).
+__global__ void __launch_bounds__(256) colsum_e5m2_kernel(const uint8_t* __restrict__ x, float* __restrict__ out,
+                                                          const float* scale, const float* scale2, int rows, int F,
+                                                          int rows_per_block) {
+  __shared__ float red[8][257];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 256 + tx * 8;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (c0 < F) {
+    for (int r = r0 + ty; r < r1; r += 8) {
+      const uint2 w = *reinterpret_cast<const uint2*>(x + (size_t)r * F + c0);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t code = ((k < 4 ? w.x : w.y) >> (8 * (k & 3))) & 0xFFu;
+        acc[k] += __half2float(__ushort_as_half((unsigned short)(code << 8)));
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) red[ty][tx * 8 + k] = acc[k];
+  __syncthreads();
+  const int col = threadIdx.x;
+  if (blockIdx.x * 256 + col < F) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][col];
+    if (scale) t *= *scale;
+    if (scale2) t *= *scale2;
+    atomicAdd(out + blockIdx.x * 256 + col, t);
+  }
+}
+
 // Generic fallback (F % 8 != 0).
 __global__ void colsum_kernel(const bf16* __restrict__ x, float* __restrict__ out, const float* scale,
                               int rows, int F, int rows_per_block) {
@@ -293,6 +330,28 @@ void gelu_bwd_(at::Tensor dact, const at::Tensor& pre) {
   if (n8 == 0) return;
   gelu_bwd_kernel<<<ew_grid(n8), 256, 0, cur_stream()>>>(
       reinterpret_cast<bf16*>(dact.data_ptr()), reinterpret_cast<const bf16*>(pre.data_ptr()), n8);
+  MT_LAUNCH_CHECK();
+}
+
+void colsum_e5m2_(const at::Tensor& codes, at::Tensor out, bool accumulate, const c10::optional<at::Tensor>& scale,
+                  const c10::optional<at::Tensor>& scale2) {
+  MT_CHECK_CONTIG(codes);
+  MT_CHECK(codes.element_size() == 1, "colsum_e5m2: uint8 codes");
+  MT_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous(), "colsum_e5m2: fp32 contiguous out");
+  const int F = codes.size(-1);
+  const int rows = codes.numel() / F;
+  MT_CHECK(F % 8 == 0 && reinterpret_cast<uintptr_t>(codes.data_ptr()) % 8 == 0 && out.numel() == F,
+           "colsum_e5m2: F % 8 == 0, 8-byte aligned codes, out [F]");
+  if (!accumulate) out.zero_();
+  if (rows == 0) return;
+  const int col_blocks = (F + 255) / 256;
+  int row_blocks = std::max(1, std::min((rows + 63) / 64, (num_sms() * 8 + col_blocks - 1) / col_blocks));
+  const int rpb = (rows + row_blocks - 1) / row_blocks;
+  row_blocks = (rows + rpb - 1) / rpb;
+  colsum_e5m2_kernel<<<dim3(col_blocks, row_blocks), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const uint8_t*>(codes.data_ptr()), out.data_ptr<float>(),
+      scale.has_value() ? scale->data_ptr<float>() : nullptr, scale2.has_value() ? scale2->data_ptr<float>() : nullptr,
+      rows, F, rpb);
   MT_LAUNCH_CHECK();
 }
 

@@ -14,6 +14,7 @@
 // and fp32 logits are never materialised.
 #include "common.cuh"
 #include "ex2poly.cuh"
+#include "amax_publish.cuh"
 
 namespace mtorus {
 
@@ -40,7 +41,12 @@ __global__ void __launch_bounds__(512) xent_fwd_bwd(bf16* __restrict__ logits,
                                                     const int64_t* __restrict__ targets,
                                                     float* __restrict__ loss_rows,
                                                     const float* __restrict__ grad_scale,
-                                                    float scale_mul, int V, int write_grad) {
+                                                    float scale_mul, int V, int write_grad,
+                                                    uint8_t* __restrict__ out8, const float* __restrict__ out8_scale,
+                                                    float* __restrict__ out8_amax) {
+  // out8 (VEC only): dlogits leave as E5M2 codes of the bf16-rounded values times *out8_scale
+  // (the LM-head backward's operand) instead of overwriting the logits, and max|dlogit|
+  // folds into *out8_amax -- the separate quantise pass and the bf16 dlogits disappear
   __shared__ float red_m[32], red_s[32];
   const int row = blockIdx.x;
   bf16* lr = logits + (size_t)row * V;
@@ -103,6 +109,8 @@ __global__ void __launch_bounds__(512) xent_fwd_bwd(bf16* __restrict__ logits,
   if (VEC) {
     const int nv = V / 8;
     const float nm = -m * kLog2e, ps = gs * inv_s;
+    const float q = out8 ? *out8_scale : 0.f;
+    float am = 0.f;
     for (int j = threadIdx.x; j < nv; j += blockDim.x) {
       float f[8];
       unpack8(reinterpret_cast<const bf16x8*>(lr)[j], f);
@@ -113,7 +121,27 @@ __global__ void __launch_bounds__(512) xent_fwd_bwd(bf16* __restrict__ logits,
         if (j * 8 + i == tgt) g -= gs;
         f[i] = g;
       }
-      reinterpret_cast<bf16x8*>(lr)[j] = pack8(f);
+      if (out8) {
+        float r[8];
+        unpack8(pack8(f), r);  // the bf16 dlogits the separate quantiser would read
+        uint32_t w[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) am = fmaxf(am, fabsf(r[4 * k + i]));
+          const uint16_t lo = cvt2_e5m2(r[4 * k] * q, r[4 * k + 1] * q);
+          const uint16_t hi = cvt2_e5m2(r[4 * k + 2] * q, r[4 * k + 3] * q);
+          w[k] = (uint32_t)lo | ((uint32_t)hi << 16);
+        }
+        reinterpret_cast<uint2*>(out8 + (size_t)row * V)[j] = make_uint2(w[0], w[1]);
+      } else {
+        reinterpret_cast<bf16x8*>(lr)[j] = pack8(f);
+      }
+    }
+    if (out8) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      if ((threadIdx.x & 31) == 0) atomic_max_pos(out8_amax, am);
     }
   } else {
     for (int j = threadIdx.x; j < V; j += blockDim.x) {
@@ -125,9 +153,12 @@ __global__ void __launch_bounds__(512) xent_fwd_bwd(bf16* __restrict__ logits,
 }
 
 // logits [T, V] bf16 (overwritten with dlogits when write_grad); returns per-row loss fp32.
+// out8 (uint8 [T, V], with out8_scale / out8_amax fp32 [1]): the dlogits go there as E5M2
+// codes instead (the logits are left as they were), their max |value| into out8_amax.
 at::Tensor xent_fused(at::Tensor logits, const at::Tensor& targets,
                       const c10::optional<at::Tensor>& grad_scale, double scale_mul,
-                      bool write_grad) {
+                      bool write_grad, const c10::optional<at::Tensor>& out8,
+                      const c10::optional<at::Tensor>& out8_scale, const c10::optional<at::Tensor>& out8_amax) {
   MT_CHECK_CUDA(logits);
   MT_CHECK_CONTIG(logits);
   MT_CHECK(logits.scalar_type() == at::kBFloat16, "xent: logits must be bf16");
@@ -143,14 +174,29 @@ at::Tensor xent_fused(at::Tensor logits, const at::Tensor& targets,
   }
   auto* lp = reinterpret_cast<bf16*>(logits.data_ptr());
   const bool vec = (V % 8 == 0) && (reinterpret_cast<uintptr_t>(lp) % 16 == 0);
+  uint8_t* o8 = nullptr;
+  const float* o8s = nullptr;
+  float* o8a = nullptr;
+  if (out8.has_value()) {
+    MT_CHECK(vec && write_grad, "xent: E5M2 dlogits need V % 8 == 0, 16-byte aligned logits and write_grad");
+    MT_CHECK(out8->is_cuda() && out8->element_size() == 1 && out8->is_contiguous() && out8->numel() == logits.numel() &&
+                 reinterpret_cast<uintptr_t>(out8->data_ptr()) % 8 == 0,
+             "xent: out8 must be contiguous uint8 shaped like the logits");
+    MT_CHECK(out8_scale.has_value() && out8_amax.has_value() && out8_scale->scalar_type() == at::kFloat &&
+                 out8_amax->scalar_type() == at::kFloat,
+             "xent: out8 needs fp32 out8_scale and out8_amax");
+    o8 = reinterpret_cast<uint8_t*>(out8->data_ptr());
+    o8s = out8_scale->data_ptr<float>();
+    o8a = out8_amax->data_ptr<float>();
+  }
   auto st = cur_stream();
   if (vec)
     xent_fwd_bwd<true><<<T, 512, 0, st>>>(lp, targets.data_ptr<int64_t>(), loss.data_ptr<float>(),
-                                          gsp, (float)scale_mul, V, write_grad);
+                                          gsp, (float)scale_mul, V, write_grad, o8, o8s, o8a);
   else
     xent_fwd_bwd<false><<<T, 512, 0, st>>>(lp, targets.data_ptr<int64_t>(),
                                            loss.data_ptr<float>(), gsp, (float)scale_mul, V,
-                                           write_grad);
+                                           write_grad, nullptr, nullptr, nullptr);
   MT_LAUNCH_CHECK();
   return loss;
 }

@@ -473,9 +473,21 @@ class LMHeadLossFn(Function):
         w, b = params
         T = h.shape[0]
         ctx.fp8 = fp8
+        ctx.g8 = False
         if fp8 is not None:
             h8, ih = fp8.quantize(h, "lm_head.in", F8.E4M3)
             logits = F8.gemm_fp8(h8, F8.E4M3, w.w8, F8.E4M3, bias=b.data, alpha=ih, alpha2=w.w8_inv)
+            slot = fp8.epilogue_slot("lm_head.grad", F8.E5M2)
+            if slot is not None:
+                # the cross-entropy kernel writes dlogits straight as the backward GEMMs' E5M2
+                # operand (the delayed scale is known), so no bf16 dlogits and no quantise pass
+                g8 = torch.empty(logits.shape, dtype=torch.uint8, device=logits.device)
+                rows = K.xent_fused(logits, targets.reshape(-1), grad_scale, 1.0 / T, True, out8=g8,
+                                    out8_scale=slot[0], out8_amax=slot[1])
+                ctx.g8 = True
+                ctx.save_for_backward(h8, ih, g8, slot[2])
+                ctx.params = params
+                return rows.mean()
             saved = (h8, ih)
         else:
             logits = K.gemm(h, w.w16, bias=b.data)
@@ -491,8 +503,13 @@ class LMHeadLossFn(Function):
         acc = FusedGradState.accumulate
         g = gloss.reshape(1).float().contiguous()
         if ctx.fp8 is not None:
-            h8, ih, dlogits = ctx.saved_tensors
-            g8, igd = ctx.fp8.quantize(dlogits, "lm_head.grad", F8.E5M2)
+            if ctx.g8:
+                h8, ih, g8, igd = ctx.saved_tensors
+                K.colsum_e5m2_(g8, b.main_grad, acc, scale=igd, scale2=g)  # bias gradient from the codes
+            else:
+                h8, ih, dlogits = ctx.saved_tensors
+                g8, igd = ctx.fp8.quantize(dlogits, "lm_head.grad", F8.E5M2)
+                K.colsum_(dlogits, b.main_grad, acc, scale=g)
             a = igd * g  # the E5M2 inverse scale times the incoming loss gradient
             dh = F8.gemm_fp8(g8, F8.E5M2, w.w8, F8.E4M3, b_mn=True, alpha=a, alpha2=w.w8_inv)
             F8.gemm_fp8(g8, F8.E5M2, h8, F8.E4M3, out=w.main_grad, a_mn=True, b_mn=True, accumulate=acc,
@@ -501,6 +518,6 @@ class LMHeadLossFn(Function):
             h, dlogits = ctx.saved_tensors
             dh = K.gemm(dlogits, w.w16, b_mn=True, alpha=g)
             K.gemm(dlogits, h, out=w.main_grad, a_mn=True, b_mn=True, accumulate=acc, alpha=g)
-        K.colsum_(dlogits, b.main_grad, acc, scale=g)
+            K.colsum_(dlogits, b.main_grad, acc, scale=g)
         _grads_done(w, b)
         return dh, None, None, None, None

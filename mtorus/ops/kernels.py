@@ -30,10 +30,14 @@ def layernorm_bwd(dy, x, gamma, mean, rstd, dgamma, dbeta, accumulate: bool, dre
 
 
 def xent_fused(logits: torch.Tensor, targets: torch.Tensor, grad_scale: Optional[torch.Tensor] = None,
-               scale_mul: float = 1.0, write_grad: bool = True) -> torch.Tensor:
+               scale_mul: float = 1.0, write_grad: bool = True, out8: Optional[torch.Tensor] = None,
+               out8_scale: Optional[torch.Tensor] = None, out8_amax: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Per-row CE loss; when write_grad, logits are overwritten in place with
-    grad_scale * scale_mul * (softmax - onehot)."""
-    return _cuda().xent_fused(logits, targets, grad_scale, float(scale_mul), bool(write_grad))
+    grad_scale * scale_mul * (softmax - onehot) -- or, with out8 (uint8 like the logits),
+    those dlogits are written there as E5M2 codes times out8_scale (the logits stay) and
+    their max |value| goes into out8_amax."""
+    return _cuda().xent_fused(logits, targets, grad_scale, float(scale_mul), bool(write_grad), out8=out8,
+                              out8_scale=out8_scale, out8_amax=out8_amax)
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *, a_mn: bool = False,
@@ -119,6 +123,12 @@ def gelu_bwd_(dact, pre):
 def colsum_(x, out, accumulate: bool, scale=None):
     """out (+)= scale * column sums of x (bf16 [rows, F] -> fp32 [F])."""
     _cuda().colsum_(x.contiguous(), out, bool(accumulate), scale)
+    return out
+
+
+def colsum_e5m2_(codes, out, accumulate: bool, scale=None, scale2=None):
+    """out (+)= scale * scale2 * column sums of E5M2 codes (uint8 [rows, F] -> fp32 [F])."""
+    _cuda().colsum_e5m2_(codes.contiguous(), out, bool(accumulate), scale, scale2)
     return out
 
 

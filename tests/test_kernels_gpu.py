@@ -415,6 +415,37 @@ def test_fp8_wire_codec_kernels_match_reference(dtype):
         assert torch.equal(back[ok], want[ok])
 
 
+def test_xent_writes_e5m2_dlogits_like_the_separate_quantiser(K):
+    """The cross-entropy kernel's E5M2 output: the codes the separate quantiser makes of the
+    bf16 dlogits it would otherwise write, the same amax, the same loss; the logits are left
+    untouched; and the column sums over the codes give the bias gradient of those codes."""
+    from mtorus.ops import fp8 as F8
+
+    T, V = 256, 50304
+    g = torch.Generator(device="cuda").manual_seed(9)
+    logits = (torch.randn(T, V, device="cuda", generator=g) * 3).bfloat16()
+    tgt = torch.randint(0, V, (T,), device="cuda", generator=g)
+    gs = torch.full((1,), 1024.0, device="cuda")
+    scale = torch.full((1,), 4096.0, device="cuda")
+    amax = torch.zeros(1, device="cuda")
+    codes = torch.empty(T, V, dtype=torch.uint8, device="cuda")
+    ref_logits = logits.clone()
+    before = logits.clone()
+    loss8 = K.xent_fused(logits, tgt, gs, 1.0 / T, True, out8=codes, out8_scale=scale, out8_amax=amax)
+    assert torch.equal(logits, before)
+    loss = K.xent_fused(ref_logits, tgt, gs, 1.0 / T, True)  # ref_logits now holds bf16 dlogits
+    assert torch.equal(loss8, loss)
+    amax_ref = torch.zeros(1, device="cuda")
+    want = F8.quantize(ref_logits, F8.E5M2, scale, amax_ref)
+    assert torch.equal(codes, want)
+    assert torch.equal(amax, amax_ref)
+    cs = torch.zeros(V, device="cuda")
+    inv = 1.0 / scale
+    K.colsum_e5m2_(codes, cs, False, scale=inv)
+    dec = F8.dequantize(codes, inv, F8.E5M2)
+    assert torch.allclose(cs, dec.sum(0), rtol=1e-5, atol=1e-6)
+
+
 def test_gemm_epilogue_gelu_matches_fp32_erf_gelu(K):
     """The CTA-pair GEMM epilogue's GELU (alternating the special-function-unit and the
     FMA-pipe forms over its values) and its dGELU agree with PyTorch's fp32 erf GELU
