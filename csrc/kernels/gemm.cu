@@ -463,7 +463,9 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
                                                 const DropoutArgs& drop, int drop_mode, const MxOutArgs& mxo,
                                                 const CUtensorMap* tma_cc) {
   if (n0 >= N) return;  // warp-uniform
-  uint8_t* stage = stages + sb * P_EPI_BUF;
+  // A single 4 KB buffer (NB == 1) still double-buffers a plain bf16 chunk (2 KB): its halves alternate
+  const bool halves = NB == 1 && !MXO && !f32out && !ep.act && !ep.act8;
+  uint8_t* stage = stages + sb * (halves ? P_EPI_BUF / 2 : P_EPI_BUF);
   uint32_t keep = 0xFFFFFFFFu;
   if constexpr (DROP) {
     const uint32_t k0 = drop.rng[0], k1 = drop.rng[1];
@@ -512,7 +514,12 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
       for (int i = 0; i < 8; ++i) v[j * 8 + i] += r8[i];
     }
   }
-  if (lane == 0) bulk_wait_group_read<NB - 1>();  // the store that last used this buffer has read it
+  if (lane == 0) {  // the store that last used this buffer has read it
+    if (halves)
+      bulk_wait_group_read<1>();
+    else
+      bulk_wait_group_read<NB - 1>();
+  }
   __syncwarp();
   if constexpr (MXO) {
     // The chunk is 32 rows (one per lane) x 32 columns: one row block per lane and,
@@ -663,7 +670,7 @@ __device__ __forceinline__ void epi_chunk_store(const uint32_t (&r)[32], const u
     }
     bulk_commit_group();
   }
-  if (NB == 2) sb ^= 1;
+  if (NB == 2 || halves) sb ^= 1;
 }
 
 // EB = operand element bytes: 2 (bf16, kind::f16) or 1 (fp8 E4M3/E5M2, kind::f8f6f4).
