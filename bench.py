@@ -37,6 +37,12 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+def _mx_library() -> bool:
+    from mtorus.ops import mxfp8
+
+    return mxfp8.LIBRARY_PLAIN_GEMM
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -230,7 +236,8 @@ def main() -> int:
             "precision": args.precision,
             "gemm": {"fp8": "tcgen05 kind::f8f6f4 fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, fp32 accumulate",
                      "mxfp8": "tcgen05 kind::mxf8f6f4 block-scaled fp8 + kind::f16 bf16, CTA-pair 256x256 tiles, "
-                              "fp32 accumulate",
+                              "fp32 accumulate" + ("; plain GEMMs (bias-only epilogue, fresh output) on cuBLASLt MXFP8"
+                                                   if _mx_library() else ""),
                      "bf16": "tcgen05 kind::f16 bf16, CTA-pair 256x256 tiles"}[args.precision],
             "l2": "per-step working set (activations, 1.4B-param optimizer state) >> 126 MB L2; no flush",
             "params": cfg.num_params(),

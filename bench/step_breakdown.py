@@ -26,6 +26,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 CLASSES = [  # (class, regex over the demangled kernel name); first match wins
     ("gemm fp8 (block GEMMs)", r"gemm_2sm_kernel<1"),
     ("gemm bf16 (LM head)", r"gemm_2sm_kernel<2|gemm_bf16_tn"),
+    ("gemm mxfp8 plain (cuBLASLt)", r"bstensorop|block_scaled"),
     ("attention fwd", r"attn_fwd"),
     ("attention bwd", r"attn_bwd|attn_dq"),
     ("cross-entropy", r"xent"),

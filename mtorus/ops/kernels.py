@@ -92,6 +92,8 @@ class gemm_dropout:
     the dGELU.  The setting is consumed by the next GEMM launch and cleared on exit in
     any case, so it never leaks into a later GEMM."""
 
+    armed = False  # a setting is pending: the GEMM inside must be this library's kernel
+
     def __init__(self, drop, mode: int):
         self.drop, self.mode = drop, mode
 
@@ -99,11 +101,13 @@ class gemm_dropout:
         if self.drop is not None:
             rng, site, thr, scale = self.drop
             _cuda().gemm_set_dropout(rng, int(site), int(thr), float(scale), int(self.mode))
+            gemm_dropout.armed = True
         return self
 
     def __exit__(self, *exc):
         if self.drop is not None:
             _cuda().gemm_set_dropout(None, 0, 0, 1.0, 0)
+            gemm_dropout.armed = False
         return False
 
 

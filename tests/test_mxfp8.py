@@ -9,6 +9,8 @@ fp32 product of the dequantised operands (and with cuBLAS's MX GEMM).
 import pytest
 import torch
 
+import mtorus.ops.mxfp8 as mxfp8_mod
+
 from mtorus.ops.mxfp8 import (E4M3, E5M2, MX_FMT_MAX, MxTensor, gemm_mxfp8, gemm_mxfp8_mx_out, gemm_mxfp8_ref,
                               mx_dequantize, mx_linear, mx_quantize, mx_quantize_rc, mx_quantize_ref, sf_numel,
                               sf_offsets)
@@ -148,11 +150,11 @@ def test_block_scaled_gemm_matches_fp32_oracle(shape, fmts):
     da = mx_dequantize(MxTensor(a.codes.cpu(), a.sf.cpu(), a.fmt)).double()
     db = mx_dequantize(MxTensor(b.codes.cpu(), b.sf.cpu(), b.fmt)).double()
     mag = (da.abs() @ db.abs().t()).float()
-    out = gemm_mxfp8(a, b, out_dtype=torch.float32)
+    out = gemm_mxfp8(a, b, out_dtype=torch.float32, impl="own")
     torch.cuda.synchronize()
     err = (out.cpu() - ref).abs()
     assert bool((err <= 1e-5 * mag + 1e-30).all()), float((err / mag.clamp_min(1e-30)).max())
-    out16 = gemm_mxfp8(a, b).float().cpu()
+    out16 = gemm_mxfp8(a, b, impl="own").float().cpu()
     assert bool(((out16 - ref).abs() <= 1e-2 * ref.abs() + 1e-5 * mag + 1e-30).all())
 
 
@@ -168,7 +170,7 @@ def test_block_scaled_gemm_both_operands_blocky():
     da = mx_dequantize(MxTensor(a.codes.cpu(), a.sf.cpu(), a.fmt)).double()
     db = mx_dequantize(MxTensor(b.codes.cpu(), b.sf.cpu(), b.fmt)).double()
     mag = (da.abs() @ db.abs().t()).float()
-    out = gemm_mxfp8(a, b, out_dtype=torch.float32)
+    out = gemm_mxfp8(a, b, out_dtype=torch.float32, impl="own")
     err = (out.cpu() - ref).abs()
     assert bool((err <= 1e-5 * mag + 1e-30).all()), float((err / mag.clamp_min(1e-30)).max())
 
@@ -185,8 +187,28 @@ def test_block_scaled_gemm_agrees_with_cublas_mx():
                                b.sf.view(torch.float8_e8m0fnu).reshape(N, -1), out_dtype=torch.float32)
     except (RuntimeError, AttributeError, TypeError) as e:
         pytest.skip(f"torch._scaled_mm has no MX path here: {e}")
-    out = gemm_mxfp8(a, b, out_dtype=torch.float32)
+    out = gemm_mxfp8(a, b, out_dtype=torch.float32, impl="own")
     assert torch.allclose(out, lib, rtol=1e-4, atol=1e-4 * float(lib.abs().max()))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("out_dtype,bias", [(torch.float32, False), (torch.bfloat16, True)])
+def test_library_path_matches_own_kernel(out_dtype, bias):
+    """The plain-GEMM routing to cuBLASLt (E5M2 x E4M3 as in dgrad / wgrad, a bias as in the
+    QKV projection) gives what gemm_2sm_kernel gives, and "auto" takes it."""
+    M, N, K = 512, 768, 1024
+    a = mx_quantize((_blocky(M, K, seed=21) * 1e-3).to(torch.bfloat16).cuda(), E5M2)
+    b = mx_quantize((torch.randn(N, K) * 0.02).to(torch.bfloat16).cuda(), E4M3)
+    bb = (torch.randn(N) * 0.1).to(torch.bfloat16).float().cuda() if bias else None
+    own = gemm_mxfp8(a, b, out_dtype=out_dtype, bias=bb, impl="own").float()
+    lib = gemm_mxfp8(a, b, out_dtype=out_dtype, bias=bb, impl="library").float()
+    auto = gemm_mxfp8(a, b, out_dtype=out_dtype, bias=bb).float()
+    tol = 1e-5 if out_dtype == torch.float32 else 8e-3
+    assert ((lib - own).norm() / own.norm()).item() < tol
+    if mxfp8_mod.LIBRARY_PLAIN_GEMM:
+        assert torch.equal(auto, lib)
+    with pytest.raises(ValueError):
+        gemm_mxfp8(a, b, out_dtype=torch.float32, accumulate=True, impl="library")
 
 
 @pytest.mark.gpu
