@@ -82,7 +82,8 @@ void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at:
                          at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, at::Tensor mean,
                          at::Tensor rstd, int64_t fmt, double fmax);
 void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, int64_t fmt,
-                    double fmax, const c10::optional<at::Tensor>& colsum, const c10::optional<at::Tensor>& xq);
+                    double fmax, const c10::optional<at::Tensor>& colsum, const c10::optional<at::Tensor>& xq,
+                    int64_t act, const c10::optional<at::Tensor>& aux);
 void gemm_fp8_gather_b(const at::Tensor& A, bool a_mn, int64_t a_fmt, const at::Tensor& B, bool b_mn,
                        int64_t b_fmt, const std::vector<int64_t>& b_peers, int64_t shard_rows, at::Tensor D,
                        const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
@@ -262,7 +263,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("st"), py::arg("ctas"), py::arg("inv_n"), py::arg("mine"), py::arg("ep_ptr") = 0);
   m.def("layernorm_fwd_mx_rc", &layernorm_fwd_mx_rc);
   m.def("mx_quantize_rc", &mx_quantize_rc, py::arg("x"), py::arg("rc"), py::arg("rsf"), py::arg("cc"),
-        py::arg("csf"), py::arg("fmt"), py::arg("fmax"), py::arg("colsum") = py::none(), py::arg("xq") = py::none());
+        py::arg("csf"), py::arg("fmt"), py::arg("fmax"), py::arg("colsum") = py::none(), py::arg("xq") = py::none(),
+        py::arg("act") = 0, py::arg("aux") = py::none());
   m.def("gemm_fp8_gather_b", &gemm_fp8_gather_b, py::arg("A"), py::arg("a_mn"), py::arg("a_fmt"), py::arg("B"),
         py::arg("b_mn"), py::arg("b_fmt"), py::arg("b_peers"), py::arg("shard_rows"), py::arg("D"),
         py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("act") = py::none(),

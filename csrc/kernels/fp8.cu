@@ -14,6 +14,7 @@
 #include <cstring>
 
 #include "amax_publish.cuh"
+#include "gelu.cuh"
 #include "mx.cuh"
 
 namespace mtorus {
@@ -339,10 +340,14 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(const bf16* __restrict
 // load-then-compute CTA exposes.  Codes go from registers straight to global
 // memory as whole 32-byte sectors (a row block of 32 codes, or a column block of
 // 32 codes of the transpose).
-// LN: the tile is LayerNorm'd in shared memory after it lands,
+// SRC picks what is quantised: 0 the tile as loaded; 1 (LN) its LayerNorm,
 // bf16((x - mean[r]) * rstd[r] * gamma[c] + beta[c]) (the MXFP8 input of the QKV /
-// FFN1 GEMMs straight from the residual stream).  colsum (optional):
-// colsum[c] += sum over r of the tile's values (one atomic per column per tile).
+// FFN1 GEMMs straight from the residual stream); 2 (GELU) bf16(GELU(x)) (the FFN2
+// GEMM's input from the FFN1 pre-activation); 3 (dGELU) bf16(x * GELU'(aux[r, c]))
+// (the FFN1 GEMMs' output gradient from the FFN2 dgrad and the pre-activation).  The
+// transform runs in shared memory after the tile lands.  colsum (optional):
+// colsum[c] += sum over r of the tile's (transformed) values (one atomic per column
+// per tile).
 constexpr int kRcTileStride = 128 + 8;  // bf16 elements per staged row (16-byte rows, bank spread)
 constexpr int kRcTileBytes = 128 * kRcTileStride * 2;
 // dynamic shared memory: two bf16 tiles | two scale atoms | fp32 column sums [4][128]
@@ -363,12 +368,13 @@ __device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, int
 __device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-template <bool LN>
+template <int SRC>
 __global__ void __launch_bounds__(256, kRcCtasPerSm) mx_rc_tile_kernel(
     const bf16* __restrict__ x, int64_t ldx, int R, int C, int fmt, uint32_t fmax_bits,
     const float* __restrict__ mean, const float* __restrict__ rstd, const float* __restrict__ gamma,
     const float* __restrict__ beta, float* __restrict__ colsum, uint8_t* __restrict__ rc, uint8_t* __restrict__ rsf,
-    uint8_t* __restrict__ cc, uint8_t* __restrict__ csf, const float* __restrict__ xq, int64_t ldq, int qcols) {
+    uint8_t* __restrict__ cc, uint8_t* __restrict__ csf, const float* __restrict__ xq, int64_t ldq, int qcols,
+    const bf16* __restrict__ aux, int64_t ldaux) {
   // xq (optional): columns [0, qcols) of the tensor come from this fp32 matrix instead of x
   // (rounded to bf16 on load; qcols a multiple of 128), e.g. the attention's dQ accumulator
   // beside the dK / dV it wrote into x
@@ -423,7 +429,7 @@ __global__ void __launch_bounds__(256, kRcCtasPerSm) mx_rc_tile_kernel(
       }
       __syncthreads();
     }
-    if (LN) {
+    if constexpr (SRC == 1) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
@@ -440,6 +446,32 @@ __global__ void __launch_bounds__(256, kRcCtasPerSm) mx_rc_tile_kernel(
           const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
           for (int q = 0; q < 8; ++q) f[q] = (f[q] - mu) * rs * g[q] + b[q];
+          *reinterpret_cast<bf16x8*>(&tl[rr][cv]) = pack8(f);
+        }
+      }
+      __syncthreads();
+    }
+    if constexpr (SRC == 2 || SRC == 3) {
+      // two pieces per step: their aux loads (dGELU) are in flight together, and the
+      // launch's register budget (three CTAs per SM) holds no more
+#pragma unroll 2
+      for (int k = 0; k < 8; ++k) {
+        const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
+        const int r = r0 + rr, c = c0 + cv;
+        if (r < R && c < C) {
+          float f[8];
+          if constexpr (SRC == 2) {
+            unpack8(*reinterpret_cast<const bf16x8*>(&tl[rr][cv]), f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) f[q] = gelu_fwd(f[q]);
+          } else {
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(aux + (int64_t)r * ldaux + c));
+            float a[8];
+            unpack8(*reinterpret_cast<const bf16x8*>(&u), a);
+            unpack8(*reinterpret_cast<const bf16x8*>(&tl[rr][cv]), f);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) f[q] *= gelu_grad(a[q]);
+          }
           *reinterpret_cast<bf16x8*>(&tl[rr][cv]) = pack8(f);
         }
       }
@@ -740,7 +772,7 @@ void mx_quantize(const at::Tensor& x, at::Tensor codes, at::Tensor sf, int64_t f
 void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, double fmax, const float* ln_mean,
                  const float* ln_rstd, const float* ln_gamma, const float* ln_beta, float* colsum, uint8_t* rc,
                  uint8_t* rsf, uint8_t* cc, uint8_t* csf, cudaStream_t st, const float* xq, int64_t ldq,
-                 int64_t qcols) {
+                 int64_t qcols, int act, const bf16* aux, int64_t ldaux) {
   const float fm = (float)fmax;
   uint32_t fbits;
   std::memcpy(&fbits, &fm, 4);
@@ -748,16 +780,25 @@ void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, 
   const int grid = (int)std::min<int64_t>(tiles, (int64_t)num_sms() * kRcCtasPerSm);
   static bool attr = false;
   if (!attr) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));
-    C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(mx_rc_tile_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRcSmem));
     attr = true;
   }
   if (ln_mean)
-    mx_rc_tile_kernel<true><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, ln_mean, ln_rstd,
-                                                   ln_gamma, ln_beta, colsum, rc, rsf, cc, csf, nullptr, 0, 0);
+    mx_rc_tile_kernel<1><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, ln_mean, ln_rstd,
+                                                ln_gamma, ln_beta, colsum, rc, rsf, cc, csf, nullptr, 0, 0, nullptr, 0);
+  else if (act == 2)
+    mx_rc_tile_kernel<2><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, nullptr, nullptr,
+                                                nullptr, nullptr, colsum, rc, rsf, cc, csf, nullptr, 0, 0, nullptr, 0);
+  else if (act == 3)
+    mx_rc_tile_kernel<3><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, nullptr, nullptr,
+                                                nullptr, nullptr, colsum, rc, rsf, cc, csf, nullptr, 0, 0, aux, ldaux);
   else
-    mx_rc_tile_kernel<false><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, nullptr, nullptr,
-                                                    nullptr, nullptr, colsum, rc, rsf, cc, csf, xq, ldq, (int)qcols);
+    mx_rc_tile_kernel<0><<<grid, 256, kRcSmem, st>>>(x, ldx, (int)R, (int)C, (int)fmt, fbits, nullptr, nullptr,
+                                                nullptr, nullptr, colsum, rc, rsf, cc, csf, xq, ldq, (int)qcols,
+                                                nullptr, 0);
   MT_LAUNCH_CHECK();
 }
 
@@ -765,7 +806,8 @@ void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, 
 // whose output gradient x is), in the same pass.  xq (optional fp32 [R, Q], Q a multiple
 // of 128): columns [0, Q) of the tensor are taken from xq (rounded to bf16) instead of x.
 void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, int64_t fmt,
-                    double fmax, const c10::optional<at::Tensor>& colsum, const c10::optional<at::Tensor>& xq) {
+                    double fmax, const c10::optional<at::Tensor>& colsum, const c10::optional<at::Tensor>& xq,
+                    int64_t act, const c10::optional<at::Tensor>& aux) {
   MT_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "mx_quantize_rc: 2-D bf16 input");
   const int64_t R = x.size(0), C = x.size(1);
   MT_CHECK(R % 32 == 0 && C % 32 == 0, "mx_quantize_rc: R and C must be multiples of 32");
@@ -795,12 +837,24 @@ void mx_quantize_rc(const at::Tensor& x, at::Tensor rc, at::Tensor rsf, at::Tens
     ldq = xq->stride(0);
     qcols = xq->size(1);
   }
+  MT_CHECK(act == 0 || act == 2 || act == 3, "mx_quantize_rc: act 0 (none), 2 (GELU) or 3 (dGELU)");
+  MT_CHECK(act == 0 || !xq.has_value(), "mx_quantize_rc: xq takes no activation");
+  const bf16* auxp = nullptr;
+  int64_t ldaux = 0;
+  if (act == 3) {
+    MT_CHECK(aux.has_value() && aux->scalar_type() == at::kBFloat16 && aux->dim() == 2 && aux->size(0) == R &&
+                 aux->size(1) == C && aux->stride(1) == 1 && (aux->stride(0) * 2) % 16 == 0 &&
+                 reinterpret_cast<uintptr_t>(aux->data_ptr()) % 16 == 0,
+             "mx_quantize_rc: dGELU needs aux bf16 [R, C] with 16-byte aligned rows");
+    auxp = reinterpret_cast<const bf16*>(aux->data_ptr());
+    ldaux = aux->stride(0);
+  }
   if (R == 0 || C == 0) return;
   mx_rc_tiles(reinterpret_cast<const bf16*>(x.data_ptr()), x.stride(0), R, C, fmt, fmax, nullptr, nullptr, nullptr,
               nullptr, colsum.has_value() ? colsum->data_ptr<float>() : nullptr,
               reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),
               reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()), cur_stream(), xqp,
-              ldq, qcols);
+              ldq, qcols, (int)act, auxp, ldaux);
 }
 
 void fp8_quantize_blocks(const at::Tensor& x, at::Tensor out, at::Tensor scales, int64_t block_size,

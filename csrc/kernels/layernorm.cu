@@ -564,7 +564,7 @@ __global__ void __launch_bounds__(256) ln_row_stats_kernel(const bf16* __restric
 void mx_rc_tiles(const bf16* x, int64_t ldx, int64_t R, int64_t C, int64_t fmt, double fmax, const float* ln_mean,
                  const float* ln_rstd, const float* ln_gamma, const float* ln_beta, float* colsum, uint8_t* rc,
                  uint8_t* rsf, uint8_t* cc, uint8_t* csf, cudaStream_t st, const float* xq, int64_t ldq,
-                 int64_t qcols);
+                 int64_t qcols, int act, const bf16* aux, int64_t ldaux);
 
 void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at::Tensor& beta, double eps,
                          at::Tensor rc, at::Tensor rsf, at::Tensor cc, at::Tensor csf, at::Tensor mean,
@@ -600,7 +600,7 @@ void layernorm_fwd_mx_rc(const at::Tensor& x, const at::Tensor& gamma, const at:
               rstd.data_ptr<float>(), gamma.data_ptr<float>(), beta.data_ptr<float>(), nullptr,
               reinterpret_cast<uint8_t*>(rc.data_ptr()), reinterpret_cast<uint8_t*>(rsf.data_ptr()),
               reinterpret_cast<uint8_t*>(cc.data_ptr()), reinterpret_cast<uint8_t*>(csf.data_ptr()), st, nullptr, 0,
-              0);
+              0, 0, nullptr, 0);
 }
 
 std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& gamma,

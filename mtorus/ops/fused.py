@@ -293,10 +293,25 @@ def _attn_fwd_mx(attention_fwd, MX, qkv, B, S, H, drop):
 
 def _mx_gemm_quant(MX, a, b, fmt, out=None, *, bias=None, aux=None, gelu=False, colsum=None, accumulate=True,
                    store_d=True):
-    """Block-scaled GEMM whose output (or its GELU) leaves as MXFP8 row and column
-    codes: fused into the epilogue when M and N are multiples of 128, else the GEMM
-    followed by the row / column quantiser.  Returns (D or None, rows, cols)."""
+    """Block-scaled GEMM whose output (or its GELU, or its product with GELU'(aux))
+    leaves as MXFP8 row and column codes.  Returns (D or None, rows, cols).
+
+    On the GPU with ``LIBRARY_PLAIN_GEMM`` (the default) the plain GEMM (bias at most)
+    runs in cuBLASLt and writes D in bf16, then the row / column quantiser applies
+    GELU / dGELU to each tile as it quantises it: measured on B200 at the GPT-1B FFN
+    shapes this pair beats the MX-output epilogue of gemm_2sm_kernel, whose mainloop
+    is the slower one.  The epilogue version runs when dropout is drawn in the GEMM
+    epilogue or the library path is off; tiles that are not multiples of 128 take this
+    library's GEMM with the GELU / dGELU epilogue, then the quantiser."""
+    from .kernels import gemm_dropout
+
     M, N = a.codes.shape[0], b.codes.shape[0]
+    if a.codes.is_cuda and MX.LIBRARY_PLAIN_GEMM and not gemm_dropout.armed and M % 32 == 0 and N % 32 == 0:
+        d = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a.codes.device)
+        MX.gemm_mxfp8(a, b, out=d, bias=bias)
+        rows, cols = MX.mx_quantize_rc(d, fmt, colsum=colsum, accumulate=accumulate,
+                                       act="gelu" if gelu else ("dgelu" if aux is not None else None), aux=aux)
+        return (d if store_d else None), rows, cols
     if M % 128 == 0 and N % 128 == 0:
         return MX.gemm_mxfp8_mx_out(a, b, fmt, out, bias=bias, aux=aux, gelu=gelu, colsum=colsum,
                                     accumulate=accumulate, store_d=store_d)
@@ -332,7 +347,8 @@ class MLPBlockFn(Function):
 
             gamma, beta, eps = ln
             hr, hc, mean, rstd = MX.mx_layernorm_rc(x2d, gamma.data, beta.data, eps, MX.E4M3)
-            # the FFN1 epilogue stores the pre-activation and quantises GELU of it both ways
+            # FFN1 stores the pre-activation; GELU of it is quantised both ways (in the
+            # quantiser's pass or in the GEMM's MX epilogue, as _mx_gemm_quant picks)
             with K.gemm_dropout(d_act, 2):
                 _, ar, ac = _mx_gemm_quant(MX, hr, w1.mx[0], MX.E4M3, out=pre, bias=b1.data, gelu=True)
             with K.gemm_dropout(d_out, 1):
@@ -421,8 +437,8 @@ class MLPBlockFn(Function):
         dbr = K.dropout_apply(dout, d_out) if d_out is not None else dout
         hc, ac = _mx_t(hcc, hcs, MX.E4M3), _mx_t(acc_codes, acs, MX.E4M3)
         grow, gcol = MX.mx_quantize_rc(dbr, MX.E5M2, colsum=b2.main_grad, accumulate=acc)
-        # dgrad: hidden-dropout mask, then dGELU; the epilogue quantises the result both ways and
-        # sums its columns into the FFN1 bias gradient
+        # dgrad: hidden-dropout mask, then dGELU; the result is quantised both ways and its
+        # columns summed into the FFN1 bias gradient (quantiser pass or MX epilogue)
         with K.gemm_dropout(d_act, 3):
             _, prow, pcol = _mx_gemm_quant(MX, grow, w2.mx[1], MX.E5M2, aux=pre, colsum=b1.main_grad,
                                            accumulate=acc, store_d=False)

@@ -236,19 +236,44 @@ def gemm_mxfp8_mx_out(a: MxTensor, b: MxTensor, fmt: int, out: Optional[torch.Te
     return (out if store_d else None), MxTensor(rc, rsf, int(fmt)), MxTensor(cc, csf, int(fmt))
 
 
+_RC_ACT = {None: 0, "gelu": 2, "dgelu": 3}
+
+
+def _erf_gelu(x: torch.Tensor) -> torch.Tensor:
+    return 0.5 * x * (1.0 + torch.erf(x * 0.7071067811865476))
+
+
+def _erf_gelu_grad(x: torch.Tensor) -> torch.Tensor:
+    return 0.5 * (1.0 + torch.erf(x * 0.7071067811865476)) + x * torch.exp(-0.5 * x * x) * 0.3989422804014327
+
+
 def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = None,
                    colsum: Optional[torch.Tensor] = None, accumulate: bool = True,
-                   xq: Optional[torch.Tensor] = None):
+                   xq: Optional[torch.Tensor] = None, act: Optional[str] = None,
+                   aux: Optional[torch.Tensor] = None):
     """Row-wise MXFP8 of x [R, C] (32-blocks along C) and of its transpose [C, R]
     (32-blocks along R), in one pass on the GPU: the operands that contract over C
     and over R.  R and C multiples of 32.  The reference on the CPU.
 
-    colsum (fp32 [C], optional): receives the column sums of x in the same pass (the
-    bias gradient when x is a layer's output gradient), added to its contents when
-    ``accumulate``, else overwriting them.  xq (fp32 [R, Q], Q a multiple of 128, optional):
-    the first Q columns are taken from xq rounded to bf16 instead of from x."""
+    colsum (fp32 [C], optional): receives the column sums of what is quantised in the
+    same pass (the bias gradient when x is a layer's output gradient), added to its
+    contents when ``accumulate``, else overwriting them.  xq (fp32 [R, Q], Q a multiple of
+    128, optional): the first Q columns are taken from xq rounded to bf16 instead of from x.
+    act: None quantises x; "gelu" bf16(GELU(x)) (x a pre-activation); "dgelu"
+    bf16(x * GELU'(aux)) with aux the bf16 pre-activation [R, C] (x the gradient of the
+    GELU output)."""
     if x.dim() != 2 or x.shape[0] % BLOCK or x.shape[1] % BLOCK:
         raise ValueError("mx_quantize_rc: 2-D input with both sizes multiples of 32 expected")
+    if act not in _RC_ACT:
+        raise ValueError(f"mx_quantize_rc: act must be None, 'gelu' or 'dgelu', not {act!r}")
+    if (act == "dgelu") != (aux is not None):
+        raise ValueError("mx_quantize_rc: aux is the pre-activation of act='dgelu' and nothing else")
+    if act is not None and xq is not None:
+        raise ValueError("mx_quantize_rc: xq takes no activation")
+    if act is not None and not x.is_cuda:
+        xf = x.to(torch.bfloat16).float()
+        xf = _erf_gelu(xf) if act == "gelu" else xf * _erf_gelu_grad(aux.to(torch.bfloat16).float())
+        x, act, aux = xf.to(torch.bfloat16), None, None
     if xq is not None:
         if xq.shape[0] != x.shape[0] or xq.shape[1] % 128 or xq.shape[1] > x.shape[1]:
             raise ValueError("mx_quantize_rc: xq must be [R, Q] with Q a multiple of 128, Q <= C")
@@ -275,7 +300,11 @@ def mx_quantize_rc(x: torch.Tensor, fmt: int = E4M3, fmax: Optional[float] = Non
     csf = torch.empty(sf_numel(C, R), dtype=torch.uint8, device=x.device)
     if colsum is not None and not accumulate:
         colsum.zero_()
-    _cuda().mx_quantize_rc(x, rc, rsf, cc, csf, int(fmt), fmax, colsum, xq)
+    if aux is not None:
+        aux = aux if aux.dtype == torch.bfloat16 else aux.to(torch.bfloat16)
+        if aux.stride(1) != 1:
+            aux = aux.contiguous()
+    _cuda().mx_quantize_rc(x, rc, rsf, cc, csf, int(fmt), fmax, colsum, xq, _RC_ACT[act], aux)
     return MxTensor(rc, rsf, int(fmt)), MxTensor(cc, csf, int(fmt))
 
 

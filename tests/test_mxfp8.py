@@ -125,6 +125,27 @@ def test_mx_quantize_rc_cpu_is_row_and_transposed_reference():
 # ---------------------------------------------------------------- GPU
 
 
+def test_mx_quantize_rc_cpu_activation_modes():
+    """act="gelu" / "dgelu" on the CPU: the quantiser of bf16(GELU(x)) / bf16(x * GELU'(aux))
+    with the erf GELU."""
+    g = torch.Generator().manual_seed(3)
+    pre = (torch.randn(64, 96, generator=g) * 2).to(torch.bfloat16)
+    dact = (torch.randn(64, 96, generator=g) * 1e-2).to(torch.bfloat16)
+    r, c = mx_quantize_rc(pre, E4M3, act="gelu")
+    x = pre.float()
+    want = (0.5 * x * (1.0 + torch.erf(x * 0.7071067811865476))).to(torch.bfloat16)
+    assert torch.equal(r.codes, mx_quantize_ref(want, E4M3).codes)
+    assert torch.equal(c.codes, mx_quantize_ref(want.t(), E4M3).codes)
+    cs = torch.zeros(96)
+    r, c = mx_quantize_rc(dact, E5M2, colsum=cs, accumulate=False, act="dgelu", aux=pre)
+    d = dact.float() * (0.5 * (1.0 + torch.erf(x * 0.7071067811865476)) + x * torch.exp(-0.5 * x * x) * 0.3989422804014327)
+    d = d.to(torch.bfloat16)
+    assert torch.equal(r.codes, mx_quantize_ref(d, E5M2).codes)
+    assert torch.allclose(cs, d.float().sum(0))
+    with pytest.raises(ValueError):
+        mx_quantize_rc(dact, E5M2, act="dgelu")
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("fmt", [E4M3, E5M2])
 def test_cuda_quantiser_matches_reference(fmt):
@@ -262,6 +283,33 @@ def test_gemm_epilogue_mx_output_matches_unfused_quantiser(M, N):
     for got, want in ((r, r_ref), (c, c_ref)):
         assert torch.equal(got.codes, want.codes) and torch.equal(got.sf, want.sf)
     assert torch.allclose(cs, cs_ref, rtol=1e-5, atol=1e-5 * float(dpre_ref.float().abs().sum(0).max()))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,C", [(512, 768), (96, 320)])
+def test_row_col_quantiser_gelu_and_dgelu_match_elementwise_then_quantise(R, C):
+    """The quantiser's GELU / dGELU source modes (the FFN1 output and the FFN2 dgrad after a
+    library GEMM) give exactly what the elementwise GELU / dGELU kernels followed by the
+    plain quantiser give: the same bf16 values, codes, scale atoms and column sums."""
+    from mtorus.ops import kernels as K
+
+    g = torch.Generator().manual_seed(R + C)
+    pre = (torch.randn(R, C, generator=g) * 2.0).to(torch.bfloat16).cuda()
+    r, c = mx_quantize_rc(pre, E4M3, act="gelu")
+    r_ref, c_ref = mx_quantize_rc(K.bias_gelu_fwd(pre), E4M3)
+    for got, want in ((r, r_ref), (c, c_ref)):
+        assert torch.equal(got.codes, want.codes) and torch.equal(got.sf, want.sf)
+    dact = (torch.randn(R, C, generator=g) * 1e-3).to(torch.bfloat16).cuda()
+    cs = torch.full((C,), 0.25, device="cuda")
+    r, c = mx_quantize_rc(dact, E5M2, colsum=cs, accumulate=True, act="dgelu", aux=pre)
+    dpre = dact.clone()
+    K.gelu_bwd_(dpre, pre)
+    cs_ref = torch.full((C,), 0.25, device="cuda")
+    r_ref, c_ref = mx_quantize_rc(dpre, E5M2, colsum=cs_ref, accumulate=True)
+    torch.cuda.synchronize()
+    for got, want in ((r, r_ref), (c, c_ref)):
+        assert torch.equal(got.codes, want.codes) and torch.equal(got.sf, want.sf)
+    assert torch.allclose(cs, cs_ref, rtol=1e-5, atol=1e-5 * float(dpre.float().abs().sum(0).max()))
 
 
 @pytest.mark.gpu
