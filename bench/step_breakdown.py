@@ -149,7 +149,7 @@ def main() -> int:
     for c, v, k in rows:
         print(f"{c:32s} {v:9.3f} {v / step_ms:7.1%} {k:9.1f}")
     gemm_seq.sort()
-    fp8 = [d for _, d, c in gemm_seq if c.startswith("gemm fp8")]
+    fp8 = [d for _, d, c in gemm_seq if c.startswith("gemm fp8") or c.startswith("gemm mxfp8")]
     per_step = len(fp8) // n if n else 0
     if per_step >= 24:
         first = fp8[:per_step]

@@ -142,6 +142,21 @@ def _library_default() -> bool:
 LIBRARY_PLAIN_GEMM = _library_default()
 
 
+def _library_residual_default() -> bool:
+    import os
+
+    return os.environ.get("MTORUS_MX_LIBRARY_RESIDUAL", "1") != "0"
+
+
+# A GEMM with a residual add and a long contraction (K >= LIBRARY_RESIDUAL_MIN_K: the FFN2
+# forward, 16384 x 2048 x 8192) also runs in the library, followed by a bf16 add of the
+# residual: the library GEMM saves more than the add's extra pass over three [M, N] bf16
+# tensors costs.  At K = 2048 (the attention output projection) it does not, and the own
+# kernel's fused epilogue stays.  The split rounds the GEMM result to bf16 before the add.
+LIBRARY_RESIDUAL = _library_residual_default()
+LIBRARY_RESIDUAL_MIN_K = 4096
+
+
 def _library_eligible(a, b, out, residual, act, aux, alpha, accumulate) -> bool:
     from .kernels import gemm_dropout
 
@@ -158,7 +173,8 @@ def gemm_mxfp8(a: MxTensor, b: MxTensor, out: Optional[torch.Tensor] = None, *, 
     (both K-major); epilogue as in ``ops.kernels.gemm`` (bias, residual, GELU / dGELU,
     fp32 accumulate).  ``impl``: "own" runs gemm_2sm_kernel, "library" cuBLASLt's MXFP8
     GEMM (plain GEMMs only; the bias is rounded to the output dtype, as cuBLASLt adds it
-    in that precision), "auto" the library for plain GEMMs when ``LIBRARY_PLAIN_GEMM``."""
+    in that precision), "auto" the library for plain GEMMs when ``LIBRARY_PLAIN_GEMM`` and
+    for residual GEMMs with K >= ``LIBRARY_RESIDUAL_MIN_K`` when ``LIBRARY_RESIDUAL`` too."""
     M, K = a.codes.shape
     N, Kb = b.codes.shape
     if K != Kb:
@@ -168,6 +184,12 @@ def gemm_mxfp8(a: MxTensor, b: MxTensor, out: Optional[torch.Tensor] = None, *, 
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=a.codes.device)
     eligible = _library_eligible(a, b, out, residual, act, aux, alpha, accumulate)
+    if (impl == "auto" and LIBRARY_PLAIN_GEMM and LIBRARY_RESIDUAL and residual is not None
+            and K >= LIBRARY_RESIDUAL_MIN_K and out.dtype == torch.bfloat16 and residual.dtype == torch.bfloat16
+            and residual.shape == out.shape
+            and _library_eligible(a, b, out, None, act, aux, alpha, accumulate)):
+        y = gemm_mxfp8(a, b, torch.empty_like(out), bias=bias, impl="library")
+        return torch.add(y, residual, out=out)
     if impl == "library" and not eligible:
         raise ValueError("gemm_mxfp8: the library path takes plain GEMMs only (bias at most, no accumulate)")
     if impl == "library" or (impl == "auto" and eligible and LIBRARY_PLAIN_GEMM):

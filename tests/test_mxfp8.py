@@ -286,6 +286,22 @@ def test_gemm_epilogue_mx_output_matches_unfused_quantiser(M, N):
 
 
 @pytest.mark.gpu
+def test_long_k_residual_gemm_library_route_matches_own_kernel():
+    """A residual GEMM with K >= LIBRARY_RESIDUAL_MIN_K (the FFN2 forward) runs as the library GEMM
+    plus a bf16 add under "auto"; it agrees with the own kernel's fused residual epilogue to bf16
+    rounding."""
+    M, N, K = 256, 512, mxfp8_mod.LIBRARY_RESIDUAL_MIN_K
+    a = mx_quantize((torch.randn(M, K) * 0.5).to(torch.bfloat16).cuda())
+    b = mx_quantize((torch.randn(N, K) * 0.02).to(torch.bfloat16).cuda())
+    bias = (torch.randn(N) * 0.1).to(torch.bfloat16).float().cuda()
+    res = (torch.randn(M, N) * 2).to(torch.bfloat16).cuda()
+    own = gemm_mxfp8(a, b, bias=bias, residual=res, impl="own").float()
+    auto = gemm_mxfp8(a, b, bias=bias, residual=res).float()
+    assert ((auto - own).norm() / own.norm()).item() < 8e-3
+    assert ((auto - own).abs() <= 2e-2 * own.abs() + 1e-2).all()
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("R,C", [(512, 768), (96, 320)])
 def test_row_col_quantiser_gelu_and_dgelu_match_elementwise_then_quantise(R, C):
     """The quantiser's GELU / dGELU source modes (the FFN1 output and the FFN2 dgrad after a
