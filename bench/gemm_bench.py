@@ -2,7 +2,7 @@
 """GEMM microbenchmark: the tcgen05 GEMM against cuBLAS (torch.matmul) on the
 GPT-1B training shapes (T = 16384 tokens, d 2048, d_ff 8192, vocab 50304).
 
-    python bench/gemm_bench.py [--shapes small]
+    python bench/gemm_bench.py [--case NAME] [--group mx] [--stalls]
 
 Times each case with CUDA events after warm-up (median of --iters), prints
 TFLOP/s and the fraction of the measured bf16 peak (MEASURED_PEAKS.json).
@@ -61,6 +61,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--json", default=None)
     ap.add_argument("--case", default=None, help="run only the named case (e.g. ffn1_fwd_fp8)")
+    ap.add_argument("--group", default=None, choices=["mx"], help="run only the MXFP8 own-vs-library cases")
     ap.add_argument("--stalls", action="store_true",
                     help="also report, per case, where the CTA-pair kernel's MMA issuer waited (for loaded "
                          "operand stages vs for the epilogue to free an accumulator) over 5 extra launches")
@@ -92,6 +93,8 @@ def main():
     if args.case:
         fp8_cases = [c for c in fp8_cases if c[0] == args.case]
         cases = [c for c in cases if c[0] == args.case]
+    if args.group == "mx":
+        fp8_cases, cases = [], []
     for name, M, N, Kd, lay in fp8_cases:
         A = (torch.randn(M, Kd, device="cuda") if not lay.startswith("wgrad") else
              torch.randn(Kd, M, device="cuda")).to(torch.float8_e4m3fn).view(torch.uint8)
@@ -145,20 +148,27 @@ def main():
     # the same scale bytes (its MX scale layout is the tcgen05 atom layout mx_quantize writes)
     from mtorus.ops import mxfp8 as MX
 
-    mx_cases = [("qkv_fwd_mx", T, 3 * d, d), ("out_fwd_mx", T, d, d), ("ffn1_fwd_mx", T, F, d),
-                ("ffn2_fwd_mx", T, d, F), ("ffn1_wgrad_mx", F, d, T), ("square8k_mx", 8192, 8192, 8192)]
+    E4, E5 = MX.E4M3, MX.E5M2
+    bf, f32 = torch.bfloat16, torch.float32
+    # (name, M, N, K, A format, B format, output dtype): forward E4M3 x E4M3; dgrad E5M2 gradient x
+    # E4M3 weight (column codes); wgrad E5M2 gradient x E4M3 activation, fp32 out
+    mx_cases = [("qkv_fwd_mx", T, 3 * d, d, E4, E4, bf), ("out_fwd_mx", T, d, d, E4, E4, bf),
+                ("ffn1_fwd_mx", T, F, d, E4, E4, bf), ("ffn2_fwd_mx", T, d, F, E4, E4, bf),
+                ("qkv_dgrad_mx", T, d, 3 * d, E5, E4, bf), ("out_dgrad_mx", T, d, d, E5, E4, bf),
+                ("ffn1_dgrad_mx", T, d, F, E5, E4, bf), ("ffn2_dgrad_mx", T, F, d, E5, E4, bf),
+                ("qkv_wgrad_mx", 3 * d, d, T, E5, E4, f32), ("out_wgrad_mx", d, d, T, E5, E4, f32),
+                ("ffn1_wgrad_mx", F, d, T, E5, E4, f32), ("ffn2_wgrad_mx", d, F, T, E5, E4, f32),
+                ("square8k_mx", 8192, 8192, 8192, E4, E4, bf)]
     if args.case:
         mx_cases = [c for c in mx_cases if c[0] == args.case]
-    for name, M, N, Kd in mx_cases:
-        a = MX.mx_quantize(torch.randn(M, Kd, device="cuda").bfloat16())
-        b = MX.mx_quantize(torch.randn(N, Kd, device="cuda").bfloat16())
-        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    for name, M, N, Kd, fa, fb, odt in mx_cases:
+        a = MX.mx_quantize(torch.randn(M, Kd, device="cuda").bfloat16(), fa)
+        b = MX.mx_quantize(torch.randn(N, Kd, device="cuda").bfloat16(), fb)
+        out = torch.empty(M, N, device="cuda", dtype=odt)
+        out2 = torch.empty_like(out)
         mine = lambda: MX.gemm_mxfp8(a, b, out, impl="own")
-        try:
-            sa = a.sf.view(torch.float8_e8m0fnu).reshape((M + 127) // 128 * 128, -1)
-            sb = b.sf.view(torch.float8_e8m0fnu).reshape((N + 127) // 128 * 128, -1)
-            ref = lambda: torch._scaled_mm(a.codes.view(torch.float8_e4m3fn), b.codes.view(torch.float8_e4m3fn).t(),
-                                           sa, sb, out_dtype=torch.bfloat16)
+        try:  # cuBLASLt's block-scaled kernel through the library route (torch._scaled_mm)
+            ref = lambda: MX.gemm_mxfp8(a, b, out2, impl="library")
             ref()
         except (RuntimeError, AttributeError, TypeError) as e:
             print(f"[{name}] torch._scaled_mm MX path unavailable: {e}", file=sys.stderr)
@@ -166,7 +176,8 @@ def main():
         flops = 2.0 * M * N * Kd
         tm = timeit(mine, args.iters)
         tr = timeit(ref, args.iters) if ref is not None else float("nan")
-        r = {"case": name, "M": M, "N": N, "K": Kd, "layout": "tn_mx", "mine_ms": round(tm, 4),
+        r = {"case": name, "M": M, "N": N, "K": Kd, "layout": "tn_mx", "formats": f"{'E4M3' if fa == E4 else 'E5M2'}"
+             f" x {'E4M3' if fb == E4 else 'E5M2'} -> {'bf16' if odt == bf else 'fp32'}", "mine_ms": round(tm, 4),
              "cublas_ms": round(tr, 4) if tr == tr else None, "mine_tflops": round(flops / tm / 1e9, 1),
              "cublas_tflops": round(flops / tr / 1e9, 1) if tr == tr else None,
              "mine_frac_of_2x_measured_bf16_peak": round(flops / tm / 1e9 / (2 * peak), 3)}
@@ -174,13 +185,15 @@ def main():
             r["stalls"] = stalls(mine)
         rows.append(r)
         print(json.dumps(r), flush=True)
-        del a, b, out
+        del a, b, out, out2
     # the MXFP8 epilogues of the fused path: FFN1 forward (bias, GELU, pre-activation stored, GELU
     # quantised to row + column MX codes) and FFN2 dgrad (dGELU, E5M2 row + column codes, bias-gradient
     # column sums, no bf16 store), against the same GEMM followed by the separate quantiser
     epi_cases = [("ffn1_fwd_mx_gelu_mxout", T, F, d), ("ffn2_dgrad_mx_dgelu_mxout", T, F, d)]
     if args.case:
         epi_cases = [c for c in epi_cases if c[0] == args.case]
+    if args.group == "mx":
+        epi_cases = []
     for name, M, N, Kd in epi_cases:
         dgrad = "dgrad" in name
         a = MX.mx_quantize(torch.randn(M, Kd, device="cuda").bfloat16(), MX.E5M2 if dgrad else MX.E4M3)
@@ -205,7 +218,8 @@ def main():
         flops = 2.0 * M * N * Kd
         tm = timeit(mine, args.iters)
         tu = timeit(unfused, args.iters)
-        r = {"case": name, "M": M, "N": N, "K": Kd, "layout": "tn_mx", "mine_ms": round(tm, 4),
+        r = {"case": name, "M": M, "N": N, "K": Kd, "layout": "tn_mx", "formats": f"{'E4M3' if fa == E4 else 'E5M2'}"
+             f" x {'E4M3' if fb == E4 else 'E5M2'} -> {'bf16' if odt == bf else 'fp32'}", "mine_ms": round(tm, 4),
              "unfused_ms": round(tu, 4), "mine_tflops": round(flops / tm / 1e9, 1)}
         if STALLS:
             r["stalls"] = stalls(mine)
