@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(256, kRcCtasPerSm) mx_rc_tile_kernel(
     }
     if constexpr (SRC == 2 || SRC == 3) {
       // two pieces per step: their aux loads (dGELU) are in flight together, and the
-      // launch's register budget (three CTAs per SM) holds no more
+      // register limit of three CTAs per SM holds no more
 #pragma unroll 2
       for (int k = 0; k < 8; ++k) {
         const int i = t + k * 256, rr = i >> 4, cv = (i & 15) * 8;
