@@ -85,6 +85,30 @@ def dropout_apply(x, drop, out=None):
     return out
 
 
+def _lib_carveout_default() -> bool:
+    import os
+
+    return os.environ.get("MTORUS_DP_LIB_CARVEOUT", "1") != "0"
+
+
+LIB_CARVEOUT = _lib_carveout_default()
+
+
+def set_reserved_sms(n: int) -> None:
+    """Keep ``n`` SMs out of the GEMM grids launched from now on, for kernels that overlap
+    them on another stream (the data-parallel reduce-scatter during backward): the own GEMM
+    kernels size their grids without those SMs, and the library GEMMs get the same count as
+    torch's cuBLASLt SM carveout (``MTORUS_DP_LIB_CARVEOUT=0`` leaves the library GEMMs on every
+    SM).  ``n = 0`` releases both."""
+    _cuda().gemm_set_reserved_sms(int(n))
+    if LIB_CARVEOUT and hasattr(torch._C, "_set_sm_carveout_experimental"):
+        import warnings
+
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            torch._C._set_sm_carveout_experimental(int(n) if n else None)
+
+
 class gemm_dropout:
     """``with gemm_dropout(drop, mode): <one GEMM call>`` -- dropout drawn in that GEMM's
     epilogue (drop = (rng, site, thr16, scale) or None for none): mode 1 drops the result

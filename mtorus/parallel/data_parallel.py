@@ -26,6 +26,8 @@ from typing import List, Optional
 import torch
 import torch.distributed as dist
 
+from ..ops.kernels import set_reserved_sms as _set_reserved_sms
+
 
 class BucketPlan:
     def __init__(self, flat, bucket_bytes: int = 25 * 1024 * 1024, align_elems: int = 64):
@@ -138,9 +140,7 @@ class NcclBucketReducer:
         s, e = self.plan.ranges[b]
         if self.on_cuda and b == 0 and self.reserve_sms:
             # NCCL kernels overlap the rest of backward: leave SMs free for them
-            from .._ext import cuda as _cuda
-
-            _cuda().gemm_set_reserved_sms(self.reserve_sms)
+            _set_reserved_sms(self.reserve_sms)
         if not self.on_cuda:
             self.reduce_range(s, e)
             self.launched[b] = True
@@ -192,7 +192,5 @@ class NcclBucketReducer:
         if self.on_cuda:
             torch.cuda.current_stream().wait_stream(self.stream)
             if self.reserve_sms:
-                from .._ext import cuda as _cuda
-
-                _cuda().gemm_set_reserved_sms(0)
+                _set_reserved_sms(0)
         self._reset()

@@ -27,6 +27,8 @@ from typing import List, Optional, Sequence
 import torch
 import torch.distributed as dist
 
+from ..ops.kernels import set_reserved_sms as _set_reserved_sms
+
 from .._ext import cuda as _cuda
 from .data_parallel import BucketPlan
 
@@ -184,7 +186,7 @@ class SymmBucketReducer:
     def _launch(self, b: int) -> None:
         if not self._reserved:
             # from now on reduce kernels overlap backward: keep their SMs out of the GEMM grids
-            _cuda().gemm_set_reserved_sms(self.reserve)
+            _set_reserved_sms(self.reserve)
             self._reserved = True
         s, e = self.plan.ranges[b]
         ev = torch.cuda.Event()
@@ -215,7 +217,7 @@ class SymmBucketReducer:
             _cuda().symm_scalars_ar(self.ctx.scalars.ptrs, self.ctx.flags.ptrs, self.me, self.slot_norm,
                                     self.epoch, self.state, self.ep_ptr)
         torch.cuda.current_stream().wait_stream(self.stream)
-        _cuda().gemm_set_reserved_sms(0)
+        _set_reserved_sms(0)
         self._reserved = False
         self._reset()
 
