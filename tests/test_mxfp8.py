@@ -471,3 +471,37 @@ def test_cuda_layernorm_mx_matches_reference():
         dr = mx_dequantize(ref)
         assert float((dg - dr).abs().max()) <= 2 ** -3 * float(dr.abs().max())
         assert float((got.sf.cpu() == ref.sf).float().mean()) > 0.99
+
+
+def test_reserved_sms_reach_the_library_gemms(monkeypatch):
+    """set_reserved_sms keeps the reduce-scatter's SMs out of both GEMM families: the own
+    kernels' grid size and torch's cuBLASLt SM carveout; 0 releases both, and the switch
+    leaves the library alone."""
+    from mtorus.ops import kernels as K
+
+    seen = []
+
+    class FakeExt:
+        def gemm_set_reserved_sms(self, n):
+            seen.append(("own", n))
+
+    monkeypatch.setattr(K, "_cuda", lambda: FakeExt())
+    monkeypatch.setattr(torch._C, "_set_sm_carveout_experimental", lambda n: seen.append(("lib", n)), raising=False)
+    monkeypatch.setattr(K, "LIB_CARVEOUT", True)
+    K.set_reserved_sms(16)
+    K.set_reserved_sms(0)
+    assert seen == [("own", 16), ("lib", 16), ("own", 0), ("lib", None)]
+    seen.clear()
+    monkeypatch.setattr(K, "LIB_CARVEOUT", False)
+    K.set_reserved_sms(16)
+    assert seen == [("own", 16)]
+
+
+def test_library_route_rejects_what_it_cannot_do():
+    """impl="library" takes plain GEMMs only, and impl must name a route."""
+    a = mx_quantize_ref(torch.randn(64, 64).to(torch.bfloat16))
+    b = mx_quantize_ref(torch.randn(32, 64).to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        gemm_mxfp8(a, b, impl="library")  # CPU operands: not eligible
+    with pytest.raises(ValueError):
+        gemm_mxfp8(a, b, impl="cublas")
